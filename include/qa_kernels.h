@@ -1,0 +1,134 @@
+/*
+ * qa_kernels.h -- C ABI of the B200 (sm_100a) QuantAnything kernel library.
+ *
+ * libqa_kernels.so is a drop-in for the reference's CPU library: the first
+ * block below is the exact symbol set and signature set that the reference's
+ * ctypes loader declares (quantization/native.py:104-128 in the reference
+ * project), so `QA_LIB=/path/to/libqa_kernels.so` swaps it in under the
+ * reference's unchanged Python.  Those entry points take HOST pointers,
+ * copy to the GPU, compute, copy back and return synchronously -- the same
+ * contract as the CPU library (outputs valid on return, caller owns every
+ * buffer, no pointer retained).
+ *
+ * The second block adds what the reference has no counterpart for: an error
+ * channel, device selection, and DEVICE-pointer entry points (suffix _dev)
+ * that enqueue on a caller-provided CUDA stream for the device-resident
+ * executor.  Every signature uses only plain C types.
+ *
+ * Conventions shared with the reference (quantization/kernels/
+ * qa_kernels.cpp:1-13): row-major contiguous buffers; activations cross the
+ * boundary as int32 arrays holding values in [qmin, qmax]; the "narrow" path
+ * has int16 operands and an int32 accumulator, the "wide" path int32 operands
+ * and an int64 accumulator; requantization rounds half up on a 128-bit
+ * product.
+ */
+#ifndef QA_KERNELS_H_
+#define QA_KERNELS_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================================================================== *
+ *  1. Reference ABI (host pointers, synchronous)                        *
+ * ===================================================================== */
+
+/* qa_kernels.cpp:233 -- number of GPUs visible to the library (the CPU
+ * library returns its OpenMP thread count). */
+int qa_num_threads(void);
+/* qa_kernels.cpp:235 -- accepted and ignored (GPU work is not threaded by
+ * the host). */
+void qa_set_num_threads(int n);
+/* qa_kernels.cpp:243 -- always 0: the GPU library has no OpenMP. */
+int qa_has_openmp(void);
+
+/* qa_kernels.cpp:252 -- C[M,N] = A[M,K]·B[K,N], float32. */
+void qa_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A,
+                 const float* B, float* C);
+/* qa_kernels.cpp:256 -- int16 operands, exact int32 accumulator (wraps
+ * modulo 2^32 exactly like the CPU library if the caller's bound fails). */
+void qa_gemm_i16_i32(int64_t M, int64_t N, int64_t K, const int16_t* A,
+                     const int16_t* B, int32_t* C);
+/* qa_kernels.cpp:260 -- int32 operands, exact int64 accumulator. */
+void qa_gemm_i32_i64(int64_t M, int64_t N, int64_t K, const int32_t* A,
+                     const int32_t* B, int64_t* C);
+
+/* qa_kernels.cpp:273-284 -- NCHW convolution with OIHW weights, G groups,
+ * strides (SH,SW), top/left padding (PH,PW), dilations (DH,DW); the
+ * bottom/right padding is implied by OH/OW.  The narrow variant casts the
+ * int32 input to int16 before multiplying, like the CPU library. */
+void qa_conv_f32(const float* x, const float* w, float* y, int64_t N,
+                 int64_t C, int64_t H, int64_t W, int64_t Cout, int64_t KH,
+                 int64_t KW, int64_t SH, int64_t SW, int64_t PH, int64_t PW,
+                 int64_t DH, int64_t DW, int64_t G, int64_t OH, int64_t OW);
+void qa_conv_i32_i16_i32(const int32_t* x, const int16_t* w, int32_t* y,
+                         int64_t N, int64_t C, int64_t H, int64_t W,
+                         int64_t Cout, int64_t KH, int64_t KW, int64_t SH,
+                         int64_t SW, int64_t PH, int64_t PW, int64_t DH,
+                         int64_t DW, int64_t G, int64_t OH, int64_t OW);
+void qa_conv_i32_i32_i64(const int32_t* x, const int32_t* w, int64_t* y,
+                         int64_t N, int64_t C, int64_t H, int64_t W,
+                         int64_t Cout, int64_t KH, int64_t KW, int64_t SH,
+                         int64_t SW, int64_t PH, int64_t PW, int64_t DH,
+                         int64_t DW, int64_t G, int64_t OH, int64_t OW);
+
+/* qa_kernels.cpp:287-302 -- accumulators viewed as [outer, C, inner]:
+ * out = clamp(mbqm(acc + pre[c], mult[c], shift[c]) + post[c] + zp).
+ * pre_bias / post_bias may be NULL. */
+void qa_requantize_i32(const int32_t* acc, int32_t* out, int64_t outer,
+                       int64_t C, int64_t inner, const int64_t* mult,
+                       const int64_t* shift, const int64_t* pre_bias,
+                       const int64_t* post_bias, int64_t zp, int64_t qmin,
+                       int64_t qmax);
+void qa_requantize_i64(const int64_t* acc, int32_t* out, int64_t outer,
+                       int64_t C, int64_t inner, const int64_t* mult,
+                       const int64_t* shift, const int64_t* pre_bias,
+                       const int64_t* post_bias, int64_t zp, int64_t qmin,
+                       int64_t qmax);
+
+/* qa_kernels.cpp:307 -- out = clamp(mbqm(x - zp_in, m, s) + zp_out). */
+void qa_rescale(const int32_t* x, int32_t* out, int64_t n, int64_t zp_in,
+                int64_t m, int64_t s, int64_t zp_out, int64_t qmin,
+                int64_t qmax);
+/* qa_kernels.cpp:319 -- out = clamp(mbqm(a-za,ma,sa) + sign·mbqm(b-zb,mb,sb)
+ * + zp_out). */
+void qa_add(const int32_t* a, const int32_t* b, int32_t* out, int64_t n,
+            int64_t za, int64_t ma, int64_t sa, int64_t zb, int64_t mb,
+            int64_t sb, int64_t sign, int64_t zp_out, int64_t qmin,
+            int64_t qmax);
+/* qa_kernels.cpp:334 -- out = clamp(mbqm((a-za)(b-zb), m, s) + zp_out). */
+void qa_mul(const int32_t* a, const int32_t* b, int32_t* out, int64_t n,
+            int64_t za, int64_t zb, int64_t m, int64_t s, int64_t zp_out,
+            int64_t qmin, int64_t qmax);
+/* qa_kernels.cpp:348 -- out = lut[clamp(x - offset, 0, lut_len - 1)]. */
+void qa_lut(const int32_t* x, int32_t* out, int64_t n, int64_t offset,
+            const int32_t* lut, int64_t lut_len);
+/* qa_kernels.cpp:363 -- q = clamp(rint(x / scale) + zp), half to even, in
+ * IEEE double. */
+void qa_quantize_f32(const float* x, int32_t* q, int64_t n, double scale,
+                     int64_t zp, int64_t qmin, int64_t qmax);
+/* qa_kernels.cpp:379 -- x = (float)((q - zp) · scale) in IEEE double. */
+void qa_dequantize_f32(const int32_t* q, float* x, int64_t n, double scale,
+                       int64_t zp);
+
+/* ===================================================================== *
+ *  2. Extensions (no counterpart in the reference)                      *
+ * ===================================================================== */
+
+/* Error channel.  The reference's entry points return void and cannot fail
+ * loudly; here every entry point records a status for the calling host
+ * thread.  Mode 1 (the default, since the reference's loader cannot check a
+ * status) prints the message and aborts the process on any failure; mode 0
+ * only records it for qa_last_status()/qa_last_error().  QA_ON_ERROR=record
+ * in the environment selects mode 0 at load time. */
+int qa_last_status(void);          /* 0 = ok */
+const char* qa_last_error(void);   /* "" when the last call succeeded */
+void qa_clear_error(void);
+void qa_set_error_mode(int abort_on_error);
+
+/* Device selection for the calling host thread (default: $QA_DEVICE or 0). */
+int qa_device_count(void);
+int qa_set_device(int ordinal);
+int qa_get_device(void);
