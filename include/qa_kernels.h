@@ -132,3 +132,70 @@ void qa_set_error_mode(int abort_on_error);
 int qa_device_count(void);
 int qa_set_device(int ordinal);
 int qa_get_device(void);
+
+/* ===================================================================== *
+ *  3. Device-pointer entry points (no counterpart in the reference)     *
+ *                                                                       *
+ *  All pointers are device pointers; `stream` is a cudaStream_t (NULL = *
+ *  the legacy default stream).  The calls only enqueue work and return  *
+ *  0 on success or a status code (see qa_last_error()).                 *
+ * ===================================================================== */
+
+/* Requantization of device accumulators (same math as qa_requantize_*). */
+int qa_requantize_i32_dev(const int32_t* acc, int32_t* out, int64_t outer, int64_t C,
+                          int64_t inner, const int64_t* mult, const int64_t* shift,
+                          const int64_t* pre_bias, const int64_t* post_bias, int64_t zp,
+                          int64_t qmin, int64_t qmax, void* stream);
+int qa_requantize_i64_dev(const int64_t* acc, int32_t* out, int64_t outer, int64_t C,
+                          int64_t inner, const int64_t* mult, const int64_t* shift,
+                          const int64_t* pre_bias, const int64_t* post_bias, int64_t zp,
+                          int64_t qmin, int64_t qmax, void* stream);
+
+/* One fused 8-bit convolution / GEMM layer of the device-resident executor:
+ * tcgen05 implicit GEMM over NHWC int8/uint8 activations followed by the
+ * reference's per-layer integer sequence (ConvQuantize/GemmQuantize
+ * requantize, optional LUT activation, optional residual Add, optional
+ * rescaled copy into a Concat slice -- quant_layers.py:320-560).
+ *
+ * Layout: activation pixel p of image n at x + ((n*H + y)*W + x)*x_pix_stride,
+ * channel c at +c (so channel slices of a wider tensor are views).  Weights
+ * are packed [w_rows][w_kp] int8, row = output channel, K ordered
+ * (ky, kx, c) with C channels per tap, zero padded; w_kp % 16 == 0 and
+ * w_rows a multiple of the column tile (16..256, chosen from Cout).  Every
+ * field is 8 bytes so the struct has no padding. */
+typedef struct qa_fused_conv_desc {
+  const void* x;          /* activations (NHWC bytes) */
+  int64_t x_pix_stride;   /* bytes between pixels; multiple of 16 (C%16==0) or 4 */
+  int64_t x_signed;       /* 1: int8, 0: uint8 */
+  int64_t x_zp;           /* raw zero point: value of out-of-image taps */
+  int64_t N, H, W, C;     /* C: channels per tap, multiple of 16 (or 4) */
+  int64_t KH, KW, SH, SW, PH, PW, DH, DW, OH, OW;
+  int64_t Cout;
+  const void* w;          /* packed weights (int8) */
+  int64_t w_rows, w_kp;
+  const int64_t* bias;    /* per channel, may be NULL; includes -x_zp*sum(w) */
+  const int64_t* mult;
+  const int64_t* shift;
+  int64_t zp, qmin, qmax;
+  int64_t fast;           /* 1: host proved the 64-bit requantize exact */
+  const int32_t* lut;     /* optional activation table */
+  int64_t lut_offset, lut_len;
+  const void* res;        /* optional residual (NHWC bytes), channel 0 */
+  int64_t res_pix_stride, res_signed;
+  int64_t za, ma, sa, zb, mb, sb, sign, add_zo, add_qmin, add_qmax;
+  void* out;              /* optional primary output (NHWC bytes), channel 0 */
+  int64_t out_pix_stride;
+  void* out2;             /* optional rescaled copy, channel 0 */
+  int64_t out2_pix_stride;
+  int64_t r_identity;
+  int64_t r_zp_in, r_m, r_s, r_zp_out, r_qmin, r_qmax;
+  int64_t block_n;        /* column tile: 0 = choose from Cout */
+} qa_fused_conv_desc;
+
+int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QA_KERNELS_H_ */

@@ -1,0 +1,774 @@
+// Tensor-core (tcgen05 kind::i8) implicit-GEMM kernel, its operand packing
+// kernels and the host routes that use it.  See qa_umma.cuh for the design.
+//
+// CTA = 6 warps:
+//   warps 0-3  gather the activation K-block tiles with cp.async (one row per
+//              thread), then drain TMEM in the epilogue (warp w owns TMEM
+//              lanes 32w..32w+31, i.e. output rows 32w..32w+31);
+//   warp 4     allocates TMEM; its lane 0 issues the MMAs;
+//   warp 5     lane 0 issues the weight-tile TMA loads.
+// Pipeline: kStages shared-memory stages with full/empty mbarriers; the MMA
+// thread releases a stage with tcgen05.commit.  All waits are bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "qa_common.cuh"
+#include "qa_direct.cuh"
+#include "qa_fixedpoint.cuh"
+#include "qa_ptx.cuh"
+#include "qa_umma.cuh"
+
+namespace qa {
+
+enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1, kEpiFused = 2 };
+
+constexpr int kBM = 128;          // tile rows (TMEM lanes)
+constexpr int kBKBytes = 128;     // K-block bytes (one 128-byte swizzle row)
+constexpr int kProducerThreads = 128;
+constexpr int kCtaThreads = 192;
+constexpr uint64_t kWaitBudgetNs = 1000000000ull;  // 1 s per wait
+constexpr int kTimeoutCode = 0x7001;
+
+struct ConvTileParams {
+  const uint8_t* a[2];      // activation planes (NHWC bytes)
+  int64_t pix_stride;       // bytes between consecutive pixels of a plane
+  int64_t group_a_off;      // byte offset between groups (grid.z)
+  uint32_t pad_word[2];     // 4-byte pattern for taps outside the image
+  int32_t a_signed;         // single-plane activations: s8 (1) or u8 (0)
+  int32_t H, W, Cin;        // Cin: bytes per pixel consumed per tap (multiple of chunk)
+  int32_t KH, KW, SH, SW, PH, PW, DH, DW, OH, OW;
+  int64_t M;                // rows = images * OH * OW
+  int32_t K;                // valid K bytes = KH*KW*Cin
+  int32_t num_kb;           // K-blocks
+  int32_t b_plane_rows;     // weight rows between planes in the tensor map
+  int32_t b_group_rows;     // weight rows between groups
+  int32_t n_valid;          // valid output columns per group
+  // int32 accumulator outputs (ABI modes)
+  int32_t* y;
+  int64_t y_ctot;           // NCHW: channels of y; row mode: leading dimension
+  int64_t ohw;
+  int32_t* status;          // device error word
+  FusedEpilogue epi;
+};
+
+template <int BN, int PA, int PB>
+struct TileShape {
+  static constexpr int kAPlaneBytes = kBM * kBKBytes;           // 16 KB
+  static constexpr int kBPlaneBytes = BN * kBKBytes;
+  static constexpr int kStageBytes = PA * kAPlaneBytes + PB * kBPlaneBytes;
+  static constexpr int kNumAcc = (PA == 1 && PB == 1) ? 1 : 3;
+  static constexpr int kTmemCols = (kNumAcc * BN <= 32)    ? 32
+                                   : (kNumAcc * BN <= 64)  ? 64
+                                   : (kNumAcc * BN <= 128) ? 128
+                                   : (kNumAcc * BN <= 256) ? 256
+                                                           : 512;
+  static_assert(kNumAcc * BN <= 512, "TMEM columns");
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+};
+
+template <int BN, int PA, int PB, int kStages>
+constexpr size_t umma_smem_bytes() {
+  return 1024 /* alignment slack */ + (size_t)kStages * TileShape<BN, PA, PB>::kStageBytes +
+         (2 * kStages + 1) * 8 + 16;
+}
+
+// Value of a stored activation byte.
+__device__ __forceinline__ int64_t byte_value(uint8_t b, int is_signed) {
+  return is_signed ? (int64_t)(int8_t)b : (int64_t)b;
+}
+
+template <int BN, int PA, int PB, int kChunk, int kEpi, int kStages>
+__global__ void __launch_bounds__(kCtaThreads, 1)
+    umma_conv_kernel(const __grid_constant__ ConvTileParams p,
+                     const __grid_constant__ CUtensorMap tmap_b) {
+  using TS = TileShape<BN, PA, PB>;
+  constexpr int kLookahead = kStages - 1;  // cp.async groups in flight per thread
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment of the swizzled tiles (the swizzle pattern is a
+  // function of the shared address bits 4..9).
+  const uint32_t raw_addr = ptx::smem_addr(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + kStages * TS::kStageBytes;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (kStages + s); };
+  const uint32_t done_bar = bar_base + 8u * (2 * kStages);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + kStages * TS::kStageBytes +
+                                                 (2 * kStages + 1) * 8);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  auto a_tile = [&](int s, int pl) {
+    return base + s * TS::kStageBytes + pl * TS::kAPlaneBytes;
+  };
+  auto b_tile = [&](int s, int pl) {
+    return base + s * TS::kStageBytes + PA * TS::kAPlaneBytes + pl * TS::kBPlaneBytes;
+  };
+
+  const int tid = threadIdx.x;
+  const int warp = tid / 32, lane = tid % 32;
+  const int64_t m0 = (int64_t)blockIdx.x * kBM;
+  const int n0 = blockIdx.y * BN;
+  const int grp = blockIdx.z;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(full_bar(s), kProducerThreads + 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    ptx::mbar_init(done_bar, 1);
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 4) {
+    ptx::tmem_alloc(ptx::smem_addr(s_tmem), TS::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  if (warp == 5 && lane == 0) ptx::prefetch_tmap(&tmap_b);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  auto fail = [&]() {
+    *s_abort = 1;
+    if (p.status) atomicExch(p.status, kTimeoutCode);
+  };
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (ptx::mbar_wait(bar, parity, kWaitBudgetNs)) return true;
+    fail();
+    return false;
+  };
+
+  if (warp < 4) {
+    // ------------------------------------------------ activation gather --
+    const int r = tid;  // tile row
+    const int64_t m = m0 + r;
+    const bool row_ok = m < p.M;
+    int64_t img = 0, iy0 = 0, ix0 = 0;
+    if (row_ok) {
+      const int64_t ohw = (int64_t)p.OH * p.OW;
+      img = m / ohw;
+      const int64_t rem = m - img * ohw;
+      const int64_t oy = rem / p.OW, ox = rem - (rem / p.OW) * p.OW;
+      iy0 = oy * p.SH - p.PH;
+      ix0 = ox * p.SW - p.PW;
+    }
+    const int64_t img_off = img * (int64_t)p.H * p.W * p.pix_stride + grp * p.group_a_off;
+    const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    const uint32_t sw = (uint32_t)(r & 7);
+    for (int kb = 0; kb < p.num_kb; ++kb) {
+      const int s = kb % kStages;
+      if (kb >= kStages) wait(empty_bar(s), ((kb / kStages) - 1) & 1);
+      const bool live = !*s_abort;
+      const int k0 = kb * kBKBytes;
+      int tap = k0 / p.Cin;
+      int c = k0 - tap * p.Cin;
+      int ky = tap / p.KW, kx = tap - (tap / p.KW) * p.KW;
+#pragma unroll 4
+      for (int kk = 0; kk < kBKBytes; kk += kChunk) {
+        const int k = k0 + kk;
+        const int64_t iy = iy0 + (int64_t)ky * p.DH, ix = ix0 + (int64_t)kx * p.DW;
+        const bool in_k = k < p.K;
+        const bool inside = row_ok && in_k && iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
+        const int64_t off = img_off + (iy * p.W + ix) * p.pix_stride + c;
+        const uint32_t soff = row_off + ((((uint32_t)kk >> 4) ^ sw) << 4) + ((uint32_t)kk & 15u);
+#pragma unroll
+        for (int pl = 0; pl < PA; ++pl) {
+          const uint32_t dst = a_tile(s, pl) + soff;
+          if (!live) continue;
+          if (inside) {
+            if (kChunk == 16)
+              ptx::cp_async_16(dst, p.a[pl] + off, 16);
+            else
+              ptx::cp_async_4(dst, p.a[pl] + off, 4);
+          } else if (row_ok && in_k && p.pad_word[pl] != 0u) {
+            // tap outside the image: the raw zero point (centred value 0)
+            uint8_t* d = smem + (dst - base);
+            if (kChunk == 16)
+              *reinterpret_cast<uint4*>(d) =
+                  make_uint4(p.pad_word[pl], p.pad_word[pl], p.pad_word[pl], p.pad_word[pl]);
+            else
+              *reinterpret_cast<uint32_t*>(d) = p.pad_word[pl];
+          } else {
+            if (kChunk == 16)
+              ptx::cp_async_16(dst, p.a[pl], 0);
+            else
+              ptx::cp_async_4(dst, p.a[pl], 0);
+          }
+        }
+        c += kChunk;
+        if (c >= p.Cin) {
+          c = 0;
+          if (++kx == p.KW) {
+            kx = 0;
+            ++ky;
+          }
+        }
+      }
+      ptx::cp_async_commit();
+      if (kb >= kLookahead) {
+        ptx::cp_async_wait<kLookahead>();
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(full_bar((kb - kLookahead) % kStages));
+      }
+    }
+    ptx::cp_async_wait_all();
+    ptx::fence_proxy_async_smem();
+    for (int kb = (p.num_kb > kLookahead ? p.num_kb - kLookahead : 0); kb < p.num_kb; ++kb)
+      ptx::mbar_arrive(full_bar(kb % kStages));
+  } else if (warp == 5) {
+    // ------------------------------------------------- weight TMA loads --
+    if (lane == 0) {
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages && !wait(empty_bar(s), ((kb / kStages) - 1) & 1)) break;
+        if (*s_abort) break;
+        ptx::mbar_arrive_expect_tx(full_bar(s), PB * TS::kBPlaneBytes);
+#pragma unroll
+        for (int q = 0; q < PB; ++q)
+          ptx::tma_load_2d(b_tile(s, q), &tmap_b, full_bar(s), kb * kBKBytes,
+                           q * p.b_plane_rows + grp * p.b_group_rows + n0);
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int s = kb % kStages;
+        if (!wait(full_bar(s), (kb / kStages) & 1)) break;
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kBKBytes / 32; ++kk) {
+#pragma unroll
+          for (int pa = 0; pa < PA; ++pa) {
+#pragma unroll
+            for (int pb = 0; pb < PB; ++pb) {
+              // accumulator of this plane pair: 0 = lo*lo, 1 = cross, 2 = hi*hi
+              const int acc = (PA == 1) ? 0 : (pa + pb);
+              const bool first_writer = (PA == 1) || !(pa == 1 && pb == 0);
+              const uint32_t accumulate = (kb > 0 || kk > 0 || !first_writer) ? 1u : 0u;
+              // operand signedness: 8-bit single plane is signed unless the
+              // caller says otherwise; split planes are (lo: u8, hi: s8)
+              const int a_signed = (PA == 1) ? p.a_signed : pa;
+              const int b_signed = (PB == 1) ? 1 : pb;
+              const uint32_t idesc = ptx::idesc_i8(kBM, BN, a_signed, b_signed);
+              const uint64_t ad = ptx::smem_desc_sw128(a_tile(s, pa) + kk * 32);
+              const uint64_t bd = ptx::smem_desc_sw128(b_tile(s, pb) + kk * 32);
+              ptx::mma_i8(tmem + acc * BN, ad, bd, idesc, accumulate);
+            }
+          }
+        }
+        ptx::mma_commit(empty_bar(s));
+      }
+      ptx::mma_commit(done_bar);
+    }
+  }
+
+  if (warp < 4) {
+    // ----------------------------------------------------------- epilogue --
+    const bool ok = wait(done_bar, 0);
+    __syncwarp();
+    ptx::tc_fence_after();
+    const int r = tid;
+    const int64_t m = m0 + r;
+    const bool row_ok = ok && m < p.M;
+    const uint32_t lane_base = tmem + (((uint32_t)warp * 32u) << 16);
+    int64_t img = 0, pix = 0;
+    if (row_ok) {
+      const int64_t ohw = (int64_t)p.OH * p.OW;
+      img = m / ohw;
+      pix = m - img * ohw;
+    }
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t v[TS::kNumAcc][16];
+#pragma unroll
+      for (int a = 0; a < TS::kNumAcc; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
+      ptx::tmem_ld_wait();
+      if (!row_ok) continue;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + c0 + j;  // column within the group
+        if (n >= p.n_valid) continue;
+        if constexpr (kEpi == kEpiAcc32Nchw || kEpi == kEpiAcc32Row) {
+          uint32_t acc;
+          if constexpr (TS::kNumAcc == 1) {
+            acc = v[0][j];
+          } else {
+            acc = v[0][j] + (v[1][j] << 8) + (v[2][j] << 16);  // modulo 2^32
+          }
+          if constexpr (kEpi == kEpiAcc32Nchw) {
+            const int64_t co = (int64_t)grp * p.n_valid + n;
+            p.y[(img * p.y_ctot + co) * p.ohw + pix] = (int32_t)acc;
+          } else {
+            p.y[m * p.y_ctot + n] = (int32_t)acc;
+          }
+        } else {
+          static_assert(TS::kNumAcc == 1, "fused epilogue is 8-bit only");
+          const FusedEpilogue& e = p.epi;
+          const int64_t x = (int64_t)(int32_t)v[0][j] + (e.bias ? e.bias[n] : 0);
+          int64_t q;
+          if (e.fast) {
+            q = requant_fast(x, e.mult[n], (int)(31 + e.shift[n]), e.zp, e.qmin, e.qmax);
+          } else {
+            q = requant_exact(x, e.mult[n], e.shift[n], e.zp, e.qmin, e.qmax);
+          }
+          if (e.lut) {
+            int64_t idx = q - e.lut_offset;
+            idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
+            q = __ldg(e.lut + idx);
+          }
+          if (e.res) {
+            const int64_t a = byte_value(e.res[m * e.res_pix_stride + n], e.res_signed);
+            I128 ta = mbqm(a - e.za, e.ma, e.sa);
+            I128 tb = mbqm(q - e.zb, e.mb, e.sb);
+            if (e.sign < 0) tb = neg_i128(tb);
+            q = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
+          }
+          if (e.out) e.out[m * e.out_pix_stride + n] = (uint8_t)q;
+          if (e.out2) {
+            int64_t q2;
+            if (e.r_identity) {
+              q2 = q < e.r_qmin ? e.r_qmin : (q > e.r_qmax ? e.r_qmax : q);
+            } else {
+              q2 = requant_exact(q - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
+            }
+            e.out2[m * e.out2_pix_stride + n] = (uint8_t)q2;
+          }
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, TS::kTmemCols);
+  }
+}
+
+// ===================================================== host utilities ==
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+// 2-D uint8 tensor map over [rows, row_bytes] with a 128 x box_rows box in
+// the 128-byte swizzle.
+bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                      int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error(kCudaError, "cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) {
+    set_error(kBadArgument, "weight tensor map: base / row stride not 16-byte aligned");
+    return false;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(kCudaError, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return false;
+  }
+  return true;
+}
+
+template <int BN, int PA, int PB, int kChunk, int kEpi, int kStages>
+bool launch_umma(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n_tiles,
+                 int64_t groups, cudaStream_t st) {
+  auto kern = umma_conv_kernel<BN, PA, PB, kChunk, kEpi, kStages>;
+  const size_t smem = umma_smem_bytes<BN, PA, PB, kStages>();
+  static bool attr_set[64] = {};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem),
+                    "cudaFuncSetAttribute(smem)"))
+      return false;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t m_tiles = (prm.M + kBM - 1) / kBM;
+  if (m_tiles > 0x7FFFFFFF || n_tiles > 65535 || groups > 65535) {
+    set_error(kUnsupported, "umma: grid too large");
+    return false;
+  }
+  kern<<<dim3((unsigned)m_tiles, (unsigned)n_tiles, (unsigned)groups), kCtaThreads, smem, st>>>(
+      prm, tmap);
+  return !cuda_failed(cudaGetLastError(), "umma_conv_kernel launch");
+}
+
+// ---------------------------------------------------- packing kernels ----
+
+// int16 [rows, K] row-major (or int32 cast to int16) -> two byte planes
+// [rows, Kp] (lo: v & 0xFF, hi: v >> 8), zero padded to Kp.
+template <typename TIn>
+__global__ void split_rows_kernel(const TIn* __restrict__ src, uint8_t* __restrict__ lo,
+                                  uint8_t* __restrict__ hi, int64_t rows, int64_t K,
+                                  int64_t Kp) {
+  const int64_t total = rows * Kp;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / Kp, k = i - r * Kp;
+    const int16_t v = k < K ? (int16_t)src[r * K + k] : (int16_t)0;
+    lo[i] = (uint8_t)(v & 0xFF);
+    hi[i] = (uint8_t)(v >> 8);
+  }
+}
+
+// int16 B[K, N] row-major -> planes [Np, Kp] (transposed, zero padded).
+__global__ void split_transpose_kernel(const int16_t* __restrict__ B, uint8_t* __restrict__ lo,
+                                       uint8_t* __restrict__ hi, int64_t K, int64_t N,
+                                       int64_t Np, int64_t Kp) {
+  const int64_t total = Np * Kp;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t n = i / Kp, k = i - n * Kp;
+    const int16_t v = (k < K && n < N) ? B[k * N + n] : (int16_t)0;
+    lo[i] = (uint8_t)(v & 0xFF);
+    hi[i] = (uint8_t)(v >> 8);
+  }
+}
+
+// int32 NCHW (cast to int16) -> NHWC planes with Cp channels (zero padded).
+__global__ void split_nchw_to_nhwc_kernel(const int32_t* __restrict__ x, uint8_t* __restrict__ lo,
+                                          uint8_t* __restrict__ hi, int64_t N, int64_t C,
+                                          int64_t HW, int64_t Cp) {
+  const int64_t total = N * HW * Cp;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t c = i % Cp;
+    const int64_t t = i / Cp;
+    const int64_t pix = t % HW, n = t / HW;
+    const int16_t v = c < C ? (int16_t)x[(n * C + c) * HW + pix] : (int16_t)0;
+    lo[i] = (uint8_t)(v & 0xFF);
+    hi[i] = (uint8_t)(v >> 8);
+  }
+}
+
+// int16 OIHW weights [G*Cog, Cg, KH, KW] -> planes [G][Cogp][KH*KW*Cgp]
+// with K ordered (ky, kx, c).
+__global__ void split_weights_kernel(const int16_t* __restrict__ w, uint8_t* __restrict__ lo,
+                                     uint8_t* __restrict__ hi, int64_t G, int64_t Cog,
+                                     int64_t Cogp, int64_t Cg, int64_t Cgp, int64_t KH,
+                                     int64_t KW, int64_t Kp) {
+  const int64_t total = G * Cogp * Kp;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t Kv = KH * KW * Cgp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t k = i % Kp;
+    const int64_t row = i / Kp;
+    const int64_t o = row % Cogp, g = row / Cogp;
+    int16_t v = 0;
+    if (o < Cog && k < Kv) {
+      const int64_t tap = k / Cgp, c = k - tap * Cgp;
+      const int64_t ky = tap / KW, kx = tap - ky * KW;
+      if (c < Cg) v = w[(((g * Cog + o) * Cg + c) * KH + ky) * KW + kx];
+    }
+    lo[i] = (uint8_t)(v & 0xFF);
+    hi[i] = (uint8_t)(v >> 8);
+  }
+}
+
+static inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Scratch for the packed planes of an ABI call: a per-thread grow-only
+// buffer separate from the HostCall arena (which holds the call's operands).
+static uint8_t* pack_scratch(size_t bytes) {
+  static thread_local uint8_t* buf = nullptr;
+  static thread_local size_t cap = 0;
+  static thread_local int dev = -1;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (buf && (bytes > cap || dev != cur)) {
+    cudaDeviceSynchronize();
+    cudaFree(buf);
+    buf = nullptr;
+    cap = 0;
+  }
+  if (!buf) {
+    size_t want = bytes < (size_t(32) << 20) ? (size_t(32) << 20) : bytes;
+    if (cuda_failed(cudaMalloc(&buf, want), "cudaMalloc(pack scratch)")) return nullptr;
+    cap = want;
+    dev = cur;
+  }
+  return buf;
+}
+
+constexpr int kSplitBN = 64;
+constexpr int kSplitStages = 4;
+
+bool umma_gemm_i16_i32_abi(const int16_t* A, const int16_t* B, int32_t* C, int64_t M, int64_t N,
+                           int64_t K, cudaStream_t st) {
+  if (K == 0 || M * N == 0 || K > (int64_t(1) << 24)) {
+    return launch_gemm_tiled<int16_t, int16_t, int32_t>(A, B, C, M, N, K, st);
+  }
+  const int64_t Kp = round_up(K, 16);
+  const int64_t Np = round_up(N, kSplitBN);
+  const size_t a_bytes = align256((size_t)(M * Kp)), b_bytes = align256((size_t)(Np * Kp));
+  uint8_t* scratch = pack_scratch(2 * a_bytes + 2 * b_bytes);
+  if (!scratch) return false;
+  uint8_t *a_lo = scratch, *a_hi = scratch + a_bytes;
+  uint8_t *b_lo = a_hi + a_bytes, *b_hi = b_lo + b_bytes;
+  split_rows_kernel<int16_t><<<grid_for(M * Kp, 256), 256, 0, st>>>(A, a_lo, a_hi, M, K, Kp);
+  split_transpose_kernel<<<grid_for(Np * Kp, 256), 256, 0, st>>>(B, b_lo, b_hi, K, N, Np, Kp);
+  if (cuda_failed(cudaGetLastError(), "split launch")) return false;
+  // the two weight planes are consecutive [Np, Kp] blocks of one tensor map
+  CUtensorMap tmap;
+  if (!make_weight_tmap(&tmap, b_lo, 2 * Np, Kp, kSplitBN)) return false;
+  if ((size_t)(b_hi - b_lo) != (size_t)(Np * Kp)) {
+    // planes must be contiguous for the single tensor map: repack offsets
+    set_error(kBadArgument, "internal: weight planes not contiguous");
+    return false;
+  }
+  ConvTileParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.a[0] = a_lo;
+  prm.a[1] = a_hi;
+  prm.pix_stride = Kp;
+  prm.H = prm.W = 1;
+  prm.Cin = (int32_t)Kp;
+  prm.KH = prm.KW = prm.SH = prm.SW = prm.DH = prm.DW = 1;
+  prm.OH = prm.OW = 1;
+  prm.M = M;
+  prm.K = (int32_t)Kp;
+  prm.num_kb = (int32_t)((Kp + kBKBytes - 1) / kBKBytes);
+  prm.b_plane_rows = (int32_t)Np;
+  prm.n_valid = (int32_t)N;
+  prm.y = C;
+  prm.y_ctot = N;
+  prm.ohw = 1;
+  prm.status = device_status_word();
+  return launch_umma<kSplitBN, 2, 2, 16, kEpiAcc32Row, kSplitStages>(prm, tmap, Np / kSplitBN, 1,
+                                                                      st);
+}
+
+bool umma_conv_i16_i32_abi(const int32_t* x, const int16_t* w, int32_t* y, const ConvGeom& g,
+                           cudaStream_t st) {
+  const int64_t Cg = g.C / g.G, Cog = g.Cout / g.G;
+  const bool tiles_fit = (g.G == 1) || (Cg % 16 == 0);
+  const int64_t Cgp = g.G == 1 ? round_up(g.C, 16) : Cg;
+  const int64_t Kv = g.KH * g.KW * Cgp;
+  if (!tiles_fit || Kv > (int64_t(1) << 24) || g.H * g.W == 0) {
+    return launch_conv_direct<int32_t, int16_t, int16_t, int32_t>(x, w, y, g, st);
+  }
+  const int64_t Cp = g.G == 1 ? Cgp : g.C;
+  const int64_t HW = g.H * g.W;
+  const int64_t Kp = round_up(Kv, 16);
+  const int64_t Cogp = round_up(Cog, kSplitBN);
+  const size_t a_bytes = align256((size_t)(g.N * HW * Cp));
+  const size_t b_bytes = (size_t)(g.G * Cogp * Kp);  // planes must be contiguous
+  uint8_t* scratch = pack_scratch(2 * a_bytes + align256(2 * b_bytes));
+  if (!scratch) return false;
+  uint8_t *a_lo = scratch, *a_hi = scratch + a_bytes;
+  uint8_t *b_lo = a_hi + a_bytes, *b_hi = b_lo + b_bytes;
+  split_nchw_to_nhwc_kernel<<<grid_for(g.N * HW * Cp, 256), 256, 0, st>>>(x, a_lo, a_hi, g.N,
+                                                                           g.C, HW, Cp);
+  split_weights_kernel<<<grid_for(g.G * Cogp * Kp, 256), 256, 0, st>>>(
+      w, b_lo, b_hi, g.G, Cog, Cogp, Cg, Cgp, g.KH, g.KW, Kp);
+  if (cuda_failed(cudaGetLastError(), "split launch")) return false;
+  CUtensorMap tmap;
+  if (!make_weight_tmap(&tmap, b_lo, 2 * g.G * Cogp, Kp, kSplitBN)) return false;
+  ConvTileParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.a[0] = a_lo;
+  prm.a[1] = a_hi;
+  prm.pix_stride = Cp;
+  prm.group_a_off = Cg;
+  prm.H = (int32_t)g.H;
+  prm.W = (int32_t)g.W;
+  prm.Cin = (int32_t)Cgp;
+  prm.KH = (int32_t)g.KH;
+  prm.KW = (int32_t)g.KW;
+  prm.SH = (int32_t)g.SH;
+  prm.SW = (int32_t)g.SW;
+  prm.PH = (int32_t)g.PH;
+  prm.PW = (int32_t)g.PW;
+  prm.DH = (int32_t)g.DH;
+  prm.DW = (int32_t)g.DW;
+  prm.OH = (int32_t)g.OH;
+  prm.OW = (int32_t)g.OW;
+  prm.M = g.N * g.OH * g.OW;
+  prm.K = (int32_t)Kv;
+  prm.num_kb = (int32_t)((Kp + kBKBytes - 1) / kBKBytes);
+  prm.b_plane_rows = (int32_t)(g.G * Cogp);
+  prm.b_group_rows = (int32_t)Cogp;
+  prm.n_valid = (int32_t)Cog;
+  prm.y = y;
+  prm.y_ctot = g.Cout;
+  prm.ohw = g.OH * g.OW;
+  prm.status = device_status_word();
+  if (prm.M == 0) return true;
+  return launch_umma<kSplitBN, 2, 2, 16, kEpiAcc32Nchw, kSplitStages>(prm, tmap, Cogp / kSplitBN,
+                                                                       g.G, st);
+}
+
+}  // namespace qa
+
+// ============================================ fused 8-bit layer (resident) ==
+#include "../../include/qa_kernels.h"
+
+namespace qa {
+
+constexpr int kFusedStages = 4;
+
+template <int BN, int kChunk>
+static bool launch_fused_bn(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n_tiles,
+                            cudaStream_t st) {
+  return launch_umma<BN, 1, 1, kChunk, kEpiFused, kFusedStages>(prm, tmap, n_tiles, 1, st);
+}
+
+static bool fused_conv(const qa_fused_conv_desc& d, cudaStream_t st) {
+  if (d.N < 0 || d.H <= 0 || d.W <= 0 || d.C <= 0 || d.Cout <= 0 || d.KH <= 0 || d.KW <= 0 ||
+      d.SH <= 0 || d.SW <= 0 || d.DH <= 0 || d.DW <= 0 || d.OH <= 0 || d.OW <= 0 || d.PH < 0 ||
+      d.PW < 0) {
+    set_error(kBadArgument, "qa_conv_fused_dev: invalid geometry");
+    return false;
+  }
+  const int chunk = (d.C % 16 == 0 && d.x_pix_stride % 16 == 0) ? 16
+                    : (d.C % 4 == 0 && d.x_pix_stride % 4 == 0) ? 4
+                                                                 : 0;
+  if (!chunk) {
+    set_error(kBadArgument, "qa_conv_fused_dev: channels per tap must be a multiple of 4");
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(d.x) & (chunk - 1)) || !d.w || !d.mult || !d.shift) {
+    set_error(kBadArgument, "qa_conv_fused_dev: misaligned or missing operand");
+    return false;
+  }
+  int bn = (int)d.block_n;
+  if (bn == 0) bn = d.Cout <= 16 ? 16 : d.Cout <= 32 ? 32 : d.Cout <= 64 ? 64
+                   : d.Cout <= 128 ? 128 : 256;
+  if (chunk == 4 && bn > 64) bn = 64;
+  const int64_t n_tiles = (d.Cout + bn - 1) / bn;
+  const int64_t K = d.KH * d.KW * d.C;
+  if (d.w_kp % 16 || d.w_kp < K || d.w_rows < n_tiles * bn) {
+    set_error(kBadArgument, "qa_conv_fused_dev: packed weight shape does not cover the layer");
+    return false;
+  }
+  if (d.N == 0) return true;
+  CUtensorMap tmap;
+  if (!make_weight_tmap(&tmap, d.w, d.w_rows, d.w_kp, bn)) return false;
+
+  ConvTileParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.a[0] = static_cast<const uint8_t*>(d.x);
+  prm.pix_stride = d.x_pix_stride;
+  const uint32_t zb = (uint32_t)(d.x_zp & 0xFF);
+  prm.pad_word[0] = zb * 0x01010101u;
+  prm.a_signed = d.x_signed ? 1 : 0;
+  prm.H = (int32_t)d.H;
+  prm.W = (int32_t)d.W;
+  prm.Cin = (int32_t)d.C;
+  prm.KH = (int32_t)d.KH;
+  prm.KW = (int32_t)d.KW;
+  prm.SH = (int32_t)d.SH;
+  prm.SW = (int32_t)d.SW;
+  prm.PH = (int32_t)d.PH;
+  prm.PW = (int32_t)d.PW;
+  prm.DH = (int32_t)d.DH;
+  prm.DW = (int32_t)d.DW;
+  prm.OH = (int32_t)d.OH;
+  prm.OW = (int32_t)d.OW;
+  prm.M = d.N * d.OH * d.OW;
+  prm.K = (int32_t)K;
+  prm.num_kb = (int32_t)((K + kBKBytes - 1) / kBKBytes);
+  prm.n_valid = (int32_t)d.Cout;
+  prm.ohw = d.OH * d.OW;
+  prm.status = device_status_word();
+  FusedEpilogue& e = prm.epi;
+  e.bias = d.bias;
+  e.mult = d.mult;
+  e.shift = d.shift;
+  e.zp = d.zp;
+  e.qmin = d.qmin;
+  e.qmax = d.qmax;
+  e.fast = d.fast ? 1 : 0;
+  e.lut = d.lut;
+  e.lut_offset = d.lut_offset;
+  e.lut_len = d.lut_len;
+  e.res = static_cast<const uint8_t*>(d.res);
+  e.res_pix_stride = d.res_pix_stride;
+  e.res_signed = d.res_signed ? 1 : 0;
+  e.za = d.za;
+  e.ma = d.ma;
+  e.sa = d.sa;
+  e.zb = d.zb;
+  e.mb = d.mb;
+  e.sb = d.sb;
+  e.sign = d.sign;
+  e.add_zo = d.add_zo;
+  e.add_qmin = d.add_qmin;
+  e.add_qmax = d.add_qmax;
+  e.out = static_cast<uint8_t*>(d.out);
+  e.out_pix_stride = d.out_pix_stride;
+  e.out2 = static_cast<uint8_t*>(d.out2);
+  e.out2_pix_stride = d.out2_pix_stride;
+  e.r_identity = d.r_identity ? 1 : 0;
+  e.r_zp_in = d.r_zp_in;
+  e.r_m = d.r_m;
+  e.r_s = d.r_s;
+  e.r_zp_out = d.r_zp_out;
+  e.r_qmin = d.r_qmin;
+  e.r_qmax = d.r_qmax;
+  if (chunk == 16) {
+    switch (bn) {
+      case 16: return launch_fused_bn<16, 16>(prm, tmap, n_tiles, st);
+      case 32: return launch_fused_bn<32, 16>(prm, tmap, n_tiles, st);
+      case 64: return launch_fused_bn<64, 16>(prm, tmap, n_tiles, st);
+      case 128: return launch_fused_bn<128, 16>(prm, tmap, n_tiles, st);
+      case 256: return launch_fused_bn<256, 16>(prm, tmap, n_tiles, st);
+    }
+  } else {
+    switch (bn) {
+      case 16: return launch_fused_bn<16, 4>(prm, tmap, n_tiles, st);
+      case 32: return launch_fused_bn<32, 4>(prm, tmap, n_tiles, st);
+      case 64: return launch_fused_bn<64, 4>(prm, tmap, n_tiles, st);
+    }
+  }
+  set_error(kBadArgument, "qa_conv_fused_dev: unsupported column tile");
+  return false;
+}
+
+}  // namespace qa
+
+QA_API int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream) {
+  qa::clear_error();
+  if (!desc) {
+    qa::set_error(qa::kBadArgument, "qa_conv_fused_dev: null descriptor");
+    return qa::last_status();
+  }
+  return qa::fused_conv(*desc, (cudaStream_t)stream) ? 0 : qa::last_status();
+}
