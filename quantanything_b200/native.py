@@ -165,6 +165,8 @@ class KernelLibrary:
     def gemm_f32(self, a, b):
         """``a[M,K] @ b[K,N]`` in float32 (native.py:207)."""
         a, b = _c(a, np.float32), _c(b, np.float32)
+        if a.shape[1] != b.shape[0]:
+            raise ValueError(f"gemm_f32: inner dimensions differ ({a.shape} @ {b.shape})")
         out = np.empty((a.shape[0], b.shape[1]), dtype=np.float32)
         self._lib.qa_gemm_f32(a.shape[0], b.shape[1], a.shape[1], _ptr(a),
                               _ptr(b), _ptr(out))
@@ -176,6 +178,8 @@ class KernelLibrary:
         (native.py:219)."""
         m, k = a.shape
         n = b.shape[1]
+        if b.shape[0] != k:
+            raise ValueError(f"gemm_int: inner dimensions differ ({a.shape} @ {b.shape})")
         if wide:
             a, b = _c(a, np.int32), _c(b, np.int32)
             out = np.empty((m, n), dtype=np.int64)
