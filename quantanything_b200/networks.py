@@ -1,0 +1,153 @@
+"""Seeded random-init graphs of the benchmark networks.
+
+No checkpoints or datasets are reachable, so the benchmark networks are
+built directly as graphs with random weights of the right architecture,
+already in the form the reference's load-time passes produce
+(graph_passes.py): BatchNorm folded into the preceding Conv, and
+``x * sigmoid(x)`` collapsed into one ``FusedElementwise`` node that the
+quantizer turns into a lookup table.
+
+* :func:`yolov8n_cls` -- YOLOv8n-cls (ultralytics ``yolov8n-cls.yaml`` at
+  depth 0.33 / width 0.25): Conv 3x3 s2 16, Conv 3x3 s2 32, C2f(32, n=1),
+  Conv s2 64, C2f(64, n=2), Conv s2 128, C2f(128, n=2), Conv s2 256,
+  C2f(256, n=1), Conv 1x1 1280, GlobalAveragePool, Linear 1000, Softmax;
+  every conv followed by SiLU; C2f bottlenecks with residual adds.
+* :func:`yolo_mini` -- the small YOLO-like test graph shape of the
+  reference's test-suite (stem, C2f-style split/add/concat, depthwise +
+  pointwise, GAP, Gemm, Softmax) at a configurable width.
+"""
+
+import numpy as np
+
+from quantanything_b200.graph import Graph, Node, ValueInfo
+
+
+class GraphBuilder:
+    """Accumulates nodes and initializers with unique names."""
+
+    def __init__(self, seed=0):
+        self.rng = np.random.default_rng(seed)
+        self.nodes, self.inits, self._n = [], {}, 0
+
+    def name(self, base):
+        self._n += 1
+        return f"{base}_{self._n}"
+
+    def const(self, value, base="const"):
+        n = self.name(base)
+        self.inits[n] = np.asarray(value)
+        return n
+
+    def op(self, op_type, inputs, n_out=1, **attrs):
+        outs = [self.name(op_type.lower()) for _ in range(n_out)]
+        self.nodes.append(Node(self.name(op_type), op_type, list(inputs), outs, attrs))
+        return outs[0] if n_out == 1 else outs
+
+    def conv(self, x, cin, cout, k=3, stride=1, pad=None, groups=1, bn=True):
+        """Conv with He-normal weights; a random inference BatchNorm is
+        folded in (w * gamma/sqrt(var+eps), bias beta - mean*gamma/sqrt(..))."""
+        pad = k // 2 if pad is None else pad
+        fan_in = (cin // groups) * k * k
+        w = self.rng.standard_normal((cout, cin // groups, k, k)) * np.sqrt(2.0 / fan_in)
+        if bn:
+            gamma = self.rng.uniform(0.5, 1.5, cout)
+            beta = self.rng.normal(0.0, 0.1, cout)
+            mean = self.rng.normal(0.0, 0.1, cout)
+            var = self.rng.uniform(0.5, 1.5, cout)
+            a = gamma / np.sqrt(var + 1e-3)
+            w = w * a.reshape(-1, 1, 1, 1)
+            b = beta - mean * a
+        else:
+            b = self.rng.normal(0.0, 0.05, cout)
+        return self.op("Conv", [x, self.const(w.astype(np.float32), "w"),
+                                self.const(b.astype(np.float32), "b")],
+                       kernel_shape=[k, k], strides=[stride, stride], pads=[pad] * 4,
+                       dilations=[1, 1], group=groups)
+
+    def silu(self, x):
+        """x * sigmoid(x) as the fused element-wise node the reference's
+        fusion pass emits (graph_passes.py:208-272)."""
+        s = self.name("sigmoid")
+        y = self.name("silu")
+        sub = [Node(self.name("Sigmoid"), "Sigmoid", [x], [s]),
+               Node(self.name("Mul"), "Mul", [x, s], [y])]
+        self.nodes.append(Node(self.name("SiLU") + "_fused", "FusedElementwise", [x], [y],
+                               {"nodes": sub, "consts": {}}))
+        return y
+
+    def conv_silu(self, x, cin, cout, k=3, stride=1, groups=1):
+        return self.silu(self.conv(x, cin, cout, k, stride, groups=groups))
+
+    def c2f(self, x, c1, c2, n=1, shortcut=True):
+        """C2f block: cv1 1x1 -> split in halves -> n bottlenecks (two 3x3
+        conv-SiLU, residual add) -> concat of all branches -> cv2 1x1."""
+        c = c2 // 2
+        y = self.conv_silu(x, c1, 2 * c, 1)
+        a, b = self.op("Split", [y, self.const(np.array([c, c], np.int64), "split")], n_out=2,
+                       axis=1)
+        branches, cur = [a, b], b
+        for _ in range(n):
+            t = self.conv_silu(cur, c, c, 3)
+            t = self.conv_silu(t, c, c, 3)
+            cur = self.op("Add", [cur, t]) if shortcut else t
+            branches.append(cur)
+        y = self.op("Concat", branches, axis=1)
+        return self.conv_silu(y, (2 + n) * c, c2, 1)
+
+    def head(self, x, cin, classes, hidden=None):
+        if hidden:
+            x = self.conv_silu(x, cin, hidden, 1)
+            cin = hidden
+        x = self.op("GlobalAveragePool", [x])
+        x = self.op("Flatten", [x], axis=1)
+        std = np.sqrt(1.0 / cin)
+        w = (self.rng.standard_normal((classes, cin)) * std).astype(np.float32)
+        b = self.rng.normal(0.0, 0.05, classes).astype(np.float32)
+        x = self.op("Gemm", [x, self.const(w, "fc_w"), self.const(b, "fc_b")], transB=1)
+        return self.op("Softmax", [x], axis=1)
+
+    def build(self, input_name, input_shape, output):
+        return Graph(self.nodes, self.inits, [ValueInfo(input_name, list(input_shape))],
+                     [output])
+
+
+def yolov8n_cls(seed=0, classes=1000, image=224):
+    """YOLOv8n-cls graph with random init (BN folded, SiLU fused)."""
+    b = GraphBuilder(seed)
+    x = "images"
+    y = b.conv_silu(x, 3, 16, 3, 2)
+    y = b.conv_silu(y, 16, 32, 3, 2)
+    y = b.c2f(y, 32, 32, 1)
+    y = b.conv_silu(y, 32, 64, 3, 2)
+    y = b.c2f(y, 64, 64, 2)
+    y = b.conv_silu(y, 64, 128, 3, 2)
+    y = b.c2f(y, 128, 128, 2)
+    y = b.conv_silu(y, 128, 256, 3, 2)
+    y = b.c2f(y, 256, 256, 1)
+    y = b.head(y, 256, classes, hidden=1280)
+    return b.build(x, ["N", 3, image, image], y)
+
+
+def yolo_mini(seed=0, size=32, classes=10, width=16):
+    """Small YOLO-like graph: stem, C2f-style split/add/concat, depthwise +
+    pointwise, GAP, Gemm, Softmax (the reference test-suite's structure)."""
+    b = GraphBuilder(seed)
+    x = "images"
+    y = b.conv_silu(x, 3, width, 3, 2)
+    y = b.conv_silu(y, width, 2 * width, 3, 2)
+    a, c = b.op("Split", [y, b.const(np.array([width, width], np.int64), "split")], n_out=2,
+                axis=1)
+    d = b.conv_silu(c, width, width, 3)
+    d = b.op("Add", [c, b.conv_silu(d, width, width, 3)])
+    y = b.op("Concat", [a, c, d], axis=1)
+    y = b.conv_silu(y, 3 * width, 4 * width, 1)
+    y = b.conv_silu(y, 4 * width, 4 * width, 3, groups=4 * width)
+    y = b.conv_silu(y, 4 * width, 8 * width, 1)
+    y = b.head(y, 8 * width, classes)
+    return b.build(x, ["N", 3, size, size], y)
+
+
+def images(n, size=224, seed=1):
+    """N(0, 1) pixels clipped to +-3 (the configuration's input distribution)."""
+    rng = np.random.default_rng(seed)
+    return np.clip(rng.standard_normal((n, 3, size, size)), -3, 3).astype(np.float32)
