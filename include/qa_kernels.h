@@ -171,6 +171,7 @@ typedef struct qa_fused_conv_desc {
   int64_t N, H, W, C;     /* C: channels per tap, multiple of 16 (or 4) */
   int64_t KH, KW, SH, SW, PH, PW, DH, DW, OH, OW;
   int64_t Cout;
+  int64_t groups;         /* >1: grouped / depthwise (C = channels per group) */
   const void* w;          /* packed weights (int8) */
   int64_t w_rows, w_kp;
   const int64_t* bias;    /* per channel, may be NULL; includes -x_zp*sum(w) */
@@ -193,6 +194,56 @@ typedef struct qa_fused_conv_desc {
 } qa_fused_conv_desc;
 
 int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream);
+
+/* Graph input: float32 NCHW -> quantized bytes NHWC with `pix_stride`
+ * channels per pixel (channels C.. hold zp), same rounding as
+ * qa_quantize_f32. */
+int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C, int64_t H, int64_t W,
+                            int64_t pix_stride, double scale, int64_t zp, int64_t qmin,
+                            int64_t qmax, void* stream);
+
+/* GlobalAveragePool (quant_layers.py:563-590): int64 sum of centred bytes
+ * over HW pixels, requantized with the scalar (mult, shift). */
+int qa_gap_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int64_t N, int64_t HW,
+               int64_t C, int64_t zp_in, int64_t mult, int64_t shift, int64_t zp_out,
+               int64_t qmin, int64_t qmax, void* y, int64_t y_pix_stride, void* stream);
+
+/* Softmax float fallback over rows of C bytes (quant_layers.py:195-205):
+ * dequantize, float64 softmax, quantize; writes the int32 result (q_out) and
+ * / or its float32 dequantization on the (y_scale, y_zp) grid (y_out). */
+int qa_softmax_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int64_t N, int64_t C,
+                   double in_scale, int64_t in_zp, double out_scale, int64_t out_zp,
+                   int64_t qmin, int64_t qmax, int32_t* q_out, float* y_out, double y_scale,
+                   int64_t y_zp, void* stream);
+
+/* Standalone byte-tensor layers over [rows, C] views (row = pixel). */
+int qa_lut_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
+                     int64_t y_stride, int64_t rows, int64_t C, int64_t offset,
+                     const int32_t* lut, int64_t lut_len, void* stream);
+int qa_add_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, const void* b,
+                     int64_t b_stride, int64_t b_signed, void* y, int64_t y_stride,
+                     int64_t rows, int64_t C, int64_t za, int64_t ma, int64_t sa, int64_t zb,
+                     int64_t mb, int64_t sb, int64_t sign, int64_t zo, int64_t qmin,
+                     int64_t qmax, void* stream);
+int qa_rescale_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
+                         int64_t y_stride, int64_t rows, int64_t C, int64_t identity,
+                         int64_t zp_in, int64_t m, int64_t s, int64_t zp_out, int64_t qmin,
+                         int64_t qmax, void* stream);
+int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
+                         int64_t y_stride, int64_t N, int64_t H, int64_t W, int64_t C,
+                         int64_t KH, int64_t KW, int64_t SH, int64_t SW, int64_t PH, int64_t PW,
+                         int64_t DH, int64_t DW, int64_t OH, int64_t OW, int64_t pad_value,
+                         void* stream);
+
+/* Layout conversion between NHWC byte views and NCHW int32 tensors. */
+int qa_bytes_to_i32_dev(const void* x, int64_t x_stride, int64_t x_signed, int32_t* y,
+                        int64_t N, int64_t HW, int64_t C, void* stream);
+int qa_i32_to_bytes_dev(const int32_t* x, void* y, int64_t y_stride, int64_t N, int64_t HW,
+                        int64_t C, void* stream);
+
+/* Synchronizes `stream` and reports (then clears) a bounded-wait timeout
+ * recorded by any kernel on this device. */
+int qa_device_status_dev(void* stream);
 
 #ifdef __cplusplus
 }

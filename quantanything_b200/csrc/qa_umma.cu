@@ -21,6 +21,7 @@
 #include "qa_fixedpoint.cuh"
 #include "qa_ptx.cuh"
 #include "qa_umma.cuh"
+#include "qa_fused_epilogue.cuh"
 
 namespace qa {
 
@@ -74,11 +75,6 @@ template <int BN, int PA, int PB, int kStages>
 constexpr size_t umma_smem_bytes() {
   return 1024 /* alignment slack */ + (size_t)kStages * TileShape<BN, PA, PB>::kStageBytes +
          (2 * kStages + 1) * 8 + 16;
-}
-
-// Value of a stored activation byte.
-__device__ __forceinline__ int64_t byte_value(uint8_t b, int is_signed) {
-  return is_signed ? (int64_t)(int8_t)b : (int64_t)b;
 }
 
 template <int BN, int PA, int PB, int kChunk, int kEpi, int kStages>
@@ -310,36 +306,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
           }
         } else {
           static_assert(TS::kNumAcc == 1, "fused epilogue is 8-bit only");
-          const FusedEpilogue& e = p.epi;
-          const int64_t x = (int64_t)(int32_t)v[0][j] + (e.bias ? e.bias[n] : 0);
-          int64_t q;
-          if (e.fast) {
-            q = requant_fast(x, e.mult[n], (int)(31 + e.shift[n]), e.zp, e.qmin, e.qmax);
-          } else {
-            q = requant_exact(x, e.mult[n], e.shift[n], e.zp, e.qmin, e.qmax);
-          }
-          if (e.lut) {
-            int64_t idx = q - e.lut_offset;
-            idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
-            q = __ldg(e.lut + idx);
-          }
-          if (e.res) {
-            const int64_t a = byte_value(e.res[m * e.res_pix_stride + n], e.res_signed);
-            I128 ta = mbqm(a - e.za, e.ma, e.sa);
-            I128 tb = mbqm(q - e.zb, e.mb, e.sb);
-            if (e.sign < 0) tb = neg_i128(tb);
-            q = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
-          }
-          if (e.out) e.out[m * e.out_pix_stride + n] = (uint8_t)q;
-          if (e.out2) {
-            int64_t q2;
-            if (e.r_identity) {
-              q2 = q < e.r_qmin ? e.r_qmin : (q > e.r_qmax ? e.r_qmax : q);
-            } else {
-              q2 = requant_exact(q - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
-            }
-            e.out2[m * e.out2_pix_stride + n] = (uint8_t)q2;
-          }
+          fused_epilogue_store(p.epi, (int64_t)(int32_t)v[0][j], m, n);
         }
       }
     }
@@ -644,6 +611,9 @@ namespace qa {
 
 constexpr int kFusedStages = 4;
 
+bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);
+bool fused_conv_grouped(const qa_fused_conv_desc& d, cudaStream_t st);
+
 template <int BN, int kChunk>
 static bool launch_fused_bn(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n_tiles,
                             cudaStream_t st) {
@@ -657,6 +627,7 @@ static bool fused_conv(const qa_fused_conv_desc& d, cudaStream_t st) {
     set_error(kBadArgument, "qa_conv_fused_dev: invalid geometry");
     return false;
   }
+  if (d.groups > 1) return fused_conv_grouped(d, st);
   const int chunk = (d.C % 16 == 0 && d.x_pix_stride % 16 == 0) ? 16
                     : (d.C % 4 == 0 && d.x_pix_stride % 4 == 0) ? 4
                                                                  : 0;
@@ -708,41 +679,7 @@ static bool fused_conv(const qa_fused_conv_desc& d, cudaStream_t st) {
   prm.n_valid = (int32_t)d.Cout;
   prm.ohw = d.OH * d.OW;
   prm.status = device_status_word();
-  FusedEpilogue& e = prm.epi;
-  e.bias = d.bias;
-  e.mult = d.mult;
-  e.shift = d.shift;
-  e.zp = d.zp;
-  e.qmin = d.qmin;
-  e.qmax = d.qmax;
-  e.fast = d.fast ? 1 : 0;
-  e.lut = d.lut;
-  e.lut_offset = d.lut_offset;
-  e.lut_len = d.lut_len;
-  e.res = static_cast<const uint8_t*>(d.res);
-  e.res_pix_stride = d.res_pix_stride;
-  e.res_signed = d.res_signed ? 1 : 0;
-  e.za = d.za;
-  e.ma = d.ma;
-  e.sa = d.sa;
-  e.zb = d.zb;
-  e.mb = d.mb;
-  e.sb = d.sb;
-  e.sign = d.sign;
-  e.add_zo = d.add_zo;
-  e.add_qmin = d.add_qmin;
-  e.add_qmax = d.add_qmax;
-  e.out = static_cast<uint8_t*>(d.out);
-  e.out_pix_stride = d.out_pix_stride;
-  e.out2 = static_cast<uint8_t*>(d.out2);
-  e.out2_pix_stride = d.out2_pix_stride;
-  e.r_identity = d.r_identity ? 1 : 0;
-  e.r_zp_in = d.r_zp_in;
-  e.r_m = d.r_m;
-  e.r_s = d.r_s;
-  e.r_zp_out = d.r_zp_out;
-  e.r_qmin = d.r_qmin;
-  e.r_qmax = d.r_qmax;
+  fill_fused_epilogue(prm.epi, d);
   if (chunk == 16) {
     switch (bn) {
       case 16: return launch_fused_bn<16, 16>(prm, tmap, n_tiles, st);

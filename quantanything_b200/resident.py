@@ -1,0 +1,680 @@
+"""Device-resident, fused execution of a prepared QuantContainer.
+
+The reference executes one layer at a time on host int32 arrays
+(quant_container.py:135-193).  ResidentNet runs the same integer arithmetic
+with every activation resident in HBM as int8 / uint8 NHWC bytes and with
+the layer chain fused into few kernels:
+
+* Conv / Gemm + requantize + activation LUT + residual Add + rescaled copy
+  into a Concat slice -> one tensor-core launch (``qa_conv_fused_dev``);
+* Split and Flatten -> zero-copy channel / shape views;
+* Concat -> producers write straight into the concatenated buffer;
+* GlobalAveragePool -> one reduction kernel; Softmax -> one float64
+  fallback kernel that also emits the graph output's dequantized float32;
+* graph-input quantization -> one kernel writing NHWC bytes.
+
+All parameters come from the container's prepared layers (``w_centered``,
+``bias_int``, ``q_mult``, ``shift``, ``lut``, ...), so results are bit-exact
+with the reference's integer pass.  The launch sequence is captured once in
+a CUDA graph; :meth:`ResidentNet.run` is the public host-to-host call
+(pinned host input -> device -> output back to the host).
+"""
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from quantanything_b200 import native
+from quantanything_b200.layers import (
+    ActivationQuantize,
+    AddQuantize,
+    ConcatQuantize,
+    ConvQuantize,
+    GemmQuantize,
+    GlobalAveragePoolQuantize,
+    ShapingQuantize,
+)
+
+_I64 = ctypes.c_int64
+_P = ctypes.c_void_p
+
+
+class FusedConvDesc(ctypes.Structure):
+    """ctypes mirror of ``qa_fused_conv_desc`` (include/qa_kernels.h)."""
+
+    _fields_ = [
+        ("x", _P), ("x_pix_stride", _I64), ("x_signed", _I64), ("x_zp", _I64),
+        ("N", _I64), ("H", _I64), ("W", _I64), ("C", _I64),
+        ("KH", _I64), ("KW", _I64), ("SH", _I64), ("SW", _I64), ("PH", _I64), ("PW", _I64),
+        ("DH", _I64), ("DW", _I64), ("OH", _I64), ("OW", _I64),
+        ("Cout", _I64), ("groups", _I64),
+        ("w", _P), ("w_rows", _I64), ("w_kp", _I64),
+        ("bias", _P), ("mult", _P), ("shift", _P),
+        ("zp", _I64), ("qmin", _I64), ("qmax", _I64), ("fast", _I64),
+        ("lut", _P), ("lut_offset", _I64), ("lut_len", _I64),
+        ("res", _P), ("res_pix_stride", _I64), ("res_signed", _I64),
+        ("za", _I64), ("ma", _I64), ("sa", _I64), ("zb", _I64), ("mb", _I64), ("sb", _I64),
+        ("sign", _I64), ("add_zo", _I64), ("add_qmin", _I64), ("add_qmax", _I64),
+        ("out", _P), ("out_pix_stride", _I64),
+        ("out2", _P), ("out2_pix_stride", _I64),
+        ("r_identity", _I64), ("r_zp_in", _I64), ("r_m", _I64), ("r_s", _I64),
+        ("r_zp_out", _I64), ("r_qmin", _I64), ("r_qmax", _I64),
+        ("block_n", _I64),
+    ]
+
+
+_DEV_SIGNATURES = {
+    "qa_conv_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P]),
+    "qa_quantize_to_nhwc_dev": (ctypes.c_int, [_P, _P] + [_I64] * 5 + [ctypes.c_double]
+                                + [_I64] * 3 + [_P]),
+    "qa_gap_dev": (ctypes.c_int, [_P] + [_I64] * 11 + [_P, _I64, _P]),
+    "qa_softmax_dev": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, ctypes.c_double, _I64,
+                                      ctypes.c_double, _I64, _I64, _I64, _P, _P,
+                                      ctypes.c_double, _I64, _P]),
+    "qa_lut_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64,
+                                        _P]),
+    "qa_add_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P] + [_I64] * 13
+                         + [_P]),
+    "qa_rescale_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 10 + [_P]),
+    "qa_maxpool_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 16 + [_P]),
+    "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
+    "qa_device_status_dev": (ctypes.c_int, [_P]),
+}
+
+
+def device_api(lib):
+    """Declares the device-pointer entry points on a loaded KernelLibrary."""
+    raw = lib.raw
+    if not getattr(raw, "_qa_dev_declared", False):
+        for name, (res, args) in _DEV_SIGNATURES.items():
+            fn = getattr(raw, name)
+            fn.restype, fn.argtypes = res, args
+        raw._qa_dev_declared = True
+    return raw
+
+
+def _check(lib, rc, what):
+    if rc != 0:
+        msg = lib.raw.qa_last_error().decode(errors="replace")
+        lib.raw.qa_clear_error()
+        raise native.KernelLibraryError(f"{what}: {msg}")
+
+
+def _round_up(v, m):
+    return (v + m - 1) // m * m
+
+
+@dataclass
+class View:
+    """An NHWC byte tensor (or a channel slice of one) resident on the GPU."""
+
+    buf: torch.Tensor
+    offset: int
+    pix_stride: int
+    N: int
+    H: int
+    W: int
+    C: int
+    signed: bool
+    qp: object = None
+
+    @property
+    def ptr(self):
+        return self.buf.data_ptr() + self.offset
+
+    def channel_slice(self, c0, c):
+        return View(self.buf, self.offset + c0, self.pix_stride, self.N, self.H, self.W, c,
+                    self.signed, self.qp)
+
+
+@dataclass
+class _ConvStep:
+    layer: object
+    desc: FusedConvDesc
+    keep: list = field(default_factory=list)
+
+
+class UnsupportedGraph(NotImplementedError):
+    """The graph has a layer the resident executor does not cover."""
+
+
+class ResidentNet:
+    """Fused device-resident integer inference of a prepared container."""
+
+    def __init__(self, container, batch, device=None):
+        if not container.calibrated:
+            raise ValueError("container is not calibrated")
+        self.c = container
+        self.graph = container.graph
+        self.batch = int(batch)
+        self.device = torch.device(device or "cuda")
+        self.lib = container.lib
+        device_api(self.lib)
+        self.bits, self.signed = container.layers[0].num_bits, container.layers[0].signed
+        if self.bits > 8:
+            raise UnsupportedGraph("the resident executor runs 8-bit graphs")
+        self._keep = []
+        self.steps = []
+        self.launch_count = 0
+        self._graph = None
+        self._plan()
+
+    # ------------------------------------------------------------- helpers --
+    def _alloc(self, nbytes):
+        t = torch.empty(int(nbytes) + 64, dtype=torch.uint8, device=self.device)
+        self._keep.append(t)
+        return t
+
+    def _dev(self, arr, dtype):
+        t = torch.from_numpy(np.ascontiguousarray(arr, dtype=dtype)).to(self.device)
+        self._keep.append(t)
+        return t
+
+    def _new_view(self, N, H, W, C, qp, pix_stride=None):
+        stride = pix_stride or (C if C % 16 == 0 else _round_up(C, 16))
+        return View(self._alloc(N * H * W * stride), 0, stride, N, H, W, C, self.signed, qp)
+
+    # ---------------------------------------------------------------- plan --
+    def _plan(self):
+        g, c = self.graph, self.c
+        layers = {l.name: l for l in c.layers}
+        consumers = {}
+        for node in g.nodes:
+            for i in node.inputs:
+                if i:
+                    consumers.setdefault(i, []).append(node)
+        self._consumers = consumers
+        if len(g.inputs) != 1 or len(g.outputs) != 1:
+            raise UnsupportedGraph("single-input single-output graphs only")
+        in_name = g.inputs[0].name
+        in_shape = g.inputs[0].shape
+        self.in_shape = (self.batch, int(in_shape[1]), int(in_shape[2]), int(in_shape[3]))
+        qp_in = c.qparams[in_name]
+        Cin = self.in_shape[1]
+        stride_in = Cin if Cin % 16 == 0 else _round_up(Cin, 4)
+        views = {in_name: View(self._alloc(self.batch * self.in_shape[2] * self.in_shape[3]
+                                           * stride_in), 0, stride_in, self.batch,
+                               self.in_shape[2], self.in_shape[3], Cin, self.signed, qp_in)}
+        self.x_dev = torch.empty(self.in_shape, dtype=torch.float32, device=self.device)
+        self.steps.append(("quantize", in_name))
+        self._in_view = views[in_name]
+
+        fused_away = set()   # layer names executed inside another layer's kernel
+        concat_slot = {}     # tensor name -> (concat layer, input index)
+        # Concat buffers are planned when the concat's first input is produced;
+        # pre-compute every concat's output view up front (shapes from inputs).
+        self._shapes = self._infer_shapes()
+        for node in g.nodes:
+            layer = layers[node.name]
+            if isinstance(layer, ConcatQuantize):
+                if node.attr("axis") not in (1, -3):
+                    raise UnsupportedGraph("Concat must be along channels")
+                N, C, H, W = self._shapes[node.outputs[0]]
+                views[node.outputs[0]] = self._new_view(N, H, W, C, layer.out_qp[0])
+                for idx, name in enumerate(node.inputs):
+                    concat_slot.setdefault(name, []).append((layer, idx))
+        self._concat_slot = concat_slot
+        self._views = views
+        self._concat_done = {}
+        self._producer_step = {}
+
+        for node in g.nodes:
+            layer = layers[node.name]
+            if node.name in fused_away:
+                continue
+            if isinstance(layer, (ConvQuantize, GemmQuantize)):
+                self._plan_contraction(layer, layers, fused_away)
+            elif isinstance(layer, ShapingQuantize) and node.op_type == "Split":
+                self._plan_split(layer)
+            elif isinstance(layer, ShapingQuantize) and node.op_type in ("Flatten", "Reshape",
+                                                                         "Squeeze"):
+                self._plan_flatten(layer)
+            elif isinstance(layer, ConcatQuantize):
+                self._plan_concat(layer)
+            elif isinstance(layer, GlobalAveragePoolQuantize):
+                self._plan_gap(layer)
+            elif isinstance(layer, ShapingQuantize) and node.op_type == "MaxPool":
+                self._plan_maxpool(layer)
+            elif isinstance(layer, ActivationQuantize):
+                self._plan_lut(layer)
+            elif isinstance(layer, AddQuantize):
+                self._plan_add(layer)
+            elif node.op_type == "Softmax" and node.outputs[0] in g.outputs:
+                self._plan_softmax(layer)
+            else:
+                raise UnsupportedGraph(f"{node.op_type} ({node.name}) has no resident kernel")
+        out = g.outputs[0]
+        if out not in self._outputs_f32:
+            raise UnsupportedGraph("the graph output must be produced by the Softmax fallback")
+
+    # --------------------------------------------------------- shape pass --
+    def _infer_shapes(self):
+        g, layers = self.graph, {l.name: l for l in self.c.layers}
+        shapes = {g.inputs[0].name: self.in_shape}
+        for node in g.nodes:
+            layer = layers[node.name]
+            ins = [shapes.get(i) for i in node.inputs if i]
+            s = ins[0]
+            if isinstance(layer, ConvQuantize):
+                strides, pads, dil, groups = layer.geometry(s)
+                g_ = native.conv_geometry(s, layer.w_q.shape, strides, pads, dil, groups)
+                shapes[node.outputs[0]] = (s[0], layer.w_q.shape[0], g_[13], g_[14])
+            elif isinstance(layer, GemmQuantize):
+                shapes[node.outputs[0]] = (s[0], layer.w_q.shape[1], 1, 1)
+            elif node.op_type == "Split":
+                sizes = list(np.asarray(g.initializers[node.inputs[1]]).reshape(-1)) if len(
+                    node.inputs) > 1 and node.inputs[1] else [s[1] // len(node.outputs)] * len(
+                    node.outputs)
+                for o, sz in zip(node.outputs, sizes):
+                    shapes[o] = (s[0], int(sz), s[2], s[3])
+            elif node.op_type == "Concat":
+                shapes[node.outputs[0]] = (s[0], sum(x[1] for x in ins), s[2], s[3])
+            elif node.op_type == "GlobalAveragePool":
+                shapes[node.outputs[0]] = (s[0], s[1], 1, 1)
+            elif node.op_type in ("Flatten", "Reshape", "Squeeze"):
+                shapes[node.outputs[0]] = (s[0], s[1] * s[2] * s[3], 1, 1)
+            elif node.op_type == "MaxPool":
+                from quantanything_b200.float_ops import pool_geometry
+
+                k, st, dl, pd = pool_geometry(node, s)
+                oh = (s[2] + pd[0] + pd[2] - dl[0] * (k[0] - 1) - 1) // st[0] + 1
+                ow = (s[3] + pd[1] + pd[3] - dl[1] * (k[1] - 1) - 1) // st[1] + 1
+                shapes[node.outputs[0]] = (s[0], s[1], oh, ow)
+            else:
+                shapes[node.outputs[0]] = s
+        return shapes
+
+    # ------------------------------------------------------- destinations --
+    def _only_consumer(self, tensor):
+        cons = self._consumers.get(tensor, [])
+        return cons[0] if len(cons) == 1 and tensor not in self.graph.outputs else None
+
+    def _destination(self, tensor, qp, N, H, W, C):
+        """(primary view or None, concat copy spec or None) for a produced tensor.
+
+        A tensor whose only consumer is a Concat on the same grid is written
+        straight into the concat slice; one with other consumers gets its own
+        buffer plus a (rescaled) copy into the slice."""
+        slots = self._concat_slot.get(tensor, [])
+        cons = self._consumers.get(tensor, [])
+        copy = None
+        if slots:
+            concat, idx = slots[0]
+            out_view = self._views[concat.node.outputs[0]]
+            c0 = sum(self._shapes[n][1] for n in concat.node.inputs[:idx])
+            slice_view = out_view.channel_slice(c0, C)
+            if len(cons) == 1 and concat.same_grid(idx):
+                self._concat_done[(concat.name, idx)] = True
+                return slice_view, None
+            copy = (concat, idx, slice_view)
+        view = self._new_view(N, H, W, C, qp)
+        return view, copy
+
+    # ------------------------------------------------------ contractions --
+    def _pack_weights(self, layer, x_view, taps_c):
+        if isinstance(layer, GemmQuantize):
+            wc = np.ascontiguousarray(layer.w_centered.T).astype(np.int64)  # [N, K]
+            cout, kh, kw, groups, cg = wc.shape[0], 1, 1, 1, wc.shape[1]
+            w4 = wc.reshape(cout, cg, 1, 1)
+        else:
+            w4 = layer.w_centered.astype(np.int64)
+            cout, cg, kh, kw = w4.shape
+            groups = layer.node.attr("group", 1)
+        if w4.min() < -128 or w4.max() > 127:
+            raise UnsupportedGraph(f"{layer.name}: centred weights exceed int8")
+        ct = taps_c if groups == 1 else cg
+        bn = 16 if cout <= 16 else 32 if cout <= 32 else 64 if cout <= 64 else (
+            128 if cout <= 128 else 256)
+        if groups == 1 and ct % 16 != 0:
+            bn = min(bn, 64)
+        rows = _round_up(cout, bn)
+        k = kh * kw * ct
+        kp = _round_up(k, 16)
+        packed = np.zeros((rows, kp), np.int8)
+        wt = np.zeros((cout, kh, kw, ct), np.int64)
+        wt[:, :, :, :cg] = np.transpose(w4, (0, 2, 3, 1))
+        packed[:cout, :k] = wt.reshape(cout, k)
+        colsum = wt.reshape(cout, k).sum(axis=1)
+        abssum = np.abs(wt.reshape(cout, k)).sum(axis=1)
+        return packed, rows, kp, bn, groups, ct, colsum, abssum
+
+    def _plan_contraction(self, layer, layers, fused_away):
+        node = layer.node
+        x_view = self._views[node.inputs[0]]
+        N, _, H, W = self._shapes[node.inputs[0]]
+        if isinstance(layer, GemmQuantize):
+            if (x_view.H, x_view.W) != (1, 1):
+                raise UnsupportedGraph("Gemm input must be a flattened vector")
+            geo = dict(KH=1, KW=1, SH=1, SW=1, PH=0, PW=0, DH=1, DW=1, OH=1, OW=1)
+            pads_bottom = (0, 0)
+        else:
+            strides, pads, dil, groups = layer.geometry((N, x_view.C, H, W))
+            g_ = native.conv_geometry((N, x_view.C, H, W), layer.w_q.shape, strides, pads, dil,
+                                      groups)
+            geo = dict(KH=g_[5], KW=g_[6], SH=g_[7], SW=g_[8], PH=g_[9], PW=g_[10], DH=g_[11],
+                       DW=g_[12], OH=g_[13], OW=g_[14])
+            pads_bottom = (pads[2], pads[3])
+        taps_c = x_view.C
+        if taps_c % 16 != 0:
+            taps_c = _round_up(taps_c, 4)
+            if taps_c > x_view.pix_stride and x_view.offset + taps_c > x_view.pix_stride:
+                raise UnsupportedGraph(f"{layer.name}: input channels not 4-aligned")
+        packed, rows, kp, bn, groups, ct, colsum, abssum = self._pack_weights(layer, x_view,
+                                                                              taps_c)
+        cout = layer.w_q.shape[1] if isinstance(layer, GemmQuantize) else layer.w_q.shape[0]
+        x_zp = layer.in_zp
+        bias = (layer.bias_int.astype(np.int64) if layer.bias_int is not None
+                else np.zeros(cout, np.int64)) - x_zp * colsum
+        mult = np.broadcast_to(np.asarray(layer.q_mult, np.int64), (cout,)).copy()
+        shift = np.broadcast_to(np.asarray(layer.shift, np.int64), (cout,)).copy()
+        xmax = max(abs(layer.in_qmin), abs(layer.in_qmax))
+        bound = xmax * abssum + np.abs(bias)
+        ts = 31 + shift
+        fast = bool(np.all((ts >= 1) & (ts <= 62)) and all(
+            int(b) * abs(int(m)) + (1 << (int(t) - 1)) < (1 << 62)
+            for b, m, t in zip(bound, mult, ts)))
+        d = FusedConvDesc()
+        d.x, d.x_pix_stride, d.x_signed, d.x_zp = x_view.ptr, x_view.pix_stride, int(
+            x_view.signed), int(x_zp)
+        d.N, d.H, d.W, d.C = N, H, W, ct
+        for k_, v in geo.items():
+            setattr(d, k_, int(v))
+        d.Cout, d.groups = cout, groups
+        wdev = self._dev(packed, np.int8)
+        d.w, d.w_rows, d.w_kp = wdev.data_ptr(), rows, kp
+        bdev, mdev, sdev = (self._dev(bias, np.int64), self._dev(mult, np.int64),
+                            self._dev(shift, np.int64))
+        d.bias, d.mult, d.shift = bdev.data_ptr(), mdev.data_ptr(), sdev.data_ptr()
+        d.zp, d.qmin, d.qmax, d.fast = layer.out_zp, layer.out_qmin, layer.out_qmax, int(fast)
+        d.block_n = bn if groups == 1 else 0
+        produced = node.outputs[0]
+        out_qp = layer.out_qp[0]
+        # activation LUT fused when it is the only consumer
+        act = self._only_consumer(produced)
+        if act is not None and isinstance(layers[act.name], ActivationQuantize):
+            a = layers[act.name]
+            ldev = self._dev(a.lut, np.int32)
+            d.lut, d.lut_offset, d.lut_len = ldev.data_ptr(), int(a.lut_offset), len(a.lut)
+            fused_away.add(act.name)
+            produced, out_qp = act.outputs[0], a.out_qp[0]
+            # residual Add fused when it is the only consumer of the LUT output
+            add = self._only_consumer(produced)
+            if add is not None and isinstance(layers[add.name], AddQuantize):
+                al = layers[add.name]
+                other = [i for i in add.inputs if i != produced]
+                if len(other) == 1 and other[0] in self._views and (
+                        add.inputs[1] == produced or al._sign == 1):
+                    res = self._views[other[0]]
+                    (ma, sa), (mb, sb) = al._mult
+                    qa, qb = al.in_qp
+                    if add.inputs[1] == produced:  # out = res (a) + sign * ours (b)
+                        d.za, d.ma, d.sa, d.zb, d.mb, d.sb = qa.zp, ma, sa, qb.zp, mb, sb
+                    else:  # ours is operand a, sign == +1: the sum commutes
+                        d.za, d.ma, d.sa, d.zb, d.mb, d.sb = qb.zp, mb, sb, qa.zp, ma, sa
+                    d.res, d.res_pix_stride, d.res_signed = res.ptr, res.pix_stride, int(
+                        res.signed)
+                    o = al.out_qp[0]
+                    d.sign, d.add_zo, d.add_qmin, d.add_qmax = al._sign, o.zp, o.qmin, o.qmax
+                    fused_away.add(add.name)
+                    produced, out_qp = add.outputs[0], o
+        NO, HO, WO = (N, geo["OH"], geo["OW"])
+        view, copy = self._destination(produced, out_qp, NO, HO, WO, cout)
+        if view is not None and (self._consumers.get(produced) or produced in self.graph.outputs
+                                 or copy is None):
+            d.out, d.out_pix_stride = view.ptr, view.pix_stride
+            self._views[produced] = view
+        if copy is not None:
+            concat, idx, sl = copy
+            self._attach_copy(d, concat, idx, sl)
+            cons = self._consumers.get(produced, [])
+            if len(cons) == 1:  # the concat is the only reader: no primary store
+                d.out = None
+        step = _ConvStep(layer, d)
+        self._producer_step[produced] = step
+        self.steps.append(("conv", step))
+
+    def _attach_copy(self, d, concat, idx, slice_view):
+        (m, s) = concat._mult[idx]
+        qp, o = concat.in_qp[idx], concat.out_qp[0]
+        d.out2, d.out2_pix_stride = slice_view.ptr, slice_view.pix_stride
+        d.r_identity = int(concat.same_grid(idx))
+        d.r_zp_in, d.r_m, d.r_s, d.r_zp_out, d.r_qmin, d.r_qmax = qp.zp, m, s, o.zp, o.qmin, o.qmax
+        self._concat_done[(concat.name, idx)] = True
+
+    # --------------------------------------------------------- other ops --
+    def _plan_split(self, layer):
+        node = layer.node
+        src = self._views[node.inputs[0]]
+        c0 = 0
+        for o in node.outputs:
+            C = self._shapes[o][1]
+            self._views[o] = src.channel_slice(c0, C)
+            c0 += C
+        # Split outputs that land, in order, in consecutive slots of one
+        # Concat (the C2f pattern) are copied by the producer of the split
+        # input as a single rescaled second output; otherwise _plan_concat
+        # emits standalone copies.
+        step = self._producer_step.get(node.inputs[0])
+        if step is None or step.desc.out2:
+            return
+        slots = [self._concat_slot.get(o, []) for o in node.outputs]
+        if any(len(sl) != 1 for sl in slots):
+            return
+        concat = slots[0][0][0]
+        idxs = [sl[0][1] for sl in slots]
+        if any(sl[0][0] is not concat for sl in slots) or idxs != list(
+                range(idxs[0], idxs[0] + len(idxs))):
+            return
+        if any(concat._mult[i] != concat._mult[idxs[0]]
+               or concat.same_grid(i) != concat.same_grid(idxs[0]) for i in idxs):
+            return
+        if c0 != src.C:
+            return
+        start = sum(self._shapes[n][1] for n in concat.node.inputs[:idxs[0]])
+        out = self._views[concat.node.outputs[0]]
+        self._attach_copy(step.desc, concat, idxs[0], out.channel_slice(start, c0))
+        for i in idxs:
+            self._concat_done[(concat.name, i)] = True
+
+    def _plan_flatten(self, layer):
+        node = layer.node
+        src = self._views[node.inputs[0]]
+        if (src.H, src.W) != (1, 1):
+            if src.pix_stride != src.C:
+                raise UnsupportedGraph("Flatten of a strided spatial tensor")
+            raise UnsupportedGraph("Flatten of a spatial tensor (NCHW order) is not resident")
+        self._views[node.outputs[0]] = src
+
+    def _plan_concat(self, layer):
+        node = layer.node
+        out = self._views[node.outputs[0]]
+        c0 = 0
+        for idx, name in enumerate(node.inputs):
+            C = self._shapes[name][1]
+            if not self._concat_done.get((layer.name, idx)):
+                self.steps.append(("rescale", (layer, idx, self._views[name],
+                                               out.channel_slice(c0, C))))
+            c0 += C
+
+    def _plan_gap(self, layer):
+        node = layer.node
+        x = self._views[node.inputs[0]]
+        N, C, H, W = self._shapes[node.inputs[0]]
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, 1, 1, C)
+        if copy is not None:
+            raise UnsupportedGraph("GlobalAveragePool feeding a Concat")
+        self._views[node.outputs[0]] = view
+        self.steps.append(("gap", (layer, x, view, H * W)))
+
+    def _plan_maxpool(self, layer):
+        node = layer.node
+        x = self._views[node.inputs[0]]
+        N, C, OH, OW = self._shapes[node.outputs[0]]
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, OH, OW, C)
+        self._views[node.outputs[0]] = view
+        self.steps.append(("maxpool", (layer, x, view)))
+        if copy is not None:
+            self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
+
+    def _plan_lut(self, layer):
+        node = layer.node
+        x = self._views[node.inputs[0]]
+        N, C, H, W = self._shapes[node.outputs[0]]
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, H, W, C)
+        self._views[node.outputs[0]] = view
+        self.steps.append(("lut", (layer, x, view, self._dev(layer.lut, np.int32))))
+        if copy is not None:
+            self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
+
+    def _plan_add(self, layer):
+        node = layer.node
+        a, b = (self._views[i] for i in node.inputs)
+        N, C, H, W = self._shapes[node.outputs[0]]
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, H, W, C)
+        self._views[node.outputs[0]] = view
+        self.steps.append(("add", (layer, a, b, view)))
+        if copy is not None:
+            self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
+
+    def _plan_softmax(self, layer):
+        node = layer.node
+        x = self._views[node.inputs[0]]
+        N, C = self._shapes[node.inputs[0]][:2]
+        self.out_f32 = torch.empty((N, C), dtype=torch.float32, device=self.device)
+        self.out_q = torch.empty((N, C), dtype=torch.int32, device=self.device)
+        self._outputs_f32 = {node.outputs[0]: self.out_f32}
+        self.steps.append(("softmax", (layer, x)))
+
+    _outputs_f32 = {}
+
+    # ------------------------------------------------------------- launch --
+    def _launch_all(self, stream):
+        raw = self.lib.raw
+        st = ctypes.c_void_p(stream)
+        n = 0
+        for kind, payload in self.steps:
+            if kind == "quantize":
+                v, qp = self._in_view, self.c.qparams[payload]
+                N, C, H, W = self.in_shape
+                rc = raw.qa_quantize_to_nhwc_dev(self.x_dev.data_ptr(), v.ptr, N, C, H, W,
+                                                 v.pix_stride, float(qp.scale), qp.zp, qp.qmin,
+                                                 qp.qmax, st)
+            elif kind == "conv":
+                rc = raw.qa_conv_fused_dev(ctypes.byref(payload.desc), st)
+            elif kind == "rescale":
+                concat, idx, src, dst = payload
+                m, s = concat._mult[idx]
+                qp, o = concat.in_qp[idx], concat.out_qp[0]
+                rows = src.N * src.H * src.W
+                rc = raw.qa_rescale_bytes_dev(src.ptr, src.pix_stride, int(src.signed), dst.ptr,
+                                              dst.pix_stride, rows, src.C,
+                                              int(concat.same_grid(idx)), qp.zp, m, s, o.zp,
+                                              o.qmin, o.qmax, st)
+            elif kind == "gap":
+                layer, x, y, area = payload
+                m, s = layer.multiplier(area)
+                rc = raw.qa_gap_dev(x.ptr, x.pix_stride, int(x.signed), x.N, area, x.C,
+                                    layer.in_zp, m, s, layer.out_zp, layer.out_qmin,
+                                    layer.out_qmax, y.ptr, y.pix_stride, st)
+            elif kind == "lut":
+                layer, x, y, ldev = payload
+                rc = raw.qa_lut_bytes_dev(x.ptr, x.pix_stride, int(x.signed), y.ptr,
+                                          y.pix_stride, x.N * x.H * x.W, x.C,
+                                          int(layer.lut_offset), ldev.data_ptr(),
+                                          len(layer.lut), st)
+            elif kind == "add":
+                layer, a, b, y = payload
+                (ma, sa), (mb, sb) = layer._mult
+                qa, qb = layer.in_qp
+                o = layer.out_qp[0]
+                rc = raw.qa_add_bytes_dev(a.ptr, a.pix_stride, int(a.signed), b.ptr,
+                                          b.pix_stride, int(b.signed), y.ptr, y.pix_stride,
+                                          a.N * a.H * a.W, a.C, qa.zp, ma, sa, qb.zp, mb, sb,
+                                          layer._sign, o.zp, o.qmin, o.qmax, st)
+            elif kind == "maxpool":
+                layer, x, y = payload
+                from quantanything_b200.float_ops import pool_geometry
+
+                k, s_, dl, pd = pool_geometry(layer.node, (x.N, x.C, x.H, x.W))
+                rc = raw.qa_maxpool_bytes_dev(x.ptr, x.pix_stride, int(x.signed), y.ptr,
+                                              y.pix_stride, x.N, x.H, x.W, x.C, k[0], k[1],
+                                              s_[0], s_[1], pd[0], pd[1], dl[0], dl[1], y.H,
+                                              y.W, layer.in_qmin, st)
+            elif kind == "softmax":
+                layer, x = payload
+                qi, o = layer.in_qp[0], layer.out_qp[0]
+                rc = raw.qa_softmax_dev(x.ptr, x.pix_stride, int(x.signed), x.N, x.C,
+                                        float(qi.scale), qi.zp, float(o.scale), o.zp, o.qmin,
+                                        o.qmax, self.out_q.data_ptr(), self.out_f32.data_ptr(),
+                                        float(o.scale), o.zp, st)
+            else:
+                raise AssertionError(kind)
+            _check(self.lib, rc, f"{kind} step")
+            n += 1
+        self.launch_count = n
+        return n
+
+    def forward_device(self, x=None):
+        """Enqueues the whole forward on the current stream (eagerly, no graph).
+
+        ``x``: optional float32 device tensor [N, C, H, W] copied into the
+        input buffer first.  Returns the float32 device output."""
+        if x is not None:
+            self.x_dev.copy_(x)
+        self._launch_all(torch.cuda.current_stream(self.device).cuda_stream)
+        return self.out_f32
+
+    def capture(self):
+        """Captures the forward in a CUDA graph (after one eager warm-up)."""
+        torch.cuda.synchronize(self.device)
+        self.forward_device()
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(self.device)
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self._launch_all(s.cuda_stream)
+        torch.cuda.synchronize(self.device)
+        self._graph = g
+        return g
+
+    def replay(self):
+        """Replays the captured forward on the current stream."""
+        if self._graph is None:
+            self.capture()
+        self._graph.replay()
+        return self.out_f32
+
+    def check_status(self):
+        """Raises if any kernel reported a bounded-wait timeout."""
+        rc = self.lib.raw.qa_device_status_dev(
+            ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        _check(self.lib, rc, "device status")
+
+    def run(self, x_host, out=None):
+        """Public host-to-host call: copies ``x_host`` (float32 NCHW) in,
+        runs the captured forward, returns the float32 output on the host."""
+        xs = torch.as_tensor(np.ascontiguousarray(x_host, dtype=np.float32))
+        if tuple(xs.shape) != self.in_shape:
+            raise ValueError(f"input shape {tuple(xs.shape)} != planned {self.in_shape}")
+        self.x_dev.copy_(xs, non_blocking=xs.is_pinned())
+        y = self.replay()
+        host = out if out is not None else torch.empty(y.shape, dtype=torch.float32,
+                                                       pin_memory=True)
+        host.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return host.numpy()
+
+    def tensor(self, name):
+        """A planned tensor as int32 NCHW (inspection helper; copies)."""
+        v = self._views[name]
+        rows = v.N * v.H * v.W
+        t = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset)
+        t = (t.view(torch.int8) if v.signed else t).to(torch.int32)
+        return t.reshape(v.N, v.H, v.W, v.C).permute(0, 3, 1, 2).contiguous()
+
+    def output_int(self):
+        """int32 graph output (before the final dequantize) of the last run."""
+        return self.out_q

@@ -78,8 +78,13 @@ def generate(outdir):
         if name == "yolov8n_cls_int8":
             # the benchmark batch: 64 images, pinned by digest
             x64 = networks.images(64, size, seed=7)
-            env64, _ = qc._execute(x64, "integer")
+            env64, _ = qc._execute(x64, "integer", trace=lambda layer, outs: None)
             extra["q64_digest"] = digest(np.asarray(env64[rg.outputs[0]], np.int32))
+            gemm = [n for n in rg.nodes if n.op_type == "Gemm"][0]
+            extra["logits64_digest"] = digest(np.asarray(env64[gemm.outputs[0]], np.int32))
+            extra["logits_name"] = gemm.outputs[0]
+            np.save(outdir / "yolov8n_cls_int8.q64.npy", np.asarray(env64[rg.outputs[0]],
+                                                                   np.int8))
         np.savez_compressed(outdir / f"{name}.npz", q=np.asarray(q, np.int32),
                             y=np.asarray(out, np.float32))
         meta = {"builder": builder, "kwargs": kw, "quant_type": qtype, "eval_batch": ne,

@@ -53,3 +53,23 @@ def test_reference_loader_signature_table_matches():
     assert len(sigs["qa_conv_i32_i16_i32"][1]) == 19
     assert len(sigs["qa_requantize_i32"][1]) == 12
     assert len(sigs["qa_add"][1]) == 14
+
+
+def test_fused_desc_layout_matches_header(tmp_path):
+    """ctypes FusedConvDesc has the exact field offsets of the C struct."""
+    import subprocess
+
+    from quantanything_b200.resident import FusedConvDesc
+
+    names = [f[0] for f in FusedConvDesc._fields_]
+    src = tmp_path / "probe.c"
+    src.write_text(
+        '#include <stddef.h>\n#include <stdio.h>\n#include "qa_kernels.h"\nint main(void){\n'
+        + "".join(f'printf("%zu\\n", offsetof(qa_fused_conv_desc, {n}));\n' for n in names)
+        + 'printf("%zu\\n", sizeof(qa_fused_conv_desc));\nreturn 0;}\n')
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    want = [getattr(FusedConvDesc, n).offset for n in names] + [ctypes.sizeof(FusedConvDesc)]
+    assert got == want

@@ -1,0 +1,110 @@
+"""Device-resident fused executor vs the reference's integer pass (B200).
+
+The container is loaded from the reference's own q.json; every integer
+tensor must match the reference bit for bit.  The Softmax float fallback is
+allowed 1 output LSB (the tolerance the task states for float fallbacks):
+float64 exp / summation order on the GPU may differ from NumPy's in the
+last ulp.
+"""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from quantanything_b200 import networks
+from quantanything_b200.container import QuantContainer
+from tests.conftest import GOLDEN
+from tests.test_oracle_golden import _digest
+
+pytestmark = pytest.mark.gpu
+GRAPHS = GOLDEN / "graphs"
+SOFTMAX_LSB = 1
+
+
+def _net(name, lib, batch):
+    from quantanything_b200.resident import ResidentNet
+
+    meta = json.loads((GRAPHS / f"{name}.meta.json").read_text())
+    g = getattr(networks, meta["builder"])(**meta["kwargs"])
+    qc = QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=lib)
+    return ResidentNet(qc, batch), qc, meta
+
+
+def _run(net, x):
+    net.forward_device(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    net.check_status()
+    return net.out_q.cpu().numpy()
+
+
+def test_yolov8n_int8_batch2_matches_reference(gpu_lib):
+    net, qc, meta = _net("yolov8n_cls_int8", gpu_lib, 2)
+    x = networks.images(2, 224, seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / "yolov8n_cls_int8.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+    assert (q == ref).mean() > 0.999
+    # every integer tensor before the Softmax, against the drop-in ABI pass
+    # of the same container (itself pinned to the reference)
+    env = {}
+    feeds = qc.quantize_inputs({"images": x})
+    env.update(feeds)
+    for node in qc.graph.nodes:
+        layer = qc.quant_layers[node.name]
+        if node.op_type == "Softmax":
+            break
+        outs = layer.quantized_infer_integer([env[n] for n in layer.data_inputs])
+        env.update(zip(node.outputs, outs))
+    logits = meta["logits_name"]
+    got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
+    np.testing.assert_array_equal(got, env[logits])
+
+
+def test_yolov8n_int8_batch64_logits_digest(gpu_lib):
+    """The benchmark batch: 64 images, logits bit-exact (digest of the
+    reference's int32 Gemm output), Softmax within 1 LSB."""
+    net, qc, meta = _net("yolov8n_cls_int8", gpu_lib, 64)
+    x = networks.images(64, 224, seed=meta["eval_seed"])
+    q = _run(net, x)
+    logits = net.tensor(meta["logits_name"]).cpu().numpy().reshape(64, -1)
+    assert _digest(logits.astype(np.int32)) == meta["logits64_digest"]
+    ref = np.load(GRAPHS / "yolov8n_cls_int8.q64.npy").astype(np.int64)
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+
+
+def test_cuda_graph_replay_matches_eager(gpu_lib):
+    net, qc, meta = _net("yolov8n_cls_int8", gpu_lib, 8)
+    x = networks.images(8, 224, seed=3)
+    eager = _run(net, x).copy()
+    net.capture()
+    for _ in range(3):
+        net.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(net.out_q.cpu().numpy(), eager)
+    host = net.run(x)
+    np.testing.assert_array_equal(host, net.out_f32.cpu().numpy())
+
+
+def test_yolo_mini_int8_grouped_and_fused(gpu_lib):
+    net, qc, meta = _net("yolo_mini_int8", gpu_lib, 2)
+    x = networks.images(2, meta["image"], seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / "yolo_mini_int8.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+
+
+def test_batch_invariance(gpu_lib):
+    """Batch sharding is exact: images 0..3 of a batch of 8 equal a batch of 4
+    (the reference's batch-size invariance, test_container.py:201-206)."""
+    net8, _, _ = _net("yolov8n_cls_int8", gpu_lib, 8)
+    net4, _, _ = _net("yolov8n_cls_int8", gpu_lib, 4)
+    x = networks.images(8, 224, seed=5)
+    np.testing.assert_array_equal(_run(net8, x)[:4], _run(net4, x[:4]))
+
+
+def test_wide_weights_are_rejected_cleanly(gpu_lib):
+    from quantanything_b200.resident import UnsupportedGraph
+
+    with pytest.raises(UnsupportedGraph):
+        _net("yolo_mini_int16", gpu_lib, 2)
