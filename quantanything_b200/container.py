@@ -114,7 +114,7 @@ class QuantContainer:
         if mode not in MODES:
             raise ValueError(f"Unknown graph mode: {mode}")
         if mode == "float":
-            return float_ops.run_float(self.graph, x)
+            return float_ops.run_float(self.graph, x, lib=self.lib)
         return self._execute(x, mode)
 
     def quantize_inputs(self, feeds):

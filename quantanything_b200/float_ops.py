@@ -65,13 +65,13 @@ def normalize_feeds(graph, feeds):
     return {k: np.asarray(v, dtype=np.float32) for k, v in feeds.items()}
 
 
-def run_float(graph, feeds, keep_all=False):
+def run_float(graph, feeds, keep_all=False, lib=None):
     """Float32 forward pass of the whole graph (float_ops.py:63-85)."""
     env = dict(graph.initializers)
     env.update(normalize_feeds(graph, feeds))
     for node in graph.nodes:
         args = [env[i] if i else None for i in node.inputs]
-        env.update(zip(node.outputs, run_node(node, args, graph.opset)))
+        env.update(zip(node.outputs, run_node(node, args, graph.opset, lib=lib)))
     if keep_all:
         return env
     res = [env[o] for o in graph.outputs]
@@ -112,7 +112,8 @@ def _conv(node, inputs, opset, **kw):
     strides = tuple(node.attr("strides", [1, 1]))
     dil = tuple(node.attr("dilations", [1, 1]))
     pads = conv_pads(node, x.shape[2:], w.shape[2:], strides, dil)
-    y = native.conv2d_f32(x, w, strides, pads, dil, node.attr("group", 1))
+    lib = kw.get("lib") or native.get_library()
+    y = lib.conv2d_f32(x, w, strides, pads, dil, node.attr("group", 1))
     if len(inputs) > 2 and inputs[2] is not None:
         y = y + inputs[2].reshape(1, -1, 1, 1)
     return y
@@ -125,7 +126,8 @@ def _gemm(node, inputs, opset, **kw):
         a = a.T
     if node.attr("transB", 0):
         b = b.T
-    y = np.float32(node.attr("alpha", 1.0)) * native.gemm_f32(a, b)
+    lib = kw.get("lib") or native.get_library()
+    y = np.float32(node.attr("alpha", 1.0)) * lib.gemm_f32(a, b)
     if len(inputs) > 2 and inputs[2] is not None:
         y = y + np.float32(node.attr("beta", 1.0)) * inputs[2]
     return y.astype(np.float32)
@@ -147,7 +149,7 @@ def _fused(node, inputs, opset, **kw):
     env[node.inputs[0]] = inputs[0]
     for sub in node.attrs["nodes"]:
         args = [env[i] if i else None for i in sub.inputs]
-        env[sub.outputs[0]] = run_node(sub, args, opset)[0]
+        env[sub.outputs[0]] = run_node(sub, args, opset, **kw)[0]
     return env[node.outputs[0]]
 
 

@@ -96,7 +96,8 @@ class BaseQuantLayer:
                 for n in self.node.inputs]
 
     def _run_float(self, data_args, **kw):
-        return run_node(self.node, self._full_args(data_args), self.graph.opset, **kw)
+        return run_node(self.node, self._full_args(data_args), self.graph.opset, lib=self.lib,
+                        **kw)
 
     def calibrate(self, inputs):
         outs = self._run_float(inputs)

@@ -1,0 +1,103 @@
+"""Multi-process (world size 2, gloo on CPU) tests of the data-parallel path.
+
+Sharded calibration with the MIN/MAX all-reduce must give exactly the
+qparams of one process calibrating on all batches, and the output gather
+must reassemble the batch in order.  The kernel library is the C oracle
+(CPU), so no GPU is involved.
+"""
+import json
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from tests.conftest import ORACLE_LIB, _ensure_oracle
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    import torch.distributed as dist
+
+    from quantanything_b200 import distributed, networks
+    from quantanything_b200.container import QuantContainer
+    from quantanything_b200.native import KernelLibrary
+
+    distributed.init("gloo", timeout_s=60)
+    lib = KernelLibrary(ORACLE_LIB)
+    qc = QuantContainer(networks.yolo_mini(width=16), "int8", lib=lib)
+    batches = [networks.images(3, 32, seed=50 + i) for i in range(4)]
+    distributed.calibrate_sharded(qc, batches)
+    qc.save(os.path.join(outdir, f"q{rank}.json"))
+    # each rank runs its shard of a 5-image batch; gather reassembles it
+    x = networks.images(5, 32, seed=9)
+    y = qc.run_graph(distributed.shard(x, rank, world), "integer")
+    full = distributed.gather_outputs(y, len(x))
+    np.save(os.path.join(outdir, f"y{rank}.npy"), full)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_calibration_and_gather(tmp_path):
+    _ensure_oracle()
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    from quantanything_b200 import networks
+    from quantanything_b200.container import QuantContainer
+    from quantanything_b200.native import KernelLibrary
+
+    lib = KernelLibrary(ORACLE_LIB)
+    single = QuantContainer(networks.yolo_mini(width=16), "int8", lib=lib)
+    single.calibrate([networks.images(3, 32, seed=50 + i) for i in range(4)])
+    single.save(tmp_path / "single.json")
+    ref = json.loads((tmp_path / "single.json").read_text())
+    for r in range(world):
+        assert json.loads((tmp_path / f"q{r}.json").read_text()) == ref
+    expect = single.run_graph(networks.images(5, 32, seed=9), "integer")
+    for r in range(world):
+        np.testing.assert_array_equal(np.load(tmp_path / f"y{r}.npy"), expect)
+
+
+def test_shard_bounds_cover_batch():
+    from quantanything_b200.distributed import shard_bounds
+
+    for total in (0, 1, 7, 64, 65):
+        for world in (1, 2, 3, 8):
+            spans = [shard_bounds(total, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == total
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [hi - lo for lo, hi in spans]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def test_rank_failure_is_reported_not_hung(tmp_path):
+    """A rank that raises before the collective ends the job with an error
+    (the survivor's collective times out) instead of hanging."""
+    _ensure_oracle()
+    port = _free_port()
+    with pytest.raises(Exception):
+        mp.start_processes(_failing_worker, args=(2, port), nprocs=2, start_method="spawn",
+                           join=True)
+
+
+def _failing_worker(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    import torch
+
+    from quantanything_b200 import distributed
+
+    distributed.init("gloo", timeout_s=10)
+    if rank == 1:
+        raise RuntimeError("injected host-side failure on rank 1")
+    distributed.allreduce_ranges({"t": (0.0, 1.0)})
+    torch.distributed.destroy_process_group()
