@@ -1,0 +1,341 @@
+#!/usr/bin/env python
+"""Benchmark: int8 YOLOv8n-cls integer inference, images/sec on B200.
+
+Workload (configuration 2): YOLOv8n-cls, random init (He-normal convs with a
+folded random BatchNorm), int8 per-channel weights, int8 activations with the
+qparams the reference's QuantContainer calibrated on 32 seeded images
+(tests/golden/graphs/yolov8n_cls_int8.qjson), batch 64 per GPU of N(0,1)
+images clipped to +-3 (synthetic: no dataset is reachable).
+
+One step = one integer forward pass over one batch of 64 images per GPU:
+graph-input quantization, 26 fused conv layers, GAP, Gemm 1280->1000 and
+the Softmax float fallback, captured in a CUDA graph.
+
+  value  -- images/s with the batch already in HBM, device time from CUDA
+            events around each step; L2 flushed (256 MiB write) between
+            steps, outside the events; max over ranks.
+  e2e    -- images/s through the public host-to-host call: pinned host
+            images -> device, forward, float32 probabilities -> host, every
+            step inside the events.
+  e2e_dropin -- images/s of the drop-in route: the reference's layer-by-layer
+            execution driving the CUDA library's host-pointer ABI
+            (one H2D/D2H per layer), wall clock.
+  roofline -- dominant kernel of the step, measured live with CUDA events.
+  cpu_baseline -- the reference's own C++ kernels (oracle/_ref, OpenMP, all
+            host threads) driven layer by layer, on a bounded sample.
+
+--impl reference runs only that CPU reference arm (rank 0; other ranks exit).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+QJSON = REPO / "tests" / "golden" / "graphs" / "yolov8n_cls_int8.qjson"
+REF_LIB = REPO / "oracle" / "_ref" / "libqa_kernels_ref.so"
+METRIC = "int8 YOLOv8n-cls images/sec"
+UNIT = "images/s"
+PER_GPU_BATCH = 64
+IMAGE = 224
+
+
+def config(world, extra=None):
+    c = {"workload": "cfg2: YOLOv8n-cls int8 integer inference (random init, BN folded, "
+                     "reference-calibrated q.json)",
+         "global_batch": PER_GPU_BATCH * world, "per_gpu_batch": PER_GPU_BATCH,
+         "image": [3, IMAGE, IMAGE], "parallelism": f"dp{world} (batch-sharded replicas)",
+         "l2": "flushed with a 256 MiB write between timed steps (outside the events)"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+# ------------------------------------------------------------ CPU arms --
+def cpu_reference_sample(seconds, images_per_step, steps=None):
+    """The reference's C++ kernels (OpenMP) driven layer by layer; returns
+    (images/s, threads, sample description, per-step seconds list)."""
+    from quantanything_b200 import networks
+    from quantanything_b200.container import QuantContainer
+    from quantanything_b200.native import KernelLibrary
+
+    if not REF_LIB.exists():
+        raise FileNotFoundError(f"{REF_LIB} missing (built by __graft_entry__.build())")
+    threads = len(os.sched_getaffinity(0))
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    lib = KernelLibrary(REF_LIB)
+    lib.set_num_threads(threads)
+    qc = QuantContainer.load(networks.yolov8n_cls(), QJSON, lib=lib)
+    x = networks.images(images_per_step, IMAGE, seed=2024)
+    qc.run_graph(x[:2], "integer")  # warm caches / thread pool
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and (not times or time.perf_counter() < t_end)) or (
+            steps is not None and len(times) < steps):
+        t0 = time.perf_counter()
+        qc.run_graph(x, "integer")
+        times.append(time.perf_counter() - t0)
+    ips = images_per_step * len(times) / sum(times)
+    sample = (f"{len(times)} step(s) of {images_per_step} images through the reference's "
+              f"qa_kernels.cpp (OpenMP, {lib.num_threads()} threads) driven layer by layer")
+    return ips, lib.num_threads(), sample, times
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    images = 8
+    ips, threads, sample, times = cpu_reference_sample(0, images, steps=args.warmup)
+    ips, threads, sample, times = cpu_reference_sample(0, images, steps=args.steps)
+    ms = 1000.0 * sum(times) / len(times)
+    line = {"impl": "reference", "metric": METRIC, "value": round(ips, 3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic N(0,1) images, random init",
+            "config": config(world, {"reference_step": f"{images} images per step on the "
+                                                       "host CPU"}),
+            "cpu_baseline": {"value": round(ips, 3), "unit": UNIT, "cores": threads,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(ips, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- clocks --
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index, period_s=0.005):
+        self.index, self.period = index, period_s
+        self.samples, self._stop = [], threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # NVML missing: report no clocks rather than fail
+            self.max_mhz = None
+
+    def _reasons(self):
+        nv = self.nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+            nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        return fn(self.h)
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append((self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
+                                     self._reasons()))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._loop, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= int(r)
+        names = [n for b, n in self.REASONS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], 2.0 * d["bf16_tflops"], "measured"
+    return 6650.0, 2.0 * 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------- main --
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-dropin", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+
+    from quantanything_b200 import networks
+    from quantanything_b200.container import QuantContainer
+    from quantanything_b200.resident import ResidentNet
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    qc = QuantContainer.load(networks.yolov8n_cls(), QJSON)
+    net = ResidentNet(qc, PER_GPU_BATCH, dev)
+    x_host = networks.images(PER_GPU_BATCH, IMAGE, seed=1000 + rank)
+    x_pinned = torch.from_numpy(x_host).pin_memory()
+    out_pinned = torch.empty((PER_GPU_BATCH, 1000), dtype=torch.float32).pin_memory()
+    net.x_dev.copy_(x_pinned)
+    net.capture()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: device-resident forward, CUDA-graph replay per step
+    for _ in range(args.warmup):
+        net.replay()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            net.replay()
+            ends[k].record(stream)
+        barrier()
+    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    net.check_status()
+    elapsed_ms = max_over_ranks(elapsed_ms)
+    value = world * PER_GPU_BATCH * args.steps / (elapsed_ms / 1e3)
+
+    # ---- e2e: pinned host images in, probabilities out, every step
+    e2e_steps = max(min(args.steps, 50), 1)
+    for _ in range(3):
+        net.run_async(x_pinned, out_pinned)
+    es = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    ee = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    barrier()
+    for k in range(e2e_steps):
+        es[k].record(stream)
+        net.run_async(x_pinned, out_pinned)
+        ee[k].record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(es, ee)))
+    e2e = world * PER_GPU_BATCH * e2e_steps / (e2e_ms / 1e3)
+
+    # ---- roofline of the dominant kernel (per-step CUDA events)
+    step_ms = net.time_steps(reps=20)
+    costs = net.step_costs()
+    dom = int(np.argmax(step_ms))
+    label, dom_bytes, dom_ops = costs[dom]
+    hbm_peak, int8_peak_tops, peak_kind = peaks()
+    dur_s = step_ms[dom] / 1e3
+    ai = dom_ops / max(dom_bytes, 1)
+    ridge = int8_peak_tops * 1e12 / (hbm_peak * 1e9)
+    traffic = None
+    tfile = REPO / "profiles" / "dram_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(label)
+    if ai < ridge:
+        achieved = dom_bytes / dur_s / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                    "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                    "traffic": traffic, "algorithmic_bytes": int(dom_bytes)}
+    else:
+        achieved = dom_ops / dur_s / 1e12
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": int8_peak_tops,
+                    "unit": "TOPS", "frac": round(achieved / int8_peak_tops, 4),
+                    "traffic": traffic, "algorithmic_ops": int(dom_ops)}
+    roofline.update({"kernel": label, "us_per_launch": round(step_ms[dom] * 1e3, 2),
+                     "share_of_step": round(float(step_ms[dom] / step_ms.sum()), 4),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json; int8 tensor = 2 x "
+                                    "measured bf16 cuBLAS)"})
+    kernels = [{"kernel": c[0], "us": round(float(t) * 1e3, 2),
+                "GB/s": round(c[1] / (t / 1e3) / 1e9, 1),
+                "TOPS": round(c[2] / (t / 1e3) / 1e12, 2) if c[2] else 0.0}
+               for c, t in zip(costs, step_ms)]
+
+    # ---- drop-in ABI route (rank 0, N=1) and CPU baseline
+    dropin = cpu = None
+    if rank == 0 and world == 1 and not args.no_dropin:
+        qc.run_graph(x_host[:8], "integer")
+        t0 = time.perf_counter()
+        qc.run_graph(x_host, "integer")
+        dt = time.perf_counter() - t0
+        dropin = {"value": round(PER_GPU_BATCH / dt, 2), "unit": UNIT,
+                  "route": "layer-by-layer host-pointer ABI (QA_LIB drop-in), wall clock"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ips, threads, sample, _ = cpu_reference_sample(args.cpu_seconds, 16)
+        cpu = {"value": round(ips, 3), "unit": UNIT, "cores": threads, "kind": "reference",
+               "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic N(0,1) images clipped to +-3, random-init weights",
+                "config": config(world),
+                "e2e": {"value": round(e2e, 1), "unit": UNIT,
+                        "h2d_bytes_per_step": int(x_pinned.numel() * 4),
+                        "d2h_bytes_per_step": int(out_pinned.numel() * 4)},
+                "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(),
+                "gpu_launches": int(net.launch_count * args.steps),
+                "launches_per_step": net.launch_count, "kernels": kernels}
+        if dropin:
+            line["e2e_dropin"] = dropin
+        print(json.dumps(line), flush=True)
+    del net._graph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

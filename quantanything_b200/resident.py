@@ -549,8 +549,62 @@ class ResidentNet:
 
     _outputs_f32 = {}
 
+    # --------------------------------------------------------------- costs --
+    def step_costs(self):
+        """Algorithmic (bytes moved, integer ops) of every step: each tensor
+        counted once (activations as stored bytes, weights once per launch),
+        ops = 2 * MACs of the contraction."""
+        costs = []
+        for kind, payload in self.steps:
+            if kind == "quantize":
+                N, C, H, W = self.in_shape
+                v = self._in_view
+                costs.append((f"quantize {N}x{C}x{H}x{W}", N * C * H * W * 4 +
+                              N * H * W * v.pix_stride, 0))
+            elif kind == "conv":
+                d = payload.desc
+                M = d.N * d.OH * d.OW
+                cg = d.C
+                k = d.KH * d.KW * cg
+                x_bytes = d.N * d.H * d.W * (cg * d.groups if d.groups > 1 else cg)
+                stores = (1 if d.out else 0) + (1 if d.out2 else 0) + (1 if d.res else 0)
+                nbytes = x_bytes + d.Cout * k + M * d.Cout * stores + d.Cout * 24
+                ops = 2 * M * d.Cout * (d.KH * d.KW * cg)
+                label = (f"{payload.layer.node.op_type.lower()} {d.KH}x{d.KW}/s{d.SH} "
+                         f"{cg * d.groups}->{d.Cout} @{d.OH}x{d.OW}")
+                costs.append((label, nbytes, ops))
+            elif kind == "gap":
+                layer, x, y, area = payload
+                costs.append((f"gap {x.C}@{x.H}x{x.W}", x.N * area * x.C + x.N * x.C, 0))
+            elif kind == "softmax":
+                layer, x = payload
+                costs.append((f"softmax {x.N}x{x.C}", x.N * x.C * 9, 0))
+            else:
+                src = payload[1] if kind != "rescale" else payload[2]
+                rows = src.N * src.H * src.W
+                costs.append((kind, rows * src.C * 2, 0))
+        return costs
+
+    def time_steps(self, reps=20):
+        """Average device time (ms) of every step over ``reps`` eager runs,
+        measured with CUDA events recorded between the launches on the
+        launching stream."""
+        stream = torch.cuda.current_stream(self.device)
+        totals = np.zeros(len(self.steps))
+        for _ in range(reps):
+            events = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.steps) + 1)]
+
+            def mark(i, events=events):
+                events[i + 1].record(stream)
+
+            events[0].record(stream)
+            self._launch_all(stream.cuda_stream, on_step=mark)
+            stream.synchronize()
+            totals += [events[i].elapsed_time(events[i + 1]) for i in range(len(self.steps))]
+        return totals / reps
+
     # ------------------------------------------------------------- launch --
-    def _launch_all(self, stream):
+    def _launch_all(self, stream, on_step=None):
         raw = self.lib.raw
         st = ctypes.c_void_p(stream)
         n = 0
@@ -612,6 +666,8 @@ class ResidentNet:
             else:
                 raise AssertionError(kind)
             _check(self.lib, rc, f"{kind} step")
+            if on_step is not None:
+                on_step(n)
             n += 1
         self.launch_count = n
         return n
@@ -652,6 +708,14 @@ class ResidentNet:
         rc = self.lib.raw.qa_device_status_dev(
             ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
         _check(self.lib, rc, "device status")
+
+    def run_async(self, x_pinned, out_pinned):
+        """Enqueues host->device copy, the captured forward and the copy of
+        the float32 output back to ``out_pinned`` on the current stream."""
+        self.x_dev.copy_(x_pinned, non_blocking=True)
+        y = self.replay()
+        out_pinned.copy_(y, non_blocking=True)
+        return out_pinned
 
     def run(self, x_host, out=None):
         """Public host-to-host call: copies ``x_host`` (float32 NCHW) in,
