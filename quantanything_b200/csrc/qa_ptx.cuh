@@ -2,9 +2,9 @@
 // kernels use: mbarriers, cp.async gathers, TMA tile loads, proxy fences
 // and the tcgen05 family (TMEM allocation, MMA, commit, loads).
 //
-// Every wait on an mbarrier is bounded by a wall-clock budget read from
-// %globaltimer; on expiry the caller is told (return false) so it can record
-// an error and leave the kernel instead of hanging the GPU.
+// Every wait on an mbarrier is bounded by a budget of SM clock cycles; on
+// expiry the caller is told (return false) so it can record an error and
+// leave the kernel instead of hanging the GPU.
 #pragma once
 #include <cstdint>
 
@@ -13,12 +13,6 @@ namespace ptx {
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ uint64_t global_timer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 
 // ------------------------------------------------------------ mbarrier --
@@ -51,14 +45,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false after `budget_ns` of wall-clock time.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
+// Bounded wait: false once `budget_cycles` SM clock cycles have passed
+// (the SM cycle counter is cheap to read, unlike the global timer).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          uint64_t budget_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > budget_ns) return false;
+    if ((uint64_t)(clock64() - t0) > budget_cycles) return false;
   }
+}
+
+// One arrival on `bar` once every cp.async this thread issued before has
+// landed in shared memory (the count is not raised first: the barrier's
+// expected count must include this arrival).  The completed copies are
+// visible to tensor-core reads that wait on the barrier.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 // ------------------------------------------------------------ cp.async --

@@ -31,7 +31,7 @@ constexpr int kBM = 128;          // tile rows (TMEM lanes)
 constexpr int kBKBytes = 128;     // K-block bytes (one 128-byte swizzle row)
 constexpr int kProducerThreads = 128;
 constexpr int kCtaThreads = 192;
-constexpr uint64_t kWaitBudgetNs = 1000000000ull;  // 1 s per wait
+constexpr uint64_t kWaitBudgetCycles = 4000000000ull;  // ~2 s at 1.9 GHz
 constexpr int kTimeoutCode = 0x7001;
 
 struct ConvTileParams {
@@ -82,7 +82,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
     umma_conv_kernel(const __grid_constant__ ConvTileParams p,
                      const __grid_constant__ CUtensorMap tmap_b) {
   using TS = TileShape<BN, PA, PB>;
-  constexpr int kLookahead = kStages - 1;  // cp.async groups in flight per thread
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment of the swizzled tiles (the swizzle pattern is a
@@ -135,7 +134,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
   };
   auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
     if (*s_abort) return false;
-    if (ptx::mbar_wait(bar, parity, kWaitBudgetNs)) return true;
+    if (ptx::mbar_wait(bar, parity, kWaitBudgetCycles)) return true;
     fail();
     return false;
   };
@@ -206,17 +205,11 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
           }
         }
       }
-      ptx::cp_async_commit();
-      if (kb >= kLookahead) {
-        ptx::cp_async_wait<kLookahead>();
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(full_bar((kb - kLookahead) % kStages));
-      }
+      // the zero-point padding stores are generic-proxy writes
+      if (p.pad_word[0] | p.pad_word[1]) ptx::fence_proxy_async_smem();
+      ptx::cp_async_mbar_arrive_noinc(full_bar(s));
     }
     ptx::cp_async_wait_all();
-    ptx::fence_proxy_async_smem();
-    for (int kb = (p.num_kb > kLookahead ? p.num_kb - kLookahead : 0); kb < p.num_kb; ++kb)
-      ptx::mbar_arrive(full_bar(kb % kStages));
   } else if (warp == 5) {
     // ------------------------------------------------- weight TMA loads --
     if (lane == 0) {
@@ -604,108 +597,3 @@ bool umma_conv_i16_i32_abi(const int32_t* x, const int16_t* w, int32_t* y, const
 
 }  // namespace qa
 
-// ============================================ fused 8-bit layer (resident) ==
-#include "../../include/qa_kernels.h"
-
-namespace qa {
-
-constexpr int kFusedStages = 4;
-
-bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);
-bool fused_conv_grouped(const qa_fused_conv_desc& d, cudaStream_t st);
-
-template <int BN, int kChunk>
-static bool launch_fused_bn(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n_tiles,
-                            cudaStream_t st) {
-  return launch_umma<BN, 1, 1, kChunk, kEpiFused, kFusedStages>(prm, tmap, n_tiles, 1, st);
-}
-
-static bool fused_conv(const qa_fused_conv_desc& d, cudaStream_t st) {
-  if (d.N < 0 || d.H <= 0 || d.W <= 0 || d.C <= 0 || d.Cout <= 0 || d.KH <= 0 || d.KW <= 0 ||
-      d.SH <= 0 || d.SW <= 0 || d.DH <= 0 || d.DW <= 0 || d.OH <= 0 || d.OW <= 0 || d.PH < 0 ||
-      d.PW < 0) {
-    set_error(kBadArgument, "qa_conv_fused_dev: invalid geometry");
-    return false;
-  }
-  if (d.groups > 1) return fused_conv_grouped(d, st);
-  const int chunk = (d.C % 16 == 0 && d.x_pix_stride % 16 == 0) ? 16
-                    : (d.C % 4 == 0 && d.x_pix_stride % 4 == 0) ? 4
-                                                                 : 0;
-  if (!chunk) {
-    set_error(kBadArgument, "qa_conv_fused_dev: channels per tap must be a multiple of 4");
-    return false;
-  }
-  if ((reinterpret_cast<uintptr_t>(d.x) & (chunk - 1)) || !d.w || !d.mult || !d.shift) {
-    set_error(kBadArgument, "qa_conv_fused_dev: misaligned or missing operand");
-    return false;
-  }
-  int bn = (int)d.block_n;
-  if (bn == 0) bn = d.Cout <= 16 ? 16 : d.Cout <= 32 ? 32 : d.Cout <= 64 ? 64
-                   : d.Cout <= 128 ? 128 : 256;
-  if (chunk == 4 && bn > 64) bn = 64;
-  const int64_t n_tiles = (d.Cout + bn - 1) / bn;
-  const int64_t K = d.KH * d.KW * d.C;
-  if (d.w_kp % 16 || d.w_kp < K || d.w_rows < n_tiles * bn) {
-    set_error(kBadArgument, "qa_conv_fused_dev: packed weight shape does not cover the layer");
-    return false;
-  }
-  if (d.N == 0) return true;
-  CUtensorMap tmap;
-  if (!make_weight_tmap(&tmap, d.w, d.w_rows, d.w_kp, bn)) return false;
-
-  ConvTileParams prm;
-  std::memset(&prm, 0, sizeof(prm));
-  prm.a[0] = static_cast<const uint8_t*>(d.x);
-  prm.pix_stride = d.x_pix_stride;
-  const uint32_t zb = (uint32_t)(d.x_zp & 0xFF);
-  prm.pad_word[0] = zb * 0x01010101u;
-  prm.a_signed = d.x_signed ? 1 : 0;
-  prm.H = (int32_t)d.H;
-  prm.W = (int32_t)d.W;
-  prm.Cin = (int32_t)d.C;
-  prm.KH = (int32_t)d.KH;
-  prm.KW = (int32_t)d.KW;
-  prm.SH = (int32_t)d.SH;
-  prm.SW = (int32_t)d.SW;
-  prm.PH = (int32_t)d.PH;
-  prm.PW = (int32_t)d.PW;
-  prm.DH = (int32_t)d.DH;
-  prm.DW = (int32_t)d.DW;
-  prm.OH = (int32_t)d.OH;
-  prm.OW = (int32_t)d.OW;
-  prm.M = d.N * d.OH * d.OW;
-  prm.K = (int32_t)K;
-  prm.num_kb = (int32_t)((K + kBKBytes - 1) / kBKBytes);
-  prm.n_valid = (int32_t)d.Cout;
-  prm.ohw = d.OH * d.OW;
-  prm.status = device_status_word();
-  fill_fused_epilogue(prm.epi, d);
-  if (chunk == 16) {
-    switch (bn) {
-      case 16: return launch_fused_bn<16, 16>(prm, tmap, n_tiles, st);
-      case 32: return launch_fused_bn<32, 16>(prm, tmap, n_tiles, st);
-      case 64: return launch_fused_bn<64, 16>(prm, tmap, n_tiles, st);
-      case 128: return launch_fused_bn<128, 16>(prm, tmap, n_tiles, st);
-      case 256: return launch_fused_bn<256, 16>(prm, tmap, n_tiles, st);
-    }
-  } else {
-    switch (bn) {
-      case 16: return launch_fused_bn<16, 4>(prm, tmap, n_tiles, st);
-      case 32: return launch_fused_bn<32, 4>(prm, tmap, n_tiles, st);
-      case 64: return launch_fused_bn<64, 4>(prm, tmap, n_tiles, st);
-    }
-  }
-  set_error(kBadArgument, "qa_conv_fused_dev: unsupported column tile");
-  return false;
-}
-
-}  // namespace qa
-
-QA_API int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream) {
-  qa::clear_error();
-  if (!desc) {
-    qa::set_error(qa::kBadArgument, "qa_conv_fused_dev: null descriptor");
-    return qa::last_status();
-  }
-  return qa::fused_conv(*desc, (cudaStream_t)stream) ? 0 : qa::last_status();
-}

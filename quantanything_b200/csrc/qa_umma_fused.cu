@@ -1,0 +1,638 @@
+// Persistent, warp-specialized fused 8-bit convolution / GEMM (tcgen05).
+//
+// One CTA per SM walks a strided list of 128-row output tiles of one
+// column tile (all CTAs of a column tile share its weights).  Roles:
+//   warps 0-3  activation gather: one tile row per thread, cp.async straight
+//              into the 128-byte swizzled K-major layout; a ring of kStages
+//              16 KB stages that runs ahead across tile boundaries;
+//   warp 4     TMEM allocation; lane 0 issues tcgen05.mma (M=128, N=BN,
+//              K=32) into one of two TMEM accumulators and commits;
+//   warp 5     lane 0 loads the weights by TMA: once for the whole kernel
+//              when they fit in shared memory (kResidentB), else one K-block
+//              per stage alongside the activations;
+//   warps 6-9  epilogue: drain the finished accumulator (the MMA meanwhile
+//              fills the other one), apply the layer's integer sequence and
+//              store 16-byte vectors of NHWC output.
+// The K padding of every stage is zeroed once and never gathered again.
+// Every mbarrier wait is bounded (1 s); a timeout sets the device status
+// word, the CTA skips the remaining work, frees TMEM and exits.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/qa_kernels.h"
+#include "qa_common.cuh"
+#include "qa_fixedpoint.cuh"
+#include "qa_ptx.cuh"
+#include "qa_umma.cuh"
+
+namespace qa {
+
+bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                      int box_rows);
+bool fused_conv_grouped(const qa_fused_conv_desc& d, cudaStream_t st);
+bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 128;                 // K-block bytes
+constexpr int kProducers = 128;
+constexpr int kEpilogueThreads = 128;    // one epilogue warpgroup
+constexpr int kEpilogueWarp0 = 6;
+constexpr uint64_t kBudgetCycles = 4000000000ull;  // ~2 s at 1.9 GHz
+constexpr int kTimeoutCode = 0x7002;
+constexpr int kMaxSmemLut = 256;
+
+// Host-proven 64-bit forms of the epilogue's fixed-point steps.
+struct FastFlags {
+  int32_t requant;  // acc + bias fits int32, |M0| < 2^31, 1 <= ts <= 62
+  int32_t add;      // both residual rescales: |v - z| * |m| + 2^(ts-1) < 2^62
+  int32_t rescale;  // concat copy rescale likewise
+};
+
+struct FusedParams {
+  const uint8_t* a;
+  int64_t pix_stride;
+  uint32_t pad_word;
+  int32_t a_signed;
+  int32_t H, W, Cin, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW;
+  int64_t M;
+  int32_t K, num_kb;
+  int32_t n_valid;
+  int32_t m_tiles, n_tiles;
+  int32_t vec_ok;  // every output / residual base and stride is 16-byte aligned
+  int32_t* status;
+  FastFlags fast;
+  FusedEpilogue epi;
+};
+
+__device__ __forceinline__ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) {
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+__device__ __forceinline__ int64_t sbyte(uint32_t word, int j, int is_signed) {
+  const uint32_t b = (word >> (8 * (j & 3))) & 0xFFu;
+  return is_signed ? (int64_t)(int8_t)b : (int64_t)b;
+}
+
+template <int BN, int kChunk, bool kResidentB, int kStages>
+struct Layout {
+  static constexpr int kAStage = kBM * kBK;       // 16 KB
+  static constexpr int kBBlock = BN * kBK;        // one K-block of weights
+  // Two epilogue warpgroups alternate tiles when four accumulators fit in
+  // TMEM (BN <= 128); each group owns two accumulators (double buffered).
+  static constexpr int kGroups = BN <= 128 ? 2 : 1;
+  static constexpr int kAccs = 2 * kGroups;
+  static constexpr int kThreads = 192 + kGroups * kEpilogueThreads;
+  static constexpr int kCols = kAccs * BN;
+  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
+                                 : kCols <= 256 ? 256 : 512;
+};
+
+// Exact (128-bit) forms, kept out of line: they run only for layers whose
+// bounds the host could not prove for the 64-bit forms.
+__device__ __noinline__ int64_t requant_exact_ool(int64_t x, int64_t m, int64_t s, int64_t zp,
+                                                  int64_t lo, int64_t hi) {
+  return requant_exact(x, m, s, zp, lo, hi);
+}
+__device__ __noinline__ int64_t add_exact_ool(int64_t a, int64_t q, const FusedEpilogue& e) {
+  const I128 ta = mbqm(a - e.za, e.ma, e.sa);
+  I128 tb = mbqm(q - e.zb, e.mb, e.sb);
+  if (e.sign < 0) tb = neg_i128(tb);
+  return clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
+}
+
+template <int BN, int kChunk, bool kResidentB, int kStages>
+__global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThreads), 1)
+    fused_conv_persistent(const __grid_constant__ FusedParams p,
+                          const __grid_constant__ CUtensorMap tmap_b) {
+  using L = Layout<BN, kChunk, kResidentB, kStages>;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ptx::smem_addr(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* sm = smem_raw + (base - raw);
+  const int b_blocks = kResidentB ? p.num_kb : kStages;
+  const uint32_t a_base = base;
+  const uint32_t b_base = a_base + kStages * L::kAStage;
+  uint8_t* tail = sm + kStages * L::kAStage + b_blocks * L::kBBlock;
+  int64_t* s_bias = reinterpret_cast<int64_t*>(tail);
+  int64_t* s_mult = s_bias + BN;
+  int64_t* s_shift = s_mult + BN;
+  int64_t* s_rnd = s_shift + BN;                 // 2^(ts-1) of the 64-bit form
+  int32_t* s_bias32 = reinterpret_cast<int32_t*>(s_rnd + BN);
+  int32_t* s_mult32 = s_bias32 + BN;
+  int32_t* s_ts = s_mult32 + BN;
+  int32_t* s_lut = s_ts + BN;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_lut + kMaxSmemLut);
+  const uint32_t bar0 = ptx::smem_addr(bars);
+  auto a_full = [&](int s) { return bar0 + 8u * s; };
+  auto a_empty = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto b_full = [&](int s) { return bar0 + 8u * (2 * kStages + s); };
+  const uint32_t acc_full0 = bar0 + 8u * (3 * kStages);
+  const uint32_t acc_empty0 = acc_full0 + 8u * L::kAccs;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2 * L::kAccs);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int n_tile = blockIdx.x % p.n_tiles;
+  const int m_first = blockIdx.x / p.n_tiles;
+  const int m_step = gridDim.x / p.n_tiles;
+  const int n0 = n_tile * BN;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(a_full(s), kProducers);
+      ptx::mbar_init(a_empty(s), 1);
+      ptx::mbar_init(b_full(s), 1);
+    }
+    for (int b = 0; b < L::kAccs; ++b) {
+      ptx::mbar_init(acc_full0 + 8u * b, 1);
+      ptx::mbar_init(acc_empty0 + 8u * b, kEpilogueThreads);
+    }
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 4) {
+    ptx::tmem_alloc(ptx::smem_addr(s_tmem), L::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  if (warp == 5 && lane == 0) ptx::prefetch_tmap(&tmap_b);
+  if (warp < 4) {
+    // zero every activation stage once: the K padding is never gathered
+    uint4* z = reinterpret_cast<uint4*>(sm);
+    for (int i = tid; i < kStages * L::kAStage / 16; i += kProducers) z[i] = make_uint4(0, 0, 0, 0);
+    ptx::fence_proxy_async_smem();
+  } else if (warp >= kEpilogueWarp0) {
+    const FusedEpilogue& e = p.epi;
+    const int et = tid - kEpilogueWarp0 * 32, nthreads = L::kGroups * kEpilogueThreads;
+    for (int c = et; c < BN; c += nthreads) {
+      const int n = n0 + c;
+      const bool v = n < p.n_valid;
+      s_bias[c] = (v && e.bias) ? e.bias[n] : 0;
+      s_mult[c] = v ? e.mult[n] : 0;
+      s_shift[c] = v ? e.shift[n] : 0;
+      const int ts = (int)(31 + s_shift[c]);
+      s_ts[c] = ts;
+      s_rnd[c] = (ts >= 1 && ts <= 62) ? ((int64_t)1 << (ts - 1)) : 0;
+      s_bias32[c] = (int32_t)s_bias[c];
+      s_mult32[c] = (int32_t)s_mult[c];
+    }
+    if (e.lut && e.lut_len <= kMaxSmemLut)
+      for (int i = et; i < e.lut_len; i += nthreads) s_lut[i] = e.lut[i];
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (ptx::mbar_wait(bar, parity, kBudgetCycles)) return true;
+    *s_abort = 1;
+    if (p.status) atomicExch(p.status, kTimeoutCode);
+    return false;
+  };
+
+  if (warp < 4) {
+    // --------------------------------------------------- activation gather --
+    const int r = tid;
+    const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    const uint32_t sw = (uint32_t)(r & 7);
+    const int64_t ohw = (int64_t)p.OH * p.OW;
+    int g = 0;  // K-blocks issued by this CTA
+    for (int mt = m_first; mt < p.m_tiles; mt += m_step) {
+      const int64_t m = (int64_t)mt * kBM + r;
+      const bool row_ok = m < p.M;
+      int64_t iy0 = 0, ix0 = 0, img_off = 0;
+      if (row_ok) {
+        const int64_t img = m / ohw, rem = m - img * ohw;
+        const int64_t oy = rem / p.OW, ox = rem - oy * p.OW;
+        iy0 = oy * p.SH - p.PH;
+        ix0 = ox * p.SW - p.PW;
+        img_off = img * (int64_t)p.H * p.W * p.pix_stride;
+      }
+      for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+        const int s = g % kStages;
+        if (g >= kStages) wait(a_empty(s), ((g / kStages) - 1) & 1);
+        const bool live = !*s_abort;
+        const int k0 = kb * kBK;
+        const int kend = min(kBK, p.K - k0);  // valid bytes of this block
+        // bytes [kend, kpad) are read by the last 32-byte MMA step: zero them
+        // (a stage may have held a fuller K-block of another tile before)
+        const int kpad = min(kBK, (kend + 31) & ~31);
+        int tap = k0 / p.Cin;
+        int c = k0 - tap * p.Cin;
+        int ky = tap / p.KW, kx = tap - ky * p.KW;
+        const uint32_t stage = a_base + s * L::kAStage;
+        bool wrote_generic = false;
+        for (int kk = 0; kk < kpad && live; kk += kChunk) {
+          const int64_t iy = iy0 + (int64_t)ky * p.DH, ix = ix0 + (int64_t)kx * p.DW;
+          const bool in_k = kk < kend;
+          const bool inside = in_k && row_ok && iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
+          const uint32_t dst =
+              stage + row_off + ((((uint32_t)kk >> 4) ^ sw) << 4) + ((uint32_t)kk & 15u);
+          if (inside) {
+            const uint8_t* src = p.a + img_off + (iy * p.W + ix) * p.pix_stride + c;
+            if (kChunk == 16) ptx::cp_async_16(dst, src, 16);
+            else ptx::cp_async_4(dst, src, 4);
+          } else if (in_k && row_ok && p.pad_word) {
+            wrote_generic = true;
+            uint8_t* d = sm + (dst - base);
+            if (kChunk == 16)
+              *reinterpret_cast<uint4*>(d) = make_uint4(p.pad_word, p.pad_word, p.pad_word,
+                                                        p.pad_word);
+            else
+              *reinterpret_cast<uint32_t*>(d) = p.pad_word;
+          } else {
+            if (kChunk == 16) ptx::cp_async_16(dst, p.a, 0);
+            else ptx::cp_async_4(dst, p.a, 0);
+          }
+          c += kChunk;
+          if (c >= p.Cin) {
+            c = 0;
+            if (++kx == p.KW) {
+              kx = 0;
+              ++ky;
+            }
+          }
+        }
+        // zero-point padding written with plain stores must reach the async
+        // proxy; copies are tracked by the barrier itself
+        if (wrote_generic) ptx::fence_proxy_async_smem();
+        ptx::cp_async_mbar_arrive_noinc(a_full(s));
+      }
+    }
+    ptx::cp_async_wait_all();
+  } else if (warp == 5) {
+    // ------------------------------------------------------ weight loads --
+    if (lane == 0) {
+      if (kResidentB) {
+        ptx::mbar_arrive_expect_tx(b_full(0), (uint32_t)(p.num_kb * L::kBBlock));
+        for (int kb = 0; kb < p.num_kb; ++kb)
+          ptx::tma_load_2d(b_base + kb * L::kBBlock, &tmap_b, b_full(0), kb * kBK, n0);
+      } else {
+        int g = 0;
+        for (int mt = m_first; mt < p.m_tiles; mt += m_step) {
+          for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+            const int s = g % kStages;
+            if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
+            ptx::mbar_arrive_expect_tx(b_full(s), (uint32_t)L::kBBlock);
+            ptx::tma_load_2d(b_base + s * L::kBBlock, &tmap_b, b_full(s), kb * kBK, n0);
+          }
+          if (*s_abort) break;
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // -------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      const uint32_t idesc = ptx::idesc_i8(kBM, BN, p.a_signed, 1);
+      bool ok = true;
+      if (kResidentB) ok = wait(b_full(0), 0);
+      int g = 0, j = 0;
+      for (int mt = m_first; ok && mt < p.m_tiles; mt += m_step, ++j) {
+        const int ab = j % L::kAccs;
+        const int use = j / L::kAccs;  // how often this accumulator was used before
+        if (use >= 1 && !wait(acc_empty0 + 8u * ab, (use - 1) & 1)) break;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem + ab * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+          const int s = g % kStages;
+          const uint32_t ph = (g / kStages) & 1;
+          if (!wait(a_full(s), ph)) { ok = false; break; }
+          if (!kResidentB && !wait(b_full(s), ph)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const int ksteps = (min(kBK, p.K - kb * kBK) + 31) / 32;
+          const uint32_t a_addr = a_base + s * L::kAStage;
+          const uint32_t b_addr = b_base + (kResidentB ? kb : s) * L::kBBlock;
+          for (int kk = 0; kk < ksteps; ++kk) {
+            ptx::mma_i8(d_tmem, ptx::smem_desc_sw128(a_addr + kk * 32),
+                        ptx::smem_desc_sw128(b_addr + kk * 32), idesc,
+                        (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit(a_empty(s));
+        }
+        if (!ok) break;
+        ptx::mma_commit(acc_full0 + 8u * ab);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue --
+    // Warpgroup `grp` drains the tiles j with j % kGroups == grp from
+    // accumulators (grp, grp + kGroups, ...).  Per 16-column chunk the work
+    // runs in phases with the layer-uniform branches hoisted out of the
+    // unrolled element loops.
+    const FusedEpilogue& e = p.epi;
+    const int grp = (warp - kEpilogueWarp0) / 4;
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter.. belong to this warp
+    const int r = quarter * 32 + lane;
+    const bool lut_smem = e.lut && e.lut_len <= kMaxSmemLut;
+    const bool fast_rq = p.fast.requant, fast_add = p.fast.add, fast_rs = p.fast.rescale;
+    int j = 0;
+    for (int mt = m_first; mt < p.m_tiles; mt += m_step, ++j) {
+      if (j % L::kGroups != grp) continue;
+      const int ab = j % L::kAccs;
+      const int use = j / L::kAccs;
+      const bool ok = wait(acc_full0 + 8u * ab, use & 1);
+      __syncwarp();
+      ptx::tc_fence_after();
+      const int64_t m = (int64_t)mt * kBM + r;
+      const bool row_ok = ok && m < p.M;
+      const uint32_t lane_base = tmem + (((uint32_t)quarter * 32u) << 16) + ab * BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[16];
+        ptx::tmem_ld16(lane_base + c0, v);
+        ptx::tmem_ld_wait();
+        if (!row_ok || n0 + c0 >= p.n_valid) continue;
+        const int nval = min(16, p.n_valid - (n0 + c0));
+        const bool vec = p.vec_ok && nval == 16;
+        int32_t q[16];
+        // requantize
+        if (fast_rq) {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int c = c0 + jj;
+            const int32_t x = (int32_t)v[jj] + s_bias32[c];
+            const int64_t r64 = ((int64_t)x * (int64_t)s_mult32[c] + s_rnd[c]) >> s_ts[c];
+            q[jj] = (int32_t)clamp64(r64 + e.zp, e.qmin, e.qmax);
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int c = c0 + jj;
+            q[jj] = (int32_t)requant_exact_ool((int64_t)(int32_t)v[jj] + s_bias[c], s_mult[c],
+                                               s_shift[c], e.zp, e.qmin, e.qmax);
+          }
+        }
+        // activation table
+        if (e.lut) {
+          const int32_t off = (int32_t)e.lut_offset, top = (int32_t)e.lut_len - 1;
+          if (lut_smem) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) q[jj] = s_lut[min(max(q[jj] - off, 0), top)];
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) q[jj] = __ldg(e.lut + min(max(q[jj] - off, 0), top));
+          }
+        }
+        // residual add: out = res (operand a) + sign * ours (operand b)
+        if (e.res) {
+          const uint8_t* rp = e.res + m * e.res_pix_stride + n0 + c0;
+          uint32_t w[4];
+          if (vec) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(rp);
+            w[0] = rv.x; w[1] = rv.y; w[2] = rv.z; w[3] = rv.w;
+          } else {
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              uint32_t acc = 0;
+#pragma unroll
+              for (int b = 0; b < 4; ++b)
+                if (k4 * 4 + b < nval) acc |= (uint32_t)rp[k4 * 4 + b] << (8 * b);
+              w[k4] = acc;
+            }
+          }
+          if (fast_add) {
+            const int tsa = (int)(31 + e.sa), tsb = (int)(31 + e.sb);
+            const int64_t rnda = (int64_t)1 << (tsa - 1), rndb = (int64_t)1 << (tsb - 1);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int64_t a = sbyte(w[jj >> 2], jj, e.res_signed);
+              const int64_t ta = ((a - e.za) * e.ma + rnda) >> tsa;
+              const int64_t tb = (((int64_t)q[jj] - e.zb) * e.mb + rndb) >> tsb;
+              q[jj] = (int32_t)clamp64(ta + e.sign * tb + e.add_zo, e.add_qmin, e.add_qmax);
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              q[jj] = (int32_t)add_exact_ool(sbyte(w[jj >> 2], jj, e.res_signed), q[jj], e);
+          }
+        }
+        // primary store
+        if (e.out) {
+          uint32_t o[4];
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4)
+            o[k4] = ((uint32_t)q[4 * k4] & 0xFFu) | (((uint32_t)q[4 * k4 + 1] & 0xFFu) << 8) |
+                    (((uint32_t)q[4 * k4 + 2] & 0xFFu) << 16) | ((uint32_t)q[4 * k4 + 3] << 24);
+          uint8_t* op = e.out + m * e.out_pix_stride + n0 + c0;
+          if (vec) {
+            *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
+          }
+        }
+        // rescaled copy into a Concat slice
+        if (e.out2) {
+          int32_t q2[16];
+          if (e.r_identity) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              q2[jj] = (int32_t)clamp64(q[jj], e.r_qmin, e.r_qmax);
+          } else if (fast_rs) {
+            const int ts = (int)(31 + e.r_s);
+            const int64_t rnd = (int64_t)1 << (ts - 1);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              q2[jj] = (int32_t)clamp64(((((int64_t)q[jj] - e.r_zp_in) * e.r_m + rnd) >> ts) +
+                                            e.r_zp_out, e.r_qmin, e.r_qmax);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              q2[jj] = (int32_t)requant_exact_ool(q[jj] - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out,
+                                                  e.r_qmin, e.r_qmax);
+          }
+          uint32_t o[4];
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4)
+            o[k4] = ((uint32_t)q2[4 * k4] & 0xFFu) | (((uint32_t)q2[4 * k4 + 1] & 0xFFu) << 8) |
+                    (((uint32_t)q2[4 * k4 + 2] & 0xFFu) << 16) | ((uint32_t)q2[4 * k4 + 3] << 24);
+          uint8_t* op = e.out2 + m * e.out2_pix_stride + n0 + c0;
+          if (vec) {
+            *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(acc_empty0 + 8u * ab);
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+template <int BN, int kChunk, bool kResidentB, int kStages>
+size_t smem_bytes(int num_kb) {
+  using L = Layout<BN, kChunk, kResidentB, kStages>;
+  const int b_blocks = kResidentB ? num_kb : kStages;
+  return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + 4 * BN * 8 +
+         3 * BN * 4 + kMaxSmemLut * 4 + (3 * kStages + 2 * L::kAccs) * 8 + 16;
+}
+
+constexpr int kStagesFused = 4;
+constexpr size_t kSmemCap = 227 * 1024;
+
+template <int BN, int kChunk, bool kResidentB>
+bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, cudaStream_t st) {
+  auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStagesFused>;
+  const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStagesFused>(prm.num_kb);
+  static size_t attr_bytes[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || attr_bytes[dev] < smem) {
+    if (cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem),
+                    "cudaFuncSetAttribute(smem)"))
+      return false;
+    if (dev >= 0 && dev < 64) attr_bytes[dev] = smem;
+  }
+  const int64_t sms = sm_count();
+  int64_t per_n = sms / prm.n_tiles;
+  if (per_n < 1) per_n = 1;
+  if (per_n > prm.m_tiles) per_n = prm.m_tiles;
+  const int64_t grid = per_n * prm.n_tiles;
+  kern<<<(unsigned)grid, Layout<BN, kChunk, kResidentB, kStagesFused>::kThreads, smem, st>>>(
+      prm, tmap);
+  return !cuda_failed(cudaGetLastError(), "fused_conv_persistent launch");
+}
+
+template <int BN, int kChunk>
+bool launch_bn(const FusedParams& prm, const CUtensorMap& tmap, cudaStream_t st) {
+  if (smem_bytes<BN, kChunk, true, kStagesFused>(prm.num_kb) <= kSmemCap)
+    return launch_persistent<BN, kChunk, true>(prm, tmap, st);
+  return launch_persistent<BN, kChunk, false>(prm, tmap, st);
+}
+
+bool fits_int32_mult(int64_t m) { return m > -(int64_t(1) << 31) && m < (int64_t(1) << 31); }
+
+// Is the 64-bit rescale ((v - z) * m + 2^(ts-1)) >> ts exact for every
+// 8-bit v?  |v - z| <= 2^9 + |z|.
+bool small_rescale_fast(int64_t z, int64_t m, int64_t s) {
+  const int64_t ts = 31 + s;
+  if (ts < 1 || ts > 62 || !fits_int32_mult(m)) return false;
+  const int64_t vmax = 512 + (z < 0 ? -z : z);
+  if (vmax >= (int64_t(1) << 31)) return false;
+  const double bound = (double)vmax * (double)(m < 0 ? -m : m) + std::ldexp(1.0, (int)ts - 1);
+  return bound < std::ldexp(1.0, 61);
+}
+
+}  // namespace
+
+bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
+  if (d.N < 0 || d.H <= 0 || d.W <= 0 || d.C <= 0 || d.Cout <= 0 || d.KH <= 0 || d.KW <= 0 ||
+      d.SH <= 0 || d.SW <= 0 || d.DH <= 0 || d.DW <= 0 || d.OH <= 0 || d.OW <= 0 || d.PH < 0 ||
+      d.PW < 0 || d.groups < 1) {
+    set_error(kBadArgument, "qa_conv_fused_dev: invalid geometry");
+    return false;
+  }
+  if (d.groups > 1) return fused_conv_grouped(d, st);
+  const int chunk = (d.C % 16 == 0 && d.x_pix_stride % 16 == 0) ? 16
+                    : (d.C % 4 == 0 && d.x_pix_stride % 4 == 0) ? 4 : 0;
+  if (!chunk || (reinterpret_cast<uintptr_t>(d.x) & (chunk - 1)) || !d.w || !d.mult ||
+      !d.shift) {
+    set_error(kBadArgument, "qa_conv_fused_dev: misaligned or missing operand");
+    return false;
+  }
+  int bn = (int)d.block_n;
+  if (bn == 0) bn = d.Cout <= 16 ? 16 : d.Cout <= 32 ? 32 : d.Cout <= 64 ? 64
+                   : d.Cout <= 128 ? 128 : 256;
+  if (chunk == 4 && bn > 64) bn = 64;
+  const int64_t n_tiles = (d.Cout + bn - 1) / bn;
+  const int64_t K = d.KH * d.KW * d.C;
+  if (d.w_kp % 16 || d.w_kp < K || d.w_rows < n_tiles * bn) {
+    set_error(kBadArgument, "qa_conv_fused_dev: packed weight shape does not cover the layer");
+    return false;
+  }
+  if (d.N == 0) return true;
+  const int64_t M = d.N * d.OH * d.OW;
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  if (m_tiles > 0x7FFFFFFF || K > (1 << 20)) {
+    set_error(kUnsupported, "qa_conv_fused_dev: layer too large");
+    return false;
+  }
+  CUtensorMap tmap;
+  if (!make_weight_tmap(&tmap, d.w, d.w_rows, d.w_kp, bn)) return false;
+
+  FusedParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.a = static_cast<const uint8_t*>(d.x);
+  prm.pix_stride = d.x_pix_stride;
+  prm.pad_word = (uint32_t)(d.x_zp & 0xFF) * 0x01010101u;
+  prm.a_signed = d.x_signed ? 1 : 0;
+  prm.H = (int32_t)d.H;
+  prm.W = (int32_t)d.W;
+  prm.Cin = (int32_t)d.C;
+  prm.KH = (int32_t)d.KH;
+  prm.KW = (int32_t)d.KW;
+  prm.SH = (int32_t)d.SH;
+  prm.SW = (int32_t)d.SW;
+  prm.PH = (int32_t)d.PH;
+  prm.PW = (int32_t)d.PW;
+  prm.DH = (int32_t)d.DH;
+  prm.DW = (int32_t)d.DW;
+  prm.OH = (int32_t)d.OH;
+  prm.OW = (int32_t)d.OW;
+  prm.M = M;
+  prm.K = (int32_t)K;
+  prm.num_kb = (int32_t)((K + kBK - 1) / kBK);
+  prm.n_valid = (int32_t)d.Cout;
+  prm.m_tiles = (int32_t)m_tiles;
+  prm.n_tiles = (int32_t)n_tiles;
+  auto al16 = [](const void* ptr, int64_t stride) {
+    return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && stride % 16 == 0);
+  };
+  prm.vec_ok = al16(d.out, d.out_pix_stride) && al16(d.out2, d.out2_pix_stride) &&
+               al16(d.res, d.res_pix_stride);
+  prm.status = device_status_word();
+  prm.fast.requant = d.fast ? 1 : 0;
+  prm.fast.add = d.res ? (small_rescale_fast(d.za, d.ma, d.sa) &&
+                          small_rescale_fast(d.zb, d.mb, d.sb) && (d.sign == 1 || d.sign == -1))
+                       : 0;
+  prm.fast.rescale = d.out2 ? small_rescale_fast(d.r_zp_in, d.r_m, d.r_s) : 0;
+  fill_fused_epilogue(prm.epi, d);
+  if (chunk == 16) {
+    switch (bn) {
+      case 16: return launch_bn<16, 16>(prm, tmap, st);
+      case 32: return launch_bn<32, 16>(prm, tmap, st);
+      case 64: return launch_bn<64, 16>(prm, tmap, st);
+      case 128: return launch_bn<128, 16>(prm, tmap, st);
+      case 256: return launch_bn<256, 16>(prm, tmap, st);
+    }
+  } else {
+    switch (bn) {
+      case 16: return launch_bn<16, 4>(prm, tmap, st);
+      case 32: return launch_bn<32, 4>(prm, tmap, st);
+      case 64: return launch_bn<64, 4>(prm, tmap, st);
+    }
+  }
+  set_error(kBadArgument, "qa_conv_fused_dev: unsupported column tile");
+  return false;
+}
+
+}  // namespace qa
+
+QA_API int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream) {
+  qa::clear_error();
+  if (!desc) {
+    qa::set_error(qa::kBadArgument, "qa_conv_fused_dev: null descriptor");
+    return qa::last_status();
+  }
+  return qa::fused_conv_v2(*desc, (cudaStream_t)stream) ? 0 : qa::last_status();
+}

@@ -372,9 +372,12 @@ class ResidentNet:
         xmax = max(abs(layer.in_qmin), abs(layer.in_qmax))
         bound = xmax * abssum + np.abs(bias)
         ts = 31 + shift
+        # 64-bit requantize is exact when acc + bias and M0 fit int32 and the
+        # rounded product cannot overflow (checked per channel, exact ints)
         fast = bool(np.all((ts >= 1) & (ts <= 62)) and all(
-            int(b) * abs(int(m)) + (1 << (int(t) - 1)) < (1 << 62)
-            for b, m, t in zip(bound, mult, ts)))
+            int(b) < (1 << 31) and abs(int(m)) < (1 << 31) and abs(int(bi)) < (1 << 31)
+            and int(b) * abs(int(m)) + (1 << (int(t) - 1)) < (1 << 62)
+            for b, m, t, bi in zip(bound, mult, ts, bias)))
         d = FusedConvDesc()
         d.x, d.x_pix_stride, d.x_signed, d.x_zp = x_view.ptr, x_view.pix_stride, int(
             x_view.signed), int(x_zp)
