@@ -596,4 +596,3 @@ bool umma_conv_i16_i32_abi(const int32_t* x, const int16_t* w, int32_t* y, const
 }
 
 }  // namespace qa
-

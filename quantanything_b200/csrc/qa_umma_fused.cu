@@ -54,6 +54,15 @@ struct FastFlags {
   int32_t rescale;  // concat copy rescale likewise
 };
 
+// One K-chunk of the implicit-GEMM row: tap displacement (dy, dx) and the
+// byte offset of its first channel from the row's top-left input pixel;
+// dy == kTapNone marks chunk positions beyond K.
+struct TapEntry {
+  int16_t dy, dx;
+  int32_t delta;
+};
+constexpr int16_t kTapNone = -32768;
+
 struct FusedParams {
   const uint8_t* a;
   int64_t pix_stride;
@@ -62,6 +71,7 @@ struct FusedParams {
   int32_t H, W, Cin, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW;
   int64_t M;
   int32_t K, num_kb;
+  int32_t n_tap;   // chunk positions covered by the tap table (num_kb * 128 / chunk)
   int32_t n_valid;
   int32_t m_tiles, n_tiles;
   int32_t vec_ok;  // every output / residual base and stride is 16-byte aligned
@@ -129,6 +139,8 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   int32_t* s_ts = s_mult32 + BN;
   int32_t* s_lut = s_ts + BN;
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_lut + kMaxSmemLut);
+  // per K-chunk gather offsets, decoded once per CTA (after the barriers)
+  TapEntry* s_tap = reinterpret_cast<TapEntry*>(bars + 3 * kStages + 2 * L::kAccs + 2);
   const uint32_t bar0 = ptx::smem_addr(bars);
   auto a_full = [&](int s) { return bar0 + 8u * s; };
   auto a_empty = [&](int s) { return bar0 + 8u * (kStages + s); };
@@ -167,6 +179,17 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     uint4* z = reinterpret_cast<uint4*>(sm);
     for (int i = tid; i < kStages * L::kAStage / 16; i += kProducers) z[i] = make_uint4(0, 0, 0, 0);
     ptx::fence_proxy_async_smem();
+    for (int i = tid; i < p.n_tap; i += kProducers) {
+      const int k = i * kChunk;
+      TapEntry t{kTapNone, 0, 0};
+      if (k < p.K) {
+        const int tap = k / p.Cin, c = k - (k / p.Cin) * p.Cin;
+        const int ky = tap / p.KW, kx = tap - (tap / p.KW) * p.KW;
+        const int dy = ky * p.DH, dx = kx * p.DW;
+        t = TapEntry{(int16_t)dy, (int16_t)dx, (int32_t)((dy * p.W + dx) * p.pix_stride + c)};
+      }
+      s_tap[i] = t;
+    }
   } else if (warp >= kEpilogueWarp0) {
     const FusedEpilogue& e = p.epi;
     const int et = tid - kEpilogueWarp0 * 32, nthreads = L::kGroups * kEpilogueThreads;
@@ -200,64 +223,60 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
 
   if (warp < 4) {
     // --------------------------------------------------- activation gather --
+    // Thread r owns tile row r: one output pixel whose receptive field it
+    // gathers K-chunk by K-chunk using the decoded tap table (32-bit math).
     const int r = tid;
     const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t sw = (uint32_t)(r & 7);
-    const int64_t ohw = (int64_t)p.OH * p.OW;
+    const int ohw = p.OH * p.OW;
+    constexpr int kPerBlock = kBK / kChunk;
     int g = 0;  // K-blocks issued by this CTA
     for (int mt = m_first; mt < p.m_tiles; mt += m_step) {
-      const int64_t m = (int64_t)mt * kBM + r;
+      const int m = mt * kBM + r;
       const bool row_ok = m < p.M;
-      int64_t iy0 = 0, ix0 = 0, img_off = 0;
+      int iy0 = 0, ix0 = 0;
+      const uint8_t* row_base = p.a;
       if (row_ok) {
-        const int64_t img = m / ohw, rem = m - img * ohw;
-        const int64_t oy = rem / p.OW, ox = rem - oy * p.OW;
+        const int img = m / ohw, rem = m - (m / ohw) * ohw;
+        const int oy = rem / p.OW, ox = rem - (rem / p.OW) * p.OW;
         iy0 = oy * p.SH - p.PH;
         ix0 = ox * p.SW - p.PW;
-        img_off = img * (int64_t)p.H * p.W * p.pix_stride;
+        row_base = p.a + ((int64_t)img * p.H * p.W + (int64_t)iy0 * p.W + ix0) * p.pix_stride;
       }
       for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
         const int s = g % kStages;
         if (g >= kStages) wait(a_empty(s), ((g / kStages) - 1) & 1);
         const bool live = !*s_abort;
-        const int k0 = kb * kBK;
-        const int kend = min(kBK, p.K - k0);  // valid bytes of this block
+        const int kend = min(kBK, p.K - kb * kBK);
         // bytes [kend, kpad) are read by the last 32-byte MMA step: zero them
         // (a stage may have held a fuller K-block of another tile before)
-        const int kpad = min(kBK, (kend + 31) & ~31);
-        int tap = k0 / p.Cin;
-        int c = k0 - tap * p.Cin;
-        int ky = tap / p.KW, kx = tap - ky * p.KW;
-        const uint32_t stage = a_base + s * L::kAStage;
+        const int npos = min(kBK, (kend + 31) & ~31) / kChunk;
+        const TapEntry* tap = s_tap + kb * kPerBlock;
+        const uint32_t stage = a_base + s * L::kAStage + row_off;
         bool wrote_generic = false;
-        for (int kk = 0; kk < kpad && live; kk += kChunk) {
-          const int64_t iy = iy0 + (int64_t)ky * p.DH, ix = ix0 + (int64_t)kx * p.DW;
-          const bool in_k = kk < kend;
-          const bool inside = in_k && row_ok && iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
-          const uint32_t dst =
-              stage + row_off + ((((uint32_t)kk >> 4) ^ sw) << 4) + ((uint32_t)kk & 15u);
-          if (inside) {
-            const uint8_t* src = p.a + img_off + (iy * p.W + ix) * p.pix_stride + c;
-            if (kChunk == 16) ptx::cp_async_16(dst, src, 16);
-            else ptx::cp_async_4(dst, src, 4);
-          } else if (in_k && row_ok && p.pad_word) {
-            wrote_generic = true;
-            uint8_t* d = sm + (dst - base);
-            if (kChunk == 16)
-              *reinterpret_cast<uint4*>(d) = make_uint4(p.pad_word, p.pad_word, p.pad_word,
-                                                        p.pad_word);
-            else
-              *reinterpret_cast<uint32_t*>(d) = p.pad_word;
-          } else {
-            if (kChunk == 16) ptx::cp_async_16(dst, p.a, 0);
-            else ptx::cp_async_4(dst, p.a, 0);
-          }
-          c += kChunk;
-          if (c >= p.Cin) {
-            c = 0;
-            if (++kx == p.KW) {
-              kx = 0;
-              ++ky;
+        if (live) {
+#pragma unroll 4
+          for (int jpos = 0; jpos < npos; ++jpos) {
+            const TapEntry t = tap[jpos];
+            const int kk = jpos * kChunk;
+            const uint32_t dst = stage + ((((uint32_t)kk >> 4) ^ sw) << 4) + ((uint32_t)kk & 15u);
+            const bool in_k = t.dy != kTapNone;
+            const bool inside = row_ok && in_k && (unsigned)(iy0 + t.dy) < (unsigned)p.H &&
+                                (unsigned)(ix0 + t.dx) < (unsigned)p.W;
+            if (inside) {
+              if (kChunk == 16) ptx::cp_async_16(dst, row_base + t.delta, 16);
+              else ptx::cp_async_4(dst, row_base + t.delta, 4);
+            } else if (in_k && row_ok && p.pad_word) {
+              wrote_generic = true;
+              uint8_t* d = sm + (dst - base);
+              if (kChunk == 16)
+                *reinterpret_cast<uint4*>(d) = make_uint4(p.pad_word, p.pad_word, p.pad_word,
+                                                          p.pad_word);
+              else
+                *reinterpret_cast<uint32_t*>(d) = p.pad_word;
+            } else {
+              if (kChunk == 16) ptx::cp_async_16(dst, p.a, 0);
+              else ptx::cp_async_4(dst, p.a, 0);
             }
           }
         }
@@ -483,7 +502,8 @@ size_t smem_bytes(int num_kb) {
   using L = Layout<BN, kChunk, kResidentB, kStages>;
   const int b_blocks = kResidentB ? num_kb : kStages;
   return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + 4 * BN * 8 +
-         3 * BN * 4 + kMaxSmemLut * 4 + (3 * kStages + 2 * L::kAccs) * 8 + 16;
+         3 * BN * 4 + kMaxSmemLut * 4 + (3 * kStages + 2 * L::kAccs + 2) * 8 +
+         (size_t)num_kb * (kBK / kChunk) * sizeof(TapEntry);
 }
 
 constexpr int kStagesFused = 4;
@@ -563,8 +583,11 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   if (d.N == 0) return true;
   const int64_t M = d.N * d.OH * d.OW;
   const int64_t m_tiles = (M + kBM - 1) / kBM;
-  if (m_tiles > 0x7FFFFFFF || K > (1 << 20)) {
-    set_error(kUnsupported, "qa_conv_fused_dev: layer too large");
+  // 32-bit row / tap arithmetic: rows, taps and one image's bytes fit int32
+  const int64_t tap_span = ((d.KH - 1) * d.DH * d.W + (d.KW - 1) * d.DW) * d.x_pix_stride + d.C;
+  if (M + kBM > 0x7FFFFFFF || K > (1 << 16) || tap_span > 0x7FFFFFFF ||
+      (d.KH - 1) * d.DH > 32767 || (d.KW - 1) * d.DW > 32767 || d.H * d.W > 0x7FFFFFFF) {
+    set_error(kUnsupported, "qa_conv_fused_dev: layer too large for the fused kernel");
     return false;
   }
   CUtensorMap tmap;
@@ -592,6 +615,7 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   prm.M = M;
   prm.K = (int32_t)K;
   prm.num_kb = (int32_t)((K + kBK - 1) / kBK);
+  prm.n_tap = prm.num_kb * (kBK / chunk);
   prm.n_valid = (int32_t)d.Cout;
   prm.m_tiles = (int32_t)m_tiles;
   prm.n_tiles = (int32_t)n_tiles;

@@ -152,6 +152,7 @@ class ResidentNet:
         self.device = torch.device(device or "cuda")
         self.lib = container.lib
         device_api(self.lib)
+        self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.bits, self.signed = container.layers[0].num_bits, container.layers[0].signed
         if self.bits > 8:
             raise UnsupportedGraph("the resident executor runs 8-bit graphs")
@@ -313,7 +314,7 @@ class ResidentNet:
         return view, copy
 
     # ------------------------------------------------------ contractions --
-    def _pack_weights(self, layer, x_view, taps_c):
+    def _pack_weights(self, layer, x_view, taps_c, m_rows):
         if isinstance(layer, GemmQuantize):
             wc = np.ascontiguousarray(layer.w_centered.T).astype(np.int64)  # [N, K]
             cout, kh, kw, groups, cg = wc.shape[0], 1, 1, 1, wc.shape[1]
@@ -329,6 +330,12 @@ class ResidentNet:
             128 if cout <= 128 else 256)
         if groups == 1 and ct % 16 != 0:
             bn = min(bn, 64)
+        # small-M layers: narrower column tiles so that at least one tile
+        # lands on every SM (each CTA then gathers the same rows; L2 serves
+        # the repeats)
+        m_tiles = -(-m_rows // 128)
+        while bn > 32 and m_tiles * -(-cout // bn) < self.sm_count:
+            bn //= 2
         rows = _round_up(cout, bn)
         k = kh * kw * ct
         kp = _round_up(k, 16)
@@ -361,8 +368,9 @@ class ResidentNet:
             taps_c = _round_up(taps_c, 4)
             if taps_c > x_view.pix_stride and x_view.offset + taps_c > x_view.pix_stride:
                 raise UnsupportedGraph(f"{layer.name}: input channels not 4-aligned")
+        m_rows = N * geo["OH"] * geo["OW"]
         packed, rows, kp, bn, groups, ct, colsum, abssum = self._pack_weights(layer, x_view,
-                                                                              taps_c)
+                                                                              taps_c, m_rows)
         cout = layer.w_q.shape[1] if isinstance(layer, GemmQuantize) else layer.w_q.shape[0]
         x_zp = layer.in_zp
         bias = (layer.bias_int.astype(np.int64) if layer.bias_int is not None
