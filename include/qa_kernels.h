@@ -245,6 +245,25 @@ int qa_i32_to_bytes_dev(const int32_t* x, void* y, int64_t y_stride, int64_t N, 
  * recorded by any kernel on this device. */
 int qa_device_status_dev(void* stream);
 
+/* Allocation-free narrow GEMM.  No counterpart in the reference: it exists
+ * for callers that may not allocate GPU memory while they run (a service
+ * that reserves all device memory up front, work recorded into a CUDA graph,
+ * a host runtime that passes only input and output buffers), which the
+ * regular entry points cannot serve because they grow device buffers with
+ * cudaMalloc on first use.
+ *
+ * C[M,N] = A[M,K]·B[K,N] (int16 operands, int32 results, bit-identical to
+ * qa_gemm_i16_i32) on DEVICE pointers, enqueued on `stream`.  The operands
+ * are packed into a fixed 16 MiB library-owned device array that every GPU
+ * holds from library load until process exit (qa_noalloc_scratch_bytes());
+ * requests needing more (about 2*M*K + 2*N*K bytes) are rejected with an
+ * error.  The first call on each device looks up the array's address, so
+ * make it before any stream capture.  Calls share the array: calls that
+ * overlap on the GPU (different streams, or another thread) race. */
+int64_t qa_noalloc_scratch_bytes(void);
+int qa_gemm_i16_i32_noalloc_dev(const int16_t* A, const int16_t* B, int32_t* C, int64_t M,
+                                int64_t N, int64_t K, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -596,3 +596,60 @@ bool umma_conv_i16_i32_abi(const int32_t* x, const int16_t* w, int32_t* y, const
 }
 
 }  // namespace qa
+
+namespace qa {
+
+// Byte-split tensor-core GEMM with caller-provided plane storage: the same
+// packing and kernel as umma_gemm_i16_i32_abi, but the four byte planes are
+// laid out in `planes` (planes_bytes long) and the timeout status goes to
+// `status`, so nothing here allocates.  Returns false (error recorded) when
+// the planes do not fit.
+size_t umma_gemm_planes_bytes(int64_t M, int64_t N, int64_t K) {
+  const int64_t Kp = round_up(K, 16);
+  const int64_t Np = round_up(N, kSplitBN);
+  return 2 * align256((size_t)(M * Kp)) + 2 * (size_t)(Np * Kp);
+}
+
+bool umma_gemm_i16_i32_into(const int16_t* A, const int16_t* B, int32_t* C, int64_t M,
+                            int64_t N, int64_t K, uint8_t* planes, size_t planes_bytes,
+                            int32_t* status, cudaStream_t st) {
+  if (K == 0 || M * N == 0) {
+    return launch_gemm_tiled<int16_t, int16_t, int32_t>(A, B, C, M, N, K, st);
+  }
+  if (K > (int64_t(1) << 24) || umma_gemm_planes_bytes(M, N, K) > planes_bytes) {
+    set_error(kBadArgument, "byte planes exceed the provided scratch");
+    return false;
+  }
+  const int64_t Kp = round_up(K, 16);
+  const int64_t Np = round_up(N, kSplitBN);
+  const size_t a_bytes = align256((size_t)(M * Kp));
+  uint8_t *a_lo = planes, *a_hi = planes + a_bytes;
+  uint8_t *b_lo = a_hi + a_bytes, *b_hi = b_lo + Np * Kp;
+  split_rows_kernel<int16_t><<<grid_for(M * Kp, 256), 256, 0, st>>>(A, a_lo, a_hi, M, K, Kp);
+  split_transpose_kernel<<<grid_for(Np * Kp, 256), 256, 0, st>>>(B, b_lo, b_hi, K, N, Np, Kp);
+  if (cuda_failed(cudaGetLastError(), "split launch")) return false;
+  CUtensorMap tmap;
+  if (!make_weight_tmap(&tmap, b_lo, 2 * Np, Kp, kSplitBN)) return false;
+  ConvTileParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.a[0] = a_lo;
+  prm.a[1] = a_hi;
+  prm.pix_stride = Kp;
+  prm.H = prm.W = 1;
+  prm.Cin = (int32_t)Kp;
+  prm.KH = prm.KW = prm.SH = prm.SW = prm.DH = prm.DW = 1;
+  prm.OH = prm.OW = 1;
+  prm.M = M;
+  prm.K = (int32_t)Kp;
+  prm.num_kb = (int32_t)((Kp + kBKBytes - 1) / kBKBytes);
+  prm.b_plane_rows = (int32_t)Np;
+  prm.n_valid = (int32_t)N;
+  prm.y = C;
+  prm.y_ctot = N;
+  prm.ohw = 1;
+  prm.status = status;
+  return launch_umma<kSplitBN, 2, 2, 16, kEpiAcc32Row, kSplitStages>(prm, tmap, Np / kSplitBN, 1,
+                                                                      st);
+}
+
+}  // namespace qa
