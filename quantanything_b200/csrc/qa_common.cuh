@@ -74,6 +74,26 @@ int* device_status_word();
 // error and returns false if a kernel reported one.
 bool check_device_status(cudaStream_t stream);
 
+// Launches `kern` on `st`; with `pdl` the launch may overlap the previous
+// kernel of the stream (programmatic dependent launch): the kernel must call
+// griddepcontrol.wait before reading anything that kernel wrote.
+template <typename... KArgs, typename... Args>
+bool launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return !cuda_failed(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...),
+                      "cudaLaunchKernelEx");
+}
+
 inline unsigned grid_for(int64_t n, int threads, int per_thread = 1) {
   int64_t blocks = (n + (int64_t)threads * per_thread - 1) / ((int64_t)threads * per_thread);
   int64_t cap = (int64_t)sm_count() * 8;

@@ -16,6 +16,7 @@
 #include "qa_common.cuh"
 #include "qa_fixedpoint.cuh"
 #include "qa_fused_epilogue.cuh"
+#include "qa_ptx.cuh"
 #include "qa_umma.cuh"
 
 namespace qa {
@@ -79,6 +80,8 @@ struct GroupedConvParams {
 // One thread per (pixel, output channel); channel fastest so a warp reads
 // shared input bytes and writes a contiguous output run.
 __global__ void grouped_conv_kernel(const __grid_constant__ GroupedConvParams p) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = p.M * p.Cout;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -141,8 +144,7 @@ bool fused_conv_grouped(const qa_fused_conv_desc& d, cudaStream_t st) {
   fill_fused_epilogue(p.epi, d);
   const int64_t total = p.M * p.Cout;
   if (total == 0) return true;
-  grouped_conv_kernel<<<grid_for(total, 256), 256, 0, st>>>(p);
-  return !cuda_failed(cudaGetLastError(), "grouped_conv launch");
+  return launch_ex(grouped_conv_kernel, dim3(grid_for(total, 256)), dim3(256), 0, st, true, p);
 }
 
 // -------------------------------------------- graph input quantization ---
@@ -151,6 +153,8 @@ bool fused_conv_grouped(const qa_fused_conv_desc& d, cudaStream_t st) {
 __global__ void quantize_to_nhwc_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
                                         int64_t N, int64_t C, int64_t HW, int64_t pix_stride,
                                         double scale, double zp, double qmin, double qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = N * HW;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -170,6 +174,44 @@ __global__ void quantize_to_nhwc_kernel(const float* __restrict__ x, uint8_t* __
   }
 }
 
+// Four consecutive pixels per thread for the common 3-channel image stored
+// with a 4-byte pixel stride: one 16-byte load per channel plane, one
+// 16-byte store of four packed pixels.
+__device__ __forceinline__ uint32_t quantize_byte(float xv, double scale, double zp,
+                                                  double qmin, double qmax) {
+  double v = rint((double)xv / scale) + zp;
+  if (v < qmin) v = qmin;
+  if (qmax < v) v = qmax;
+  return (uint32_t)(int32_t)v & 0xFFu;
+}
+
+__global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
+                                         int C, int quads_per_image, int quads, double scale,
+                                         double zp, double qmin, double qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const uint32_t pad = (uint32_t)(int32_t)zp & 0xFFu;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += gridDim.x * blockDim.x) {
+    const int n = i / quads_per_image, q = i - n * quads_per_image;
+    uint32_t px[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (c < C) {
+        const float4 v = *reinterpret_cast<const float4*>(
+            x + ((int64_t)n * C + c) * quads_per_image * 4 + (int64_t)q * 4);
+        px[0] |= quantize_byte(v.x, scale, zp, qmin, qmax) << (8 * c);
+        px[1] |= quantize_byte(v.y, scale, zp, qmin, qmax) << (8 * c);
+        px[2] |= quantize_byte(v.z, scale, zp, qmin, qmax) << (8 * c);
+        px[3] |= quantize_byte(v.w, scale, zp, qmin, qmax) << (8 * c);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) px[k] |= pad << (8 * c);
+      }
+    }
+    *reinterpret_cast<uint4*>(y + (int64_t)i * 16) = make_uint4(px[0], px[1], px[2], px[3]);
+  }
+}
+
 // ------------------------------------------------------------------ GAP --
 // y[n, c] = clamp(mbqm(sum_p(x[n,p,c]) - HW*zp_in, m, s) + zp_out)
 // (quant_layers.py:569-590: int64 sum of centred values, no bias).
@@ -177,6 +219,8 @@ __global__ void gap_kernel(const uint8_t* __restrict__ x, int64_t x_pix_stride, 
                            int64_t N, int64_t HW, int64_t C, int64_t zp_in, int64_t m,
                            int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
                            uint8_t* __restrict__ y, int64_t y_pix_stride) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = N * C;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -223,6 +267,8 @@ __global__ void __launch_bounds__(kSoftmaxThreads)
                    double in_scale, int64_t in_zp, double out_scale, double out_zp, double qmin,
                    double qmax, int32_t* __restrict__ q_out, float* __restrict__ y_out,
                    double y_scale, int64_t y_zp) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   __shared__ double sh[32];
   const int64_t row = blockIdx.x;
   const uint8_t* xr = x + row * x_pix_stride;
@@ -260,6 +306,8 @@ struct ByteView {
 __global__ void lut_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride,
                                  int64_t rows, int64_t C, int64_t offset,
                                  const int32_t* __restrict__ lut, int64_t len) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = rows * C;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -274,6 +322,8 @@ __global__ void add_bytes_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y
                                  int64_t y_stride, int64_t rows, int64_t C, int64_t za,
                                  int64_t ma, int64_t sa, int64_t zb, int64_t mb, int64_t sb,
                                  int64_t sign, int64_t zo, int64_t qmin, int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = rows * C;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -289,6 +339,8 @@ __global__ void rescale_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_
                                      int64_t rows, int64_t C, int identity, int64_t zp_in,
                                      int64_t m, int64_t s, int64_t zp_out, int64_t qmin,
                                      int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = rows * C;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -309,6 +361,8 @@ __global__ void maxpool_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_
                                      int64_t KW, int64_t SH, int64_t SW, int64_t PH, int64_t PW,
                                      int64_t DH, int64_t DW, int64_t OH, int64_t OW,
                                      int64_t pad_value) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = N * OH * OW * C;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -334,6 +388,8 @@ __global__ void maxpool_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_
 // NHWC bytes [N, HW, C] <-> NCHW int32.
 __global__ void bytes_to_i32_kernel(ByteView x, int32_t* __restrict__ y, int64_t N, int64_t HW,
                                     int64_t C) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = N * C * HW;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -345,6 +401,8 @@ __global__ void bytes_to_i32_kernel(ByteView x, int32_t* __restrict__ y, int64_t
 
 __global__ void i32_to_bytes_kernel(const int32_t* __restrict__ x, uint8_t* __restrict__ y,
                                     int64_t y_stride, int64_t N, int64_t HW, int64_t C) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int64_t total = N * C * HW;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -354,9 +412,6 @@ __global__ void i32_to_bytes_kernel(const int32_t* __restrict__ x, uint8_t* __re
   }
 }
 
-static int finish(const char* what) {
-  return cuda_failed(cudaGetLastError(), what) ? last_status() : 0;
-}
 
 }  // namespace qa
 
@@ -372,10 +427,21 @@ QA_API int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C
   }
   const int64_t n = N * H * W;
   if (n == 0) return 0;
-  quantize_to_nhwc_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-      x, static_cast<uint8_t*>(y), N, C, H * W, pix_stride, scale, (double)zp, (double)qmin,
-      (double)qmax);
-  return finish("quantize_to_nhwc launch");
+  const int64_t HW = H * W;
+  if (pix_stride == 4 && C <= 4 && HW % 4 == 0 && HW * N / 4 < 0x7FFFFFFF &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    const int64_t quads = N * HW / 4;
+    return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
+                     (int)(HW / 4), (int)quads, scale, (double)zp, (double)qmin, (double)qmax)
+               ? 0
+               : last_status();
+  }
+  return launch_ex(quantize_to_nhwc_kernel, dim3(grid_for(n, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), N, C, HW,
+                   pix_stride, scale, (double)zp, (double)qmin, (double)qmax)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_gap_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int64_t N,
@@ -384,10 +450,11 @@ QA_API int qa_gap_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int
                       void* stream) {
   clear_error();
   if (N * C == 0) return 0;
-  gap_kernel<<<grid_for(N * C, 256), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const uint8_t*>(x), x_pix_stride, (int)x_signed, N, HW, C, zp_in, mult, shift,
-      zp_out, qmin, qmax, static_cast<uint8_t*>(y), y_pix_stride);
-  return finish("gap launch");
+  return launch_ex(gap_kernel, dim3(grid_for(N * C, 256)), dim3(256), 0, (cudaStream_t)stream,
+                   true, static_cast<const uint8_t*>(x), x_pix_stride, (int)x_signed, N, HW, C,
+                   zp_in, mult, shift, zp_out, qmin, qmax, static_cast<uint8_t*>(y), y_pix_stride)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_softmax_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int64_t N,
@@ -400,10 +467,12 @@ QA_API int qa_softmax_dev(const void* x, int64_t x_pix_stride, int64_t x_signed,
     set_error(kBadArgument, "qa_softmax_dev: too many rows");
     return last_status();
   }
-  softmax_kernel<<<(unsigned)N, kSoftmaxThreads, 0, (cudaStream_t)stream>>>(
-      static_cast<const uint8_t*>(x), x_pix_stride, (int)x_signed, C, in_scale, in_zp,
-      out_scale, (double)out_zp, (double)qmin, (double)qmax, q_out, y_out, y_scale, y_zp);
-  return finish("softmax launch");
+  return launch_ex(softmax_kernel, dim3((unsigned)N), dim3(kSoftmaxThreads), 0,
+                   (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_pix_stride,
+                   (int)x_signed, C, in_scale, in_zp, out_scale, (double)out_zp, (double)qmin,
+                   (double)qmax, q_out, y_out, y_scale, y_zp)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_lut_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
@@ -411,10 +480,11 @@ QA_API int qa_lut_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, v
                             const int32_t* lut, int64_t lut_len, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
-  lut_bytes_kernel<<<grid_for(rows * C, 256), 256, 0, (cudaStream_t)stream>>>(
+  return launch_ex(lut_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
-      static_cast<uint8_t*>(y), y_stride, rows, C, offset, lut, lut_len);
-  return finish("lut_bytes launch");
+      static_cast<uint8_t*>(y), y_stride, rows, C, offset, lut, lut_len)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_add_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, const void* b,
@@ -424,11 +494,12 @@ QA_API int qa_add_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, c
                             int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
-  add_bytes_kernel<<<grid_for(rows * C, 256), 256, 0, (cudaStream_t)stream>>>(
+  return launch_ex(add_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
       ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
-      static_cast<uint8_t*>(y), y_stride, rows, C, za, ma, sa, zb, mb, sb, sign, zo, qmin, qmax);
-  return finish("add_bytes launch");
+      static_cast<uint8_t*>(y), y_stride, rows, C, za, ma, sa, zb, mb, sb, sign, zo, qmin, qmax)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_rescale_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
@@ -437,11 +508,12 @@ QA_API int qa_rescale_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
                                 int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
-  rescale_bytes_kernel<<<grid_for(rows * C, 256), 256, 0, (cudaStream_t)stream>>>(
+  return launch_ex(rescale_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
       static_cast<uint8_t*>(y), y_stride, rows, C, (int)identity, zp_in, m, s, zp_out, qmin,
-      qmax);
-  return finish("rescale_bytes launch");
+      qmax)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
@@ -452,29 +524,32 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
   clear_error();
   const int64_t total = N * OH * OW * C;
   if (total == 0) return 0;
-  maxpool_bytes_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(
+  return launch_ex(maxpool_bytes_kernel, dim3(grid_for(total, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
       static_cast<uint8_t*>(y), y_stride, N, H, W, C, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW,
-      pad_value);
-  return finish("maxpool_bytes launch");
+      pad_value)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_bytes_to_i32_dev(const void* x, int64_t x_stride, int64_t x_signed, int32_t* y,
                                int64_t N, int64_t HW, int64_t C, void* stream) {
   clear_error();
   if (N * HW * C == 0) return 0;
-  bytes_to_i32_kernel<<<grid_for(N * HW * C, 256), 256, 0, (cudaStream_t)stream>>>(
-      ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed}, y, N, HW, C);
-  return finish("bytes_to_i32 launch");
+  return launch_ex(bytes_to_i32_kernel, dim3(grid_for(N * HW * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
+      ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed}, y, N, HW, C)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_i32_to_bytes_dev(const int32_t* x, void* y, int64_t y_stride, int64_t N,
                                int64_t HW, int64_t C, void* stream) {
   clear_error();
   if (N * HW * C == 0) return 0;
-  i32_to_bytes_kernel<<<grid_for(N * HW * C, 256), 256, 0, (cudaStream_t)stream>>>(
-      x, static_cast<uint8_t*>(y), y_stride, N, HW, C);
-  return finish("i32_to_bytes launch");
+  return launch_ex(i32_to_bytes_kernel, dim3(grid_for(N * HW * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
+      x, static_cast<uint8_t*>(y), y_stride, N, HW, C)
+             ? 0
+             : last_status();
 }
 
 QA_API int qa_device_status_dev(void* stream) {

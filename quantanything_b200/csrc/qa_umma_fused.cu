@@ -72,6 +72,7 @@ struct FusedParams {
   int64_t M;
   int32_t K, num_kb;
   int32_t n_tap;   // chunk positions covered by the tap table (num_kb * 128 / chunk)
+  int32_t stable;  // every stage always holds the same K-block (kStages % num_kb == 0)
   int32_t n_valid;
   int32_t m_tiles, n_tiles;
   int32_t vec_ok;  // every output / residual base and stride is 16-byte aligned
@@ -150,6 +151,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 2 * L::kAccs);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
+  ptx::pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int n_tile = blockIdx.x % p.n_tiles;
   const int m_first = blockIdx.x / p.n_tiles;
@@ -212,6 +214,14 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  // Static weights may stream in while the previous layer finishes; its
+  // outputs (this layer's activations) are read only after pdl_wait.
+  if (kResidentB && warp == 5 && lane == 0) {
+    ptx::mbar_arrive_expect_tx(b_full(0), (uint32_t)(p.num_kb * L::kBBlock));
+    for (int kb = 0; kb < p.num_kb; ++kb)
+      ptx::tma_load_2d(b_base + kb * L::kBBlock, &tmap_b, b_full(0), kb * kBK, n0);
+  }
+  ptx::pdl_wait();
 
   auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
     if (*s_abort) return false;
@@ -250,7 +260,9 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
         const int kend = min(kBK, p.K - kb * kBK);
         // bytes [kend, kpad) are read by the last 32-byte MMA step: zero them
         // (a stage may have held a fuller K-block of another tile before)
-        const int npos = min(kBK, (kend + 31) & ~31) / kChunk;
+        // (not needed when each stage always holds this same K-block: its
+        // padding stays zero from the initial clear)
+        const int npos = (p.stable ? kend : min(kBK, (kend + 31) & ~31)) / kChunk;
         const TapEntry* tap = s_tap + kb * kPerBlock;
         const uint32_t stage = a_base + s * L::kAStage + row_off;
         bool wrote_generic = false;
@@ -290,11 +302,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   } else if (warp == 5) {
     // ------------------------------------------------------ weight loads --
     if (lane == 0) {
-      if (kResidentB) {
-        ptx::mbar_arrive_expect_tx(b_full(0), (uint32_t)(p.num_kb * L::kBBlock));
-        for (int kb = 0; kb < p.num_kb; ++kb)
-          ptx::tma_load_2d(b_base + kb * L::kBBlock, &tmap_b, b_full(0), kb * kBK, n0);
-      } else {
+      if (!kResidentB) {
         int g = 0;
         for (int mt = m_first; mt < p.m_tiles; mt += m_step) {
           for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
@@ -528,9 +536,9 @@ bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, cudaStre
   if (per_n < 1) per_n = 1;
   if (per_n > prm.m_tiles) per_n = prm.m_tiles;
   const int64_t grid = per_n * prm.n_tiles;
-  kern<<<(unsigned)grid, Layout<BN, kChunk, kResidentB, kStagesFused>::kThreads, smem, st>>>(
-      prm, tmap);
-  return !cuda_failed(cudaGetLastError(), "fused_conv_persistent launch");
+  return launch_ex(kern, dim3((unsigned)grid),
+                   dim3(Layout<BN, kChunk, kResidentB, kStagesFused>::kThreads), smem, st,
+                   /*pdl=*/true, prm, tmap);
 }
 
 template <int BN, int kChunk>
@@ -616,6 +624,7 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   prm.K = (int32_t)K;
   prm.num_kb = (int32_t)((K + kBK - 1) / kBK);
   prm.n_tap = prm.num_kb * (kBK / chunk);
+  prm.stable = (kStagesFused % prm.num_kb) == 0;
   prm.n_valid = (int32_t)d.Cout;
   prm.m_tiles = (int32_t)m_tiles;
   prm.n_tiles = (int32_t)n_tiles;
