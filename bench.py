@@ -93,7 +93,7 @@ def cpu_reference_sample(seconds, images_per_step, steps=None):
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    images = 8
+    images = 32  # half the per-GPU batch per step: enough work for every host thread
     ips, threads, sample, times = cpu_reference_sample(0, images, steps=args.warmup)
     ips, threads, sample, times = cpu_reference_sample(0, images, steps=args.steps)
     ms = 1000.0 * sum(times) / len(times)
@@ -214,6 +214,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
+    from quantanything_b200 import native
+
+    native.get_library().set_device(local)  # library work on this rank's GPU
     qc = QuantContainer.load(networks.yolov8n_cls(), QJSON)
     net = ResidentNet(qc, PER_GPU_BATCH, dev)
     x_host = networks.images(PER_GPU_BATCH, IMAGE, seed=1000 + rank)

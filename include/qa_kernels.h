@@ -245,6 +245,15 @@ int qa_i32_to_bytes_dev(const int32_t* x, void* y, int64_t y_stride, int64_t N, 
  * recorded by any kernel on this device. */
 int qa_device_status_dev(void* stream);
 
+/* Fused network-input layer: float32 NCHW images with c_in <= 4 channels
+ * are quantized with (scale, desc->x_zp, qmin, qmax) exactly like
+ * qa_quantize_f32, convolved with the packed int8 weights of `desc`
+ * (desc->C = 4: taps packed 4 channels wide, unused channels zero) on CUDA
+ * cores, and passed through the layer epilogue of `desc` (requantize,
+ * optional LUT; no residual / concat copy).  desc->x is ignored. */
+int qa_conv_input_fused_dev(const qa_fused_conv_desc* desc, const float* x, int64_t c_in,
+                            double scale, int64_t qmin, int64_t qmax, void* stream);
+
 /* Allocation-free narrow GEMM.  No counterpart in the reference: it exists
  * for callers that may not allocate GPU memory while they run (a service
  * that reserves all device memory up front, work recorded into a CUDA graph,

@@ -22,9 +22,15 @@ bool abort_mode() {
   return g_abort_on_error == 1;
 }
 
+// The device host-pointer calls run on when the thread never called
+// qa_set_device: $QA_DEVICE if set, else the calling thread's current CUDA
+// device (so a caller that selected its GPU is never switched away from it).
 int default_device() {
   const char* v = std::getenv("QA_DEVICE");
-  return v ? std::atoi(v) : 0;
+  if (v) return std::atoi(v);
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return 0;
+  return cur;
 }
 
 thread_local ThreadContext t_ctx;

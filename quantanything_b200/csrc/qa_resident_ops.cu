@@ -11,6 +11,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 
 #include "../../include/qa_kernels.h"
 #include "qa_common.cuh"
@@ -555,4 +556,213 @@ QA_API int qa_i32_to_bytes_dev(const int32_t* x, void* y, int64_t y_stride, int6
 QA_API int qa_device_status_dev(void* stream) {
   clear_error();
   return check_device_status((cudaStream_t)stream) ? 0 : last_status();
+}
+
+// ================================================ fused input convolution ==
+// Graph input (float32 NCHW, at most 4 channels) -> quantize -> conv ->
+// layer epilogue, in one CUDA-core kernel.  A block owns an 8 x 32 tile of
+// output pixels and all output channels: it quantizes the input patch the
+// tile reads (same rounding as qa_quantize_f32) into shared memory as one
+// 4-channel word per pixel, then each thread accumulates its pixel's
+// channels with dp4a over the KH x KW taps and runs the fused epilogue.
+// Out-of-image taps hold the raw input zero point (the packed bias already
+// carries -zp * sum(w)), exactly like the tensor-core path.
+namespace qa {
+
+constexpr int kInTileH = 8, kInTileW = 32, kInThreads = kInTileH * kInTileW;
+constexpr int kInMaxCout = 64;
+
+struct InputConvParams {
+  const float* x;
+  int32_t N, C, H, W, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, Cout;
+  int32_t patch_h, patch_w;  // input pixels a tile reads
+  int32_t vec4;              // W % 4 == 0 and 16-byte aligned planes: float4 loads
+  double scale, zp, qmin, qmax;
+  const int8_t* w;  // [Cout][KH*KW*4] rows of w_kp bytes
+  int64_t w_kp;
+  int32_t fast;
+  FusedEpilogue epi;
+};
+
+__global__ void __launch_bounds__(kInThreads)
+    input_conv_kernel(const __grid_constant__ InputConvParams p) {
+  extern __shared__ uint32_t in_smem[];
+  uint32_t* s_patch = in_smem;                          // patch_h * patch_w words
+  uint32_t* s_w = s_patch + p.patch_h * p.patch_w;      // Cout * KH * KW words
+  const int tiles_x = (p.OW + kInTileW - 1) / kInTileW;
+  const int tiles_y = (p.OH + kInTileH - 1) / kInTileH;
+  const int img = blockIdx.x / (tiles_x * tiles_y);
+  const int t = blockIdx.x - img * tiles_x * tiles_y;
+  const int oy0 = (t / tiles_x) * kInTileH, ox0 = (t % tiles_x) * kInTileW;
+  const int iy0 = oy0 * p.SH - p.PH, ix0 = ox0 * p.SW - p.PW;
+  const int taps = p.KH * p.KW;
+  // weights are static: stage them before waiting for the previous kernel
+  for (int i = threadIdx.x; i < p.Cout * taps; i += kInThreads) {
+    const int co = i / taps, tap = i - co * taps;
+    s_w[i] = *reinterpret_cast<const uint32_t*>(p.w + co * p.w_kp + tap * 4);
+  }
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const uint32_t zpb = (uint32_t)(int32_t)p.zp & 0xFFu;
+  const uint32_t zp_word = zpb * 0x01010101u;
+  const int plane = p.H * p.W;
+  const float* img_base = p.x + (int64_t)img * p.C * plane;
+  if (p.vec4) {
+    // Groups of 4 image columns aligned to absolute x % 4 == 0: with W % 4 == 0
+    // a group is wholly inside or wholly outside the image, and each channel
+    // of a group is one aligned 16-byte load (all issued before any math).
+    const int xa = ix0 & ~3;                    // first group's absolute x
+    const int shift = ix0 - xa;                 // patch column 0 inside group 0
+    const int groups = (shift + p.patch_w + 3) >> 2;
+    for (int i = threadIdx.x; i < p.patch_h * groups; i += kInThreads) {
+      const int py = i / groups, gx = i - py * groups;
+      const int iy = iy0 + py, x0 = xa + 4 * gx;
+      uint32_t w4[4] = {zp_word, zp_word, zp_word, zp_word};
+      if (iy >= 0 && iy < p.H && x0 >= 0 && x0 < p.W) {
+        float4 v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (c < p.C)
+            v[c] = *reinterpret_cast<const float4*>(img_base + (int64_t)c * plane + iy * p.W + x0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w4[k] = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (c < p.C) {
+            w4[0] |= quantize_byte(v[c].x, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
+            w4[1] |= quantize_byte(v[c].y, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
+            w4[2] |= quantize_byte(v[c].z, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
+            w4[3] |= quantize_byte(v[c].w, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w4[k] |= zpb << (8 * c);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int px = 4 * gx + k - shift;  // patch column of this pixel
+        if (px >= 0 && px < p.patch_w) s_patch[py * p.patch_w + px] = w4[k];
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < p.patch_h * p.patch_w; i += kInThreads) {
+      const int py = i / p.patch_w, px = i - py * p.patch_w;
+      const int iy = iy0 + py, ix = ix0 + px;
+      uint32_t word = zp_word;
+      if (iy >= 0 && iy < p.H && ix >= 0 && ix < p.W) {
+        word = 0;
+        const float* src = img_base + iy * p.W + ix;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          word |= (c < p.C ? quantize_byte(src[(int64_t)c * plane], p.scale, p.zp, p.qmin,
+                                           p.qmax)
+                           : zpb) << (8 * c);
+      }
+      s_patch[i] = word;
+    }
+  }
+  __syncthreads();
+  const int oy = oy0 + threadIdx.x / kInTileW, ox = ox0 + threadIdx.x % kInTileW;
+  if (oy >= p.OH || ox >= p.OW) return;
+  const int64_t m = ((int64_t)img * p.OH + oy) * p.OW + ox;
+  const int ly = (oy - oy0) * p.SH, lx = (ox - ox0) * p.SW;
+  const FusedEpilogue& e = p.epi;
+  for (int c0 = 0; c0 < p.Cout; c0 += 16) {
+    int32_t acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0;
+    for (int ky = 0; ky < p.KH; ++ky)
+      for (int kx = 0; kx < p.KW; ++kx) {
+        const int word = (int)s_patch[(ly + ky * p.DH) * p.patch_w + lx + kx * p.DW];
+        const int tap = ky * p.KW + kx;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c0 + j < p.Cout) acc[j] = __dp4a(word, (int)s_w[(c0 + j) * taps + tap], acc[j]);
+      }
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = c0 + j;
+      if (n >= p.Cout) continue;
+      int64_t q;
+      const int64_t x = (int64_t)acc[j] + (e.bias ? e.bias[n] : 0);
+      if (p.fast) {
+        const int ts = (int)(31 + e.shift[n]);
+        q = ((x * e.mult[n] + ((int64_t)1 << (ts - 1))) >> ts) + e.zp;
+        q = q < e.qmin ? e.qmin : (q > e.qmax ? e.qmax : q);
+      } else {
+        q = requant_exact(x, e.mult[n], e.shift[n], e.zp, e.qmin, e.qmax);
+      }
+      if (e.lut) {
+        int64_t idx = q - e.lut_offset;
+        idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
+        q = __ldg(e.lut + idx);
+      }
+      o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+    }
+    uint8_t* op = e.out + m * e.out_pix_stride + c0;
+    if (c0 + 16 <= p.Cout && (e.out_pix_stride % 16) == 0 &&
+        (reinterpret_cast<uintptr_t>(e.out) & 15) == 0) {
+      *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c0 + j < p.Cout) op[j] = (uint8_t)(o[j >> 2] >> (8 * (j & 3)));
+    }
+  }
+}
+
+}  // namespace qa
+
+QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, int64_t c_in,
+                                   double scale, int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (!d || !x || d->C != 4 || c_in < 1 || c_in > 4 || d->groups != 1 || !d->x_signed ||
+      d->Cout > kInMaxCout || d->w_kp < d->KH * d->KW * 4 || !d->out || d->res || d->out2 ||
+      !d->mult || !d->shift || scale == 0.0) {
+    set_error(kBadArgument, "qa_conv_input_fused_dev: unsupported layer");
+    return last_status();
+  }
+  InputConvParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.N = (int32_t)d->N;
+  p.C = (int32_t)c_in;  // channels of the float tensor (taps are packed 4 wide)
+  p.H = (int32_t)d->H;
+  p.W = (int32_t)d->W;
+  p.KH = (int32_t)d->KH;
+  p.KW = (int32_t)d->KW;
+  p.SH = (int32_t)d->SH;
+  p.SW = (int32_t)d->SW;
+  p.PH = (int32_t)d->PH;
+  p.PW = (int32_t)d->PW;
+  p.DH = (int32_t)d->DH;
+  p.DW = (int32_t)d->DW;
+  p.OH = (int32_t)d->OH;
+  p.OW = (int32_t)d->OW;
+  p.Cout = (int32_t)d->Cout;
+  p.patch_h = (kInTileH - 1) * p.SH + (p.KH - 1) * p.DH + 1;
+  p.patch_w = (kInTileW - 1) * p.SW + (p.KW - 1) * p.DW + 1;
+  p.vec4 = (p.W % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  p.scale = scale;
+  p.zp = (double)d->x_zp;
+  p.qmin = (double)qmin;
+  p.qmax = (double)qmax;
+  p.w = static_cast<const int8_t*>(d->w);
+  p.w_kp = d->w_kp;
+  p.fast = d->fast ? 1 : 0;
+  fill_fused_epilogue(p.epi, *d);
+  const int64_t tiles = d->N * ((d->OH + kInTileH - 1) / kInTileH) *
+                        ((d->OW + kInTileW - 1) / kInTileW);
+  const size_t smem = ((size_t)p.patch_h * p.patch_w + (size_t)p.Cout * p.KH * p.KW) * 4;
+  if (tiles == 0) return 0;
+  if (tiles > 0x7FFFFFFF || smem > 48 * 1024) {
+    set_error(kUnsupported, "qa_conv_input_fused_dev: layer too large");
+    return last_status();
+  }
+  return launch_ex(input_conv_kernel, dim3((unsigned)tiles), dim3(kInThreads), smem,
+                   (cudaStream_t)stream, true, p)
+             ? 0
+             : last_status();
 }

@@ -31,7 +31,11 @@ def init(backend=None, timeout_s=120):
         return dist.get_rank(), dist.get_world_size()
     backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
     if backend == "nccl":
-        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        local = int(os.environ.get("LOCAL_RANK", 0))
+        torch.cuda.set_device(local)
+        from quantanything_b200 import native
+
+        native.get_library().set_device(local)
     dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s))
     return dist.get_rank(), dist.get_world_size()
 

@@ -152,6 +152,14 @@ class KernelLibrary:
             self._lib.qa_clear_error()
             raise KernelLibraryError(f"{what}: {msg}")
 
+    def set_device(self, ordinal):
+        """Binds the calling host thread's library work to GPU ``ordinal``
+        (host-pointer calls, and the device entry points' launches)."""
+        if self.has_status:
+            rc = self._lib.qa_set_device(int(ordinal))
+            if rc != 0:
+                self.check("qa_set_device")
+
     def num_threads(self):
         return self._lib.qa_num_threads()
 

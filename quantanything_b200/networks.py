@@ -147,6 +147,25 @@ def yolo_mini(seed=0, size=32, classes=10, width=16):
     return b.build(x, ["N", 3, size, size], y)
 
 
+def sppf_mini(seed=0, size=32, classes=10, width=16):
+    """Small graph with a YOLOv8 SPPF block (three chained MaxPool k5 s1 p2
+    whose outputs are concatenated), exercising integer MaxPool padded with
+    qmin (quant_layers.py:647-648)."""
+    b = GraphBuilder(seed)
+    x = "images"
+    y = b.conv_silu(x, 3, width, 3, 2)
+    y = b.conv_silu(y, width, 2 * width, 3, 2)
+    c = b.conv_silu(y, 2 * width, width, 1)
+    pools = [c]
+    for _ in range(3):
+        pools.append(b.op("MaxPool", [pools[-1]], kernel_shape=[5, 5], strides=[1, 1],
+                          pads=[2, 2, 2, 2]))
+    y = b.op("Concat", pools, axis=1)
+    y = b.conv_silu(y, 4 * width, 2 * width, 1)
+    y = b.head(y, 2 * width, classes)
+    return b.build(x, ["N", 3, size, size], y)
+
+
 def images(n, size=224, seed=1):
     """N(0, 1) pixels clipped to +-3 (the configuration's input distribution)."""
     rng = np.random.default_rng(seed)

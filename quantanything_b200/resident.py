@@ -81,6 +81,8 @@ _DEV_SIGNATURES = {
     "qa_maxpool_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 16 + [_P]),
     "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
     "qa_device_status_dev": (ctypes.c_int, [_P]),
+    "qa_conv_input_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P, _I64,
+                                               ctypes.c_double, _I64, _I64, _P]),
 }
 
 
@@ -143,7 +145,7 @@ class UnsupportedGraph(NotImplementedError):
 class ResidentNet:
     """Fused device-resident integer inference of a prepared container."""
 
-    def __init__(self, container, batch, device=None):
+    def __init__(self, container, batch, device=None, fuse_input=False):
         if not container.calibrated:
             raise ValueError("container is not calibrated")
         self.c = container
@@ -152,10 +154,14 @@ class ResidentNet:
         self.device = torch.device(device or "cuda")
         self.lib = container.lib
         device_api(self.lib)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.lib.set_device(self.device.index)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.bits, self.signed = container.layers[0].num_bits, container.layers[0].signed
         if self.bits > 8:
             raise UnsupportedGraph("the resident executor runs 8-bit graphs")
+        self.fuse_input = fuse_input
         self._keep = []
         self.steps = []
         self.launch_count = 0
@@ -249,6 +255,25 @@ class ResidentNet:
         out = g.outputs[0]
         if out not in self._outputs_f32:
             raise UnsupportedGraph("the graph output must be produced by the Softmax fallback")
+        self._fuse_input_layer(in_name)
+
+    def _fuse_input_layer(self, in_name):
+        """Graph input -> first conv as one CUDA-core kernel
+        (qa_conv_input_fused_dev), when ``fuse_input`` is set and the conv is
+        the input's only reader with at most 4 input channels and no residual
+        or concat copy.  Off by default: on B200 the separate vectorized
+        quantize + tensor-core conv is faster for the 224x224 stem."""
+        if (not self.fuse_input or len(self.steps) < 2 or self.steps[0][0] != "quantize"
+                or self.steps[1][0] != "conv"):
+            return
+        step = self.steps[1][1]
+        d = step.desc
+        readers = self._consumers.get(in_name, [])
+        if (len(readers) != 1 or readers[0] is not step.layer.node or d.groups != 1 or d.C != 4
+                or self.in_shape[1] > 4
+                or not d.x_signed or d.Cout > 64 or d.res or d.out2 or not d.out):
+            return
+        self.steps[0:2] = [("conv_input", step)]
 
     # --------------------------------------------------------- shape pass --
     def _infer_shapes(self):
@@ -572,17 +597,21 @@ class ResidentNet:
                 v = self._in_view
                 costs.append((f"quantize {N}x{C}x{H}x{W}", N * C * H * W * 4 +
                               N * H * W * v.pix_stride, 0))
-            elif kind == "conv":
+            elif kind in ("conv", "conv_input"):
                 d = payload.desc
                 M = d.N * d.OH * d.OW
                 cg = d.C
                 k = d.KH * d.KW * cg
                 x_bytes = d.N * d.H * d.W * (cg * d.groups if d.groups > 1 else cg)
+                if kind == "conv_input":  # float32 images, 3 channels read
+                    x_bytes = d.N * d.H * d.W * self.in_shape[1] * 4
                 stores = (1 if d.out else 0) + (1 if d.out2 else 0) + (1 if d.res else 0)
                 nbytes = x_bytes + d.Cout * k + M * d.Cout * stores + d.Cout * 24
                 ops = 2 * M * d.Cout * (d.KH * d.KW * cg)
                 label = (f"{payload.layer.node.op_type.lower()} {d.KH}x{d.KW}/s{d.SH} "
                          f"{cg * d.groups}->{d.Cout} @{d.OH}x{d.OW}")
+                if kind == "conv_input":
+                    label = "quantize+" + label
                 costs.append((label, nbytes, ops))
             elif kind == "gap":
                 layer, x, y, area = payload
@@ -617,6 +646,7 @@ class ResidentNet:
     # ------------------------------------------------------------- launch --
     def _launch_all(self, stream, on_step=None):
         raw = self.lib.raw
+        raw.qa_set_device(self.device.index)  # launches go to this executor's GPU
         st = ctypes.c_void_p(stream)
         n = 0
         for kind, payload in self.steps:
@@ -628,6 +658,11 @@ class ResidentNet:
                                                  qp.qmax, st)
             elif kind == "conv":
                 rc = raw.qa_conv_fused_dev(ctypes.byref(payload.desc), st)
+            elif kind == "conv_input":
+                qp = self.c.qparams[self.graph.inputs[0].name]
+                rc = raw.qa_conv_input_fused_dev(ctypes.byref(payload.desc),
+                                                 self.x_dev.data_ptr(), self.in_shape[1],
+                                                 float(qp.scale), qp.qmin, qp.qmax, st)
             elif kind == "rescale":
                 concat, idx, src, dst = payload
                 m, s = concat._mult[idx]

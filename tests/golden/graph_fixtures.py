@@ -21,6 +21,8 @@ NETWORKS = {
     "yolo_mini_int16": ("yolo_mini", {"width": 16}, "int16", 2, 4, 2),
     "yolov8n_cls_int8": ("yolov8n_cls", {}, "int8", 4, 8, 2),
     "yolov8n_cls_int16": ("yolov8n_cls", {}, "int16", 4, 8, 2),
+    "sppf_mini_int8": ("sppf_mini", {"width": 16}, "int8", 2, 4, 2),
+    "sppf_mini_uint8": ("sppf_mini", {"width": 16}, "uint8", 2, 4, 2),
 }
 
 

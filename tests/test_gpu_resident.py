@@ -22,13 +22,13 @@ GRAPHS = GOLDEN / "graphs"
 SOFTMAX_LSB = 1
 
 
-def _net(name, lib, batch):
+def _net(name, lib, batch, **kw):
     from quantanything_b200.resident import ResidentNet
 
     meta = json.loads((GRAPHS / f"{name}.meta.json").read_text())
     g = getattr(networks, meta["builder"])(**meta["kwargs"])
     qc = QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=lib)
-    return ResidentNet(qc, batch), qc, meta
+    return ResidentNet(qc, batch, **kw), qc, meta
 
 
 def _run(net, x):
@@ -91,6 +91,27 @@ def test_yolo_mini_int8_grouped_and_fused(gpu_lib):
     x = networks.images(2, meta["image"], seed=meta["eval_seed"])
     q = _run(net, x)
     ref = np.load(GRAPHS / "yolo_mini_int8.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+
+
+@pytest.mark.parametrize("name,batch", [("yolov8n_cls_int8", 3), ("yolo_mini_int8", 2)])
+def test_fused_input_layer_matches_separate_path(gpu_lib, name, batch):
+    """qa_conv_input_fused_dev (quantize + stem conv in one kernel) gives the
+    same integer tensors as the quantize kernel + tensor-core conv."""
+    fused, _, meta = _net(name, gpu_lib, batch, fuse_input=True)
+    plain, _, _ = _net(name, gpu_lib, batch)
+    assert fused.steps[0][0] == "conv_input" and plain.steps[0][0] == "quantize"
+    x = networks.images(batch, meta["image"], seed=21)
+    np.testing.assert_array_equal(_run(fused, x), _run(plain, x))
+
+
+def test_sppf_mini_int8_maxpool(gpu_lib):
+    """Resident MaxPool (padded with qmin) chained three times into a Concat."""
+    net, qc, meta = _net("sppf_mini_int8", gpu_lib, 2)
+    assert any(kind == "maxpool" for kind, _ in net.steps)
+    x = networks.images(2, meta["image"], seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / "sppf_mini_int8.npz")["q"]
     assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
 
 
