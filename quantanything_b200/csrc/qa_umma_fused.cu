@@ -45,13 +45,15 @@ constexpr int kEpilogueThreads = 128;    // one epilogue warpgroup
 constexpr int kEpilogueWarp0 = 6;
 constexpr uint64_t kBudgetCycles = 4000000000ull;  // ~2 s at 1.9 GHz
 constexpr int kTimeoutCode = 0x7002;
-constexpr int kMaxSmemLut = 256;
+// Byte-domain tables: every 8-bit value v in [-128, 255] at index v + 128.
+constexpr int kTab = 384;
 
-// Host-proven 64-bit forms of the epilogue's fixed-point steps.
+// Host-proven shortcuts of the epilogue's fixed-point steps.
 struct FastFlags {
   int32_t requant;  // acc + bias fits int32, |M0| < 2^31, 1 <= ts <= 62
-  int32_t add;      // both residual rescales: |v - z| * |m| + 2^(ts-1) < 2^62
-  int32_t rescale;  // concat copy rescale likewise
+  int32_t add_tab;  // residual Add by two int32 tables is exact (|terms| < 2^29, sign = +-1)
+  int32_t add64;    // both residual rescales: |v - z| * |m| + 2^(ts-1) < 2^62
+  int32_t r64;      // concat copy rescale likewise
 };
 
 // One K-chunk of the implicit-GEMM row: tap displacement (dy, dx) and the
@@ -88,6 +90,17 @@ __device__ __forceinline__ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) {
 __device__ __forceinline__ int64_t sbyte(uint32_t word, int j, int is_signed) {
   const uint32_t b = (word >> (8 * (j & 3))) & 0xFFu;
   return is_signed ? (int64_t)(int8_t)b : (int64_t)b;
+}
+
+__device__ __forceinline__ int32_t sbyte32(uint32_t word, int j, int is_signed) {
+  return is_signed ? ((int32_t)(word << (24 - 8 * (j & 3))) >> 24)
+                   : (int32_t)((word >> (8 * (j & 3))) & 0xFFu);
+}
+
+// Low bytes of four values, little-endian, in one word.
+__device__ __forceinline__ uint32_t pack4(int32_t a, int32_t b, int32_t c, int32_t d) {
+  return __byte_perm(__byte_perm((uint32_t)a, (uint32_t)b, 0x0040),
+                     __byte_perm((uint32_t)c, (uint32_t)d, 0x0040), 0x5410);
 }
 
 template <int BN, int kChunk, bool kResidentB, int kStages>
@@ -131,15 +144,17 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   const uint32_t a_base = base;
   const uint32_t b_base = a_base + kStages * L::kAStage;
   uint8_t* tail = sm + kStages * L::kAStage + b_blocks * L::kBBlock;
-  int64_t* s_bias = reinterpret_cast<int64_t*>(tail);
+  // per channel {bias, M0, 2^(sh-1), sh = ts - 32} of the high-word form
+  int4* s_ch = reinterpret_cast<int4*>(tail);
+  int64_t* s_bias = reinterpret_cast<int64_t*>(s_ch + BN);
   int64_t* s_mult = s_bias + BN;
   int64_t* s_shift = s_mult + BN;
   int64_t* s_rnd = s_shift + BN;                 // 2^(ts-1) of the 64-bit form
-  int32_t* s_bias32 = reinterpret_cast<int32_t*>(s_rnd + BN);
-  int32_t* s_mult32 = s_bias32 + BN;
-  int32_t* s_ts = s_mult32 + BN;
-  int32_t* s_lut = s_ts + BN;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_lut + kMaxSmemLut);
+  int32_t* s_ts = reinterpret_cast<int32_t*>(s_rnd + BN);
+  // byte-domain tables: activation, residual term a (+ zero point), residual
+  // term b (signed), concat rescale
+  int32_t* s_tab = s_ts + BN;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_tab + 4 * kTab);
   // per K-chunk gather offsets, decoded once per CTA (after the barriers)
   TapEntry* s_tap = reinterpret_cast<TapEntry*>(bars + 3 * kStages + 2 * L::kAccs + 2);
   const uint32_t bar0 = ptx::smem_addr(bars);
@@ -153,6 +168,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
 
   ptx::pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  int hi_ok = 1;  // this thread's channels all admit the high-word requantize
   const int n_tile = blockIdx.x % p.n_tiles;
   const int m_first = blockIdx.x / p.n_tiles;
   const int m_step = gridDim.x / p.n_tiles;
@@ -204,14 +220,49 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       const int ts = (int)(31 + s_shift[c]);
       s_ts[c] = ts;
       s_rnd[c] = (ts >= 1 && ts <= 62) ? ((int64_t)1 << (ts - 1)) : 0;
-      s_bias32[c] = (int32_t)s_bias[c];
-      s_mult32[c] = (int32_t)s_mult[c];
+      // (x * M0 + 2^(ts-1)) >> ts == (hi32(x * M0) + 2^(ts-33)) >> (ts - 32)
+      // for ts in [33, 62]: the low word cannot carry into the rounding
+      const bool hi = ts >= 33 && ts <= 62;
+      if (v && !hi) hi_ok = 0;
+      const int sh = hi ? ts - 32 : 1;
+      s_ch[c] = make_int4((int32_t)s_bias[c], (int32_t)s_mult[c], 1 << (sh - 1), sh);
     }
-    if (e.lut && e.lut_len <= kMaxSmemLut)
-      for (int i = et; i < e.lut_len; i += nthreads) s_lut[i] = e.lut[i];
+    // Every value the epilogue carries between steps is an 8-bit one (the
+    // host checks the clamp ranges), so each step after the requantize is a
+    // lookup in a table over [-128, 255].
+    const bool add_tab = e.res && p.fast.add_tab;
+    const int tsa = (int)(31 + e.sa), tsb = (int)(31 + e.sb), tsr = (int)(31 + e.r_s);
+    for (int i = et; i < kTab; i += nthreads) {
+      const int64_t v = i - 128;
+      if (e.lut) {
+        const int64_t idx = clamp64(v - e.lut_offset, 0, e.lut_len - 1);
+        s_tab[i] = (int32_t)clamp64(e.lut[idx], -128, 255);
+      }
+      if (add_tab) {
+        int64_t ta, tb;
+        if (p.fast.add64) {
+          ta = ((v - e.za) * e.ma + ((int64_t)1 << (tsa - 1))) >> tsa;
+          tb = ((v - e.zb) * e.mb + ((int64_t)1 << (tsb - 1))) >> tsb;
+        } else {
+          ta = clamp_i128(mbqm(v - e.za, e.ma, e.sa), -(int64_t(1) << 40), int64_t(1) << 40);
+          tb = clamp_i128(mbqm(v - e.zb, e.mb, e.sb), -(int64_t(1) << 40), int64_t(1) << 40);
+        }
+        s_tab[kTab + i] = (int32_t)(ta + e.add_zo);
+        s_tab[2 * kTab + i] = (int32_t)(e.sign * tb);
+      }
+      if (e.out2) {
+        int64_t r;
+        if (e.r_identity) r = clamp64(v, e.r_qmin, e.r_qmax);
+        else if (p.fast.r64)
+          r = clamp64(((((v - e.r_zp_in) * e.r_m) + ((int64_t)1 << (tsr - 1))) >> tsr) + e.r_zp_out,
+                      e.r_qmin, e.r_qmax);
+        else r = requant_exact(v - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
+        s_tab[3 * kTab + i] = (int32_t)r;
+      }
+    }
   }
   ptx::tc_fence_before();
-  __syncthreads();
+  const int hi_all = __syncthreads_and(hi_ok);
   ptx::tc_fence_after();
   const uint32_t tmem = *s_tmem;
   // Static weights may stream in while the previous layer finishes; its
@@ -351,15 +402,23 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   } else {
     // ---------------------------------------------------------- epilogue --
     // Warpgroup `grp` drains the tiles j with j % kGroups == grp from
-    // accumulators (grp, grp + kGroups, ...).  Per 16-column chunk the work
-    // runs in phases with the layer-uniform branches hoisted out of the
-    // unrolled element loops.
+    // accumulators (grp, grp + kGroups, ...).  Each thread owns one tile row;
+    // per 16-column chunk the layer-uniform branches are hoisted out of the
+    // unrolled element loops, and the next chunk's TMEM load is in flight
+    // while this one is processed.
     const FusedEpilogue& e = p.epi;
     const int grp = (warp - kEpilogueWarp0) / 4;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter.. belong to this warp
     const int r = quarter * 32 + lane;
-    const bool lut_smem = e.lut && e.lut_len <= kMaxSmemLut;
-    const bool fast_rq = p.fast.requant, fast_add = p.fast.add, fast_rs = p.fast.rescale;
+    const bool fast_rq = p.fast.requant;
+    const bool hi_rq = fast_rq && hi_all && e.zp > -(1 << 20) && e.zp < (1 << 20);
+    const bool has_lut = e.lut != nullptr, add_tab = p.fast.add_tab;
+    const int32_t zp32 = (int32_t)e.zp, qmin32 = (int32_t)e.qmin, qmax32 = (int32_t)e.qmax;
+    const int32_t aqmin32 = (int32_t)e.add_qmin, aqmax32 = (int32_t)e.add_qmax;
+    const int32_t* t_lut = s_tab + 128;
+    const int32_t* t_a = s_tab + kTab + 128;
+    const int32_t* t_b = s_tab + 2 * kTab + 128;
+    const int32_t* t_r = s_tab + 3 * kTab + 128;
     int j = 0;
     for (int mt = m_first; mt < p.m_tiles; mt += m_step, ++j) {
       if (j % L::kGroups != grp) continue;
@@ -371,125 +430,112 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       const int64_t m = (int64_t)mt * kBM + r;
       const bool row_ok = ok && m < p.M;
       const uint32_t lane_base = tmem + (((uint32_t)quarter * 32u) << 16) + ab * BN;
+      uint32_t v[16], vn[16];
+      ptx::tmem_ld16(lane_base, v);
+      ptx::tmem_ld_wait(v);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t v[16];
-        ptx::tmem_ld16(lane_base + c0, v);
-        ptx::tmem_ld_wait();
-        if (!row_ok || n0 + c0 >= p.n_valid) continue;
-        const int nval = min(16, p.n_valid - (n0 + c0));
-        const bool vec = p.vec_ok && nval == 16;
-        int32_t q[16];
-        // requantize
-        if (fast_rq) {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int c = c0 + jj;
-            const int32_t x = (int32_t)v[jj] + s_bias32[c];
-            const int64_t r64 = ((int64_t)x * (int64_t)s_mult32[c] + s_rnd[c]) >> s_ts[c];
-            q[jj] = (int32_t)clamp64(r64 + e.zp, e.qmin, e.qmax);
-          }
-        } else {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int c = c0 + jj;
-            q[jj] = (int32_t)requant_exact_ool((int64_t)(int32_t)v[jj] + s_bias[c], s_mult[c],
-                                               s_shift[c], e.zp, e.qmin, e.qmax);
-          }
-        }
-        // activation table
-        if (e.lut) {
-          const int32_t off = (int32_t)e.lut_offset, top = (int32_t)e.lut_len - 1;
-          if (lut_smem) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) q[jj] = s_lut[min(max(q[jj] - off, 0), top)];
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) q[jj] = __ldg(e.lut + min(max(q[jj] - off, 0), top));
-          }
-        }
-        // residual add: out = res (operand a) + sign * ours (operand b)
-        if (e.res) {
-          const uint8_t* rp = e.res + m * e.res_pix_stride + n0 + c0;
-          uint32_t w[4];
-          if (vec) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(rp);
-            w[0] = rv.x; w[1] = rv.y; w[2] = rv.z; w[3] = rv.w;
-          } else {
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              uint32_t acc = 0;
-#pragma unroll
-              for (int b = 0; b < 4; ++b)
-                if (k4 * 4 + b < nval) acc |= (uint32_t)rp[k4 * 4 + b] << (8 * b);
-              w[k4] = acc;
-            }
-          }
-          if (fast_add) {
-            const int tsa = (int)(31 + e.sa), tsb = (int)(31 + e.sb);
-            const int64_t rnda = (int64_t)1 << (tsa - 1), rndb = (int64_t)1 << (tsb - 1);
+        const bool more = c0 + 16 < BN;
+        if (more) ptx::tmem_ld16(lane_base + c0 + 16, vn);
+        if (row_ok && n0 + c0 < p.n_valid) {
+          const int nval = min(16, p.n_valid - (n0 + c0));
+          const bool vec = p.vec_ok && nval == 16;
+          int32_t q[16];
+          // requantize
+          if (hi_rq) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
-              const int64_t a = sbyte(w[jj >> 2], jj, e.res_signed);
-              const int64_t ta = ((a - e.za) * e.ma + rnda) >> tsa;
-              const int64_t tb = (((int64_t)q[jj] - e.zb) * e.mb + rndb) >> tsb;
-              q[jj] = (int32_t)clamp64(ta + e.sign * tb + e.add_zo, e.add_qmin, e.add_qmax);
+              const int4 ch = s_ch[c0 + jj];
+              const int32_t x = (int32_t)v[jj] + ch.x;
+              const int32_t t = (__mulhi(x, ch.y) + ch.z) >> ch.w;
+              q[jj] = min(max(t + zp32, qmin32), qmax32);
+            }
+          } else if (fast_rq) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int c = c0 + jj;
+              const int32_t x = (int32_t)v[jj] + s_ch[c].x;
+              const int64_t r64 = ((int64_t)x * (int64_t)s_ch[c].y + s_rnd[c]) >> s_ts[c];
+              q[jj] = (int32_t)clamp64(r64 + e.zp, e.qmin, e.qmax);
             }
           } else {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              q[jj] = (int32_t)add_exact_ool(sbyte(w[jj >> 2], jj, e.res_signed), q[jj], e);
+            for (int jj = 0; jj < 16; ++jj) {
+              const int c = c0 + jj;
+              q[jj] = (int32_t)requant_exact_ool((int64_t)(int32_t)v[jj] + s_bias[c], s_mult[c],
+                                                 s_shift[c], e.zp, e.qmin, e.qmax);
+            }
+          }
+          // activation table
+          if (has_lut) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) q[jj] = t_lut[q[jj]];
+          }
+          // residual add: out = res (operand a) + sign * ours (operand b)
+          if (e.res) {
+            const uint8_t* rp = e.res + m * e.res_pix_stride + n0 + c0;
+            uint32_t w[4];
+            if (vec) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(rp);
+              w[0] = rv.x; w[1] = rv.y; w[2] = rv.z; w[3] = rv.w;
+            } else {
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4) {
+                uint32_t acc = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+                  if (k4 * 4 + b < nval) acc |= (uint32_t)rp[k4 * 4 + b] << (8 * b);
+                w[k4] = acc;
+              }
+            }
+            if (add_tab) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const int32_t a = sbyte32(w[jj >> 2], jj, e.res_signed);
+                q[jj] = min(max(t_a[a] + t_b[q[jj]], aqmin32), aqmax32);
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                q[jj] = (int32_t)add_exact_ool(sbyte(w[jj >> 2], jj, e.res_signed), q[jj], e);
+            }
+          }
+          // primary store
+          if (e.out) {
+            uint32_t o[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              o[k4] = pack4(q[4 * k4], q[4 * k4 + 1], q[4 * k4 + 2], q[4 * k4 + 3]);
+            uint8_t* op = e.out + m * e.out_pix_stride + n0 + c0;
+            if (vec) {
+              *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
+            }
+          }
+          // rescaled copy into a Concat slice
+          if (e.out2) {
+            uint32_t o[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              o[k4] = pack4(t_r[q[4 * k4]], t_r[q[4 * k4 + 1]], t_r[q[4 * k4 + 2]],
+                            t_r[q[4 * k4 + 3]]);
+            uint8_t* op = e.out2 + m * e.out2_pix_stride + n0 + c0;
+            if (vec) {
+              *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
+            }
           }
         }
-        // primary store
-        if (e.out) {
-          uint32_t o[4];
+        if (more) {
+          ptx::tmem_ld_wait(vn);
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4)
-            o[k4] = ((uint32_t)q[4 * k4] & 0xFFu) | (((uint32_t)q[4 * k4 + 1] & 0xFFu) << 8) |
-                    (((uint32_t)q[4 * k4 + 2] & 0xFFu) << 16) | ((uint32_t)q[4 * k4 + 3] << 24);
-          uint8_t* op = e.out + m * e.out_pix_stride + n0 + c0;
-          if (vec) {
-            *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
-          }
-        }
-        // rescaled copy into a Concat slice
-        if (e.out2) {
-          int32_t q2[16];
-          if (e.r_identity) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              q2[jj] = (int32_t)clamp64(q[jj], e.r_qmin, e.r_qmax);
-          } else if (fast_rs) {
-            const int ts = (int)(31 + e.r_s);
-            const int64_t rnd = (int64_t)1 << (ts - 1);
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              q2[jj] = (int32_t)clamp64(((((int64_t)q[jj] - e.r_zp_in) * e.r_m + rnd) >> ts) +
-                                            e.r_zp_out, e.r_qmin, e.r_qmax);
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              q2[jj] = (int32_t)requant_exact_ool(q[jj] - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out,
-                                                  e.r_qmin, e.r_qmax);
-          }
-          uint32_t o[4];
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4)
-            o[k4] = ((uint32_t)q2[4 * k4] & 0xFFu) | (((uint32_t)q2[4 * k4 + 1] & 0xFFu) << 8) |
-                    (((uint32_t)q2[4 * k4 + 2] & 0xFFu) << 16) | ((uint32_t)q2[4 * k4 + 3] << 24);
-          uint8_t* op = e.out2 + m * e.out2_pix_stride + n0 + c0;
-          if (vec) {
-            *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
-          }
+          for (int jj = 0; jj < 16; ++jj) v[jj] = vn[jj];
         }
       }
       ptx::tc_fence_before();
@@ -509,8 +555,8 @@ template <int BN, int kChunk, bool kResidentB, int kStages>
 size_t smem_bytes(int num_kb) {
   using L = Layout<BN, kChunk, kResidentB, kStages>;
   const int b_blocks = kResidentB ? num_kb : kStages;
-  return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + 4 * BN * 8 +
-         3 * BN * 4 + kMaxSmemLut * 4 + (3 * kStages + 2 * L::kAccs + 2) * 8 +
+  return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + BN * 16 +
+         4 * BN * 8 + BN * 4 + 4 * kTab * 4 + (3 * kStages + 2 * L::kAccs + 2) * 8 +
          (size_t)num_kb * (kBK / kChunk) * sizeof(TapEntry);
 }
 
@@ -561,6 +607,16 @@ bool small_rescale_fast(int64_t z, int64_t m, int64_t s) {
   return bound < std::ldexp(1.0, 61);
 }
 
+// Is |mbqm(v - z, m, s)| < 2^29 for every 8-bit v (so that two such terms
+// and a zero point add up exactly in int32)?
+bool table_term_small(int64_t z, int64_t m, int64_t s) {
+  const double vmax = 383.0 + std::fabs((double)z);
+  const double t = vmax * std::fabs((double)m) * std::ldexp(1.0, -(int)(31 + s)) + 2.0;
+  return s > -64 && s < 64 && t < std::ldexp(1.0, 29);
+}
+
+bool byte_range(int64_t lo, int64_t hi) { return lo >= -128 && hi <= 255 && lo <= hi; }
+
 }  // namespace
 
 bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
@@ -568,6 +624,12 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
       d.SH <= 0 || d.SW <= 0 || d.DH <= 0 || d.DW <= 0 || d.OH <= 0 || d.OW <= 0 || d.PH < 0 ||
       d.PW < 0 || d.groups < 1) {
     set_error(kBadArgument, "qa_conv_fused_dev: invalid geometry");
+    return false;
+  }
+  // every value the epilogue passes between its steps is stored as a byte
+  if (!byte_range(d.qmin, d.qmax) || (d.res && !byte_range(d.add_qmin, d.add_qmax)) ||
+      (d.out2 && !byte_range(d.r_qmin, d.r_qmax))) {
+    set_error(kUnsupported, "qa_conv_fused_dev: output ranges must be 8-bit");
     return false;
   }
   if (d.groups > 1) return fused_conv_grouped(d, st);
@@ -635,10 +697,14 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
                al16(d.res, d.res_pix_stride);
   prm.status = device_status_word();
   prm.fast.requant = d.fast ? 1 : 0;
-  prm.fast.add = d.res ? (small_rescale_fast(d.za, d.ma, d.sa) &&
-                          small_rescale_fast(d.zb, d.mb, d.sb) && (d.sign == 1 || d.sign == -1))
-                       : 0;
-  prm.fast.rescale = d.out2 ? small_rescale_fast(d.r_zp_in, d.r_m, d.r_s) : 0;
+  prm.fast.add64 = d.res ? (small_rescale_fast(d.za, d.ma, d.sa) &&
+                            small_rescale_fast(d.zb, d.mb, d.sb))
+                         : 0;
+  prm.fast.add_tab = d.res ? (table_term_small(d.za, d.ma, d.sa) &&
+                              table_term_small(d.zb, d.mb, d.sb) && (d.sign == 1 || d.sign == -1) &&
+                              d.add_zo > -(1 << 20) && d.add_zo < (1 << 20))
+                           : 0;
+  prm.fast.r64 = d.out2 ? small_rescale_fast(d.r_zp_in, d.r_m, d.r_s) : 0;
   fill_fused_epilogue(prm.epi, d);
   if (chunk == 16) {
     switch (bn) {
