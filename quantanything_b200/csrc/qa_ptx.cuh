@@ -114,6 +114,22 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// Im2col load of a 4-D NHWC tensor: pixelsPerColumn consecutive output
+// positions (walking W, then H, then N inside the map's bounding box, with
+// its traversal strides) starting at (w, h, n), each displaced by the filter
+// tap (off_w, off_h); `c` (channels, 16-byte aligned) selects the slice.
+// Pixels outside the tensor read as zero.  The start (w, h) must lie inside
+// the bounding box.
+__device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const void* tmap, uint32_t bar,
+                                                   int c, int w, int h, int n, uint16_t off_w,
+                                                   uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
+      "l"(tmap), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -184,6 +200,19 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
 
 // Shared-memory matrix descriptor for a K-major operand tile stored in the
 // 128-byte swizzled layout (8-row atoms of 1024 bytes).
+// Shared-memory matrix descriptor for a K-major operand without swizzle:
+// 8-row x 16-byte core matrices, `lbo` bytes apart along K and `sbo` bytes
+// apart along M/N.
+__device__ __forceinline__ uint64_t smem_desc_kmajor_plain(uint32_t addr, uint32_t lbo,
+                                                           uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);          // start address
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;     // leading byte offset (K direction)
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;     // stride byte offset (8-row groups)
+  d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
+  return d;                                       // layout 0: no swizzle
+}
+
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);       // start address

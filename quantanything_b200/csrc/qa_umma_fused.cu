@@ -21,7 +21,9 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/qa_kernels.h"
 #include "qa_common.cuh"
@@ -130,11 +132,16 @@ __device__ __noinline__ int64_t add_exact_ool(int64_t a, int64_t q, const FusedE
   return clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
 }
 
+// kChunk: bytes per gathered tap chunk of the thread gather (4 or 16), or 0
+// for the TMA im2col gather (16-byte channel slices, no swizzle).
 template <int BN, int kChunk, bool kResidentB, int kStages>
 __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThreads), 1)
     fused_conv_persistent(const __grid_constant__ FusedParams p,
-                          const __grid_constant__ CUtensorMap tmap_b) {
+                          const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_a) {
   using L = Layout<BN, kChunk, kResidentB, kStages>;
+  constexpr bool kTmaA = kChunk == 0;
+  constexpr int kTapBytes = kTmaA ? 16 : kChunk;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_addr(smem_raw);
@@ -176,7 +183,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      ptx::mbar_init(a_full(s), kProducers);
+      ptx::mbar_init(a_full(s), kTmaA ? 1 : kProducers);
       ptx::mbar_init(a_empty(s), 1);
       ptx::mbar_init(b_full(s), 1);
     }
@@ -191,20 +198,29 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     ptx::tmem_alloc(ptx::smem_addr(s_tmem), L::kTmemCols);
     ptx::tmem_relinquish();
   }
-  if (warp == 5 && lane == 0) ptx::prefetch_tmap(&tmap_b);
+  if (warp == 5 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_b);
+    if (kTmaA) ptx::prefetch_tmap(&tmap_a);
+  }
   if (warp < 4) {
-    // zero every activation stage once: the K padding is never gathered
-    uint4* z = reinterpret_cast<uint4*>(sm);
-    for (int i = tid; i < kStages * L::kAStage / 16; i += kProducers) z[i] = make_uint4(0, 0, 0, 0);
-    ptx::fence_proxy_async_smem();
+    if (!kTmaA) {
+      // zero every activation stage once: the K padding is never gathered
+      // (the TMA gather leaves it stale: it meets zero weight columns)
+      uint4* z = reinterpret_cast<uint4*>(sm);
+      for (int i = tid; i < kStages * L::kAStage / 16; i += kProducers) z[i] = make_uint4(0, 0, 0, 0);
+      ptx::fence_proxy_async_smem();
+    }
     for (int i = tid; i < p.n_tap; i += kProducers) {
-      const int k = i * kChunk;
+      const int k = i * kTapBytes;
       TapEntry t{kTapNone, 0, 0};
       if (k < p.K) {
         const int tap = k / p.Cin, c = k - (k / p.Cin) * p.Cin;
         const int ky = tap / p.KW, kx = tap - (tap / p.KW) * p.KW;
         const int dy = ky * p.DH, dx = kx * p.DW;
-        t = TapEntry{(int16_t)dy, (int16_t)dx, (int32_t)((dy * p.W + dx) * p.pix_stride + c)};
+        // the TMA gather needs the channel offset, the thread gather the
+        // byte offset from the row's top-left input pixel
+        t = TapEntry{(int16_t)dy, (int16_t)dx,
+                     kTmaA ? (int32_t)c : (int32_t)((dy * p.W + dx) * p.pix_stride + c)};
       }
       s_tap[i] = t;
     }
@@ -282,7 +298,39 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     return false;
   };
 
-  if (warp < 4) {
+  if (kTmaA && warp < 4) {
+    // ------------------------------------------- activation gather (TMA) --
+    // One thread: per K-block, one im2col load per 16-byte channel slice of
+    // a tap brings that slice for all 128 output pixels of the tile, in
+    // rows of 16 bytes (slice i of the block at byte 2048 * i).
+    if (tid == 0) {
+      const int ohw = p.OH * p.OW;
+      int g = 0;
+      for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
+        const int m0 = mt * kBM;
+        const int img = m0 / ohw, rem = m0 - img * ohw;
+        const int oy = rem / p.OW, ox = rem - oy * p.OW;
+        const int w0 = ox * p.SW - p.PW, h0 = oy * p.SH - p.PH;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
+          const int nsl = min(kBK / 16, (p.K - kb * kBK + 15) / 16);
+          ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * 16));
+          const TapEntry* tap = s_tap + kb * (kBK / 16);
+          const uint32_t stage = a_base + s * L::kAStage;
+          for (int i = 0; i < nsl; ++i) {
+            const TapEntry t = tap[i];
+            ptx::tma_load_im2col_4d(stage + i * (kBM * 16), &tmap_a, a_full(s), t.delta, w0, h0,
+                                    img, (uint16_t)t.dx, (uint16_t)t.dy);
+          }
+        }
+      }
+      // after an abort, wait (bounded) for the loads still in flight
+      if (*s_abort)
+        for (int gg = max(0, g - kStages); gg < g; ++gg)
+          ptx::mbar_wait(a_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
+    }
+  } else if (warp < 4) {
     // --------------------------------------------------- activation gather --
     // Thread r owns tile row r: one output pixel whose receptive field it
     // gathers K-chunk by K-chunk using the decoded tap table (32-bit math).
@@ -290,7 +338,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t sw = (uint32_t)(r & 7);
     const int ohw = p.OH * p.OW;
-    constexpr int kPerBlock = kBK / kChunk;
+    constexpr int kPerBlock = kBK / kTapBytes;
     int g = 0;  // K-blocks issued by this CTA
     for (int mt = m_first; mt < p.m_tiles; mt += m_step) {
       const int m = mt * kBM + r;
@@ -364,6 +412,12 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           }
           if (*s_abort) break;
         }
+        // after an abort, wait (bounded) for the loads still in flight
+        if (*s_abort)
+          for (int gg = max(0, g - kStages); gg < g; ++gg)
+            ptx::mbar_wait(b_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
+      } else if (*s_abort) {
+        ptx::mbar_wait(b_full(0), 0, kBudgetCycles);
       }
     }
   } else if (warp == 4) {
@@ -389,8 +443,12 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           const uint32_t a_addr = a_base + s * L::kAStage;
           const uint32_t b_addr = b_base + (kResidentB ? kb : s) * L::kBBlock;
           for (int kk = 0; kk < ksteps; ++kk) {
-            ptx::mma_i8(d_tmem, ptx::smem_desc_sw128(a_addr + kk * 32),
-                        ptx::smem_desc_sw128(b_addr + kk * 32), idesc,
+            // TMA gather: 16-byte slices 2048 bytes apart along K, 8-row
+            // groups 128 bytes apart; thread gather: 128-byte swizzle
+            const uint64_t adesc =
+                kTmaA ? ptx::smem_desc_kmajor_plain(a_addr + kk * 2 * (kBM * 16), kBM * 16, 128)
+                      : ptx::smem_desc_sw128(a_addr + kk * 32);
+            ptx::mma_i8(d_tmem, adesc, ptx::smem_desc_sw128(b_addr + kk * 32), idesc,
                         (kb > 0 || kk > 0) ? 1u : 0u);
           }
           ptx::mma_commit(a_empty(s));
@@ -557,14 +615,15 @@ size_t smem_bytes(int num_kb) {
   const int b_blocks = kResidentB ? num_kb : kStages;
   return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + BN * 16 +
          4 * BN * 8 + BN * 4 + 4 * kTab * 4 + (3 * kStages + 2 * L::kAccs + 2) * 8 +
-         (size_t)num_kb * (kBK / kChunk) * sizeof(TapEntry);
+         (size_t)num_kb * (kBK / (kChunk == 0 ? 16 : kChunk)) * sizeof(TapEntry);
 }
 
 constexpr int kStagesFused = 4;
 constexpr size_t kSmemCap = 227 * 1024;
 
 template <int BN, int kChunk, bool kResidentB>
-bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, cudaStream_t st) {
+bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
+                       cudaStream_t st) {
   auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStagesFused>;
   const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStagesFused>(prm.num_kb);
   static size_t attr_bytes[64] = {};
@@ -584,14 +643,80 @@ bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, cudaStre
   const int64_t grid = per_n * prm.n_tiles;
   return launch_ex(kern, dim3((unsigned)grid),
                    dim3(Layout<BN, kChunk, kResidentB, kStagesFused>::kThreads), smem, st,
-                   /*pdl=*/true, prm, tmap);
+                   /*pdl=*/true, prm, tmap, tmap_a);
 }
 
 template <int BN, int kChunk>
-bool launch_bn(const FusedParams& prm, const CUtensorMap& tmap, cudaStream_t st) {
+bool launch_bn(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
+               cudaStream_t st) {
   if (smem_bytes<BN, kChunk, true, kStagesFused>(prm.num_kb) <= kSmemCap)
-    return launch_persistent<BN, kChunk, true>(prm, tmap, st);
-  return launch_persistent<BN, kChunk, false>(prm, tmap, st);
+    return launch_persistent<BN, kChunk, true>(prm, tmap, tmap_a, st);
+  return launch_persistent<BN, kChunk, false>(prm, tmap, tmap_a, st);
+}
+
+using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const int*, const int*,
+                                    cuuint32_t, cuuint32_t, const cuuint32_t*,
+                                    CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeIm2colFn im2col_encoder() {
+  static EncodeIm2colFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeIm2colFn>(ptr);
+  });
+  return fn;
+}
+
+// The thread gather stays in use when QA_FUSED_GATHER=threads.
+bool tma_gather_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("QA_FUSED_GATHER");
+    return !(v && std::strcmp(v, "threads") == 0);
+  }();
+  return on;
+}
+
+// Im2col tensor map of the layer's input for the TMA gather: 4-D {C, W, H, N}
+// uint8 over the (possibly channel-sliced) NHWC view, 16 channels x 128
+// output pixels per load.  The bounding box holds exactly the output
+// lattice (lower corner -pad, upper corner at the last output position), so
+// every tile's first pixel is a start inside it; the traversal strides are
+// the convolution strides and the taps are the load's offsets.  Returns
+// false (no error recorded) for layers the map cannot describe.
+bool make_im2col_tmap(CUtensorMap* map, const qa_fused_conv_desc& d) {
+  if (!tma_gather_enabled()) return false;
+  EncodeIm2colFn fn = im2col_encoder();
+  if (!fn) return false;
+  // out-of-image taps read zero: exact only for a zero point of 0 (or no
+  // out-of-image taps at all)
+  const bool no_oob = d.PH == 0 && d.PW == 0 && (d.OH - 1) * d.SH + (d.KH - 1) * d.DH < d.H &&
+                      (d.OW - 1) * d.SW + (d.KW - 1) * d.DW < d.W;
+  if ((d.x_zp & 0xFF) != 0 && !no_oob) return false;
+  if (d.C % 16 || d.x_pix_stride % 16 || (reinterpret_cast<uintptr_t>(d.x) & 15)) return false;
+  if (d.SH > 8 || d.SW > 8 || (d.KH - 1) * d.DH > 64 || (d.KW - 1) * d.DW > 64) return false;
+  const int64_t up_w = (d.OW - 1) * d.SW - d.PW - d.W + 1;
+  const int64_t up_h = (d.OH - 1) * d.SH - d.PH - d.H + 1;
+  if (d.PW > 128 || d.PH > 128 || up_w < -128 || up_w > 127 || up_h < -128 || up_h > 127)
+    return false;
+  if (d.W > (int64_t(1) << 31) || d.H > (int64_t(1) << 31) || d.N > (int64_t(1) << 31))
+    return false;
+  cuuint64_t dims[4] = {(cuuint64_t)d.C, (cuuint64_t)d.W, (cuuint64_t)d.H, (cuuint64_t)d.N};
+  cuuint64_t strides[3] = {(cuuint64_t)d.x_pix_stride, (cuuint64_t)(d.x_pix_stride * d.W),
+                           (cuuint64_t)(d.x_pix_stride * d.W * d.H)};
+  if (strides[2] >= (cuuint64_t(1) << 40)) return false;
+  const int lower[2] = {(int)-d.PW, (int)-d.PH};  // {W, H}
+  const int upper[2] = {(int)up_w, (int)up_h};
+  cuuint32_t estr[4] = {1u, (cuuint32_t)d.SW, (cuuint32_t)d.SH, 1u};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(d.x), dims, strides, lower,
+            upper, 16, kBM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool fits_int32_mult(int64_t m) { return m > -(int64_t(1) << 31) && m < (int64_t(1) << 31); }
@@ -662,6 +787,9 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   }
   CUtensorMap tmap;
   if (!make_weight_tmap(&tmap, d.w, d.w_rows, d.w_kp, bn)) return false;
+  CUtensorMap tmap_a;
+  std::memset(&tmap_a, 0, sizeof(tmap_a));
+  const bool tma_a = chunk == 16 && make_im2col_tmap(&tmap_a, d);
 
   FusedParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -685,7 +813,7 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   prm.M = M;
   prm.K = (int32_t)K;
   prm.num_kb = (int32_t)((K + kBK - 1) / kBK);
-  prm.n_tap = prm.num_kb * (kBK / chunk);
+  prm.n_tap = prm.num_kb * (kBK / chunk);  // chunk 16 for the TMA gather too
   prm.stable = (kStagesFused % prm.num_kb) == 0;
   prm.n_valid = (int32_t)d.Cout;
   prm.m_tiles = (int32_t)m_tiles;
@@ -706,19 +834,27 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
                            : 0;
   prm.fast.r64 = d.out2 ? small_rescale_fast(d.r_zp_in, d.r_m, d.r_s) : 0;
   fill_fused_epilogue(prm.epi, d);
-  if (chunk == 16) {
+  if (tma_a) {
     switch (bn) {
-      case 16: return launch_bn<16, 16>(prm, tmap, st);
-      case 32: return launch_bn<32, 16>(prm, tmap, st);
-      case 64: return launch_bn<64, 16>(prm, tmap, st);
-      case 128: return launch_bn<128, 16>(prm, tmap, st);
-      case 256: return launch_bn<256, 16>(prm, tmap, st);
+      case 16: return launch_bn<16, 0>(prm, tmap, tmap_a, st);
+      case 32: return launch_bn<32, 0>(prm, tmap, tmap_a, st);
+      case 64: return launch_bn<64, 0>(prm, tmap, tmap_a, st);
+      case 128: return launch_bn<128, 0>(prm, tmap, tmap_a, st);
+      case 256: return launch_bn<256, 0>(prm, tmap, tmap_a, st);
+    }
+  } else if (chunk == 16) {
+    switch (bn) {
+      case 16: return launch_bn<16, 16>(prm, tmap, tmap_a, st);
+      case 32: return launch_bn<32, 16>(prm, tmap, tmap_a, st);
+      case 64: return launch_bn<64, 16>(prm, tmap, tmap_a, st);
+      case 128: return launch_bn<128, 16>(prm, tmap, tmap_a, st);
+      case 256: return launch_bn<256, 16>(prm, tmap, tmap_a, st);
     }
   } else {
     switch (bn) {
-      case 16: return launch_bn<16, 4>(prm, tmap, st);
-      case 32: return launch_bn<32, 4>(prm, tmap, st);
-      case 64: return launch_bn<64, 4>(prm, tmap, st);
+      case 16: return launch_bn<16, 4>(prm, tmap, tmap_a, st);
+      case 32: return launch_bn<32, 4>(prm, tmap, tmap_a, st);
+      case 64: return launch_bn<64, 4>(prm, tmap, tmap_a, st);
     }
   }
   set_error(kBadArgument, "qa_conv_fused_dev: unsupported column tile");
