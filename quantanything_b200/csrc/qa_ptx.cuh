@@ -114,6 +114,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 4-D tiled TMA load (coordinates innermost first); out-of-range elements
+// read as zero.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int x,
+                                            int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
 // Im2col load of a 4-D NHWC tensor: pixelsPerColumn consecutive output
 // positions (walking W, then H, then N inside the map's bounding box, with
 // its traversal strides) starting at (w, h, n), each displaced by the filter

@@ -7,8 +7,10 @@
 //
 // Activations are NHWC byte tensors: pixel p (row of the [pixels, C] view)
 // at base + p * pix_stride, channel c at + c; int8 or uint8 by a flag.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -21,6 +23,9 @@
 #include "qa_umma.cuh"
 
 namespace qa {
+
+bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides, const uint32_t* box);
 
 __device__ __forceinline__ int64_t bval(const uint8_t* p, int is_signed) {
   return is_signed ? (int64_t)(int8_t)*p : (int64_t)*p;
@@ -186,30 +191,125 @@ __device__ __forceinline__ uint32_t quantize_byte(float xv, double scale, double
   return (uint32_t)(int32_t)v & 0xFFu;
 }
 
+// The same byte through a float product with 1/scale.  With inv = fl32(1/s)
+// the product m = fl32(x * inv) is within |m| * 2^-22.9 of the double quotient
+// fl64(x / s), so both round to the same integer unless m lies within
+// |m| * 2^-21 of a half-integer.  Those cases (ties included), NaN and inf
+// (the distance test is false) and scales the host could not invert
+// (inv = NaN) take the double division.  zp / qmin / qmax are small integers,
+// exact in float.
+struct QuantK {
+  float inv, zp, qmin, qmax;
+  float lo, hi;      // qmin - zp, qmax - zp
+  float magic_zp;    // 1.5 * 2^23 + zp
+  int32_t zp_i, qmin_i, qmax_i;
+  double scale, zpd, qmind, qmaxd;
+};
+
+// Branch-free form of quantize_byte_fast for unrolled code: the float-path
+// byte, with `ok` cleared when the element needs the double division (the
+// caller then recomputes its whole group with quantize_word_exact).
+// Clamp-then-round in the float adder.  With lo = qmin - zp and hi =
+// qmax - zp integers of at most 2^10, clamp(rint(d) + zp) ==
+// rint(clamp(m, lo, hi)) + zp whenever m and the double quotient d round
+// alike, which holds (|m - d| < 2^-12 on that range) unless the clamped
+// product lies within 2^-11 of a half-integer; saturated and infinite
+// products clamp to an integer and pass.  t = mc + (1.5 * 2^23 + zp) then
+// holds rint(mc) + zp in its low mantissa bits, so its low byte is the
+// quantized byte.  `ok` is cleared near half-integers and for NaN: the caller
+// recomputes that pixel with quantize_word_exact.
+__device__ __forceinline__ uint32_t quantize_bits_try(float xv, const QuantK& k, bool& ok) {
+  const float m = __fmul_rn(xv, k.inv);  // no contraction into the adds below
+  const float mc = fminf(fmaxf(m, k.lo), k.hi);
+  const float t = __fadd_rn(mc, k.magic_zp);
+  const float r = __fsub_rn(t, k.magic_zp);
+  ok = ok && (fabsf(mc - r) < 0.49951171875f) && (m == m);  // 0.5 - 2^-11
+  return __float_as_uint(t);
+}
+
+// Word of four channel bytes from quantize_bits_try results (byte 0 of each).
+__device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_t b2,
+                                               uint32_t b3) {
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
+// Four channel bytes of one pixel (channels >= C hold `pad`), exactly; the
+// channels are read from `src` at a stride of `plane` floats.
+__device__ __noinline__ uint32_t quantize_word_exact(const float* src, int64_t plane, int C,
+                                                     uint32_t pad, const QuantK& k) {
+  uint32_t w = 0;
+  for (int c = 0; c < 4; ++c)
+    w |= (c < C ? quantize_byte(src[c * plane], k.scale, k.zpd, k.qmind, k.qmaxd) : pad)
+         << (8 * c);
+  return w;
+}
+
+__device__ __forceinline__ uint32_t quantize_byte_fast(float xv, const QuantK& k) {
+  const float m = xv * k.inv;
+  const float r = rintf(m);
+  if (fabsf(fabsf(m - r) - 0.5f) > fabsf(m) * 4.76837158203125e-07f) {
+    const float v = fminf(fmaxf(r + k.zp, k.qmin), k.qmax);
+    return (uint32_t)__float2int_rz(v) & 0xFFu;
+  }
+  return quantize_byte(xv, k.scale, k.zpd, k.qmind, k.qmaxd);
+}
+
 __global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
-                                         int C, int quads_per_image, int quads, double scale,
-                                         double zp, double qmin, double qmax) {
+                                         int C, int quads_per_image, int quads,
+                                         const QuantK k) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const uint32_t pad = (uint32_t)(int32_t)zp & 0xFFu;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += gridDim.x * blockDim.x) {
-    const int n = i / quads_per_image, q = i - n * quads_per_image;
-    uint32_t px[4] = {0, 0, 0, 0};
+  const uint32_t pad = (uint32_t)(int32_t)k.zpd & 0xFFu;
+  // each warp takes 32 * kQ consecutive quads; lane l the quads l, l + 32,
+  // ..., all of their 16-byte loads in flight before any is used
+  constexpr int kQ = 2;
+  const int lane = threadIdx.x & 31;
+  const int warp0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int w = warp0; w * 32 * kQ < quads; w += nwarps) {
+    float4 v[kQ][4];
+    int qi[kQ];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      if (c < C) {
-        const float4 v = *reinterpret_cast<const float4*>(
-            x + ((int64_t)n * C + c) * quads_per_image * 4 + (int64_t)q * 4);
-        px[0] |= quantize_byte(v.x, scale, zp, qmin, qmax) << (8 * c);
-        px[1] |= quantize_byte(v.y, scale, zp, qmin, qmax) << (8 * c);
-        px[2] |= quantize_byte(v.z, scale, zp, qmin, qmax) << (8 * c);
-        px[3] |= quantize_byte(v.w, scale, zp, qmin, qmax) << (8 * c);
-      } else {
+    for (int u = 0; u < kQ; ++u) {
+      qi[u] = w * 32 * kQ + u * 32 + lane;
+      const bool ok = qi[u] < quads;
+      const int n = ok ? qi[u] / quads_per_image : 0, q = ok ? qi[u] - n * quads_per_image : 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) px[k] |= pad << (8 * c);
-      }
+      for (int c = 0; c < 4; ++c)
+        v[u][c] = (ok && c < C) ? *reinterpret_cast<const float4*>(
+                                      x + ((int64_t)n * C + c) * quads_per_image * 4 + (int64_t)q * 4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    *reinterpret_cast<uint4*>(y + (int64_t)i * 16) = make_uint4(px[0], px[1], px[2], px[3]);
+#pragma unroll
+    for (int u = 0; u < kQ; ++u) {
+      if (qi[u] >= quads) break;
+      uint32_t bits[4][4];  // [channel][pixel]
+      bool ok = true;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c < C) {
+          bits[c][0] = quantize_bits_try(v[u][c].x, k, ok);
+          bits[c][1] = quantize_bits_try(v[u][c].y, k, ok);
+          bits[c][2] = quantize_bits_try(v[u][c].z, k, ok);
+          bits[c][3] = quantize_bits_try(v[u][c].w, k, ok);
+        } else {
+          bits[c][0] = bits[c][1] = bits[c][2] = bits[c][3] = pad;
+        }
+      }
+      uint32_t px[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) px[b] = pack_bytes(bits[0][b], bits[1][b], bits[2][b], bits[3][b]);
+      if (!ok) {
+        // rare: an element near a rounding boundary, NaN, or no float scale;
+        // the four pixels are re-read and quantized exactly
+        const int n = qi[u] / quads_per_image, q = qi[u] - n * quads_per_image;
+        const float* src = x + (int64_t)n * C * quads_per_image * 4 + (int64_t)q * 4;
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          px[b] = quantize_word_exact(src + b, (int64_t)quads_per_image * 4, C, pad, k);
+      }
+      *reinterpret_cast<uint4*>(y + (int64_t)qi[u] * 16) = make_uint4(px[0], px[1], px[2], px[3]);
+    }
   }
 }
 
@@ -414,6 +514,33 @@ __global__ void i32_to_bytes_kernel(const int32_t* __restrict__ x, uint8_t* __re
 }
 
 
+// Host side of quantize_byte_fast: 1/scale in float, or NaN (every element
+// takes the double division) when the scale or the integer bounds are out of
+// the range the error bound covers.
+bool byte_range_host(int64_t lo, int64_t hi) { return lo >= -128 && hi <= 255 && lo <= hi; }
+
+QuantK make_quant_k(double scale, int64_t zp, int64_t qmin, int64_t qmax) {
+  QuantK k;
+  k.scale = scale;
+  k.zpd = (double)zp;
+  k.qmind = (double)qmin;
+  k.qmaxd = (double)qmax;
+  k.zp = (float)zp;
+  k.qmin = (float)qmin;
+  k.qmax = (float)qmax;
+  k.zp_i = (int32_t)zp;
+  k.qmin_i = (int32_t)qmin;
+  k.qmax_i = (int32_t)qmax;
+  k.lo = (float)(qmin - zp);
+  k.hi = (float)(qmax - zp);
+  k.magic_zp = 12582912.0f + (float)zp;
+  const bool ok = std::fabs(scale) > 1e-30 && std::fabs(scale) < 1e30 &&
+                  std::llabs(zp) <= 1024 && std::llabs(qmin - zp) <= 1024 &&
+                  std::llabs(qmax - zp) <= 1024 && qmin <= qmax;
+  k.inv = ok ? (float)(1.0 / scale) : std::nanf("");
+  return k;
+}
+
 }  // namespace qa
 
 using namespace qa;
@@ -432,9 +559,9 @@ QA_API int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C
   if (pix_stride == 4 && C <= 4 && HW % 4 == 0 && HW * N / 4 < 0x7FFFFFFF &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const int64_t quads = N * HW / 4;
-    return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
+    return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256, 2)), dim3(256), 0,
                      (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
-                     (int)(HW / 4), (int)quads, scale, (double)zp, (double)qmin, (double)qmax)
+                     (int)(HW / 4), (int)quads, make_quant_k(scale, zp, qmin, qmax))
                ? 0
                : last_status();
   }
@@ -569,147 +696,312 @@ QA_API int qa_device_status_dev(void* stream) {
 // carries -zp * sum(w)), exactly like the tensor-core path.
 namespace qa {
 
-constexpr int kInTileH = 8, kInTileW = 32, kInThreads = kInTileH * kInTileW;
+constexpr int kInTileH = 16, kInTileW = 32, kInThreads = 256;  // 512 output pixels per tile
 constexpr int kInMaxCout = 64;
+constexpr int kInMaxTaps = 16;  // K = taps * 4 bytes <= 64: four 16-byte K chunks
+constexpr int kInTab = 384;     // byte-domain activation table, index v + 128
+constexpr int kInStages = 2;    // float patches in flight per CTA
+constexpr int kInABlock = 128 * 64;  // one 128-row A block: 4 K chunks x 16 row groups x 128 B
+constexpr uint64_t kInBudget = 4000000000ull;  // bounded waits (~2 s)
 
 struct InputConvParams {
-  const float* x;
-  int32_t N, C, H, W, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, Cout;
+  int32_t N, C, H, W, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, Cout, CoutP;
   int32_t patch_h, patch_w;  // input pixels a tile reads
-  int32_t vec4;              // W % 4 == 0 and 16-byte aligned planes: float4 loads
-  double scale, zp, qmin, qmax;
+  int32_t box_w, shift;      // TMA box width (floats, multiple of 4); patch column 0 in the box
+  int32_t stage_bytes;       // one float patch (C x patch_h x box_w), 1024-aligned
+  int32_t tiles_x, tiles_y, tiles;
+  int32_t tmem_cols;
+  uint32_t pw_magic;         // ceil(2^32 / patch_w): i / patch_w == umulhi(i, pw_magic)
+  QuantK qk;
   const int8_t* w;  // [Cout][KH*KW*4] rows of w_kp bytes
   int64_t w_kp;
   int32_t fast;
+  int32_t vec_out;  // output base and pixel stride 16-byte aligned
+  int32_t* status;
   FusedEpilogue epi;
 };
 
-__global__ void __launch_bounds__(kInThreads)
-    input_conv_kernel(const __grid_constant__ InputConvParams p) {
-  extern __shared__ uint32_t in_smem[];
-  uint32_t* s_patch = in_smem;                          // patch_h * patch_w words
-  uint32_t* s_w = s_patch + p.patch_h * p.patch_w;      // Cout * KH * KW words
-  const int tiles_x = (p.OW + kInTileW - 1) / kInTileW;
-  const int tiles_y = (p.OH + kInTileH - 1) / kInTileH;
-  const int img = blockIdx.x / (tiles_x * tiles_y);
-  const int t = blockIdx.x - img * tiles_x * tiles_y;
-  const int oy0 = (t / tiles_x) * kInTileH, ox0 = (t % tiles_x) * kInTileW;
-  const int iy0 = oy0 * p.SH - p.PH, ix0 = ox0 * p.SW - p.PW;
-  const int taps = p.KH * p.KW;
-  // weights are static: stage them before waiting for the previous kernel
-  for (int i = threadIdx.x; i < p.Cout * taps; i += kInThreads) {
-    const int co = i / taps, tap = i - co * taps;
-    s_w[i] = *reinterpret_cast<const uint32_t*>(p.w + co * p.w_kp + tap * 4);
+// Bytes of 16 channel values of one pixel (16-byte store when aligned).
+__device__ __forceinline__ void store_pixel16(const int32_t (&q)[16], uint8_t* op, bool vec,
+                                              int nval) {
+  uint32_t o[4];
+#pragma unroll
+  for (int k4 = 0; k4 < 4; ++k4)
+    o[k4] = __byte_perm(__byte_perm((uint32_t)q[4 * k4], (uint32_t)q[4 * k4 + 1], 0x0040),
+                        __byte_perm((uint32_t)q[4 * k4 + 2], (uint32_t)q[4 * k4 + 3], 0x0040),
+                        0x5410);
+  if (vec) {
+    *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nval) op[j] = (uint8_t)(o[j >> 2] >> (8 * (j & 3)));
   }
+}
+
+// Graph input quantization fused with the first convolution, on the tensor
+// cores.  Persistent: each CTA walks 16 x 32 tiles of output pixels.
+//   * thread 0 keeps kInStages float input patches in flight by TMA (4-D
+//     tiled loads of C x patch_h x box_w; outside the image they read 0.0,
+//     which quantizes to the input zero point exactly as the reference pads);
+//   * the block quantizes the patch (quantize_bits_try) into one 4-channel
+//     word per input pixel, then writes the 512 implicit-GEMM rows (one
+//     4-byte tap per word, K <= 64) as four 128-row A blocks in the plain
+//     K-major layout (8-row x 16-byte core matrices);
+//   * thread 0 issues tcgen05.mma (M = 128, N = Cout rounded to 16) for the
+//     four blocks into four TMEM accumulators and commits;
+//   * all eight warps drain TMEM (warp w: lanes 32 * (w % 4), blocks
+//     2 * (w / 4) and 2 * (w / 4) + 1) through the fused epilogue
+//     (high-word requantize, byte-domain activation table).
+__global__ void __launch_bounds__(kInThreads, 2)
+    input_conv_kernel(const __grid_constant__ InputConvParams p,
+                      const __grid_constant__ CUtensorMap xmap) {
+  extern __shared__ uint8_t in_smem_raw[];
+  const uint32_t raw = ptx::smem_addr(in_smem_raw);
+  uint8_t* sm = in_smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const int CoutP = p.CoutP, taps = p.KH * p.KW;
+  const float* s_x = reinterpret_cast<const float*>(sm);
+  uint8_t* s_a = sm + kInStages * p.stage_bytes;        // 4 A blocks
+  uint8_t* s_b = s_a + 4 * kInABlock;                   // CoutP rows x 64 B, same layout
+  int4* s_ch = reinterpret_cast<int4*>(s_b + CoutP * 64);
+  int64_t* s_bias = reinterpret_cast<int64_t*>(s_ch + CoutP);
+  int64_t* s_mult = s_bias + CoutP;
+  int64_t* s_shift = s_mult + CoutP;
+  int32_t* s_tab = reinterpret_cast<int32_t*>(s_shift + CoutP);
+  int32_t* s_tapoff = s_tab + kInTab;  // patch word offset of each tap
+  uint32_t* s_patch = reinterpret_cast<uint32_t*>(s_tapoff + kInMaxTaps);  // patch_h * patch_w words
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(s_patch + p.patch_h * p.patch_w) + 7) & ~uintptr_t(7));
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + kInStages + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  const uint32_t bar0 = ptx::smem_addr(bars);
+  const uint32_t mma_bar = bar0 + 8u * kInStages;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const FusedEpilogue& e = p.epi;
+  // B: row co, K chunk j at j * (CoutP / 8) * 128 + (co / 8) * 128 + (co % 8) * 16
+  const uint32_t b_lbo = (uint32_t)(CoutP / 8) * 128u;
+
+  // static operands, loaded while the previous kernel may still run
+  int hi_ok = 1;
+  for (int i = tid; i < CoutP * 4; i += kInThreads) {
+    const int co = i / 4, j = i % 4;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (co < p.Cout) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int tap = 4 * j + q;
+        wv[q] = tap < taps ? *reinterpret_cast<const uint32_t*>(p.w + co * p.w_kp + tap * 4) : 0u;
+      }
+      v = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    *reinterpret_cast<uint4*>(s_b + j * b_lbo + (co / 8) * 128 + (co % 8) * 16) = v;
+  }
+  for (int c = tid; c < CoutP; c += kInThreads) {
+    const bool v = c < p.Cout;
+    s_bias[c] = (v && e.bias) ? e.bias[c] : 0;
+    s_mult[c] = v ? e.mult[c] : 0;
+    s_shift[c] = v ? e.shift[c] : 0;
+    const int ts = (int)(31 + s_shift[c]);
+    const bool hi = ts >= 33 && ts <= 62;
+    if (v && !hi) hi_ok = 0;
+    const int sh = hi ? ts - 32 : 1;
+    s_ch[c] = make_int4((int32_t)s_bias[c], (int32_t)s_mult[c], 1 << (sh - 1), sh);
+  }
+  if (e.lut)
+    for (int i = tid; i < kInTab; i += kInThreads) {
+      const int64_t idx = min(max((int64_t)(i - 128) - e.lut_offset, (int64_t)0), e.lut_len - 1);
+      s_tab[i] = (int32_t)min(max((int64_t)e.lut[idx], (int64_t)-128), (int64_t)255);
+    }
+  if (tid < kInMaxTaps) {
+    const int ky = tid / p.KW, kx = tid - (tid / p.KW) * p.KW;
+    s_tapoff[tid] = tid < taps ? ky * p.DH * p.patch_w + kx * p.DW : 0;
+  }
+  ptx::fence_proxy_async_smem();  // B, written here, is read by the tensor cores
+  if (tid == 0) {
+    for (int s = 0; s <= kInStages; ++s) ptx::mbar_init(bar0 + 8u * s, 1);
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&xmap);
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_addr(s_tmem), (uint32_t)p.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  const int hi_all = __syncthreads_and(hi_ok);
+  ptx::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const uint32_t zpb = (uint32_t)(int32_t)p.zp & 0xFFu;
-  const uint32_t zp_word = zpb * 0x01010101u;
-  const int plane = p.H * p.W;
-  const float* img_base = p.x + (int64_t)img * p.C * plane;
-  if (p.vec4) {
-    // Groups of 4 image columns aligned to absolute x % 4 == 0: with W % 4 == 0
-    // a group is wholly inside or wholly outside the image, and each channel
-    // of a group is one aligned 16-byte load (all issued before any math).
-    const int xa = ix0 & ~3;                    // first group's absolute x
-    const int shift = ix0 - xa;                 // patch column 0 inside group 0
-    const int groups = (shift + p.patch_w + 3) >> 2;
-    for (int i = threadIdx.x; i < p.patch_h * groups; i += kInThreads) {
-      const int py = i / groups, gx = i - py * groups;
-      const int iy = iy0 + py, x0 = xa + 4 * gx;
-      uint32_t w4[4] = {zp_word, zp_word, zp_word, zp_word};
-      if (iy >= 0 && iy < p.H && x0 >= 0 && x0 < p.W) {
-        float4 v[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if (c < p.C)
-            v[c] = *reinterpret_cast<const float4*>(img_base + (int64_t)c * plane + iy * p.W + x0);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) w4[k] = 0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c < p.C) {
-            w4[0] |= quantize_byte(v[c].x, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
-            w4[1] |= quantize_byte(v[c].y, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
-            w4[2] |= quantize_byte(v[c].z, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
-            w4[3] |= quantize_byte(v[c].w, p.scale, p.zp, p.qmin, p.qmax) << (8 * c);
-          } else {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) w4[k] |= zpb << (8 * c);
-          }
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int px = 4 * gx + k - shift;  // patch column of this pixel
-        if (px >= 0 && px < p.patch_w) s_patch[py * p.patch_w + px] = w4[k];
-      }
+
+  // tile k of this CTA is blockIdx.x + k * gridDim.x
+  auto issue = [&](int k) {
+    const int t = blockIdx.x + k * gridDim.x;
+    const int img = t / (p.tiles_x * p.tiles_y), r = t - img * p.tiles_x * p.tiles_y;
+    const int oy0 = (r / p.tiles_x) * kInTileH, ox0 = (r % p.tiles_x) * kInTileW;
+    const int s = k % kInStages;
+    ptx::mbar_arrive_expect_tx(bar0 + 8u * s, (uint32_t)(p.C * p.patch_h * p.box_w * 4));
+    ptx::tma_load_4d(ptx::smem_addr(sm) + s * p.stage_bytes, &xmap, bar0 + 8u * s,
+                     ox0 * p.SW - p.PW - p.shift, oy0 * p.SH - p.PH, 0, img);
+  };
+  const int my_tiles = p.tiles > (int)blockIdx.x
+                           ? (p.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                           : 0;
+  int issued = 0;  // tiles whose patch load thread 0 has issued
+  int mmas = 0;    // tiles whose MMAs thread 0 has committed
+  if (tid == 0)
+    for (; issued < kInStages && issued < my_tiles; ++issued) issue(issued);
+
+  const bool hi_rq = p.fast && hi_all && e.zp > -(1 << 20) && e.zp < (1 << 20);
+  const int32_t zp32 = (int32_t)e.zp, qmin32 = (int32_t)e.qmin, qmax32 = (int32_t)e.qmax;
+  const int32_t* t_lut = s_tab + 128;
+  const bool has_lut = e.lut != nullptr;
+  uint8_t* const out_p = e.out;
+  const int64_t out_stride = e.out_pix_stride;
+  const uint32_t in_zp = (uint32_t)p.qk.zp_i & 0xFFu;
+  const int plane = p.patch_h * p.box_w;  // floats per channel in a staged patch
+  const int npatch = p.patch_h * p.patch_w;
+  const uint32_t idesc = ptx::idesc_i8(128, CoutP, 1, 1);
+  const int ksteps = (taps * 4 + 31) / 32;
+  const uint32_t a_base = ptx::smem_addr(s_a), b_base = ptx::smem_addr(s_b);
+  const int quarter = warp & 3, half = warp >> 2;
+
+  int k = 0;
+  for (; k < my_tiles; ++k) {
+    const int t = blockIdx.x + k * gridDim.x;
+    const int img = t / (p.tiles_x * p.tiles_y), r = t - img * p.tiles_x * p.tiles_y;
+    const int oy0 = (r / p.tiles_x) * kInTileH, ox0 = (r % p.tiles_x) * kInTileW;
+    const int s = k % kInStages;
+    if (!ptx::mbar_wait(bar0 + 8u * s, (k / kInStages) & 1, kInBudget)) {
+      *s_abort = 1;
+      if (p.status) atomicExch(p.status, 0x7003);
     }
-  } else {
-    for (int i = threadIdx.x; i < p.patch_h * p.patch_w; i += kInThreads) {
-      const int py = i / p.patch_w, px = i - py * p.patch_w;
-      const int iy = iy0 + py, ix = ix0 + px;
-      uint32_t word = zp_word;
-      if (iy >= 0 && iy < p.H && ix >= 0 && ix < p.W) {
-        word = 0;
-        const float* src = img_base + iy * p.W + ix;
+    // (1) quantize the staged float patch into 4-channel words
+    const float* xs = s_x + s * (p.stage_bytes / 4) + p.shift;
+#pragma unroll 2
+    for (int i = tid; i < npatch; i += kInThreads) {
+      const int py = (int)__umulhi((uint32_t)i, p.pw_magic), px = i - py * p.patch_w;
+      const float* src = xs + py * p.box_w + px;
+      float f[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          word |= (c < p.C ? quantize_byte(src[(int64_t)c * plane], p.scale, p.zp, p.qmin,
-                                           p.qmax)
-                           : zpb) << (8 * c);
-      }
+      for (int c = 0; c < 4; ++c) f[c] = c < p.C ? src[c * plane] : 0.f;
+      bool ok = true;
+      uint32_t b[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) b[c] = c < p.C ? quantize_bits_try(f[c], p.qk, ok) : in_zp;
+      uint32_t word = pack_bytes(b[0], b[1], b[2], b[3]);
+      if (!ok) word = quantize_word_exact(src, plane, p.C, in_zp, p.qk);
       s_patch[i] = word;
     }
+    __syncthreads();
+    if (*s_abort) break;
+    // stage s is free again: thread 0 refills it
+    if (tid == 0 && issued < my_tiles) {
+      ptx::fence_proxy_async_smem();
+      issue(issued++);
+    }
+    // (2) the implicit-GEMM rows: pixel P of the tile is row P % 128 of
+    // block P / 128; chunk j holds taps 4j .. 4j + 3
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int P = tid + u * kInThreads;
+      const int py = P / kInTileW, px = P % kInTileW;
+      const int base = py * p.SH * p.patch_w + px * p.SW;
+      uint8_t* row = s_a + (P / 128) * kInABlock + ((P % 128) / 8) * 128 + (P % 8) * 16;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int tap = 4 * j + q;
+          // taps past the filter read word 0 (in bounds) and contribute 0
+          const int idx = tap < taps ? base + s_tapoff[tap] : 0;
+          const uint32_t wd = s_patch[idx];
+          wv[q] = tap < taps ? wd : 0u;
+        }
+        if (4 * j < taps || j < 2 * ksteps)
+          *reinterpret_cast<uint4*>(row + j * 2048) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
+    }
+    ptx::fence_proxy_async_smem();
+    __syncthreads();
+    // (3) the tensor cores: four 128-row blocks into four accumulators
+    if (tid == 0) {
+      ptx::tc_fence_after();
+#pragma unroll 1
+      for (int b = 0; b < 4; ++b)
+        for (int kk = 0; kk < ksteps; ++kk)
+          ptx::mma_i8(tmem + (uint32_t)(b * CoutP),
+                      ptx::smem_desc_kmajor_plain(a_base + b * kInABlock + kk * 4096, 2048, 128),
+                      ptx::smem_desc_kmajor_plain(b_base + kk * 2 * b_lbo, b_lbo, 128), idesc,
+                      kk > 0 ? 1u : 0u);
+      ptx::mma_commit(mma_bar);
+      ++mmas;
+    }
+    if (!ptx::mbar_wait(mma_bar, k & 1, kInBudget)) {
+      *s_abort = 1;
+      if (p.status) atomicExch(p.status, 0x7003);
+    }
+    __syncwarp();
+    ptx::tc_fence_after();
+    // (4) epilogue: this warp's 32 rows of blocks 2 * half and 2 * half + 1
+#pragma unroll 1
+    for (int bb = 0; bb < 2; ++bb) {
+      const int b = 2 * half + bb;
+      const int P = b * 128 + quarter * 32 + lane;
+      const int oy = oy0 + P / kInTileW, ox = ox0 + P % kInTileW;
+      const bool valid = oy < p.OH && ox < p.OW && !*s_abort;
+      const int64_t m = ((int64_t)img * p.OH + oy) * p.OW + ox;
+#pragma unroll 1
+      for (int c0 = 0; c0 < CoutP; c0 += 16) {
+        uint32_t v[16];
+        ptx::tmem_ld16(tmem + (((uint32_t)quarter * 32u) << 16) + (uint32_t)(b * CoutP + c0), v);
+        ptx::tmem_ld_wait(v);
+        const int nval = min(16, p.Cout - c0);
+        if (!valid || nval <= 0) continue;
+        int32_t q[16];
+        if (hi_rq) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int4 ch = s_ch[c0 + j];
+            const int32_t rq = (__mulhi((int32_t)v[j] + ch.x, ch.y) + ch.z) >> ch.w;
+            q[j] = min(max(rq + zp32, qmin32), qmax32);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int c = c0 + j;
+            const int64_t xv = (int64_t)(int32_t)v[j] + s_bias[c];
+            q[j] = p.fast ? (int32_t)requant_fast(xv, s_mult[c], (int)(31 + s_shift[c]), e.zp,
+                                                  e.qmin, e.qmax)
+                          : (int32_t)requant_exact(xv, s_mult[c], s_shift[c], e.zp, e.qmin,
+                                                   e.qmax);
+          }
+        }
+        if (has_lut) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) q[j] = t_lut[q[j]];
+        }
+        store_pixel16(q, out_p + m * out_stride + c0, p.vec_out && nval == 16, nval);
+      }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();  // TMEM and the A blocks are rewritten by the next tile
+    if (*s_abort) break;
   }
+  // after an abort, wait (bounded) for the patch loads and the MMAs still in
+  // flight before the CTA's shared memory and TMEM are released
+  if (tid == 0 && *s_abort) {
+    for (int kk = k; kk < issued; ++kk)
+      ptx::mbar_wait(bar0 + 8u * (kk % kInStages), (kk / kInStages) & 1, kInBudget);
+    if (mmas > k) ptx::mbar_wait(mma_bar, k & 1, kInBudget);
+  }
+  ptx::tc_fence_before();
   __syncthreads();
-  const int oy = oy0 + threadIdx.x / kInTileW, ox = ox0 + threadIdx.x % kInTileW;
-  if (oy >= p.OH || ox >= p.OW) return;
-  const int64_t m = ((int64_t)img * p.OH + oy) * p.OW + ox;
-  const int ly = (oy - oy0) * p.SH, lx = (ox - ox0) * p.SW;
-  const FusedEpilogue& e = p.epi;
-  for (int c0 = 0; c0 < p.Cout; c0 += 16) {
-    int32_t acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0;
-    for (int ky = 0; ky < p.KH; ++ky)
-      for (int kx = 0; kx < p.KW; ++kx) {
-        const int word = (int)s_patch[(ly + ky * p.DH) * p.patch_w + lx + kx * p.DW];
-        const int tap = ky * p.KW + kx;
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c0 + j < p.Cout) acc[j] = __dp4a(word, (int)s_w[(c0 + j) * taps + tap], acc[j]);
-      }
-    uint32_t o[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int n = c0 + j;
-      if (n >= p.Cout) continue;
-      int64_t q;
-      const int64_t x = (int64_t)acc[j] + (e.bias ? e.bias[n] : 0);
-      if (p.fast) {
-        const int ts = (int)(31 + e.shift[n]);
-        q = ((x * e.mult[n] + ((int64_t)1 << (ts - 1))) >> ts) + e.zp;
-        q = q < e.qmin ? e.qmin : (q > e.qmax ? e.qmax : q);
-      } else {
-        q = requant_exact(x, e.mult[n], e.shift[n], e.zp, e.qmin, e.qmax);
-      }
-      if (e.lut) {
-        int64_t idx = q - e.lut_offset;
-        idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
-        q = __ldg(e.lut + idx);
-      }
-      o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
-    }
-    uint8_t* op = e.out + m * e.out_pix_stride + c0;
-    if (c0 + 16 <= p.Cout && (e.out_pix_stride % 16) == 0 &&
-        (reinterpret_cast<uintptr_t>(e.out) & 15) == 0) {
-      *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (c0 + j < p.Cout) op[j] = (uint8_t)(o[j >> 2] >> (8 * (j & 3)));
-    }
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
   }
 }
 
@@ -719,14 +1011,18 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
                                    double scale, int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (!d || !x || d->C != 4 || c_in < 1 || c_in > 4 || d->groups != 1 || !d->x_signed ||
-      d->Cout > kInMaxCout || d->w_kp < d->KH * d->KW * 4 || !d->out || d->res || d->out2 ||
+      d->Cout > kInMaxCout || d->KH * d->KW > kInMaxTaps || d->w_kp < d->KH * d->KW * 4 ||
+      !d->out || d->res || d->out2 ||
       !d->mult || !d->shift || scale == 0.0) {
     set_error(kBadArgument, "qa_conv_input_fused_dev: unsupported layer");
     return last_status();
   }
+  if (!byte_range_host(d->qmin, d->qmax)) {
+    set_error(kUnsupported, "qa_conv_input_fused_dev: output range must be 8-bit");
+    return last_status();
+  }
   InputConvParams p;
   std::memset(&p, 0, sizeof(p));
-  p.x = x;
   p.N = (int32_t)d->N;
   p.C = (int32_t)c_in;  // channels of the float tensor (taps are packed 4 wide)
   p.H = (int32_t)d->H;
@@ -742,27 +1038,65 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
   p.OH = (int32_t)d->OH;
   p.OW = (int32_t)d->OW;
   p.Cout = (int32_t)d->Cout;
+  p.CoutP = (p.Cout + 15) / 16 * 16;
   p.patch_h = (kInTileH - 1) * p.SH + (p.KH - 1) * p.DH + 1;
   p.patch_w = (kInTileW - 1) * p.SW + (p.KW - 1) * p.DW + 1;
-  p.vec4 = (p.W % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-  p.scale = scale;
-  p.zp = (double)d->x_zp;
-  p.qmin = (double)qmin;
-  p.qmax = (double)qmax;
+  // exact for i * patch_w < 2^32 (i < patch_h * patch_w < 2^16 here)
+  p.pw_magic = (uint32_t)(((uint64_t)1 << 32) / (uint64_t)p.patch_w + 1);
+  // every tile's first input column is ox0 * SW - PW with ox0 a multiple of
+  // 32: the same residue mod 4, so one shift aligns every box start to 16 B
+  p.shift = (int32_t)(((-(d->PW)) % 4 + 4) % 4);
+  p.box_w = (p.patch_w + p.shift + 3) / 4 * 4;
+  p.stage_bytes = (p.C * p.patch_h * p.box_w * 4 + 1023) / 1024 * 1024;
+  p.tiles_x = (p.OW + kInTileW - 1) / kInTileW;
+  p.tiles_y = (p.OH + kInTileH - 1) / kInTileH;
+  const int64_t tiles = d->N * (int64_t)p.tiles_x * p.tiles_y;
+  p.tiles = (int32_t)tiles;
+  p.qk = make_quant_k(scale, d->x_zp, qmin, qmax);
+  {
+    int cols = 32;
+    while (cols < 4 * p.CoutP) cols *= 2;
+    p.tmem_cols = cols;
+  }
   p.w = static_cast<const int8_t*>(d->w);
   p.w_kp = d->w_kp;
   p.fast = d->fast ? 1 : 0;
+  p.vec_out = (reinterpret_cast<uintptr_t>(d->out) & 15) == 0 && d->out_pix_stride % 16 == 0;
+  p.status = device_status_word();
   fill_fused_epilogue(p.epi, *d);
-  const int64_t tiles = d->N * ((d->OH + kInTileH - 1) / kInTileH) *
-                        ((d->OW + kInTileW - 1) / kInTileW);
-  const size_t smem = ((size_t)p.patch_h * p.patch_w + (size_t)p.Cout * p.KH * p.KW) * 4;
   if (tiles == 0) return 0;
-  if (tiles > 0x7FFFFFFF || smem > 48 * 1024) {
-    set_error(kUnsupported, "qa_conv_input_fused_dev: layer too large");
+  const size_t smem = 1024 + (size_t)kInStages * p.stage_bytes + 4 * kInABlock +
+                      (size_t)p.CoutP * 64 + (size_t)p.CoutP * (16 + 3 * 8) + kInTab * 4 +
+                      (size_t)kInMaxTaps * 4 + (size_t)p.patch_h * p.patch_w * 4 + 8 +
+                      (kInStages + 1) * 8 + 16;
+  // zero padding in float must quantize to the zero point, and the box must
+  // fit the TMA limits
+  if (tiles > 0x7FFFFFFF || smem > 110 * 1024 || p.box_w > 256 || p.patch_h > 256 ||
+      (int64_t)p.patch_h * p.patch_w >= 65536 ||
+      d->W % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15)) {
+    set_error(kUnsupported, "qa_conv_input_fused_dev: layer geometry outside the kernel's limits");
     return last_status();
   }
-  return launch_ex(input_conv_kernel, dim3((unsigned)tiles), dim3(kInThreads), smem,
-                   (cudaStream_t)stream, true, p)
+  CUtensorMap xmap;
+  const uint64_t dims[4] = {(uint64_t)d->W, (uint64_t)d->H, (uint64_t)c_in, (uint64_t)d->N};
+  const uint64_t strides[3] = {(uint64_t)d->W * 4, (uint64_t)(d->W * d->H) * 4,
+                               (uint64_t)(d->W * d->H * c_in) * 4};
+  const uint32_t box[4] = {(uint32_t)p.box_w, (uint32_t)p.patch_h, (uint32_t)c_in, 1u};
+  if (!encode_tiled_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, box))
+    return last_status();
+  static size_t attr_bytes[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || attr_bytes[dev] < smem) {
+    if (cuda_failed(cudaFuncSetAttribute(input_conv_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                    "cudaFuncSetAttribute(input_conv)"))
+      return last_status();
+    if (dev >= 0 && dev < 64) attr_bytes[dev] = smem;
+  }
+  const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count() * 2);
+  return launch_ex(input_conv_kernel, dim3((unsigned)grid), dim3(kInThreads), smem,
+                   (cudaStream_t)stream, true, p, xmap)
              ? 0
              : last_status();
 }

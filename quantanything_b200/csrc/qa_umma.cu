@@ -338,6 +338,34 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
+// Tiled tensor map of any rank (dims / box innermost first, strides in
+// bytes for dims 1..rank-1), no interleave, no swizzle, zero fill.  Returns
+// false with the error recorded.
+bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error(kCudaError, "cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  CUresult r = fn(map, type, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(kCudaError, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return false;
+  }
+  return true;
+}
+
 // 2-D uint8 tensor map over [rows, row_bytes] with a 128 x box_rows box in
 // the 128-byte swizzle.
 bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,

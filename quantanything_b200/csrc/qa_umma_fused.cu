@@ -112,6 +112,10 @@ struct Layout {
   // Two epilogue warpgroups alternate tiles when four accumulators fit in
   // TMEM (BN <= 128); each group owns two accumulators (double buffered).
   static constexpr int kGroups = BN <= 128 ? 2 : 1;
+  // with two groups and at least 32 columns, both groups drain every tile
+  // (group g its half of the columns); with 16 columns they alternate tiles
+  static constexpr bool kSplit = kGroups == 2 && BN >= 32;
+  static constexpr int kGroupCols = kSplit ? BN / 2 : BN;
   static constexpr int kAccs = 2 * kGroups;
   static constexpr int kThreads = 192 + kGroups * kEpilogueThreads;
   static constexpr int kCols = kAccs * BN;
@@ -189,7 +193,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     }
     for (int b = 0; b < L::kAccs; ++b) {
       ptx::mbar_init(acc_full0 + 8u * b, 1);
-      ptx::mbar_init(acc_empty0 + 8u * b, kEpilogueThreads);
+      ptx::mbar_init(acc_empty0 + 8u * b, L::kSplit ? 2 * kEpilogueThreads : kEpilogueThreads);
     }
     *s_abort = 0;
     ptx::fence_mbar_init();
@@ -361,7 +365,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
         // (a stage may have held a fuller K-block of another tile before)
         // (not needed when each stage always holds this same K-block: its
         // padding stays zero from the initial clear)
-        const int npos = (p.stable ? kend : min(kBK, (kend + 31) & ~31)) / kChunk;
+        const int npos = (p.stable ? kend : min(kBK, (kend + 31) & ~31)) / kTapBytes;
         const TapEntry* tap = s_tap + kb * kPerBlock;
         const uint32_t stage = a_base + s * L::kAStage + row_off;
         bool wrote_generic = false;
@@ -459,8 +463,9 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     }
   } else {
     // ---------------------------------------------------------- epilogue --
-    // Warpgroup `grp` drains the tiles j with j % kGroups == grp from
-    // accumulators (grp, grp + kGroups, ...).  Each thread owns one tile row;
+    // With kSplit, warpgroup `grp` drains columns [grp * kGroupCols, +
+    // kGroupCols) of every tile; otherwise the tiles j with j % kGroups == grp.
+    // Each thread owns one tile row;
     // per 16-column chunk the layer-uniform branches are hoisted out of the
     // unrolled element loops, and the next chunk's TMEM load is in flight
     // while this one is processed.
@@ -477,33 +482,52 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     const int32_t* t_a = s_tab + kTab + 128;
     const int32_t* t_b = s_tab + 2 * kTab + 128;
     const int32_t* t_r = s_tab + 3 * kTab + 128;
+    // Everything the tile loop reads from the parameters, read once: the
+    // parameter block is reached through a generic pointer here, and every
+    // such read is a long-latency load.
+    const uint8_t* const res_p = e.res;
+    const int64_t res_stride = e.res_pix_stride;
+    const int res_signed = (int)e.res_signed;
+    uint8_t* const out_p = e.out;
+    const int64_t out_stride = e.out_pix_stride;
+    uint8_t* const out2_p = e.out2;
+    const int64_t out2_stride = e.out2_pix_stride;
+    const int n_valid = p.n_valid;
+    const bool vec_ok = p.vec_ok != 0;
+    const int64_t M = p.M;
     int j = 0;
     for (int mt = m_first; mt < p.m_tiles; mt += m_step, ++j) {
-      if (j % L::kGroups != grp) continue;
+      if (!L::kSplit && j % L::kGroups != grp) continue;
+      const int cbase = L::kSplit ? grp * L::kGroupCols : 0;
       const int ab = j % L::kAccs;
       const int use = j / L::kAccs;
       const bool ok = wait(acc_full0 + 8u * ab, use & 1);
       __syncwarp();
       ptx::tc_fence_after();
       const int64_t m = (int64_t)mt * kBM + r;
-      const bool row_ok = ok && m < p.M;
-      const uint32_t lane_base = tmem + (((uint32_t)quarter * 32u) << 16) + ab * BN;
+      const bool row_ok = ok && m < M;
+      // this row's first output channel in each destination
+      const uint8_t* const res_row = res_p + m * res_stride + n0 + cbase;
+      uint8_t* const out_row = out_p + m * out_stride + n0 + cbase;
+      uint8_t* const out2_row = out2_p + m * out2_stride + n0 + cbase;
+      const uint32_t lane_base = tmem + (((uint32_t)quarter * 32u) << 16) + ab * BN + cbase;
       uint32_t v[16], vn[16];
       ptx::tmem_ld16(lane_base, v);
       ptx::tmem_ld_wait(v);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        const bool more = c0 + 16 < BN;
+      for (int c0 = 0; c0 < L::kGroupCols; c0 += 16) {
+        const int cc = cbase + c0;  // tile column of this chunk
+        const bool more = c0 + 16 < L::kGroupCols;
         if (more) ptx::tmem_ld16(lane_base + c0 + 16, vn);
-        if (row_ok && n0 + c0 < p.n_valid) {
-          const int nval = min(16, p.n_valid - (n0 + c0));
-          const bool vec = p.vec_ok && nval == 16;
+        if (row_ok && n0 + cc < n_valid) {
+          const int nval = min(16, n_valid - (n0 + cc));
+          const bool vec = vec_ok && nval == 16;
           int32_t q[16];
           // requantize
           if (hi_rq) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
-              const int4 ch = s_ch[c0 + jj];
+              const int4 ch = s_ch[cc + jj];
               const int32_t x = (int32_t)v[jj] + ch.x;
               const int32_t t = (__mulhi(x, ch.y) + ch.z) >> ch.w;
               q[jj] = min(max(t + zp32, qmin32), qmax32);
@@ -511,7 +535,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           } else if (fast_rq) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
-              const int c = c0 + jj;
+              const int c = cc + jj;
               const int32_t x = (int32_t)v[jj] + s_ch[c].x;
               const int64_t r64 = ((int64_t)x * (int64_t)s_ch[c].y + s_rnd[c]) >> s_ts[c];
               q[jj] = (int32_t)clamp64(r64 + e.zp, e.qmin, e.qmax);
@@ -519,7 +543,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           } else {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
-              const int c = c0 + jj;
+              const int c = cc + jj;
               q[jj] = (int32_t)requant_exact_ool((int64_t)(int32_t)v[jj] + s_bias[c], s_mult[c],
                                                  s_shift[c], e.zp, e.qmin, e.qmax);
             }
@@ -530,8 +554,8 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
             for (int jj = 0; jj < 16; ++jj) q[jj] = t_lut[q[jj]];
           }
           // residual add: out = res (operand a) + sign * ours (operand b)
-          if (e.res) {
-            const uint8_t* rp = e.res + m * e.res_pix_stride + n0 + c0;
+          if (res_p) {
+            const uint8_t* rp = res_row + c0;
             uint32_t w[4];
             if (vec) {
               const uint4 rv = *reinterpret_cast<const uint4*>(rp);
@@ -549,22 +573,22 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
             if (add_tab) {
 #pragma unroll
               for (int jj = 0; jj < 16; ++jj) {
-                const int32_t a = sbyte32(w[jj >> 2], jj, e.res_signed);
+                const int32_t a = sbyte32(w[jj >> 2], jj, res_signed);
                 q[jj] = min(max(t_a[a] + t_b[q[jj]], aqmin32), aqmax32);
               }
             } else {
 #pragma unroll
               for (int jj = 0; jj < 16; ++jj)
-                q[jj] = (int32_t)add_exact_ool(sbyte(w[jj >> 2], jj, e.res_signed), q[jj], e);
+                q[jj] = (int32_t)add_exact_ool(sbyte(w[jj >> 2], jj, res_signed), q[jj], e);
             }
           }
           // primary store
-          if (e.out) {
+          if (out_p) {
             uint32_t o[4];
 #pragma unroll
             for (int k4 = 0; k4 < 4; ++k4)
               o[k4] = pack4(q[4 * k4], q[4 * k4 + 1], q[4 * k4 + 2], q[4 * k4 + 3]);
-            uint8_t* op = e.out + m * e.out_pix_stride + n0 + c0;
+            uint8_t* op = out_row + c0;
             if (vec) {
               *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
             } else {
@@ -574,13 +598,13 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
             }
           }
           // rescaled copy into a Concat slice
-          if (e.out2) {
+          if (out2_p) {
             uint32_t o[4];
 #pragma unroll
             for (int k4 = 0; k4 < 4; ++k4)
               o[k4] = pack4(t_r[q[4 * k4]], t_r[q[4 * k4 + 1]], t_r[q[4 * k4 + 2]],
                             t_r[q[4 * k4 + 3]]);
-            uint8_t* op = e.out2 + m * e.out2_pix_stride + n0 + c0;
+            uint8_t* op = out2_row + c0;
             if (vec) {
               *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
             } else {

@@ -145,7 +145,7 @@ class UnsupportedGraph(NotImplementedError):
 class ResidentNet:
     """Fused device-resident integer inference of a prepared container."""
 
-    def __init__(self, container, batch, device=None, fuse_input=False):
+    def __init__(self, container, batch, device=None, fuse_input=True):
         if not container.calibrated:
             raise ValueError("container is not calibrated")
         self.c = container
@@ -258,11 +258,12 @@ class ResidentNet:
         self._fuse_input_layer(in_name)
 
     def _fuse_input_layer(self, in_name):
-        """Graph input -> first conv as one CUDA-core kernel
-        (qa_conv_input_fused_dev), when ``fuse_input`` is set and the conv is
-        the input's only reader with at most 4 input channels and no residual
-        or concat copy.  Off by default: on B200 the separate vectorized
-        quantize + tensor-core conv is faster for the 224x224 stem."""
+        """Graph input -> first conv as one kernel (qa_conv_input_fused_dev:
+        float patches by TMA, quantize in shared memory, tcgen05 MMA, fused
+        epilogue), when ``fuse_input`` is set and the conv is the input's only
+        reader with at most 4 input channels, at most 16 taps and no residual
+        or concat copy, and its input tile fits the kernel's limits (the
+        same checks the entry point makes)."""
         if (not self.fuse_input or len(self.steps) < 2 or self.steps[0][0] != "quantize"
                 or self.steps[1][0] != "conv"):
             return
@@ -270,8 +271,18 @@ class ResidentNet:
         d = step.desc
         readers = self._consumers.get(in_name, [])
         if (len(readers) != 1 or readers[0] is not step.layer.node or d.groups != 1 or d.C != 4
-                or self.in_shape[1] > 4
-                or not d.x_signed or d.Cout > 64 or d.res or d.out2 or not d.out):
+                or self.in_shape[1] > 4 or d.KH * d.KW > 16 or self.in_shape[3] % 4
+                or not d.x_signed or d.Cout > 64 or d.res or d.out2 or not d.out
+                or d.qmin < -128 or d.qmax > 255):
+            return
+        patch_h = 15 * d.SH + (d.KH - 1) * d.DH + 1
+        patch_w = 31 * d.SW + (d.KW - 1) * d.DW + 1
+        box_w = _round_up(patch_w + (-d.PW) % 4, 4)
+        cout_p = _round_up(d.Cout, 16)
+        stage = _round_up(self.in_shape[1] * patch_h * box_w * 4, 1024)
+        smem = (1024 + 2 * stage + 4 * 128 * 64 + cout_p * 64 + cout_p * 40 + 384 * 4 + 64
+                + patch_h * patch_w * 4 + 48)
+        if box_w > 256 or patch_h > 256 or patch_h * patch_w >= 65536 or smem > 110 * 1024:
             return
         self.steps[0:2] = [("conv_input", step)]
 

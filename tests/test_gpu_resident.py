@@ -99,7 +99,7 @@ def test_fused_input_layer_matches_separate_path(gpu_lib, name, batch):
     """qa_conv_input_fused_dev (quantize + stem conv in one kernel) gives the
     same integer tensors as the quantize kernel + tensor-core conv."""
     fused, _, meta = _net(name, gpu_lib, batch, fuse_input=True)
-    plain, _, _ = _net(name, gpu_lib, batch)
+    plain, _, _ = _net(name, gpu_lib, batch, fuse_input=False)
     assert fused.steps[0][0] == "conv_input" and plain.steps[0][0] == "quantize"
     x = networks.images(batch, meta["image"], seed=21)
     np.testing.assert_array_equal(_run(fused, x), _run(plain, x))
