@@ -190,6 +190,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dropin", action="store_true")
+    ap.add_argument("--profile-forwards", type=int, default=0,
+                    help="run this many plain forward passes of the workload and exit "
+                         "(the command the ncu summaries under profiles/ are taken with)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -223,6 +226,14 @@ def main():
     x_pinned = torch.from_numpy(x_host).pin_memory()
     out_pinned = torch.empty((PER_GPU_BATCH, 1000), dtype=torch.float32).pin_memory()
     net.x_dev.copy_(x_pinned)
+    if args.profile_forwards:
+        for _ in range(args.profile_forwards):
+            net.forward_device()
+        torch.cuda.synchronize(dev)
+        net.check_status()
+        print(json.dumps({"profile_forwards": args.profile_forwards, "launches_per_forward":
+                          len(net.steps)}))
+        return
     net.capture()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
