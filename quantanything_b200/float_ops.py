@@ -292,6 +292,23 @@ def softmax_axis(node, opset, ndim):
     return _axis(node.attr("axis", -1 if opset >= 13 else 1), ndim)
 
 
+@op("LogSoftmax")
+def _log_softmax(node, inputs, opset, **kw):
+    """float64, max-subtracted (float_ops.py:388-395)."""
+    x = inputs[0].astype(np.float64)
+    axis = softmax_axis(node, opset, x.ndim)
+    z = x - x.max(axis=axis, keepdims=True)
+    return (z - np.log(np.exp(z).sum(axis=axis, keepdims=True))).astype(np.float32)
+
+
+@op("ReduceMean")
+def _reduce_mean(node, inputs, opset, **kw):
+    x = inputs[0]
+    axes = _attr_or_input(node, inputs, 1, "axes")
+    axes = tuple(_axis(a, x.ndim) for a in axes) if axes is not None and len(axes) else None
+    return x.mean(axis=axes, keepdims=bool(node.attr("keepdims", 1))).astype(np.float32)
+
+
 @op("Softmax")
 def _softmax(node, inputs, opset, **kw):
     """float64, max-subtracted (float_ops.py:380-385)."""
@@ -302,6 +319,34 @@ def _softmax(node, inputs, opset, **kw):
 
 
 # ---------------------------------------------------------------- shapes --
+# ONNX TensorProto element types -> NumPy (the ones a Cast can name)
+_ONNX_DTYPES = {1: np.float32, 2: np.uint8, 3: np.int8, 4: np.uint16, 5: np.int16, 6: np.int32,
+                7: np.int64, 9: np.bool_, 10: np.float16, 11: np.float64, 12: np.uint32,
+                13: np.uint64}
+
+
+@op("Cast")
+def _cast(node, inputs, opset, **kw):
+    return inputs[0].astype(_ONNX_DTYPES[int(node.attr("to"))])
+
+
+@op("Shape")
+def _shape(node, inputs, opset, **kw):
+    shape = np.array(inputs[0].shape, dtype=np.int64)
+    return shape[node.attr("start", 0): node.attr("end", None)]
+
+
+@op("Gather")
+def _gather(node, inputs, opset, **kw):
+    return np.take(inputs[0], np.asarray(inputs[1]).astype(np.int64), axis=node.attr("axis", 0))
+
+
+@op("Expand")
+def _expand(node, inputs, opset, **kw):
+    shape = tuple(int(v) for v in np.asarray(inputs[1]).reshape(-1))
+    return np.broadcast_to(inputs[0], np.broadcast_shapes(inputs[0].shape, shape)).copy()
+
+
 @op("Identity", "Dropout")
 def _identity(node, inputs, opset, **kw):
     return inputs[0]
@@ -409,6 +454,25 @@ def pool_geometry(node, x_shape):
             out = -(-(size - ek) // strides[ax]) + 1
             pads[ax + 2] += max((out - 1) * strides[ax] + ek - size, 0)
     return kernel, strides, dil, tuple(pads)
+
+
+@op("AveragePool")
+def _avgpool(node, inputs, opset, **kw):
+    """Window mean; padded positions count only with ``count_include_pad``
+    (float_ops.py:563-577)."""
+    x = inputs[0].astype(np.float32)
+    kernel, strides, dil, pads = pool_geometry(node, x.shape)
+    spec = ((0, 0), (0, 0), (pads[0], pads[2]), (pads[1], pads[3]))
+
+    def window_sum(t):
+        ek = [d * (k - 1) + 1 for k, d in zip(kernel, dil)]
+        win = sliding_window_view(np.pad(t, spec), tuple(ek), axis=(2, 3))
+        return win[:, :, :: strides[0], :: strides[1], :: dil[0], :: dil[1]].sum(axis=(4, 5))
+
+    total = window_sum(x)
+    if node.attr("count_include_pad", 0):
+        return (total / (kernel[0] * kernel[1])).astype(np.float32)
+    return (total / window_sum(np.ones_like(x[:1, :1]))).astype(np.float32)
 
 
 @op("MaxPool")

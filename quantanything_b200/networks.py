@@ -15,6 +15,8 @@ quantizer turns into a lookup table.
 * :func:`yolo_mini` -- the small YOLO-like test graph shape of the
   reference's test-suite (stem, C2f-style split/add/concat, depthwise +
   pointwise, GAP, Gemm, Softmax) at a configurable width.
+* :func:`vit` -- a Vision Transformer (ViT-B/16 at full size) in the
+  reference's post-pass form.
 """
 
 import numpy as np
@@ -164,6 +166,93 @@ def sppf_mini(seed=0, size=32, classes=10, width=16):
     y = b.conv_silu(y, 4 * width, 2 * width, 1)
     y = b.head(y, 2 * width, classes)
     return b.build(x, ["N", 3, size, size], y)
+
+
+def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, mlp=4,
+        std=None):
+    """A Vision Transformer in the reference's post-pass form (the structure
+    of its ``build_vit`` test model after graph_passes.py): patch-embedding
+    Conv -> Reshape -> Transpose, a constant cls token concatenated in front
+    (the batch Expand folded), a positional-embedding Add, ``depth`` pre-LN
+    blocks (LayerNormalization; MatMul with the bias as third input; head
+    split by Reshape / Transpose / Split / Squeeze; activation x activation
+    MatMuls, the 1/sqrt(head_dim) Mul and Softmax; GELU as one fused
+    element-wise erf chain), the cls token gathered before the final
+    LayerNormalization, and a Gemm head.  The batch is static (it appears in
+    the Reshape shapes).  ``std``: weight init (trunc-normal-like, default
+    1/sqrt(fan_in); ViT-B/16 uses 0.02).
+
+    ``vit(img=224, patch=16, dim=768, heads=12, depth=12, classes=1000,
+    batch=B, std=0.02)`` is ViT-B/16."""
+    b = GraphBuilder(seed)
+    rng = b.rng
+    hd = dim // heads
+    grid = img // patch
+    tokens = grid * grid + 1
+    f32 = np.float32
+
+    def weight(fan_in, shape):
+        s_ = std if std is not None else 1.0 / np.sqrt(fan_in)
+        return np.clip(rng.standard_normal(shape), -2, 2).astype(f32) * f32(s_)
+
+    def linear(x, cin, cout):
+        w = b.const(weight(cin, (cin, cout)), "w")
+        bias = b.const(rng.normal(0.0, 0.02, cout).astype(f32), "b")
+        return b.op("MatMul", [x, w, bias])
+
+    def layer_norm(x):
+        # the reference's passes move the LayerNorm gain into the next linear
+        # layer; random-init gains are 1 and shifts 0
+        return b.op("LayerNormalization", [x, b.const(np.ones(dim, f32), "ln_g"),
+                                           b.const(np.zeros(dim, f32), "ln_b")],
+                    axis=-1, epsilon=1e-6)
+
+    def gelu(x):
+        d, e, a, m, y = (b.name(t) for t in ("div", "erf", "add", "mul", "gelu"))
+        sub = [Node(b.name("Div"), "Div", [x, "sqrt2"], [d]),
+               Node(b.name("Erf"), "Erf", [d], [e]),
+               Node(b.name("Add"), "Add", [e, "one"], [a]),
+               Node(b.name("Mul"), "Mul", [x, a], [m]),
+               Node(b.name("Mul"), "Mul", [m, "half"], [y])]
+        consts = {"sqrt2": np.float32(np.sqrt(2.0)), "one": np.float32(1.0),
+                  "half": np.float32(0.5)}
+        b.nodes.append(Node(b.name("GELU") + "_fused", "FusedElementwise", [x], [y],
+                            {"nodes": sub, "consts": consts}))
+        return y
+
+    pw = weight(3 * patch * patch, (dim, 3, patch, patch))
+    x = b.op("Conv", ["images", b.const(pw, "w"), b.const(rng.normal(0, 0.02, dim).astype(f32),
+                                                           "b")],
+             kernel_shape=[patch, patch], strides=[patch, patch], pads=[0, 0, 0, 0],
+             dilations=[1, 1], group=1)
+    x = b.op("Reshape", [x, b.const(np.array([batch, dim, -1], np.int64), "shape")])
+    x = b.op("Transpose", [x], perm=[0, 2, 1])
+    cls = np.broadcast_to(rng.normal(0.0, 0.1, (1, 1, dim)), (batch, 1, dim)).astype(f32)
+    x = b.op("Concat", [b.const(np.ascontiguousarray(cls), "cls"), x], axis=1)
+    x = b.op("Add", [x, b.const(rng.normal(0.0, 0.1, (1, tokens, dim)).astype(f32), "pos")])
+    for _ in range(depth):
+        h = layer_norm(x)
+        qkv = linear(h, dim, 3 * dim)
+        qkv = b.op("Reshape", [qkv, b.const(np.array([batch, tokens, 3, heads, hd], np.int64),
+                                             "shape")])
+        qkv = b.op("Transpose", [qkv], perm=[2, 0, 3, 1, 4])
+        parts = b.op("Split", [qkv], n_out=3, axis=0)
+        q, k, v = [b.op("Squeeze", [t, b.const(np.array([0], np.int64), "axes")])
+                   for t in parts]
+        att = b.op("MatMul", [q, b.op("Transpose", [k], perm=[0, 1, 3, 2])])
+        att = b.op("Mul", [att, b.const(np.float32(hd ** -0.5), "scale")])
+        att = b.op("Softmax", [att], axis=-1)
+        o = b.op("Transpose", [b.op("MatMul", [att, v])], perm=[0, 2, 1, 3])
+        o = b.op("Reshape", [o, b.const(np.array([batch, tokens, dim], np.int64), "shape")])
+        x = b.op("Add", [x, linear(o, dim, dim)])
+        h = gelu(linear(layer_norm(x), dim, mlp * dim))
+        x = b.op("Add", [x, linear(h, mlp * dim, dim)])
+    x = b.op("Gather", [x, b.const(np.array(0, np.int64), "index")], axis=1)
+    x = layer_norm(x)
+    w = weight(dim, (classes, dim))
+    y = b.op("Gemm", [x, b.const(w, "head_w"), b.const(rng.normal(0, 0.02, classes).astype(f32),
+                                                        "head_b")], transB=1)
+    return b.build("images", [batch, 3, img, img], y)
 
 
 def images(n, size=224, seed=1):

@@ -23,6 +23,9 @@ NETWORKS = {
     "yolov8n_cls_int16": ("yolov8n_cls", {}, "int16", 4, 8, 2),
     "sppf_mini_int8": ("sppf_mini", {"width": 16}, "int8", 2, 4, 2),
     "sppf_mini_uint8": ("sppf_mini", {"width": 16}, "uint8", 2, 4, 2),
+    # the batch is static in a ViT graph: calibration and evaluation use it
+    "vit_mini_int8": ("vit", {"batch": 4}, "int8", 2, 4, 4),
+    "vit_mini_int16": ("vit", {"batch": 4}, "int16", 2, 4, 4),
 }
 
 
@@ -59,12 +62,14 @@ def layer_digests(container):
     return out
 
 
-def generate(outdir):
+def generate(outdir, only=None):
     from quantanything_b200 import networks
     from quantization import QuantContainer
 
     outdir.mkdir(parents=True, exist_ok=True)
     for name, (builder, kw, qtype, nb, bs, ne) in NETWORKS.items():
+        if only and name not in only:
+            continue
         g = getattr(networks, builder)(**kw)
         size = g.inputs[0].shape[2]
         rg = to_reference_graph(g)

@@ -287,15 +287,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
     ap.add_argument("--graphs", action="store_true")
+    ap.add_argument("--only", nargs="*", help="graph fixtures to (re)write; nothing else")
     args = ap.parse_args()
     native = _setup_reference(Path(args.ref))
-    np.savez_compressed(HERE / "kernels.npz", **kernel_cases(native))
-    (HERE / "host_math.json").write_text(json.dumps(host_math_cases(), indent=1))
-    (HERE / "configs.json").write_text(json.dumps(config_digests(native), indent=1))
-    if args.graphs:
+    if not args.only:
+        np.savez_compressed(HERE / "kernels.npz", **kernel_cases(native))
+        (HERE / "host_math.json").write_text(json.dumps(host_math_cases(), indent=1))
+        (HERE / "configs.json").write_text(json.dumps(config_digests(native), indent=1))
+    if args.graphs or args.only:
         from tests.golden import graph_fixtures  # noqa: E402
 
-        graph_fixtures.generate(HERE / "graphs")
+        graph_fixtures.generate(HERE / "graphs", args.only)
     print("fixtures written to", HERE)
 
 
