@@ -254,6 +254,53 @@ int qa_device_status_dev(void* stream);
 int qa_conv_input_fused_dev(const qa_fused_conv_desc* desc, const float* x, int64_t c_in,
                             double scale, int64_t qmin, int64_t qmax, void* stream);
 
+/* Transformer (ViT) graphs, activations as byte rows [rows, features].
+ *
+ * Token embedding: out[n, 0, :] = cls_row, out[n, t, d] =
+ * clamp(ta[x[n, t-1, d] + 128] + pos[t * D + d], qmin, qmax) for t >= 1: the
+ * Concat of the class token with the patch tokens followed by the
+ * positional-embedding Add (quant_layers.py:486-513, 543-560), as exact
+ * integer tables (ta: 384 entries over byte values -128..255). */
+int qa_vit_embed_dev(const void* x, int64_t x_stride, int32_t x_signed, const int32_t* ta,
+                     const int32_t* pos, const void* cls_row, int64_t qmin, int64_t qmax,
+                     void* out, int64_t out_stride, int64_t B, int64_t T, int64_t D,
+                     void* stream);
+
+/* LayerNormalization over the last axis as the reference's float fallback
+ * (float_ops.py:336-347 between qa_dequantize_f32 and qa_quantize_f32);
+ * beta may be NULL. */
+int qa_layernorm_bytes_dev(const void* x, int64_t x_stride, int32_t x_signed, int64_t zp_in,
+                           double scale_in, const float* gamma, const float* beta, double eps,
+                           double scale_out, int64_t zp_out, int64_t qmin, int64_t qmax,
+                           void* out, int64_t out_stride, int64_t rows, int64_t D,
+                           void* stream);
+
+/* Multi-head self-attention of one block, fused: scores MatMul, the Mul by
+ * 1/sqrt(head_dim) (mul_table: 384 entries), Softmax over the keys and the
+ * MatMul with V, each quantized like the reference's float fallbacks
+ * (quant_layers.py:195-205), written in the head-merged [B*T, H*hd] layout.
+ * qkv rows hold q | k | v (H*hd bytes each).  s_params: scales of
+ * {scores, Mul output, softmax output, attention output}; z_params:
+ * {scores zp, qmin, qmax, softmax zp, qmin, qmax, output zp, qmin, qmax,
+ * Mul output zp} (host arrays, read at the call).  T <= 256, head_dim <= 128
+ * and a multiple of 4. */
+int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t qkv_signed,
+                           int64_t z_qkv, double s_qkv, int64_t B, int64_t T, int64_t H,
+                           int64_t hd, const double* s_params, const int64_t* z_params,
+                           const int32_t* mul_table, int32_t p_signed, void* out,
+                           int64_t out_stride, void* stream);
+
+/* out[r, :] = table[x[r * every + first, :] + 128]: a Gather of one token per
+ * image through its requantization (table: 384 entries). */
+int qa_gather_table_dev(const void* x, int64_t x_stride, int32_t x_signed, int64_t every,
+                        int64_t first, const int32_t* table, void* out, int64_t out_stride,
+                        int64_t rows, int64_t D, void* stream);
+
+/* Byte rows to int32 and/or float32 (qa_dequantize_f32 semantics). */
+int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_signed, int64_t zp,
+                           double scale, int32_t* q_out, float* f_out, int64_t rows, int64_t C,
+                           void* stream);
+
 /* Allocation-free narrow GEMM.  No counterpart in the reference: it exists
  * for callers that may not allocate GPU memory while they run (a service
  * that reserves all device memory up front, work recorded into a CUDA graph,

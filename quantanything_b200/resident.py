@@ -83,6 +83,18 @@ _DEV_SIGNATURES = {
     "qa_device_status_dev": (ctypes.c_int, [_P]),
     "qa_conv_input_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P, _I64,
                                                ctypes.c_double, _I64, _I64, _P]),
+    "qa_vit_embed_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _P, _P, _P, _I64, _I64, _P,
+                                        _I64, _I64, _I64, _I64, _P]),
+    "qa_layernorm_bytes_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _I64, ctypes.c_double,
+                                              _P, _P, ctypes.c_double, ctypes.c_double, _I64,
+                                              _I64, _I64, _P, _I64, _I64, _I64, _P]),
+    "qa_attention_bytes_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _I64, ctypes.c_double,
+                                              _I64, _I64, _I64, _I64, _P, _P, _P,
+                                              ctypes.c_int32, _P, _I64, _P]),
+    "qa_gather_table_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _I64, _I64, _P, _P, _I64,
+                                           _I64, _I64, _P]),
+    "qa_dequantize_rows_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _I64, ctypes.c_double,
+                                              _P, _P, _I64, _I64, _P]),
 }
 
 
@@ -446,26 +458,27 @@ class ResidentNet:
             d.lut, d.lut_offset, d.lut_len = ldev.data_ptr(), int(a.lut_offset), len(a.lut)
             fused_away.add(act.name)
             produced, out_qp = act.outputs[0], a.out_qp[0]
-            # residual Add fused when it is the only consumer of the LUT output
-            add = self._only_consumer(produced)
-            if add is not None and isinstance(layers[add.name], AddQuantize):
-                al = layers[add.name]
-                other = [i for i in add.inputs if i != produced]
-                if len(other) == 1 and other[0] in self._views and (
-                        add.inputs[1] == produced or al._sign == 1):
-                    res = self._views[other[0]]
-                    (ma, sa), (mb, sb) = al._mult
-                    qa, qb = al.in_qp
-                    if add.inputs[1] == produced:  # out = res (a) + sign * ours (b)
-                        d.za, d.ma, d.sa, d.zb, d.mb, d.sb = qa.zp, ma, sa, qb.zp, mb, sb
-                    else:  # ours is operand a, sign == +1: the sum commutes
-                        d.za, d.ma, d.sa, d.zb, d.mb, d.sb = qb.zp, mb, sb, qa.zp, ma, sa
-                    d.res, d.res_pix_stride, d.res_signed = res.ptr, res.pix_stride, int(
-                        res.signed)
-                    o = al.out_qp[0]
-                    d.sign, d.add_zo, d.add_qmin, d.add_qmax = al._sign, o.zp, o.qmin, o.qmax
-                    fused_away.add(add.name)
-                    produced, out_qp = add.outputs[0], o
+        # residual Add fused when it is the only consumer (of the LUT output, or
+        # of the contraction itself)
+        add = self._only_consumer(produced)
+        if add is not None and isinstance(layers[add.name], AddQuantize):
+            al = layers[add.name]
+            other = [i for i in add.inputs if i != produced]
+            if len(other) == 1 and other[0] in self._views and (
+                    add.inputs[1] == produced or al._sign == 1):
+                res = self._views[other[0]]
+                (ma, sa), (mb, sb) = al._mult
+                qa, qb = al.in_qp
+                if add.inputs[1] == produced:  # out = res (a) + sign * ours (b)
+                    d.za, d.ma, d.sa, d.zb, d.mb, d.sb = qa.zp, ma, sa, qb.zp, mb, sb
+                else:  # ours is operand a, sign == +1: the sum commutes
+                    d.za, d.ma, d.sa, d.zb, d.mb, d.sb = qb.zp, mb, sb, qa.zp, ma, sa
+                d.res, d.res_pix_stride, d.res_signed = res.ptr, res.pix_stride, int(
+                    res.signed)
+                o = al.out_qp[0]
+                d.sign, d.add_zo, d.add_qmin, d.add_qmax = al._sign, o.zp, o.qmin, o.qmax
+                fused_away.add(add.name)
+                produced, out_qp = add.outputs[0], o
         NO, HO, WO = (N, geo["OH"], geo["OW"])
         view, copy = self._destination(produced, out_qp, NO, HO, WO, cout)
         if view is not None and (self._consumers.get(produced) or produced in self.graph.outputs
@@ -721,13 +734,17 @@ class ResidentNet:
                                         o.qmax, self.out_q.data_ptr(), self.out_f32.data_ptr(),
                                         float(o.scale), o.zp, st)
             else:
-                raise AssertionError(kind)
+                rc = self._launch_step(kind, payload, raw, st)
             _check(self.lib, rc, f"{kind} step")
             if on_step is not None:
                 on_step(n)
             n += 1
         self.launch_count = n
         return n
+
+    def _launch_step(self, kind, payload, raw, st):
+        """Launch of a step kind this class does not plan (subclasses)."""
+        raise AssertionError(kind)
 
     def forward_device(self, x=None):
         """Enqueues the whole forward on the current stream (eagerly, no graph).
