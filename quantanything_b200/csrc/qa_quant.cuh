@@ -1,0 +1,106 @@
+// Exact per-tensor quantization of float32 values on the device: the
+// reference's qa_quantize_f32 (qa_kernels.cpp:363-386),
+//   q = clamp(rint((double)x / scale) + zp, qmin, qmax)
+// (NaN -> 0 in the low byte, as x86's truncating conversion leaves it),
+// computed through a float product with 1/scale and exact fallbacks.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+
+namespace qa {
+
+// The double-precision definition, for the rare elements the float path
+// cannot decide.
+__device__ __forceinline__ uint32_t quantize_byte(float xv, double scale, double zp,
+                                                  double qmin, double qmax) {
+  double v = rint((double)xv / scale) + zp;
+  if (v < qmin) v = qmin;
+  if (qmax < v) v = qmax;
+  return (uint32_t)(int32_t)v & 0xFFu;
+}
+
+struct QuantK {
+  float inv, zp, qmin, qmax;
+  float lo, hi;      // qmin - zp, qmax - zp
+  float magic_zp;    // 1.5 * 2^23 + zp
+  int32_t zp_i, qmin_i, qmax_i;
+  double scale, zpd, qmind, qmaxd;
+};
+
+// Clamp-then-round in the float adder.  With lo = qmin - zp and hi =
+// qmax - zp integers of at most 2^10, clamp(rint(d) + zp) ==
+// rint(clamp(m, lo, hi)) + zp whenever m = fl32(x * fl32(1/scale)) and the
+// double quotient d = x / scale round alike, which holds (|m - d| < 2^-12 on
+// that range) unless the clamped product lies within 2^-11 of a
+// half-integer; saturated and infinite products clamp to an integer and
+// pass.  t = mc + (1.5 * 2^23 + zp) then holds rint(mc) + zp in its low
+// mantissa bits, so its low byte is the quantized byte.  `ok` is cleared
+// near half-integers, for NaN and when the host could not invert the scale
+// (inv = NaN): the caller then uses quantize_byte.
+__device__ __forceinline__ uint32_t quantize_bits_try(float xv, const QuantK& k, bool& ok) {
+  const float m = __fmul_rn(xv, k.inv);  // no contraction into the adds below
+  const float mc = fminf(fmaxf(m, k.lo), k.hi);
+  const float t = __fadd_rn(mc, k.magic_zp);
+  const float r = __fsub_rn(t, k.magic_zp);
+  ok = ok && (fabsf(mc - r) < 0.49951171875f) && (m == m);  // 0.5 - 2^-11
+  return __float_as_uint(t);
+}
+
+// The quantized value as an integer (not only its byte).
+__device__ __forceinline__ int32_t quantize_value(float xv, const QuantK& k) {
+  bool ok = true;
+  const uint32_t t = quantize_bits_try(xv, k, ok);
+  if (ok) return (int32_t)(t - 0x4B400000u);  // rint(mc) + zp
+  const uint32_t b = quantize_byte(xv, k.scale, k.zpd, k.qmind, k.qmaxd);
+  return k.qmin_i < 0 ? (int32_t)(int8_t)b : (int32_t)b;
+}
+
+// Word of four channel bytes from quantize_bits_try results (byte 0 of each).
+__device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_t b2,
+                                               uint32_t b3) {
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
+// Four channel bytes of one pixel (channels >= C hold `pad`), exactly; the
+// channels are read from `src` at a stride of `plane` floats.
+__device__ __noinline__ inline uint32_t quantize_word_exact(const float* src, int64_t plane,
+                                                            int C, uint32_t pad,
+                                                            const QuantK& k) {
+  uint32_t w = 0;
+  for (int c = 0; c < 4; ++c)
+    w |= (c < C ? quantize_byte(src[c * plane], k.scale, k.zpd, k.qmind, k.qmaxd) : pad)
+         << (8 * c);
+  return w;
+}
+
+// Host side: 1/scale in float, or NaN (every element takes the double
+// division) when the scale or the integer bounds are outside the range the
+// error bound covers.
+inline QuantK make_quant_k(double scale, int64_t zp, int64_t qmin, int64_t qmax) {
+  QuantK k;
+  k.scale = scale;
+  k.zpd = (double)zp;
+  k.qmind = (double)qmin;
+  k.qmaxd = (double)qmax;
+  k.zp = (float)zp;
+  k.qmin = (float)qmin;
+  k.qmax = (float)qmax;
+  k.zp_i = (int32_t)zp;
+  k.qmin_i = (int32_t)qmin;
+  k.qmax_i = (int32_t)qmax;
+  k.lo = (float)(qmin - zp);
+  k.hi = (float)(qmax - zp);
+  k.magic_zp = 12582912.0f + (float)zp;
+  const bool ok = std::fabs(scale) > 1e-30 && std::fabs(scale) < 1e30 &&
+                  std::llabs(zp) <= 1024 && std::llabs(qmin - zp) <= 1024 &&
+                  std::llabs(qmax - zp) <= 1024 && qmin <= qmax;
+  k.inv = ok ? (float)(1.0 / scale) : std::nanf("");
+  return k;
+}
+
+inline bool byte_range_host(int64_t lo, int64_t hi) { return lo >= -128 && hi <= 255 && lo <= hi; }
+
+}  // namespace qa

@@ -20,6 +20,7 @@
 #include "qa_fixedpoint.cuh"
 #include "qa_fused_epilogue.cuh"
 #include "qa_ptx.cuh"
+#include "qa_quant.cuh"
 #include "qa_umma.cuh"
 
 namespace qa {
@@ -183,77 +184,6 @@ __global__ void quantize_to_nhwc_kernel(const float* __restrict__ x, uint8_t* __
 // Four consecutive pixels per thread for the common 3-channel image stored
 // with a 4-byte pixel stride: one 16-byte load per channel plane, one
 // 16-byte store of four packed pixels.
-__device__ __forceinline__ uint32_t quantize_byte(float xv, double scale, double zp,
-                                                  double qmin, double qmax) {
-  double v = rint((double)xv / scale) + zp;
-  if (v < qmin) v = qmin;
-  if (qmax < v) v = qmax;
-  return (uint32_t)(int32_t)v & 0xFFu;
-}
-
-// The same byte through a float product with 1/scale.  With inv = fl32(1/s)
-// the product m = fl32(x * inv) is within |m| * 2^-22.9 of the double quotient
-// fl64(x / s), so both round to the same integer unless m lies within
-// |m| * 2^-21 of a half-integer.  Those cases (ties included), NaN and inf
-// (the distance test is false) and scales the host could not invert
-// (inv = NaN) take the double division.  zp / qmin / qmax are small integers,
-// exact in float.
-struct QuantK {
-  float inv, zp, qmin, qmax;
-  float lo, hi;      // qmin - zp, qmax - zp
-  float magic_zp;    // 1.5 * 2^23 + zp
-  int32_t zp_i, qmin_i, qmax_i;
-  double scale, zpd, qmind, qmaxd;
-};
-
-// Branch-free form of quantize_byte_fast for unrolled code: the float-path
-// byte, with `ok` cleared when the element needs the double division (the
-// caller then recomputes its whole group with quantize_word_exact).
-// Clamp-then-round in the float adder.  With lo = qmin - zp and hi =
-// qmax - zp integers of at most 2^10, clamp(rint(d) + zp) ==
-// rint(clamp(m, lo, hi)) + zp whenever m and the double quotient d round
-// alike, which holds (|m - d| < 2^-12 on that range) unless the clamped
-// product lies within 2^-11 of a half-integer; saturated and infinite
-// products clamp to an integer and pass.  t = mc + (1.5 * 2^23 + zp) then
-// holds rint(mc) + zp in its low mantissa bits, so its low byte is the
-// quantized byte.  `ok` is cleared near half-integers and for NaN: the caller
-// recomputes that pixel with quantize_word_exact.
-__device__ __forceinline__ uint32_t quantize_bits_try(float xv, const QuantK& k, bool& ok) {
-  const float m = __fmul_rn(xv, k.inv);  // no contraction into the adds below
-  const float mc = fminf(fmaxf(m, k.lo), k.hi);
-  const float t = __fadd_rn(mc, k.magic_zp);
-  const float r = __fsub_rn(t, k.magic_zp);
-  ok = ok && (fabsf(mc - r) < 0.49951171875f) && (m == m);  // 0.5 - 2^-11
-  return __float_as_uint(t);
-}
-
-// Word of four channel bytes from quantize_bits_try results (byte 0 of each).
-__device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_t b2,
-                                               uint32_t b3) {
-  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
-}
-
-// Four channel bytes of one pixel (channels >= C hold `pad`), exactly; the
-// channels are read from `src` at a stride of `plane` floats.
-__device__ __noinline__ uint32_t quantize_word_exact(const float* src, int64_t plane, int C,
-                                                     uint32_t pad, const QuantK& k) {
-  uint32_t w = 0;
-  for (int c = 0; c < 4; ++c)
-    w |= (c < C ? quantize_byte(src[c * plane], k.scale, k.zpd, k.qmind, k.qmaxd) : pad)
-         << (8 * c);
-  return w;
-}
-
-__device__ __forceinline__ uint32_t quantize_byte_fast(float xv, const QuantK& k) {
-  const float m = xv * k.inv;
-  const float r = rintf(m);
-  if (fabsf(fabsf(m - r) - 0.5f) > fabsf(m) * 4.76837158203125e-07f) {
-    const float v = fminf(fmaxf(r + k.zp, k.qmin), k.qmax);
-    return (uint32_t)__float2int_rz(v) & 0xFFu;
-  }
-  return quantize_byte(xv, k.scale, k.zpd, k.qmind, k.qmaxd);
-}
-
 __global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
                                          int C, int quads_per_image, int quads,
                                          const QuantK k) {
@@ -513,33 +443,6 @@ __global__ void i32_to_bytes_kernel(const int32_t* __restrict__ x, uint8_t* __re
   }
 }
 
-
-// Host side of quantize_byte_fast: 1/scale in float, or NaN (every element
-// takes the double division) when the scale or the integer bounds are out of
-// the range the error bound covers.
-bool byte_range_host(int64_t lo, int64_t hi) { return lo >= -128 && hi <= 255 && lo <= hi; }
-
-QuantK make_quant_k(double scale, int64_t zp, int64_t qmin, int64_t qmax) {
-  QuantK k;
-  k.scale = scale;
-  k.zpd = (double)zp;
-  k.qmind = (double)qmin;
-  k.qmaxd = (double)qmax;
-  k.zp = (float)zp;
-  k.qmin = (float)qmin;
-  k.qmax = (float)qmax;
-  k.zp_i = (int32_t)zp;
-  k.qmin_i = (int32_t)qmin;
-  k.qmax_i = (int32_t)qmax;
-  k.lo = (float)(qmin - zp);
-  k.hi = (float)(qmax - zp);
-  k.magic_zp = 12582912.0f + (float)zp;
-  const bool ok = std::fabs(scale) > 1e-30 && std::fabs(scale) < 1e30 &&
-                  std::llabs(zp) <= 1024 && std::llabs(qmin - zp) <= 1024 &&
-                  std::llabs(qmax - zp) <= 1024 && qmin <= qmax;
-  k.inv = ok ? (float)(1.0 / scale) : std::nanf("");
-  return k;
-}
 
 }  // namespace qa
 

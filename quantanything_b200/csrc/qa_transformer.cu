@@ -20,6 +20,7 @@
 #include "../../include/qa_kernels.h"
 #include "qa_common.cuh"
 #include "qa_ptx.cuh"
+#include "qa_quant.cuh"
 
 namespace qa {
 namespace {
@@ -32,18 +33,6 @@ __device__ __forceinline__ float dequant(int32_t q, int64_t zp, double scale) {
   return (float)((double)((int64_t)q - zp) * scale);
 }
 
-__device__ __forceinline__ int32_t quant(float x, double scale, int64_t zp, int64_t qmin,
-                                         int64_t qmax) {
-  double v = rint((double)x / scale) + (double)zp;
-  if (v < (double)qmin) v = (double)qmin;
-  if ((double)qmax < v) v = (double)qmax;
-  return (int32_t)v;  // NaN -> 0 here and in the byte it becomes
-}
-
-struct QP {
-  double scale;
-  int64_t zp, qmin, qmax;
-};
 
 // Four-byte dot product with each operand's bytes signed or unsigned.
 __device__ __forceinline__ int32_t dp4a_any(uint32_t a, uint32_t b, int32_t c, int a_signed,
@@ -94,37 +83,72 @@ __global__ void vit_embed_kernel(const uint8_t* __restrict__ x, int64_t x_stride
 // ------------------------------------------------------------ LayerNorm --
 // One warp per row: float64 mean and variance of the dequantized row,
 // (x - mean) / sqrt(var + eps) * gamma + beta in float64, rounded to float32,
-// then quantized.
+// then quantized.  Rows of up to 32 * kLnCache features stay in registers.
+constexpr int kLnCache = 32;
+
 __global__ void layernorm_kernel(const uint8_t* __restrict__ x, int64_t x_stride, int x_signed,
                                  int64_t zp_in, double s_in, const float* __restrict__ gamma,
-                                 const float* __restrict__ beta, double eps, QP o,
+                                 const float* __restrict__ beta, double eps, QuantK o,
                                  uint8_t* __restrict__ out, int64_t out_stride, int64_t rows,
                                  int D) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const bool cached = D <= 32 * kLnCache;
   for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
     const uint8_t* xr = x + r * x_stride;
+    float v[kLnCache];
     double sum = 0.0;
-    for (int d = lane; d < D; d += 32) sum += (double)dequant(load_q(xr + d, x_signed), zp_in, s_in);
+    if (cached) {
+#pragma unroll
+      for (int j = 0; j < kLnCache; ++j) {
+        const int d = lane + 32 * j;
+        v[j] = d < D ? dequant(load_q(xr + d, x_signed), zp_in, s_in) : 0.f;
+        sum += (double)v[j];
+      }
+    } else {
+      for (int d = lane; d < D; d += 32) sum += (double)dequant(load_q(xr + d, x_signed), zp_in, s_in);
+    }
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
     const double mean = sum / D;
     double sq = 0.0;
-    for (int d = lane; d < D; d += 32) {
-      const double c = (double)dequant(load_q(xr + d, x_signed), zp_in, s_in) - mean;
-      sq += c * c;
+    if (cached) {
+#pragma unroll
+      for (int j = 0; j < kLnCache; ++j) {
+        const double c = (double)v[j] - mean;
+        if (lane + 32 * j < D) sq += c * c;
+      }
+    } else {
+      for (int d = lane; d < D; d += 32) {
+        const double c = (double)dequant(load_q(xr + d, x_signed), zp_in, s_in) - mean;
+        sq += c * c;
+      }
     }
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o_);
+    // the reference divides by the deviation; one reciprocal and a product
+    // differ from that quotient by at most one float64 ulp, which reaches
+    // the float32 result only on a float32 rounding boundary
     const double inv = 1.0 / sqrt(sq / D + eps);
     uint8_t* orow = out + r * out_stride;
-    for (int d = lane; d < D; d += 32) {
-      double y = ((double)dequant(load_q(xr + d, x_signed), zp_in, s_in) - mean) * inv;
-      y = y * (double)gamma[d];
-      if (beta) y = y + (double)beta[d];
-      orow[d] = (uint8_t)quant((float)y, o.scale, o.zp, o.qmin, o.qmax);
+    if (cached) {
+#pragma unroll
+      for (int j = 0; j < kLnCache; ++j) {
+        const int d = lane + 32 * j;
+        if (d >= D) break;
+        double y = ((double)v[j] - mean) * inv * (double)gamma[d];
+        if (beta) y = y + (double)beta[d];
+        orow[d] = (uint8_t)quantize_value((float)y, o);
+      }
+    } else {
+      for (int d = lane; d < D; d += 32) {
+        double y = ((double)dequant(load_q(xr + d, x_signed), zp_in, s_in) - mean) * inv;
+        y = y * (double)gamma[d];
+        if (beta) y = y + (double)beta[d];
+        orow[d] = (uint8_t)quantize_value((float)y, o);
+      }
     }
   }
 }
@@ -142,6 +166,7 @@ __global__ void layernorm_kernel(const uint8_t* __restrict__ x, int64_t x_stride
 // reference's float32 MatMul result.
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxT = 256, kAttnMaxHd = 128;
+constexpr int kAttnKeys = kAttnMaxT / 32;  // keys per lane of a score row
 
 struct AttnParams {
   const uint8_t* qkv;
@@ -150,13 +175,13 @@ struct AttnParams {
   int64_t z_qkv;
   double s_qkv;
   int T, H, hd, D;
-  QP S;                     // scores quantization
+  QuantK S;                 // scores quantization
   const int32_t* mul_table; // [384]: Mul output for S byte value v at v + 128
   int64_t z_m;              // Mul output (softmax input) quantization
   double s_m;
-  QP P;                     // softmax output quantization
+  QuantK P;                 // softmax output quantization
   int p_signed;
-  QP O;                     // second MatMul output quantization
+  QuantK O;                 // second MatMul output quantization
   uint8_t* out;
   int64_t out_stride;
 };
@@ -173,7 +198,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   int32_t* s_ksum = s_qsum + T;                                   // [T]
   int32_t* s_vsum = s_ksum + T;                                   // [hd]
   uint8_t* s_p = reinterpret_cast<uint8_t*>(s_vsum + hd);         // [warps][tp] P rows
-  float* s_x = reinterpret_cast<float*>(s_p + (kAttnThreads / 32) * tp);  // [warps][T]
+  int32_t* s_mul = reinterpret_cast<int32_t*>(s_p + (kAttnThreads / 32) * tp);  // [384]
 
   const int n = blockIdx.x / a.H, h = blockIdx.x - n * a.H;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -209,47 +234,65 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     for (int t = 0; t < T; ++t) sv += load_q(s_vt + d * tp + t, a.qkv_signed);
     s_vsum[d] = sv;
   }
+  for (int i = tid; i < 384; i += kAttnThreads) s_mul[i] = a.mul_table[i];
   __syncthreads();
 
   const int64_t z = a.z_qkv;
   const double ss = a.s_qkv * a.s_qkv;
   uint8_t* prow = s_p + warp * tp;
-  float* xrow = s_x + warp * T;
   for (int t1 = warp; t1 < T; t1 += kAttnThreads / 32) {
-    // scores of this query row -> S bytes -> Mul table -> dequantized M
+    // scores of this query row, lane l taking keys l, l + 32, ...: eight
+    // independent dot products per lane -> S -> Mul table -> dequantized M
     const int32_t* qr = s_q + t1 * wpr;
+    int32_t acc[kAttnKeys];
+#pragma unroll
+    for (int j = 0; j < kAttnKeys; ++j) acc[j] = 0;
+    for (int w = 0; w < wpr; ++w) {
+      const uint32_t qv = (uint32_t)qr[w];
+#pragma unroll
+      for (int j = 0; j < kAttnKeys; ++j) {
+        const int t2 = min(lane + 32 * j, T - 1);  // clamped rows are discarded below
+        acc[j] = dp4a_any(qv, (uint32_t)s_k[t2 * kw + w], acc[j], a.qkv_signed, a.qkv_signed);
+      }
+    }
+    float xm[kAttnKeys];
     float mx = -INFINITY;
-    for (int t2 = lane; t2 < T; t2 += 32) {
-      const int32_t* kr = s_k + t2 * kw;
-      int32_t acc = 0;
-      for (int w = 0; w < wpr; ++w)
-        acc = dp4a_any((uint32_t)qr[w], (uint32_t)kr[w], acc, a.qkv_signed, a.qkv_signed);
-      // sum (q - z)(k - z) over the head dimension
-      const int64_t dot = (int64_t)acc - z * s_ksum[t2] - z * s_qsum[t1] + (int64_t)hd * z * z;
-      const float sf = (float)((double)dot * ss);
-      const int32_t sq8 = quant(sf, a.S.scale, a.S.zp, a.S.qmin, a.S.qmax);
-      const int32_t m = a.mul_table[sq8 + 128];
-      const float xm = dequant(m, a.z_m, a.s_m);
-      xrow[t2] = xm;
-      mx = fmaxf(mx, xm);
+#pragma unroll
+    for (int j = 0; j < kAttnKeys; ++j) {
+      const int t2 = lane + 32 * j;
+      xm[j] = -INFINITY;
+      if (t2 < T) {
+        // sum (q - z)(k - z) over the head dimension
+        const int64_t dot =
+            (int64_t)acc[j] - z * s_ksum[t2] - z * s_qsum[t1] + (int64_t)hd * z * z;
+        const int32_t sq8 = quantize_value((float)((double)dot * ss), a.S);
+        xm[j] = dequant(s_mul[sq8 + 128], a.z_m, a.s_m);
+        mx = fmaxf(mx, xm[j]);
+      }
     }
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o_));
+    double e[kAttnKeys];
     double sum = 0.0;
-    for (int t2 = lane; t2 < T; t2 += 32) sum += exp((double)xrow[t2] - (double)mx);
+#pragma unroll
+    for (int j = 0; j < kAttnKeys; ++j) {
+      e[j] = lane + 32 * j < T ? exp((double)xm[j] - (double)mx) : 0.0;
+      sum += e[j];
+    }
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
     int32_t psum = 0;
-    for (int t2 = lane; t2 < tp; t2 += 32) {
-      int32_t pq;
+    const double rsum = 1.0 / sum;  // (e * rsum differs from e / sum by <= 1 ulp)
+#pragma unroll
+    for (int j = 0; j < kAttnKeys; ++j) {
+      const int t2 = lane + 32 * j;
       if (t2 < T) {
-        const float pf = (float)(exp((double)xrow[t2] - (double)mx) / sum);
-        pq = quant(pf, a.P.scale, a.P.zp, a.P.qmin, a.P.qmax);
+        const int32_t pq = quantize_value((float)(e[j] * rsum), a.P);
         psum += pq;
-      } else {
-        pq = (int32_t)a.P.zp;  // padding keys: P byte = its zero point
+        prow[t2] = (uint8_t)pq;
+      } else if (t2 < tp) {
+        prow[t2] = (uint8_t)a.P.zp_i;  // padding keys: P byte = its zero point
       }
-      prow[t2] = (uint8_t)pq;
     }
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o_);
@@ -257,20 +300,19 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     // P . V for this row: lane handles head dimensions d = lane, lane + 32, ...
     const int32_t* pw = reinterpret_cast<const int32_t*>(prow);
     const double sp = a.P.scale * a.s_qkv;
+    const int64_t zP = a.P.zp_i;
     for (int d = lane; d < hd; d += 32) {
       const int32_t* vw = reinterpret_cast<const int32_t*>(s_vt + d * tp);
-      int32_t acc = 0;
+      int32_t acc2 = 0;
       for (int w = 0; w < tp / 4; ++w)
-        acc = dp4a_any((uint32_t)pw[w], (uint32_t)vw[w], acc, a.p_signed, a.qkv_signed);
+        acc2 = dp4a_any((uint32_t)pw[w], (uint32_t)vw[w], acc2, a.p_signed, a.qkv_signed);
       // sum over real keys of (p - zP)(v - z): the padded keys add
-      // zP * z (their v is z) to acc, removed with the padded count
-      const int64_t zP = a.P.zp;
+      // zP * z (their v is z) to acc2, removed with the padded count
       const int64_t pad = tp - T;
-      const int64_t dot = (int64_t)acc - pad * zP * z - z * psum - zP * s_vsum[d] +
+      const int64_t dot = (int64_t)acc2 - pad * zP * z - z * psum - zP * s_vsum[d] +
                           (int64_t)T * zP * z;
-      const float of = (float)((double)dot * sp);
       a.out[((int64_t)n * T + t1) * a.out_stride + (int64_t)h * hd + d] =
-          (uint8_t)quant(of, a.O.scale, a.O.zp, a.O.qmin, a.O.qmax);
+          (uint8_t)quantize_value((float)((double)dot * sp), a.O);
     }
     __syncwarp();
   }
@@ -346,7 +388,7 @@ QA_API int qa_layernorm_bytes_dev(const void* x, int64_t x_stride, int32_t x_sig
     return last_status();
   }
   if (rows == 0) return 0;
-  QP o{scale_out, zp_out, qmin, qmax};
+  const QuantK o = make_quant_k(scale_out, zp_out, qmin, qmax);
   return launch_ex(layernorm_kernel, dim3(grid_for(rows * 32, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_stride,
                    (int)x_signed, zp_in, scale_in, gamma, beta, eps, o,
@@ -381,11 +423,11 @@ QA_API int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t q
   a.D = (int)(H * hd);
   // s_params: scale of S, Mul output, P, O; z_params: (zp, qmin, qmax) of
   // S, P, O and the Mul output zero point
-  a.S = QP{s_params[0], z_params[0], z_params[1], z_params[2]};
+  a.S = make_quant_k(s_params[0], z_params[0], z_params[1], z_params[2]);
   a.s_m = s_params[1];
   a.z_m = z_params[9];
-  a.P = QP{s_params[2], z_params[3], z_params[4], z_params[5]};
-  a.O = QP{s_params[3], z_params[6], z_params[7], z_params[8]};
+  a.P = make_quant_k(s_params[2], z_params[3], z_params[4], z_params[5]);
+  a.O = make_quant_k(s_params[3], z_params[6], z_params[7], z_params[8]);
   a.p_signed = p_signed ? 1 : 0;
   a.mul_table = mul_table;
   a.out = static_cast<uint8_t*>(out);
@@ -393,8 +435,7 @@ QA_API int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t q
   const int tp = ((int)T + 3) & ~3;
   const int kw = (int)hd / 4 + 1;
   const size_t smem = (size_t)T * (hd / 4) * 4 + (size_t)T * kw * 4 + (size_t)hd * tp +
-                      (size_t)(2 * T + hd) * 4 + (size_t)(kAttnThreads / 32) * tp +
-                      (size_t)(kAttnThreads / 32) * T * 4 + 64;
+                      (size_t)(2 * T + hd) * 4 + (size_t)(kAttnThreads / 32) * tp + 384 * 4 + 64;
   static size_t attr_bytes[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
