@@ -25,6 +25,10 @@ the Softmax float fallback, captured in a CUDA graph.
             host threads) driven layer by layer, on a bounded sample.
 
 --impl reference runs only that CPU reference arm (rank 0; other ranks exit).
+
+--workload vit_b16 measures configuration 3 instead: ViT-B/16 (trunc-normal
+0.02 random init), int8, batch 256 per GPU, with the reference-calibrated
+q.json of tests/golden/graphs/vit_b16_int8.qjson, on the same contract.
 """
 
 import argparse
@@ -41,17 +45,50 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-QJSON = REPO / "tests" / "golden" / "graphs" / "yolov8n_cls_int8.qjson"
+GRAPHS = REPO / "tests" / "golden" / "graphs"
 REF_LIB = REPO / "oracle" / "_ref" / "libqa_kernels_ref.so"
-METRIC = "int8 YOLOv8n-cls images/sec"
 UNIT = "images/s"
-PER_GPU_BATCH = 64
 IMAGE = 224
+_VIT_B16 = {"img": 224, "patch": 16, "dim": 768, "heads": 12, "depth": 12, "classes": 1000,
+            "std": 0.02}
+
+def _graph(kind, batch):
+    """The workload's graph (a ViT graph holds its batch in its Reshapes)."""
+    from quantanything_b200 import networks
+
+    if kind == "vit_b16":
+        return networks.vit(batch=batch, **_VIT_B16)
+    return networks.yolov8n_cls()
+
+
+# workload name -> metric, q.json, graph for a batch, per-GPU batch, CPU sample batch
+WORKLOADS = {
+    "yolov8n_cls": {
+        "metric": "int8 YOLOv8n-cls images/sec", "qjson": GRAPHS / "yolov8n_cls_int8.qjson",
+        "graph": lambda b: _graph("yolov8n_cls", b),
+        "batch": 64, "cpu_batch": 16, "ref_batch": 32, "classes": 1000,
+        "name": "cfg2: YOLOv8n-cls int8 integer inference (random init, BN folded, "
+                "reference-calibrated q.json)"},
+    "vit_b16": {
+        "metric": "int8 ViT-B/16 images/sec", "qjson": GRAPHS / "vit_b16_int8.qjson",
+        "graph": lambda b: _graph("vit_b16", b),
+        "batch": 256, "cpu_batch": 1, "ref_batch": 2, "classes": 1000,
+        "name": "cfg3: ViT-B/16 int8 integer inference (random init, reference-calibrated "
+                "q.json; LayerNorm / attention float fallbacks on the GPU)"},
+}
+W = WORKLOADS["yolov8n_cls"]
+METRIC = W["metric"]
+PER_GPU_BATCH = W["batch"]
+
+
+def select_workload(name):
+    global W, METRIC, PER_GPU_BATCH
+    W = WORKLOADS[name]
+    METRIC, PER_GPU_BATCH = W["metric"], W["batch"]
 
 
 def config(world, extra=None):
-    c = {"workload": "cfg2: YOLOv8n-cls int8 integer inference (random init, BN folded, "
-                     "reference-calibrated q.json)",
+    c = {"workload": W["name"],
          "global_batch": PER_GPU_BATCH * world, "per_gpu_batch": PER_GPU_BATCH,
          "image": [3, IMAGE, IMAGE], "parallelism": f"dp{world} (batch-sharded replicas)",
          "l2": "flushed with a 256 MiB write between timed steps (outside the events)"}
@@ -74,9 +111,9 @@ def cpu_reference_sample(seconds, images_per_step, steps=None):
     os.environ["OMP_NUM_THREADS"] = str(threads)
     lib = KernelLibrary(REF_LIB)
     lib.set_num_threads(threads)
-    qc = QuantContainer.load(networks.yolov8n_cls(), QJSON, lib=lib)
+    qc = QuantContainer.load(W["graph"](images_per_step), W["qjson"], lib=lib)
     x = networks.images(images_per_step, IMAGE, seed=2024)
-    qc.run_graph(x[:2], "integer")  # warm caches / thread pool
+    qc.run_graph(x, "integer")  # warm caches / thread pool
     times = []
     t_end = time.perf_counter() + seconds
     while (steps is None and (not times or time.perf_counter() < t_end)) or (
@@ -93,7 +130,7 @@ def cpu_reference_sample(seconds, images_per_step, steps=None):
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    images = 32  # half the per-GPU batch per step: enough work for every host thread
+    images = W["ref_batch"]  # enough work per step for every host thread
     ips, threads, sample, times = cpu_reference_sample(0, images, steps=args.warmup)
     ips, threads, sample, times = cpu_reference_sample(0, images, steps=args.steps)
     ms = 1000.0 * sum(times) / len(times)
@@ -190,10 +227,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dropin", action="store_true")
+    ap.add_argument("--workload", default="yolov8n_cls", choices=sorted(WORKLOADS))
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="run this many plain forward passes of the workload and exit "
                          "(the command the ncu summaries under profiles/ are taken with)")
     args = ap.parse_args()
+    select_workload(args.workload)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -220,11 +259,16 @@ def main():
     from quantanything_b200 import native
 
     native.get_library().set_device(local)  # library work on this rank's GPU
-    qc = QuantContainer.load(networks.yolov8n_cls(), QJSON)
-    net = ResidentNet(qc, PER_GPU_BATCH, dev)
+    qc = QuantContainer.load(W["graph"](PER_GPU_BATCH), W["qjson"])
+    if args.workload == "vit_b16":
+        from quantanything_b200.resident_vit import ResidentViT
+
+        net = ResidentViT(qc, PER_GPU_BATCH, dev)
+    else:
+        net = ResidentNet(qc, PER_GPU_BATCH, dev)
     x_host = networks.images(PER_GPU_BATCH, IMAGE, seed=1000 + rank)
     x_pinned = torch.from_numpy(x_host).pin_memory()
-    out_pinned = torch.empty((PER_GPU_BATCH, 1000), dtype=torch.float32).pin_memory()
+    out_pinned = torch.empty((PER_GPU_BATCH, W["classes"]), dtype=torch.float32).pin_memory()
     net.x_dev.copy_(x_pinned)
     if args.profile_forwards:
         for _ in range(args.profile_forwards):
@@ -318,14 +362,17 @@ def main():
     # ---- drop-in ABI route (rank 0, N=1) and CPU baseline
     dropin = cpu = None
     if rank == 0 and world == 1 and not args.no_dropin:
-        qc.run_graph(x_host[:8], "integer")
+        nb = PER_GPU_BATCH if args.workload == "yolov8n_cls" else W["ref_batch"]
+        qd = qc if nb == PER_GPU_BATCH else QuantContainer.load(W["graph"](nb), W["qjson"])
+        qd.run_graph(x_host[:nb], "integer")
         t0 = time.perf_counter()
-        qc.run_graph(x_host, "integer")
+        qd.run_graph(x_host[:nb], "integer")
         dt = time.perf_counter() - t0
-        dropin = {"value": round(PER_GPU_BATCH / dt, 2), "unit": UNIT,
-                  "route": "layer-by-layer host-pointer ABI (QA_LIB drop-in), wall clock"}
+        dropin = {"value": round(nb / dt, 2), "unit": UNIT,
+                  "route": "layer-by-layer host-pointer ABI (QA_LIB drop-in), wall clock, "
+                           f"{nb} images"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ips, threads, sample, _ = cpu_reference_sample(args.cpu_seconds, 16)
+        ips, threads, sample, _ = cpu_reference_sample(args.cpu_seconds, W["cpu_batch"])
         cpu = {"value": round(ips, 3), "unit": UNIT, "cores": threads, "kind": "reference",
                "sample": sample}
 
