@@ -14,6 +14,7 @@
 // the reference's by one output step when it lies on a rounding boundary.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
@@ -153,28 +154,164 @@ __global__ void layernorm_kernel(const uint8_t* __restrict__ x, int64_t x_stride
   }
 }
 
+// Rows of D % 16 == 0 features, D <= 16 * 16 * kLnChunks, 16-byte aligned
+// rows: sixteen lanes per row, each holding up to kLnChunks 16-byte chunks
+// in registers.  The dequantized value of each byte comes from a 256-entry
+// float64 table.  Their float64 row sum is exact in any order (every value
+// is a float32 multiple of the same scale, the sum spans fewer than 53
+// bits), so the mean is the reference's to the bit; the variance sum runs
+// in another order than NumPy's.  gamma / beta are staged as float64 and
+// skipped when they are all ones / zeros (x * 1 + 0 == x).
+constexpr int kLnChunks = 4;
+constexpr int kLnThreads = 256;
+constexpr int kLnMaxD = 16 * 16 * kLnChunks;
+
+__global__ void __launch_bounds__(kLnThreads, 2)
+    layernorm_rows16_kernel(const uint8_t* __restrict__ x, int64_t x_stride, int x_signed,
+                            int64_t zp_in, double s_in, const float* __restrict__ gamma,
+                            const float* __restrict__ beta, double eps, QuantK o,
+                            uint8_t* __restrict__ out, int64_t out_stride, int64_t rows, int D) {
+  __shared__ double s_v[256];
+  __shared__ double s_g[kLnMaxD], s_b[kLnMaxD];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_v[tid] = (double)dequant(x_signed ? (int32_t)(int8_t)tid : tid, zp_in, s_in);
+  int ident = 1;
+  for (int d = tid; d < D; d += kLnThreads) {
+    const double g = (double)gamma[d], b = beta ? (double)beta[d] : 0.0;
+    s_g[d] = g;
+    s_b[d] = b;
+    ident &= (g == 1.0 && b == 0.0) ? 1 : 0;
+  }
+  const bool affine = !__syncthreads_and(ident);
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int l16 = lane & 15;
+  const int chunks = D / 16;
+  const double rD = (double)D;
+  for (int64_t pair = (int64_t)blockIdx.x * (kLnThreads / 32) + warp; 2 * pair < rows;
+       pair += (int64_t)gridDim.x * (kLnThreads / 32)) {
+    const int64_t row = 2 * pair + (lane >> 4);
+    const bool valid = row < rows;  // both halves of the warp run every shuffle
+    uint4 c[kLnChunks];
+#pragma unroll
+    for (int i = 0; i < kLnChunks; ++i) {
+      const int j = l16 + 16 * i;
+      c[i] = (valid && j < chunks) ? *reinterpret_cast<const uint4*>(x + row * x_stride + 16 * j)
+                                   : make_uint4(0u, 0u, 0u, 0u);
+    }
+    auto word = [&](int i, int g) -> uint32_t {
+      return g == 0 ? c[i].x : g == 1 ? c[i].y : g == 2 ? c[i].z : c[i].w;
+    };
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < kLnChunks; ++i)
+      if (l16 + 16 * i < chunks) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t w = word(i, g);
+          sum += (s_v[w & 0xFFu] + s_v[(w >> 8) & 0xFFu]) +
+                 (s_v[(w >> 16) & 0xFFu] + s_v[w >> 24]);
+        }
+      }
+#pragma unroll
+    for (int o_ = 8; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
+    const double mean = sum / rD;
+    double sq0 = 0.0, sq1 = 0.0;
+#pragma unroll
+    for (int i = 0; i < kLnChunks; ++i)
+      if (l16 + 16 * i < chunks) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t w = word(i, g);
+          const double a0 = s_v[w & 0xFFu] - mean, a1 = s_v[(w >> 8) & 0xFFu] - mean;
+          const double a2 = s_v[(w >> 16) & 0xFFu] - mean, a3 = s_v[w >> 24] - mean;
+          sq0 = fma(a0, a0, sq0);
+          sq1 = fma(a1, a1, sq1);
+          sq0 = fma(a2, a2, sq0);
+          sq1 = fma(a3, a3, sq1);
+        }
+      }
+    double sq = sq0 + sq1;
+#pragma unroll
+    for (int o_ = 8; o_ > 0; o_ >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o_);
+    // the reference divides by the deviation; one reciprocal and a product
+    // differ from that quotient by at most one float64 ulp, which reaches
+    // the float32 result only on a float32 rounding boundary
+    const double inv = 1.0 / sqrt(sq / rD + eps);
+    if (!valid) continue;
+    uint8_t* orow = out + row * out_stride;
+#pragma unroll
+    for (int i = 0; i < kLnChunks; ++i) {
+      const int j = l16 + 16 * i;
+      if (j < chunks) {
+        uint32_t ow[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t w = word(i, g);
+          uint32_t q[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            double y = (s_v[(w >> (8 * e)) & 0xFFu] - mean) * inv;
+            if (affine) {
+              const int d = 16 * j + 4 * g + e;
+              y = y * s_g[d] + s_b[d];
+            }
+            q[e] = (uint32_t)quantize_value((float)y, o);
+          }
+          ow[g] = pack_bytes(q[0], q[1], q[2], q[3]);
+        }
+        *reinterpret_cast<uint4*>(orow + 16 * j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ attention --
-// One CTA per (image, head).  q, k, v are the head's columns of the QKV
-// rows (k and v at +D and +2D); all three share the QKV quantization.
+// One CTA per (image, head, 128-query tile).  q, k, v are the head's columns
+// of the QKV rows (k and v at +D and +2D); all three share the QKV
+// quantization.
 //   S = quant_S(deq(q) . deq(k)^T)          (activation x activation MatMul)
 //   M = mul_table[S]                          (Mul by the 1/sqrt(hd) constant)
 //   P = quant_P(softmax(deq_M(M)))            (float64, along the keys)
 //   O = quant_O(deq_P(P) . deq(v))            (second MatMul)
 // written to out[(n * T + t) * out_stride + h * hd + d] (the head merge
-// Transpose + Reshape).  The dot products are exact integer sums of the
-// centred bytes; each is scaled in double and rounded to float32 like the
-// reference's float32 MatMul result.
+// Transpose + Reshape).  Both products run on the tensor cores over the raw
+// bytes (tcgen05.mma kind::i8, M = 128 query rows, accumulators in TMEM);
+// the zero points come off with row and column byte sums, so each dot
+// product is the exact integer sum of the centred bytes, scaled in double
+// and rounded to float32 like the reference's float32 MatMul result.
+//
+// Softmax: thread (row, column half) reads its scores straight from TMEM.
+// The softmax input is a byte b (M's quantized value), so exp only ever sees
+// 256 arguments: E[b] = exp(x(b) - x_top) with x_top the largest x over the
+// byte range is a 256-entry table per CTA, and p = E[b] / sum_row E, which
+// equals exp(x - max_row) / sum_row exp(x - max_row) up to the last bit of
+// a double (the common factor exp(max_row - x_top) cancels).  When the byte
+// range of x spans more than 600 (E would leave the normal doubles) the
+// kernel takes exp(x - max_row) per element instead.
+//
+// Operand layouts (no swizzle, K-major): a 16-byte K slice of all R rows is
+// one block of R * 16 bytes (row r at r * 16), so core matrices are 128
+// bytes apart along M/N and R * 16 bytes apart along K.  Padded rows, keys
+// and head dimensions hold raw 0 bytes and add nothing to the raw sums.
 constexpr int kAttnThreads = 256;
 constexpr int kAttnMaxT = 256, kAttnMaxHd = 128;
-constexpr int kAttnKeys = kAttnMaxT / 32;  // keys per lane of a score row
+constexpr int kAttnTile = 128;       // query rows per CTA
+constexpr uint64_t kAttnBudget = 4000000000ull;  // bounded waits (~2 s)
+constexpr int kAttnTimeoutCode = 0x7005;
+constexpr double kAttnTableSpan = 600.0;  // largest x range the exp table covers
 
 struct AttnParams {
   const uint8_t* qkv;
   int64_t qkv_stride;
   int qkv_signed;
-  int64_t z_qkv;
+  int32_t z_qkv;
   double s_qkv;
   int T, H, hd, D;
+  int tiles;               // query tiles per head
+  int hdp, hdn, nk, tk;    // hd to 32 (S K-dim), hd to 16 (O N-dim), T to 16 (S N-dim), T to 32
+  int vec_in, vec_out;     // 16-byte row segments of qkv / out
+  uint32_t tmem_cols;
   QuantK S;                 // scores quantization
   const int32_t* mul_table; // [384]: Mul output for S byte value v at v + 128
   int64_t z_m;              // Mul output (softmax input) quantization
@@ -184,137 +321,347 @@ struct AttnParams {
   QuantK O;                 // second MatMul output quantization
   uint8_t* out;
   int64_t out_stride;
+  int* status;
 };
 
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnParams a) {
-  extern __shared__ __align__(16) uint8_t attn_smem[];
-  const int T = a.T, hd = a.hd;
-  const int kw = hd / 4 + 1;      // words per padded k row (bank spread)
-  const int tp = (T + 3) & ~3;    // keys padded to whole words for P . V
-  int32_t* s_q = reinterpret_cast<int32_t*>(attn_smem);  // [T][hd/4] words
-  int32_t* s_k = s_q + T * (hd / 4);                        // [T][kw] words
-  uint8_t* s_vt = reinterpret_cast<uint8_t*>(s_k + T * kw); // [hd][tp] bytes (v transposed)
-  int32_t* s_qsum = reinterpret_cast<int32_t*>(s_vt + hd * tp);  // [T]
-  int32_t* s_ksum = s_qsum + T;                                   // [T]
-  int32_t* s_vsum = s_ksum + T;                                   // [hd]
-  uint8_t* s_p = reinterpret_cast<uint8_t*>(s_vsum + hd);         // [warps][tp] P rows
-  int32_t* s_mul = reinterpret_cast<int32_t*>(s_p + (kAttnThreads / 32) * tp);  // [384]
+__device__ __forceinline__ int32_t byte_sum4(uint4 v, int is_signed) {
+  int32_t s = 0;
+  s = dp4a_any(v.x, 0x01010101u, s, is_signed, 0);
+  s = dp4a_any(v.y, 0x01010101u, s, is_signed, 0);
+  s = dp4a_any(v.z, 0x01010101u, s, is_signed, 0);
+  return dp4a_any(v.w, 0x01010101u, s, is_signed, 0);
+}
 
-  const int n = blockIdx.x / a.H, h = blockIdx.x - n * a.H;
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attention_kernel(const __grid_constant__ AttnParams a) {
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  const int T = a.T, hd = a.hd, hdp = a.hdp, hdn = a.hdn, nk = a.nk, tk = a.tk;
+  uint8_t* s_q = attn_smem;                   // hdp / 16 slices of 128 rows
+  uint8_t* s_k = s_q + kAttnTile * hdp;       // hdp / 16 slices of nk rows
+  uint8_t* s_vt = s_k + nk * hdp;             // tk / 16 slices of hdn rows (v transposed)
+  uint8_t* s_p = s_vt + hdn * tk;             // tk / 16 slices of 128 rows
+  double* s_ex = reinterpret_cast<double*>(s_p + kAttnTile * tk);  // [256] exp table
+  float* s_xm = reinterpret_cast<float*>(s_ex + 256);              // [256] softmax input of b
+  int32_t* s_kz = reinterpret_cast<int32_t*>(s_xm + 256);          // [256] z * sum k (per key)
+  int32_t* s_qsum = s_kz + 256;                                    // [128]
+  int32_t* s_vz = s_qsum + kAttnTile;                              // [128] per head dimension
+  double* s_part = reinterpret_cast<double*>(s_vz + kAttnMaxHd);   // [2][128] row sums
+  float* s_rmax = reinterpret_cast<float*>(s_part + 2 * kAttnTile);  // [2][128] row maxima
+  int32_t* s_psum = reinterpret_cast<int32_t*>(s_rmax + 2 * kAttnTile);  // [2][128]
+  float* s_red = reinterpret_cast<float*>(s_psum + 2 * kAttnTile);       // [2][8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_red + 16);              // [2]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int tile = blockIdx.x % a.tiles, nh = blockIdx.x / a.tiles;
+  const int n = nh / a.H, h = nh - n * a.H;
+  const int row0 = tile * kAttnTile;
+  const uint32_t bar_s = ptx::smem_addr(bars), bar_o = bar_s + 8u;
+  const int32_t z = a.z_qkv;
+
+  // ---- launch-constant tables (before waiting on the producer of qkv) ----
+  {
+    const int b = tid;  // 256 threads, one byte value each
+    const int v = a.S.qmin_i < 0 ? (int)(int8_t)b : b;
+    const bool in_range = v >= a.S.qmin_i && v <= a.S.qmax_i;
+    const float xm = dequant(a.mul_table[v + 128], a.z_m, a.s_m);
+    s_xm[b] = xm;
+    float hi = in_range ? xm : -INFINITY, lo = in_range ? xm : INFINITY;
+#pragma unroll
+    for (int o_ = 16; o_ > 0; o_ >>= 1) {
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o_));
+      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o_));
+    }
+    if (lane == 0) {
+      s_red[warp] = hi;
+      s_red[8 + warp] = lo;
+    }
+  }
+  if (tid == 0) {
+    ptx::mbar_init(bar_s, 1);
+    ptx::mbar_init(bar_o, 1);
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ptx::tmem_alloc(ptx::smem_addr(s_tmem), a.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  float x_top = s_red[0], x_low = s_red[8];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) {
+    x_top = fmaxf(x_top, s_red[w]);
+    x_low = fminf(x_low, s_red[8 + w]);
+  }
+  const bool table = (double)x_top - (double)x_low <= kAttnTableSpan;
+  if (table) s_ex[tid] = exp((double)s_xm[tid] - (double)x_top);
+
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
 
-  // stage q, k, v (bytes of the head's columns) and their sums
+  // ---- stage q (this tile's rows), k and v (all keys) in the MMA layouts ----
   const uint8_t* base = a.qkv + (int64_t)n * T * a.qkv_stride + (int64_t)h * hd;
-  const int wpr = hd / 4;
-  for (int i = tid; i < T * wpr; i += kAttnThreads) {
-    const int t = i / wpr, w = i - t * wpr;
-    const uint8_t* row = base + (int64_t)t * a.qkv_stride;
-    s_q[t * wpr + w] = *reinterpret_cast<const int32_t*>(row + 4 * w);
-    s_k[t * kw + w] = *reinterpret_cast<const int32_t*>(row + a.D + 4 * w);
-  }
-  for (int i = tid; i < hd * tp; i += kAttnThreads) {
-    const int d = i / tp, t = i - d * tp;
-    s_vt[i] = t < T ? base[(int64_t)t * a.qkv_stride + 2 * a.D + d]
-                    : (uint8_t)(int8_t)a.z_qkv;  // padding keys contribute (z - z) = 0
-  }
-  __syncthreads();
-  for (int t = tid; t < T; t += kAttnThreads) {
-    int32_t sq = 0, sk = 0;
-    for (int d = 0; d < hd; ++d) {
-      sq += load_q(reinterpret_cast<const uint8_t*>(s_q + t * wpr) + d, a.qkv_signed);
-      sk += load_q(reinterpret_cast<const uint8_t*>(s_k + t * kw) + d, a.qkv_signed);
+  const int qs = hdp / 16;
+  for (int i = tid; i < (kAttnTile + nk) * qs; i += kAttnThreads) {
+    const int r = i / qs, j = i - r * qs;
+    const bool is_q = r < kAttnTile;
+    const int rr = is_q ? r : r - kAttnTile;
+    const int t = is_q ? row0 + rr : rr;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t < T) {
+      const uint8_t* src = base + (int64_t)t * a.qkv_stride + (is_q ? 0 : a.D) + 16 * j;
+      if (a.vec_in) {
+        if (16 * j < hd) v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        uint32_t w4[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+          w4[w] = 16 * j + 4 * w < hd ? *reinterpret_cast<const uint32_t*>(src + 4 * w) : 0u;
+        v = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
     }
-    s_qsum[t] = sq;
-    s_ksum[t] = sk;
+    uint8_t* dst = is_q ? s_q + j * (kAttnTile * 16) : s_k + j * (nk * 16);
+    *reinterpret_cast<uint4*>(dst + rr * 16) = v;
   }
-  for (int d = tid; d < hd; d += kAttnThreads) {
-    int32_t sv = 0;
-    for (int t = 0; t < T; ++t) sv += load_q(s_vt + d * tp + t, a.qkv_signed);
-    s_vsum[d] = sv;
+  const int dgs = hdn / 4;
+  for (int i = tid; i < (tk / 4) * dgs; i += kAttnThreads) {
+    const int kb = i / dgs, dg = i - kb * dgs;
+    const int k0 = 4 * kb, d0 = 4 * dg;
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      w[q] = (k0 + q < T && d0 < hd)
+                 ? *reinterpret_cast<const uint32_t*>(base + (int64_t)(k0 + q) * a.qkv_stride +
+                                                      2 * a.D + d0)
+                 : 0u;
+    // 4 x 4 byte transpose: word j gets byte j of each key's word
+    const uint32_t t0 = __byte_perm(w[0], w[1], 0x5140), t1 = __byte_perm(w[0], w[1], 0x7362);
+    const uint32_t t2 = __byte_perm(w[2], w[3], 0x5140), t3 = __byte_perm(w[2], w[3], 0x7362);
+    uint8_t* dst = s_vt + (k0 / 16) * (hdn * 16) + d0 * 16 + (k0 & 15);
+    *reinterpret_cast<uint32_t*>(dst) = __byte_perm(t0, t2, 0x5410);
+    *reinterpret_cast<uint32_t*>(dst + 16) = __byte_perm(t0, t2, 0x7632);
+    *reinterpret_cast<uint32_t*>(dst + 32) = __byte_perm(t1, t3, 0x5410);
+    *reinterpret_cast<uint32_t*>(dst + 48) = __byte_perm(t1, t3, 0x7632);
   }
-  for (int i = tid; i < 384; i += kAttnThreads) s_mul[i] = a.mul_table[i];
+  ptx::fence_proxy_async_smem();
   __syncthreads();
 
-  const int64_t z = a.z_qkv;
+  // ---- S = q k^T (raw bytes) on the tensor cores ----
+  if (tid == 0) {
+    ptx::tc_fence_after();
+    const uint32_t idesc = ptx::idesc_i8(kAttnTile, nk, a.qkv_signed, a.qkv_signed);
+    const uint32_t qa = ptx::smem_addr(s_q), ka = ptx::smem_addr(s_k);
+    for (int kk = 0; kk < hdp / 32; ++kk)
+      ptx::mma_i8(tmem, ptx::smem_desc_kmajor_plain(qa + kk * 2 * (kAttnTile * 16), kAttnTile * 16, 128),
+                  ptx::smem_desc_kmajor_plain(ka + kk * 2 * (nk * 16), nk * 16, 128), idesc,
+                  kk > 0 ? 1u : 0u);
+    ptx::mma_commit(bar_s);
+  }
+  // byte sums for the zero-point terms, while the MMA runs
+  for (int i = tid; i < kAttnTile + nk + hdn; i += kAttnThreads) {
+    if (i < kAttnTile) {
+      int32_t s = 0;
+      for (int j = 0; j < qs; ++j)
+        s += byte_sum4(*reinterpret_cast<const uint4*>(s_q + j * (kAttnTile * 16) + i * 16),
+                       a.qkv_signed);
+      s_qsum[i] = s;
+    } else if (i < kAttnTile + nk) {
+      const int r = i - kAttnTile;
+      int32_t s = 0;
+      for (int j = 0; j < qs; ++j)
+        s += byte_sum4(*reinterpret_cast<const uint4*>(s_k + j * (nk * 16) + r * 16),
+                       a.qkv_signed);
+      s_kz[r] = z * s;
+    } else {
+      const int d = i - kAttnTile - nk;
+      int32_t s = 0;
+      for (int j = 0; j < tk / 16; ++j)
+        s += byte_sum4(*reinterpret_cast<const uint4*>(s_vt + j * (hdn * 16) + d * 16),
+                       a.qkv_signed);
+      s_vz[d] = a.P.zp_i * s - T * a.P.zp_i * z;
+    }
+  }
+  __syncthreads();
+  if (!ptx::mbar_wait(bar_s, 0, kAttnBudget)) {
+    *s_abort = 1;
+    if (a.status) atomicExch(a.status, kAttnTimeoutCode);
+  }
+  __syncthreads();
+  ptx::tc_fence_after();
+  const bool ok = !*s_abort;
+
+  // ---- softmax rows: this thread owns row r, score chunks [c_beg, c_end) ----
+  const int r = quarter * 32 + lane;
+  const int t1 = row0 + r;
+  const bool warp_live = ok && row0 + quarter * 32 < T;  // warp-uniform
+  const int nchunks = nk / 16;
+  const int c_split = (nchunks + 1) / 2;
+  const int c_beg = half ? c_split : 0, c_end = half ? nchunks : c_split;
+  const uint32_t lane_base = ((uint32_t)(quarter * 32)) << 16;
   const double ss = a.s_qkv * a.s_qkv;
-  uint8_t* prow = s_p + warp * tp;
-  for (int t1 = warp; t1 < T; t1 += kAttnThreads / 32) {
-    // scores of this query row, lane l taking keys l, l + 32, ...: eight
-    // independent dot products per lane -> S -> Mul table -> dequantized M
-    const int32_t* qr = s_q + t1 * wpr;
-    int32_t acc[kAttnKeys];
+  const int32_t rowc = hd * z * z - z * s_qsum[r];
+  // pass 1: scores -> bytes b (kept in the P buffer at their P positions),
+  // with the row's partial exp-table sum (or its maximum without the table)
+  double part = 0.0;
+  float mx = -INFINITY;
+  if (warp_live) {
+#pragma unroll 1
+    for (int cc = c_beg; cc < c_end; ++cc) {
+      uint32_t v[16];
+      ptx::tmem_ld16(tmem + lane_base + (uint32_t)(cc * 16), v);
+      ptx::tmem_ld_wait(v);
+      const int4* kz4 = reinterpret_cast<const int4*>(s_kz + cc * 16);
+      uint32_t bw[4];
 #pragma unroll
-    for (int j = 0; j < kAttnKeys; ++j) acc[j] = 0;
-    for (int w = 0; w < wpr; ++w) {
-      const uint32_t qv = (uint32_t)qr[w];
+      for (int g = 0; g < 4; ++g) {
+        const int4 kz = kz4[g];
+        const int32_t kzv[4] = {kz.x, kz.y, kz.z, kz.w};
+        uint32_t bq[4];
 #pragma unroll
-      for (int j = 0; j < kAttnKeys; ++j) {
-        const int t2 = min(lane + 32 * j, T - 1);  // clamped rows are discarded below
-        acc[j] = dp4a_any(qv, (uint32_t)s_k[t2 * kw + w], acc[j], a.qkv_signed, a.qkv_signed);
+        for (int e = 0; e < 4; ++e) {
+          const int32_t dot = (int32_t)v[4 * g + e] - kzv[e] + rowc;
+          bq[e] = (uint32_t)quantize_value((float)((double)dot * ss), a.S) & 0xFFu;
+          if (cc * 16 + 4 * g + e < T) {
+            if (table)
+              part += s_ex[bq[e]];
+            else
+              mx = fmaxf(mx, s_xm[bq[e]]);
+          }
+        }
+        bw[g] = pack_bytes(bq[0], bq[1], bq[2], bq[3]);
+      }
+      *reinterpret_cast<uint4*>(s_p + cc * (kAttnTile * 16) + r * 16) =
+          make_uint4(bw[0], bw[1], bw[2], bw[3]);
+    }
+  }
+  if (!table) {  // CTA-uniform: the row maximum, then the sum of exp(x - max)
+    s_rmax[half * kAttnTile + r] = mx;
+    __syncthreads();
+    mx = fmaxf(s_rmax[r], s_rmax[kAttnTile + r]);
+    if (warp_live) {
+#pragma unroll 1
+      for (int cc = c_beg; cc < c_end; ++cc) {
+        const uint4 bw = *reinterpret_cast<const uint4*>(s_p + cc * (kAttnTile * 16) + r * 16);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t word = g == 0 ? bw.x : g == 1 ? bw.y : g == 2 ? bw.z : bw.w;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (cc * 16 + 4 * g + e < T)
+              part += exp((double)s_xm[(word >> (8 * e)) & 0xFFu] - (double)mx);
+        }
       }
     }
-    float xm[kAttnKeys];
-    float mx = -INFINITY;
+  }
+  s_part[half * kAttnTile + r] = part;
+  __syncthreads();
+  const double rsum = 1.0 / (s_part[r] + s_part[kAttnTile + r]);
+  // pass 2: P bytes over the b bytes
+  int32_t psum = 0;
+  if (warp_live) {
+#pragma unroll 1
+    for (int cc = c_beg; cc < c_end; ++cc) {
+      uint4* slot = reinterpret_cast<uint4*>(s_p + cc * (kAttnTile * 16) + r * 16);
+      const uint4 bw = *slot;
+      uint32_t pw[4];
 #pragma unroll
-    for (int j = 0; j < kAttnKeys; ++j) {
-      const int t2 = lane + 32 * j;
-      xm[j] = -INFINITY;
-      if (t2 < T) {
-        // sum (q - z)(k - z) over the head dimension
-        const int64_t dot =
-            (int64_t)acc[j] - z * s_ksum[t2] - z * s_qsum[t1] + (int64_t)hd * z * z;
-        const int32_t sq8 = quantize_value((float)((double)dot * ss), a.S);
-        xm[j] = dequant(s_mul[sq8 + 128], a.z_m, a.s_m);
-        mx = fmaxf(mx, xm[j]);
+      for (int g = 0; g < 4; ++g) {
+        const uint32_t word = g == 0 ? bw.x : g == 1 ? bw.y : g == 2 ? bw.z : bw.w;
+        uint32_t pq[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t b = (word >> (8 * e)) & 0xFFu;
+          int32_t p = 0;  // padded keys: raw 0
+          if (cc * 16 + 4 * g + e < T) {
+            const double ev = table ? s_ex[b] : exp((double)s_xm[b] - (double)mx);
+            p = quantize_value((float)(ev * rsum), a.P);
+            psum += p;
+          }
+          pq[e] = (uint32_t)p;
+        }
+        pw[g] = pack_bytes(pq[0], pq[1], pq[2], pq[3]);
       }
+      *slot = make_uint4(pw[0], pw[1], pw[2], pw[3]);
     }
-#pragma unroll
-    for (int o_ = 16; o_ > 0; o_ >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o_));
-    double e[kAttnKeys];
-    double sum = 0.0;
-#pragma unroll
-    for (int j = 0; j < kAttnKeys; ++j) {
-      e[j] = lane + 32 * j < T ? exp((double)xm[j] - (double)mx) : 0.0;
-      sum += e[j];
-    }
-#pragma unroll
-    for (int o_ = 16; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
-    int32_t psum = 0;
-    const double rsum = 1.0 / sum;  // (e * rsum differs from e / sum by <= 1 ulp)
-#pragma unroll
-    for (int j = 0; j < kAttnKeys; ++j) {
-      const int t2 = lane + 32 * j;
-      if (t2 < T) {
-        const int32_t pq = quantize_value((float)(e[j] * rsum), a.P);
-        psum += pq;
-        prow[t2] = (uint8_t)pq;
-      } else if (t2 < tp) {
-        prow[t2] = (uint8_t)a.P.zp_i;  // padding keys: P byte = its zero point
-      }
-    }
-#pragma unroll
-    for (int o_ = 16; o_ > 0; o_ >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o_);
-    __syncwarp();
-    // P . V for this row: lane handles head dimensions d = lane, lane + 32, ...
-    const int32_t* pw = reinterpret_cast<const int32_t*>(prow);
+  }
+  // key slices past the score columns (tk > nk) hold zeros
+  for (int cc = nchunks + half; cc < tk / 16; cc += 2)
+    *reinterpret_cast<uint4*>(s_p + cc * (kAttnTile * 16) + r * 16) = make_uint4(0u, 0u, 0u, 0u);
+  s_psum[half * kAttnTile + r] = psum;
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+
+  // ---- O = P v (raw bytes) into the score columns ----
+  if (tid == 0 && ok) {
+    ptx::tc_fence_after();
+    const uint32_t idesc = ptx::idesc_i8(kAttnTile, hdn, a.p_signed, a.qkv_signed);
+    const uint32_t pa = ptx::smem_addr(s_p), va = ptx::smem_addr(s_vt);
+    for (int kk = 0; kk < tk / 32; ++kk)
+      ptx::mma_i8(tmem, ptx::smem_desc_kmajor_plain(pa + kk * 2 * (kAttnTile * 16), kAttnTile * 16, 128),
+                  ptx::smem_desc_kmajor_plain(va + kk * 2 * (hdn * 16), hdn * 16, 128), idesc,
+                  kk > 0 ? 1u : 0u);
+    ptx::mma_commit(bar_o);
+  }
+  if (ok && !ptx::mbar_wait(bar_o, 0, kAttnBudget)) {
+    *s_abort = 1;
+    if (a.status) atomicExch(a.status, kAttnTimeoutCode);
+  }
+  __syncthreads();
+  ptx::tc_fence_after();
+
+  // ---- epilogue: O row r, head-dimension chunks of this half ----
+  if (warp_live && !*s_abort) {
+    const int ochunks = hdn / 16, o_split = (ochunks + 1) / 2;
+    const int o_beg = half ? o_split : 0, o_end = half ? ochunks : o_split;
+    const int32_t prow = psum + s_psum[(1 - half) * kAttnTile + r];
+    const int32_t rowo = z * prow;
     const double sp = a.P.scale * a.s_qkv;
-    const int64_t zP = a.P.zp_i;
-    for (int d = lane; d < hd; d += 32) {
-      const int32_t* vw = reinterpret_cast<const int32_t*>(s_vt + d * tp);
-      int32_t acc2 = 0;
-      for (int w = 0; w < tp / 4; ++w)
-        acc2 = dp4a_any((uint32_t)pw[w], (uint32_t)vw[w], acc2, a.p_signed, a.qkv_signed);
-      // sum over real keys of (p - zP)(v - z): the padded keys add
-      // zP * z (their v is z) to acc2, removed with the padded count
-      const int64_t pad = tp - T;
-      const int64_t dot = (int64_t)acc2 - pad * zP * z - z * psum - zP * s_vsum[d] +
-                          (int64_t)T * zP * z;
-      a.out[((int64_t)n * T + t1) * a.out_stride + (int64_t)h * hd + d] =
-          (uint8_t)quantize_value((float)((double)dot * sp), a.O);
+    uint8_t* orow = a.out + ((int64_t)n * T + t1) * a.out_stride + (int64_t)h * hd;
+    for (int oc = o_beg; oc < o_end; ++oc) {
+      uint32_t v[16];
+      ptx::tmem_ld16(tmem + lane_base + (uint32_t)(oc * 16), v);
+      ptx::tmem_ld_wait(v);
+      uint32_t ow[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t oq[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = oc * 16 + 4 * g + e;
+          const int32_t dot = (int32_t)v[4 * g + e] - rowo - s_vz[d];
+          oq[e] = (uint32_t)quantize_value((float)((double)dot * sp), a.O);
+        }
+        ow[g] = pack_bytes(oq[0], oq[1], oq[2], oq[3]);
+      }
+      if (t1 < T) {
+        if (a.vec_out) {
+          *reinterpret_cast<uint4*>(orow + oc * 16) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        } else {
+          for (int j = 0; j < 16 && oc * 16 + j < hd; ++j)
+            orow[oc * 16 + j] = (uint8_t)(ow[j >> 2] >> (8 * (j & 3)));
+        }
+      }
     }
-    __syncwarp();
+  }
+
+  // after an abort, wait (bounded) for the MMAs still in flight before the
+  // CTA's shared memory and TMEM are released
+  if (tid == 0 && *s_abort) {
+    ptx::mbar_wait(bar_s, 0, kAttnBudget);
+    if (ok) ptx::mbar_wait(bar_o, 0, kAttnBudget);
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, a.tmem_cols);
   }
 }
 
@@ -389,6 +736,18 @@ QA_API int qa_layernorm_bytes_dev(const void* x, int64_t x_stride, int32_t x_sig
   }
   if (rows == 0) return 0;
   const QuantK o = make_quant_k(scale_out, zp_out, qmin, qmax);
+  const bool rows16 = D % 16 == 0 && D <= kLnMaxD && x_stride % 16 == 0 &&
+                      out_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (rows16) {
+    const int64_t blocks = std::min<int64_t>((rows + 15) / 16, 2 * (int64_t)sm_count());
+    return launch_ex(layernorm_rows16_kernel, dim3((unsigned)blocks), dim3(kLnThreads), 0,
+                     (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_stride,
+                     (int)x_signed, zp_in, scale_in, gamma, beta, eps, o,
+                     static_cast<uint8_t*>(out), out_stride, rows, (int)D)
+               ? 0
+               : last_status();
+  }
   return launch_ex(layernorm_kernel, dim3(grid_for(rows * 32, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_stride,
                    (int)x_signed, zp_in, scale_in, gamma, beta, eps, o,
@@ -410,19 +769,41 @@ QA_API int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t q
     set_error(kBadArgument, "qa_attention_bytes_dev: bad arguments");
     return last_status();
   }
+  // s_params: scale of S, Mul output, P, O; z_params: (zp, qmin, qmax) of
+  // S, P, O and the Mul output zero point
+  const bool qkv_ok = qkv_signed ? (z_qkv >= -128 && z_qkv <= 127) : (z_qkv >= 0 && z_qkv <= 255);
+  if (!qkv_ok || !byte_range_host(z_params[1], z_params[2]) ||
+      !byte_range_host(z_params[4], z_params[5]) || !byte_range_host(z_params[7], z_params[8]) ||
+      (p_signed != 0) != (z_params[4] < 0) || z_params[3] < z_params[4] ||
+      z_params[3] > z_params[5]) {
+    set_error(kUnsupported, "qa_attention_bytes_dev: quantization ranges must be 8-bit");
+    return last_status();
+  }
   if (B == 0) return 0;
   AttnParams a;
   a.qkv = static_cast<const uint8_t*>(qkv);
   a.qkv_stride = qkv_stride;
   a.qkv_signed = qkv_signed ? 1 : 0;
-  a.z_qkv = z_qkv;
+  a.z_qkv = (int32_t)z_qkv;
   a.s_qkv = s_qkv;
   a.T = (int)T;
   a.H = (int)H;
   a.hd = (int)hd;
   a.D = (int)(H * hd);
-  // s_params: scale of S, Mul output, P, O; z_params: (zp, qmin, qmax) of
-  // S, P, O and the Mul output zero point
+  a.tiles = (int)((T + kAttnTile - 1) / kAttnTile);
+  a.hdp = (int)((hd + 31) & ~31);
+  a.hdn = (int)((hd + 15) & ~15);
+  a.nk = (int)((T + 15) & ~15);
+  a.tk = (int)((T + 31) & ~31);
+  a.vec_in = (hd % 16 == 0 && qkv_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0)
+                 ? 1
+                 : 0;
+  a.vec_out = (hd % 16 == 0 && out_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0)
+                  ? 1
+                  : 0;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)a.nk || cols < (uint32_t)a.hdn) cols <<= 1;
+  a.tmem_cols = cols;
   a.S = make_quant_k(s_params[0], z_params[0], z_params[1], z_params[2]);
   a.s_m = s_params[1];
   a.z_m = z_params[9];
@@ -432,10 +813,15 @@ QA_API int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t q
   a.mul_table = mul_table;
   a.out = static_cast<uint8_t*>(out);
   a.out_stride = out_stride;
-  const int tp = ((int)T + 3) & ~3;
-  const int kw = (int)hd / 4 + 1;
-  const size_t smem = (size_t)T * (hd / 4) * 4 + (size_t)T * kw * 4 + (size_t)hd * tp +
-                      (size_t)(2 * T + hd) * 4 + (size_t)(kAttnThreads / 32) * tp + 384 * 4 + 64;
+  a.status = device_status_word();
+  size_t smem = (size_t)kAttnTile * a.hdp + (size_t)a.nk * a.hdp + (size_t)a.hdn * a.tk +
+                (size_t)kAttnTile * a.tk + 256 * 8 + 256 * 4 + 256 * 4 + kAttnTile * 4 +
+                kAttnMaxHd * 4 + 2 * kAttnTile * 8 + 2 * kAttnTile * 4 + 2 * kAttnTile * 4 +
+                16 * 4 + 2 * 8 + 16;
+  // at most 512 / tmem_cols CTAs per SM, so that every allocation succeeds at once
+  const size_t per_sm = 227 * 1024;
+  const size_t ctas = 512 / cols;
+  if (ctas < 8 && smem * (ctas + 1) <= per_sm) smem = per_sm / (ctas + 1) + 1024;
   static size_t attr_bytes[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -446,7 +832,7 @@ QA_API int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t q
       return last_status();
     if (dev >= 0 && dev < 64) attr_bytes[dev] = smem;
   }
-  const int64_t grid = B * H;
+  const int64_t grid = B * H * a.tiles;
   if (grid > 0x7FFFFFFF) {
     set_error(kUnsupported, "qa_attention_bytes_dev: too many heads");
     return last_status();
