@@ -231,8 +231,16 @@ def main():
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="run this many plain forward passes of the workload and exit "
                          "(the command the ncu summaries under profiles/ are taken with)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch of a --profile-forwards run (the bench line itself "
+                         "always uses the workload's configured batch)")
     args = ap.parse_args()
     select_workload(args.workload)
+    if args.batch is not None:
+        if not args.profile_forwards:
+            ap.error("--batch only applies to --profile-forwards runs")
+        global PER_GPU_BATCH
+        PER_GPU_BATCH = args.batch
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))

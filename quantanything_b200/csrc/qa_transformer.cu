@@ -290,6 +290,13 @@ __global__ void __launch_bounds__(kLnThreads, 2)
 // range of x spans more than 600 (E would leave the normal doubles) the
 // kernel takes exp(x - max_row) per element instead.
 //
+// Quantizing S, P and O: the reference quantizes a float32 value
+// (rint((double)x / scale)); the fast path forms m = x / scale in float32
+// from the integer dot product (or the table value) and one float constant,
+// within 2^-14 of the reference's quotient wherever the clamp does not
+// decide, and keeps it when m lies farther than 2^-12 from a half-integer;
+// other elements take the double-precision definition (outlined, rare).
+//
 // Operand layouts (no swizzle, K-major): a 16-byte K slice of all R rows is
 // one block of R * 16 bytes (row r at r * 16), so core matrices are 128
 // bytes apart along M/N and R * 16 bytes apart along K.  Padded rows, keys
@@ -300,6 +307,8 @@ constexpr int kAttnTile = 128;       // query rows per CTA
 constexpr uint64_t kAttnBudget = 4000000000ull;  // bounded waits (~2 s)
 constexpr int kAttnTimeoutCode = 0x7005;
 constexpr double kAttnTableSpan = 600.0;  // largest x range the exp table covers
+constexpr double kAttnFloatSpan = 80.0;   // ... and its float copy (normal floats)
+constexpr float kAttnTieBand = 0.499755859375f;  // 0.5 - 2^-12
 
 struct AttnParams {
   const uint8_t* qkv;
@@ -319,10 +328,33 @@ struct AttnParams {
   QuantK P;                 // softmax output quantization
   int p_signed;
   QuantK O;                 // second MatMul output quantization
+  float c_s, c_o;           // s_qkv^2 / S.scale, P.scale * s_qkv / O.scale (NaN: no fast path)
   uint8_t* out;
   int64_t out_stride;
   int* status;
 };
+
+// rint(clamp(m, lo, hi)) + zp, and whether m is far enough from a
+// half-integer for that to be the reference's value (m must not be NaN).
+__device__ __forceinline__ bool quant_fast(float m, const QuantK& k, int32_t& q) {
+  const float mc = fminf(fmaxf(m, k.lo), k.hi);
+  const float t = __fadd_rn(mc, k.magic_zp);
+  const float r = __fsub_rn(t, k.magic_zp);
+  q = (int32_t)(__float_as_uint(t) - 0x4B400000u);
+  return fabsf(mc - r) < kAttnTieBand;
+}
+
+// The definitions the fast paths fall back to.
+__device__ __noinline__ int32_t quant_dot_exact(int32_t dot, double scale2, const QuantK& k) {
+  return quantize_value((float)((double)dot * scale2), k);
+}
+__device__ __noinline__ int32_t quant_prob_exact(double e, double rsum, const QuantK& k) {
+  return quantize_value((float)(e * rsum), k);
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int g) {
+  return g == 0 ? v.x : g == 1 ? v.y : g == 2 ? v.z : v.w;
+}
 
 __device__ __forceinline__ int32_t byte_sum4(uint4 v, int is_signed) {
   int32_t s = 0;
@@ -332,6 +364,7 @@ __device__ __forceinline__ int32_t byte_sum4(uint4 v, int is_signed) {
   return dp4a_any(v.w, 0x01010101u, s, is_signed, 0);
 }
 
+template <bool kMagicS>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     attention_kernel(const __grid_constant__ AttnParams a) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
@@ -340,8 +373,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   uint8_t* s_k = s_q + kAttnTile * hdp;       // hdp / 16 slices of nk rows
   uint8_t* s_vt = s_k + nk * hdp;             // tk / 16 slices of hdn rows (v transposed)
   uint8_t* s_p = s_vt + hdn * tk;             // tk / 16 slices of 128 rows
-  double* s_ex = reinterpret_cast<double*>(s_p + kAttnTile * tk);  // [256] exp table
-  float* s_xm = reinterpret_cast<float*>(s_ex + 256);              // [256] softmax input of b
+  double* s_ex = reinterpret_cast<double*>(s_p + kAttnTile * tk);  // [264] exp table, [256] = 0
+  float* s_exf = reinterpret_cast<float*>(s_ex + 264);             // [264] its float copy
+  float* s_xm = s_exf + 264;                                        // [256] softmax input of b
   int32_t* s_kz = reinterpret_cast<int32_t*>(s_xm + 256);          // [256] z * sum k (per key)
   int32_t* s_qsum = s_kz + 256;                                    // [128]
   int32_t* s_vz = s_qsum + kAttnTile;                              // [128] per head dimension
@@ -378,6 +412,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       s_red[warp] = hi;
       s_red[8 + warp] = lo;
     }
+    if (tid < 8) {
+      s_ex[256 + tid] = 0.0;  // padded keys
+      s_exf[256 + tid] = 0.f;
+    }
   }
   if (tid == 0) {
     ptx::mbar_init(bar_s, 1);
@@ -399,8 +437,14 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     x_top = fmaxf(x_top, s_red[w]);
     x_low = fminf(x_low, s_red[8 + w]);
   }
-  const bool table = (double)x_top - (double)x_low <= kAttnTableSpan;
-  if (table) s_ex[tid] = exp((double)s_xm[tid] - (double)x_top);
+  const double span = (double)x_top - (double)x_low;
+  const bool table = span <= kAttnTableSpan;
+  const bool table_f = span <= kAttnFloatSpan && a.P.inv == a.P.inv;
+  if (table) {
+    const double e = exp((double)s_xm[tid] - (double)x_top);
+    s_ex[tid] = e;
+    s_exf[tid] = (float)e;
+  }
 
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
@@ -458,7 +502,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const uint32_t idesc = ptx::idesc_i8(kAttnTile, nk, a.qkv_signed, a.qkv_signed);
     const uint32_t qa = ptx::smem_addr(s_q), ka = ptx::smem_addr(s_k);
     for (int kk = 0; kk < hdp / 32; ++kk)
-      ptx::mma_i8(tmem, ptx::smem_desc_kmajor_plain(qa + kk * 2 * (kAttnTile * 16), kAttnTile * 16, 128),
+      ptx::mma_i8(tmem,
+                  ptx::smem_desc_kmajor_plain(qa + kk * 2 * (kAttnTile * 16), kAttnTile * 16, 128),
                   ptx::smem_desc_kmajor_plain(ka + kk * 2 * (nk * 16), nk * 16, 128), idesc,
                   kk > 0 ? 1u : 0u);
     ptx::mma_commit(bar_s);
@@ -505,6 +550,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   const int c_beg = half ? c_split : 0, c_end = half ? nchunks : c_split;
   const uint32_t lane_base = ((uint32_t)(quarter * 32)) << 16;
   const double ss = a.s_qkv * a.s_qkv;
+  const float c_s = a.c_s;
+  const bool fast_s = c_s == c_s;
   const int32_t rowc = hd * z * z - z * s_qsum[r];
   // pass 1: scores -> bytes b (kept in the P buffer at their P positions),
   // with the row's partial exp-table sum (or its maximum without the table)
@@ -517,22 +564,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       ptx::tmem_ld16(tmem + lane_base + (uint32_t)(cc * 16), v);
       ptx::tmem_ld_wait(v);
       const int4* kz4 = reinterpret_cast<const int4*>(s_kz + cc * 16);
+      const int lim = T - cc * 16;  // columns of this chunk that are real keys
       uint32_t bw[4];
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int4 kz = kz4[g];
-        const int32_t kzv[4] = {kz.x, kz.y, kz.z, kz.w};
         uint32_t bq[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int32_t dot = (int32_t)v[4 * g + e] - kzv[e] + rowc;
-          bq[e] = (uint32_t)quantize_value((float)((double)dot * ss), a.S) & 0xFFu;
-          if (cc * 16 + 4 * g + e < T) {
-            if (table)
-              part += s_ex[bq[e]];
-            else
-              mx = fmaxf(mx, s_xm[bq[e]]);
-          }
+          const int32_t kze = e == 0 ? kz.x : e == 1 ? kz.y : e == 2 ? kz.z : kz.w;
+          const int32_t dot = (int32_t)v[4 * g + e] - kze + rowc;
+          const float df = kMagicS ? __int_as_float(0x4B400000 + dot) - 12582912.0f
+                                   : __int2float_rn(dot);
+          int32_t q;
+          if (!(fast_s && quant_fast(df * c_s, a.S, q))) q = quant_dot_exact(dot, ss, a.S);
+          const uint32_t b = (uint32_t)q & 0xFFu;
+          bq[e] = b;
+          const uint32_t idx = 4 * g + e < lim ? b : 256u;
+          if (table)
+            part += s_ex[idx];
+          else
+            mx = fmaxf(mx, idx < 256u ? s_xm[b] : -INFINITY);
         }
         bw[g] = pack_bytes(bq[0], bq[1], bq[2], bq[3]);
       }
@@ -550,7 +602,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const uint4 bw = *reinterpret_cast<const uint4*>(s_p + cc * (kAttnTile * 16) + r * 16);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const uint32_t word = g == 0 ? bw.x : g == 1 ? bw.y : g == 2 ? bw.z : bw.w;
+          const uint32_t word = word_of(bw, g);
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             if (cc * 16 + 4 * g + e < T)
@@ -562,6 +614,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   s_part[half * kAttnTile + r] = part;
   __syncthreads();
   const double rsum = 1.0 / (s_part[r] + s_part[kAttnTile + r]);
+  const float r_f = (float)(rsum * a.P.inv);  // P.inv: 1 / P.scale in float
+  const bool fast_p = table_f && fabsf(r_f) <= 3.0e38f;
   // pass 2: P bytes over the b bytes
   int32_t psum = 0;
   if (warp_live) {
@@ -569,20 +623,24 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     for (int cc = c_beg; cc < c_end; ++cc) {
       uint4* slot = reinterpret_cast<uint4*>(s_p + cc * (kAttnTile * 16) + r * 16);
       const uint4 bw = *slot;
+      const int lim = T - cc * 16;
       uint32_t pw[4];
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const uint32_t word = g == 0 ? bw.x : g == 1 ? bw.y : g == 2 ? bw.z : bw.w;
+        const uint32_t word = word_of(bw, g);
         uint32_t pq[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t b = (word >> (8 * e)) & 0xFFu;
-          int32_t p = 0;  // padded keys: raw 0
-          if (cc * 16 + 4 * g + e < T) {
+          int32_t p;
+          if (fast_p) {
+            if (!quant_fast(s_exf[b] * r_f, a.P, p)) p = quant_prob_exact(s_ex[b], rsum, a.P);
+          } else {
             const double ev = table ? s_ex[b] : exp((double)s_xm[b] - (double)mx);
-            p = quantize_value((float)(ev * rsum), a.P);
-            psum += p;
+            p = quant_prob_exact(ev, rsum, a.P);
           }
+          p = 4 * g + e < lim ? p : 0;  // padded keys: raw 0
+          psum += p;
           pq[e] = (uint32_t)p;
         }
         pw[g] = pack_bytes(pq[0], pq[1], pq[2], pq[3]);
@@ -604,7 +662,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const uint32_t idesc = ptx::idesc_i8(kAttnTile, hdn, a.p_signed, a.qkv_signed);
     const uint32_t pa = ptx::smem_addr(s_p), va = ptx::smem_addr(s_vt);
     for (int kk = 0; kk < tk / 32; ++kk)
-      ptx::mma_i8(tmem, ptx::smem_desc_kmajor_plain(pa + kk * 2 * (kAttnTile * 16), kAttnTile * 16, 128),
+      ptx::mma_i8(tmem,
+                  ptx::smem_desc_kmajor_plain(pa + kk * 2 * (kAttnTile * 16), kAttnTile * 16, 128),
                   ptx::smem_desc_kmajor_plain(va + kk * 2 * (hdn * 16), hdn * 16, 128), idesc,
                   kk > 0 ? 1u : 0u);
     ptx::mma_commit(bar_o);
@@ -623,7 +682,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const int32_t prow = psum + s_psum[(1 - half) * kAttnTile + r];
     const int32_t rowo = z * prow;
     const double sp = a.P.scale * a.s_qkv;
+    const float c_o = a.c_o;
+    const bool fast_o = c_o == c_o;
     uint8_t* orow = a.out + ((int64_t)n * T + t1) * a.out_stride + (int64_t)h * hd;
+#pragma unroll 1
     for (int oc = o_beg; oc < o_end; ++oc) {
       uint32_t v[16];
       ptx::tmem_ld16(tmem + lane_base + (uint32_t)(oc * 16), v);
@@ -636,7 +698,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         for (int e = 0; e < 4; ++e) {
           const int d = oc * 16 + 4 * g + e;
           const int32_t dot = (int32_t)v[4 * g + e] - rowo - s_vz[d];
-          oq[e] = (uint32_t)quantize_value((float)((double)dot * sp), a.O);
+          int32_t q;
+          if (!(fast_o && quant_fast(__int2float_rn(dot) * c_o, a.O, q)))
+            q = quant_dot_exact(dot, sp, a.O);
+          oq[e] = (uint32_t)q;
         }
         ow[g] = pack_bytes(oq[0], oq[1], oq[2], oq[3]);
       }
@@ -814,30 +879,42 @@ QA_API int qa_attention_bytes_dev(const void* qkv, int64_t qkv_stride, int32_t q
   a.out = static_cast<uint8_t*>(out);
   a.out_stride = out_stride;
   a.status = device_status_word();
+  // float constants of the fast quantize paths (NaN where the scales fall
+  // outside the range their error bound covers)
+  const double c_s = s_qkv * s_qkv / s_params[0], c_o = s_params[2] * s_qkv / s_params[3];
+  a.c_s = (a.S.inv == a.S.inv && std::isfinite(c_s) && c_s > 1e-30 && c_s < 1e30) ? (float)c_s
+                                                                                  : std::nanf("");
+  a.c_o = (a.O.inv == a.O.inv && std::isfinite(c_o) && c_o > 1e-30 && c_o < 1e30) ? (float)c_o
+                                                                                  : std::nanf("");
+  // the scores' integer dot products fit the exact float conversion by
+  // exponent-field addition when |dot| < 2^22
+  const bool magic_s = hd * 255 * 255 < (1 << 22);
   size_t smem = (size_t)kAttnTile * a.hdp + (size_t)a.nk * a.hdp + (size_t)a.hdn * a.tk +
-                (size_t)kAttnTile * a.tk + 256 * 8 + 256 * 4 + 256 * 4 + kAttnTile * 4 +
-                kAttnMaxHd * 4 + 2 * kAttnTile * 8 + 2 * kAttnTile * 4 + 2 * kAttnTile * 4 +
-                16 * 4 + 2 * 8 + 16;
+                (size_t)kAttnTile * a.tk + 264 * 8 + 264 * 4 + 256 * 4 + 256 * 4 +
+                kAttnTile * 4 + kAttnMaxHd * 4 + 2 * kAttnTile * 8 + 2 * kAttnTile * 4 +
+                2 * kAttnTile * 4 + 16 * 4 + 2 * 8 + 16;
+  auto kern = magic_s ? attention_kernel<true> : attention_kernel<false>;
   // at most 512 / tmem_cols CTAs per SM, so that every allocation succeeds at once
   const size_t per_sm = 227 * 1024;
   const size_t ctas = 512 / cols;
   if (ctas < 8 && smem * (ctas + 1) <= per_sm) smem = per_sm / (ctas + 1) + 1024;
-  static size_t attr_bytes[64] = {};
+  static size_t attr_bytes[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || attr_bytes[dev] < smem)) {
-    if (cuda_failed(cudaFuncSetAttribute(attention_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                    "cudaFuncSetAttribute(attention)"))
+  size_t* attr = (dev >= 0 && dev < 64) ? &attr_bytes[magic_s ? 1 : 0][dev] : nullptr;
+  if (smem > 48 * 1024 && (!attr || *attr < smem)) {
+    if (cuda_failed(
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+            "cudaFuncSetAttribute(attention)"))
       return last_status();
-    if (dev >= 0 && dev < 64) attr_bytes[dev] = smem;
+    if (attr) *attr = smem;
   }
   const int64_t grid = B * H * a.tiles;
   if (grid > 0x7FFFFFFF) {
     set_error(kUnsupported, "qa_attention_bytes_dev: too many heads");
     return last_status();
   }
-  return launch_ex(attention_kernel, dim3((unsigned)grid), dim3(kAttnThreads), smem,
+  return launch_ex(kern, dim3((unsigned)grid), dim3(kAttnThreads), smem,
                    (cudaStream_t)stream, true, a)
              ? 0
              : last_status();
