@@ -366,21 +366,22 @@ bool encode_tiled_map(CUtensorMap* map, CUtensorMapDataType type, int rank, cons
   return true;
 }
 
-// 2-D uint8 tensor map over [rows, row_bytes] with a 128 x box_rows box in
-// the 128-byte swizzle.
-bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
-                      int box_rows) {
+// 2-D uint8 tensor map over [rows, row_bytes] (rows `row_stride` bytes
+// apart) with a 128 x box_rows box in the 128-byte swizzle; bytes past
+// row_bytes and rows past `rows` read as zero.
+bool make_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                    int64_t row_stride, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error(kCudaError, "cuTensorMapEncodeTiled unavailable");
     return false;
   }
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) {
-    set_error(kBadArgument, "weight tensor map: base / row stride not 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride & 15) || row_bytes > row_stride) {
+    set_error(kBadArgument, "row tensor map: base / row stride not 16-byte aligned");
     return false;
   }
   cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride};
   cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1u, 1u};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
@@ -391,6 +392,11 @@ bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t 
     return false;
   }
   return true;
+}
+
+bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                      int box_rows) {
+  return make_rows_tmap(map, base, rows, row_bytes, row_bytes, box_rows);
 }
 
 template <int BN, int PA, int PB, int kChunk, int kEpi, int kStages>

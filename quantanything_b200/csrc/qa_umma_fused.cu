@@ -35,6 +35,8 @@ namespace qa {
 
 bool make_weight_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
                       int box_rows);
+bool make_rows_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes,
+                    int64_t row_stride, int box_rows);
 bool fused_conv_grouped(const qa_fused_conv_desc& d, cudaStream_t st);
 bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);
 
@@ -136,7 +138,9 @@ __device__ __noinline__ int64_t add_exact_ool(int64_t a, int64_t q, const FusedE
   return clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
 }
 
-// kChunk: bytes per gathered tap chunk of the thread gather (4 or 16), or 0
+// kChunk: bytes per gathered tap chunk of the thread gather (4 or 16), 1
+// for a pointwise layer read as a row matrix by 2-D tiled TMA (one load per
+// K-block, 128-byte swizzle), or 0
 // for the TMA im2col gather (16-byte channel slices, no swizzle).
 template <int BN, int kChunk, bool kResidentB, int kStages>
 __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThreads), 1)
@@ -145,7 +149,8 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
                           const __grid_constant__ CUtensorMap tmap_a) {
   using L = Layout<BN, kChunk, kResidentB, kStages>;
   constexpr bool kTmaA = kChunk == 0;
-  constexpr int kTapBytes = kTmaA ? 16 : kChunk;
+  constexpr bool kTileA = kChunk == 1;
+  constexpr int kTapBytes = (kTmaA || kTileA) ? 16 : kChunk;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_addr(smem_raw);
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      ptx::mbar_init(a_full(s), kTmaA ? 1 : kProducers);
+      ptx::mbar_init(a_full(s), (kTmaA || kTileA) ? 1 : kProducers);
       ptx::mbar_init(a_empty(s), 1);
       ptx::mbar_init(b_full(s), 1);
     }
@@ -204,10 +209,10 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   }
   if (warp == 5 && lane == 0) {
     ptx::prefetch_tmap(&tmap_b);
-    if (kTmaA) ptx::prefetch_tmap(&tmap_a);
+    if (kTmaA || kTileA) ptx::prefetch_tmap(&tmap_a);
   }
   if (warp < 4) {
-    if (!kTmaA) {
+    if (!kTmaA && !kTileA) {
       // zero every activation stage once: the K padding is never gathered
       // (the TMA gather leaves it stale: it meets zero weight columns)
       uint4* z = reinterpret_cast<uint4*>(sm);
@@ -302,7 +307,26 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     return false;
   };
 
-  if (kTmaA && warp < 4) {
+  if (kTileA && warp < 4) {
+    // ------------------------------------------ activation rows (TMA) --
+    // One thread: per K-block, one 2-D load of 128 rows x 128 bytes in the
+    // 128-byte swizzle (bytes past C and rows past M read as zero).
+    if (tid == 0) {
+      int g = 0;
+      for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
+        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
+          ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)L::kAStage);
+          ptx::tma_load_2d(a_base + s * L::kAStage, &tmap_a, a_full(s), kb * kBK, mt * kBM);
+        }
+      }
+      // after an abort, wait (bounded) for the loads still in flight
+      if (*s_abort)
+        for (int gg = max(0, g - kStages); gg < g; ++gg)
+          ptx::mbar_wait(a_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
+    }
+  } else if (kTmaA && warp < 4) {
     // ------------------------------------------- activation gather (TMA) --
     // One thread: per K-block, one im2col load per 16-byte channel slice of
     // a tap brings that slice for all 128 output pixels of the tile, in
@@ -448,7 +472,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           const uint32_t b_addr = b_base + (kResidentB ? kb : s) * L::kBBlock;
           for (int kk = 0; kk < ksteps; ++kk) {
             // TMA gather: 16-byte slices 2048 bytes apart along K, 8-row
-            // groups 128 bytes apart; thread gather: 128-byte swizzle
+            // groups 128 bytes apart; row TMA / thread gather: 128-byte swizzle
             const uint64_t adesc =
                 kTmaA ? ptx::smem_desc_kmajor_plain(a_addr + kk * 2 * (kBM * 16), kBM * 16, 128)
                       : ptx::smem_desc_sw128(a_addr + kk * 32);
@@ -639,7 +663,7 @@ size_t smem_bytes(int num_kb) {
   const int b_blocks = kResidentB ? num_kb : kStages;
   return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + BN * 16 +
          4 * BN * 8 + BN * 4 + 4 * kTab * 4 + (3 * kStages + 2 * L::kAccs + 2) * 8 +
-         (size_t)num_kb * (kBK / (kChunk == 0 ? 16 : kChunk)) * sizeof(TapEntry);
+         (size_t)num_kb * (kBK / (kChunk <= 1 ? 16 : kChunk)) * sizeof(TapEntry);
 }
 
 constexpr int kStagesFused = 4;
@@ -813,7 +837,14 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   if (!make_weight_tmap(&tmap, d.w, d.w_rows, d.w_kp, bn)) return false;
   CUtensorMap tmap_a;
   std::memset(&tmap_a, 0, sizeof(tmap_a));
-  const bool tma_a = chunk == 16 && make_im2col_tmap(&tmap_a, d);
+  // pointwise layers (1x1, stride 1, no padding) read their input pixels
+  // as a plain row matrix: one 2-D TMA load per 16 KB K-block
+  const bool tile_a = chunk == 16 && tma_gather_enabled() && d.KH == 1 && d.KW == 1 &&
+                      d.SH == 1 && d.SW == 1 && d.PH == 0 && d.PW == 0 && d.OH == d.H &&
+                      d.OW == d.W &&
+                      make_rows_tmap(&tmap_a, d.x, d.N * d.H * d.W, d.C, d.x_pix_stride, kBM);
+  if (!tile_a) clear_error();
+  const bool tma_a = !tile_a && chunk == 16 && make_im2col_tmap(&tmap_a, d);
 
   FusedParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -858,6 +889,15 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
                            : 0;
   prm.fast.r64 = d.out2 ? small_rescale_fast(d.r_zp_in, d.r_m, d.r_s) : 0;
   fill_fused_epilogue(prm.epi, d);
+  if (tile_a) {
+    switch (bn) {
+      case 16: return launch_bn<16, 1>(prm, tmap, tmap_a, st);
+      case 32: return launch_bn<32, 1>(prm, tmap, tmap_a, st);
+      case 64: return launch_bn<64, 1>(prm, tmap, tmap_a, st);
+      case 128: return launch_bn<128, 1>(prm, tmap, tmap_a, st);
+      case 256: return launch_bn<256, 1>(prm, tmap, tmap_a, st);
+    }
+  }
   if (tma_a) {
     switch (bn) {
       case 16: return launch_bn<16, 0>(prm, tmap, tmap_a, st);
