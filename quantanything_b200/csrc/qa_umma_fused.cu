@@ -111,14 +111,14 @@ template <int BN, int kChunk, bool kResidentB, int kStages>
 struct Layout {
   static constexpr int kAStage = kBM * kBK;       // 16 KB
   static constexpr int kBBlock = BN * kBK;        // one K-block of weights
-  // Two epilogue warpgroups alternate tiles when four accumulators fit in
-  // TMEM (BN <= 128); each group owns two accumulators (double buffered).
-  static constexpr int kGroups = BN <= 128 ? 2 : 1;
-  // with two groups and at least 32 columns, both groups drain every tile
-  // (group g its half of the columns); with 16 columns they alternate tiles
-  static constexpr bool kSplit = kGroups == 2 && BN >= 32;
+  // Two epilogue warpgroups.  With at least 32 columns both drain every
+  // tile (group g its half of the columns); with 16 columns they alternate
+  // tiles.  Accumulators: four when they fit in TMEM (BN <= 128), else two
+  // (still double buffered).
+  static constexpr int kGroups = 2;
+  static constexpr bool kSplit = BN >= 32;
   static constexpr int kGroupCols = kSplit ? BN / 2 : BN;
-  static constexpr int kAccs = 2 * kGroups;
+  static constexpr int kAccs = BN <= 128 ? 4 : 2;
   static constexpr int kThreads = 192 + kGroups * kEpilogueThreads;
   static constexpr int kCols = kAccs * BN;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
