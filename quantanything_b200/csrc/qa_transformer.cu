@@ -356,6 +356,88 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int g) {
   return g == 0 ? v.x : g == 1 ? v.y : g == 2 ? v.z : v.w;
 }
 
+// Sixteen scores of one key chunk -> their quantized S values (low byte of
+// each tb word: the float bits of rint(m) + zp + 1.5 * 2^23, or the value
+// itself where the exact definition decided).  One warp vote per chunk sends
+// the lanes with an element near a rounding tie to the exact path.
+template <bool kMagicS>
+__device__ __forceinline__ void score_bytes(const uint32_t (&v)[16], const int4* kz4, int32_t rowc,
+                                            float c_s, bool fast_s, double ss, const QuantK& S,
+                                            uint32_t (&tb)[16]) {
+  uint32_t okm = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int4 kz = kz4[g];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * g + e;
+      const int32_t kze = e == 0 ? kz.x : e == 1 ? kz.y : e == 2 ? kz.z : kz.w;
+      const int32_t dot = (int32_t)v[i] - kze + rowc;
+      const float df = kMagicS ? __int_as_float(0x4B400000 + dot) - 12582912.0f
+                               : __int2float_rn(dot);
+      const float mc = fminf(fmaxf(df * c_s, S.lo), S.hi);
+      const float t = __fadd_rn(mc, S.magic_zp);
+      const float rr = __fsub_rn(t, S.magic_zp);
+      okm |= (fabsf(mc - rr) < kAttnTieBand ? 1u : 0u) << i;
+      tb[i] = __float_as_uint(t);
+    }
+  }
+  if (!fast_s) okm = 0;
+  if (__any_sync(0xffffffffu, okm != 0xFFFFu)) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int4 kz = kz4[g];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * g + e;
+        if (!((okm >> i) & 1u)) {
+          const int32_t kze = e == 0 ? kz.x : e == 1 ? kz.y : e == 2 ? kz.z : kz.w;
+          tb[i] = (uint32_t)quant_dot_exact((int32_t)v[i] - kze + rowc, ss, S);
+        }
+      }
+    }
+  }
+}
+
+// Sixteen probabilities of one key chunk from its score bytes `bw`: the
+// float bits of rint(m) + zp + 1.5 * 2^23 per element (the exact path's
+// value is stored in the same form).
+__device__ __forceinline__ void prob_bytes(uint4 bw, const double* s_ex, const float* s_exf,
+                                           const float* s_xm, bool table, bool fast_p, float r_f,
+                                           double rsum, float mx, const QuantK& P,
+                                           uint32_t (&tp)[16]) {
+  uint32_t okm = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t word = word_of(bw, g);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * g + e;
+      const float mc = fminf(fmaxf(s_exf[(word >> (8 * e)) & 0xFFu] * r_f, P.lo), P.hi);
+      const float t = __fadd_rn(mc, P.magic_zp);
+      const float rr = __fsub_rn(t, P.magic_zp);
+      okm |= (fabsf(mc - rr) < kAttnTieBand ? 1u : 0u) << i;
+      tp[i] = __float_as_uint(t);
+    }
+  }
+  if (!fast_p) okm = 0;
+  if (__any_sync(0xffffffffu, okm != 0xFFFFu)) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t word = word_of(bw, g);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * g + e;
+        if (!((okm >> i) & 1u)) {
+          const uint32_t b = (word >> (8 * e)) & 0xFFu;
+          const double ev = table ? s_ex[b] : exp((double)s_xm[b] - (double)mx);
+          tp[i] = (uint32_t)quant_prob_exact(ev, rsum, P) + 0x4B400000u;
+        }
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ int32_t byte_sum4(uint4 v, int is_signed) {
   int32_t s = 0;
   s = dp4a_any(v.x, 0x01010101u, s, is_signed, 0);
@@ -560,36 +642,34 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   if (warp_live) {
 #pragma unroll 1
     for (int cc = c_beg; cc < c_end; ++cc) {
-      uint32_t v[16];
+      uint32_t v[16], tb[16];
       ptx::tmem_ld16(tmem + lane_base + (uint32_t)(cc * 16), v);
       ptx::tmem_ld_wait(v);
-      const int4* kz4 = reinterpret_cast<const int4*>(s_kz + cc * 16);
+      score_bytes<kMagicS>(v, reinterpret_cast<const int4*>(s_kz + cc * 16), rowc, c_s,
+                           fast_s, ss, a.S, tb);
       const int lim = T - cc * 16;  // columns of this chunk that are real keys
-      uint32_t bw[4];
+      if (table) {
+        if (lim >= 16) {
+          double p0 = 0.0, p1 = 0.0;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int4 kz = kz4[g];
-        uint32_t bq[4];
+          for (int i = 0; i < 16; i += 2) {
+            p0 += s_ex[tb[i] & 0xFFu];
+            p1 += s_ex[tb[i + 1] & 0xFFu];
+          }
+          part += p0 + p1;
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int32_t kze = e == 0 ? kz.x : e == 1 ? kz.y : e == 2 ? kz.z : kz.w;
-          const int32_t dot = (int32_t)v[4 * g + e] - kze + rowc;
-          const float df = kMagicS ? __int_as_float(0x4B400000 + dot) - 12582912.0f
-                                   : __int2float_rn(dot);
-          int32_t q;
-          if (!(fast_s && quant_fast(df * c_s, a.S, q))) q = quant_dot_exact(dot, ss, a.S);
-          const uint32_t b = (uint32_t)q & 0xFFu;
-          bq[e] = b;
-          const uint32_t idx = 4 * g + e < lim ? b : 256u;
-          if (table)
-            part += s_ex[idx];
-          else
-            mx = fmaxf(mx, idx < 256u ? s_xm[b] : -INFINITY);
+          for (int i = 0; i < 16; ++i) part += s_ex[i < lim ? (tb[i] & 0xFFu) : 256u];
         }
-        bw[g] = pack_bytes(bq[0], bq[1], bq[2], bq[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < lim) mx = fmaxf(mx, s_xm[tb[i] & 0xFFu]);
       }
       *reinterpret_cast<uint4*>(s_p + cc * (kAttnTile * 16) + r * 16) =
-          make_uint4(bw[0], bw[1], bw[2], bw[3]);
+          make_uint4(pack_bytes(tb[0], tb[1], tb[2], tb[3]), pack_bytes(tb[4], tb[5], tb[6], tb[7]),
+                     pack_bytes(tb[8], tb[9], tb[10], tb[11]),
+                     pack_bytes(tb[12], tb[13], tb[14], tb[15]));
     }
   }
   if (!table) {  // CTA-uniform: the row maximum, then the sum of exp(x - max)
@@ -622,30 +702,22 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll 1
     for (int cc = c_beg; cc < c_end; ++cc) {
       uint4* slot = reinterpret_cast<uint4*>(s_p + cc * (kAttnTile * 16) + r * 16);
-      const uint4 bw = *slot;
+      uint32_t tp[16];
+      prob_bytes(*slot, s_ex, s_exf, s_xm, table, fast_p, r_f, rsum, mx, a.P, tp);
       const int lim = T - cc * 16;
-      uint32_t pw[4];
+      int32_t pv[16];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const uint32_t word = word_of(bw, g);
-        uint32_t pq[4];
+      for (int i = 0; i < 16; ++i) pv[i] = (int32_t)(tp[i] - 0x4B400000u);
+      if (lim < 16) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t b = (word >> (8 * e)) & 0xFFu;
-          int32_t p;
-          if (fast_p) {
-            if (!quant_fast(s_exf[b] * r_f, a.P, p)) p = quant_prob_exact(s_ex[b], rsum, a.P);
-          } else {
-            const double ev = table ? s_ex[b] : exp((double)s_xm[b] - (double)mx);
-            p = quant_prob_exact(ev, rsum, a.P);
-          }
-          p = 4 * g + e < lim ? p : 0;  // padded keys: raw 0
-          psum += p;
-          pq[e] = (uint32_t)p;
-        }
-        pw[g] = pack_bytes(pq[0], pq[1], pq[2], pq[3]);
+        for (int i = 0; i < 16; ++i) pv[i] = i < lim ? pv[i] : 0;  // padded keys: raw 0
       }
-      *slot = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) psum += pv[i];
+      *slot = make_uint4(pack_bytes(pv[0], pv[1], pv[2], pv[3]),
+                         pack_bytes(pv[4], pv[5], pv[6], pv[7]),
+                         pack_bytes(pv[8], pv[9], pv[10], pv[11]),
+                         pack_bytes(pv[12], pv[13], pv[14], pv[15]));
     }
   }
   // key slices past the score columns (tk > nk) hold zeros
