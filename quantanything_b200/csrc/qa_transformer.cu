@@ -156,25 +156,46 @@ __global__ void layernorm_kernel(const uint8_t* __restrict__ x, int64_t x_stride
 
 // Rows of D % 16 == 0 features, D <= 16 * 16 * kLnChunks, 16-byte aligned
 // rows: sixteen lanes per row, each holding up to kLnChunks 16-byte chunks
-// in registers.  The dequantized value of each byte comes from a 256-entry
-// float64 table.  Their float64 row sum is exact in any order (every value
-// is a float32 multiple of the same scale, the sum spans fewer than 53
-// bits), so the mean is the reference's to the bit; the variance sum runs
-// in another order than NumPy's.  gamma / beta are staged as float64 and
-// skipped when they are all ones / zeros (x * 1 + 0 == x).
+// in registers.  The dequantized value of each byte comes from a float64
+// table kept in 32 copies, one per lane (entry b of lane l at b * 32 + l,
+// so a warp's lookups never share a bank).  The float64 row sum of those
+// values is exact in any order (every value is a float32 multiple of the
+// same scale and the sum spans fewer than 53 bits), so the mean is the
+// reference's to the bit; the variance sum runs in another order than
+// NumPy's.  With gamma all ones and beta all zeros (x * 1 + 0 == x) the
+// output depends on the input byte alone, so each row builds a 256-entry
+// output table over its byte range and its elements look it up; otherwise
+// gamma and beta are applied per element in float64.
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int g) {
+  return g == 0 ? v.x : g == 1 ? v.y : g == 2 ? v.z : v.w;
+}
+
 constexpr int kLnChunks = 4;
 constexpr int kLnThreads = 256;
 constexpr int kLnMaxD = 16 * 16 * kLnChunks;
+constexpr int kLnRows = kLnThreads / 16;  // rows in flight per block
+
+size_t layernorm_rows16_smem(int D) {
+  return (size_t)256 * 32 * 8 + (size_t)2 * D * 8 + (size_t)kLnRows * 256;
+}
 
 __global__ void __launch_bounds__(kLnThreads, 2)
     layernorm_rows16_kernel(const uint8_t* __restrict__ x, int64_t x_stride, int x_signed,
                             int64_t zp_in, double s_in, const float* __restrict__ gamma,
                             const float* __restrict__ beta, double eps, QuantK o,
                             uint8_t* __restrict__ out, int64_t out_stride, int64_t rows, int D) {
-  __shared__ double s_v[256];
-  __shared__ double s_g[kLnMaxD], s_b[kLnMaxD];
+  extern __shared__ __align__(16) double ln_smem[];
+  double* s_v = ln_smem;            // [256][32]
+  double* s_g = s_v + 256 * 32;     // [D]
+  double* s_b = s_g + D;            // [D]
+  uint8_t* s_out = reinterpret_cast<uint8_t*>(s_b + D);  // [kLnRows][256]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  s_v[tid] = (double)dequant(x_signed ? (int32_t)(int8_t)tid : tid, zp_in, s_in);
+  {
+    const double vb = (double)dequant(x_signed ? (int32_t)(int8_t)tid : tid, zp_in, s_in);
+    double2* row = reinterpret_cast<double2*>(s_v + tid * 32);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) row[c] = make_double2(vb, vb);
+  }
   int ident = 1;
   for (int d = tid; d < D; d += kLnThreads) {
     const double g = (double)gamma[d], b = beta ? (double)beta[d] : 0.0;
@@ -185,12 +206,14 @@ __global__ void __launch_bounds__(kLnThreads, 2)
   const bool affine = !__syncthreads_and(ident);
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const int l16 = lane & 15;
+  const int l16 = lane & 15, sub = lane >> 4;
   const int chunks = D / 16;
   const double rD = (double)D;
+  const double* v_l = s_v + lane;  // this lane's copy: entry b at v_l[b * 32]
+  uint8_t* tab = s_out + (warp * 2 + sub) * 256;
   for (int64_t pair = (int64_t)blockIdx.x * (kLnThreads / 32) + warp; 2 * pair < rows;
        pair += (int64_t)gridDim.x * (kLnThreads / 32)) {
-    const int64_t row = 2 * pair + (lane >> 4);
+    const int64_t row = 2 * pair + sub;
     const bool valid = row < rows;  // both halves of the warp run every shuffle
     uint4 c[kLnChunks];
 #pragma unroll
@@ -199,18 +222,24 @@ __global__ void __launch_bounds__(kLnThreads, 2)
       c[i] = (valid && j < chunks) ? *reinterpret_cast<const uint4*>(x + row * x_stride + 16 * j)
                                    : make_uint4(0u, 0u, 0u, 0u);
     }
-    auto word = [&](int i, int g) -> uint32_t {
-      return g == 0 ? c[i].x : g == 1 ? c[i].y : g == 2 ? c[i].z : c[i].w;
-    };
+    // pass 1: sum, and the byte range (as the bytes' integer values)
     double sum = 0.0;
+    uint32_t bmin = x_signed ? 0x7F7F7F7Fu : 0xFFFFFFFFu, bmax = x_signed ? 0x80808080u : 0u;
 #pragma unroll
     for (int i = 0; i < kLnChunks; ++i)
       if (l16 + 16 * i < chunks) {
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const uint32_t w = word(i, g);
-          sum += (s_v[w & 0xFFu] + s_v[(w >> 8) & 0xFFu]) +
-                 (s_v[(w >> 16) & 0xFFu] + s_v[w >> 24]);
+          const uint32_t w = word_of(c[i], g);
+          sum += (v_l[(w & 0xFFu) * 32] + v_l[((w >> 8) & 0xFFu) * 32]) +
+                 (v_l[((w >> 16) & 0xFFu) * 32] + v_l[(w >> 24) * 32]);
+          if (x_signed) {
+            bmin = __vmins4(bmin, w);
+            bmax = __vmaxs4(bmax, w);
+          } else {
+            bmin = __vminu4(bmin, w);
+            bmax = __vmaxu4(bmax, w);
+          }
         }
       }
 #pragma unroll
@@ -222,9 +251,9 @@ __global__ void __launch_bounds__(kLnThreads, 2)
       if (l16 + 16 * i < chunks) {
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const uint32_t w = word(i, g);
-          const double a0 = s_v[w & 0xFFu] - mean, a1 = s_v[(w >> 8) & 0xFFu] - mean;
-          const double a2 = s_v[(w >> 16) & 0xFFu] - mean, a3 = s_v[w >> 24] - mean;
+          const uint32_t w = word_of(c[i], g);
+          const double a0 = v_l[(w & 0xFFu) * 32] - mean, a1 = v_l[((w >> 8) & 0xFFu) * 32] - mean;
+          const double a2 = v_l[((w >> 16) & 0xFFu) * 32] - mean, a3 = v_l[(w >> 24) * 32] - mean;
           sq0 = fma(a0, a0, sq0);
           sq1 = fma(a1, a1, sq1);
           sq0 = fma(a2, a2, sq0);
@@ -238,29 +267,66 @@ __global__ void __launch_bounds__(kLnThreads, 2)
     // differ from that quotient by at most one float64 ulp, which reaches
     // the float32 result only on a float32 rounding boundary
     const double inv = 1.0 / sqrt(sq / rD + eps);
-    if (!valid) continue;
     uint8_t* orow = out + row * out_stride;
+    if (!affine) {
+      // the row's byte range [lo, hi] as integer values
+      int lo, hi;
+      if (x_signed) {
+        lo = min(min((int)(int8_t)bmin, (int)(int8_t)(bmin >> 8)),
+                 min((int)(int8_t)(bmin >> 16), (int)(int8_t)(bmin >> 24)));
+        hi = max(max((int)(int8_t)bmax, (int)(int8_t)(bmax >> 8)),
+                 max((int)(int8_t)(bmax >> 16), (int)(int8_t)(bmax >> 24)));
+      } else {
+        lo = (int)min(min(bmin & 0xFFu, (bmin >> 8) & 0xFFu), min((bmin >> 16) & 0xFFu, bmin >> 24));
+        hi = (int)max(max(bmax & 0xFFu, (bmax >> 8) & 0xFFu), max((bmax >> 16) & 0xFFu, bmax >> 24));
+      }
 #pragma unroll
-    for (int i = 0; i < kLnChunks; ++i) {
-      const int j = l16 + 16 * i;
-      if (j < chunks) {
-        uint32_t ow[4];
+      for (int o_ = 8; o_ > 0; o_ >>= 1) {
+        lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o_));
+        hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o_));
+      }
+      for (int v = lo + l16; v <= hi; v += 16) {
+        const uint32_t b = (uint32_t)v & 0xFFu;
+        tab[b] = (uint8_t)quantize_value((float)((v_l[b * 32] - mean) * inv), o);
+      }
+      __syncwarp();
+      if (valid) {
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const uint32_t w = word(i, g);
-          uint32_t q[4];
+        for (int i = 0; i < kLnChunks; ++i) {
+          const int j = l16 + 16 * i;
+          if (j < chunks) {
+            uint32_t ow[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            double y = (s_v[(w >> (8 * e)) & 0xFFu] - mean) * inv;
-            if (affine) {
-              const int d = 16 * j + 4 * g + e;
-              y = y * s_g[d] + s_b[d];
+            for (int g = 0; g < 4; ++g) {
+              const uint32_t w = word_of(c[i], g);
+              ow[g] = pack_bytes(tab[w & 0xFFu], tab[(w >> 8) & 0xFFu], tab[(w >> 16) & 0xFFu],
+                                 tab[w >> 24]);
             }
-            q[e] = (uint32_t)quantize_value((float)y, o);
+            *reinterpret_cast<uint4*>(orow + 16 * j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
           }
-          ow[g] = pack_bytes(q[0], q[1], q[2], q[3]);
         }
-        *reinterpret_cast<uint4*>(orow + 16 * j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
+      __syncwarp();  // the table is rebuilt for the next row
+    } else if (valid) {
+#pragma unroll
+      for (int i = 0; i < kLnChunks; ++i) {
+        const int j = l16 + 16 * i;
+        if (j < chunks) {
+          uint32_t ow[4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint32_t w = word_of(c[i], g);
+            uint32_t q[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int d = 16 * j + 4 * g + e;
+              const double y = (v_l[((w >> (8 * e)) & 0xFFu) * 32] - mean) * inv * s_g[d] + s_b[d];
+              q[e] = (uint32_t)quantize_value((float)y, o);
+            }
+            ow[g] = pack_bytes(q[0], q[1], q[2], q[3]);
+          }
+          *reinterpret_cast<uint4*>(orow + 16 * j) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
       }
     }
   }
@@ -350,10 +416,6 @@ __device__ __noinline__ int32_t quant_dot_exact(int32_t dot, double scale2, cons
 }
 __device__ __noinline__ int32_t quant_prob_exact(double e, double rsum, const QuantK& k) {
   return quantize_value((float)(e * rsum), k);
-}
-
-__device__ __forceinline__ uint32_t word_of(const uint4& v, int g) {
-  return g == 0 ? v.x : g == 1 ? v.y : g == 2 ? v.z : v.w;
 }
 
 // Sixteen scores of one key chunk -> their quantized S values (low byte of
@@ -877,8 +939,20 @@ QA_API int qa_layernorm_bytes_dev(const void* x, int64_t x_stride, int32_t x_sig
                       out_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(out) & 15) == 0;
   if (rows16) {
+    const size_t smem = layernorm_rows16_smem((int)D);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      if (cuda_failed(cudaFuncSetAttribute(layernorm_rows16_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)layernorm_rows16_smem(kLnMaxD)),
+                      "cudaFuncSetAttribute(layernorm)"))
+        return last_status();
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
     const int64_t blocks = std::min<int64_t>((rows + 15) / 16, 2 * (int64_t)sm_count());
-    return launch_ex(layernorm_rows16_kernel, dim3((unsigned)blocks), dim3(kLnThreads), 0,
+    return launch_ex(layernorm_rows16_kernel, dim3((unsigned)blocks), dim3(kLnThreads), smem,
                      (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_stride,
                      (int)x_signed, zp_in, scale_in, gamma, beta, eps, o,
                      static_cast<uint8_t*>(out), out_stride, rows, (int)D)
