@@ -107,6 +107,22 @@ __device__ __forceinline__ uint32_t pack4(int32_t a, int32_t b, int32_t c, int32
                      __byte_perm((uint32_t)c, (uint32_t)d, 0x0040), 0x5410);
 }
 
+// Four int32 values saturated to 8 bits (int8 or uint8) and packed
+// little-endian: cvt.pack.sat gives sat(b) | sat(a) << 8 | c << 16.
+__device__ __forceinline__ uint32_t pack_sat4(int32_t a, int32_t b, int32_t c, int32_t d,
+                                              bool is_signed) {
+  uint32_t hi, r;
+  const uint32_t zero = 0;
+  if (is_signed) {
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(d), "r"(c), "r"(zero));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  } else {
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(d), "r"(c), "r"(zero));
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  }
+  return r;
+}
+
 template <int BN, int kChunk, bool kResidentB, int kStages>
 struct Layout {
   static constexpr int kAStage = kBM * kBK;       // 16 KB
@@ -246,11 +262,18 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       s_ts[c] = ts;
       s_rnd[c] = (ts >= 1 && ts <= 62) ? ((int64_t)1 << (ts - 1)) : 0;
       // (x * M0 + 2^(ts-1)) >> ts == (hi32(x * M0) + 2^(ts-33)) >> (ts - 32)
-      // for ts in [33, 62]: the low word cannot carry into the rounding
-      const bool hi = ts >= 33 && ts <= 62;
+      // for ts in [33, 62]: the low word cannot carry into the rounding.
+      // The output zero point rides in the rounding term (z * 2^sh added
+      // before the arithmetic shift adds z after it) while the sum stays
+      // in int32: |hi32| < 2^30.
+      const bool hi0 = ts >= 33 && ts <= 62;
+      const int sh = hi0 ? ts - 32 : 1;
+      const int64_t zfold = e.zp * ((int64_t)1 << sh);
+      const bool hi = hi0 && e.zp > -(1 << 20) && e.zp < (1 << 20) &&
+                      (zfold < 0 ? -zfold : zfold) + ((int64_t)1 << (sh - 1)) < ((int64_t)1 << 30);
       if (v && !hi) hi_ok = 0;
-      const int sh = hi ? ts - 32 : 1;
-      s_ch[c] = make_int4((int32_t)s_bias[c], (int32_t)s_mult[c], 1 << (sh - 1), sh);
+      s_ch[c] = make_int4((int32_t)s_bias[c], (int32_t)s_mult[c],
+                          (int32_t)(((int64_t)1 << (sh - 1)) + (hi ? zfold : 0)), sh);
     }
     // Every value the epilogue carries between steps is an 8-bit one (the
     // host checks the clamp ranges), so each step after the requantize is a
@@ -498,7 +521,13 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     const int quarter = warp & 3;  // TMEM lanes 32*quarter.. belong to this warp
     const int r = quarter * 32 + lane;
     const bool fast_rq = p.fast.requant;
-    const bool hi_rq = fast_rq && hi_all && e.zp > -(1 << 20) && e.zp < (1 << 20);
+    const bool hi_rq = fast_rq && hi_all;
+    // plain requantize to the full 8-bit range: clamp and pack in one step
+    // (streamed-weight variants only: the resident ones are at their
+    // register limit)
+    const bool pack_sat = !kResidentB && hi_rq && !e.lut && !e.res && !e.out2 &&
+                          ((e.qmin == 0 && e.qmax == 255) || (e.qmin == -128 && e.qmax == 127));
+    const bool pack_signed = e.qmin < 0;
     const bool has_lut = e.lut != nullptr, add_tab = p.fast.add_tab;
     const int32_t zp32 = (int32_t)e.zp, qmin32 = (int32_t)e.qmin, qmax32 = (int32_t)e.qmax;
     const int32_t aqmin32 = (int32_t)e.add_qmin, aqmax32 = (int32_t)e.add_qmax;
@@ -547,14 +576,35 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           const int nval = min(16, n_valid - (n0 + cc));
           const bool vec = vec_ok && nval == 16;
           int32_t q[16];
+          if (pack_sat) {
+            int32_t t[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int4 ch = s_ch[cc + jj];
+              t[jj] = (__mulhi((int32_t)v[jj] + ch.x, ch.y) + ch.z) >> ch.w;
+            }
+            uint32_t o[4];
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              o[k4] = pack_sat4(t[4 * k4], t[4 * k4 + 1], t[4 * k4 + 2], t[4 * k4 + 3],
+                                pack_signed);
+            uint8_t* op = out_row + c0;
+            if (vec) {
+              *reinterpret_cast<uint4*>(op) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
+            }
+          } else {
           // requantize
           if (hi_rq) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               const int4 ch = s_ch[cc + jj];
               const int32_t x = (int32_t)v[jj] + ch.x;
-              const int32_t t = (__mulhi(x, ch.y) + ch.z) >> ch.w;
-              q[jj] = min(max(t + zp32, qmin32), qmax32);
+              const int32_t t = (__mulhi(x, ch.y) + ch.z) >> ch.w;  // zero point included
+              q[jj] = min(max(t, qmin32), qmax32);
             }
           } else if (fast_rq) {
 #pragma unroll
@@ -637,6 +687,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
                 if (jj < nval) op[jj] = (uint8_t)(o[jj >> 2] >> (8 * (jj & 3)));
             }
           }
+          }  // requantize with table steps
         }
         if (more) {
           ptx::tmem_ld_wait(vn);
