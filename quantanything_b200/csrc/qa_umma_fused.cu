@@ -351,10 +351,11 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     }
   } else if (kTmaA && warp < 4) {
     // ------------------------------------------- activation gather (TMA) --
-    // One thread: per K-block, one im2col load per 16-byte channel slice of
-    // a tap brings that slice for all 128 output pixels of the tile, in
-    // rows of 16 bytes (slice i of the block at byte 2048 * i).
-    if (tid == 0) {
+    // Lanes 0-7 of warp 0: per K-block, one im2col load per 16-byte channel
+    // slice of a tap (lane i: slice i) brings that slice for all 128 output
+    // pixels of the tile, in rows of 16 bytes (slice i of the block at byte
+    // 2048 * i); lane 0 posts the stage's byte count.
+    if (tid < kBK / 16) {
       const int ohw = p.OH * p.OW;
       int g = 0;
       for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
@@ -366,13 +367,12 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           const int s = g % kStages;
           if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
           const int nsl = min(kBK / 16, (p.K - kb * kBK + 15) / 16);
-          ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * 16));
-          const TapEntry* tap = s_tap + kb * (kBK / 16);
-          const uint32_t stage = a_base + s * L::kAStage;
-          for (int i = 0; i < nsl; ++i) {
-            const TapEntry t = tap[i];
-            ptx::tma_load_im2col_4d(stage + i * (kBM * 16), &tmap_a, a_full(s), t.delta, w0, h0,
-                                    img, (uint16_t)t.dx, (uint16_t)t.dy);
+          if (tid == 0) ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * 16));
+          if (tid < nsl) {
+            const TapEntry t = s_tap[kb * (kBK / 16) + tid];
+            ptx::tma_load_im2col_4d(a_base + s * L::kAStage + tid * (kBM * 16), &tmap_a,
+                                    a_full(s), t.delta, w0, h0, img, (uint16_t)t.dx,
+                                    (uint16_t)t.dy);
           }
         }
       }
