@@ -87,6 +87,40 @@ def select_workload(name):
     METRIC, PER_GPU_BATCH = W["metric"], W["batch"]
 
 
+def measure_fused_configs(dev, stream, flush, peak_tops, reps=10):
+    """cfg0 (Linear 256x768x3072) and cfg1 (conv 3x3 [32,64,56,56] -> 128 with
+    the SiLU table) on the fused int8 tensor-core kernel, device-resident:
+    median CUDA-event time of single launches, L2 flushed before each one."""
+    import torch
+
+    from quantanything_b200 import native
+    from quantanything_b200.fused_cases import FusedCase
+
+    res = {}
+    for name, shape in (("cfg0", "Linear [256, 768] x [768, 3072], int8 out"),
+                        ("cfg1", "conv 3x3 [32, 64, 56, 56] * [128, 64, 3, 3] + SiLU table")):
+        case = FusedCase(native.get_library(), name, dev)
+        for _ in range(3):
+            case.launch(stream.cuda_stream)
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            case.launch(stream.cuda_stream)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        t = float(np.median(times)) / 1e3
+        tops = case.ops / t / 1e12
+        res[name] = {"shape": shape, "us": round(t * 1e6, 2), "TOPS": round(tops, 1),
+                     "frac": round(tops / peak_tops, 4), "block_n": int(case.desc.block_n)}
+    res["peak_TOPS"] = peak_tops
+    res["timing"] = f"median of {reps} single launches, L2 flushed before each"
+    return res
+
+
 def config(world, extra=None):
     c = {"workload": W["name"],
          "global_batch": PER_GPU_BATCH * world, "per_gpu_batch": PER_GPU_BATCH,
@@ -367,6 +401,15 @@ def main():
                 "TOPS": round(c[2] / (t / 1e3) / 1e12, 2) if c[2] else 0.0}
                for c, t in zip(costs, step_ms)]
 
+    # all contraction launches of the step against the int8 tensor peak
+    con = [(c, float(t)) for c, t in zip(costs, step_ms) if c[2]]
+    con_ms = sum(t for _, t in con)
+    con_tops = sum(c[2] for c, _ in con) / (con_ms / 1e3) / 1e12
+    contractions = {"launches": len(con), "us": round(con_ms * 1e3, 1),
+                    "achieved": round(con_tops, 1), "peak": int8_peak_tops, "unit": "TOPS",
+                    "frac": round(con_tops / int8_peak_tops, 4)}
+    fused_gemm = measure_fused_configs(dev, stream, flush, int8_peak_tops)
+
     # ---- drop-in ABI route (rank 0, N=1) and CPU baseline
     dropin = cpu = None
     if rank == 0 and world == 1 and not args.no_dropin:
@@ -396,7 +439,8 @@ def main():
                         "d2h_bytes_per_step": int(out_pinned.numel() * 4)},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(),
                 "gpu_launches": int(net.launch_count * args.steps),
-                "launches_per_step": net.launch_count, "kernels": kernels}
+                "launches_per_step": net.launch_count, "contractions": contractions,
+                "fused_gemm": fused_gemm, "kernels": kernels}
         if dropin:
             line["e2e_dropin"] = dropin
         print(json.dumps(line), flush=True)

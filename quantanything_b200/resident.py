@@ -116,6 +116,21 @@ def _check(lib, rc, what):
         raise native.KernelLibraryError(f"{what}: {msg}")
 
 
+def choose_block_n(cout, m_rows, taps_c, sm_count):
+    """Column tile of the fused kernel: the output channels rounded up to a
+    tile width (64 at most when the input is gathered 4 channels at a time);
+    small-M layers take narrower tiles so that at least one tile lands on
+    every SM (each CTA then gathers the same rows; L2 serves the repeats)."""
+    bn = 16 if cout <= 16 else 32 if cout <= 32 else 64 if cout <= 64 else (
+        128 if cout <= 128 else 256)
+    if taps_c % 16 != 0:
+        bn = min(bn, 64)
+    m_tiles = -(-m_rows // 128)
+    while bn > 32 and m_tiles * -(-cout // bn) < sm_count:
+        bn //= 2
+    return bn
+
+
 def _round_up(v, m):
     return (v + m - 1) // m * m
 
@@ -374,16 +389,7 @@ class ResidentNet:
         if w4.min() < -128 or w4.max() > 127:
             raise UnsupportedGraph(f"{layer.name}: centred weights exceed int8")
         ct = taps_c if groups == 1 else cg
-        bn = 16 if cout <= 16 else 32 if cout <= 32 else 64 if cout <= 64 else (
-            128 if cout <= 128 else 256)
-        if groups == 1 and ct % 16 != 0:
-            bn = min(bn, 64)
-        # small-M layers: narrower column tiles so that at least one tile
-        # lands on every SM (each CTA then gathers the same rows; L2 serves
-        # the repeats)
-        m_tiles = -(-m_rows // 128)
-        while bn > 32 and m_tiles * -(-cout // bn) < self.sm_count:
-            bn //= 2
+        bn = choose_block_n(cout, m_rows, ct if groups == 1 else 16, self.sm_count)
         rows = _round_up(cout, bn)
         k = kh * kw * ct
         kp = _round_up(k, 16)
