@@ -191,6 +191,16 @@ typedef struct qa_fused_conv_desc {
   int64_t r_identity;
   int64_t r_zp_in, r_m, r_s, r_zp_out, r_qmin, r_qmax;
   int64_t block_n;        /* column tile: 0 = choose from Cout */
+  /* Border corrections for a nonzero x_zp with out-of-image taps (NULL:
+   * none; such a layer then gathers its input with plain loads): the TMA
+   * gather reads those taps as 0, and pad_corr[cls * Cout + co] =
+   * x_zp * (sum of channel co's weights over the taps outside the image)
+   * restores them; cls = pad_row_class[oy] * pad_col_classes +
+   * pad_col_class[ox], class 0 for interior pixels. */
+  const int32_t* pad_corr;
+  const int32_t* pad_row_class;  /* [OH] */
+  const int32_t* pad_col_class;  /* [OW] */
+  int64_t pad_col_classes, pad_classes;
 } qa_fused_conv_desc;
 
 int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream);

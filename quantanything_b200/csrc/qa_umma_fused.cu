@@ -82,6 +82,12 @@ struct FusedParams {
   int32_t n_valid;
   int32_t m_tiles, n_tiles;
   int32_t vec_ok;  // every output / residual base and stride is 16-byte aligned
+  // border corrections of a nonzero input zero point under the TMA gather
+  // (classes x Cout; NULL when none)
+  const int32_t* pad_corr;
+  const int32_t* pad_row_class;
+  const int32_t* pad_col_class;
+  int32_t pad_ncol, pad_classes;
   int32_t* status;
   FastFlags fast;
   FusedEpilogue epi;
@@ -186,7 +192,8 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
   // byte-domain tables: activation, residual term a (+ zero point), residual
   // term b (signed), concat rescale
   int32_t* s_tab = s_ts + BN;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_tab + 4 * kTab);
+  int32_t* s_corr = s_tab + 4 * kTab;  // [pad_classes][BN] border corrections
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_corr + p.pad_classes * BN);
   // per K-chunk gather offsets, decoded once per CTA (after the barriers)
   TapEntry* s_tap = reinterpret_cast<TapEntry*>(bars + 3 * kStages + 2 * L::kAccs + 2);
   const uint32_t bar0 = ptx::smem_addr(bars);
@@ -274,6 +281,10 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       if (v && !hi) hi_ok = 0;
       s_ch[c] = make_int4((int32_t)s_bias[c], (int32_t)s_mult[c],
                           (int32_t)(((int64_t)1 << (sh - 1)) + (hi ? zfold : 0)), sh);
+    }
+    for (int i = et; i < p.pad_classes * BN; i += nthreads) {
+      const int cls = i / BN, n = n0 + (i - cls * BN);
+      s_corr[i] = n < p.n_valid ? p.pad_corr[(int64_t)cls * p.n_valid + n] : 0;
     }
     // Every value the epilogue carries between steps is an 8-bit one (the
     // host checks the clamp ranges), so each step after the requantize is a
@@ -547,6 +558,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     const int64_t out2_stride = e.out2_pix_stride;
     const int n_valid = p.n_valid;
     const bool vec_ok = p.vec_ok != 0;
+    const bool pad_corr = p.pad_corr != nullptr;
     const int64_t M = p.M;
     int j = 0;
     for (int mt = m_first; mt < p.m_tiles; mt += m_step, ++j) {
@@ -559,6 +571,14 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       ptx::tc_fence_after();
       const int64_t m = (int64_t)mt * kBM + r;
       const bool row_ok = ok && m < M;
+      // border class of this output pixel (nonzero input zero point with
+      // out-of-image taps read as 0 by the TMA gather)
+      const int32_t* corr = nullptr;
+      if (pad_corr && row_ok) {
+        const int ohw = p.OH * p.OW;
+        const int rem = (int)(m % ohw), oy = rem / p.OW, ox = rem - oy * p.OW;
+        corr = s_corr + (p.pad_row_class[oy] * p.pad_ncol + p.pad_col_class[ox]) * BN + cbase;
+      }
       // this row's first output channel in each destination
       const uint8_t* const res_row = res_p + m * res_stride + n0 + cbase;
       uint8_t* const out_row = out_p + m * out_stride + n0 + cbase;
@@ -574,6 +594,10 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
         if (more) ptx::tmem_ld16(lane_base + c0 + 16, vn);
         if (row_ok && n0 + cc < n_valid) {
           const int nval = min(16, n_valid - (n0 + cc));
+          if (corr) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] += (uint32_t)corr[c0 + jj];
+          }
           const bool vec = vec_ok && nval == 16;
           int32_t q[16];
           if (pack_sat) {
@@ -709,11 +733,12 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
 }
 
 template <int BN, int kChunk, bool kResidentB, int kStages>
-size_t smem_bytes(int num_kb) {
+size_t smem_bytes(int num_kb, int pad_classes) {
   using L = Layout<BN, kChunk, kResidentB, kStages>;
   const int b_blocks = kResidentB ? num_kb : kStages;
   return 1024 + (size_t)kStages * L::kAStage + (size_t)b_blocks * L::kBBlock + BN * 16 +
-         4 * BN * 8 + BN * 4 + 4 * kTab * 4 + (3 * kStages + 2 * L::kAccs + 2) * 8 +
+         4 * BN * 8 + BN * 4 + 4 * kTab * 4 + (size_t)pad_classes * BN * 4 +
+         (3 * kStages + 2 * L::kAccs + 2) * 8 +
          (size_t)num_kb * (kBK / (kChunk <= 1 ? 16 : kChunk)) * sizeof(TapEntry);
 }
 
@@ -724,7 +749,7 @@ template <int BN, int kChunk, bool kResidentB>
 bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
                        cudaStream_t st) {
   auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStagesFused>;
-  const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStagesFused>(prm.num_kb);
+  const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStagesFused>(prm.num_kb, prm.pad_classes);
   static size_t attr_bytes[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -748,7 +773,7 @@ bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, const CU
 template <int BN, int kChunk>
 bool launch_bn(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
                cudaStream_t st) {
-  if (smem_bytes<BN, kChunk, true, kStagesFused>(prm.num_kb) <= kSmemCap)
+  if (smem_bytes<BN, kChunk, true, kStagesFused>(prm.num_kb, prm.pad_classes) <= kSmemCap)
     return launch_persistent<BN, kChunk, true>(prm, tmap, tmap_a, st);
   return launch_persistent<BN, kChunk, false>(prm, tmap, tmap_a, st);
 }
@@ -797,7 +822,7 @@ bool make_im2col_tmap(CUtensorMap* map, const qa_fused_conv_desc& d) {
   // out-of-image taps at all)
   const bool no_oob = d.PH == 0 && d.PW == 0 && (d.OH - 1) * d.SH + (d.KH - 1) * d.DH < d.H &&
                       (d.OW - 1) * d.SW + (d.KW - 1) * d.DW < d.W;
-  if ((d.x_zp & 0xFF) != 0 && !no_oob) return false;
+  if ((d.x_zp & 0xFF) != 0 && !no_oob && !d.pad_corr) return false;
   if (d.C % 16 || d.x_pix_stride % 16 || (reinterpret_cast<uintptr_t>(d.x) & 15)) return false;
   if (d.SH > 8 || d.SW > 8 || (d.KH - 1) * d.DH > 64 || (d.KW - 1) * d.DW > 64) return false;
   const int64_t up_w = (d.OW - 1) * d.SW - d.PW - d.W + 1;
@@ -895,6 +920,12 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
                       d.OW == d.W &&
                       make_rows_tmap(&tmap_a, d.x, d.N * d.H * d.W, d.C, d.x_pix_stride, kBM);
   if (!tile_a) clear_error();
+  if (d.pad_corr && !(d.pad_row_class && d.pad_col_class && d.pad_classes >= 1 &&
+                      d.pad_classes <= 16 && d.pad_col_classes >= 1 &&
+                      d.pad_classes % d.pad_col_classes == 0)) {
+    set_error(kBadArgument, "qa_conv_fused_dev: inconsistent border correction tables");
+    return false;
+  }
   const bool tma_a = !tile_a && chunk == 16 && make_im2col_tmap(&tmap_a, d);
 
   FusedParams prm;
@@ -927,6 +958,15 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   auto al16 = [](const void* ptr, int64_t stride) {
     return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && stride % 16 == 0);
   };
+  // the border corrections apply to the TMA gather only (the thread gather
+  // writes the zero point into out-of-image taps itself)
+  if (tma_a && d.pad_corr && (d.x_zp & 0xFF) != 0) {
+    prm.pad_corr = d.pad_corr;
+    prm.pad_row_class = d.pad_row_class;
+    prm.pad_col_class = d.pad_col_class;
+    prm.pad_ncol = (int32_t)d.pad_col_classes;
+    prm.pad_classes = (int32_t)d.pad_classes;
+  }
   prm.vec_ok = al16(d.out, d.out_pix_stride) && al16(d.out2, d.out2_pix_stride) &&
                al16(d.res, d.res_pix_stride);
   prm.status = device_status_word();

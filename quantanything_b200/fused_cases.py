@@ -22,7 +22,7 @@ import ctypes
 import numpy as np
 
 from . import configs
-from .resident import FusedConvDesc, choose_block_n, device_api
+from .resident import FusedConvDesc, choose_block_n, device_api, pad_corrections
 from .utils import dequantize, quantize
 
 
@@ -35,10 +35,10 @@ def silu_table(c):
                     c.qmax).astype(np.int32)
 
 
-def _fast_requant(bias, mult, shift, abssum, xmax):
+def _fast_requant(bias, mult, shift, abssum, xmax, x_zp):
     """Host proof that the kernel's 64-bit requantize is exact (as the
     resident planner does it)."""
-    bound = xmax * abssum + np.abs(bias)
+    bound = xmax * abssum + np.abs(bias) + abs(x_zp) * abssum
     ts = 31 + shift
     return bool(np.all((ts >= 1) & (ts <= 62)) and all(
         int(b) < (1 << 31) and abs(int(m)) < (1 << 31) and abs(int(bi)) < (1 << 31)
@@ -85,7 +85,7 @@ class FusedCase:
         colsum = w.sum(axis=1)
         bias = c.bias.astype(np.int64) - x_zp * colsum
         mult, shift = c.mult.astype(np.int64), c.shift.astype(np.int64)
-        fast = _fast_requant(bias, mult, shift, np.abs(w).sum(axis=1), 128)
+        fast = _fast_requant(bias, mult, shift, np.abs(w).sum(axis=1), 128, x_zp)
 
         def put(a):
             return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
@@ -108,6 +108,12 @@ class FusedCase:
             d.lut, d.lut_offset, d.lut_len = self.lut_dev.data_ptr(), int(c.qmin), len(lut)
         d.out, d.out_pix_stride = self.out_dev.data_ptr(), cout
         d.block_n = bn
+        if name == "cfg1":
+            corr, rcls, ccls, ncol = pad_corrections(w.reshape(cout, 3, 3, C), x_zp, H, W, **geo)
+            self.corr_dev, self.rcls_dev, self.ccls_dev = put(corr), put(rcls), put(ccls)
+            d.pad_corr, d.pad_row_class = self.corr_dev.data_ptr(), self.rcls_dev.data_ptr()
+            d.pad_col_class = self.ccls_dev.data_ptr()
+            d.pad_col_classes, d.pad_classes = ncol, corr.shape[0]
         self.desc = d
         self.ops = 2 * self.M * cout * self.K
         self.bytes = x.nbytes + packed.nbytes + self.M * cout

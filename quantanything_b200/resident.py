@@ -62,6 +62,8 @@ class FusedConvDesc(ctypes.Structure):
         ("r_identity", _I64), ("r_zp_in", _I64), ("r_m", _I64), ("r_s", _I64),
         ("r_zp_out", _I64), ("r_qmin", _I64), ("r_qmax", _I64),
         ("block_n", _I64),
+        ("pad_corr", _P), ("pad_row_class", _P), ("pad_col_class", _P),
+        ("pad_col_classes", _I64), ("pad_classes", _I64),
     ]
 
 
@@ -129,6 +131,40 @@ def choose_block_n(cout, m_rows, taps_c, sm_count):
     while bn > 32 and m_tiles * -(-cout // bn) < sm_count:
         bn //= 2
     return bn
+
+
+def pad_corrections(wt, x_zp, H, W, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, max_classes=9):
+    """Border correction tables of a padded conv whose input zero point is
+    not 0 (the TMA gather reads out-of-image taps as 0 where the reference
+    pads with the zero point): returns (corr [classes, Cout] int32, row class
+    [OH] int32, column class [OW] int32, column classes) or None when no
+    correction is needed or there are more than ``max_classes`` classes.
+    ``wt`` holds the packed weights as [Cout, KH, KW, C] integers."""
+    if x_zp == 0:
+        return None
+    rows = [tuple(ky for ky in range(KH) if not 0 <= oy * SH - PH + ky * DH < H)
+            for oy in range(OH)]
+    cols = [tuple(kx for kx in range(KW) if not 0 <= ox * SW - PW + kx * DW < W)
+            for ox in range(OW)]
+    rpat = sorted(set(rows), key=lambda t: (len(t), t))
+    cpat = sorted(set(cols), key=lambda t: (len(t), t))
+    if rpat == [()] and cpat == [()]:
+        return None
+    if len(rpat) * len(cpat) > max_classes or rpat[0] != () or cpat[0] != ():
+        return None
+    tapsum = np.asarray(wt, np.int64).sum(axis=3)  # [Cout, KH, KW]
+    corr = np.zeros((len(rpat) * len(cpat), tapsum.shape[0]), np.int64)
+    for i, rp in enumerate(rpat):
+        for j, cp in enumerate(cpat):
+            mask = np.zeros((KH, KW), bool)
+            mask[list(rp), :] = True
+            mask[:, list(cp)] = True
+            corr[i * len(cpat) + j] = x_zp * tapsum[:, mask].sum(axis=1)
+    if np.abs(corr).max() >= 1 << 30:
+        return None
+    row_class = np.array([rpat.index(t) for t in rows], np.int32)
+    col_class = np.array([cpat.index(t) for t in cols], np.int32)
+    return corr.astype(np.int32), row_class, col_class, len(cpat)
 
 
 def _round_up(v, m):
@@ -432,7 +468,8 @@ class ResidentNet:
         mult = np.broadcast_to(np.asarray(layer.q_mult, np.int64), (cout,)).copy()
         shift = np.broadcast_to(np.asarray(layer.shift, np.int64), (cout,)).copy()
         xmax = max(abs(layer.in_qmin), abs(layer.in_qmax))
-        bound = xmax * abssum + np.abs(bias)
+        # (|x_zp| * abssum covers the border corrections of the TMA gather)
+        bound = xmax * abssum + np.abs(bias) + abs(int(x_zp)) * abssum
         ts = 31 + shift
         # 64-bit requantize is exact when acc + bias and M0 fit int32 and the
         # rounded product cannot overflow (checked per channel, exact ints)
@@ -454,6 +491,15 @@ class ResidentNet:
         d.bias, d.mult, d.shift = bdev.data_ptr(), mdev.data_ptr(), sdev.data_ptr()
         d.zp, d.qmin, d.qmax, d.fast = layer.out_zp, layer.out_qmin, layer.out_qmax, int(fast)
         d.block_n = bn if groups == 1 else 0
+        if groups == 1 and ct % 16 == 0 and x_zp != 0:
+            wt = packed[:cout, :geo["KH"] * geo["KW"] * ct].reshape(cout, geo["KH"], geo["KW"], ct)
+            pc = pad_corrections(wt, int(x_zp), H, W, **geo)
+            if pc is not None:
+                corr, rcls, ccls, ncol = pc
+                d.pad_corr = self._dev(corr, np.int32).data_ptr()
+                d.pad_row_class = self._dev(rcls, np.int32).data_ptr()
+                d.pad_col_class = self._dev(ccls, np.int32).data_ptr()
+                d.pad_col_classes, d.pad_classes = ncol, corr.shape[0]
         produced = node.outputs[0]
         out_qp = layer.out_qp[0]
         # activation LUT fused when it is the only consumer
