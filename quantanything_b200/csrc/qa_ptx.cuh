@@ -209,8 +209,6 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
                : "memory");
 }
 
-// Shared-memory matrix descriptor for a K-major operand tile stored in the
-// 128-byte swizzled layout (8-row atoms of 1024 bytes).
 // Shared-memory matrix descriptor for a K-major operand without swizzle:
 // 8-row x 16-byte core matrices, `lbo` bytes apart along K and `sbo` bytes
 // apart along M/N.
@@ -224,6 +222,20 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor_plain(uint32_t addr, uint32
   return d;                                       // layout 0: no swizzle
 }
 
+// K-major operand tile in the 64-byte swizzled layout (8-row atoms of 512
+// bytes, rows of 64 bytes).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);       // start address
+  d |= (uint64_t)1 << 16;                      // leading byte offset (unused, 16 B)
+  d |= (uint64_t)(512 >> 4) << 32;             // stride byte offset: 8 rows x 64 B
+  d |= (uint64_t)1 << 46;                      // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;                      // layout: 64-byte swizzle
+  return d;
+}
+
+// K-major operand tile in the 128-byte swizzled layout (8-row atoms of 1024
+// bytes, rows of 128 bytes).
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);       // start address

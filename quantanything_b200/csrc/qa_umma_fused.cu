@@ -78,6 +78,7 @@ struct FusedParams {
   int64_t M;
   int32_t K, num_kb;
   int32_t n_tap;   // chunk positions covered by the tap table (num_kb * 128 / chunk)
+  int32_t slice;   // TMA gather: channel bytes per im2col load (16, 64 or 128)
   int32_t stable;  // every stage always holds the same K-block (kStages % num_kb == 0)
   int32_t n_valid;
   int32_t m_tiles, n_tiles;
@@ -242,8 +243,9 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       for (int i = tid; i < kStages * L::kAStage / 16; i += kProducers) z[i] = make_uint4(0, 0, 0, 0);
       ptx::fence_proxy_async_smem();
     }
+    const int tap_bytes = kTmaA ? p.slice : kTapBytes;
     for (int i = tid; i < p.n_tap; i += kProducers) {
-      const int k = i * kTapBytes;
+      const int k = i * tap_bytes;
       TapEntry t{kTapNone, 0, 0};
       if (k < p.K) {
         const int tap = k / p.Cin, c = k - (k / p.Cin) * p.Cin;
@@ -362,11 +364,14 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     }
   } else if (kTmaA && warp < 4) {
     // ------------------------------------------- activation gather (TMA) --
-    // Lanes 0-7 of warp 0: per K-block, one im2col load per 16-byte channel
-    // slice of a tap (lane i: slice i) brings that slice for all 128 output
-    // pixels of the tile, in rows of 16 bytes (slice i of the block at byte
-    // 2048 * i); lane 0 posts the stage's byte count.
-    if (tid < kBK / 16) {
+    // Lanes of warp 0: per K-block, one im2col load per channel slice of a
+    // tap (lane i: slice i) brings that slice for all 128 output pixels of
+    // the tile: 16-byte slices as rows of 16 bytes (slice i of the block at
+    // byte 2048 * i), 64- and 128-byte slices in the 64- / 128-byte swizzled
+    // layout (slice i at byte 128 * slice * i); lane 0 posts the stage's
+    // byte count.
+    const int sl = p.slice, per_kb = kBK / sl;
+    if (tid < per_kb) {
       const int ohw = p.OH * p.OW;
       int g = 0;
       for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
@@ -377,11 +382,11 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
         for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
           const int s = g % kStages;
           if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
-          const int nsl = min(kBK / 16, (p.K - kb * kBK + 15) / 16);
-          if (tid == 0) ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * 16));
+          const int nsl = min(per_kb, (p.K - kb * kBK + sl - 1) / sl);
+          if (tid == 0) ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * sl));
           if (tid < nsl) {
-            const TapEntry t = s_tap[kb * (kBK / 16) + tid];
-            ptx::tma_load_im2col_4d(a_base + s * L::kAStage + tid * (kBM * 16), &tmap_a,
+            const TapEntry t = s_tap[kb * per_kb + tid];
+            ptx::tma_load_im2col_4d(a_base + s * L::kAStage + tid * (kBM * sl), &tmap_a,
                                     a_full(s), t.delta, w0, h0, img, (uint16_t)t.dx,
                                     (uint16_t)t.dy);
           }
@@ -486,6 +491,21 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     // -------------------------------------------------------- MMA issuer --
     if (lane == 0) {
       const uint32_t idesc = ptx::idesc_i8(kBM, BN, p.a_signed, 1);
+      // A operand layouts: TMA gather with 16-byte slices (2048 bytes apart
+      // along K, 8-row groups 128 bytes apart), 64-byte slices (8 KB apart,
+      // 64-byte swizzle); row TMA / thread gather / 128-byte slices: 128-byte
+      // swizzle.  a_off[kk]: the K-step's offset in 16-byte units.
+      const int slice = kTmaA ? p.slice : 128;
+      const uint64_t a_desc0 = slice == 16   ? ptx::smem_desc_kmajor_plain(a_base, kBM * 16, 128)
+                               : slice == 64 ? ptx::smem_desc_sw64(a_base)
+                                             : ptx::smem_desc_sw128(a_base);
+      uint32_t a_off[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        a_off[kk] = (slice == 16   ? kk * 2 * (kBM * 16)
+                     : slice == 64 ? (kk >> 1) * (kBM * 64) + (kk & 1) * 32
+                                   : kk * 32) >> 4;
+      const uint64_t b_desc0 = ptx::smem_desc_sw128(b_base);
       bool ok = true;
       if (kResidentB) ok = wait(b_full(0), 0);
       int g = 0, j = 0;
@@ -502,16 +522,23 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           if (!kResidentB && !wait(b_full(s), ph)) { ok = false; break; }
           ptx::tc_fence_after();
           const int ksteps = (min(kBK, p.K - kb * kBK) + 31) / 32;
-          const uint32_t a_addr = a_base + s * L::kAStage;
-          const uint32_t b_addr = b_base + (kResidentB ? kb : s) * L::kBBlock;
-          for (int kk = 0; kk < ksteps; ++kk) {
-            // TMA gather: 16-byte slices 2048 bytes apart along K, 8-row
-            // groups 128 bytes apart; row TMA / thread gather: 128-byte swizzle
-            const uint64_t adesc =
-                kTmaA ? ptx::smem_desc_kmajor_plain(a_addr + kk * 2 * (kBM * 16), kBM * 16, 128)
-                      : ptx::smem_desc_sw128(a_addr + kk * 32);
-            ptx::mma_i8(d_tmem, adesc, ptx::smem_desc_sw128(b_addr + kk * 32), idesc,
-                        (kb > 0 || kk > 0) ? 1u : 0u);
+          // descriptors of this stage: the bases plus the stage offset (in
+          // 16-byte units: the start-address field), then the K-steps'
+          // offsets, so that the MMAs leave back to back
+          const uint64_t ad = a_desc0 + (uint64_t)((uint32_t)(s * L::kAStage) >> 4);
+          const uint64_t bd =
+              b_desc0 + (uint64_t)((uint32_t)((kResidentB ? kb : s) * L::kBBlock) >> 4);
+          const uint32_t acc0 = kb > 0 ? 1u : 0u;
+          if (ksteps == 4) {
+            ptx::mma_i8(d_tmem, ad + a_off[0], bd, idesc, acc0);
+            ptx::mma_i8(d_tmem, ad + a_off[1], bd + 2, idesc, 1u);
+            ptx::mma_i8(d_tmem, ad + a_off[2], bd + 4, idesc, 1u);
+            ptx::mma_i8(d_tmem, ad + a_off[3], bd + 6, idesc, 1u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              if (kk < ksteps)
+                ptx::mma_i8(d_tmem, ad + a_off[kk], bd + 2 * kk, idesc, (acc0 | kk) ? 1u : 0u);
           }
           ptx::mma_commit(a_empty(s));
         }
@@ -745,11 +772,14 @@ size_t smem_bytes(int num_kb, int pad_classes) {
 constexpr int kStagesFused = 4;
 constexpr size_t kSmemCap = 227 * 1024;
 
-template <int BN, int kChunk, bool kResidentB>
-bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
-                       cudaStream_t st) {
-  auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStagesFused>;
-  const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStagesFused>(prm.num_kb, prm.pad_classes);
+template <int BN, int kChunk, bool kResidentB, int kStages>
+bool launch_persistent(const FusedParams& prm_in, const CUtensorMap& tmap,
+                       const CUtensorMap& tmap_a, cudaStream_t st) {
+  auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStages>;
+  const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStages>(prm_in.num_kb,
+                                                                   prm_in.pad_classes);
+  FusedParams prm = prm_in;
+  prm.stable = (kStages % prm.num_kb) == 0;
   static size_t attr_bytes[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -766,16 +796,31 @@ bool launch_persistent(const FusedParams& prm, const CUtensorMap& tmap, const CU
   if (per_n > prm.m_tiles) per_n = prm.m_tiles;
   const int64_t grid = per_n * prm.n_tiles;
   return launch_ex(kern, dim3((unsigned)grid),
-                   dim3(Layout<BN, kChunk, kResidentB, kStagesFused>::kThreads), smem, st,
+                   dim3(Layout<BN, kChunk, kResidentB, kStages>::kThreads), smem, st,
                    /*pdl=*/true, prm, tmap, tmap_a);
+}
+
+// TMA-fed layers keep up to eight activation stages in flight when shared
+// memory allows: a stage's load latency is then covered by the MMAs of the
+// stages ahead of it.
+template <int BN, int kChunk, bool kResidentB>
+bool launch_staged(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
+                   cudaStream_t st) {
+  if constexpr (kChunk <= 1) {
+    if (smem_bytes<BN, kChunk, kResidentB, 8>(prm.num_kb, prm.pad_classes) <= kSmemCap)
+      return launch_persistent<BN, kChunk, kResidentB, 8>(prm, tmap, tmap_a, st);
+    if (smem_bytes<BN, kChunk, kResidentB, 6>(prm.num_kb, prm.pad_classes) <= kSmemCap)
+      return launch_persistent<BN, kChunk, kResidentB, 6>(prm, tmap, tmap_a, st);
+  }
+  return launch_persistent<BN, kChunk, kResidentB, kStagesFused>(prm, tmap, tmap_a, st);
 }
 
 template <int BN, int kChunk>
 bool launch_bn(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
                cudaStream_t st) {
   if (smem_bytes<BN, kChunk, true, kStagesFused>(prm.num_kb, prm.pad_classes) <= kSmemCap)
-    return launch_persistent<BN, kChunk, true>(prm, tmap, tmap_a, st);
-  return launch_persistent<BN, kChunk, false>(prm, tmap, tmap_a, st);
+    return launch_staged<BN, kChunk, true>(prm, tmap, tmap_a, st);
+  return launch_staged<BN, kChunk, false>(prm, tmap, tmap_a, st);
 }
 
 using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -814,7 +859,13 @@ bool tma_gather_enabled() {
 // every tile's first pixel is a start inside it; the traversal strides are
 // the convolution strides and the taps are the load's offsets.  Returns
 // false (no error recorded) for layers the map cannot describe.
-bool make_im2col_tmap(CUtensorMap* map, const qa_fused_conv_desc& d) {
+// Channel bytes per im2col load: whole 128- or 64-byte runs of a pixel's
+// channels when C allows (one load moves 4-8x the bytes of a 16-byte one).
+int im2col_slice(const qa_fused_conv_desc& d) {
+  return d.C % 128 == 0 ? 128 : d.C % 64 == 0 ? 64 : 16;
+}
+
+bool make_im2col_tmap(CUtensorMap* map, const qa_fused_conv_desc& d, int slice) {
   if (!tma_gather_enabled()) return false;
   EncodeIm2colFn fn = im2col_encoder();
   if (!fn) return false;
@@ -839,7 +890,10 @@ bool make_im2col_tmap(CUtensorMap* map, const qa_fused_conv_desc& d) {
   const int upper[2] = {(int)up_w, (int)up_h};
   cuuint32_t estr[4] = {1u, (cuuint32_t)d.SW, (cuuint32_t)d.SH, 1u};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(d.x), dims, strides, lower,
-            upper, 16, kBM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            upper, (cuuint32_t)slice, kBM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            slice == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+            : slice == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -926,7 +980,8 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
     set_error(kBadArgument, "qa_conv_fused_dev: inconsistent border correction tables");
     return false;
   }
-  const bool tma_a = !tile_a && chunk == 16 && make_im2col_tmap(&tmap_a, d);
+  const int slice = im2col_slice(d);
+  const bool tma_a = !tile_a && chunk == 16 && make_im2col_tmap(&tmap_a, d, slice);
 
   FusedParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -950,8 +1005,8 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
   prm.M = M;
   prm.K = (int32_t)K;
   prm.num_kb = (int32_t)((K + kBK - 1) / kBK);
-  prm.n_tap = prm.num_kb * (kBK / chunk);  // chunk 16 for the TMA gather too
-  prm.stable = (kStagesFused % prm.num_kb) == 0;
+  prm.slice = tma_a ? slice : 16;
+  prm.n_tap = prm.num_kb * (kBK / (tma_a ? slice : chunk));
   prm.n_valid = (int32_t)d.Cout;
   prm.m_tiles = (int32_t)m_tiles;
   prm.n_tiles = (int32_t)n_tiles;
