@@ -265,6 +265,9 @@ def main():
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="run this many plain forward passes of the workload and exit "
                          "(the command the ncu summaries under profiles/ are taken with)")
+    ap.add_argument("--profile-fused", choices=["cfg0", "cfg1"], default=None,
+                    help="launch the fused int8 kernel on this kernel-level configuration "
+                         "three times and exit (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch of a --profile-forwards run (the bench line itself "
                          "always uses the workload's configured batch)")
@@ -280,6 +283,18 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.profile_fused:
+        import torch
+
+        from quantanything_b200 import native
+        from quantanything_b200.fused_cases import FusedCase
+
+        case = FusedCase(native.get_library(), args.profile_fused, torch.device("cuda", local))
+        for _ in range(3):
+            case.launch(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_fused": args.profile_fused, "launches": 3}))
         return
     args.warmup = max(args.warmup, 3)
 
