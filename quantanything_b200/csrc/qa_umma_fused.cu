@@ -2,20 +2,23 @@
 //
 // One CTA per SM walks a strided list of 128-row output tiles of one
 // column tile (all CTAs of a column tile share its weights).  Roles:
-//   warps 0-3  activation gather: one tile row per thread, cp.async straight
-//              into the 128-byte swizzled K-major layout; a ring of kStages
-//              16 KB stages that runs ahead across tile boundaries;
+//   warps 0-3  thread gather (4- or 16-byte taps): one tile row per thread,
+//              cp.async straight into the 128-byte swizzled K-major layout;
+//              a ring of kStages 16 KB stages that runs ahead across tile
+//              boundaries.  Layers fed by TMA use them as a third epilogue
+//              warpgroup instead (BN >= 64);
 //   warp 4     TMEM allocation; lane 0 issues tcgen05.mma (M=128, N=BN,
-//              K=32) into one of two TMEM accumulators and commits;
-//   warp 5     lane 0 loads the weights by TMA: once for the whole kernel
-//              when they fit in shared memory (kResidentB), else one K-block
-//              per stage alongside the activations;
-//   warps 6-9  epilogue: drain the finished accumulator (the MMA meanwhile
-//              fills the other one), apply the layer's integer sequence and
+//              K=32) into one of the TMEM accumulators and commits;
+//   warp 5     TMA loads: the weights once for the whole kernel when they
+//              fit in shared memory (kResidentB), else one K-block per
+//              stage; for TMA-fed layers also the activations (row tiles or
+//              im2col slices, lanes 0-7 in one instruction);
+//   warps 6-13 epilogue: drain the finished accumulator (the MMA meanwhile
+//              fills the next one), apply the layer's integer sequence and
 //              store 16-byte vectors of NHWC output.
-// The K padding of every stage is zeroed once and never gathered again.
-// Every mbarrier wait is bounded (1 s); a timeout sets the device status
-// word, the CTA skips the remaining work, frees TMEM and exits.
+// The K padding of every thread-gathered stage is zeroed once and never
+// gathered again.  Every mbarrier wait is bounded (~2 s); a timeout sets the
+// device status word, the CTA skips the remaining work, frees TMEM and exits.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -138,11 +141,13 @@ struct Layout {
   // tile (group g its half of the columns); with 16 columns they alternate
   // tiles.  Accumulators: four when they fit in TMEM (BN <= 128), else two
   // (still double buffered).
-  static constexpr int kGroups = 2;
+  // Layers fed by TMA (kChunk <= 1) leave warps 0-3 free: with BN >= 64
+  // they form a third group, so three groups split every tile's columns.
+  static constexpr bool kTmaFed = kChunk <= 1;
+  static constexpr int kGroups = (kTmaFed && BN >= 64) ? 3 : 2;
   static constexpr bool kSplit = BN >= 32;
-  static constexpr int kGroupCols = kSplit ? BN / 2 : BN;
   static constexpr int kAccs = BN <= 128 ? 4 : 2;
-  static constexpr int kThreads = 192 + kGroups * kEpilogueThreads;
+  static constexpr int kThreads = 192 + 2 * kEpilogueThreads;
   static constexpr int kCols = kAccs * BN;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                  : kCols <= 256 ? 256 : 512;
@@ -222,7 +227,8 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     }
     for (int b = 0; b < L::kAccs; ++b) {
       ptx::mbar_init(acc_full0 + 8u * b, 1);
-      ptx::mbar_init(acc_empty0 + 8u * b, L::kSplit ? 2 * kEpilogueThreads : kEpilogueThreads);
+      ptx::mbar_init(acc_empty0 + 8u * b,
+                     L::kSplit ? L::kGroups * kEpilogueThreads : kEpilogueThreads);
     }
     *s_abort = 0;
     ptx::fence_mbar_init();
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     }
   } else if (warp >= kEpilogueWarp0) {
     const FusedEpilogue& e = p.epi;
-    const int et = tid - kEpilogueWarp0 * 32, nthreads = L::kGroups * kEpilogueThreads;
+    const int et = tid - kEpilogueWarp0 * 32, nthreads = 2 * kEpilogueThreads;
     for (int c = et; c < BN; c += nthreads) {
       const int n = n0 + c;
       const bool v = n < p.n_valid;
@@ -343,61 +349,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     return false;
   };
 
-  if (kTileA && warp < 4) {
-    // ------------------------------------------ activation rows (TMA) --
-    // One thread: per K-block, one 2-D load of 128 rows x 128 bytes in the
-    // 128-byte swizzle (bytes past C and rows past M read as zero).
-    if (tid == 0) {
-      int g = 0;
-      for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
-        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
-          const int s = g % kStages;
-          if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
-          ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)L::kAStage);
-          ptx::tma_load_2d(a_base + s * L::kAStage, &tmap_a, a_full(s), kb * kBK, mt * kBM);
-        }
-      }
-      // after an abort, wait (bounded) for the loads still in flight
-      if (*s_abort)
-        for (int gg = max(0, g - kStages); gg < g; ++gg)
-          ptx::mbar_wait(a_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
-    }
-  } else if (kTmaA && warp < 4) {
-    // ------------------------------------------- activation gather (TMA) --
-    // Lanes of warp 0: per K-block, one im2col load per channel slice of a
-    // tap (lane i: slice i) brings that slice for all 128 output pixels of
-    // the tile: 16-byte slices as rows of 16 bytes (slice i of the block at
-    // byte 2048 * i), 64- and 128-byte slices in the 64- / 128-byte swizzled
-    // layout (slice i at byte 128 * slice * i); lane 0 posts the stage's
-    // byte count.
-    const int sl = p.slice, per_kb = kBK / sl;
-    if (tid < per_kb) {
-      const int ohw = p.OH * p.OW;
-      int g = 0;
-      for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
-        const int m0 = mt * kBM;
-        const int img = m0 / ohw, rem = m0 - img * ohw;
-        const int oy = rem / p.OW, ox = rem - oy * p.OW;
-        const int w0 = ox * p.SW - p.PW, h0 = oy * p.SH - p.PH;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
-          const int s = g % kStages;
-          if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
-          const int nsl = min(per_kb, (p.K - kb * kBK + sl - 1) / sl);
-          if (tid == 0) ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * sl));
-          if (tid < nsl) {
-            const TapEntry t = s_tap[kb * per_kb + tid];
-            ptx::tma_load_im2col_4d(a_base + s * L::kAStage + tid * (kBM * sl), &tmap_a,
-                                    a_full(s), t.delta, w0, h0, img, (uint16_t)t.dx,
-                                    (uint16_t)t.dy);
-          }
-        }
-      }
-      // after an abort, wait (bounded) for the loads still in flight
-      if (*s_abort)
-        for (int gg = max(0, g - kStages); gg < g; ++gg)
-          ptx::mbar_wait(a_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
-    }
-  } else if (warp < 4) {
+  if (!L::kTmaFed && warp < 4) {
     // --------------------------------------------------- activation gather --
     // Thread r owns tile row r: one output pixel whose receptive field it
     // gathers K-chunk by K-chunk using the decoded tap table (32-bit math).
@@ -465,6 +417,59 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       }
     }
     ptx::cp_async_wait_all();
+  } else if (warp == 5 && L::kTmaFed) {
+    // ------------------------------------------ activation + weight loads --
+    // Lanes 0-7, converged: per K-block, lane 0 posts the stage's byte
+    // counts and loads the weights' K-block (when they are not resident);
+    // the activations come as one 2-D load of 128 rows x 128 bytes in the
+    // 128-byte swizzle (row TMA: bytes past C and rows past M read 0), or
+    // as one im2col load per channel slice of a tap (lane i: slice i) that
+    // brings the slice for all 128 output pixels of the tile: 16-byte slices
+    // as rows of 16 bytes (slice i at byte 2048 * i), 64- and 128-byte
+    // slices in the 64- / 128-byte swizzle (slice i at byte 128 * slice * i).
+    const int sl = kTileA ? kBK : p.slice, per_kb = kBK / sl;
+    if (lane < per_kb) {
+      const int ohw = p.OH * p.OW;
+      int g = 0;
+      for (int mt = m_first; mt < p.m_tiles && !*s_abort; mt += m_step) {
+        const int m0 = mt * kBM;
+        const int img = m0 / ohw, rem = m0 - img * ohw;
+        const int oy = rem / p.OW, ox = rem - oy * p.OW;
+        const int w0 = ox * p.SW - p.PW, h0 = oy * p.SH - p.PH;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages && !wait(a_empty(s), ((g / kStages) - 1) & 1)) break;
+          if (!kResidentB && lane == 0) {
+            ptx::mbar_arrive_expect_tx(b_full(s), (uint32_t)L::kBBlock);
+            ptx::tma_load_2d(b_base + s * L::kBBlock, &tmap_b, b_full(s), kb * kBK, n0);
+          }
+          if (kTileA) {
+            if (lane == 0) {
+              ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)L::kAStage);
+              ptx::tma_load_2d(a_base + s * L::kAStage, &tmap_a, a_full(s), kb * kBK, m0);
+            }
+          } else {
+            const int nsl = min(per_kb, (p.K - kb * kBK + sl - 1) / sl);
+            if (lane == 0) ptx::mbar_arrive_expect_tx(a_full(s), (uint32_t)(nsl * kBM * sl));
+            if (lane < nsl) {
+              const TapEntry t = s_tap[kb * per_kb + lane];
+              ptx::tma_load_im2col_4d(a_base + s * L::kAStage + lane * (kBM * sl), &tmap_a,
+                                      a_full(s), t.delta, w0, h0, img, (uint16_t)t.dx,
+                                      (uint16_t)t.dy);
+            }
+          }
+        }
+      }
+      // after an abort, wait (bounded) for the loads still in flight
+      if (*s_abort && lane == 0) {
+        for (int gg = max(0, g - kStages); gg < g; ++gg) {
+          ptx::mbar_wait(a_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
+          if (!kResidentB)
+            ptx::mbar_wait(b_full(gg % kStages), (gg / kStages) & 1, kBudgetCycles);
+        }
+        if (kResidentB) ptx::mbar_wait(b_full(0), 0, kBudgetCycles);
+      }
+    }
   } else if (warp == 5) {
     // ------------------------------------------------------ weight loads --
     if (lane == 0) {
@@ -546,16 +551,19 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
         ptx::mma_commit(acc_full0 + 8u * ab);
       }
     }
-  } else {
+  } else if (warp >= kEpilogueWarp0 || (L::kGroups == 3 && warp < 4)) {
     // ---------------------------------------------------------- epilogue --
-    // With kSplit, warpgroup `grp` drains columns [grp * kGroupCols, +
-    // kGroupCols) of every tile; otherwise the tiles j with j % kGroups == grp.
+    // With kSplit, warpgroup `grp` drains its share of every tile's
+    // 16-column chunks; otherwise the tiles j with j % kGroups == grp.
     // Each thread owns one tile row;
     // per 16-column chunk the layer-uniform branches are hoisted out of the
     // unrolled element loops, and the next chunk's TMEM load is in flight
     // while this one is processed.
     const FusedEpilogue& e = p.epi;
-    const int grp = (warp - kEpilogueWarp0) / 4;
+    const int grp = warp < 4 ? 2 : (warp - kEpilogueWarp0) / 4;
+    // this group's share of the tile's 16-column chunks (kSplit)
+    const int g_lo = grp * (BN / 16) / L::kGroups, g_hi = (grp + 1) * (BN / 16) / L::kGroups;
+    const int gcols = L::kSplit ? (g_hi - g_lo) * 16 : BN;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter.. belong to this warp
     const int r = quarter * 32 + lane;
     const bool fast_rq = p.fast.requant;
@@ -590,7 +598,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     int j = 0;
     for (int mt = m_first; mt < p.m_tiles; mt += m_step, ++j) {
       if (!L::kSplit && j % L::kGroups != grp) continue;
-      const int cbase = L::kSplit ? grp * L::kGroupCols : 0;
+      const int cbase = L::kSplit ? g_lo * 16 : 0;
       const int ab = j % L::kAccs;
       const int use = j / L::kAccs;
       const bool ok = wait(acc_full0 + 8u * ab, use & 1);
@@ -615,9 +623,9 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       ptx::tmem_ld16(lane_base, v);
       ptx::tmem_ld_wait(v);
 #pragma unroll 1
-      for (int c0 = 0; c0 < L::kGroupCols; c0 += 16) {
+      for (int c0 = 0; c0 < gcols; c0 += 16) {
         const int cc = cbase + c0;  // tile column of this chunk
-        const bool more = c0 + 16 < L::kGroupCols;
+        const bool more = c0 + 16 < gcols;
         if (more) ptx::tmem_ld16(lane_base + c0 + 16, vn);
         if (row_ok && n0 + cc < n_valid) {
           const int nval = min(16, n_valid - (n0 + cc));
