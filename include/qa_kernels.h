@@ -212,6 +212,14 @@ int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C, int64
                             int64_t pix_stride, double scale, int64_t zp, int64_t qmin,
                             int64_t qmax, void* stream);
 
+/* The same quantization written as the im2col rows of a P x P, stride-P
+ * convolution (a patch embedding): row (n * H/P + py) * W/P + px holds the
+ * patch's P * P pixels, (ky * P + kx) * 4 bytes in, 4 channel bytes each
+ * (channels C.. hold zp).  C <= 4, P % 4 == 0, H and W multiples of P. */
+int qa_quantize_to_patch_rows_dev(const float* x, void* y, int64_t N, int64_t C, int64_t H,
+                                  int64_t W, int64_t P, double scale, int64_t zp, int64_t qmin,
+                                  int64_t qmax, void* stream);
+
 /* GlobalAveragePool (quant_layers.py:563-590): int64 sum of centred bytes
  * over HW pixels, requantized with the scalar (mult, shift). */
 int qa_gap_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int64_t N, int64_t HW,

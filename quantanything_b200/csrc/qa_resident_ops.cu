@@ -184,8 +184,12 @@ __global__ void quantize_to_nhwc_kernel(const float* __restrict__ x, uint8_t* __
 // Four consecutive pixels per thread for the common 3-channel image stored
 // with a 4-byte pixel stride: one 16-byte load per channel plane, one
 // 16-byte store of four packed pixels.
+// Output layout: NHWC with 4 bytes per pixel (P == 0), or patch rows
+// (P > 0): the P x P pixels of patch (py, px) of image n form row
+// (n * H / P + py) * W / P + px of P * P * 4 bytes, pixel (ky, kx) at
+// (ky * P + kx) * 4 -- the im2col rows of a P x P, stride-P convolution.
 __global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
-                                         int C, int quads_per_image, int quads,
+                                         int C, int quads_per_image, int quads, int W, int P,
                                          const QuantK k) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
@@ -238,7 +242,15 @@ __global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* _
         for (int b = 0; b < 4; ++b)
           px[b] = quantize_word_exact(src + b, (int64_t)quads_per_image * 4, C, pad, k);
       }
-      *reinterpret_cast<uint4*>(y + (int64_t)qi[u] * 16) = make_uint4(px[0], px[1], px[2], px[3]);
+      int64_t off = (int64_t)qi[u] * 16;
+      if (P > 0) {
+        const int n = qi[u] / quads_per_image, p0 = (qi[u] - n * quads_per_image) * 4;
+        const int yy = p0 / W, xx = p0 - yy * W;
+        const int pr = W / P, pc = quads_per_image * 4 / W / P;  // patches per row / column
+        const int64_t row = ((int64_t)n * pc + yy / P) * pr + xx / P;
+        off = row * (P * P * 4) + ((yy % P) * P + xx % P) * 4;
+      }
+      *reinterpret_cast<uint4*>(y + off) = make_uint4(px[0], px[1], px[2], px[3]);
     }
   }
 }
@@ -464,13 +476,33 @@ QA_API int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C
     const int64_t quads = N * HW / 4;
     return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256, 2)), dim3(256), 0,
                      (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
-                     (int)(HW / 4), (int)quads, make_quant_k(scale, zp, qmin, qmax))
+                     (int)(HW / 4), (int)quads, (int)W, 0, make_quant_k(scale, zp, qmin, qmax))
                ? 0
                : last_status();
   }
   return launch_ex(quantize_to_nhwc_kernel, dim3(grid_for(n, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), N, C, HW,
                    pix_stride, scale, (double)zp, (double)qmin, (double)qmax)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_quantize_to_patch_rows_dev(const float* x, void* y, int64_t N, int64_t C, int64_t H,
+                                         int64_t W, int64_t P, double scale, int64_t zp,
+                                         int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (N < 0 || C <= 0 || C > 4 || P <= 0 || P % 4 || H % P || W % P || W % 4 || scale == 0.0 ||
+      N * H * W / 4 >= 0x7FFFFFFF || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(y) & 15)) {
+    set_error(kBadArgument, "qa_quantize_to_patch_rows_dev: bad arguments");
+    return last_status();
+  }
+  const int64_t quads = N * H * W / 4;
+  if (quads == 0) return 0;
+  return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256, 2)), dim3(256), 0,
+                   (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
+                   (int)(H * W / 4), (int)quads, (int)W, (int)P,
+                   make_quant_k(scale, zp, qmin, qmax))
              ? 0
              : last_status();
 }

@@ -69,6 +69,8 @@ class FusedConvDesc(ctypes.Structure):
 
 _DEV_SIGNATURES = {
     "qa_conv_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P]),
+    "qa_quantize_to_patch_rows_dev": (ctypes.c_int, [_P, _P] + [_I64] * 5 + [ctypes.c_double]
+                                      + [_I64] * 3 + [_P]),
     "qa_quantize_to_nhwc_dev": (ctypes.c_int, [_P, _P] + [_I64] * 5 + [ctypes.c_double]
                                 + [_I64] * 3 + [_P]),
     "qa_gap_dev": (ctypes.c_int, [_P] + [_I64] * 11 + [_P, _I64, _P]),
@@ -225,6 +227,7 @@ class ResidentNet:
         if self.bits > 8:
             raise UnsupportedGraph("the resident executor runs 8-bit graphs")
         self.fuse_input = fuse_input
+        self._in_patch = 0  # > 0: the input quantizer writes patch rows (patch embedding)
         self._keep = []
         self.steps = []
         self.launch_count = 0
@@ -437,11 +440,33 @@ class ResidentNet:
         abssum = np.abs(wt.reshape(cout, k)).sum(axis=1)
         return packed, rows, kp, bn, groups, ct, colsum, abssum
 
-    def _plan_contraction(self, layer, layers, fused_away):
+    def _plan_contraction(self, layer, layers, fused_away, patch=0):
+        """``patch`` > 0: the input view holds the im2col rows of this
+        patch x patch, stride-patch conv (written by the input quantizer), so
+        the layer runs as a pointwise GEMM over those rows with the conv's own
+        packed weights (K = patch * patch * 4)."""
         node = layer.node
         x_view = self._views[node.inputs[0]]
         N, _, H, W = self._shapes[node.inputs[0]]
-        if isinstance(layer, GemmQuantize):
+        if patch:
+            cin = int(layer.w_q.shape[1])
+            strides, pads, dil, groups = layer.geometry((N, cin, H, W))
+            g_ = native.conv_geometry((N, cin, H, W), layer.w_q.shape, strides, pads, dil, groups)
+            m_rows = N * g_[13] * g_[14]
+            packed, rows, kp, bn, groups, ct, colsum, abssum = self._pack_weights(layer, x_view,
+                                                                                  4, m_rows)
+            geo = dict(KH=1, KW=1, SH=1, SW=1, PH=0, PW=0, DH=1, DW=1, OH=g_[13], OW=g_[14])
+            H, W, ct_desc = g_[13], g_[14], g_[5] * g_[6] * 4
+            pads_bottom = (0, 0)
+            # column tile of a 16-byte-aligned row matrix (the packing above
+            # chose one for 4-byte taps)
+            cout_ = int(layer.w_q.shape[0])
+            bn = choose_block_n(cout_, m_rows, 16, self.sm_count)
+            rows = _round_up(cout_, bn)
+            if rows != packed.shape[0]:
+                packed = np.concatenate(
+                    [packed[:cout_], np.zeros((rows - cout_, packed.shape[1]), np.int8)])
+        elif isinstance(layer, GemmQuantize):
             if (x_view.H, x_view.W) != (1, 1):
                 raise UnsupportedGraph("Gemm input must be a flattened vector")
             geo = dict(KH=1, KW=1, SH=1, SW=1, PH=0, PW=0, DH=1, DW=1, OH=1, OW=1)
@@ -453,14 +478,16 @@ class ResidentNet:
             geo = dict(KH=g_[5], KW=g_[6], SH=g_[7], SW=g_[8], PH=g_[9], PW=g_[10], DH=g_[11],
                        DW=g_[12], OH=g_[13], OW=g_[14])
             pads_bottom = (pads[2], pads[3])
-        taps_c = x_view.C
-        if taps_c % 16 != 0:
-            taps_c = _round_up(taps_c, 4)
-            if taps_c > x_view.pix_stride and x_view.offset + taps_c > x_view.pix_stride:
-                raise UnsupportedGraph(f"{layer.name}: input channels not 4-aligned")
-        m_rows = N * geo["OH"] * geo["OW"]
-        packed, rows, kp, bn, groups, ct, colsum, abssum = self._pack_weights(layer, x_view,
-                                                                              taps_c, m_rows)
+        if not patch:
+            taps_c = x_view.C
+            if taps_c % 16 != 0:
+                taps_c = _round_up(taps_c, 4)
+                if taps_c > x_view.pix_stride and x_view.offset + taps_c > x_view.pix_stride:
+                    raise UnsupportedGraph(f"{layer.name}: input channels not 4-aligned")
+            m_rows = N * geo["OH"] * geo["OW"]
+            packed, rows, kp, bn, groups, ct, colsum, abssum = self._pack_weights(
+                layer, x_view, taps_c, m_rows)
+            ct_desc = ct
         cout = layer.w_q.shape[1] if isinstance(layer, GemmQuantize) else layer.w_q.shape[0]
         x_zp = layer.in_zp
         bias = (layer.bias_int.astype(np.int64) if layer.bias_int is not None
@@ -480,7 +507,7 @@ class ResidentNet:
         d = FusedConvDesc()
         d.x, d.x_pix_stride, d.x_signed, d.x_zp = x_view.ptr, x_view.pix_stride, int(
             x_view.signed), int(x_zp)
-        d.N, d.H, d.W, d.C = N, H, W, ct
+        d.N, d.H, d.W, d.C = N, H, W, ct_desc
         for k_, v in geo.items():
             setattr(d, k_, int(v))
         d.Cout, d.groups = cout, groups
@@ -491,7 +518,7 @@ class ResidentNet:
         d.bias, d.mult, d.shift = bdev.data_ptr(), mdev.data_ptr(), sdev.data_ptr()
         d.zp, d.qmin, d.qmax, d.fast = layer.out_zp, layer.out_qmin, layer.out_qmax, int(fast)
         d.block_n = bn if groups == 1 else 0
-        if groups == 1 and ct % 16 == 0 and x_zp != 0:
+        if groups == 1 and ct % 16 == 0 and x_zp != 0 and not patch:
             wt = packed[:cout, :geo["KH"] * geo["KW"] * ct].reshape(cout, geo["KH"], geo["KW"], ct)
             pc = pad_corrections(wt, int(x_zp), H, W, **geo)
             if pc is not None:
@@ -672,7 +699,7 @@ class ResidentNet:
                 N, C, H, W = self.in_shape
                 v = self._in_view
                 costs.append((f"quantize {N}x{C}x{H}x{W}", N * C * H * W * 4 +
-                              N * H * W * v.pix_stride, 0))
+                              N * H * W * (4 if self._in_patch else v.pix_stride), 0))
             elif kind in ("conv", "conv_input"):
                 d = payload.desc
                 M = d.N * d.OH * d.OW
@@ -729,9 +756,14 @@ class ResidentNet:
             if kind == "quantize":
                 v, qp = self._in_view, self.c.qparams[payload]
                 N, C, H, W = self.in_shape
-                rc = raw.qa_quantize_to_nhwc_dev(self.x_dev.data_ptr(), v.ptr, N, C, H, W,
-                                                 v.pix_stride, float(qp.scale), qp.zp, qp.qmin,
-                                                 qp.qmax, st)
+                if self._in_patch:
+                    rc = raw.qa_quantize_to_patch_rows_dev(
+                        self.x_dev.data_ptr(), v.ptr, N, C, H, W, self._in_patch,
+                        float(qp.scale), qp.zp, qp.qmin, qp.qmax, st)
+                else:
+                    rc = raw.qa_quantize_to_nhwc_dev(self.x_dev.data_ptr(), v.ptr, N, C, H, W,
+                                                     v.pix_stride, float(qp.scale), qp.zp,
+                                                     qp.qmin, qp.qmax, st)
             elif kind == "conv":
                 rc = raw.qa_conv_fused_dev(ctypes.byref(payload.desc), st)
             elif kind == "conv_input":

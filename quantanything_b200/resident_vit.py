@@ -83,7 +83,17 @@ class ResidentViT(ResidentNet):
             if isinstance(layer, ConvQuantize):
                 if node.inputs[0] != in_name:
                     raise UnsupportedGraph("only the patch embedding may be a Conv")
-                self._plan_contraction(layer, layers, fused_away)
+                P = self._patch_rows(layer)
+                if P:
+                    # the input quantizer writes the conv's im2col rows; the
+                    # conv runs as a row-matrix GEMM over them
+                    v = self._in_view
+                    N, _, H, W = self.in_shape
+                    K = P * P * 4
+                    pv = View(v.buf, 0, K, N, H // P, W // P, K, v.signed, v.qp)
+                    self._views[in_name] = self._in_view = pv
+                    self._in_patch = P
+                self._plan_contraction(layer, layers, fused_away, patch=P)
             elif op in ("Reshape", "Transpose") and node.outputs[0] not in attention["all"]:
                 self._plan_token_alias(node)
             elif isinstance(layer, ConcatQuantize):
@@ -114,6 +124,18 @@ class ResidentViT(ResidentNet):
         self.out_f32 = torch.empty((N, C), dtype=torch.float32, device=self.device)
         self._outputs_f32 = {out: self.out_f32}
         self.steps.append(("dequant", (y, c.qparams[out])))
+
+    def _patch_rows(self, layer):
+        """Patch size P when the patch embedding is a P x P, stride-P conv
+        without padding or dilation that the input quantizer can write as
+        im2col rows (qa_quantize_to_patch_rows_dev), else 0."""
+        N, C, H, W = self.in_shape
+        kh, kw = (int(v) for v in layer.w_q.shape[2:])
+        strides, pads, dil, groups = layer.geometry((N, C, H, W))
+        if (kh != kw or tuple(strides) != (kh, kw) or any(pads) or tuple(dil) != (1, 1)
+                or groups != 1 or C > 4 or kh % 4 or H % kh or W % kw or W % 4):
+            return 0
+        return kh
 
     def _last_produced(self):
         step = self.steps[-1][1]
@@ -352,3 +374,4 @@ class _Only:
         self.steps = [(kind, payload)]
         self.in_shape = net.in_shape
         self._in_view = net._in_view
+        self._in_patch = net._in_patch
