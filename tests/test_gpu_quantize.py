@@ -62,3 +62,28 @@ def test_quantize_to_nhwc_matches_reference(gpu_lib, oracle, scale, zp, qmin, qm
     want_b = (want.reshape(C, H * W).T.astype(np.int64) & 0xFF).astype(np.uint8)
     np.testing.assert_array_equal(got[:, :C], want_b)
     assert (got[:, C] == (zp & 0xFF)).all()
+
+
+@pytest.mark.parametrize("P,H,W", [(16, 32, 48), (8, 16, 8), (4, 12, 20)])
+def test_patch_rows_are_the_nhwc_bytes_in_im2col_order(gpu_lib, oracle, P, H, W):
+    """qa_quantize_to_patch_rows_dev: the same bytes as the NHWC quantizer
+    (pinned to the reference above), rearranged into the im2col rows of a
+    P x P, stride-P conv: row (n, py, px), pixel (ky, kx) at (ky * P + kx) * 4."""
+    rng = np.random.default_rng(P)
+    N, C, scale, zp = 2, 3, 0.02, 7
+    x = (rng.standard_normal((N, C, H, W)) * 2).astype(np.float32)
+    raw = device_api(gpu_lib)
+    xd = torch.from_numpy(x).cuda()
+    nhwc = torch.empty(N * H * W * 4, dtype=torch.uint8, device="cuda")
+    rows = torch.empty_like(nhwc)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert raw.qa_quantize_to_nhwc_dev(xd.data_ptr(), nhwc.data_ptr(), N, C, H, W, 4, scale, zp,
+                                       -128, 127, st) == 0
+    assert raw.qa_quantize_to_patch_rows_dev(xd.data_ptr(), rows.data_ptr(), N, C, H, W, P,
+                                             scale, zp, -128, 127, st) == 0
+    torch.cuda.synchronize()
+    a = nhwc.cpu().numpy().reshape(N, H // P, P, W // P, P, 4).transpose(0, 1, 3, 2, 4, 5)
+    np.testing.assert_array_equal(rows.cpu().numpy().reshape(a.shape), a)
+    want = oracle.quantize_f32(x, scale, zp, -128, 127)
+    assert (nhwc.cpu().numpy().reshape(N, H, W, 4)[..., :C].view(np.int8)
+            == want.transpose(0, 2, 3, 1)).all()
