@@ -631,7 +631,12 @@ QA_API int qa_device_status_dev(void* stream) {
 // carries -zp * sum(w)), exactly like the tensor-core path.
 namespace qa {
 
-constexpr int kInTileH = 16, kInTileW = 32, kInThreads = 256;  // 512 output pixels per tile
+// 16 x 28 output pixels per tile (448 rows of four 128-row MMA blocks, the
+// last one half used): 28 divides the 112-pixel rows of a 224 x 224 image
+// after a stride-2 stem, and a multiple of 4 keeps every tile's first input
+// column on one residue mod 4
+constexpr int kInTileH = 16, kInTileW = 28, kInThreads = 256;
+constexpr int kInPix = kInTileH * kInTileW;
 constexpr int kInMaxCout = 64;
 constexpr int kInMaxTaps = 16;  // K = taps * 4 bytes <= 64: four 16-byte K chunks
 constexpr int kInTab = 384;     // byte-domain activation table, index v + 128
@@ -675,12 +680,12 @@ __device__ __forceinline__ void store_pixel16(const int32_t (&q)[16], uint8_t* o
 }
 
 // Graph input quantization fused with the first convolution, on the tensor
-// cores.  Persistent: each CTA walks 16 x 32 tiles of output pixels.
+// cores.  Persistent: each CTA walks 16 x 28 tiles of output pixels.
 //   * thread 0 keeps kInStages float input patches in flight by TMA (4-D
 //     tiled loads of C x patch_h x box_w; outside the image they read 0.0,
 //     which quantizes to the input zero point exactly as the reference pads);
 //   * the block quantizes the patch (quantize_bits_try) into one 4-channel
-//     word per input pixel, then writes the 512 implicit-GEMM rows (one
+//     word per input pixel, then writes the 448 implicit-GEMM rows (one
 //     4-byte tap per word, K <= 64) as four 128-row A blocks in the plain
 //     K-major layout (8-row x 16-byte core matrices);
 //   * thread 0 issues tcgen05.mma (M = 128, N = Cout rounded to 16) for the
@@ -841,6 +846,7 @@ __global__ void __launch_bounds__(kInThreads, 2)
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int P = tid + u * kInThreads;
+      if (P >= kInPix) continue;  // rows past the tile: their results are discarded
       const int py = P / kInTileW, px = P % kInTileW;
       const int base = py * p.SH * p.patch_w + px * p.SW;
       uint8_t* row = s_a + (P / 128) * kInABlock + ((P % 128) / 8) * 128 + (P % 8) * 16;
@@ -886,7 +892,7 @@ __global__ void __launch_bounds__(kInThreads, 2)
       const int b = 2 * half + bb;
       const int P = b * 128 + quarter * 32 + lane;
       const int oy = oy0 + P / kInTileW, ox = ox0 + P % kInTileW;
-      const bool valid = oy < p.OH && ox < p.OW && !*s_abort;
+      const bool valid = P < kInPix && oy < p.OH && ox < p.OW && !*s_abort;
       const int64_t m = ((int64_t)img * p.OH + oy) * p.OW + ox;
 #pragma unroll 1
       for (int c0 = 0; c0 < CoutP; c0 += 16) {
@@ -979,7 +985,8 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
   // exact for i * patch_w < 2^32 (i < patch_h * patch_w < 2^16 here)
   p.pw_magic = (uint32_t)(((uint64_t)1 << 32) / (uint64_t)p.patch_w + 1);
   // every tile's first input column is ox0 * SW - PW with ox0 a multiple of
-  // 32: the same residue mod 4, so one shift aligns every box start to 16 B
+  // 28 (so of 4): the same residue mod 4, so one shift aligns every box start
+  // to 16 B
   p.shift = (int32_t)(((-(d->PW)) % 4 + 4) % 4);
   p.box_w = (p.patch_w + p.shift + 3) / 4 * 4;
   p.stage_bytes = (p.C * p.patch_h * p.box_w * 4 + 1023) / 1024 * 1024;

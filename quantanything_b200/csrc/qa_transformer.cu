@@ -767,19 +767,21 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       uint32_t tp[16];
       prob_bytes(*slot, s_ex, s_exf, s_xm, table, fast_p, r_f, rsum, mx, a.P, tp);
       const int lim = T - cc * 16;
-      int32_t pv[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) pv[i] = (int32_t)(tp[i] - 0x4B400000u);
       if (lim < 16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pv[i] = i < lim ? pv[i] : 0;  // padded keys: raw 0
+        for (int i = 0; i < 16; ++i)
+          tp[i] = i < lim ? tp[i] : 0x4B400000u;  // padded keys: value 0 (raw byte 0)
       }
+      // each word is value + 0x4B400000 (low byte 0): the value's byte is the
+      // word's, and the sixteen offsets cancel modulo 2^32
+      uint32_t bsum = 0;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) psum += pv[i];
-      *slot = make_uint4(pack_bytes(pv[0], pv[1], pv[2], pv[3]),
-                         pack_bytes(pv[4], pv[5], pv[6], pv[7]),
-                         pack_bytes(pv[8], pv[9], pv[10], pv[11]),
-                         pack_bytes(pv[12], pv[13], pv[14], pv[15]));
+      for (int i = 0; i < 16; ++i) bsum += tp[i];
+      psum += (int32_t)(bsum - 16u * 0x4B400000u);
+      *slot = make_uint4(pack_bytes(tp[0], tp[1], tp[2], tp[3]),
+                         pack_bytes(tp[4], tp[5], tp[6], tp[7]),
+                         pack_bytes(tp[8], tp[9], tp[10], tp[11]),
+                         pack_bytes(tp[12], tp[13], tp[14], tp[15]));
     }
   }
   // key slices past the score columns (tk > nk) hold zeros

@@ -342,7 +342,7 @@ class ResidentNet:
                 or d.qmin < -128 or d.qmax > 255):
             return
         patch_h = 15 * d.SH + (d.KH - 1) * d.DH + 1
-        patch_w = 31 * d.SW + (d.KW - 1) * d.DW + 1
+        patch_w = 27 * d.SW + (d.KW - 1) * d.DW + 1
         box_w = _round_up(patch_w + (-d.PW) % 4, 4)
         cout_p = _round_up(d.Cout, 16)
         stage = _round_up(self.in_shape[1] * patch_h * box_w * 4, 1024)
