@@ -29,6 +29,10 @@ the Softmax float fallback, captured in a CUDA graph.
 --workload vit_b16 measures configuration 3 instead: ViT-B/16 (trunc-normal
 0.02 random init), int8, batch 256 per GPU, with the reference-calibrated
 q.json of tests/golden/graphs/vit_b16_int8.qjson, on the same contract.
+--workload yolov8n_cls_int16 measures configuration 4: the same YOLOv8n-cls
+graph quantized int16 (tests/golden/graphs/yolov8n_cls_int16.qjson, every
+Conv / Gemm on the reference's int64-accumulator route), batch 1024 per GPU,
+run by the 16-bit resident executor (byte-split tensor-core contractions).
 """
 
 import argparse
@@ -69,6 +73,13 @@ WORKLOADS = {
         "batch": 64, "cpu_batch": 16, "ref_batch": 32, "classes": 1000,
         "name": "cfg2: YOLOv8n-cls int8 integer inference (random init, BN folded, "
                 "reference-calibrated q.json)"},
+    "yolov8n_cls_int16": {
+        "metric": "int16 YOLOv8n-cls images/sec", "qjson": GRAPHS / "yolov8n_cls_int16.qjson",
+        "graph": lambda b: _graph("yolov8n_cls", b), "dtype": "int16",
+        "batch": 1024, "cpu_batch": 16, "ref_batch": 32, "classes": 1000,
+        "name": "cfg4: YOLOv8n-cls int16 integer inference (random init, BN folded, "
+                "reference-calibrated q.json; every Conv / Gemm on the reference's wide "
+                "int64-accumulator route)"},
     "vit_b16": {
         "metric": "int8 ViT-B/16 images/sec", "qjson": GRAPHS / "vit_b16_int8.qjson",
         "graph": lambda b: _graph("vit_b16", b),
@@ -171,7 +182,8 @@ def run_reference_arm(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": round(ips, 3), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic N(0,1) images, random init",
+            "vs_baseline": None, "dtype": W.get("dtype", "int8"),
+            "data": "synthetic N(0,1) images, random init",
             "config": config(world, {"reference_step": f"{images} images per step on the "
                                                        "host CPU"}),
             "cpu_baseline": {"value": round(ips, 3), "unit": UNIT, "cores": threads,
@@ -321,6 +333,10 @@ def main():
         from quantanything_b200.resident_vit import ResidentViT
 
         net = ResidentViT(qc, PER_GPU_BATCH, dev)
+    elif W.get("dtype") == "int16":
+        from quantanything_b200.resident16 import ResidentNet16
+
+        net = ResidentNet16(qc, PER_GPU_BATCH, dev)
     else:
         net = ResidentNet(qc, PER_GPU_BATCH, dev)
     x_host = networks.images(PER_GPU_BATCH, IMAGE, seed=1000 + rank)
@@ -390,9 +406,13 @@ def main():
     dom = int(np.argmax(step_ms))
     label, dom_bytes, dom_ops = costs[dom]
     hbm_peak, int8_peak_tops, peak_kind = peaks()
+    # 16-bit contractions issue four 8-bit tensor-core products per MAC
+    tensor_peak = int8_peak_tops / 4 if W.get("dtype") == "int16" else int8_peak_tops
+    tensor_note = ("; int16 tensor = int8 / 4 (byte-split: four int8 MMAs per int16 MAC)"
+                   if W.get("dtype") == "int16" else "")
     dur_s = step_ms[dom] / 1e3
     ai = dom_ops / max(dom_bytes, 1)
-    ridge = int8_peak_tops * 1e12 / (hbm_peak * 1e9)
+    ridge = tensor_peak * 1e12 / (hbm_peak * 1e9)
     traffic = None
     tfile = REPO / "profiles" / "dram_traffic.json"
     if tfile.exists():
@@ -404,13 +424,13 @@ def main():
                     "traffic": traffic, "algorithmic_bytes": int(dom_bytes)}
     else:
         achieved = dom_ops / dur_s / 1e12
-        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": int8_peak_tops,
-                    "unit": "TOPS", "frac": round(achieved / int8_peak_tops, 4),
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": tensor_peak,
+                    "unit": "TOPS", "frac": round(achieved / tensor_peak, 4),
                     "traffic": traffic, "algorithmic_ops": int(dom_ops)}
     roofline.update({"kernel": label, "us_per_launch": round(step_ms[dom] * 1e3, 2),
                      "share_of_step": round(float(step_ms[dom] / step_ms.sum()), 4),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json; int8 tensor = 2 x "
-                                    "measured bf16 cuBLAS)"})
+                                    f"measured bf16 cuBLAS{tensor_note})"})
     kernels = [{"kernel": c[0], "us": round(float(t) * 1e3, 2),
                 "GB/s": round(c[1] / (t / 1e3) / 1e9, 1),
                 "TOPS": round(c[2] / (t / 1e3) / 1e12, 2) if c[2] else 0.0}
@@ -421,8 +441,8 @@ def main():
     con_ms = sum(t for _, t in con)
     con_tops = sum(c[2] for c, _ in con) / (con_ms / 1e3) / 1e12
     contractions = {"launches": len(con), "us": round(con_ms * 1e3, 1),
-                    "achieved": round(con_tops, 1), "peak": int8_peak_tops, "unit": "TOPS",
-                    "frac": round(con_tops / int8_peak_tops, 4)}
+                    "achieved": round(con_tops, 1), "peak": tensor_peak, "unit": "TOPS",
+                    "frac": round(con_tops / tensor_peak, 4)}
     fused_gemm = measure_fused_configs(dev, stream, flush, int8_peak_tops)
 
     # ---- drop-in ABI route (rank 0, N=1) and CPU baseline
@@ -446,7 +466,7 @@ def main():
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "scaling": "weak", "vs_baseline": None, "dtype": W.get("dtype", "int8"),
                 "data": "synthetic N(0,1) images clipped to +-3, random-init weights",
                 "config": config(world),
                 "e2e": {"value": round(e2e, 1), "unit": UNIT,

@@ -319,6 +319,64 @@ int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_signed, in
                            double scale, int32_t* q_out, float* f_out, int64_t rows, int64_t C,
                            void* stream);
 
+/* 16-bit device-resident layers (int16 graphs: quant_type "int16").
+ *
+ * An int16 activation tensor is two NHWC byte planes of the same geometry:
+ * the low plane holds v & 0xFF, the high plane (`plane` bytes further on)
+ * holds v >> 8, so v = lo + 256 * (int8)hi.  Every pointer below names the
+ * LOW plane of channel 0 of its view; `*_plane` is the distance in bytes to
+ * the high plane.
+ *
+ * Fused 16-bit Conv / Gemm (ConvQuantize / GemmQuantize with the wide
+ * accumulator, quant_layers.py:320-341, 384-401, native.py:363-373 route
+ * them to qa_conv_i32_i32_i64 / qa_gemm_i32_i64, qa_kernels.cpp:260-263,
+ * 281-284): base.w holds the packed int16 weights as two byte planes
+ * [2][base.w_rows][base.w_kp] (low plane rows first), K ordered (ky, kx, c).
+ * Dense layers run on the tensor cores as four 8-bit products (lo*lo,
+ * lo*hi, hi*lo, hi*hi) in three int32 TMEM accumulators that the epilogue
+ * combines exactly in int64 (exact while K * 255 * 255 < 2^31, checked);
+ * grouped / depthwise layers run on CUDA cores.  The epilogue is the 8-bit
+ * one's layer sequence (requantize with the exact 128-bit mbqm, activation
+ * LUT of 65536 entries, residual Add, rescaled Concat copy) on int16 values.
+ * base.x_signed, res_signed must be 1; base.fast and the pad_corr fields are
+ * ignored (out-of-image taps read the raw zero point). */
+typedef struct qa_fused_conv16_desc {
+  qa_fused_conv_desc base;
+  int64_t x_plane, res_plane, out_plane, out2_plane;
+} qa_fused_conv16_desc;
+
+int qa_conv16_fused_dev(const qa_fused_conv16_desc* desc, void* stream);
+
+/* Graph input: float32 NCHW -> int16 planes NHWC with `pix_stride` channels
+ * per pixel (channels C.. hold zp), qa_quantize_f32's rounding. */
+int qa_quantize_to_planes16_dev(const float* x, void* y, int64_t y_plane, int64_t N, int64_t C,
+                                int64_t H, int64_t W, int64_t pix_stride, double scale,
+                                int64_t zp, int64_t qmin, int64_t qmax, void* stream);
+
+/* GlobalAveragePool, Softmax fallback and the standalone scale-matching
+ * layers (LUT, Add, Concat rescale) of qa_gap_dev, qa_softmax_dev and
+ * qa_*_bytes_dev on int16 planes. */
+int qa_gap16_dev(const void* x, int64_t x_plane, int64_t x_pix_stride, int64_t N, int64_t HW,
+                 int64_t C, int64_t zp_in, int64_t mult, int64_t shift, int64_t zp_out,
+                 int64_t qmin, int64_t qmax, void* y, int64_t y_plane, int64_t y_pix_stride,
+                 void* stream);
+int qa_softmax16_dev(const void* x, int64_t x_plane, int64_t x_pix_stride, int64_t N, int64_t C,
+                     double in_scale, int64_t in_zp, double out_scale, int64_t out_zp,
+                     int64_t qmin, int64_t qmax, int32_t* q_out, float* y_out, double y_scale,
+                     int64_t y_zp, void* stream);
+int qa_lut16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, int64_t y_plane,
+                 int64_t y_stride, int64_t rows, int64_t C, int64_t offset, const int32_t* lut,
+                 int64_t lut_len, void* stream);
+int qa_add16_dev(const void* a, int64_t a_plane, int64_t a_stride, const void* b,
+                 int64_t b_plane, int64_t b_stride, void* y, int64_t y_plane, int64_t y_stride,
+                 int64_t rows, int64_t C, int64_t za, int64_t ma, int64_t sa, int64_t zb,
+                 int64_t mb, int64_t sb, int64_t sign, int64_t zo, int64_t qmin, int64_t qmax,
+                 void* stream);
+int qa_rescale16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, int64_t y_plane,
+                     int64_t y_stride, int64_t rows, int64_t C, int64_t identity, int64_t zp_in,
+                     int64_t m, int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
+                     void* stream);
+
 /* Allocation-free narrow GEMM.  No counterpart in the reference: it exists
  * for callers that may not allocate GPU memory while they run (a service
  * that reserves all device memory up front, work recorded into a CUDA graph,

@@ -1,0 +1,395 @@
+// Device-resident layers of 16-bit (int16) graphs other than the dense
+// tensor-core contraction (qa_umma.cu, umma_conv16_fused): graph-input
+// quantization into int16 planes, grouped / depthwise convolution with the
+// 16-bit fused epilogue, GlobalAveragePool, the Softmax float fallback and
+// the standalone scale-matching layers (LUT, Add, Concat rescale).
+//
+// An int16 tensor is two NHWC byte planes of one geometry: pixel p,
+// channel c at base + p * pix_stride + c in the low plane (v & 0xFF) and
+// `plane` bytes further in the high plane (v >> 8).  The arithmetic of each
+// layer is the reference's (quant_layers.py, qa_kernels.cpp) on int64 /
+// exact 128-bit values, as in the 8-bit kernels of qa_resident_ops.cu.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "../../include/qa_kernels.h"
+#include "qa_common.cuh"
+#include "qa_fixedpoint.cuh"
+#include "qa_fused_epilogue.cuh"
+#include "qa_ptx.cuh"
+#include "qa_umma.cuh"
+
+namespace qa {
+
+bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);  // qa_resident_ops.cu
+bool umma_conv16_fused(const qa_fused_conv16_desc& d, cudaStream_t st);  // qa_umma.cu
+
+namespace {
+
+struct Planes16 {
+  const uint8_t* p;  // low plane, channel 0
+  int64_t plane;     // bytes to the high plane
+  int64_t stride;    // bytes between pixels
+};
+
+__device__ __forceinline__ int64_t at(const Planes16& v, int64_t pix, int64_t c) {
+  return plane16_value(v.p + pix * v.stride + c, v.plane);
+}
+
+// -------------------------------------------- grouped / depthwise conv ---
+struct GroupedConv16Params {
+  Planes16 x;
+  int64_t x_zp;
+  int64_t H, W, Cg, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, Cout, Cog;
+  const uint8_t* w;  // planes [2][w_rows][w_kp]
+  int64_t w_plane, w_kp;
+  int64_t M;
+  FusedEpilogue epi;
+};
+
+// One thread per (pixel, output channel), channel fastest.  Exact int64
+// accumulation of the raw values; out-of-image taps contribute the raw
+// zero point, whose centred value is 0 (qa_kernels.cpp:124-133).
+__global__ void grouped_conv16_kernel(const __grid_constant__ GroupedConv16Params p) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = p.M * p.Cout;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t n = i % p.Cout, m = i / p.Cout;
+    const int64_t ohw = p.OH * p.OW;
+    const int64_t img = m / ohw, rem = m - img * ohw;
+    const int64_t oy = rem / p.OW, ox = rem - oy * p.OW;
+    const int64_t g = n / p.Cog;
+    const int64_t img_pix = img * p.H * p.W;
+    const uint8_t* wb = p.w + n * p.w_kp;
+    int64_t acc = 0;
+    for (int64_t ky = 0; ky < p.KH; ++ky) {
+      const int64_t iy = oy * p.SH - p.PH + ky * p.DH;
+      for (int64_t kx = 0; kx < p.KW; ++kx) {
+        const int64_t ix = ox * p.SW - p.PW + kx * p.DW;
+        const uint8_t* wt = wb + (ky * p.KW + kx) * p.Cg;
+        const bool inside = iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
+        const int64_t pix = img_pix + iy * p.W + ix;
+        for (int64_t c = 0; c < p.Cg; ++c) {
+          const int64_t wv = plane16_value(wt + c, p.w_plane);
+          acc += wv * (inside ? at(p.x, pix, g * p.Cg + c) : p.x_zp);
+        }
+      }
+    }
+    fused_epilogue_store16(p.epi, acc, m, (int)n);
+  }
+}
+
+bool grouped_conv16(const qa_fused_conv16_desc& d16, cudaStream_t st) {
+  const qa_fused_conv_desc& d = d16.base;
+  if (d.groups <= 0 || d.Cout % d.groups || d.x_signed != 1 || !d.mult || !d.shift ||
+      d.w_kp < d.KH * d.KW * d.C || d.w_rows < d.Cout || (d.res && d.res_signed != 1)) {
+    set_error(kBadArgument, "qa_conv16_fused_dev: bad grouped layer");
+    return false;
+  }
+  GroupedConv16Params p;
+  p.x = Planes16{static_cast<const uint8_t*>(d.x), d16.x_plane, d.x_pix_stride};
+  p.x_zp = d.x_zp;
+  p.H = d.H;
+  p.W = d.W;
+  p.Cg = d.C;
+  p.KH = d.KH;
+  p.KW = d.KW;
+  p.SH = d.SH;
+  p.SW = d.SW;
+  p.PH = d.PH;
+  p.PW = d.PW;
+  p.DH = d.DH;
+  p.DW = d.DW;
+  p.OH = d.OH;
+  p.OW = d.OW;
+  p.Cout = d.Cout;
+  p.Cog = d.Cout / d.groups;
+  p.w = static_cast<const uint8_t*>(d.w);
+  p.w_plane = d.w_rows * d.w_kp;
+  p.w_kp = d.w_kp;
+  p.M = d.N * d.OH * d.OW;
+  fill_fused_epilogue(p.epi, d);
+  p.epi.res_plane = d16.res_plane;
+  p.epi.out_plane = d16.out_plane;
+  p.epi.out2_plane = d16.out2_plane;
+  const int64_t total = p.M * p.Cout;
+  if (total == 0) return true;
+  return launch_ex(grouped_conv16_kernel, dim3(grid_for(total, 256)), dim3(256), 0, st, true, p);
+}
+
+// -------------------------------------------- graph input quantization ---
+// float NCHW -> int16 planes NHWC; channels C..pix_stride-1 hold zp.  The
+// reference's qa_quantize_f32 (qa_kernels.cpp:363-376):
+// clamp(rint((double)x / scale) + zp, qmin, qmax).
+__global__ void quantize_to_planes16_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
+                                            int64_t plane, int64_t N, int64_t C, int64_t HW,
+                                            int64_t pix_stride, double scale, double zp,
+                                            double qmin, double qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = N * HW * pix_stride;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t c = i % pix_stride, t = i / pix_stride;
+    const int64_t n = t / HW, pix = t - n * HW;
+    double v = zp;
+    if (c < C) {
+      v = rint((double)x[(n * C + c) * HW + pix] / scale) + zp;
+      if (v < qmin) v = qmin;
+      if (qmax < v) v = qmax;
+    }
+    plane16_store(y + i, plane, (int64_t)(int32_t)v);
+  }
+}
+
+// ------------------------------------------------------------------ GAP --
+// y[n, c] = clamp(mbqm(sum_p(x[n,p,c]) - HW*zp_in, m, s) + zp_out)
+// (quant_layers.py:569-590).  One warp per (n, c) run of 32 channels:
+// lanes read consecutive channels of each pixel.
+__global__ void gap16_kernel(Planes16 x, int64_t N, int64_t HW, int64_t C, int64_t zp_in,
+                             int64_t m, int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
+                             uint8_t* __restrict__ y, int64_t y_plane, int64_t y_pix_stride) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = N * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t n = i / C, c = i - n * C;
+    int64_t acc = 0;
+    for (int64_t p = 0; p < HW; ++p) acc += at(x, n * HW + p, c);
+    acc -= HW * zp_in;
+    plane16_store(y + n * y_pix_stride + c, y_plane,
+                  requant_exact(acc, m, s, zp_out, qmin, qmax));
+  }
+}
+
+// -------------------------------------------------------------- Softmax --
+// quant_layers.py:195-205 / float_ops.py:380-385 over int16 rows, as
+// softmax_kernel of qa_resident_ops.cu.
+constexpr int kSoftmaxThreads = 256;
+
+__device__ __forceinline__ double block_reduce16(double v, bool is_max, double* sh) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const double u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmax(v, u) : v + u;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x / 32) ? sh[lane] : (is_max ? -INFINITY : 0.0);
+    for (int o = 16; o > 0; o >>= 1) {
+      const double u = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmax(v, u) : v + u;
+    }
+    if (lane == 0) sh[0] = v;
+  }
+  __syncthreads();
+  const double r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kSoftmaxThreads)
+    softmax16_kernel(Planes16 x, int64_t C, double in_scale, int64_t in_zp, double out_scale,
+                     double out_zp, double qmin, double qmax, int32_t* __restrict__ q_out,
+                     float* __restrict__ y_out, double y_scale, int64_t y_zp) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  __shared__ double sh[32];
+  const int64_t row = blockIdx.x;
+  double mx = -INFINITY;
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    const float xf = (float)((double)(at(x, row, c) - in_zp) * in_scale);
+    mx = fmax(mx, (double)xf);
+  }
+  mx = block_reduce16(mx, true, sh);
+  double sum = 0.0;
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    const float xf = (float)((double)(at(x, row, c) - in_zp) * in_scale);
+    sum += exp((double)xf - mx);
+  }
+  sum = block_reduce16(sum, false, sh);
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    const float xf = (float)((double)(at(x, row, c) - in_zp) * in_scale);
+    const float pr = (float)(exp((double)xf - mx) / sum);
+    double v = rint((double)pr / out_scale) + out_zp;
+    if (v < qmin) v = qmin;
+    if (qmax < v) v = qmax;
+    const int32_t q = (int32_t)v;
+    if (q_out) q_out[row * C + c] = q;
+    if (y_out) y_out[row * C + c] = (float)((double)((int64_t)q - y_zp) * y_scale);
+  }
+}
+
+// ----------------------------------------------------- element-wise ----
+__global__ void lut16_kernel(Planes16 x, uint8_t* __restrict__ y, int64_t y_plane,
+                             int64_t y_stride, int64_t rows, int64_t C, int64_t offset,
+                             const int32_t* __restrict__ lut, int64_t lut_len) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    int64_t idx = at(x, r, c) - offset;  // qa_kernels.cpp:348-358
+    idx = idx < 0 ? 0 : (idx >= lut_len ? lut_len - 1 : idx);
+    plane16_store(y + r * y_stride + c, y_plane, __ldg(lut + idx));
+  }
+}
+
+__global__ void add16_kernel(Planes16 a, Planes16 b, uint8_t* __restrict__ y, int64_t y_plane,
+                             int64_t y_stride, int64_t rows, int64_t C, int64_t za, int64_t ma,
+                             int64_t sa, int64_t zb, int64_t mb, int64_t sb, int64_t sign,
+                             int64_t zo, int64_t qmin, int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    const I128 ta = mbqm(at(a, r, c) - za, ma, sa);  // qa_kernels.cpp:319-331
+    I128 tb = mbqm(at(b, r, c) - zb, mb, sb);
+    if (sign < 0) tb = neg_i128(tb);
+    plane16_store(y + r * y_stride + c, y_plane,
+                  clamp_i128(add_i128_i64(add_i128(ta, tb), zo), qmin, qmax));
+  }
+}
+
+__global__ void rescale16_kernel(Planes16 x, uint8_t* __restrict__ y, int64_t y_plane,
+                                 int64_t y_stride, int64_t rows, int64_t C, int identity,
+                                 int64_t zp_in, int64_t m, int64_t s, int64_t zp_out,
+                                 int64_t qmin, int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    const int64_t v = at(x, r, c);
+    // quant_layers.py:553-559: clip on the same grid, else qa_rescale
+    const int64_t q = identity ? (v < qmin ? qmin : (v > qmax ? qmax : v))
+                               : requant_exact(v - zp_in, m, s, zp_out, qmin, qmax);
+    plane16_store(y + r * y_stride + c, y_plane, q);
+  }
+}
+
+}  // namespace
+}  // namespace qa
+
+using namespace qa;
+
+QA_API int qa_conv16_fused_dev(const qa_fused_conv16_desc* desc, void* stream) {
+  clear_error();
+  if (!desc) {
+    set_error(kBadArgument, "qa_conv16_fused_dev: null descriptor");
+    return last_status();
+  }
+  const bool ok = desc->base.groups == 1 ? umma_conv16_fused(*desc, (cudaStream_t)stream)
+                                         : grouped_conv16(*desc, (cudaStream_t)stream);
+  return ok ? 0 : last_status();
+}
+
+QA_API int qa_quantize_to_planes16_dev(const float* x, void* y, int64_t y_plane, int64_t N,
+                                       int64_t C, int64_t H, int64_t W, int64_t pix_stride,
+                                       double scale, int64_t zp, int64_t qmin, int64_t qmax,
+                                       void* stream) {
+  clear_error();
+  if (pix_stride < C || N < 0 || C <= 0 || scale == 0.0 || qmin < -32768 || qmax > 32767) {
+    set_error(kBadArgument, "qa_quantize_to_planes16_dev: bad arguments");
+    return last_status();
+  }
+  const int64_t total = N * H * W * pix_stride;
+  if (total == 0) return 0;
+  return launch_ex(quantize_to_planes16_kernel, dim3(grid_for(total, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), y_plane, N, C,
+                   H * W, pix_stride, scale, (double)zp, (double)qmin, (double)qmax)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_gap16_dev(const void* x, int64_t x_plane, int64_t x_pix_stride, int64_t N,
+                        int64_t HW, int64_t C, int64_t zp_in, int64_t mult, int64_t shift,
+                        int64_t zp_out, int64_t qmin, int64_t qmax, void* y, int64_t y_plane,
+                        int64_t y_pix_stride, void* stream) {
+  clear_error();
+  if (N * C == 0) return 0;
+  return launch_ex(gap16_kernel, dim3(grid_for(N * C, 256)), dim3(256), 0, (cudaStream_t)stream,
+                   true, Planes16{static_cast<const uint8_t*>(x), x_plane, x_pix_stride}, N, HW,
+                   C, zp_in, mult, shift, zp_out, qmin, qmax, static_cast<uint8_t*>(y), y_plane,
+                   y_pix_stride)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_softmax16_dev(const void* x, int64_t x_plane, int64_t x_pix_stride, int64_t N,
+                            int64_t C, double in_scale, int64_t in_zp, double out_scale,
+                            int64_t out_zp, int64_t qmin, int64_t qmax, int32_t* q_out,
+                            float* y_out, double y_scale, int64_t y_zp, void* stream) {
+  clear_error();
+  if (N == 0 || C == 0) return 0;
+  if (N > 0x7FFFFFFF) {
+    set_error(kBadArgument, "qa_softmax16_dev: too many rows");
+    return last_status();
+  }
+  return launch_ex(softmax16_kernel, dim3((unsigned)N), dim3(kSoftmaxThreads), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(x), x_plane, x_pix_stride}, C, in_scale,
+                   in_zp, out_scale, (double)out_zp, (double)qmin, (double)qmax, q_out, y_out,
+                   y_scale, y_zp)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_lut16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y,
+                        int64_t y_plane, int64_t y_stride, int64_t rows, int64_t C,
+                        int64_t offset, const int32_t* lut, int64_t lut_len, void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  if (!lut || lut_len <= 0) {
+    set_error(kBadArgument, "qa_lut16_dev: empty table");
+    return last_status();
+  }
+  return launch_ex(lut16_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(x), x_plane, x_stride},
+                   static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, offset, lut, lut_len)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_add16_dev(const void* a, int64_t a_plane, int64_t a_stride, const void* b,
+                        int64_t b_plane, int64_t b_stride, void* y, int64_t y_plane,
+                        int64_t y_stride, int64_t rows, int64_t C, int64_t za, int64_t ma,
+                        int64_t sa, int64_t zb, int64_t mb, int64_t sb, int64_t sign, int64_t zo,
+                        int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  return launch_ex(add16_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(a), a_plane, a_stride},
+                   Planes16{static_cast<const uint8_t*>(b), b_plane, b_stride},
+                   static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, za, ma, sa, zb, mb, sb,
+                   sign, zo, qmin, qmax)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_rescale16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y,
+                            int64_t y_plane, int64_t y_stride, int64_t rows, int64_t C,
+                            int64_t identity, int64_t zp_in, int64_t m, int64_t s, int64_t zp_out,
+                            int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  return launch_ex(rescale16_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(x), x_plane, x_stride},
+                   static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, (int)(identity != 0),
+                   zp_in, m, s, zp_out, qmin, qmax)
+             ? 0
+             : last_status();
+}

@@ -25,7 +25,7 @@
 
 namespace qa {
 
-enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1, kEpiFused = 2 };
+enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1, kEpiFused = 2, kEpiFused16 = 3 };
 
 constexpr int kBM = 128;          // tile rows (TMEM lanes)
 constexpr int kBKBytes = 128;     // K-block bytes (one 128-byte swizzle row)
@@ -297,6 +297,13 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
           } else {
             p.y[m * p.y_ctot + n] = (int32_t)acc;
           }
+        } else if constexpr (kEpi == kEpiFused16) {
+          // lo*lo (u8 x u8), the two cross products and hi*hi, each exact in
+          // int32 for K * 255 * 255 < 2^31 (host-checked), combined in int64
+          static_assert(TS::kNumAcc == 3, "16-bit epilogue needs the split planes");
+          const int64_t acc = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
+                              (int64_t)(int32_t)v[2][j] * 65536;
+          fused_epilogue_store16(p.epi, acc, m, n);
         } else {
           static_assert(TS::kNumAcc == 1, "fused epilogue is 8-bit only");
           fused_epilogue_store(p.epi, (int64_t)(int32_t)v[0][j], m, n);
@@ -684,6 +691,104 @@ bool umma_gemm_i16_i32_into(const int16_t* A, const int16_t* B, int32_t* C, int6
   prm.status = status;
   return launch_umma<kSplitBN, 2, 2, 16, kEpiAcc32Row, kSplitStages>(prm, tmap, Np / kSplitBN, 1,
                                                                       st);
+}
+
+}  // namespace qa
+
+// ============================================ 16-bit resident layers ==
+
+#include "../../include/qa_kernels.h"
+
+namespace qa {
+
+bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);  // qa_resident_ops.cu
+
+namespace {
+
+template <int BN, int kChunk>
+bool launch_conv16(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n_tiles,
+                   cudaStream_t st) {
+  // two stages (about 100 KB) keep two CTAs on an SM up to BN = 64, so one
+  // CTA's epilogue overlaps the other's gather and MMAs; BN = 128 takes the
+  // whole SM (its three accumulators fill the 512 TMEM columns)
+  constexpr int kStages = BN <= 64 ? 2 : 3;
+  return launch_umma<BN, 2, 2, kChunk, kEpiFused16, kStages>(prm, tmap, n_tiles, 1, st);
+}
+
+template <int kChunk>
+bool launch_conv16_bn(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
+                      int64_t n_tiles, cudaStream_t st) {
+  switch (bn) {
+    case 16: return launch_conv16<16, kChunk>(prm, tmap, n_tiles, st);
+    case 32: return launch_conv16<32, kChunk>(prm, tmap, n_tiles, st);
+    case 64: return launch_conv16<64, kChunk>(prm, tmap, n_tiles, st);
+    default: return launch_conv16<128, kChunk>(prm, tmap, n_tiles, st);
+  }
+}
+
+}  // namespace
+
+// Dense (groups == 1) 16-bit layer on the byte-split tensor-core kernel.
+bool umma_conv16_fused(const qa_fused_conv16_desc& d16, cudaStream_t st) {
+  const qa_fused_conv_desc& d = d16.base;
+  const int64_t bn = d.block_n;
+  const int64_t K = d.KH * d.KW * d.C;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(d.x);
+  if (bn != 16 && bn != 32 && bn != 64 && bn != 128) {
+    set_error(kBadArgument, "qa_conv16_fused_dev: block_n must be 16, 32, 64 or 128");
+    return false;
+  }
+  if (d.w_rows % bn || d.w_rows < d.Cout || d.w_kp % 16 || d.w_kp < K || !d.mult || !d.shift ||
+      d.C % 4 || d.x_pix_stride % 4 || d.x_pix_stride < d.C || (xa & 3) ||
+      (d16.x_plane & 3) || d.x_signed != 1 || (d.res && d.res_signed != 1)) {
+    set_error(kBadArgument, "qa_conv16_fused_dev: bad layout");
+    return false;
+  }
+  // each 8-bit partial product sum must stay exact in its int32 accumulator
+  if (K * 255 * 255 >= (int64_t(1) << 31)) {
+    set_error(kUnsupported, "qa_conv16_fused_dev: K too large for exact int32 partial sums");
+    return false;
+  }
+  const int64_t M = d.N * d.OH * d.OW;
+  if (M == 0 || d.Cout == 0) return true;
+  ConvTileParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.a[0] = static_cast<const uint8_t*>(d.x);
+  prm.a[1] = static_cast<const uint8_t*>(d.x) + d16.x_plane;
+  prm.pix_stride = d.x_pix_stride;
+  // out-of-image taps read the raw zero point (centred value 0), per plane
+  prm.pad_word[0] = (uint32_t)(d.x_zp & 0xFF) * 0x01010101u;
+  prm.pad_word[1] = (uint32_t)((d.x_zp >> 8) & 0xFF) * 0x01010101u;
+  prm.H = (int32_t)d.H;
+  prm.W = (int32_t)d.W;
+  prm.Cin = (int32_t)d.C;
+  prm.KH = (int32_t)d.KH;
+  prm.KW = (int32_t)d.KW;
+  prm.SH = (int32_t)d.SH;
+  prm.SW = (int32_t)d.SW;
+  prm.PH = (int32_t)d.PH;
+  prm.PW = (int32_t)d.PW;
+  prm.DH = (int32_t)d.DH;
+  prm.DW = (int32_t)d.DW;
+  prm.OH = (int32_t)d.OH;
+  prm.OW = (int32_t)d.OW;
+  prm.M = M;
+  prm.K = (int32_t)K;
+  prm.num_kb = (int32_t)((d.w_kp + kBKBytes - 1) / kBKBytes);
+  prm.b_plane_rows = (int32_t)d.w_rows;
+  prm.n_valid = (int32_t)d.Cout;
+  prm.status = device_status_word();
+  fill_fused_epilogue(prm.epi, d);
+  prm.epi.res_plane = d16.res_plane;
+  prm.epi.out_plane = d16.out_plane;
+  prm.epi.out2_plane = d16.out2_plane;
+  CUtensorMap tmap;
+  if (!make_weight_tmap(&tmap, d.w, 2 * d.w_rows, d.w_kp, (int)bn)) return false;
+  const bool wide = d.C % 16 == 0 && d.x_pix_stride % 16 == 0 && (xa & 15) == 0 &&
+                    (d16.x_plane & 15) == 0;
+  const int64_t n_tiles = d.w_rows / bn;
+  return wide ? launch_conv16_bn<16>((int)bn, prm, tmap, n_tiles, st)
+              : launch_conv16_bn<4>((int)bn, prm, tmap, n_tiles, st);
 }
 
 }  // namespace qa

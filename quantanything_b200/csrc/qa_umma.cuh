@@ -48,6 +48,9 @@ struct FusedEpilogue {
   int64_t out2_pix_stride;
   int32_t r_identity;    // copy (after clamping to r_qmin..r_qmax) instead of rescale
   int64_t r_zp_in, r_m, r_s, r_zp_out, r_qmin, r_qmax;
+  // 16-bit layers: bytes from each low plane (res, out, out2) to its high
+  // plane (v = lo + 256 * (int8)hi); unused by the 8-bit epilogue
+  int64_t res_plane, out_plane, out2_plane;
 };
 
 // ABI routes (host-pointer entry points, operands already on the device).

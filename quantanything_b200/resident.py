@@ -186,6 +186,7 @@ class View:
     C: int
     signed: bool
     qp: object = None
+    plane: int = 0  # 16-bit tensors: bytes from the low byte plane to the high one
 
     @property
     def ptr(self):
@@ -193,7 +194,7 @@ class View:
 
     def channel_slice(self, c0, c):
         return View(self.buf, self.offset + c0, self.pix_stride, self.N, self.H, self.W, c,
-                    self.signed, self.qp)
+                    self.signed, self.qp, self.plane)
 
 
 @dataclass
@@ -210,6 +211,8 @@ class UnsupportedGraph(NotImplementedError):
 class ResidentNet:
     """Fused device-resident integer inference of a prepared container."""
 
+    _max_block_n = 256  # widest column tile of the contraction kernel
+
     def __init__(self, container, batch, device=None, fuse_input=True):
         if not container.calibrated:
             raise ValueError("container is not calibrated")
@@ -224,8 +227,7 @@ class ResidentNet:
         self.lib.set_device(self.device.index)
         self.sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.bits, self.signed = container.layers[0].num_bits, container.layers[0].signed
-        if self.bits > 8:
-            raise UnsupportedGraph("the resident executor runs 8-bit graphs")
+        self._check_bits()
         self.fuse_input = fuse_input
         self._in_patch = 0  # > 0: the input quantizer writes patch rows (patch embedding)
         self._keep = []
@@ -235,6 +237,10 @@ class ResidentNet:
         self._plan()
 
     # ------------------------------------------------------------- helpers --
+    def _check_bits(self):
+        if self.bits > 8:
+            raise UnsupportedGraph("the resident executor runs 8-bit graphs")
+
     def _alloc(self, nbytes):
         t = torch.empty(int(nbytes) + 64, dtype=torch.uint8, device=self.device)
         self._keep.append(t)
@@ -267,9 +273,8 @@ class ResidentNet:
         qp_in = c.qparams[in_name]
         Cin = self.in_shape[1]
         stride_in = Cin if Cin % 16 == 0 else _round_up(Cin, 4)
-        views = {in_name: View(self._alloc(self.batch * self.in_shape[2] * self.in_shape[3]
-                                           * stride_in), 0, stride_in, self.batch,
-                               self.in_shape[2], self.in_shape[3], Cin, self.signed, qp_in)}
+        views = {in_name: self._new_view(self.batch, self.in_shape[2], self.in_shape[3], Cin,
+                                         qp_in, pix_stride=stride_in)}
         self.x_dev = torch.empty(self.in_shape, dtype=torch.float32, device=self.device)
         self.steps.append(("quantize", in_name))
         self._in_view = views[in_name]
@@ -425,20 +430,25 @@ class ResidentNet:
             w4 = layer.w_centered.astype(np.int64)
             cout, cg, kh, kw = w4.shape
             groups = layer.node.attr("group", 1)
-        if w4.min() < -128 or w4.max() > 127:
-            raise UnsupportedGraph(f"{layer.name}: centred weights exceed int8")
+        lim = 1 << (self.bits - 1)
+        if w4.min() < -lim or w4.max() >= lim:
+            raise UnsupportedGraph(f"{layer.name}: centred weights exceed int{self.bits}")
         ct = taps_c if groups == 1 else cg
-        bn = choose_block_n(cout, m_rows, ct if groups == 1 else 16, self.sm_count)
+        bn = min(choose_block_n(cout, m_rows, ct if groups == 1 else 16, self.sm_count),
+                 self._max_block_n)
         rows = _round_up(cout, bn)
         k = kh * kw * ct
         kp = _round_up(k, 16)
-        packed = np.zeros((rows, kp), np.int8)
+        packed = np.zeros((rows, kp), np.int8 if self.bits == 8 else np.int16)
         wt = np.zeros((cout, kh, kw, ct), np.int64)
         wt[:, :, :, :cg] = np.transpose(w4, (0, 2, 3, 1))
         packed[:cout, :k] = wt.reshape(cout, k)
         colsum = wt.reshape(cout, k).sum(axis=1)
         abssum = np.abs(wt.reshape(cout, k)).sum(axis=1)
         return packed, rows, kp, bn, groups, ct, colsum, abssum
+
+    def _upload_weights(self, packed):
+        return self._dev(packed, np.int8)
 
     def _plan_contraction(self, layer, layers, fused_away, patch=0):
         """``patch`` > 0: the input view holds the im2col rows of this
@@ -465,7 +475,7 @@ class ResidentNet:
             rows = _round_up(cout_, bn)
             if rows != packed.shape[0]:
                 packed = np.concatenate(
-                    [packed[:cout_], np.zeros((rows - cout_, packed.shape[1]), np.int8)])
+                    [packed[:cout_], np.zeros((rows - cout_, packed.shape[1]), packed.dtype)])
         elif isinstance(layer, GemmQuantize):
             if (x_view.H, x_view.W) != (1, 1):
                 raise UnsupportedGraph("Gemm input must be a flattened vector")
@@ -511,14 +521,14 @@ class ResidentNet:
         for k_, v in geo.items():
             setattr(d, k_, int(v))
         d.Cout, d.groups = cout, groups
-        wdev = self._dev(packed, np.int8)
+        wdev = self._upload_weights(packed)
         d.w, d.w_rows, d.w_kp = wdev.data_ptr(), rows, kp
         bdev, mdev, sdev = (self._dev(bias, np.int64), self._dev(mult, np.int64),
                             self._dev(shift, np.int64))
         d.bias, d.mult, d.shift = bdev.data_ptr(), mdev.data_ptr(), sdev.data_ptr()
         d.zp, d.qmin, d.qmax, d.fast = layer.out_zp, layer.out_qmin, layer.out_qmax, int(fast)
         d.block_n = bn if groups == 1 else 0
-        if groups == 1 and ct % 16 == 0 and x_zp != 0 and not patch:
+        if groups == 1 and ct % 16 == 0 and x_zp != 0 and not patch and self.bits == 8:
             wt = packed[:cout, :geo["KH"] * geo["KW"] * ct].reshape(cout, geo["KH"], geo["KW"], ct)
             pc = pad_corrections(wt, int(x_zp), H, W, **geo)
             if pc is not None:

@@ -1,0 +1,212 @@
+"""Device-resident, fused execution of 16-bit (int16) graphs.
+
+The reference runs an int16 graph with every Conv and Gemm on its wide
+route: int32 operands, int64 accumulators (``native.accumulator_is_wide``,
+native.py:363-373 -> qa_conv_i32_i32_i64 / qa_gemm_i32_i64,
+qa_kernels.cpp:260-263, 281-284), then requantizes with the 128-bit
+``mbqm`` (qa_kernels.cpp:188-228).  ResidentNet16 computes the same
+integers with the activations resident in HBM as two NHWC byte planes per
+tensor (low byte ``v & 0xFF``, high byte ``v >> 8``):
+
+* dense Conv / Gemm run on the tensor cores as four 8-bit products per
+  K-step (lo*lo, lo*hi, hi*lo, hi*hi) into three int32 TMEM accumulators
+  that the epilogue combines in int64 -- exact, and so identical to the
+  reference's int64 accumulation, while K * 255 * 255 < 2^31 (K < 33025;
+  YOLOv8n-cls's largest K is 1280) -- with requantize, the 65536-entry
+  activation LUT, the residual Add and the rescaled Concat copy fused into
+  the same launch (``qa_conv16_fused_dev``); grouped / depthwise layers run
+  the same epilogue on CUDA cores;
+* Split / Flatten are views, Concat inputs are written into their slice,
+  GlobalAveragePool and the Softmax fallback are one kernel each, and the
+  graph input is quantized straight into the planes.
+
+The planner is ResidentNet's (same fusion decisions); only the storage,
+the weight packing and the launches differ.
+"""
+
+import ctypes
+
+import numpy as np
+import torch
+
+from quantanything_b200.resident import (
+    FusedConvDesc,
+    ResidentNet,
+    UnsupportedGraph,
+    View,
+    _check,
+    _round_up,
+)
+
+_I64 = ctypes.c_int64
+_P = ctypes.c_void_p
+_D = ctypes.c_double
+
+
+class FusedConv16Desc(ctypes.Structure):
+    """ctypes mirror of ``qa_fused_conv16_desc`` (include/qa_kernels.h)."""
+
+    _fields_ = [("base", FusedConvDesc), ("x_plane", _I64), ("res_plane", _I64),
+                ("out_plane", _I64), ("out2_plane", _I64)]
+
+
+_DEV16_SIGNATURES = {
+    "qa_conv16_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConv16Desc), _P]),
+    "qa_quantize_to_planes16_dev": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                                   _D, _I64, _I64, _I64, _P]),
+    "qa_gap16_dev": (ctypes.c_int, [_P] + [_I64] * 11 + [_P, _I64, _I64, _P]),
+    "qa_softmax16_dev": (ctypes.c_int, [_P, _I64, _I64, _I64, _I64, _D, _I64, _D, _I64, _I64,
+                                        _I64, _P, _P, _D, _I64, _P]),
+    "qa_lut16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P,
+                                    _I64, _P]),
+    "qa_add16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64]
+                     + [_I64] * 12 + [_P]),
+    "qa_rescale16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64] + [_I64] * 9 + [_P]),
+}
+
+
+def device_api16(lib):
+    """Declares the 16-bit device-pointer entry points on a KernelLibrary."""
+    raw = lib.raw
+    if not getattr(raw, "_qa_dev16_declared", False):
+        for name, (res, args) in _DEV16_SIGNATURES.items():
+            fn = getattr(raw, name)
+            fn.restype, fn.argtypes = res, args
+        raw._qa_dev16_declared = True
+    return raw
+
+
+class ResidentNet16(ResidentNet):
+    """Fused device-resident integer inference of a prepared int16 container."""
+
+    # three accumulators of BN columns per CTA: BN = 64 leaves room for two
+    # CTAs per SM in TMEM (2 x 256 columns) and shared memory
+    _max_block_n = 64
+
+    def __init__(self, container, batch, device=None):
+        self._planes = []  # (low plane start, plane bytes) of every allocation
+        super().__init__(container, batch, device, fuse_input=False)
+        device_api16(self.lib)
+        self._descs = {}
+
+    # ---------------------------------------------------------- storage --
+    def _check_bits(self):
+        if self.bits != 16 or not self.signed:
+            raise UnsupportedGraph("ResidentNet16 runs int16 graphs")
+
+    def _new_view(self, N, H, W, C, qp, pix_stride=None):
+        stride = pix_stride or (C if C % 16 == 0 else _round_up(C, 16))
+        plane = _round_up(N * H * W * stride, 256)
+        buf = self._alloc(2 * plane)
+        self._planes.append((buf.data_ptr(), plane))
+        return View(buf, 0, stride, N, H, W, C, True, qp, plane)
+
+    def _plane_of(self, ptr):
+        """Plane distance of the allocation holding device address ``ptr``."""
+        for start, plane in self._planes:
+            if start <= ptr < start + plane:
+                return plane
+        raise AssertionError(f"address {ptr:#x} is not in a planned 16-bit tensor")
+
+    def _upload_weights(self, packed):
+        # [rows, kp] int16 -> [2][rows][kp] bytes: low plane, then high plane
+        v = packed.astype(np.int64)
+        planes = np.concatenate([(v & 0xFF).astype(np.uint8),
+                                 ((v >> 8) & 0xFF).astype(np.uint8)])
+        return self._dev(planes, np.uint8)
+
+    def _desc16(self, step):
+        d16 = self._descs.get(id(step))
+        if d16 is None:
+            d = step.desc
+            d16 = FusedConv16Desc()
+            d16.base = d
+            d16.x_plane = self._plane_of(d.x)
+            d16.res_plane = self._plane_of(d.res) if d.res else 0
+            d16.out_plane = self._plane_of(d.out) if d.out else 0
+            d16.out2_plane = self._plane_of(d.out2) if d.out2 else 0
+            self._descs[id(step)] = d16
+        return d16
+
+    # ----------------------------------------------------------- launch --
+    def _launch_all(self, stream, on_step=None):
+        raw = self.lib.raw
+        raw.qa_set_device(self.device.index)
+        st = ctypes.c_void_p(stream)
+        n = 0
+        for kind, payload in self.steps:
+            if kind == "quantize":
+                v, qp = self._in_view, self.c.qparams[payload]
+                N, C, H, W = self.in_shape
+                rc = raw.qa_quantize_to_planes16_dev(self.x_dev.data_ptr(), v.ptr, v.plane, N, C,
+                                                     H, W, v.pix_stride, float(qp.scale), qp.zp,
+                                                     qp.qmin, qp.qmax, st)
+            elif kind == "conv":
+                rc = raw.qa_conv16_fused_dev(ctypes.byref(self._desc16(payload)), st)
+            elif kind == "rescale":
+                concat, idx, src, dst = payload
+                m, s = concat._mult[idx]
+                qp, o = concat.in_qp[idx], concat.out_qp[0]
+                rc = raw.qa_rescale16_dev(src.ptr, src.plane, src.pix_stride, dst.ptr, dst.plane,
+                                          dst.pix_stride, src.N * src.H * src.W, src.C,
+                                          int(concat.same_grid(idx)), qp.zp, m, s, o.zp, o.qmin,
+                                          o.qmax, st)
+            elif kind == "gap":
+                layer, x, y, area = payload
+                m, s = layer.multiplier(area)
+                rc = raw.qa_gap16_dev(x.ptr, x.plane, x.pix_stride, x.N, area, x.C, layer.in_zp,
+                                      m, s, layer.out_zp, layer.out_qmin, layer.out_qmax, y.ptr,
+                                      y.plane, y.pix_stride, st)
+            elif kind == "lut":
+                layer, x, y, ldev = payload
+                rc = raw.qa_lut16_dev(x.ptr, x.plane, x.pix_stride, y.ptr, y.plane, y.pix_stride,
+                                      x.N * x.H * x.W, x.C, int(layer.lut_offset),
+                                      ldev.data_ptr(), len(layer.lut), st)
+            elif kind == "add":
+                layer, a, b, y = payload
+                (ma, sa), (mb, sb) = layer._mult
+                qa, qb = layer.in_qp
+                o = layer.out_qp[0]
+                rc = raw.qa_add16_dev(a.ptr, a.plane, a.pix_stride, b.ptr, b.plane, b.pix_stride,
+                                      y.ptr, y.plane, y.pix_stride, a.N * a.H * a.W, a.C, qa.zp,
+                                      ma, sa, qb.zp, mb, sb, layer._sign, o.zp, o.qmin, o.qmax,
+                                      st)
+            elif kind == "softmax":
+                layer, x = payload
+                qi, o = layer.in_qp[0], layer.out_qp[0]
+                rc = raw.qa_softmax16_dev(x.ptr, x.plane, x.pix_stride, x.N, x.C,
+                                          float(qi.scale), qi.zp, float(o.scale), o.zp, o.qmin,
+                                          o.qmax, self.out_q.data_ptr(), self.out_f32.data_ptr(),
+                                          float(o.scale), o.zp, st)
+            else:
+                raise UnsupportedGraph(f"{kind} has no 16-bit resident kernel")
+            _check(self.lib, rc, f"{kind} step (16-bit)")
+            if on_step is not None:
+                on_step(n)
+            n += 1
+        self.launch_count = n
+        return n
+
+    # ------------------------------------------------------------ costs --
+    def step_costs(self):
+        """Algorithmic (bytes, integer ops) per step with 2-byte activations
+        and weights: ResidentNet's byte counts doubled, except the float32
+        input of the quantize step."""
+        costs = []
+        for (label, nbytes, ops), (kind, payload) in zip(super().step_costs(), self.steps):
+            if kind == "quantize":
+                N, C, H, W = self.in_shape
+                nbytes = N * C * H * W * 4 + 2 * N * H * W * self._in_view.pix_stride
+            else:
+                nbytes *= 2
+            costs.append((label, nbytes, ops))
+        return costs
+
+    def tensor(self, name):
+        """A planned tensor as int32 NCHW (inspection helper; copies)."""
+        v = self._views[name]
+        rows = v.N * v.H * v.W
+        lo = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset).to(torch.int32)
+        hi = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset + v.plane)
+        t = lo + hi.view(torch.int8).to(torch.int32) * 256
+        return t.reshape(v.N, v.H, v.W, v.C).permute(0, 3, 1, 2).contiguous()

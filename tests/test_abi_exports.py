@@ -73,3 +73,24 @@ def test_fused_desc_layout_matches_header(tmp_path):
                                           check=True).stdout.split()]
     want = [getattr(FusedConvDesc, n).offset for n in names] + [ctypes.sizeof(FusedConvDesc)]
     assert got == want
+
+
+def test_fused16_desc_layout_matches_header(tmp_path):
+    """ctypes FusedConv16Desc has the exact field offsets of the C struct."""
+    import subprocess
+
+    from quantanything_b200.resident16 import FusedConv16Desc
+
+    names = [f[0] for f in FusedConv16Desc._fields_]
+    src = tmp_path / "probe16.c"
+    src.write_text(
+        '#include <stddef.h>\n#include <stdio.h>\n#include "qa_kernels.h"\nint main(void){\n'
+        + "".join(f'printf("%zu\\n", offsetof(qa_fused_conv16_desc, {n}));\n' for n in names)
+        + 'printf("%zu\\n", sizeof(qa_fused_conv16_desc));\nreturn 0;}\n')
+    exe = tmp_path / "probe16"
+    subprocess.run(["gcc", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    want = [getattr(FusedConv16Desc, n).offset for n in names] + [
+        ctypes.sizeof(FusedConv16Desc)]
+    assert got == want

@@ -1,0 +1,109 @@
+"""Device-resident int16 executor (ResidentNet16) vs the reference (B200).
+
+An int16 graph takes the reference's wide route for every Conv / Gemm
+(int32 operands, int64 accumulation).  The resident executor computes it as
+byte-split tensor-core products combined exactly in int64, so every integer
+tensor must equal the reference's bit for bit; the Softmax float fallback
+is allowed 1 output LSB like the int8 tests.
+"""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from quantanything_b200 import networks
+from quantanything_b200.container import QuantContainer
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+GRAPHS = GOLDEN / "graphs"
+SOFTMAX_LSB = 1
+
+
+def _net(name, lib, batch):
+    from quantanything_b200.resident16 import ResidentNet16
+
+    meta = json.loads((GRAPHS / f"{name}.meta.json").read_text())
+    g = getattr(networks, meta["builder"])(**meta["kwargs"])
+    qc = QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=lib)
+    return ResidentNet16(qc, batch), qc, meta
+
+
+def _run(net, x):
+    net.forward_device(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    net.check_status()
+    return net.out_q.cpu().numpy()
+
+
+def _integer_pass(qc, x, stop_at="Softmax"):
+    """The container's layer-by-layer integer pass (drop-in ABI route,
+    itself pinned bit-exactly to the reference) up to the Softmax."""
+    env = dict(qc.quantize_inputs({qc.graph.inputs[0].name: x}))
+    for node in qc.graph.nodes:
+        if node.op_type == stop_at:
+            return env, node.inputs[0]
+        layer = qc.quant_layers[node.name]
+        outs = layer.quantized_infer_integer([env[n] for n in layer.data_inputs])
+        env.update(zip(node.outputs, outs))
+    raise AssertionError("no Softmax")
+
+
+def test_yolov8n_int16_batch2_matches_reference(gpu_lib):
+    net, qc, meta = _net("yolov8n_cls_int16", gpu_lib, 2)
+    assert all(p.desc.groups == 1 for k, p in net.steps if k == "conv")
+    x = networks.images(2, 224, seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / "yolov8n_cls_int16.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+    env, logits = _integer_pass(qc, x)
+    got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
+    np.testing.assert_array_equal(got, env[logits])
+
+
+def test_yolov8n_int16_every_tensor_bit_exact(gpu_lib):
+    """Each planned tensor (convolution outputs with their fused LUT / Add,
+    Concat buffers, the pooled features) equals the drop-in pass's."""
+    net, qc, meta = _net("yolov8n_cls_int16", gpu_lib, 2)
+    x = networks.images(2, 224, seed=11)
+    _run(net, x)
+    env, _ = _integer_pass(qc, x)
+    checked = 0
+    for name, view in net._views.items():
+        if name not in env or name == qc.graph.inputs[0].name:
+            continue
+        got = net.tensor(name).cpu().numpy().reshape(env[name].shape)
+        np.testing.assert_array_equal(got, env[name], err_msg=name)
+        checked += 1
+    assert checked >= 20
+
+
+def test_yolo_mini_int16_grouped_and_fused(gpu_lib):
+    """The small YOLO graph: depthwise conv on the CUDA-core route, fused
+    LUT / residual Add / Concat copies on the tensor-core route."""
+    net, qc, meta = _net("yolo_mini_int16", gpu_lib, 2)
+    assert any(p.desc.groups > 1 for k, p in net.steps if k == "conv")
+    x = networks.images(2, meta["image"], seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / "yolo_mini_int16.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+    env, logits = _integer_pass(qc, x)
+    got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
+    np.testing.assert_array_equal(got, env[logits])
+
+
+def test_int16_batch_invariance_and_graph_replay(gpu_lib):
+    """Images 0..3 of a batch of 8 equal a batch of 4 (batch sharding is
+    exact), and CUDA-graph replay equals the eager pass."""
+    net8, _, _ = _net("yolov8n_cls_int16", gpu_lib, 8)
+    net4, _, _ = _net("yolov8n_cls_int16", gpu_lib, 4)
+    x = networks.images(8, 224, seed=5)
+    eager = _run(net8, x).copy()
+    np.testing.assert_array_equal(eager[:4], _run(net4, x[:4]))
+    net8.capture()
+    for _ in range(2):
+        net8.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(net8.out_q.cpu().numpy(), eager)
+    np.testing.assert_array_equal(net8.run(x), net8.out_f32.cpu().numpy())
