@@ -280,6 +280,20 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
       for (int a = 0; a < TS::kNumAcc; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
       ptx::tmem_ld_wait();
       if (!row_ok) continue;
+      if constexpr (kEpi == kEpiFused16) {
+        // lo*lo (u8 x u8), the two cross products and hi*hi, each exact in
+        // int32 for K * 255 * 255 < 2^31 (host-checked), combined in int64
+        static_assert(TS::kNumAcc == 3, "16-bit epilogue needs the split planes");
+        int64_t acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          acc[j] = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
+                   (int64_t)(int32_t)v[2][j] * 65536;
+        const int nb = n0 + c0;
+        const int cnt = p.n_valid - nb < 16 ? p.n_valid - nb : 16;
+        if (cnt > 0) fused_epilogue_store16_run(p.epi, acc, m, nb, cnt);
+        continue;
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int n = n0 + c0 + j;  // column within the group
@@ -297,14 +311,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
           } else {
             p.y[m * p.y_ctot + n] = (int32_t)acc;
           }
-        } else if constexpr (kEpi == kEpiFused16) {
-          // lo*lo (u8 x u8), the two cross products and hi*hi, each exact in
-          // int32 for K * 255 * 255 < 2^31 (host-checked), combined in int64
-          static_assert(TS::kNumAcc == 3, "16-bit epilogue needs the split planes");
-          const int64_t acc = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
-                              (int64_t)(int32_t)v[2][j] * 65536;
-          fused_epilogue_store16(p.epi, acc, m, n);
-        } else {
+        } else if constexpr (kEpi == kEpiFused) {
           static_assert(TS::kNumAcc == 1, "fused epilogue is 8-bit only");
           fused_epilogue_store(p.epi, (int64_t)(int32_t)v[0][j], m, n);
         }
