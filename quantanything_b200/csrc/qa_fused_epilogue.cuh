@@ -100,56 +100,62 @@ __device__ __forceinline__ bool aligned16(const uint8_t* p, int64_t plane) {
 __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& e,
                                                            const int64_t (&acc)[16], int64_t m,
                                                            int n0, int cnt) {
+  // Phased so that the independent loads of the sixteen channels are in
+  // flight together: channel parameters, then requantize, then the sixteen
+  // table lookups, then the residual terms and the stores.  Columns past
+  // cnt compute on channel n0's parameters and are not stored.
   const uint8_t* rp = e.res ? e.res + m * e.res_pix_stride + n0 : nullptr;
   uint8_t* op = e.out ? e.out + m * e.out_pix_stride + n0 : nullptr;
   uint8_t* op2 = e.out2 ? e.out2 + m * e.out2_pix_stride + n0 : nullptr;
   const bool full = cnt == 16;
-  const bool rvec = rp && full && aligned16(rp, e.res_plane);
-  uint4 rl = make_uint4(0, 0, 0, 0), rh = rl;
-  if (rvec) {
-    rl = *reinterpret_cast<const uint4*>(rp);
-    rh = *reinterpret_cast<const uint4*>(rp + e.res_plane);
-  }
-  uint32_t wl[4] = {0, 0, 0, 0}, wh[4] = {0, 0, 0, 0}, wl2[4] = {0, 0, 0, 0},
-           wh2[4] = {0, 0, 0, 0};
+  int64_t q[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    if (j < cnt) {
-      const int n = n0 + j;
-      int64_t q = requant_exact(acc[j] + (e.bias ? e.bias[n] : 0), e.mult[n], e.shift[n], e.zp,
-                                e.qmin, e.qmax);
-      if (e.lut) {
-        int64_t idx = q - e.lut_offset;
-        idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
-        q = __ldg(e.lut + idx);
-      }
-      if (rp) {
-        int64_t a;
-        if (rvec) {
-          const uint32_t l = (reinterpret_cast<const uint32_t*>(&rl)[j >> 2] >> (8 * (j & 3))) & 0xFF;
-          const uint32_t h = (reinterpret_cast<const uint32_t*>(&rh)[j >> 2] >> (8 * (j & 3))) & 0xFF;
-          a = (int64_t)(int16_t)(uint16_t)(l | (h << 8));
-        } else {
-          a = plane16_value(rp + j, e.res_plane);
-        }
-        const I128 ta = mbqm(a - e.za, e.ma, e.sa);
-        I128 tb = mbqm(q - e.zb, e.mb, e.sb);
-        if (e.sign < 0) tb = neg_i128(tb);
-        q = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
-      }
-      wl[j >> 2] |= (uint32_t)(q & 0xFF) << (8 * (j & 3));
-      wh[j >> 2] |= (uint32_t)((q >> 8) & 0xFF) << (8 * (j & 3));
-      if (op2) {
-        int64_t q2;
-        if (e.r_identity) {
-          q2 = q < e.r_qmin ? e.r_qmin : (q > e.r_qmax ? e.r_qmax : q);
-        } else {
-          q2 = requant_exact(q - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
-        }
-        wl2[j >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (j & 3));
-        wh2[j >> 2] |= (uint32_t)((q2 >> 8) & 0xFF) << (8 * (j & 3));
-      }
+    const int n = n0 + (j < cnt ? j : 0);
+    const int64_t b = e.bias ? __ldg(e.bias + n) : 0;
+    q[j] = requant_exact(acc[j] + b, __ldg(e.mult + n), __ldg(e.shift + n), e.zp, e.qmin,
+                         e.qmax);
+  }
+  if (e.lut) {
+    int32_t t[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      int64_t idx = q[j] - e.lut_offset;
+      idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
+      t[j] = __ldg(e.lut + idx);
     }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) q[j] = t[j];
+  }
+  if (rp) {
+    int64_t a[16];
+    if (full && aligned16(rp, e.res_plane)) {
+      const uint4 rl = *reinterpret_cast<const uint4*>(rp);
+      const uint4 rh = *reinterpret_cast<const uint4*>(rp + e.res_plane);
+      const uint32_t lw[4] = {rl.x, rl.y, rl.z, rl.w}, hw[4] = {rh.x, rh.y, rh.z, rh.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t l = (lw[j >> 2] >> (8 * (j & 3))) & 0xFF;
+        const uint32_t h = (hw[j >> 2] >> (8 * (j & 3))) & 0xFF;
+        a[j] = (int64_t)(int16_t)(uint16_t)(l | (h << 8));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) a[j] = plane16_value(rp + (j < cnt ? j : 0), e.res_plane);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const I128 ta = mbqm(a[j] - e.za, e.ma, e.sa);
+      I128 tb = mbqm(q[j] - e.zb, e.mb, e.sb);
+      if (e.sign < 0) tb = neg_i128(tb);
+      q[j] = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
+    }
+  }
+  uint32_t wl[4] = {0, 0, 0, 0}, wh[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    wl[j >> 2] |= (uint32_t)(q[j] & 0xFF) << (8 * (j & 3));
+    wh[j >> 2] |= (uint32_t)((q[j] >> 8) & 0xFF) << (8 * (j & 3));
   }
   auto put = [&](uint8_t* p, int64_t plane, const uint32_t (&l)[4], const uint32_t (&h)[4]) {
     if (full && aligned16(p, plane)) {
@@ -166,7 +172,20 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
     }
   };
   if (op) put(op, e.out_plane, wl, wh);
-  if (op2) put(op2, e.out2_plane, wl2, wh2);
+  if (op2) {
+    uint32_t ml[4] = {0, 0, 0, 0}, mh[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t v = q[j];
+      const int64_t q2 = e.r_identity
+                             ? (v < e.r_qmin ? e.r_qmin : (v > e.r_qmax ? e.r_qmax : v))
+                             : requant_exact(v - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin,
+                                             e.r_qmax);
+      ml[j >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (j & 3));
+      mh[j >> 2] |= (uint32_t)((q2 >> 8) & 0xFF) << (8 * (j & 3));
+    }
+    put(op2, e.out2_plane, ml, mh);
+  }
 }
 
 }  // namespace qa

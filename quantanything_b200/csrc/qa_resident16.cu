@@ -146,6 +146,42 @@ __global__ void quantize_to_planes16_kernel(const float* __restrict__ x, uint8_t
   }
 }
 
+// Four consecutive pixels per thread (pix_stride 4, C <= 4, H*W % 4 == 0):
+// 16-byte reads of each channel plane, 16-byte stores of both output planes.
+__global__ void quantize_to_planes16_x4_kernel(const float* __restrict__ x,
+                                               uint8_t* __restrict__ y, int64_t plane, int C,
+                                               int64_t HW, int64_t quads, double scale,
+                                               double zp, double qmin, double qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < quads; q += stride) {
+    const int64_t p0 = q * 4;
+    const int64_t n = p0 / HW, pix = p0 - n * HW;
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < C) v = __ldg(reinterpret_cast<const float4*>(x + (n * C + c) * HW + pix));
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        double d = zp;
+        if (c < C) {
+          d = rint((double)e[j] / scale) + zp;
+          if (d < qmin) d = qmin;
+          if (qmax < d) d = qmax;
+        }
+        const uint32_t b = (uint32_t)(int32_t)d;
+        lo[j] |= (b & 0xFFu) << (8 * c);
+        hi[j] |= ((b >> 8) & 0xFFu) << (8 * c);
+      }
+    }
+    *reinterpret_cast<uint4*>(y + p0 * 4) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(y + plane + p0 * 4) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  }
+}
+
 // ------------------------------------------------------------------ GAP --
 // y[n, c] = clamp(mbqm(sum_p(x[n,p,c]) - HW*zp_in, m, s) + zp_out)
 // (quant_layers.py:569-590).  One warp per (n, c) run of 32 channels:
@@ -305,6 +341,16 @@ QA_API int qa_quantize_to_planes16_dev(const float* x, void* y, int64_t y_plane,
   }
   const int64_t total = N * H * W * pix_stride;
   if (total == 0) return 0;
+  const int64_t HW = H * W;
+  if (pix_stride == 4 && C <= 4 && HW % 4 == 0 && (y_plane & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    const int64_t quads = N * HW / 4;
+    return launch_ex(quantize_to_planes16_x4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), y_plane, (int)C,
+                     HW, quads, scale, (double)zp, (double)qmin, (double)qmax)
+               ? 0
+               : last_status();
+  }
   return launch_ex(quantize_to_planes16_kernel, dim3(grid_for(total, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), y_plane, N, C,
                    H * W, pix_stride, scale, (double)zp, (double)qmin, (double)qmax)

@@ -708,6 +708,289 @@ bool umma_gemm_i16_i32_into(const int16_t* A, const int16_t* B, int32_t* C, int6
 
 namespace qa {
 
+// Persistent, warp-specialized form of the byte-split kernel for the
+// resident 16-bit layers.  One CTA per SM walks a strided list of
+// (128-row, BN-column) output tiles; roles:
+//   warps 0-3  gather both activation planes of every K-block (cp.async,
+//              one tile row per thread, K-block bytes past K skipped: the
+//              packed weights are zero there);
+//   warp 4     allocates TMEM; lane 0 issues four MMAs per 32-byte K-step
+//              (lo*lo, lo*hi, hi*lo, hi*hi) into one of two accumulator
+//              sets of three int32 accumulators, K-steps past K skipped;
+//   warp 5     lane 0 loads both weight planes of every K-block by TMA;
+//   warps 6-13 two epilogue warpgroups, one per accumulator set (even
+//              tiles / odd tiles; TMEM lane quarter = warp % 4), run the
+//              16-bit epilogue while the MMAs fill the other set.
+// Every mbarrier wait is bounded; on expiry the kernel records
+// kTimeoutCode in the status word, stops issuing work and exits.
+constexpr int kP16Threads = 448;
+constexpr int kP16Stages = 4;
+
+template <int BN>
+struct P16Layout {
+  static constexpr int kAPlane = kBM * kBKBytes;  // 16 KB
+  static constexpr int kBPlane = BN * kBKBytes;
+  static constexpr int kStage = 2 * kAPlane + 2 * kBPlane;
+  static constexpr int kSetCols = 3 * BN;  // one accumulator set
+  static constexpr int kCols = 2 * kSetCols;
+  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
+                                   : kCols <= 256 ? 256 : 512;
+  static_assert(kCols <= 512, "two accumulator sets must fit TMEM");
+  static constexpr size_t kSmem = 1024 + (size_t)kP16Stages * kStage + (2 * kP16Stages + 4) * 8 + 16;
+};
+
+template <int BN, int kChunk>
+__global__ void __launch_bounds__(kP16Threads, 1)
+    umma16_persistent_kernel(const __grid_constant__ ConvTileParams p,
+                             const __grid_constant__ CUtensorMap tmap_b, int64_t n_tiles,
+                             int64_t total_tiles) {
+  using L = P16Layout<BN>;
+  constexpr int S = kP16Stages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_addr(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + S * L::kStage;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (S + s); };
+  auto accf_bar = [&](int b) { return bar_base + 8u * (2 * S + b); };
+  auto acce_bar = [&](int b) { return bar_base + 8u * (2 * S + 2 + b); };
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + S * L::kStage + (2 * S + 4) * 8);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  auto a_tile = [&](int s, int pl) { return base + s * L::kStage + pl * L::kAPlane; };
+  auto b_tile = [&](int s, int pl) {
+    return base + s * L::kStage + 2 * L::kAPlane + pl * L::kBPlane;
+  };
+
+  const int tid = threadIdx.x;
+  const int warp = tid / 32, lane = tid % 32;
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(full_bar(s), kProducerThreads + 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(accf_bar(b), 1);
+      ptx::mbar_init(acce_bar(b), 128);
+    }
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 4) {
+    ptx::tmem_alloc(ptx::smem_addr(s_tmem), L::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  if (warp == 5 && lane == 0) ptx::prefetch_tmap(&tmap_b);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  auto fail = [&]() {
+    *s_abort = 1;
+    if (p.status) atomicExch(p.status, kTimeoutCode);
+  };
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (ptx::mbar_wait(bar, parity, kWaitBudgetCycles)) return true;
+    fail();
+    return false;
+  };
+  const int64_t first = blockIdx.x, step = gridDim.x;
+
+  if (warp < 4) {
+    // ------------------------------------------------ activation gather --
+    const int r = tid;
+    const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    const uint32_t sw = (uint32_t)(r & 7);
+    const int64_t ohw = (int64_t)p.OH * p.OW;
+    int64_t g = 0;
+    for (int64_t t = first; t < total_tiles; t += step) {
+      const int64_t m = (t / n_tiles) * kBM + r;
+      const bool row_ok = m < p.M;
+      int64_t img = 0, iy0 = 0, ix0 = 0;
+      if (row_ok) {
+        img = m / ohw;
+        const int64_t rem = m - img * ohw;
+        const int64_t oy = rem / p.OW, ox = rem - oy * p.OW;
+        iy0 = oy * p.SH - p.PH;
+        ix0 = ox * p.SW - p.PW;
+      }
+      const int64_t img_off = img * (int64_t)p.H * p.W * p.pix_stride;
+      for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+        const int s = (int)(g % S);
+        if (g >= S && !wait(empty_bar(s), (uint32_t)(((g / S) - 1) & 1))) break;
+        const int k0 = kb * kBKBytes;
+        const int kend = p.K - k0 < kBKBytes ? p.K - k0 : kBKBytes;
+        if (row_ok) {
+          int tap = k0 / p.Cin;
+          int c = k0 - tap * p.Cin;
+          int ky = tap / p.KW, kx = tap - (tap / p.KW) * p.KW;
+          for (int kk = 0; kk < kend; kk += kChunk) {
+            const int64_t iy = iy0 + (int64_t)ky * p.DH, ix = ix0 + (int64_t)kx * p.DW;
+            const bool inside = iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
+            const int64_t off = img_off + (iy * p.W + ix) * p.pix_stride + c;
+            const uint32_t soff =
+                row_off + ((((uint32_t)kk >> 4) ^ sw) << 4) + ((uint32_t)kk & 15u);
+#pragma unroll
+            for (int pl = 0; pl < 2; ++pl) {
+              const uint32_t dst = a_tile(s, pl) + soff;
+              if (inside) {
+                if (kChunk == 16)
+                  ptx::cp_async_16(dst, p.a[pl] + off, 16);
+                else
+                  ptx::cp_async_4(dst, p.a[pl] + off, 4);
+              } else if (p.pad_word[pl] != 0u) {
+                // tap outside the image: the raw zero point (centred value 0)
+                uint8_t* d = smem + (dst - base);
+                if (kChunk == 16)
+                  *reinterpret_cast<uint4*>(d) = make_uint4(p.pad_word[pl], p.pad_word[pl],
+                                                            p.pad_word[pl], p.pad_word[pl]);
+                else
+                  *reinterpret_cast<uint32_t*>(d) = p.pad_word[pl];
+              } else {
+                if (kChunk == 16)
+                  ptx::cp_async_16(dst, p.a[pl], 0);
+                else
+                  ptx::cp_async_4(dst, p.a[pl], 0);
+              }
+            }
+            c += kChunk;
+            if (c >= p.Cin) {
+              c = 0;
+              if (++kx == p.KW) {
+                kx = 0;
+                ++ky;
+              }
+            }
+          }
+          if (p.pad_word[0] | p.pad_word[1]) ptx::fence_proxy_async_smem();
+        }
+        ptx::cp_async_mbar_arrive_noinc(full_bar(s));
+      }
+      if (*s_abort) break;
+    }
+    ptx::cp_async_wait_all();
+  } else if (warp == 5) {
+    // ------------------------------------------------- weight TMA loads --
+    if (lane == 0) {
+      int64_t g = 0;
+      for (int64_t t = first; t < total_tiles && !*s_abort; t += step) {
+        const int n0 = (int)(t % n_tiles) * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+          const int s = (int)(g % S);
+          if (g >= S && !wait(empty_bar(s), (uint32_t)(((g / S) - 1) & 1))) break;
+          ptx::mbar_arrive_expect_tx(full_bar(s), 2 * L::kBPlane);
+          ptx::tma_load_2d(b_tile(s, 0), &tmap_b, full_bar(s), kb * kBKBytes, n0);
+          ptx::tma_load_2d(b_tile(s, 1), &tmap_b, full_bar(s), kb * kBKBytes,
+                           p.b_plane_rows + n0);
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      int64_t g = 0, i = 0;
+      for (int64_t t = first; t < total_tiles && !*s_abort; t += step, ++i) {
+        const int b = (int)(i & 1);
+        if (i >= 2 && !wait(acce_bar(b), (uint32_t)(((i >> 1) - 1) & 1))) break;
+        ptx::tc_fence_after();
+        const uint32_t d0 = tmem + (uint32_t)(b * L::kSetCols);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
+          const int s = (int)(g % S);
+          if (!wait(full_bar(s), (uint32_t)((g / S) & 1))) break;
+          ptx::tc_fence_after();
+          const int krem = p.K - kb * kBKBytes;
+          const int ksteps = krem >= kBKBytes ? kBKBytes / 32 : (krem + 31) / 32;
+          for (int kk = 0; kk < ksteps; ++kk) {
+#pragma unroll
+            for (int pa = 0; pa < 2; ++pa) {
+#pragma unroll
+              for (int pb = 0; pb < 2; ++pb) {
+                // accumulator 0 = lo*lo (u8 x u8), 1 = cross products, 2 = hi*hi
+                const bool first_writer = !(pa == 1 && pb == 0);
+                const uint32_t accumulate = (kb > 0 || kk > 0 || !first_writer) ? 1u : 0u;
+                const uint32_t idesc = ptx::idesc_i8(kBM, BN, pa, pb);
+                const uint64_t ad = ptx::smem_desc_sw128(a_tile(s, pa) + kk * 32);
+                const uint64_t bd = ptx::smem_desc_sw128(b_tile(s, pb) + kk * 32);
+                ptx::mma_i8(d0 + (uint32_t)((pa + pb) * BN), ad, bd, idesc, accumulate);
+              }
+            }
+          }
+          ptx::mma_commit(empty_bar(s));
+        }
+        ptx::mma_commit(accf_bar(b));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue --
+    const int b = (warp - 6) / 4;  // this warpgroup's accumulator set
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    int64_t i = b;
+    for (int64_t t = first + b * step; t < total_tiles; t += 2 * step, i += 2) {
+      if (!wait(accf_bar(b), (uint32_t)((i >> 1) & 1))) break;
+      __syncwarp();
+      ptx::tc_fence_after();
+      const int64_t m = (t / n_tiles) * kBM + r;
+      const int n_base = (int)(t % n_tiles) * BN;
+      const bool row_ok = m < p.M;
+      const uint32_t lane_base =
+          tmem + (((uint32_t)quarter * 32u) << 16) + (uint32_t)(b * L::kSetCols);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[3][16];
+#pragma unroll
+        for (int a = 0; a < 3; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
+        ptx::tmem_ld_wait();
+        const int nb = n_base + c0;
+        const int cnt = p.n_valid - nb < 16 ? p.n_valid - nb : 16;
+        if (!row_ok || cnt <= 0) continue;
+        // each partial sum is exact in int32 (K * 255 * 255 < 2^31, host-
+        // checked); the int64 combination is the reference's accumulator
+        int64_t acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          acc[j] = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
+                   (int64_t)(int32_t)v[2][j] * 65536;
+        fused_epilogue_store16_run(p.epi, acc, m, nb, cnt);
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(acce_bar(b));
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+template <int BN, int kChunk>
+bool launch_umma16_persistent(const ConvTileParams& prm, const CUtensorMap& tmap,
+                              int64_t n_tiles, cudaStream_t st) {
+  auto kern = umma16_persistent_kernel<BN, kChunk>;
+  const size_t smem = P16Layout<BN>::kSmem;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (cuda_failed(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem),
+                    "cudaFuncSetAttribute(smem)"))
+      return false;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t m_tiles = (prm.M + kBM - 1) / kBM;
+  const int64_t total = m_tiles * n_tiles;
+  const int64_t grid = total < sm_count() ? total : sm_count();
+  kern<<<(unsigned)grid, kP16Threads, smem, st>>>(prm, tmap, n_tiles, total);
+  return !cuda_failed(cudaGetLastError(), "umma16_persistent_kernel launch");
+}
+
+
 bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);  // qa_resident_ops.cu
 
 namespace {
@@ -722,13 +1005,15 @@ bool launch_conv16(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n
   return launch_umma<BN, 2, 2, kChunk, kEpiFused16, kStages>(prm, tmap, n_tiles, 1, st);
 }
 
+// BN <= 64: the persistent kernel (two accumulator sets of 3 x BN columns
+// fit TMEM); BN = 128: one tile per CTA.
 template <int kChunk>
 bool launch_conv16_bn(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
                       int64_t n_tiles, cudaStream_t st) {
   switch (bn) {
-    case 16: return launch_conv16<16, kChunk>(prm, tmap, n_tiles, st);
-    case 32: return launch_conv16<32, kChunk>(prm, tmap, n_tiles, st);
-    case 64: return launch_conv16<64, kChunk>(prm, tmap, n_tiles, st);
+    case 16: return launch_umma16_persistent<16, kChunk>(prm, tmap, n_tiles, st);
+    case 32: return launch_umma16_persistent<32, kChunk>(prm, tmap, n_tiles, st);
+    case 64: return launch_umma16_persistent<64, kChunk>(prm, tmap, n_tiles, st);
     default: return launch_conv16<128, kChunk>(prm, tmap, n_tiles, st);
   }
 }
