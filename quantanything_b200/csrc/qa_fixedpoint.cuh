@@ -128,4 +128,42 @@ __device__ __forceinline__ int64_t requant_fast(int64_t x, int64_t m, int ts,
   return r > hi ? hi : r;
 }
 
+// clamp(mbqm(x, m, s) + bias, lo, hi) for 0 <= m < 2^31 and
+// 32 <= ts = 31 + s <= 94, exact for every int64 x without 128-bit
+// arithmetic.  With x = xh * 2^32 + xl (xl the unsigned low word),
+//   x * m + 2^(ts-1) = C * 2^32 + low,  0 <= low < 2^32,
+//   C = xh * m + hi32(xl * m) + 2^(ts-33)          (ts >= 33)
+// so floor(. / 2^ts) = C >> (ts - 32): the low word cannot move the floor
+// when ts >= 32.  |C| < 2^62 + 2^61 + 2^31, so nothing overflows.  At
+// ts = 32 the rounding term 2^31 is added to the low product before its
+// high word is taken.
+__device__ __forceinline__ int64_t requant_hi32(int64_t x, int64_t m, int ts, int64_t bias,
+                                                int64_t lo, int64_t hi) {
+  const int64_t xh = x >> 32;
+  const uint64_t xlm = (uint64_t)(uint32_t)x * (uint64_t)m;
+  int64_t r;
+  if (ts == 32) {
+    r = xh * m + (int64_t)((xlm + (1ull << 31)) >> 32);
+  } else {
+    r = (xh * m + (int64_t)(xlm >> 32) + ((int64_t)1 << (ts - 33))) >> (ts - 32);
+  }
+  r += bias;
+  r = r < lo ? lo : r;
+  return r > hi ? hi : r;
+}
+
+__device__ __forceinline__ bool hi32_applies(int64_t m, int64_t ts) {
+  return m >= 0 && m < ((int64_t)1 << 31) && ts >= 32 && ts <= 94;
+}
+
+// mbqm for |x| < 2^31 when |m| < 2^31 and 1 <= ts <= 62 (small_applies):
+// |x * m| + 2^(ts-1) < 2^63, so one 64-bit product is exact.
+__device__ __forceinline__ int64_t mbqm_small(int64_t x, int64_t m, int ts) {
+  return (x * m + ((int64_t)1 << (ts - 1))) >> ts;
+}
+
+__device__ __forceinline__ bool small_applies(int64_t m, int64_t s) {
+  return m > -((int64_t)1 << 31) && m < ((int64_t)1 << 31) && s >= -30 && s <= 31;
+}
+
 }  // namespace qa

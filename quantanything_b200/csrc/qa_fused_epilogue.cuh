@@ -113,8 +113,12 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
   for (int j = 0; j < 16; ++j) {
     const int n = n0 + (j < cnt ? j : 0);
     const int64_t b = e.bias ? __ldg(e.bias + n) : 0;
-    q[j] = requant_exact(acc[j] + b, __ldg(e.mult + n), __ldg(e.shift + n), e.zp, e.qmin,
-                         e.qmax);
+    const int64_t mv = __ldg(e.mult + n), sv = __ldg(e.shift + n);
+    // int16 accumulators pass 2^40: the high-word form when it applies (the
+    // usual positive M0 in [2^30, 2^31)), else the 128-bit mbqm
+    q[j] = hi32_applies(mv, 31 + sv)
+               ? requant_hi32(acc[j] + b, mv, (int)(31 + sv), e.zp, e.qmin, e.qmax)
+               : requant_exact(acc[j] + b, mv, sv, e.zp, e.qmin, e.qmax);
   }
   if (e.lut) {
     int32_t t[16];
@@ -143,12 +147,27 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
 #pragma unroll
       for (int j = 0; j < 16; ++j) a[j] = plane16_value(rp + (j < cnt ? j : 0), e.res_plane);
     }
+    // both terms are int16-range values times multipliers: one 64-bit
+    // product each when the multipliers and shifts allow it
+    const bool small = small_applies(e.ma, e.sa) && small_applies(e.mb, e.sb) &&
+                       e.za > -32768 && e.za < 32768 && e.zb > -32768 && e.zb < 32768;
+    if (small) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const I128 ta = mbqm(a[j] - e.za, e.ma, e.sa);
-      I128 tb = mbqm(q[j] - e.zb, e.mb, e.sb);
-      if (e.sign < 0) tb = neg_i128(tb);
-      q[j] = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
+      for (int j = 0; j < 16; ++j) {
+        const int64_t ta = mbqm_small(a[j] - e.za, e.ma, (int)(31 + e.sa));
+        const int64_t tb = mbqm_small(q[j] - e.zb, e.mb, (int)(31 + e.sb));
+        int64_t v = ta + (e.sign < 0 ? -tb : tb) + e.add_zo;
+        v = v < e.add_qmin ? e.add_qmin : v;
+        q[j] = v > e.add_qmax ? e.add_qmax : v;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const I128 ta = mbqm(a[j] - e.za, e.ma, e.sa);
+        I128 tb = mbqm(q[j] - e.zb, e.mb, e.sb);
+        if (e.sign < 0) tb = neg_i128(tb);
+        q[j] = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
+      }
     }
   }
   uint32_t wl[4] = {0, 0, 0, 0}, wh[4] = {0, 0, 0, 0};
@@ -177,10 +196,15 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int64_t v = q[j];
-      const int64_t q2 = e.r_identity
-                             ? (v < e.r_qmin ? e.r_qmin : (v > e.r_qmax ? e.r_qmax : v))
-                             : requant_exact(v - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin,
-                                             e.r_qmax);
+      int64_t q2;
+      if (e.r_identity) {
+        q2 = v < e.r_qmin ? e.r_qmin : (v > e.r_qmax ? e.r_qmax : v);
+      } else if (small_applies(e.r_m, e.r_s) && e.r_zp_in > -32768 && e.r_zp_in < 32768) {
+        q2 = mbqm_small(v - e.r_zp_in, e.r_m, (int)(31 + e.r_s)) + e.r_zp_out;
+        q2 = q2 < e.r_qmin ? e.r_qmin : (q2 > e.r_qmax ? e.r_qmax : q2);
+      } else {
+        q2 = requant_exact(v - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
+      }
       ml[j >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (j & 3));
       mh[j >> 2] |= (uint32_t)((q2 >> 8) & 0xFF) << (8 * (j & 3));
     }
