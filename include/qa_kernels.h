@@ -343,6 +343,10 @@ int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_signed, in
 typedef struct qa_fused_conv16_desc {
   qa_fused_conv_desc base;
   int64_t x_plane, res_plane, out_plane, out2_plane;
+  /* optional: base.lut's entries as int16 (every entry in int16 range,
+   * base.lut_len <= 65536); dense layers then keep the table in shared
+   * memory */
+  const int16_t* lut16;
 } qa_fused_conv16_desc;
 
 int qa_conv16_fused_dev(const qa_fused_conv16_desc* desc, void* stream);

@@ -97,9 +97,12 @@ __device__ __forceinline__ bool aligned16(const uint8_t* p, int64_t plane) {
   return ((reinterpret_cast<uintptr_t>(p) | (uint64_t)plane) & 15) == 0;
 }
 
+// s_lut: the activation table in shared memory (int16 entries), or null to
+// read e.lut from global memory.
 __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& e,
                                                            const int64_t (&acc)[16], int64_t m,
-                                                           int n0, int cnt) {
+                                                           int n0, int cnt,
+                                                           const int16_t* s_lut = nullptr) {
   // Phased so that the independent loads of the sixteen channels are in
   // flight together: channel parameters, then requantize, then the sixteen
   // table lookups, then the residual terms and the stores.  Columns past
@@ -126,7 +129,7 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
     for (int j = 0; j < 16; ++j) {
       int64_t idx = q[j] - e.lut_offset;
       idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
-      t[j] = __ldg(e.lut + idx);
+      t[j] = s_lut ? (int32_t)s_lut[idx] : __ldg(e.lut + idx);
     }
 #pragma unroll
     for (int j = 0; j < 16; ++j) q[j] = t[j];

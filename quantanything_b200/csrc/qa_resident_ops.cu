@@ -68,6 +68,8 @@ bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d) {
   e.r_zp_out = d.r_zp_out;
   e.r_qmin = d.r_qmin;
   e.r_qmax = d.r_qmax;
+  e.res_plane = e.out_plane = e.out2_plane = 0;
+  e.lut16 = nullptr;
   return true;
 }
 

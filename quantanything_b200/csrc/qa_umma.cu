@@ -721,13 +721,18 @@ namespace qa {
 //   warps 6-13 two epilogue warpgroups, one per accumulator set (even
 //              tiles / odd tiles; TMEM lane quarter = warp % 4), run the
 //              16-bit epilogue while the MMAs fill the other set.
+// kSmemLut: the layer's activation table (65536 int16 entries at most) is
+// copied into shared memory at the start, so each lookup is a shared-memory
+// read (a few bank conflicts) instead of a gather of 32 L1 sectors per warp;
+// the table takes 128 KB, so such layers run two stages instead of four.
 // Every mbarrier wait is bounded; on expiry the kernel records
 // kTimeoutCode in the status word, stops issuing work and exits.
 constexpr int kP16Threads = 448;
-constexpr int kP16Stages = 4;
+constexpr int kP16LutEntries = 65536;
 
-template <int BN>
+template <int BN, bool kSmemLut>
 struct P16Layout {
+  static constexpr int kStages = kSmemLut ? 2 : 4;
   static constexpr int kAPlane = kBM * kBKBytes;  // 16 KB
   static constexpr int kBPlane = BN * kBKBytes;
   static constexpr int kStage = 2 * kAPlane + 2 * kBPlane;
@@ -736,26 +741,30 @@ struct P16Layout {
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                    : kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "two accumulator sets must fit TMEM");
-  static constexpr size_t kSmem = 1024 + (size_t)kP16Stages * kStage + (2 * kP16Stages + 4) * 8 + 16;
+  static constexpr int kLutBytes = kSmemLut ? kP16LutEntries * 2 : 0;
+  static constexpr size_t kBarOff = (size_t)kStages * kStage + kLutBytes;
+  static constexpr size_t kSmem = 1024 + kBarOff + (2 * kStages + 4) * 8 + 16;
+  static_assert(kSmem <= 232448, "shared memory per CTA");
 };
 
-template <int BN, int kChunk>
+template <int BN, int kChunk, bool kSmemLut>
 __global__ void __launch_bounds__(kP16Threads, 1)
     umma16_persistent_kernel(const __grid_constant__ ConvTileParams p,
                              const __grid_constant__ CUtensorMap tmap_b, int64_t n_tiles,
                              int64_t total_tiles) {
-  using L = P16Layout<BN>;
-  constexpr int S = kP16Stages;
+  using L = P16Layout<BN, kSmemLut>;
+  constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_addr(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
-  const uint32_t bar_base = base + S * L::kStage;
+  const uint32_t bar_base = base + (uint32_t)L::kBarOff;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (S + s); };
   auto accf_bar = [&](int b) { return bar_base + 8u * (2 * S + b); };
   auto acce_bar = [&](int b) { return bar_base + 8u * (2 * S + 2 + b); };
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + S * L::kStage + (2 * S + 4) * 8);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kBarOff + (2 * S + 4) * 8);
+  int16_t* s_lut = reinterpret_cast<int16_t*>(smem + (size_t)S * L::kStage);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   auto a_tile = [&](int s, int pl) { return base + s * L::kStage + pl * L::kAPlane; };
   auto b_tile = [&](int s, int pl) {
@@ -781,6 +790,13 @@ __global__ void __launch_bounds__(kP16Threads, 1)
     ptx::tmem_relinquish();
   }
   if (warp == 5 && lane == 0) ptx::prefetch_tmap(&tmap_b);
+  if constexpr (kSmemLut) {
+    // the host guarantees lut_len <= 65536 and a 16-byte aligned table
+    const int64_t n16 = (p.epi.lut_len * 2 + 15) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(p.epi.lut16);
+    uint4* dst = reinterpret_cast<uint4*>(s_lut);
+    for (int64_t i = tid; i < n16; i += kP16Threads) dst[i] = __ldg(src + i);
+  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -800,23 +816,28 @@ __global__ void __launch_bounds__(kP16Threads, 1)
 
   if (warp < 4) {
     // ------------------------------------------------ activation gather --
+    // offsets within one image fit 32 bits (host-checked H*W*pix_stride)
     const int r = tid;
     const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t sw = (uint32_t)(r & 7);
     const int64_t ohw = (int64_t)p.OH * p.OW;
+    const int pix_stride = (int)p.pix_stride;
     int64_t g = 0;
     for (int64_t t = first; t < total_tiles; t += step) {
       const int64_t m = (t / n_tiles) * kBM + r;
       const bool row_ok = m < p.M;
-      int64_t img = 0, iy0 = 0, ix0 = 0;
+      int iy0 = 0, ix0 = 0;
+      const uint8_t* src[2] = {p.a[0], p.a[1]};
       if (row_ok) {
-        img = m / ohw;
-        const int64_t rem = m - img * ohw;
-        const int64_t oy = rem / p.OW, ox = rem - oy * p.OW;
+        const int64_t img = m / ohw;
+        const int rem = (int)(m - img * ohw);
+        const int oy = rem / p.OW, ox = rem - (rem / p.OW) * p.OW;
         iy0 = oy * p.SH - p.PH;
         ix0 = ox * p.SW - p.PW;
+        const int64_t img_off = img * (int64_t)p.H * p.W * p.pix_stride;
+        src[0] += img_off;
+        src[1] += img_off;
       }
-      const int64_t img_off = img * (int64_t)p.H * p.W * p.pix_stride;
       for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
         const int s = (int)(g % S);
         if (g >= S && !wait(empty_bar(s), (uint32_t)(((g / S) - 1) & 1))) break;
@@ -827,9 +848,9 @@ __global__ void __launch_bounds__(kP16Threads, 1)
           int c = k0 - tap * p.Cin;
           int ky = tap / p.KW, kx = tap - (tap / p.KW) * p.KW;
           for (int kk = 0; kk < kend; kk += kChunk) {
-            const int64_t iy = iy0 + (int64_t)ky * p.DH, ix = ix0 + (int64_t)kx * p.DW;
+            const int iy = iy0 + ky * p.DH, ix = ix0 + kx * p.DW;
             const bool inside = iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
-            const int64_t off = img_off + (iy * p.W + ix) * p.pix_stride + c;
+            const int off = (iy * p.W + ix) * pix_stride + c;
             const uint32_t soff =
                 row_off + ((((uint32_t)kk >> 4) ^ sw) << 4) + ((uint32_t)kk & 15u);
 #pragma unroll
@@ -837,9 +858,9 @@ __global__ void __launch_bounds__(kP16Threads, 1)
               const uint32_t dst = a_tile(s, pl) + soff;
               if (inside) {
                 if (kChunk == 16)
-                  ptx::cp_async_16(dst, p.a[pl] + off, 16);
+                  ptx::cp_async_16(dst, src[pl] + off, 16);
                 else
-                  ptx::cp_async_4(dst, p.a[pl] + off, 4);
+                  ptx::cp_async_4(dst, src[pl] + off, 4);
               } else if (p.pad_word[pl] != 0u) {
                 // tap outside the image: the raw zero point (centred value 0)
                 uint8_t* d = smem + (dst - base);
@@ -890,6 +911,16 @@ __global__ void __launch_bounds__(kP16Threads, 1)
   } else if (warp == 4) {
     // ------------------------------------------------------- MMA issuer --
     if (lane == 0) {
+      // descriptors formed once; a stage / plane / K-step offset moves only
+      // the 14-bit start-address field (shared addresses stay below 256 KB)
+      const uint64_t a_desc0 = ptx::smem_desc_sw128(a_tile(0, 0));
+      const uint64_t b_desc0 = ptx::smem_desc_sw128(b_tile(0, 0));
+      constexpr uint64_t kAPl = L::kAPlane >> 4, kBPl = L::kBPlane >> 4;
+      // lo*lo (u8 x u8) -> acc 0; lo*hi, hi*lo -> acc 1; hi*hi (s8 x s8) -> acc 2
+      constexpr uint32_t id_ll = ptx::idesc_i8(kBM, BN, 0, 0);
+      constexpr uint32_t id_lh = ptx::idesc_i8(kBM, BN, 0, 1);
+      constexpr uint32_t id_hl = ptx::idesc_i8(kBM, BN, 1, 0);
+      constexpr uint32_t id_hh = ptx::idesc_i8(kBM, BN, 1, 1);
       int64_t g = 0, i = 0;
       for (int64_t t = first; t < total_tiles && !*s_abort; t += step, ++i) {
         const int b = (int)(i & 1);
@@ -902,20 +933,16 @@ __global__ void __launch_bounds__(kP16Threads, 1)
           ptx::tc_fence_after();
           const int krem = p.K - kb * kBKBytes;
           const int ksteps = krem >= kBKBytes ? kBKBytes / 32 : (krem + 31) / 32;
+          const uint64_t so = (uint64_t)((uint32_t)(s * L::kStage) >> 4);
+          const uint64_t al = a_desc0 + so, bl = b_desc0 + so;
+#pragma unroll 4
           for (int kk = 0; kk < ksteps; ++kk) {
-#pragma unroll
-            for (int pa = 0; pa < 2; ++pa) {
-#pragma unroll
-              for (int pb = 0; pb < 2; ++pb) {
-                // accumulator 0 = lo*lo (u8 x u8), 1 = cross products, 2 = hi*hi
-                const bool first_writer = !(pa == 1 && pb == 0);
-                const uint32_t accumulate = (kb > 0 || kk > 0 || !first_writer) ? 1u : 0u;
-                const uint32_t idesc = ptx::idesc_i8(kBM, BN, pa, pb);
-                const uint64_t ad = ptx::smem_desc_sw128(a_tile(s, pa) + kk * 32);
-                const uint64_t bd = ptx::smem_desc_sw128(b_tile(s, pb) + kk * 32);
-                ptx::mma_i8(d0 + (uint32_t)((pa + pb) * BN), ad, bd, idesc, accumulate);
-              }
-            }
+            const uint64_t a0 = al + (uint64_t)(kk * 2), b0 = bl + (uint64_t)(kk * 2);
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            ptx::mma_i8(d0, a0, b0, id_ll, acc);
+            ptx::mma_i8(d0 + BN, a0, b0 + kBPl, id_lh, acc);
+            ptx::mma_i8(d0 + BN, a0 + kAPl, b0, id_hl, 1u);
+            ptx::mma_i8(d0 + 2 * BN, a0 + kAPl, b0 + kBPl, id_hh, acc);
           }
           ptx::mma_commit(empty_bar(s));
         }
@@ -953,7 +980,7 @@ __global__ void __launch_bounds__(kP16Threads, 1)
         for (int j = 0; j < 16; ++j)
           acc[j] = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
                    (int64_t)(int32_t)v[2][j] * 65536;
-        fused_epilogue_store16_run(p.epi, acc, m, nb, cnt);
+        fused_epilogue_store16_run(p.epi, acc, m, nb, cnt, kSmemLut ? s_lut : nullptr);
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(acce_bar(b));
@@ -968,11 +995,11 @@ __global__ void __launch_bounds__(kP16Threads, 1)
   }
 }
 
-template <int BN, int kChunk>
+template <int BN, int kChunk, bool kSmemLut>
 bool launch_umma16_persistent(const ConvTileParams& prm, const CUtensorMap& tmap,
                               int64_t n_tiles, cudaStream_t st) {
-  auto kern = umma16_persistent_kernel<BN, kChunk>;
-  const size_t smem = P16Layout<BN>::kSmem;
+  auto kern = umma16_persistent_kernel<BN, kChunk, kSmemLut>;
+  const size_t smem = P16Layout<BN, kSmemLut>::kSmem;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1007,15 +1034,26 @@ bool launch_conv16(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n
 
 // BN <= 64: the persistent kernel (two accumulator sets of 3 x BN columns
 // fit TMEM); BN = 128: one tile per CTA.
+template <int kChunk, bool kSmemLut>
+bool launch_conv16_lut(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
+                       int64_t n_tiles, cudaStream_t st) {
+  switch (bn) {
+    case 16: return launch_umma16_persistent<16, kChunk, kSmemLut>(prm, tmap, n_tiles, st);
+    case 32: return launch_umma16_persistent<32, kChunk, kSmemLut>(prm, tmap, n_tiles, st);
+    default: return launch_umma16_persistent<64, kChunk, kSmemLut>(prm, tmap, n_tiles, st);
+  }
+}
+
 template <int kChunk>
 bool launch_conv16_bn(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
                       int64_t n_tiles, cudaStream_t st) {
-  switch (bn) {
-    case 16: return launch_umma16_persistent<16, kChunk>(prm, tmap, n_tiles, st);
-    case 32: return launch_umma16_persistent<32, kChunk>(prm, tmap, n_tiles, st);
-    case 64: return launch_umma16_persistent<64, kChunk>(prm, tmap, n_tiles, st);
-    default: return launch_conv16<128, kChunk>(prm, tmap, n_tiles, st);
-  }
+  if (bn == 128) return launch_conv16<128, kChunk>(prm, tmap, n_tiles, st);
+  // the kernel copies the table in 16-byte pieces
+  const bool smem_lut = prm.epi.lut && prm.epi.lut16 && prm.epi.lut_len <= kP16LutEntries &&
+                        prm.epi.lut_len % 8 == 0 &&
+                        (reinterpret_cast<uintptr_t>(prm.epi.lut16) & 15) == 0;
+  return smem_lut ? launch_conv16_lut<kChunk, true>(bn, prm, tmap, n_tiles, st)
+                  : launch_conv16_lut<kChunk, false>(bn, prm, tmap, n_tiles, st);
 }
 
 }  // namespace
@@ -1039,6 +1077,10 @@ bool umma_conv16_fused(const qa_fused_conv16_desc& d16, cudaStream_t st) {
   // each 8-bit partial product sum must stay exact in its int32 accumulator
   if (K * 255 * 255 >= (int64_t(1) << 31)) {
     set_error(kUnsupported, "qa_conv16_fused_dev: K too large for exact int32 partial sums");
+    return false;
+  }
+  if (d.H * d.W * d.x_pix_stride >= (int64_t(1) << 31) || d.OH * d.OW >= (int64_t(1) << 31)) {
+    set_error(kUnsupported, "qa_conv16_fused_dev: image too large");
     return false;
   }
   const int64_t M = d.N * d.OH * d.OW;
@@ -1074,6 +1116,7 @@ bool umma_conv16_fused(const qa_fused_conv16_desc& d16, cudaStream_t st) {
   prm.epi.res_plane = d16.res_plane;
   prm.epi.out_plane = d16.out_plane;
   prm.epi.out2_plane = d16.out2_plane;
+  prm.epi.lut16 = d16.lut16;
   CUtensorMap tmap;
   if (!make_weight_tmap(&tmap, d.w, 2 * d.w_rows, d.w_kp, (int)bn)) return false;
   const bool wide = d.C % 16 == 0 && d.x_pix_stride % 16 == 0 && (xa & 15) == 0 &&

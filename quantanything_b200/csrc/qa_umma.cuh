@@ -51,6 +51,7 @@ struct FusedEpilogue {
   // 16-bit layers: bytes from each low plane (res, out, out2) to its high
   // plane (v = lo + 256 * (int8)hi); unused by the 8-bit epilogue
   int64_t res_plane, out_plane, out2_plane;
+  const int16_t* lut16;  // 16-bit layers: the table as int16 (shared-memory copy)
 };
 
 // ABI routes (host-pointer entry points, operands already on the device).

@@ -47,7 +47,7 @@ class FusedConv16Desc(ctypes.Structure):
     """ctypes mirror of ``qa_fused_conv16_desc`` (include/qa_kernels.h)."""
 
     _fields_ = [("base", FusedConvDesc), ("x_plane", _I64), ("res_plane", _I64),
-                ("out_plane", _I64), ("out2_plane", _I64)]
+                ("out_plane", _I64), ("out2_plane", _I64), ("lut16", _P)]
 
 
 _DEV16_SIGNATURES = {
@@ -85,6 +85,7 @@ class ResidentNet16(ResidentNet):
 
     def __init__(self, container, batch, device=None):
         self._planes = []  # (low plane start, plane bytes) of every allocation
+        self._lut16 = {}   # int32 table address -> int16 device copy
         super().__init__(container, batch, device, fuse_input=False)
         device_api16(self.lib)
         self._descs = {}
@@ -125,8 +126,24 @@ class ResidentNet16(ResidentNet):
             d16.res_plane = self._plane_of(d.res) if d.res else 0
             d16.out_plane = self._plane_of(d.out) if d.out else 0
             d16.out2_plane = self._plane_of(d.out2) if d.out2 else 0
+            lut = self._lut_as_int16(d.lut, d.lut_len) if d.lut else None
+            d16.lut16 = lut.data_ptr() if lut is not None else None
             self._descs[id(step)] = d16
         return d16
+
+    def _lut_as_int16(self, ptr, n):
+        """int16 copy of a planned int32 activation table (the kernel keeps
+        it in shared memory), or None when it does not fit int16.  Made on
+        the first (eager) launch, never inside a graph capture."""
+        if ptr in self._lut16:
+            return self._lut16[ptr]
+        src = next(t for t in self._keep if t.data_ptr() == ptr)
+        t = None
+        if n <= 65536 and int(src.min()) >= -32768 and int(src.max()) <= 32767:
+            t = src.to(torch.int16)
+            self._keep.append(t)
+        self._lut16[ptr] = t
+        return t
 
     # ----------------------------------------------------------- launch --
     def _launch_all(self, stream, on_step=None):
