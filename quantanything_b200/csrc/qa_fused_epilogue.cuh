@@ -89,6 +89,22 @@ __device__ __forceinline__ void fused_epilogue_store16(const FusedEpilogue& e, i
   }
 }
 
+// Out-of-line exact forms for the rare channels / layers the 64-bit forms
+// do not cover (keeps the unrolled hot loop small).
+__device__ __noinline__ inline int64_t requant_exact_cold(int64_t x, int64_t m, int64_t s,
+                                                          int64_t bias, int64_t lo,
+                                                          int64_t hi) {
+  return requant_exact(x, m, s, bias, lo, hi);
+}
+
+__device__ __noinline__ inline int64_t add_exact_cold(const FusedEpilogue& e, int64_t a,
+                                                      int64_t q) {
+  const I128 ta = mbqm(a - e.za, e.ma, e.sa);
+  I128 tb = mbqm(q - e.zb, e.mb, e.sb);
+  if (e.sign < 0) tb = neg_i128(tb);
+  return clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
+}
+
 // Sixteen consecutive output channels n0 .. n0 + cnt - 1 (cnt <= 16) of
 // pixel m: the per-element sequence of fused_epilogue_store16, with the
 // residual read and both planes of each output stored 16 bytes at a time
@@ -121,7 +137,7 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
     // usual positive M0 in [2^30, 2^31)), else the 128-bit mbqm
     q[j] = hi32_applies(mv, 31 + sv)
                ? requant_hi32(acc[j] + b, mv, (int)(31 + sv), e.zp, e.qmin, e.qmax)
-               : requant_exact(acc[j] + b, mv, sv, e.zp, e.qmin, e.qmax);
+               : requant_exact_cold(acc[j] + b, mv, sv, e.zp, e.qmin, e.qmax);
   }
   if (e.lut) {
     int32_t t[16];
@@ -164,13 +180,7 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
         q[j] = v > e.add_qmax ? e.add_qmax : v;
       }
     } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const I128 ta = mbqm(a[j] - e.za, e.ma, e.sa);
-        I128 tb = mbqm(q[j] - e.zb, e.mb, e.sb);
-        if (e.sign < 0) tb = neg_i128(tb);
-        q[j] = clamp_i128(add_i128_i64(add_i128(ta, tb), e.add_zo), e.add_qmin, e.add_qmax);
-      }
+      for (int j = 0; j < 16; ++j) q[j] = add_exact_cold(e, a[j], q[j]);
     }
   }
   uint32_t wl[4] = {0, 0, 0, 0}, wh[4] = {0, 0, 0, 0};
@@ -206,7 +216,7 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
         q2 = mbqm_small(v - e.r_zp_in, e.r_m, (int)(31 + e.r_s)) + e.r_zp_out;
         q2 = q2 < e.r_qmin ? e.r_qmin : (q2 > e.r_qmax ? e.r_qmax : q2);
       } else {
-        q2 = requant_exact(v - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
+        q2 = requant_exact_cold(v - e.r_zp_in, e.r_m, e.r_s, e.r_zp_out, e.r_qmin, e.r_qmax);
       }
       ml[j >> 2] |= (uint32_t)(q2 & 0xFF) << (8 * (j & 3));
       mh[j >> 2] |= (uint32_t)((q2 >> 8) & 0xFF) << (8 * (j & 3));

@@ -67,6 +67,34 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// try_wait with a suspend-time hint: the warp may sleep in hardware until
+// the phase completes or `hint_ns` elapses, instead of spinning on issue
+// slots that other warps of the CTA need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait built on mbar_try_wait_sleep (same budget semantics as
+// mbar_wait).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity,
+                                                uint64_t budget_cycles) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if ((uint64_t)(clock64() - t0) > budget_cycles) return false;
+  }
+}
+
 // One arrival on `bar` once every cp.async this thread issued before has
 // landed in shared memory (the count is not raised first: the barrier's
 // expected count must include this arrival).  The completed copies are

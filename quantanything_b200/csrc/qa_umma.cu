@@ -808,7 +808,7 @@ __global__ void __launch_bounds__(kP16Threads, 1)
   };
   auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
     if (*s_abort) return false;
-    if (ptx::mbar_wait(bar, parity, kWaitBudgetCycles)) return true;
+    if (ptx::mbar_wait_sleep(bar, parity, kWaitBudgetCycles)) return true;
     fail();
     return false;
   };
