@@ -815,7 +815,7 @@ __global__ void __launch_bounds__(kInThreads, 2)
     const int img = t / (p.tiles_x * p.tiles_y), r = t - img * p.tiles_x * p.tiles_y;
     const int oy0 = (r / p.tiles_x) * kInTileH, ox0 = (r % p.tiles_x) * kInTileW;
     const int s = k % kInStages;
-    if (!ptx::mbar_wait(bar0 + 8u * s, (k / kInStages) & 1, kInBudget)) {
+    if (!ptx::mbar_wait_sleep(bar0 + 8u * s, (k / kInStages) & 1, kInBudget)) {
       *s_abort = 1;
       if (p.status) atomicExch(p.status, 0x7003);
     }
@@ -882,7 +882,7 @@ __global__ void __launch_bounds__(kInThreads, 2)
       ptx::mma_commit(mma_bar);
       ++mmas;
     }
-    if (!ptx::mbar_wait(mma_bar, k & 1, kInBudget)) {
+    if (!ptx::mbar_wait_sleep(mma_bar, k & 1, kInBudget)) {
       *s_abort = 1;
       if (p.status) atomicExch(p.status, 0x7003);
     }

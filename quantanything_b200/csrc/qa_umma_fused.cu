@@ -343,7 +343,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
 
   auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
     if (*s_abort) return false;
-    if (ptx::mbar_wait(bar, parity, kBudgetCycles)) return true;
+    if (ptx::mbar_wait_sleep(bar, parity, kBudgetCycles)) return true;
     *s_abort = 1;
     if (p.status) atomicExch(p.status, kTimeoutCode);
     return false;
