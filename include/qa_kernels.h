@@ -338,8 +338,10 @@ int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_signed, in
  * grouped / depthwise layers run on CUDA cores.  The epilogue is the 8-bit
  * one's layer sequence (requantize with the exact 128-bit mbqm, activation
  * LUT of 65536 entries, residual Add, rescaled Concat copy) on int16 values.
- * base.x_signed, res_signed must be 1; base.fast and the pad_corr fields are
- * ignored (out-of-image taps read the raw zero point). */
+ * base.x_signed, res_signed must be 1; base.fast = 1 asserts that every
+ * channel has 0 <= mult < 2^31 and 32 <= 31 + shift <= 94 (the requantize
+ * then skips its per-channel check); the pad_corr fields are ignored
+ * (out-of-image taps read the raw zero point). */
 typedef struct qa_fused_conv16_desc {
   qa_fused_conv_desc base;
   int64_t x_plane, res_plane, out_plane, out2_plane;

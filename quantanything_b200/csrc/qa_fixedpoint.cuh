@@ -139,13 +139,17 @@ __device__ __forceinline__ int64_t requant_fast(int64_t x, int64_t m, int ts,
 // high word is taken.
 __device__ __forceinline__ int64_t requant_hi32(int64_t x, int64_t m, int ts, int64_t bias,
                                                 int64_t lo, int64_t hi) {
-  const int64_t xh = x >> 32;
-  const uint64_t xlm = (uint64_t)(uint32_t)x * (uint64_t)m;
+  // x >> 32 always fits int32 and 0 <= m < 2^31: both partial products are
+  // single 32 x 32 -> 64-bit multiplies
+  const int32_t xh = (int32_t)(x >> 32);
+  const int32_t m32 = (int32_t)m;
+  const int64_t a = (int64_t)xh * (int64_t)m32;
+  const uint64_t xlm = (uint64_t)(uint32_t)x * (uint64_t)(uint32_t)m32;
   int64_t r;
   if (ts == 32) {
-    r = xh * m + (int64_t)((xlm + (1ull << 31)) >> 32);
+    r = a + (int64_t)((xlm + (1ull << 31)) >> 32);
   } else {
-    r = (xh * m + (int64_t)(xlm >> 32) + ((int64_t)1 << (ts - 33))) >> (ts - 32);
+    r = (a + (int64_t)(xlm >> 32) + ((int64_t)1 << (ts - 33))) >> (ts - 32);
   }
   r += bias;
   r = r < lo ? lo : r;

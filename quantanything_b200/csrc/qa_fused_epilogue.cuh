@@ -134,8 +134,9 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
     const int64_t b = e.bias ? __ldg(e.bias + n) : 0;
     const int64_t mv = __ldg(e.mult + n), sv = __ldg(e.shift + n);
     // int16 accumulators pass 2^40: the high-word form when it applies (the
-    // usual positive M0 in [2^30, 2^31)), else the 128-bit mbqm
-    q[j] = hi32_applies(mv, 31 + sv)
+    // usual positive M0 in [2^30, 2^31); e.fast: the host proved it for every
+    // channel of the layer), else the 128-bit mbqm
+    q[j] = (e.fast || hi32_applies(mv, 31 + sv))
                ? requant_hi32(acc[j] + b, mv, (int)(31 + sv), e.zp, e.qmin, e.qmax)
                : requant_exact_cold(acc[j] + b, mv, sv, e.zp, e.qmin, e.qmax);
   }

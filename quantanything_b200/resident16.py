@@ -109,6 +109,17 @@ class ResidentNet16(ResidentNet):
                 return plane
         raise AssertionError(f"address {ptr:#x} is not in a planned 16-bit tensor")
 
+    def _plan_contraction(self, layer, layers, fused_away, patch=0):
+        super()._plan_contraction(layer, layers, fused_away, patch)
+        # desc.fast (16-bit meaning): every channel takes the kernel's exact
+        # high-word requantize, 0 <= M0 < 2^31 and 32 <= 31 + shift <= 94
+        step = self.steps[-1][1]
+        cout = int(step.desc.Cout)
+        mult = np.broadcast_to(np.asarray(layer.q_mult, np.int64), (cout,))
+        ts = 31 + np.broadcast_to(np.asarray(layer.shift, np.int64), (cout,))
+        step.desc.fast = int(bool(np.all((mult >= 0) & (mult < 2**31) & (ts >= 32)
+                                         & (ts <= 94))))
+
     def _upload_weights(self, packed):
         # [rows, kp] int16 -> [2][rows][kp] bytes: low plane, then high plane
         v = packed.astype(np.int64)
