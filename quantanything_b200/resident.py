@@ -889,6 +889,40 @@ class ResidentNet:
         out_pinned.copy_(y, non_blocking=True)
         return out_pinned
 
+    def run_pipelined(self, xs_pinned, outs_pinned):
+        """Host-to-host forwards of a sequence of pinned float32 batches, each
+        batch's host->device copy overlapped with the previous batch's
+        forward: the copies run on a side stream into two alternating staging
+        buffers; the current stream waits for its batch, moves it into the
+        input buffer (device to device), replays the captured forward and
+        copies the float32 result into ``outs_pinned[i]``.  Everything is
+        enqueued; the outputs are valid after the current stream
+        synchronizes."""
+        if len(xs_pinned) != len(outs_pinned):
+            raise ValueError("one output buffer per input batch")
+        comp = torch.cuda.current_stream(self.device)
+        if getattr(self, "_copy_stream", None) is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+            self._staging = [torch.empty_like(self.x_dev) for _ in range(2)]
+            self._copied = [torch.cuda.Event() for _ in range(2)]
+            self._consumed = [torch.cuda.Event() for _ in range(2)]
+        cs = self._copy_stream
+        start = torch.cuda.Event()
+        start.record(comp)
+        cs.wait_event(start)  # nothing of this call starts before the caller's work
+        for i, (x, out) in enumerate(zip(xs_pinned, outs_pinned)):
+            b = i % 2
+            with torch.cuda.stream(cs):
+                if i >= 2:
+                    cs.wait_event(self._consumed[b])  # staging b was moved out
+                self._staging[b].copy_(x, non_blocking=True)
+                self._copied[b].record(cs)
+            comp.wait_event(self._copied[b])
+            self.x_dev.copy_(self._staging[b], non_blocking=True)
+            self._consumed[b].record(comp)
+            out.copy_(self.replay(), non_blocking=True)
+        return outs_pinned
+
     def run(self, x_host, out=None):
         """Public host-to-host call: copies ``x_host`` (float32 NCHW) in,
         runs the captured forward, returns the float32 output on the host."""

@@ -129,3 +129,18 @@ def test_wide_weights_are_rejected_cleanly(gpu_lib):
 
     with pytest.raises(UnsupportedGraph):
         _net("yolo_mini_int16", gpu_lib, 2)
+
+
+def test_pipelined_host_calls_match_single_runs(gpu_lib):
+    """run_pipelined (copies of batch i+1 overlapped with the forward of
+    batch i through two staging buffers) returns, per batch, exactly what
+    run() returns for that batch alone."""
+    net, _, _ = _net("yolov8n_cls_int8", gpu_lib, 4)
+    xs = [networks.images(4, 224, seed=40 + i) for i in range(5)]
+    want = [net.run(x).copy() for x in xs]
+    xs_pinned = [torch.from_numpy(x).pin_memory() for x in xs]
+    outs = [torch.empty((4, 1000), dtype=torch.float32).pin_memory() for _ in xs]
+    net.run_pipelined(xs_pinned, outs)
+    torch.cuda.current_stream().synchronize()
+    for w, o in zip(want, outs):
+        np.testing.assert_array_equal(o.numpy(), w)
