@@ -203,6 +203,51 @@ __global__ void gap16_kernel(Planes16 x, int64_t N, int64_t HW, int64_t C, int64
   }
 }
 
+// Warp per (image, 16-channel group), as gap16ch_kernel of the 8-bit
+// kernels: lanes take pixels, 16-byte loads of both planes, int64 partial
+// sums reduced by shuffles, lane c (c < 16) requantizes channel c.
+__global__ void gap16_planes_kernel(Planes16 x, int64_t N, int64_t HW, int64_t C, int64_t zp_in,
+                                    int64_t m, int64_t s, int64_t zp_out, int64_t qmin,
+                                    int64_t qmax, uint8_t* __restrict__ y, int64_t y_plane,
+                                    int64_t y_pix_stride) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t groups = C / 16;
+  const int64_t warps = N * groups;
+  const int64_t wstride = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < warps;
+       w += wstride) {
+    const int64_t n = w / groups, g = w - n * groups;
+    const uint8_t* base = x.p + n * HW * x.stride + g * 16;
+    int64_t acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0;
+    for (int64_t p = lane; p < HW; p += 32) {
+      const uint4 l = __ldg(reinterpret_cast<const uint4*>(base + p * x.stride));
+      const uint4 h = __ldg(reinterpret_cast<const uint4*>(base + x.plane + p * x.stride));
+      const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t lb = (lw[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+        const uint32_t hb = (hw[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+        acc[j] += (int64_t)(int16_t)(uint16_t)(lb | (hb << 8));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    }
+    int64_t mine = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) mine = lane == j ? acc[j] : mine;
+    if (lane < 16)
+      plane16_store(y + n * y_pix_stride + g * 16 + lane, y_plane,
+                    requant_exact(mine - HW * zp_in, m, s, zp_out, qmin, qmax));
+  }
+}
+
 // -------------------------------------------------------------- Softmax --
 // quant_layers.py:195-205 / float_ops.py:380-385 over int16 rows, as
 // softmax_kernel of qa_resident_ops.cu.
@@ -364,6 +409,17 @@ QA_API int qa_gap16_dev(const void* x, int64_t x_plane, int64_t x_pix_stride, in
                         int64_t y_pix_stride, void* stream) {
   clear_error();
   if (N * C == 0) return 0;
+  if (C % 16 == 0 && x_pix_stride % 16 == 0 && (x_plane & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const int64_t warps = N * (C / 16);
+    return launch_ex(gap16_planes_kernel, dim3(grid_for(warps * 32, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true,
+                     Planes16{static_cast<const uint8_t*>(x), x_plane, x_pix_stride}, N, HW, C,
+                     zp_in, mult, shift, zp_out, qmin, qmax, static_cast<uint8_t*>(y), y_plane,
+                     y_pix_stride)
+               ? 0
+               : last_status();
+  }
   return launch_ex(gap16_kernel, dim3(grid_for(N * C, 256)), dim3(256), 0, (cudaStream_t)stream,
                    true, Planes16{static_cast<const uint8_t*>(x), x_plane, x_pix_stride}, N, HW,
                    C, zp_in, mult, shift, zp_out, qmin, qmax, static_cast<uint8_t*>(y), y_plane,
