@@ -109,6 +109,9 @@ class ResidentNet16(ResidentNet):
                 return plane
         raise AssertionError(f"address {ptr:#x} is not in a planned 16-bit tensor")
 
+    def _plan_maxpool(self, layer):
+        raise UnsupportedGraph(f"{layer.name}: MaxPool has no 16-bit resident kernel")
+
     def _plan_contraction(self, layer, layers, fused_away, patch=0):
         super()._plan_contraction(layer, layers, fused_away, patch)
         # desc.fast (16-bit meaning): every channel takes the kernel's exact
