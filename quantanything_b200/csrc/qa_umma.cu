@@ -25,7 +25,7 @@
 
 namespace qa {
 
-enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1, kEpiFused = 2, kEpiFused16 = 3 };
+enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1, kEpiFused = 2 };
 
 constexpr int kBM = 128;          // tile rows (TMEM lanes)
 constexpr int kBKBytes = 128;     // K-block bytes (one 128-byte swizzle row)
@@ -280,20 +280,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
       for (int a = 0; a < TS::kNumAcc; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
       ptx::tmem_ld_wait();
       if (!row_ok) continue;
-      if constexpr (kEpi == kEpiFused16) {
-        // lo*lo (u8 x u8), the two cross products and hi*hi, each exact in
-        // int32 for K * 255 * 255 < 2^31 (host-checked), combined in int64
-        static_assert(TS::kNumAcc == 3, "16-bit epilogue needs the split planes");
-        int64_t acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          acc[j] = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
-                   (int64_t)(int32_t)v[2][j] * 65536;
-        const int nb = n0 + c0;
-        const int cnt = p.n_valid - nb < 16 ? p.n_valid - nb : 16;
-        if (cnt > 0) fused_epilogue_store16_run(p.epi, acc, m, nb, cnt);
-        continue;
-      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int n = n0 + c0 + j;  // column within the group
@@ -730,17 +716,22 @@ namespace qa {
 constexpr int kP16Threads = 448;
 constexpr int kP16LutEntries = 65536;
 
+// BN <= 64: two accumulator sets (double buffering, one epilogue warpgroup
+// per set); BN = 128: one set (3 x 128 of the 512 TMEM columns), both
+// epilogue warpgroups drain half of each tile's columns.
 template <int BN, bool kSmemLut>
 struct P16Layout {
-  static constexpr int kStages = kSmemLut ? 2 : 4;
+  static constexpr int kSets = 6 * BN <= 512 ? 2 : 1;
+  static constexpr int kStages = kSmemLut ? 2 : (BN >= 128 ? 3 : 4);
   static constexpr int kAPlane = kBM * kBKBytes;  // 16 KB
   static constexpr int kBPlane = BN * kBKBytes;
   static constexpr int kStage = 2 * kAPlane + 2 * kBPlane;
   static constexpr int kSetCols = 3 * BN;  // one accumulator set
-  static constexpr int kCols = 2 * kSetCols;
+  static constexpr int kCols = kSets * kSetCols;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                    : kCols <= 256 ? 256 : 512;
-  static_assert(kCols <= 512, "two accumulator sets must fit TMEM");
+  static_assert(kCols <= 512, "accumulator sets must fit TMEM");
+  static_assert(!(kSmemLut && BN >= 128), "the shared-memory table leaves one stage at BN 128");
   static constexpr int kLutBytes = kSmemLut ? kP16LutEntries * 2 : 0;
   static constexpr size_t kBarOff = (size_t)kStages * kStage + kLutBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + (2 * kStages + 4) * 8 + 16;
@@ -780,7 +771,7 @@ __global__ void __launch_bounds__(kP16Threads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(accf_bar(b), 1);
-      ptx::mbar_init(acce_bar(b), 128);
+      ptx::mbar_init(acce_bar(b), L::kSets == 2 ? 128 : 256);
     }
     *s_abort = 0;
     ptx::fence_mbar_init();
@@ -923,8 +914,9 @@ __global__ void __launch_bounds__(kP16Threads, 1)
       constexpr uint32_t id_hh = ptx::idesc_i8(kBM, BN, 1, 1);
       int64_t g = 0, i = 0;
       for (int64_t t = first; t < total_tiles && !*s_abort; t += step, ++i) {
-        const int b = (int)(i & 1);
-        if (i >= 2 && !wait(acce_bar(b), (uint32_t)(((i >> 1) - 1) & 1))) break;
+        const int b = L::kSets == 2 ? (int)(i & 1) : 0;
+        const int64_t u = L::kSets == 2 ? (i >> 1) : i;  // earlier uses of set b
+        if (u >= 1 && !wait(acce_bar(b), (uint32_t)((u - 1) & 1))) break;
         ptx::tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(b * L::kSetCols);
         for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
@@ -951,12 +943,19 @@ __global__ void __launch_bounds__(kP16Threads, 1)
     }
   } else {
     // ---------------------------------------------------------- epilogue --
-    const int b = (warp - 6) / 4;  // this warpgroup's accumulator set
+    // two sets: warpgroup wg drains set wg (tiles wg, wg + 2, ...), all
+    // columns; one set: both drain every tile, warpgroup wg half the columns
+    const int wg = (warp - 6) / 4;
+    const int b = L::kSets == 2 ? wg : 0;
+    const int c_lo = L::kSets == 2 ? 0 : wg * (BN / 2);
+    const int c_hi = L::kSets == 2 ? BN : c_lo + BN / 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    int64_t i = b;
-    for (int64_t t = first + b * step; t < total_tiles; t += 2 * step, i += 2) {
-      if (!wait(accf_bar(b), (uint32_t)((i >> 1) & 1))) break;
+    const int64_t istep = L::kSets == 2 ? 2 : 1;
+    int64_t i = L::kSets == 2 ? wg : 0;
+    for (int64_t t = first + i * step; t < total_tiles; t += istep * step, i += istep) {
+      const int64_t u = L::kSets == 2 ? (i >> 1) : i;
+      if (!wait(accf_bar(b), (uint32_t)(u & 1))) break;
       __syncwarp();
       ptx::tc_fence_after();
       const int64_t m = (t / n_tiles) * kBM + r;
@@ -965,7 +964,7 @@ __global__ void __launch_bounds__(kP16Threads, 1)
       const uint32_t lane_base =
           tmem + (((uint32_t)quarter * 32u) << 16) + (uint32_t)(b * L::kSetCols);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
         uint32_t v[3][16];
 #pragma unroll
         for (int a = 0; a < 3; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
@@ -1022,18 +1021,6 @@ bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);  // qa_
 
 namespace {
 
-template <int BN, int kChunk>
-bool launch_conv16(const ConvTileParams& prm, const CUtensorMap& tmap, int64_t n_tiles,
-                   cudaStream_t st) {
-  // two stages (about 100 KB) keep two CTAs on an SM up to BN = 64, so one
-  // CTA's epilogue overlaps the other's gather and MMAs; BN = 128 takes the
-  // whole SM (its three accumulators fill the 512 TMEM columns)
-  constexpr int kStages = BN <= 64 ? 2 : 3;
-  return launch_umma<BN, 2, 2, kChunk, kEpiFused16, kStages>(prm, tmap, n_tiles, 1, st);
-}
-
-// BN <= 64: the persistent kernel (two accumulator sets of 3 x BN columns
-// fit TMEM); BN = 128: one tile per CTA.
 template <int kChunk, bool kSmemLut>
 bool launch_conv16_lut(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
                        int64_t n_tiles, cudaStream_t st) {
@@ -1047,7 +1034,8 @@ bool launch_conv16_lut(int bn, const ConvTileParams& prm, const CUtensorMap& tma
 template <int kChunk>
 bool launch_conv16_bn(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
                       int64_t n_tiles, cudaStream_t st) {
-  if (bn == 128) return launch_conv16<128, kChunk>(prm, tmap, n_tiles, st);
+  // BN = 128 keeps the table in global memory (see P16Layout)
+  if (bn == 128) return launch_umma16_persistent<128, kChunk, false>(prm, tmap, n_tiles, st);
   // the kernel copies the table in 16-byte pieces
   const bool smem_lut = prm.epi.lut && prm.epi.lut16 && prm.epi.lut_len <= kP16LutEntries &&
                         prm.epi.lut_len % 8 == 0 &&

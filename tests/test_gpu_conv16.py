@@ -48,7 +48,7 @@ def _from_planes(buf, plane, N, H, W, C, pix_stride):
     return (lo + 256 * hi.astype(np.int64)).reshape(N, H, W, C)
 
 
-def _run(gpu_lib, oracle, name, epi, x_zp, seed):
+def _run(gpu_lib, oracle, name, epi, x_zp, seed, block_n=None):
     from quantanything_b200 import native
     from quantanything_b200.resident import device_api
     from quantanything_b200.resident16 import FusedConv16Desc, device_api16
@@ -95,6 +95,8 @@ def _run(gpu_lib, oracle, name, epi, x_zp, seed):
     xs = C if C % 16 == 0 else _ru(C, 16)
     xdev, xplane = _to_planes(np.transpose(xr, (0, 2, 3, 1)), xs, x_zp)
     bn = 0 if groups > 1 else (16 if Cout <= 16 else 32 if Cout <= 32 else 64)
+    if block_n and groups == 1:
+        bn = block_n
     rows = _ru(Cout, bn or 16)
     K = KH * KW * ct
     kp = _ru(K, 16)
@@ -159,3 +161,11 @@ EPIS = [("plain", 0), ("lut", 37), ("lut16", 0), ("res", -5)]
 def test_conv16_matches_wide_route(gpu_lib, oracle, name, epi, x_zp):
     seed = 100 * GEOMS.index(name) + EPIS.index((epi, x_zp))
     _run(gpu_lib, oracle, name, epi, x_zp, seed=seed)
+
+
+@pytest.mark.parametrize("name", [g for g in GEOMS if int(G[f"{g}_geom"][8]) == 1])
+@pytest.mark.parametrize("epi,x_zp", [("lut", 11), ("res", 0)])
+def test_conv16_wide_column_tile(gpu_lib, oracle, name, epi, x_zp):
+    """128-column tiles: one TMEM accumulator set, both epilogue warpgroups
+    on every tile (half the columns each), the table in global memory."""
+    _run(gpu_lib, oracle, name, epi, x_zp, seed=7 + GEOMS.index(name), block_n=128)
