@@ -382,6 +382,12 @@ int qa_rescale16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, 
                      int64_t y_stride, int64_t rows, int64_t C, int64_t identity, int64_t zp_in,
                      int64_t m, int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
                      void* stream);
+/* MaxPool over int16 planes (out-of-image taps read pad_value: the
+ * reference pads with qmin, quant_layers.py:647-648). */
+int qa_maxpool16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, int64_t y_plane,
+                     int64_t y_stride, int64_t N, int64_t H, int64_t W, int64_t C, int64_t KH,
+                     int64_t KW, int64_t SH, int64_t SW, int64_t PH, int64_t PW, int64_t DH,
+                     int64_t DW, int64_t OH, int64_t OW, int64_t pad_value, void* stream);
 
 /* Allocation-free narrow GEMM.  No counterpart in the reference: it exists
  * for callers that may not allocate GPU memory while they run (a service

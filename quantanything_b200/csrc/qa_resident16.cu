@@ -248,6 +248,38 @@ __global__ void gap16_planes_kernel(Planes16 x, int64_t N, int64_t HW, int64_t C
   }
 }
 
+// ------------------------------------------------------------- MaxPool --
+// Integer MaxPool as the reference runs it through float_ops on int32
+// tensors, out-of-image taps padded with qmin (quant_layers.py:647-648).
+__global__ void maxpool16_kernel(Planes16 x, uint8_t* __restrict__ y, int64_t y_plane,
+                                 int64_t y_stride, int64_t N, int64_t H, int64_t W, int64_t C,
+                                 int64_t KH, int64_t KW, int64_t SH, int64_t SW, int64_t PH,
+                                 int64_t PW, int64_t DH, int64_t DW, int64_t OH, int64_t OW,
+                                 int64_t pad_value) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = N * OH * OW * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t c = i % C, pix = i / C;
+    const int64_t ohw = OH * OW;
+    const int64_t n = pix / ohw, rem = pix - n * ohw;
+    const int64_t oy = rem / OW, ox = rem - oy * OW;
+    int64_t best = INT64_MIN;
+    for (int64_t ky = 0; ky < KH; ++ky) {
+      const int64_t iy = oy * SH - PH + ky * DH;
+      for (int64_t kx = 0; kx < KW; ++kx) {
+        const int64_t ix = ox * SW - PW + kx * DW;
+        const int64_t v = (iy < 0 || iy >= H || ix < 0 || ix >= W)
+                              ? pad_value
+                              : at(x, (n * H + iy) * W + ix, c);
+        best = v > best ? v : best;
+      }
+    }
+    plane16_store(y + pix * y_stride + c, y_plane, best);
+  }
+}
+
 // -------------------------------------------------------------- Softmax --
 // quant_layers.py:195-205 / float_ops.py:380-385 over int16 rows, as
 // softmax_kernel of qa_resident_ops.cu.
@@ -492,6 +524,23 @@ QA_API int qa_rescale16_dev(const void* x, int64_t x_plane, int64_t x_stride, vo
                    Planes16{static_cast<const uint8_t*>(x), x_plane, x_stride},
                    static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, (int)(identity != 0),
                    zp_in, m, s, zp_out, qmin, qmax)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_maxpool16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y,
+                            int64_t y_plane, int64_t y_stride, int64_t N, int64_t H, int64_t W,
+                            int64_t C, int64_t KH, int64_t KW, int64_t SH, int64_t SW,
+                            int64_t PH, int64_t PW, int64_t DH, int64_t DW, int64_t OH,
+                            int64_t OW, int64_t pad_value, void* stream) {
+  clear_error();
+  const int64_t total = N * OH * OW * C;
+  if (total == 0) return 0;
+  return launch_ex(maxpool16_kernel, dim3(grid_for(total, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(x), x_plane, x_stride},
+                   static_cast<uint8_t*>(y), y_plane, y_stride, N, H, W, C, KH, KW, SH, SW, PH,
+                   PW, DH, DW, OH, OW, pad_value)
              ? 0
              : last_status();
 }

@@ -62,6 +62,7 @@ _DEV16_SIGNATURES = {
     "qa_add16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64]
                      + [_I64] * 12 + [_P]),
     "qa_rescale16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64] + [_I64] * 9 + [_P]),
+    "qa_maxpool16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64] + [_I64] * 15 + [_P]),
 }
 
 
@@ -110,9 +111,6 @@ class ResidentNet16(ResidentNet):
             if start <= ptr < start + plane:
                 return plane
         raise AssertionError(f"address {ptr:#x} is not in a planned 16-bit tensor")
-
-    def _plan_maxpool(self, layer):
-        raise UnsupportedGraph(f"{layer.name}: MaxPool has no 16-bit resident kernel")
 
     def _plan_contraction(self, layer, layers, fused_away, patch=0):
         super()._plan_contraction(layer, layers, fused_away, patch)
@@ -204,6 +202,15 @@ class ResidentNet16(ResidentNet):
                                       y.ptr, y.plane, y.pix_stride, a.N * a.H * a.W, a.C, qa.zp,
                                       ma, sa, qb.zp, mb, sb, layer._sign, o.zp, o.qmin, o.qmax,
                                       st)
+            elif kind == "maxpool":
+                layer, x, y = payload
+                from quantanything_b200.float_ops import pool_geometry
+
+                k, s_, dl, pd = pool_geometry(layer.node, (x.N, x.C, x.H, x.W))
+                rc = raw.qa_maxpool16_dev(x.ptr, x.plane, x.pix_stride, y.ptr, y.plane,
+                                          y.pix_stride, x.N, x.H, x.W, x.C, k[0], k[1], s_[0],
+                                          s_[1], pd[0], pd[1], dl[0], dl[1], y.H, y.W,
+                                          layer.in_qmin, st)
             elif kind == "softmax":
                 layer, x = payload
                 qi, o = layer.in_qp[0], layer.out_qp[0]

@@ -107,3 +107,25 @@ def test_int16_batch_invariance_and_graph_replay(gpu_lib):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(net8.out_q.cpu().numpy(), eager)
     np.testing.assert_array_equal(net8.run(x), net8.out_f32.cpu().numpy())
+
+
+def test_sppf_mini_int16_maxpool(gpu_lib, oracle, tmp_path):
+    """The SPPF block (three chained MaxPool k5 s1 p2, padded with qmin, into
+    a Concat) on the int16 executor: calibrated on the C oracle, the same
+    q.json loaded for the GPU; the logits equal the oracle's layer-by-layer
+    integer pass bit for bit, the Softmax output within 1 LSB."""
+    from quantanything_b200.resident16 import ResidentNet16
+
+    g = networks.sppf_mini(width=16)
+    qc = QuantContainer(g, "int16", per_channel=True, lib=oracle)
+    qc.calibrate([networks.images(4, 32, seed=s) for s in range(2)])
+    qc.save(tmp_path / "sppf_mini_int16.qjson")
+    net = ResidentNet16(QuantContainer.load(g, tmp_path / "sppf_mini_int16.qjson",
+                                            lib=gpu_lib), 2)
+    assert sum(kind == "maxpool" for kind, _ in net.steps) == 3
+    x = networks.images(2, 32, seed=7)
+    q = _run(net, x)
+    assert np.abs(q.astype(np.int64) - qc.run_integer_raw(x)).max() <= SOFTMAX_LSB
+    env, logits = _integer_pass(qc, x)
+    got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
+    np.testing.assert_array_equal(got, env[logits])
