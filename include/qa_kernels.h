@@ -243,6 +243,12 @@ int qa_add_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, const vo
                      int64_t rows, int64_t C, int64_t za, int64_t ma, int64_t sa, int64_t zb,
                      int64_t mb, int64_t sb, int64_t sign, int64_t zo, int64_t qmin,
                      int64_t qmax, void* stream);
+/* Integer Mul of two activations (qa_kernels.cpp:334-345):
+ * out = clamp(mbqm((a - za)(b - zb), m, s) + zo). */
+int qa_mul_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, const void* b,
+                     int64_t b_stride, int64_t b_signed, void* y, int64_t y_stride,
+                     int64_t rows, int64_t C, int64_t za, int64_t zb, int64_t m, int64_t s,
+                     int64_t zo, int64_t qmin, int64_t qmax, void* stream);
 int qa_rescale_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
                          int64_t y_stride, int64_t rows, int64_t C, int64_t identity,
                          int64_t zp_in, int64_t m, int64_t s, int64_t zp_out, int64_t qmin,
@@ -382,6 +388,10 @@ int qa_rescale16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, 
                      int64_t y_stride, int64_t rows, int64_t C, int64_t identity, int64_t zp_in,
                      int64_t m, int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
                      void* stream);
+int qa_mul16_dev(const void* a, int64_t a_plane, int64_t a_stride, const void* b,
+                 int64_t b_plane, int64_t b_stride, void* y, int64_t y_plane, int64_t y_stride,
+                 int64_t rows, int64_t C, int64_t za, int64_t zb, int64_t m, int64_t s,
+                 int64_t zo, int64_t qmin, int64_t qmax, void* stream);
 /* MaxPool over int16 planes (out-of-image taps read pad_value: the
  * reference pads with qmin, quant_layers.py:647-648). */
 int qa_maxpool16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, int64_t y_plane,

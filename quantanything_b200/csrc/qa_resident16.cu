@@ -248,6 +248,22 @@ __global__ void gap16_planes_kernel(Planes16 x, int64_t N, int64_t HW, int64_t C
   }
 }
 
+// Integer Mul of two activations (qa_kernels.cpp:334-345): the product of
+// two centred int16 values fits int64; the 128-bit mbqm requantizes it.
+__global__ void mul16_kernel(Planes16 a, Planes16 b, uint8_t* __restrict__ y, int64_t y_plane,
+                             int64_t y_stride, int64_t rows, int64_t C, int64_t za, int64_t zb,
+                             int64_t m, int64_t s, int64_t zo, int64_t qmin, int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    const int64_t p = (at(a, r, c) - za) * (at(b, r, c) - zb);
+    plane16_store(y + r * y_stride + c, y_plane, requant_exact(p, m, s, zo, qmin, qmax));
+  }
+}
+
 // ------------------------------------------------------------- MaxPool --
 // Integer MaxPool as the reference runs it through float_ops on int32
 // tensors, out-of-image taps padded with qmin (quant_layers.py:647-648).
@@ -541,6 +557,23 @@ QA_API int qa_maxpool16_dev(const void* x, int64_t x_plane, int64_t x_stride, vo
                    Planes16{static_cast<const uint8_t*>(x), x_plane, x_stride},
                    static_cast<uint8_t*>(y), y_plane, y_stride, N, H, W, C, KH, KW, SH, SW, PH,
                    PW, DH, DW, OH, OW, pad_value)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_mul16_dev(const void* a, int64_t a_plane, int64_t a_stride, const void* b,
+                        int64_t b_plane, int64_t b_stride, void* y, int64_t y_plane,
+                        int64_t y_stride, int64_t rows, int64_t C, int64_t za, int64_t zb,
+                        int64_t m, int64_t s, int64_t zo, int64_t qmin, int64_t qmax,
+                        void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  return launch_ex(mul16_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(a), a_plane, a_stride},
+                   Planes16{static_cast<const uint8_t*>(b), b_plane, b_stride},
+                   static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, za, zb, m, s, zo, qmin,
+                   qmax)
              ? 0
              : last_status();
 }

@@ -475,6 +475,24 @@ __global__ void maxpool_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_
   }
 }
 
+// out = clamp(mbqm((a - za)(b - zb), m, s) + zo): the integer Mul of two
+// activations (qa_kernels.cpp:334-345, quant_layers.py:516-540).
+__global__ void mul_bytes_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y,
+                                 int64_t y_stride, int64_t rows, int64_t C, int64_t za,
+                                 int64_t zb, int64_t m, int64_t s, int64_t zo, int64_t qmin,
+                                 int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    const int64_t va = bval(a.p + r * a.stride + c, a.is_signed) - za;
+    const int64_t vb = bval(b.p + r * b.stride + c, b.is_signed) - zb;
+    y[r * y_stride + c] = (uint8_t)requant_exact(va * vb, m, s, zo, qmin, qmax);
+  }
+}
+
 // NHWC bytes [N, HW, C] <-> NCHW int32.
 __global__ void bytes_to_i32_kernel(ByteView x, int32_t* __restrict__ y, int64_t N, int64_t HW,
                                     int64_t C) {
@@ -1096,6 +1114,21 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
   const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count() * 2);
   return launch_ex(input_conv_kernel, dim3((unsigned)grid), dim3(kInThreads), smem,
                    (cudaStream_t)stream, true, p, xmap)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_mul_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, const void* b,
+                            int64_t b_stride, int64_t b_signed, void* y, int64_t y_stride,
+                            int64_t rows, int64_t C, int64_t za, int64_t zb, int64_t m,
+                            int64_t s, int64_t zo, int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  return launch_ex(mul_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
+                   ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
+                   static_cast<uint8_t*>(y), y_stride, rows, C, za, zb, m, s, zo, qmin, qmax)
              ? 0
              : last_status();
 }

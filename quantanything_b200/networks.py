@@ -168,6 +168,21 @@ def sppf_mini(seed=0, size=32, classes=10, width=16):
     return b.build(x, ["N", 3, size, size], y)
 
 
+def mul_mini(seed=0, size=32, classes=10, width=16):
+    """Small graph whose activations stay unfused: Sigmoid (a table) and an
+    activation x activation Mul, i.e. SiLU as the graph holds it before the
+    reference's element-wise fusion pass (graph_passes.py:208-272), so the
+    integer Mul layer (quant_layers.py:516-540) runs on its own."""
+    b = GraphBuilder(seed)
+    x = "images"
+    y = b.conv_silu(x, 3, width, 3, 2)
+    y = b.conv(y, width, 2 * width, 3, 2)
+    y = b.op("Mul", [y, b.op("Sigmoid", [y])])
+    y = b.conv_silu(y, 2 * width, 2 * width, 3)
+    y = b.head(y, 2 * width, classes)
+    return b.build(x, ["N", 3, size, size], y)
+
+
 def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, mlp=4,
         std=None):
     """A Vision Transformer in the reference's post-pass form (the structure

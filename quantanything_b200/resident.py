@@ -34,6 +34,7 @@ from quantanything_b200.layers import (
     ConvQuantize,
     GemmQuantize,
     GlobalAveragePoolQuantize,
+    MulQuantize,
     ShapingQuantize,
 )
 
@@ -82,6 +83,8 @@ _DEV_SIGNATURES = {
     "qa_add_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P] + [_I64] * 13
                          + [_P]),
     "qa_rescale_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 10 + [_P]),
+    "qa_mul_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P] + [_I64] * 10
+                         + [_P]),
     "qa_maxpool_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 16 + [_P]),
     "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
     "qa_device_status_dev": (ctypes.c_int, [_P]),
@@ -323,6 +326,8 @@ class ResidentNet:
                 self._plan_lut(layer)
             elif isinstance(layer, AddQuantize):
                 self._plan_add(layer)
+            elif isinstance(layer, MulQuantize):
+                self._plan_mul(layer)
             elif node.op_type == "Softmax" and node.outputs[0] in g.outputs:
                 self._plan_softmax(layer)
             else:
@@ -691,6 +696,16 @@ class ResidentNet:
         if copy is not None:
             self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
 
+    def _plan_mul(self, layer):
+        node = layer.node
+        a, b = (self._views[i] for i in node.inputs)
+        N, C, H, W = self._shapes[node.outputs[0]]
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, H, W, C)
+        self._views[node.outputs[0]] = view
+        self.steps.append(("mul", (layer, a, b, view)))
+        if copy is not None:
+            self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
+
     def _plan_softmax(self, layer):
         node = layer.node
         x = self._views[node.inputs[0]]
@@ -815,6 +830,14 @@ class ResidentNet:
                                           b.pix_stride, int(b.signed), y.ptr, y.pix_stride,
                                           a.N * a.H * a.W, a.C, qa.zp, ma, sa, qb.zp, mb, sb,
                                           layer._sign, o.zp, o.qmin, o.qmax, st)
+            elif kind == "mul":
+                layer, a, b, y = payload
+                qa, qb = layer.in_qp
+                o = layer.out_qp[0]
+                rc = raw.qa_mul_bytes_dev(a.ptr, a.pix_stride, int(a.signed), b.ptr,
+                                          b.pix_stride, int(b.signed), y.ptr, y.pix_stride,
+                                          a.N * a.H * a.W, a.C, qa.zp, qb.zp, layer._mult,
+                                          layer._shift, o.zp, o.qmin, o.qmax, st)
             elif kind == "maxpool":
                 layer, x, y = payload
                 from quantanything_b200.float_ops import pool_geometry

@@ -63,6 +63,8 @@ _DEV16_SIGNATURES = {
                      + [_I64] * 12 + [_P]),
     "qa_rescale16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64] + [_I64] * 9 + [_P]),
     "qa_maxpool16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64] + [_I64] * 15 + [_P]),
+    "qa_mul16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64]
+                     + [_I64] * 9 + [_P]),
 }
 
 
@@ -201,6 +203,14 @@ class ResidentNet16(ResidentNet):
                 rc = raw.qa_add16_dev(a.ptr, a.plane, a.pix_stride, b.ptr, b.plane, b.pix_stride,
                                       y.ptr, y.plane, y.pix_stride, a.N * a.H * a.W, a.C, qa.zp,
                                       ma, sa, qb.zp, mb, sb, layer._sign, o.zp, o.qmin, o.qmax,
+                                      st)
+            elif kind == "mul":
+                layer, a, b, y = payload
+                qa, qb = layer.in_qp
+                o = layer.out_qp[0]
+                rc = raw.qa_mul16_dev(a.ptr, a.plane, a.pix_stride, b.ptr, b.plane, b.pix_stride,
+                                      y.ptr, y.plane, y.pix_stride, a.N * a.H * a.W, a.C, qa.zp,
+                                      qb.zp, layer._mult, layer._shift, o.zp, o.qmin, o.qmax,
                                       st)
             elif kind == "maxpool":
                 layer, x, y = payload
