@@ -248,6 +248,10 @@ class ResidentNet:
         if self.bits > 8:
             raise UnsupportedGraph("the resident executor runs 8-bit graphs")
 
+    def _operand_bits(self):
+        """Width of the contraction operands (packed weights, activations)."""
+        return self.bits
+
     def _alloc(self, nbytes):
         t = torch.empty(int(nbytes) + 64, dtype=torch.uint8, device=self.device)
         self._keep.append(t)
@@ -439,16 +443,17 @@ class ResidentNet:
             w4 = layer.w_centered.astype(np.int64)
             cout, cg, kh, kw = w4.shape
             groups = layer.node.attr("group", 1)
-        lim = 1 << (self.bits - 1)
+        bits = self._operand_bits()
+        lim = 1 << (bits - 1)
         if w4.min() < -lim or w4.max() >= lim:
-            raise UnsupportedGraph(f"{layer.name}: centred weights exceed int{self.bits}")
+            raise UnsupportedGraph(f"{layer.name}: centred weights exceed int{bits}")
         ct = taps_c if groups == 1 else cg
         bn = min(choose_block_n(cout, m_rows, ct if groups == 1 else 16, self.sm_count),
                  self._max_block_n)
         rows = _round_up(cout, bn)
         k = kh * kw * ct
         kp = _round_up(k, 16)
-        packed = np.zeros((rows, kp), np.int8 if self.bits == 8 else np.int16)
+        packed = np.zeros((rows, kp), np.int8 if bits == 8 else np.int16)
         wt = np.zeros((cout, kh, kw, ct), np.int64)
         wt[:, :, :, :cg] = np.transpose(w4, (0, 2, 3, 1))
         packed[:cout, :k] = wt.reshape(cout, k)
@@ -537,7 +542,8 @@ class ResidentNet:
         d.bias, d.mult, d.shift = bdev.data_ptr(), mdev.data_ptr(), sdev.data_ptr()
         d.zp, d.qmin, d.qmax, d.fast = layer.out_zp, layer.out_qmin, layer.out_qmax, int(fast)
         d.block_n = bn if groups == 1 else 0
-        if groups == 1 and ct % 16 == 0 and x_zp != 0 and not patch and self.bits == 8:
+        if (groups == 1 and ct % 16 == 0 and x_zp != 0 and not patch
+                and self._operand_bits() == 8):
             wt = packed[:cout, :geo["KH"] * geo["KW"] * ct].reshape(cout, geo["KH"], geo["KW"], ct)
             pc = pad_corrections(wt, int(x_zp), H, W, **geo)
             if pc is not None:

@@ -1,4 +1,5 @@
-"""Device-resident, fused execution of 16-bit (int16) graphs.
+"""Device-resident, fused execution of 16-bit (int16) graphs -- and of uint8
+graphs, whose asymmetric weights do not fit the 8-bit tensor path.
 
 The reference runs an int16 graph with every Conv and Gemm on its wide
 route: int32 operands, int64 accumulators (``native.accumulator_is_wide``,
@@ -97,8 +98,14 @@ class ResidentNet16(ResidentNet):
 
     # ---------------------------------------------------------- storage --
     def _check_bits(self):
-        if self.bits != 16 or not self.signed:
-            raise UnsupportedGraph("ResidentNet16 runs int16 graphs")
+        # uint8 graphs (asymmetric activations and weights) take this route
+        # too: their centred weights span [-255, 255], past int8 but within
+        # int16, and a uint8 value is an int16 with a zero high byte
+        if not ((self.bits == 16 and self.signed) or (self.bits == 8 and not self.signed)):
+            raise UnsupportedGraph("ResidentNet16 runs int16 and uint8 graphs")
+
+    def _operand_bits(self):
+        return 16
 
     def _new_view(self, N, H, W, C, qp, pix_stride=None):
         stride = pix_stride or (C if C % 16 == 0 else _round_up(C, 16))

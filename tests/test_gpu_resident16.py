@@ -129,3 +129,18 @@ def test_sppf_mini_int16_maxpool(gpu_lib, oracle, tmp_path):
     env, logits = _integer_pass(qc, x)
     got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
     np.testing.assert_array_equal(got, env[logits])
+
+
+@pytest.mark.parametrize("name", ["yolo_mini_uint8", "sppf_mini_uint8"])
+def test_uint8_graphs_on_the_16bit_route(gpu_lib, name):
+    """uint8 graphs (asymmetric activations and weights: centred weights up
+    to +-255) run on the int16 executor; the reference's golden outputs
+    within the Softmax's 1 LSB, the logits equal to the drop-in pass."""
+    net, qc, meta = _net(name, gpu_lib, 2)
+    x = networks.images(2, meta["image"], seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / f"{name}.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+    env, logits = _integer_pass(qc, x)
+    got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
+    np.testing.assert_array_equal(got, env[logits])
