@@ -446,6 +446,188 @@ __global__ void rescale_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_
   }
 }
 
+// ----------------------------------------- 16-channel vector forms ----
+// One thread handles 16 channel bytes of one pixel with 16-byte loads and
+// stores (C, the pixel strides and the base pointers multiples of 16).  An
+// 8-bit operand takes only 256 values, so per-element maps are 256-entry
+// tables built per block from the exact definitions.
+
+// byte -> byte map of a standalone table layer or Concat rescale
+struct ByteMap {
+  int is_signed;
+  int kind;                  // 0: activation table, 1: rescale / clip
+  const int32_t* lut;
+  int64_t offset, len;       // table: out = lut[clamp(v - offset, 0, len - 1)]
+  int identity;              // rescale: clip to [qmin, qmax] instead
+  int64_t zin, m, s, zout, qmin, qmax;
+};
+
+__device__ __forceinline__ uint8_t byte_map_entry(const ByteMap& mp, int b) {
+  const int64_t v = mp.is_signed ? (int64_t)(int8_t)b : (int64_t)b;
+  if (mp.kind == 0) {
+    int64_t idx = v - mp.offset;
+    idx = idx < 0 ? 0 : (idx >= mp.len ? mp.len - 1 : idx);
+    return (uint8_t)mp.lut[idx];
+  }
+  if (mp.identity) return (uint8_t)(v < mp.qmin ? mp.qmin : (v > mp.qmax ? mp.qmax : v));
+  return (uint8_t)requant_exact(v - mp.zin, mp.m, mp.s, mp.zout, mp.qmin, mp.qmax);
+}
+
+__device__ __forceinline__ uint4 map16(const uint8_t* tab, uint4 v) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w}, o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    o[k] = (uint32_t)tab[w[k] & 0xFF] | ((uint32_t)tab[(w[k] >> 8) & 0xFF] << 8) |
+           ((uint32_t)tab[(w[k] >> 16) & 0xFF] << 16) | ((uint32_t)tab[w[k] >> 24] << 24);
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void map_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride,
+                                   int64_t rows, int64_t groups, ByteMap mp) {
+  __shared__ uint8_t tab[256];
+  ptx::pdl_launch_dependents();
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) tab[b] = byte_map_entry(mp, b);
+  __syncthreads();
+  ptx::pdl_wait();
+  const int64_t total = rows * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / groups, g = i - r * groups;
+    const uint4 v = *reinterpret_cast<const uint4*>(x.p + r * x.stride + g * 16);
+    *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = map16(tab, v);
+  }
+}
+
+// Add: the two rescaled terms (sign applied to the second) as int64 tables;
+// exact when every entry's 128-bit value lies within +-2^61 (checked while
+// building: the sum of two terms and the zero point then cannot overflow),
+// else every element takes the 128-bit path.
+__global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y,
+                                   int64_t y_stride, int64_t rows, int64_t groups, int64_t za,
+                                   int64_t ma, int64_t sa, int64_t zb, int64_t mb, int64_t sb,
+                                   int64_t sign, int64_t zo, int64_t qmin, int64_t qmax) {
+  __shared__ int64_t ta[256], tb[256];
+  ptx::pdl_launch_dependents();
+  int ok = 1;
+  for (int e = threadIdx.x; e < 256; e += blockDim.x) {
+    const int64_t va = a.is_signed ? (int64_t)(int8_t)e : (int64_t)e;
+    const int64_t vb = b.is_signed ? (int64_t)(int8_t)e : (int64_t)e;
+    const I128 x1 = mbqm(va - za, ma, sa);
+    I128 x2 = mbqm(vb - zb, mb, sb);
+    if (sign < 0) x2 = neg_i128(x2);
+    const int64_t lim = (int64_t)1 << 61;
+    ok &= x1.hi == ((int64_t)x1.lo >> 63) && (int64_t)x1.lo > -lim && (int64_t)x1.lo < lim;
+    ok &= x2.hi == ((int64_t)x2.lo >> 63) && (int64_t)x2.lo > -lim && (int64_t)x2.lo < lim;
+    ta[e] = (int64_t)x1.lo;
+    tb[e] = (int64_t)x2.lo;
+  }
+  const bool tables = __syncthreads_and(ok);
+  ptx::pdl_wait();
+  const int64_t total = rows * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / groups, g = i - r * groups;
+    const uint4 va4 = *reinterpret_cast<const uint4*>(a.p + r * a.stride + g * 16);
+    const uint4 vb4 = *reinterpret_cast<const uint4*>(b.p + r * b.stride + g * 16);
+    const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int ea = (wa[j >> 2] >> (8 * (j & 3))) & 0xFF;
+      const int eb = (wb[j >> 2] >> (8 * (j & 3))) & 0xFF;
+      int64_t q;
+      if (tables) {
+        q = ta[ea] + tb[eb] + zo;
+        q = q < qmin ? qmin : (q > qmax ? qmax : q);
+      } else {
+        const I128 x1 = mbqm((a.is_signed ? (int64_t)(int8_t)ea : ea) - za, ma, sa);
+        I128 x2 = mbqm((b.is_signed ? (int64_t)(int8_t)eb : eb) - zb, mb, sb);
+        if (sign < 0) x2 = neg_i128(x2);
+        q = clamp_i128(add_i128_i64(add_i128(x1, x2), zo), qmin, qmax);
+      }
+      o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Mul: (a - za)(b - zb) is at most 2^18 in magnitude, so one 64-bit product
+// requantizes exactly when the multiplier allows (small_applies).
+__global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y,
+                                   int64_t y_stride, int64_t rows, int64_t groups, int64_t za,
+                                   int64_t zb, int64_t m, int64_t s, int64_t zo, int64_t qmin,
+                                   int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const bool small = small_applies(m, s);
+  const int64_t total = rows * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / groups, g = i - r * groups;
+    const uint4 va4 = *reinterpret_cast<const uint4*>(a.p + r * a.stride + g * 16);
+    const uint4 vb4 = *reinterpret_cast<const uint4*>(b.p + r * b.stride + g * 16);
+    const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int ea = (wa[j >> 2] >> (8 * (j & 3))) & 0xFF;
+      const int eb = (wb[j >> 2] >> (8 * (j & 3))) & 0xFF;
+      const int64_t p = ((a.is_signed ? (int64_t)(int8_t)ea : ea) - za) *
+                        ((b.is_signed ? (int64_t)(int8_t)eb : eb) - zb);
+      int64_t q;
+      if (small) {
+        q = mbqm_small(p, m, (int)(31 + s)) + zo;
+        q = q < qmin ? qmin : (q > qmax ? qmax : q);
+      } else {
+        q = requant_exact(p, m, s, zo, qmin, qmax);
+      }
+      o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// MaxPool: per-byte SIMD max over the window, out-of-image taps read the
+// pad value (qmin) in every byte.
+__global__ void maxpool_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride,
+                                       int64_t N, int64_t H, int64_t W, int64_t groups,
+                                       int64_t KH, int64_t KW, int64_t SH, int64_t SW,
+                                       int64_t PH, int64_t PW, int64_t DH, int64_t DW,
+                                       int64_t OH, int64_t OW, uint32_t pad_word) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = N * OH * OW * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t g = i % groups, pix = i / groups;
+    const int64_t ohw = OH * OW;
+    const int64_t n = pix / ohw, rem = pix - n * ohw;
+    const int64_t oy = rem / OW, ox = rem - oy * OW;
+    uint32_t best[4] = {pad_word, pad_word, pad_word, pad_word};
+    bool first = true;
+    for (int64_t ky = 0; ky < KH; ++ky) {
+      const int64_t iy = oy * SH - PH + ky * DH;
+      for (int64_t kx = 0; kx < KW; ++kx) {
+        const int64_t ix = ox * SW - PW + kx * DW;
+        uint4 v = make_uint4(pad_word, pad_word, pad_word, pad_word);
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+          v = *reinterpret_cast<const uint4*>(x.p + ((n * H + iy) * W + ix) * x.stride + g * 16);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          best[k] = first ? w[k] : (x.is_signed ? __vmaxs4(best[k], w[k]) : __vmaxu4(best[k], w[k]));
+        first = false;
+      }
+    }
+    *reinterpret_cast<uint4*>(y + pix * y_stride + g * 16) =
+        make_uint4(best[0], best[1], best[2], best[3]);
+  }
+}
+
+__host__ __device__ inline bool vec16_ok(const void* p, int64_t stride) {
+  return ((reinterpret_cast<uintptr_t>(p) | (uint64_t)stride) & 15) == 0;
+}
+
 __global__ void maxpool_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride,
                                      int64_t N, int64_t H, int64_t W, int64_t C, int64_t KH,
                                      int64_t KW, int64_t SH, int64_t SW, int64_t PH, int64_t PW,
@@ -618,6 +800,20 @@ QA_API int qa_lut_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, v
                             const int32_t* lut, int64_t lut_len, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
+  if (C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride)) {
+    ByteMap mp{};
+    mp.is_signed = (int)x_signed;
+    mp.kind = 0;
+    mp.lut = lut;
+    mp.offset = offset;
+    mp.len = lut_len;
+    return launch_ex(map_bytes16_kernel, dim3(grid_for(rows * C / 16, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true,
+                     ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
+                     static_cast<uint8_t*>(y), y_stride, rows, C / 16, mp)
+               ? 0
+               : last_status();
+  }
   return launch_ex(lut_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
       static_cast<uint8_t*>(y), y_stride, rows, C, offset, lut, lut_len)
@@ -632,6 +828,15 @@ QA_API int qa_add_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, c
                             int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
+  if (C % 16 == 0 && vec16_ok(a, a_stride) && vec16_ok(b, b_stride) && vec16_ok(y, y_stride))
+    return launch_ex(add_bytes16_kernel, dim3(grid_for(rows * C / 16, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true,
+                     ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
+                     ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
+                     static_cast<uint8_t*>(y), y_stride, rows, C / 16, za, ma, sa, zb, mb, sb,
+                     sign, zo, qmin, qmax)
+               ? 0
+               : last_status();
   return launch_ex(add_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
       ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
@@ -646,6 +851,24 @@ QA_API int qa_rescale_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
                                 int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
+  if (C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride)) {
+    ByteMap mp{};
+    mp.is_signed = (int)x_signed;
+    mp.kind = 1;
+    mp.identity = identity != 0;
+    mp.zin = zp_in;
+    mp.m = m;
+    mp.s = s;
+    mp.zout = zp_out;
+    mp.qmin = qmin;
+    mp.qmax = qmax;
+    return launch_ex(map_bytes16_kernel, dim3(grid_for(rows * C / 16, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true,
+                     ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
+                     static_cast<uint8_t*>(y), y_stride, rows, C / 16, mp)
+               ? 0
+               : last_status();
+  }
   return launch_ex(rescale_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
       static_cast<uint8_t*>(y), y_stride, rows, C, (int)identity, zp_in, m, s, zp_out, qmin,
@@ -662,6 +885,16 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
   clear_error();
   const int64_t total = N * OH * OW * C;
   if (total == 0) return 0;
+  if (C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride)) {
+    const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
+    return launch_ex(maxpool_bytes16_kernel, dim3(grid_for(N * OH * OW * (C / 16), 256)),
+                     dim3(256), 0, (cudaStream_t)stream, true,
+                     ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
+                     static_cast<uint8_t*>(y), y_stride, N, H, W, C / 16, KH, KW, SH, SW, PH, PW,
+                     DH, DW, OH, OW, pw)
+               ? 0
+               : last_status();
+  }
   return launch_ex(maxpool_bytes_kernel, dim3(grid_for(total, 256)), dim3(256), 0, (cudaStream_t)stream, true,
       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
       static_cast<uint8_t*>(y), y_stride, N, H, W, C, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW,
@@ -1124,6 +1357,15 @@ QA_API int qa_mul_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, c
                             int64_t s, int64_t zo, int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
+  if (C % 16 == 0 && vec16_ok(a, a_stride) && vec16_ok(b, b_stride) && vec16_ok(y, y_stride))
+    return launch_ex(mul_bytes16_kernel, dim3(grid_for(rows * C / 16, 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true,
+                     ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
+                     ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
+                     static_cast<uint8_t*>(y), y_stride, rows, C / 16, za, zb, m, s, zo, qmin,
+                     qmax)
+               ? 0
+               : last_status();
   return launch_ex(mul_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true,
                    ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
