@@ -134,6 +134,80 @@ def measure_fused_configs(dev, stream, flush, peak_tops, reps=10):
     return res
 
 
+def measure_elementwise(dev, stream, flush, hbm_peak, reps=5):
+    """The standalone memory-bound resident kernels on tensors larger than
+    L2 (2^21 pixels x 64 channels: 128 MiB per 8-bit operand): median
+    CUDA-event time of single launches, L2 flushed before each; algorithmic
+    bytes = every operand read once plus the output written once."""
+    import ctypes
+
+    import torch
+
+    from quantanything_b200 import native
+    from quantanything_b200.resident import device_api
+
+    lib = native.get_library()
+    raw = device_api(lib)
+    st = ctypes.c_void_p(stream.cuda_stream)
+    rows, C = 1 << 21, 64
+    n = rows * C
+    a = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev)
+    b = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev)
+    y = torch.empty(n, dtype=torch.uint8, device=dev)
+    tab = torch.randint(-128, 128, (256,), dtype=torch.int32, device=dev)
+    acc = torch.randint(-(2**20), 2**20, (n,), dtype=torch.int32, device=dev)
+    q32 = torch.empty(n, dtype=torch.int32, device=dev)
+    mult = torch.full((C,), 1 << 30, dtype=torch.int64, device=dev)
+    shift = torch.full((C,), 4, dtype=torch.int64, device=dev)
+    img = torch.randn(512, 3, 64, 64, device=dev)  # 2^21 pixels
+    m30 = 1 << 30
+    cases = {
+        "lut (table)": (2 * n, lambda: raw.qa_lut_bytes_dev(a.data_ptr(), C, 1, y.data_ptr(), C,
+                                                           rows, C, -128, tab.data_ptr(), 256, st)),
+        "rescale": (2 * n, lambda: raw.qa_rescale_bytes_dev(a.data_ptr(), C, 1, y.data_ptr(), C,
+                                                            rows, C, 0, 3, m30, 1, -4, -128, 127,
+                                                            st)),
+        "add": (3 * n, lambda: raw.qa_add_bytes_dev(a.data_ptr(), C, 1, b.data_ptr(), C, 1,
+                                                    y.data_ptr(), C, rows, C, 5, m30, 1, -2, m30,
+                                                    1, 1, 7, -128, 127, st)),
+        "mul": (3 * n, lambda: raw.qa_mul_bytes_dev(a.data_ptr(), C, 1, b.data_ptr(), C, 1,
+                                                    y.data_ptr(), C, rows, C, 3, -1, m30, 6, 2,
+                                                    -128, 127, st)),
+        "maxpool k5 s1 p2": (2 * n, lambda: raw.qa_maxpool_bytes_dev(
+            a.data_ptr(), C, 1, y.data_ptr(), C, 512, 64, 64, C, 5, 5, 1, 1, 2, 2, 1, 1, 64, 64,
+            -128, st)),
+        "gap 49 px": (n + n // 49, lambda: raw.qa_gap_dev(
+            a.data_ptr(), C, 1, rows // 49, 49, C, 0, m30, 5, 0, -128, 127, y.data_ptr(), C, st)),
+        "requantize i32 -> i32": (8 * n, lambda: raw.qa_requantize_i32_dev(
+            acc.data_ptr(), q32.data_ptr(), rows, C, 1, mult.data_ptr(), shift.data_ptr(), None,
+            None, 0, -128, 127, st)),
+        "quantize f32 -> nhwc": (img.numel() * 4 + rows * 4, lambda: raw.qa_quantize_to_nhwc_dev(
+            img.data_ptr(), y.data_ptr(), 512, 3, 64, 64, 4, 0.0235, 0, -128, 127, st)),
+    }
+    res = {}
+    for name, (nbytes, fn) in cases.items():
+        for _ in range(2):
+            if fn() != 0:
+                raise RuntimeError(f"{name}: {lib.raw.qa_last_error().decode()}")
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        t = float(np.median(times)) / 1e3
+        gbs = nbytes / t / 1e9
+        res[name] = {"us": round(t * 1e6, 1), "GB/s": round(gbs, 1),
+                     "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes)}
+    res["timing"] = (f"median of {reps} single launches on 2^21 pixels x 64 channels, "
+                     "L2 flushed before each; bytes = operands read once + output written once")
+    return res
+
+
 def config(world, extra=None):
     c = {"workload": W["name"],
          "global_batch": PER_GPU_BATCH * world, "per_gpu_batch": PER_GPU_BATCH,
@@ -282,6 +356,9 @@ def main():
     ap.add_argument("--profile-fused", choices=["cfg0", "cfg1"], default=None,
                     help="launch the fused int8 kernel on this kernel-level configuration "
                          "three times and exit (for ncu captures)")
+    ap.add_argument("--profile-elementwise", action="store_true",
+                    help="run the standalone memory-bound kernels of the bench line's "
+                         "'elementwise' entry once each and exit (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch of a --profile-forwards run (the bench line itself "
                          "always uses the workload's configured batch)")
@@ -309,6 +386,16 @@ def main():
             case.launch(torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         print(json.dumps({"profile_fused": args.profile_fused, "launches": 3}))
+        return
+    if args.profile_elementwise:
+        import torch
+
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        res = measure_elementwise(dev, torch.cuda.current_stream(dev), flush, peaks()[0], reps=1)
+        print(json.dumps({"profile_elementwise": {k: v for k, v in res.items()
+                                                  if isinstance(v, dict)}}))
         return
     args.warmup = max(args.warmup, 3)
 
@@ -446,6 +533,7 @@ def main():
                     "achieved": round(con_tops, 1), "peak": tensor_peak, "unit": "TOPS",
                     "frac": round(con_tops / tensor_peak, 4)}
     fused_gemm = measure_fused_configs(dev, stream, flush, int8_peak_tops)
+    elementwise = measure_elementwise(dev, stream, flush, hbm_peak)
 
     # ---- drop-in ABI route (rank 0, N=1) and CPU baseline
     dropin = cpu = None
@@ -477,7 +565,7 @@ def main():
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(),
                 "gpu_launches": int(net.launch_count * args.steps),
                 "launches_per_step": net.launch_count, "contractions": contractions,
-                "fused_gemm": fused_gemm, "kernels": kernels}
+                "fused_gemm": fused_gemm, "elementwise": elementwise, "kernels": kernels}
         if dropin:
             line["e2e_dropin"] = dropin
         print(json.dumps(line), flush=True)

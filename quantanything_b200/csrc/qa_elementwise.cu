@@ -21,6 +21,26 @@ namespace qa {
 
 // ------------------------------------------------------------ kernels --
 
+// clamp(mbqm(x + pre[c], mult[c], shift[c]) + post[c] + zp): the exact
+// high-word form when the channel's multiplier and shift allow it (the
+// usual case: M0 in [2^30, 2^31)), else the 128-bit mbqm.
+__device__ __forceinline__ int64_t requant_channel(int64_t x, int64_t c,
+                                                   const int64_t* __restrict__ mult,
+                                                   const int64_t* __restrict__ shift,
+                                                   const int64_t* __restrict__ pre,
+                                                   const int64_t* __restrict__ post, int64_t zp,
+                                                   int64_t qmin, int64_t qmax) {
+  const int64_t pb = pre ? __ldg(pre + c) : 0;
+  const int64_t qb = (post ? __ldg(post + c) : 0) + zp;
+  const int64_t m = __ldg(mult + c), s = __ldg(shift + c);
+  const int64_t v = x + pb;
+  // the sum x + pre stays exact in int64 (|x| < 2^63 - |pre| for the inputs
+  // the reference accepts); the bias add may not overflow the clamp bounds
+  if (hi32_applies(m, 31 + s) && qb > -(1ll << 62) && qb < (1ll << 62))
+    return requant_hi32(v, m, (int)(31 + s), qb, qmin, qmax);
+  return requant_exact(v, m, s, qb, qmin, qmax);
+}
+
 // acc viewed as [outer, C, inner]; channel = (i / inner) % C.
 template <typename TAcc>
 __global__ void requantize_kernel(const TAcc* __restrict__ acc, int32_t* __restrict__ out,
@@ -33,9 +53,31 @@ __global__ void requantize_kernel(const TAcc* __restrict__ acc, int32_t* __restr
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int64_t c = (inner == 1 ? i : i / inner) % C;
-    const int64_t pb = pre ? pre[c] : 0;
-    const int64_t qb = (post ? post[c] : 0) + zp;
-    out[i] = (int32_t)requant_exact((int64_t)acc[i] + pb, mult[c], shift[c], qb, qmin, qmax);
+    out[i] = (int32_t)requant_channel((int64_t)acc[i], c, mult, shift, pre, post, zp, qmin, qmax);
+  }
+}
+
+// Four consecutive elements per thread with 16-byte int32 loads and stores
+// (total % 4 == 0, 16-byte aligned pointers).
+__global__ void requantize_i32x4_kernel(const int32_t* __restrict__ acc, int32_t* __restrict__ out,
+                                        int64_t quads, int64_t C, int64_t inner,
+                                        const int64_t* __restrict__ mult,
+                                        const int64_t* __restrict__ shift,
+                                        const int64_t* __restrict__ pre,
+                                        const int64_t* __restrict__ post, int64_t zp,
+                                        int64_t qmin, int64_t qmax) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += stride) {
+    const int4 v = __ldg(reinterpret_cast<const int4*>(acc) + i);
+    const int32_t a[4] = {v.x, v.y, v.z, v.w};
+    int32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t e = 4 * i + k;
+      const int64_t c = (inner == 1 ? e : e / inner) % C;
+      o[k] = (int32_t)requant_channel((int64_t)a[k], c, mult, shift, pre, post, zp, qmin, qmax);
+    }
+    reinterpret_cast<int4*>(out)[i] = make_int4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -129,6 +171,13 @@ static bool launch_requantize(const TAcc* acc, int32_t* out, int64_t outer, int6
                               int64_t qmin, int64_t qmax, cudaStream_t st) {
   const int64_t total = outer * C * inner;
   if (total <= 0) return true;
+  if (sizeof(TAcc) == 4 && total % 4 == 0 &&
+      ((reinterpret_cast<uintptr_t>(acc) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+    requantize_i32x4_kernel<<<grid_for(total / 4, kThreads, 2), kThreads, 0, st>>>(
+        reinterpret_cast<const int32_t*>(acc), out, total / 4, C, inner, mult, shift, pre, post,
+        zp, qmin, qmax);
+    return !cuda_failed(cudaGetLastError(), "requantize launch");
+  }
   requantize_kernel<TAcc><<<grid_for(total, kThreads, 4), kThreads, 0, st>>>(
       acc, out, total, C, inner, mult, shift, pre, post, zp, qmin, qmax);
   return !cuda_failed(cudaGetLastError(), "requantize launch");

@@ -491,10 +491,16 @@ __global__ void map_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int64_t 
   ptx::pdl_wait();
   const int64_t total = rows * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+  // two vectors in flight per thread
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+    const int64_t i2 = i + stride;
     const int64_t r = i / groups, g = i - r * groups;
+    const int64_t r2 = i2 / groups, g2 = i2 - r2 * groups;
     const uint4 v = *reinterpret_cast<const uint4*>(x.p + r * x.stride + g * 16);
+    uint4 v2 = make_uint4(0, 0, 0, 0);
+    if (i2 < total) v2 = *reinterpret_cast<const uint4*>(x.p + r2 * x.stride + g2 * 16);
     *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = map16(tab, v);
+    if (i2 < total) *reinterpret_cast<uint4*>(y + r2 * y_stride + g2 * 16) = map16(tab, v2);
   }
 }
 
@@ -507,8 +513,9 @@ __global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
                                    int64_t ma, int64_t sa, int64_t zb, int64_t mb, int64_t sb,
                                    int64_t sign, int64_t zo, int64_t qmin, int64_t qmax) {
   __shared__ int64_t ta[256], tb[256];
+  __shared__ int32_t ta32[256], tb32[256];
   ptx::pdl_launch_dependents();
-  int ok = 1;
+  int ok = 1, ok32 = 1;
   for (int e = threadIdx.x; e < 256; e += blockDim.x) {
     const int64_t va = a.is_signed ? (int64_t)(int8_t)e : (int64_t)e;
     const int64_t vb = b.is_signed ? (int64_t)(int8_t)e : (int64_t)e;
@@ -520,8 +527,15 @@ __global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
     ok &= x2.hi == ((int64_t)x2.lo >> 63) && (int64_t)x2.lo > -lim && (int64_t)x2.lo < lim;
     ta[e] = (int64_t)x1.lo;
     tb[e] = (int64_t)x2.lo;
+    const int64_t l30 = (int64_t)1 << 30;
+    ok32 &= ta[e] > -l30 && ta[e] < l30 && tb[e] > -l30 && tb[e] < l30;
+    ta32[e] = (int32_t)ta[e];
+    tb32[e] = (int32_t)tb[e];
   }
   const bool tables = __syncthreads_and(ok);
+  // both terms and the zero point within 2^30 each: the sum is exact in int32
+  const bool tables32 = __syncthreads_and(ok32) && zo > -(1 << 30) && zo < (1 << 30) &&
+                        qmin > -(1ll << 31) && qmax < (1ll << 31);
   ptx::pdl_wait();
   const int64_t total = rows * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -536,7 +550,11 @@ __global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
       const int ea = (wa[j >> 2] >> (8 * (j & 3))) & 0xFF;
       const int eb = (wb[j >> 2] >> (8 * (j & 3))) & 0xFF;
       int64_t q;
-      if (tables) {
+      if (tables32) {
+        int32_t q32 = ta32[ea] + tb32[eb] + (int32_t)zo;
+        q32 = q32 < (int32_t)qmin ? (int32_t)qmin : (q32 > (int32_t)qmax ? (int32_t)qmax : q32);
+        q = q32;
+      } else if (tables) {
         q = ta[ea] + tb[eb] + zo;
         q = q < qmin ? qmin : (q > qmax ? qmax : q);
       } else {
@@ -560,6 +578,11 @@ __global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const bool small = small_applies(m, s);
+  // the centred operands lie within +-2^9, so |p| < 2^18 always fits int32
+  const bool small32 = small && za > -(1 << 20) && za < (1 << 20) && zb > -(1 << 20) &&
+                       zb < (1 << 20);
+  const int ts = (int)(31 + s);
+  const int64_t rnd = small ? ((int64_t)1 << (ts - 1)) : 0;
   const int64_t total = rows * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -575,7 +598,12 @@ __global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
       const int64_t p = ((a.is_signed ? (int64_t)(int8_t)ea : ea) - za) *
                         ((b.is_signed ? (int64_t)(int8_t)eb : eb) - zb);
       int64_t q;
-      if (small) {
+      if (small32) {
+        // |p| < 2^31 and |m| < 2^31: one 32 x 32 -> 64-bit product
+        const int64_t t = ((int64_t)(int32_t)p * (int64_t)(int32_t)m + rnd) >> ts;
+        q = t + zo;
+        q = q < qmin ? qmin : (q > qmax ? qmax : q);
+      } else if (small) {
         q = mbqm_small(p, m, (int)(31 + s)) + zo;
         q = q < qmin ? qmin : (q > qmax ? qmax : q);
       } else {

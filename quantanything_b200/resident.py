@@ -88,6 +88,8 @@ _DEV_SIGNATURES = {
     "qa_maxpool_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 16 + [_P]),
     "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
     "qa_device_status_dev": (ctypes.c_int, [_P]),
+    "qa_requantize_i32_dev": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64,
+                                             _I64, _I64, _P]),
     "qa_conv_input_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P, _I64,
                                                ctypes.c_double, _I64, _I64, _P]),
     "qa_vit_embed_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _P, _P, _P, _I64, _I64, _P,
