@@ -652,6 +652,59 @@ __global__ void maxpool_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int6
   }
 }
 
+// Stride-1 MaxPool (SPPF's k5 s1 p2) tiled and separable: a block stages
+// the input rows and columns of an 8 x 32 output tile (plus the window's
+// halo, out-of-image taps = the pad value) for one 16-channel group in
+// shared memory, takes the maxima along each row, then along each column.
+constexpr int kMpTH = 8, kMpTW = 32, kMpMaxK = 7;
+
+__global__ void __launch_bounds__(256)
+    maxpool_bytes16_s1_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride, int64_t H,
+                              int64_t W, int64_t groups, int KH, int KW, int64_t PH, int64_t PW,
+                              int64_t OH, int64_t OW, int64_t tiles_x, int64_t tiles_y,
+                              uint32_t pad_word) {
+  __shared__ uint4 s_in[kMpTH + kMpMaxK - 1][kMpTW + kMpMaxK - 1];
+  __shared__ uint4 s_row[kMpTH + kMpMaxK - 1][kMpTW];
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t t = blockIdx.x;
+  const int64_t tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, ng = t / (tiles_x * tiles_y);
+  const int64_t n = ng / groups, g = ng - n * groups;
+  const int64_t oy0 = ty * kMpTH, ox0 = tx * kMpTW;
+  const int rows = kMpTH + KH - 1, cols = kMpTW + KW - 1;
+  auto vmax = [&](uint4 a, uint4 b) {
+    return x.is_signed ? make_uint4(__vmaxs4(a.x, b.x), __vmaxs4(a.y, b.y), __vmaxs4(a.z, b.z),
+                                    __vmaxs4(a.w, b.w))
+                       : make_uint4(__vmaxu4(a.x, b.x), __vmaxu4(a.y, b.y), __vmaxu4(a.z, b.z),
+                                    __vmaxu4(a.w, b.w));
+  };
+  for (int i = threadIdx.x; i < rows * cols; i += blockDim.x) {
+    const int r = i / cols, c = i - r * cols;
+    const int64_t iy = oy0 - PH + r, ix = ox0 - PW + c;
+    uint4 v = make_uint4(pad_word, pad_word, pad_word, pad_word);
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+      v = __ldg(reinterpret_cast<const uint4*>(x.p + ((n * H + iy) * W + ix) * x.stride +
+                                               g * 16));
+    s_in[r][c] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows * kMpTW; i += blockDim.x) {
+    const int r = i / kMpTW, c = i - r * kMpTW;
+    uint4 m = s_in[r][c];
+    for (int k = 1; k < KW; ++k) m = vmax(m, s_in[r][c + k]);
+    s_row[r][c] = m;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kMpTH * kMpTW; i += blockDim.x) {
+    const int r = i / kMpTW, c = i - r * kMpTW;
+    const int64_t oy = oy0 + r, ox = ox0 + c;
+    if (oy >= OH || ox >= OW) continue;
+    uint4 m = s_row[r][c];
+    for (int k = 1; k < KH; ++k) m = vmax(m, s_row[r + k][c]);
+    *reinterpret_cast<uint4*>(y + ((n * OH + oy) * OW + ox) * y_stride + g * 16) = m;
+  }
+}
+
 __host__ __device__ inline bool vec16_ok(const void* p, int64_t stride) {
   return ((reinterpret_cast<uintptr_t>(p) | (uint64_t)stride) & 15) == 0;
 }
@@ -913,6 +966,20 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
   clear_error();
   const int64_t total = N * OH * OW * C;
   if (total == 0) return 0;
+  if (C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride) && SH == 1 && SW == 1 &&
+      DH == 1 && DW == 1 && KH <= kMpMaxK && KW <= kMpMaxK && KH >= 1 && KW >= 1) {
+    const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
+    const int64_t tiles_x = (OW + kMpTW - 1) / kMpTW, tiles_y = (OH + kMpTH - 1) / kMpTH;
+    const int64_t blocks = tiles_x * tiles_y * N * (C / 16);
+    if (blocks < 0x7FFFFFFF)
+      return launch_ex(maxpool_bytes16_s1_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                       (cudaStream_t)stream, true,
+                       ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
+                       static_cast<uint8_t*>(y), y_stride, H, W, C / 16, (int)KH, (int)KW, PH,
+                       PW, OH, OW, tiles_x, tiles_y, pw)
+                 ? 0
+                 : last_status();
+  }
   if (C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride)) {
     const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
     return launch_ex(maxpool_bytes16_kernel, dim3(grid_for(N * OH * OW * (C / 16), 256)),
