@@ -181,6 +181,9 @@ def measure_elementwise(dev, stream, flush, hbm_peak, reps=5):
         "requantize i32 -> i32": (8 * n, lambda: raw.qa_requantize_i32_dev(
             acc.data_ptr(), q32.data_ptr(), rows, C, 1, mult.data_ptr(), shift.data_ptr(), None,
             None, 0, -128, 127, st)),
+        "requantize i32 -> i32, NCHW (inner 4096)": (8 * n, lambda: raw.qa_requantize_i32_dev(
+            acc.data_ptr(), q32.data_ptr(), rows // 4096, C, 4096, mult.data_ptr(),
+            shift.data_ptr(), None, None, 0, -128, 127, st)),
         "quantize f32 -> nhwc": (img.numel() * 4 + rows * 4, lambda: raw.qa_quantize_to_nhwc_dev(
             img.data_ptr(), y.data_ptr(), 512, 3, 64, 64, 4, 0.0235, 0, -128, 127, st)),
     }

@@ -71,11 +71,25 @@ __global__ void requantize_i32x4_kernel(const int32_t* __restrict__ acc, int32_t
     const int4 v = __ldg(reinterpret_cast<const int4*>(acc) + i);
     const int32_t a[4] = {v.x, v.y, v.z, v.w};
     int32_t o[4];
+    if (inner % 4 == 0) {
+      // the quad lies in one channel (NCHW accumulators): its parameters once
+      const int64_t c = (4 * i / inner) % C;
+      const int64_t pb = pre ? __ldg(pre + c) : 0;
+      const int64_t qb = (post ? __ldg(post + c) : 0) + zp;
+      const int64_t m = __ldg(mult + c), s = __ldg(shift + c);
+      const bool hi = hi32_applies(m, 31 + s) && qb > -(1ll << 62) && qb < (1ll << 62);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int64_t e = 4 * i + k;
-      const int64_t c = (inner == 1 ? e : e / inner) % C;
-      o[k] = (int32_t)requant_channel((int64_t)a[k], c, mult, shift, pre, post, zp, qmin, qmax);
+      for (int k = 0; k < 4; ++k)
+        o[k] = (int32_t)(hi ? requant_hi32((int64_t)a[k] + pb, m, (int)(31 + s), qb, qmin, qmax)
+                            : requant_exact((int64_t)a[k] + pb, m, s, qb, qmin, qmax));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int64_t e = 4 * i + k;
+        const int64_t c = (inner == 1 ? e : e / inner) % C;
+        o[k] = (int32_t)requant_channel((int64_t)a[k], c, mult, shift, pre, post, zp, qmin,
+                                        qmax);
+      }
     }
     reinterpret_cast<int4*>(out)[i] = make_int4(o[0], o[1], o[2], o[3]);
   }
