@@ -885,6 +885,25 @@ class ResidentNet:
         self._launch_all(torch.cuda.current_stream(self.device).cuda_stream)
         return self.out_f32
 
+    def forward_traced(self, x=None):
+        """forward_device with one NVTX range per launch, named
+        ``step <i>: <layer label>`` (the labels of step_costs), so that a
+        profiler can attribute kernels to layers (``ncu --nvtx
+        --nvtx-include "step 3: *"`` captures one layer)."""
+        nvtx = torch.cuda.nvtx
+        labels = [c[0] for c in self.step_costs()]
+        if x is not None:
+            self.x_dev.copy_(x)
+
+        def mark(i):
+            nvtx.range_pop()
+            if i + 1 < len(labels):
+                nvtx.range_push(f"step {i + 1}: {labels[i + 1]}")
+
+        nvtx.range_push(f"step 0: {labels[0]}")
+        self._launch_all(torch.cuda.current_stream(self.device).cuda_stream, on_step=mark)
+        return self.out_f32
+
     def capture(self):
         """Captures the forward in a CUDA graph (after one eager warm-up)."""
         torch.cuda.synchronize(self.device)

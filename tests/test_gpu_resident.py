@@ -144,3 +144,13 @@ def test_pipelined_host_calls_match_single_runs(gpu_lib):
     torch.cuda.current_stream().synchronize()
     for w, o in zip(want, outs):
         np.testing.assert_array_equal(o.numpy(), w)
+
+
+def test_traced_forward_matches_plain(gpu_lib):
+    """forward_traced (NVTX range per launch) computes the same outputs."""
+    net, _, _ = _net("yolo_mini_int8", gpu_lib, 2)
+    x = networks.images(2, 32, seed=3)
+    plain = _run(net, x).copy()
+    net.forward_traced(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(net.out_q.cpu().numpy(), plain)
