@@ -249,6 +249,13 @@ int qa_mul_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, const vo
                      int64_t b_stride, int64_t b_signed, void* y, int64_t y_stride,
                      int64_t rows, int64_t C, int64_t za, int64_t zb, int64_t m, int64_t s,
                      int64_t zo, int64_t qmin, int64_t qmax, void* stream);
+/* Inference BatchNorm (quant_layers.py:405-441, qa_kernels.cpp:207-228 with
+ * a post-bias): out = clamp(mbqm(x - zp_in, mult[c], shift[c]) + post[c] +
+ * zp_out), per-channel int64 device arrays. */
+int qa_bn_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
+                    int64_t y_stride, int64_t rows, int64_t C, int64_t zp_in,
+                    const int64_t* mult, const int64_t* shift, const int64_t* post,
+                    int64_t zp_out, int64_t qmin, int64_t qmax, void* stream);
 int qa_rescale_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
                          int64_t y_stride, int64_t rows, int64_t C, int64_t identity,
                          int64_t zp_in, int64_t m, int64_t s, int64_t zp_out, int64_t qmin,
@@ -388,6 +395,10 @@ int qa_rescale16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, 
                      int64_t y_stride, int64_t rows, int64_t C, int64_t identity, int64_t zp_in,
                      int64_t m, int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
                      void* stream);
+int qa_bn16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, int64_t y_plane,
+                int64_t y_stride, int64_t rows, int64_t C, int64_t zp_in, const int64_t* mult,
+                const int64_t* shift, const int64_t* post, int64_t zp_out, int64_t qmin,
+                int64_t qmax, void* stream);
 int qa_mul16_dev(const void* a, int64_t a_plane, int64_t a_stride, const void* b,
                  int64_t b_plane, int64_t b_stride, void* y, int64_t y_plane, int64_t y_stride,
                  int64_t rows, int64_t C, int64_t za, int64_t zb, int64_t m, int64_t s,

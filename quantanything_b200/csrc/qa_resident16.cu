@@ -264,6 +264,24 @@ __global__ void mul16_kernel(Planes16 a, Planes16 b, uint8_t* __restrict__ y, in
   }
 }
 
+// Inference BatchNorm on int16 planes (quant_layers.py:405-441).
+__global__ void bn16_kernel(Planes16 x, uint8_t* __restrict__ y, int64_t y_plane,
+                            int64_t y_stride, int64_t rows, int64_t C, int64_t zp_in,
+                            const int64_t* __restrict__ mult, const int64_t* __restrict__ shift,
+                            const int64_t* __restrict__ post, int64_t zp_out, int64_t qmin,
+                            int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    plane16_store(y + r * y_stride + c, y_plane,
+                  requant_exact(at(x, r, c) - zp_in, __ldg(mult + c), __ldg(shift + c),
+                                __ldg(post + c) + zp_out, qmin, qmax));
+  }
+}
+
 // ------------------------------------------------------------- MaxPool --
 // Integer MaxPool as the reference runs it through float_ops on int32
 // tensors, out-of-image taps padded with qmin (quant_layers.py:647-648).
@@ -574,6 +592,26 @@ QA_API int qa_mul16_dev(const void* a, int64_t a_plane, int64_t a_stride, const 
                    Planes16{static_cast<const uint8_t*>(b), b_plane, b_stride},
                    static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, za, zb, m, s, zo, qmin,
                    qmax)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_bn16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y,
+                       int64_t y_plane, int64_t y_stride, int64_t rows, int64_t C,
+                       int64_t zp_in, const int64_t* mult, const int64_t* shift,
+                       const int64_t* post, int64_t zp_out, int64_t qmin, int64_t qmax,
+                       void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  if (!mult || !shift || !post) {
+    set_error(kBadArgument, "qa_bn16_dev: null parameter array");
+    return last_status();
+  }
+  return launch_ex(bn16_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   Planes16{static_cast<const uint8_t*>(x), x_plane, x_stride},
+                   static_cast<uint8_t*>(y), y_plane, y_stride, rows, C, zp_in, mult, shift,
+                   post, zp_out, qmin, qmax)
              ? 0
              : last_status();
 }

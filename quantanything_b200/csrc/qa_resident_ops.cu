@@ -756,6 +756,26 @@ __global__ void mul_bytes_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y
   }
 }
 
+// Inference BatchNorm (quant_layers.py:405-441): per channel
+// clamp(mbqm(x - zp_in, mult[c], shift[c]) + post[c] + zp_out).
+__global__ void bn_bytes_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride,
+                                int64_t rows, int64_t C, int64_t zp_in,
+                                const int64_t* __restrict__ mult,
+                                const int64_t* __restrict__ shift,
+                                const int64_t* __restrict__ post, int64_t zp_out, int64_t qmin,
+                                int64_t qmax) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = rows * C;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / C, c = i - r * C;
+    const int64_t v = bval(x.p + r * x.stride + c, x.is_signed) - zp_in;
+    y[r * y_stride + c] = (uint8_t)requant_exact(v, __ldg(mult + c), __ldg(shift + c),
+                                                 __ldg(post + c) + zp_out, qmin, qmax);
+  }
+}
+
 // NHWC bytes [N, HW, C] <-> NCHW int32.
 __global__ void bytes_to_i32_kernel(ByteView x, int32_t* __restrict__ y, int64_t N, int64_t HW,
                                     int64_t C) {
@@ -1466,6 +1486,25 @@ QA_API int qa_mul_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, c
                    ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
                    ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
                    static_cast<uint8_t*>(y), y_stride, rows, C, za, zb, m, s, zo, qmin, qmax)
+             ? 0
+             : last_status();
+}
+
+QA_API int qa_bn_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void* y,
+                           int64_t y_stride, int64_t rows, int64_t C, int64_t zp_in,
+                           const int64_t* mult, const int64_t* shift, const int64_t* post,
+                           int64_t zp_out, int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (rows * C == 0) return 0;
+  if (!mult || !shift || !post) {
+    set_error(kBadArgument, "qa_bn_bytes_dev: null parameter array");
+    return last_status();
+  }
+  return launch_ex(bn_bytes_kernel, dim3(grid_for(rows * C, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true,
+                   ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
+                   static_cast<uint8_t*>(y), y_stride, rows, C, zp_in, mult, shift, post, zp_out,
+                   qmin, qmax)
              ? 0
              : last_status();
 }

@@ -119,6 +119,17 @@ def _conv(node, inputs, opset, **kw):
     return y
 
 
+@op("BatchNormalization")
+def _batchnorm(node, inputs, opset, **kw):
+    """Inference BatchNorm (float_ops.py:200-206): x * a + b with
+    a = gamma / sqrt(var + eps), b = beta - a * mean, in float32."""
+    x, gamma, beta, mean, var = inputs[:5]
+    shape = [1, -1] + [1] * (x.ndim - 2)
+    a = gamma / np.sqrt(var + node.attr("epsilon", 1e-5))
+    b = beta - a * mean
+    return (x * a.reshape(shape) + b.reshape(shape)).astype(np.float32)
+
+
 @op("Gemm")
 def _gemm(node, inputs, opset, **kw):
     a, b = inputs[0], inputs[1]

@@ -183,6 +183,26 @@ def mul_mini(seed=0, size=32, classes=10, width=16):
     return b.build(x, ["N", 3, size, size], y)
 
 
+def bn_mini(seed=0, size=32, classes=10, width=16):
+    """Small graph with an unfolded inference BatchNormalization after a
+    bias-free conv (some channels with negative gamma), i.e. the integer
+    BatchNorm layer (quant_layers.py:405-441) running on its own."""
+    b = GraphBuilder(seed)
+    x = "images"
+    y = b.conv_silu(x, 3, width, 3, 2)
+    y = b.conv(y, width, 2 * width, 3, 2, bn=False)
+    c = 2 * width
+    gamma = b.rng.uniform(0.5, 1.5, c) * np.where(np.arange(c) % 5 == 0, -1.0, 1.0)
+    params = [gamma, b.rng.normal(0.0, 0.1, c), b.rng.normal(0.0, 0.1, c),
+              b.rng.uniform(0.5, 1.5, c)]
+    y = b.op("BatchNormalization", [y] + [b.const(v.astype(np.float32), "bn") for v in params],
+             epsilon=1e-3)
+    y = b.silu(y)
+    y = b.conv_silu(y, 2 * width, 2 * width, 3)
+    y = b.head(y, 2 * width, classes)
+    return b.build(x, ["N", 3, size, size], y)
+
+
 def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, mlp=4,
         std=None):
     """A Vision Transformer in the reference's post-pass form (the structure

@@ -30,6 +30,7 @@ from quantanything_b200 import native
 from quantanything_b200.layers import (
     ActivationQuantize,
     AddQuantize,
+    BatchNormalizationQuantize,
     ConcatQuantize,
     ConvQuantize,
     GemmQuantize,
@@ -85,6 +86,8 @@ _DEV_SIGNATURES = {
     "qa_rescale_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 10 + [_P]),
     "qa_mul_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P] + [_I64] * 10
                          + [_P]),
+    "qa_bn_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P,
+                                       _I64, _I64, _I64, _P]),
     "qa_maxpool_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 16 + [_P]),
     "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
     "qa_device_status_dev": (ctypes.c_int, [_P]),
@@ -334,6 +337,8 @@ class ResidentNet:
                 self._plan_add(layer)
             elif isinstance(layer, MulQuantize):
                 self._plan_mul(layer)
+            elif isinstance(layer, BatchNormalizationQuantize):
+                self._plan_bn(layer)
             elif node.op_type == "Softmax" and node.outputs[0] in g.outputs:
                 self._plan_softmax(layer)
             else:
@@ -714,6 +719,18 @@ class ResidentNet:
         if copy is not None:
             self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
 
+    def _plan_bn(self, layer):
+        node = layer.node
+        x = self._views[node.inputs[0]]
+        N, C, H, W = self._shapes[node.outputs[0]]
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, H, W, C)
+        self._views[node.outputs[0]] = view
+        params = [self._dev(np.broadcast_to(np.asarray(v, np.int64), (C,)).copy(), np.int64)
+                  for v in (layer.q_mult, layer.shift, layer.q_B)]
+        self.steps.append(("bn", (layer, x, view, params)))
+        if copy is not None:
+            self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
+
     def _plan_softmax(self, layer):
         node = layer.node
         x = self._views[node.inputs[0]]
@@ -838,6 +855,12 @@ class ResidentNet:
                                           b.pix_stride, int(b.signed), y.ptr, y.pix_stride,
                                           a.N * a.H * a.W, a.C, qa.zp, ma, sa, qb.zp, mb, sb,
                                           layer._sign, o.zp, o.qmin, o.qmax, st)
+            elif kind == "bn":
+                layer, x, y, (mdev, sdev, bdev) = payload
+                rc = raw.qa_bn_bytes_dev(x.ptr, x.pix_stride, int(x.signed), y.ptr, y.pix_stride,
+                                         x.N * x.H * x.W, x.C, layer.in_zp, mdev.data_ptr(),
+                                         sdev.data_ptr(), bdev.data_ptr(), layer.out_zp,
+                                         layer.out_qmin, layer.out_qmax, st)
             elif kind == "mul":
                 layer, a, b, y = payload
                 qa, qb = layer.in_qp

@@ -66,6 +66,8 @@ _DEV16_SIGNATURES = {
     "qa_maxpool16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64] + [_I64] * 15 + [_P]),
     "qa_mul16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64]
                      + [_I64] * 9 + [_P]),
+    "qa_bn16_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P,
+                                   _I64, _I64, _I64, _P]),
 }
 
 
@@ -211,6 +213,12 @@ class ResidentNet16(ResidentNet):
                                       y.ptr, y.plane, y.pix_stride, a.N * a.H * a.W, a.C, qa.zp,
                                       ma, sa, qb.zp, mb, sb, layer._sign, o.zp, o.qmin, o.qmax,
                                       st)
+            elif kind == "bn":
+                layer, x, y, (mdev, sdev, bdev) = payload
+                rc = raw.qa_bn16_dev(x.ptr, x.plane, x.pix_stride, y.ptr, y.plane, y.pix_stride,
+                                     x.N * x.H * x.W, x.C, layer.in_zp, mdev.data_ptr(),
+                                     sdev.data_ptr(), bdev.data_ptr(), layer.out_zp,
+                                     layer.out_qmin, layer.out_qmax, st)
             elif kind == "mul":
                 layer, a, b, y = payload
                 qa, qb = layer.in_qp
