@@ -125,7 +125,7 @@ class QuantContainer:
             out[name] = self.lib.quantize_f32(value, qp.scale, qp.zp, qp.qmin, qp.qmax)
         return out
 
-    def _execute(self, x, mode):
+    def _execute(self, x, mode, trace=None):
         graph = self.graph
         if mode != "calibrate" and not self.calibrated:
             raise ValueError("Container is not calibrated; call calibrate().")
@@ -151,6 +151,8 @@ class QuantContainer:
             layer = self.quant_layers[node.name]
             ins = [env[n] for n in layer.data_inputs]
             outs = layer.calibrate(ins) if mode == "calibrate" else layer.quantized_infer_integer(ins)
+            if trace is not None:
+                trace(layer, outs)
             env.update(zip(node.outputs, outs))
             for n in set(layer.data_inputs):
                 if last_use.get(n) == idx and n not in keep:
@@ -163,6 +165,32 @@ class QuantContainer:
                 value = self.lib.dequantize_f32(value, qp.scale, qp.zp)
             results.append(value)
         return results[0] if len(results) == 1 else results
+
+    def compare_layers(self, x, mode="integer"):
+        """Per-layer error of the integer pass against the float pass
+        (quant_container.py:196-223): ``{layer name: {"max_diff",
+        "mean_diff", "layer_type"}}``, each layer's dequantized outputs
+        against the float run's on the same input.  The fake-quant mode of
+        the reference is not part of this build."""
+        if mode != "integer":
+            raise ValueError("mode must be 'integer' (fake-quant is not provided)")
+        float_env = float_ops.run_float(self.graph, x, keep_all=True, lib=self.lib)
+        comparison = {}
+
+        def trace(layer, outs):
+            diffs = []
+            for name, q in zip(layer.node.outputs, outs):
+                qp = self.qparams[name]
+                deq = self.lib.dequantize_f32(np.asarray(q), qp.scale, qp.zp)
+                diffs.append(np.abs(float_env[name] - deq))
+            comparison[layer.name] = {
+                "max_diff": float(max(d.max() for d in diffs)),
+                "mean_diff": float(np.mean([d.mean() for d in diffs])),
+                "layer_type": layer.node.op_type,
+            }
+
+        self._execute(x, mode, trace=trace)
+        return comparison
 
     def run_integer_raw(self, x):
         """Integer pass returning the graph outputs as int32 tensors (no

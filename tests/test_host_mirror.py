@@ -61,3 +61,18 @@ def test_load_rejects_mismatched_qparams(oracle, tmp_path):
     (tmp_path / "bad.json").write_text(json.dumps(payload))
     with pytest.raises(ValueError):
         QuantContainer.load(networks.yolo_mini(width=16), tmp_path / "bad.json", lib=oracle)
+
+
+def test_compare_layers_reports_every_layer(oracle):
+    """compare_layers (quant_container.py:196-223): one entry per layer, the
+    integer pass tracking the float pass (small errors on an int8 graph)."""
+    from quantanything_b200 import networks
+    from quantanything_b200.container import QuantContainer
+
+    g = networks.yolo_mini(width=16)
+    qc = QuantContainer.load(g, GRAPHS / "yolo_mini_int8.qjson", lib=oracle)
+    cmp = qc.compare_layers(networks.images(2, 32, seed=7))
+    assert set(cmp) == {layer.name for layer in qc.layers}
+    assert all(v["max_diff"] >= v["mean_diff"] >= 0 for v in cmp.values())
+    first_conv = next(k for k, v in cmp.items() if v["layer_type"] == "Conv")
+    assert cmp[first_conv]["mean_diff"] < 0.05
