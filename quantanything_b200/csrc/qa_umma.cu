@@ -25,7 +25,8 @@
 
 namespace qa {
 
-enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1, kEpiFused = 2 };
+// int32 accumulators out: NCHW conv layout, or row-major GEMM rows
+enum EpiMode : int { kEpiAcc32Nchw = 0, kEpiAcc32Row = 1 };
 
 constexpr int kBM = 128;          // tile rows (TMEM lanes)
 constexpr int kBKBytes = 128;     // K-block bytes (one 128-byte swizzle row)
@@ -297,9 +298,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1)
           } else {
             p.y[m * p.y_ctot + n] = (int32_t)acc;
           }
-        } else if constexpr (kEpi == kEpiFused) {
-          static_assert(TS::kNumAcc == 1, "fused epilogue is 8-bit only");
-          fused_epilogue_store(p.epi, (int64_t)(int32_t)v[0][j], m, n);
         }
       }
     }
