@@ -154,3 +154,21 @@ def test_traced_forward_matches_plain(gpu_lib):
     net.forward_traced(torch.from_numpy(x).cuda())
     torch.cuda.synchronize()
     np.testing.assert_array_equal(net.out_q.cpu().numpy(), plain)
+
+
+@pytest.mark.parametrize("name,cls", [("yolo_mini_int8", "ResidentNet"),
+                                      ("yolo_mini_uint8", "ResidentNet16"),
+                                      ("yolo_mini_int16", "ResidentNet16"),
+                                      ("vit_mini_int8", "ResidentViT")])
+def test_make_resident_picks_the_executor(gpu_lib, name, cls):
+    from quantanything_b200.resident import make_resident
+
+    meta = json.loads((GRAPHS / f"{name}.meta.json").read_text())
+    g = getattr(networks, meta["builder"])(**meta["kwargs"])
+    qc = QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=gpu_lib)
+    net = make_resident(qc, meta["eval_batch"])
+    assert type(net).__name__ == cls
+    x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
+    q = _run(net, x)
+    ref = np.load(GRAPHS / f"{name}.npz")["q"]
+    assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
