@@ -41,6 +41,13 @@ __device__ __forceinline__ int64_t requant_channel(int64_t x, int64_t c,
   return requant_exact(v, m, s, qb, qmin, qmax);
 }
 
+// The 128-bit form out of line: channels outside the high-word form are
+// rare, and inlining it would double the vector kernels' registers.
+__device__ __noinline__ int64_t requant_exact_slow(int64_t x, int64_t m, int64_t s, int64_t bias,
+                                                   int64_t lo, int64_t hi) {
+  return requant_exact(x, m, s, bias, lo, hi);
+}
+
 // acc viewed as [outer, C, inner]; channel = (i / inner) % C.
 template <typename TAcc>
 __global__ void requantize_kernel(const TAcc* __restrict__ acc, int32_t* __restrict__ out,
@@ -67,13 +74,16 @@ __global__ void requantize_i32x4_kernel(const int32_t* __restrict__ acc, int32_t
                                         const int64_t* __restrict__ post, int64_t zp,
                                         int64_t qmin, int64_t qmax) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += stride) {
-    const int4 v = __ldg(reinterpret_cast<const int4*>(acc) + i);
+  auto one = [&](const int4 v, const int64_t i) {
     const int32_t a[4] = {v.x, v.y, v.z, v.w};
     int32_t o[4];
     if (inner % 4 == 0) {
-      // the quad lies in one channel (NCHW accumulators): its parameters once
-      const int64_t c = (4 * i / inner) % C;
+      // the quad lies in one channel (NCHW accumulators): its parameters once;
+      // 32-bit division when the element index fits (a 64-bit one costs
+      // several times the instructions)
+      const int64_t c = quads < (1ll << 30)
+                            ? (int64_t)((uint32_t)(4 * i) / (uint32_t)inner % (uint32_t)C)
+                            : (4 * i / inner) % C;
       const int64_t pb = pre ? __ldg(pre + c) : 0;
       const int64_t qb = (post ? __ldg(post + c) : 0) + zp;
       const int64_t m = __ldg(mult + c), s = __ldg(shift + c);
@@ -81,7 +91,7 @@ __global__ void requantize_i32x4_kernel(const int32_t* __restrict__ acc, int32_t
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         o[k] = (int32_t)(hi ? requant_hi32((int64_t)a[k] + pb, m, (int)(31 + s), qb, qmin, qmax)
-                            : requant_exact((int64_t)a[k] + pb, m, s, qb, qmin, qmax));
+                            : requant_exact_slow((int64_t)a[k] + pb, m, s, qb, qmin, qmax));
     } else {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -91,8 +101,74 @@ __global__ void requantize_i32x4_kernel(const int32_t* __restrict__ acc, int32_t
                                         qmax);
       }
     }
-    reinterpret_cast<int4*>(out)[i] = make_int4(o[0], o[1], o[2], o[3]);
+    return make_int4(o[0], o[1], o[2], o[3]);
+  };
+  const int4* src = reinterpret_cast<const int4*>(acc);
+  int4* dst = reinterpret_cast<int4*>(out);
+  // four loads in flight per thread before any arithmetic
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < quads; i += 4 * stride) {
+    int4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dst[i + u * stride] = one(v[u], i + u * stride);
   }
+  for (; i < quads; i += stride) dst[i] = one(__ldg(src + i), i);
+}
+
+// Rows of C channels (inner == 1, C % 4 == 0) with a grid whose stride in
+// quads is a multiple of C / 4 (or that visits each quad once): every quad a
+// thread visits holds the same four channels, so their parameters and the
+// choice of requantize form are taken once, outside the loop.
+__global__ void requantize_rows_i32x4_kernel(const int32_t* __restrict__ acc,
+                                             int32_t* __restrict__ out, int64_t quads, int64_t C,
+                                             const int64_t* __restrict__ mult,
+                                             const int64_t* __restrict__ shift,
+                                             const int64_t* __restrict__ pre,
+                                             const int64_t* __restrict__ post, int64_t zp,
+                                             int64_t qmin, int64_t qmax) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i0 >= quads) return;
+  const int64_t c0 = 4 * (i0 % (C / 4));
+  // per channel: the high-word form's 31-bit multiplier and total shift, or
+  // ts = 0 for the exact form (its parameters are re-read on that cold path)
+  int64_t pb[4], qb[4];
+  int32_t m32[4], ts[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    pb[k] = pre ? __ldg(pre + c0 + k) : 0;
+    qb[k] = (post ? __ldg(post + c0 + k) : 0) + zp;
+    const int64_t m = __ldg(mult + c0 + k), sh = __ldg(shift + c0 + k);
+    const bool hi = hi32_applies(m, 31 + sh) && qb[k] > -(1ll << 62) && qb[k] < (1ll << 62);
+    m32[k] = hi ? (int32_t)m : 0;
+    ts[k] = hi ? (int32_t)(31 + sh) : 0;
+  }
+  const int4* src = reinterpret_cast<const int4*>(acc);
+  int4* dst = reinterpret_cast<int4*>(out);
+  auto one = [&](const int4 v) {
+    const int32_t a[4] = {v.x, v.y, v.z, v.w};
+    int32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      o[k] = (int32_t)(ts[k] ? requant_hi32((int64_t)a[k] + pb[k], m32[k], ts[k], qb[k], qmin,
+                                            qmax)
+                             : requant_exact_slow((int64_t)a[k] + pb[k], __ldg(mult + c0 + k),
+                                                  __ldg(shift + c0 + k), qb[k], qmin, qmax));
+    return make_int4(o[0], o[1], o[2], o[3]);
+  };
+  // four loads in flight per thread before any arithmetic (the quads a
+  // thread visits all hold its four channels)
+  int64_t i = i0;
+  for (; i + 3 * stride < quads; i += 4 * stride) {
+    int4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dst[i + u * stride] = one(v[u]);
+  }
+  for (; i < quads; i += stride) dst[i] = one(__ldg(src + i));
 }
 
 __global__ void rescale_kernel(const int32_t* __restrict__ x, int32_t* __restrict__ out,
@@ -187,6 +263,22 @@ static bool launch_requantize(const TAcc* acc, int32_t* out, int64_t outer, int6
   if (total <= 0) return true;
   if (sizeof(TAcc) == 4 && total % 4 == 0 &&
       ((reinterpret_cast<uintptr_t>(acc) | reinterpret_cast<uintptr_t>(out)) & 15) == 0) {
+    const int64_t quads = total / 4;
+    if (inner == 1 && C % 4 == 0) {
+      // grid stride a multiple of C / 4 quads: blocks a multiple of
+      // (C / 4) / gcd(C / 4, kThreads)
+      int64_t a = C / 4, b = kThreads;
+      while (b) { const int64_t t = a % b; a = b; b = t; }
+      const int64_t unit = (C / 4) / a;
+      int64_t grid = grid_for(quads, kThreads, 2);
+      if (grid * kThreads < quads) grid -= grid % unit;
+      if (grid >= 1) {
+        requantize_rows_i32x4_kernel<<<(unsigned)grid, kThreads, 0, st>>>(
+            reinterpret_cast<const int32_t*>(acc), out, quads, C, mult, shift, pre, post, zp,
+            qmin, qmax);
+        return !cuda_failed(cudaGetLastError(), "requantize launch");
+      }
+    }
     requantize_i32x4_kernel<<<grid_for(total / 4, kThreads, 2), kThreads, 0, st>>>(
         reinterpret_cast<const int32_t*>(acc), out, total / 4, C, inner, mult, shift, pre, post,
         zp, qmin, qmax);

@@ -78,6 +78,25 @@ def test_requantize_large_vs_oracle(gpu_lib, oracle):
                                   oracle.requantize(*args, pre_bias=pre, post_bias=post))
 
 
+@pytest.mark.parametrize("outer,C,inner", [(20000, 12, 1), (3001, 96, 1), (64, 20, 1),
+                                           (7, 16, 4096), (2, 40, 12)])
+def test_requantize_vector_layouts_vs_oracle(gpu_lib, oracle, outer, C, inner):
+    """The 16-byte forms: rows of C % 4 == 0 channels (parameters held per
+    thread across the grid-stride loop) and NCHW planes of inner % 4 == 0,
+    with channels on the high-word form and on the exact 128-bit one."""
+    rng = np.random.default_rng(outer + C + inner)
+    acc = rng.integers(-(2**31), 2**31, (outer, C, inner)).astype(np.int32)
+    mult = rng.integers(0, 2**31, C)
+    shift = rng.integers(15, 22, C)  # most outputs inside the int16 range
+    mult[::3] = rng.integers(-(2**31) + 1, 0, len(mult[::3]))  # negative: exact form
+    shift[1::5] = rng.integers(-3, 0, len(shift[1::5]))  # 31 + shift < 32: exact form
+    pre = rng.integers(-(2**28), 2**28, C)
+    post = rng.integers(-(2**10), 2**10, C)
+    args = (acc, outer, C, inner, mult, shift, -3, -(2**15), 2**15 - 1)
+    np.testing.assert_array_equal(gpu_lib.requantize(*args, pre_bias=pre, post_bias=post),
+                                  oracle.requantize(*args, pre_bias=pre, post_bias=post))
+
+
 def test_empty_inputs(gpu_lib):
     z = np.zeros((0,), np.int32)
     assert gpu_lib.rescale(z, 0, 1 << 30, 0, 0, -128, 127).shape == (0,)
