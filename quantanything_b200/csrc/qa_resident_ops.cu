@@ -504,11 +504,52 @@ __global__ void map_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int64_t 
   }
 }
 
+// Sum of the two rescaled terms on 128 bits (the tables' range check failed).
+__device__ __noinline__ int64_t add_bytes_exact(int64_t va, int64_t vb, int64_t za, int64_t ma,
+                                                int64_t sa, int64_t zb, int64_t mb, int64_t sb,
+                                                int64_t sign, int64_t zo, int64_t qmin,
+                                                int64_t qmax) {
+  const I128 x1 = mbqm(va - za, ma, sa);
+  I128 x2 = mbqm(vb - zb, mb, sb);
+  if (sign < 0) x2 = neg_i128(x2);
+  return clamp_i128(add_i128_i64(add_i128(x1, x2), zo), qmin, qmax);
+}
+
+// Grid-stride walk over the 16-byte vectors of two byte views (rows x
+// groups), two vectors per operand in flight per thread before `one`
+// combines them; 32-bit row division when the vector count allows.
+template <typename F>
+__device__ __forceinline__ void two_in_flight(const ByteView& a, const ByteView& b,
+                                              uint8_t* __restrict__ y, int64_t y_stride,
+                                              int64_t total, int64_t groups, F&& one) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const bool narrow = total < (1ll << 31);
+  auto row = [&](int64_t i) {
+    return narrow ? (int64_t)((uint32_t)i / (uint32_t)groups) : i / groups;
+  };
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+    const int64_t i2 = i + stride;
+    const int64_t r = row(i), g = i - r * groups;
+    const uint4 va = *reinterpret_cast<const uint4*>(a.p + r * a.stride + g * 16);
+    const uint4 vb = *reinterpret_cast<const uint4*>(b.p + r * b.stride + g * 16);
+    uint4 va2 = make_uint4(0, 0, 0, 0), vb2 = va2;
+    int64_t r2 = 0, g2 = 0;
+    if (i2 < total) {
+      r2 = row(i2);
+      g2 = i2 - r2 * groups;
+      va2 = *reinterpret_cast<const uint4*>(a.p + r2 * a.stride + g2 * 16);
+      vb2 = *reinterpret_cast<const uint4*>(b.p + r2 * b.stride + g2 * 16);
+    }
+    *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = one(va, vb);
+    if (i2 < total) *reinterpret_cast<uint4*>(y + r2 * y_stride + g2 * 16) = one(va2, vb2);
+  }
+}
+
 // Add: the two rescaled terms (sign applied to the second) as int64 tables;
 // exact when every entry's 128-bit value lies within +-2^61 (checked while
 // building: the sum of two terms and the zero point then cannot overflow),
 // else every element takes the 128-bit path.
-__global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y,
+__global__ void __launch_bounds__(256, 3) add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y,
                                    int64_t y_stride, int64_t rows, int64_t groups, int64_t za,
                                    int64_t ma, int64_t sa, int64_t zb, int64_t mb, int64_t sb,
                                    int64_t sign, int64_t zo, int64_t qmin, int64_t qmax) {
@@ -537,12 +578,7 @@ __global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
   const bool tables32 = __syncthreads_and(ok32) && zo > -(1 << 30) && zo < (1 << 30) &&
                         qmin > -(1ll << 31) && qmax < (1ll << 31);
   ptx::pdl_wait();
-  const int64_t total = rows * groups;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int64_t r = i / groups, g = i - r * groups;
-    const uint4 va4 = *reinterpret_cast<const uint4*>(a.p + r * a.stride + g * 16);
-    const uint4 vb4 = *reinterpret_cast<const uint4*>(b.p + r * b.stride + g * 16);
+  auto one = [&](const uint4 va4, const uint4 vb4) {
     const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
     uint32_t o[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -558,19 +594,17 @@ __global__ void add_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
         q = ta[ea] + tb[eb] + zo;
         q = q < qmin ? qmin : (q > qmax ? qmax : q);
       } else {
-        const I128 x1 = mbqm((a.is_signed ? (int64_t)(int8_t)ea : ea) - za, ma, sa);
-        I128 x2 = mbqm((b.is_signed ? (int64_t)(int8_t)eb : eb) - zb, mb, sb);
-        if (sign < 0) x2 = neg_i128(x2);
-        q = clamp_i128(add_i128_i64(add_i128(x1, x2), zo), qmin, qmax);
+        q = add_bytes_exact(a.is_signed ? (int64_t)(int8_t)ea : ea,
+                            b.is_signed ? (int64_t)(int8_t)eb : eb, za, ma, sa, zb, mb, sb, sign,
+                            zo, qmin, qmax);
       }
       o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
     }
-    *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-  }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  two_in_flight(a, b, y, y_stride, rows * groups, groups, one);
 }
 
-// Mul: (a - za)(b - zb) is at most 2^18 in magnitude, so one 64-bit product
-// requantizes exactly when the multiplier allows (small_applies).
 __global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__ y,
                                    int64_t y_stride, int64_t rows, int64_t groups, int64_t za,
                                    int64_t zb, int64_t m, int64_t s, int64_t zo, int64_t qmin,
@@ -583,12 +617,7 @@ __global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
                        zb < (1 << 20);
   const int ts = (int)(31 + s);
   const int64_t rnd = small ? ((int64_t)1 << (ts - 1)) : 0;
-  const int64_t total = rows * groups;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int64_t r = i / groups, g = i - r * groups;
-    const uint4 va4 = *reinterpret_cast<const uint4*>(a.p + r * a.stride + g * 16);
-    const uint4 vb4 = *reinterpret_cast<const uint4*>(b.p + r * b.stride + g * 16);
+  auto one = [&](const uint4 va4, const uint4 vb4) {
     const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
     uint32_t o[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -607,12 +636,13 @@ __global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
         q = mbqm_small(p, m, (int)(31 + s)) + zo;
         q = q < qmin ? qmin : (q > qmax ? qmax : q);
       } else {
-        q = requant_exact(p, m, s, zo, qmin, qmax);
+        q = requant_exact_cold(p, m, s, zo, qmin, qmax);
       }
       o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
     }
-    *reinterpret_cast<uint4*>(y + r * y_stride + g * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-  }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  two_in_flight(a, b, y, y_stride, rows * groups, groups, one);
 }
 
 // MaxPool: per-byte SIMD max over the window, out-of-image taps read the
