@@ -9,6 +9,7 @@
 // reference's 128-bit `mbqm`.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <vector>
@@ -171,6 +172,47 @@ __global__ void requantize_rows_i32x4_kernel(const int32_t* __restrict__ acc,
   for (; i < quads; i += stride) dst[i] = one(__ldg(src + i));
 }
 
+// NCHW planes (inner % 4 == 0): a block walks whole (image, channel) planes,
+// so the channel's parameters are taken once per plane; each thread keeps
+// up to four of the plane's quads in flight (predicated at the plane's end).
+__global__ void requantize_planes_i32x4_kernel(const int32_t* __restrict__ acc,
+                                               int32_t* __restrict__ out, int64_t planes,
+                                               int64_t C, int64_t plane_quads,
+                                               const int64_t* __restrict__ mult,
+                                               const int64_t* __restrict__ shift,
+                                               const int64_t* __restrict__ pre,
+                                               const int64_t* __restrict__ post, int64_t zp,
+                                               int64_t qmin, int64_t qmax) {
+  const int64_t bd = blockDim.x;
+  for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
+    const int64_t c = pl % C;
+    const int64_t pb = pre ? __ldg(pre + c) : 0;
+    const int64_t qb = (post ? __ldg(post + c) : 0) + zp;
+    const int64_t m = __ldg(mult + c), sh = __ldg(shift + c);
+    const bool hi = hi32_applies(m, 31 + sh) && qb > -(1ll << 62) && qb < (1ll << 62);
+    const int4* src = reinterpret_cast<const int4*>(acc) + pl * plane_quads;
+    int4* dst = reinterpret_cast<int4*>(out) + pl * plane_quads;
+    for (int64_t q = threadIdx.x; q < plane_quads; q += 4 * bd) {
+      int4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (q + u * bd < plane_quads) v[u] = __ldg(src + q + u * bd);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (q + u * bd >= plane_quads) break;
+        const int32_t a[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        int32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          o[k] = (int32_t)(hi ? requant_hi32((int64_t)a[k] + pb, m, (int)(31 + sh), qb, qmin,
+                                             qmax)
+                              : requant_exact_slow((int64_t)a[k] + pb, m, sh, qb, qmin, qmax));
+        dst[q + u * bd] = make_int4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
 __global__ void rescale_kernel(const int32_t* __restrict__ x, int32_t* __restrict__ out,
                                int64_t n, int64_t zp_in, int64_t m, int64_t s,
                                int64_t zp_out, int64_t qmin, int64_t qmax) {
@@ -278,6 +320,18 @@ static bool launch_requantize(const TAcc* acc, int32_t* out, int64_t outer, int6
             qmin, qmax);
         return !cuda_failed(cudaGetLastError(), "requantize launch");
       }
+    }
+    if (inner % 4 == 0 && inner / 4 >= 32) {
+      // threads: a quarter of the plane's quads (four in flight each), in warps
+      const int64_t pq = inner / 4;
+      const int threads = (int)std::min<int64_t>(256, ((pq + 3) / 4 + 31) / 32 * 32);
+      const int64_t planes = outer * C;
+      // one block per plane (the block scheduler balances the waves)
+      const unsigned grid = (unsigned)std::min<int64_t>(planes, 0x7FFFFFFF);
+      requantize_planes_i32x4_kernel<<<grid, threads, 0, st>>>(
+          reinterpret_cast<const int32_t*>(acc), out, planes, C, pq, mult, shift, pre, post, zp,
+          qmin, qmax);
+      return !cuda_failed(cudaGetLastError(), "requantize launch");
     }
     requantize_i32x4_kernel<<<grid_for(total / 4, kThreads, 2), kThreads, 0, st>>>(
         reinterpret_cast<const int32_t*>(acc), out, total / 4, C, inner, mult, shift, pre, post,

@@ -79,11 +79,14 @@ def test_requantize_large_vs_oracle(gpu_lib, oracle):
 
 
 @pytest.mark.parametrize("outer,C,inner", [(20000, 12, 1), (3001, 96, 1), (64, 20, 1),
-                                           (7, 16, 4096), (2, 40, 12)])
+                                           (7, 16, 4096), (3, 24, 3136), (5, 8, 132),
+                                           (2, 40, 12)])
 def test_requantize_vector_layouts_vs_oracle(gpu_lib, oracle, outer, C, inner):
     """The 16-byte forms: rows of C % 4 == 0 channels (parameters held per
-    thread across the grid-stride loop) and NCHW planes of inner % 4 == 0,
-    with channels on the high-word form and on the exact 128-bit one."""
+    thread across the grid-stride loop), NCHW planes of inner % 4 == 0 (a
+    block per plane; planes whose quads do not fill the last pass) and short
+    planes, with channels on the high-word form and on the exact 128-bit
+    one."""
     rng = np.random.default_rng(outer + C + inner)
     acc = rng.integers(-(2**31), 2**31, (outer, C, inner)).astype(np.int32)
     mult = rng.integers(0, 2**31, C)
