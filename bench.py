@@ -72,7 +72,8 @@ WORKLOADS = {
     "yolov8n_cls": {
         "metric": "int8 YOLOv8n-cls images/sec", "qjson": GRAPHS / "yolov8n_cls_int8.qjson",
         "graph": lambda b: _graph("yolov8n_cls", b),
-        "batch": 64, "cpu_batch": 16, "ref_batch": 32, "classes": 1000,
+        "batch": 64, "cpu_batch": 64, "ref_batch": 64, "classes": 1000,
+        "calib": (4, 8),
         "name": "cfg2: YOLOv8n-cls int8 integer inference (random init, BN folded, "
                 "reference-calibrated q.json)"},
     "yolov8n_cls_int16": {
@@ -209,6 +210,34 @@ def measure_elementwise(dev, stream, flush, hbm_peak, reps=5):
     res["timing"] = (f"median of {reps} single launches on 2^21 pixels x 64 channels, "
                      "L2 flushed before each; bytes = operands read once + output written once")
     return res
+
+
+def calibrate_over_nccl(world):
+    """Sharded calibration of the workload's graph over the process group
+    (each rank runs the float graph on its share of the reference's
+    calibration images through the CUDA library, then one MIN/MAX
+    all-reduce of the ranges), compared with the reference-calibrated
+    q.json the timed forward uses.  Outside every timed region."""
+    import torch
+    import torch.distributed as dist
+
+    from quantanything_b200 import distributed, networks
+    from quantanything_b200.container import QuantContainer
+
+    nb, bs = W["calib"]
+    images = [networks.images(bs, IMAGE, seed=100 + i) for i in range(nb)]
+    batches = [x[j:j + 1] for x in images for j in range(bs)]  # one image per batch
+    qc = QuantContainer(W["graph"](1), W.get("dtype", "int8"), per_channel=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    distributed.calibrate_sharded(qc, batches)
+    dt = time.perf_counter() - t0
+    ref = json.loads(Path(W["qjson"]).read_text())["qparams"]
+    rel = max(abs(qc.qparams[k].scale - v["scale"]) / abs(v["scale"]) for k, v in ref.items())
+    dzp = max(abs(int(qc.qparams[k].zp) - int(v["zp"])) for k, v in ref.items())
+    return {"backend": dist.get_backend(), "ranks": dist.get_world_size(),
+            "images": nb * bs, "tensors": len(ref), "seconds": round(dt, 3),
+            "max_rel_scale_diff_vs_qjson": float(f"{rel:.3g}"), "max_zp_diff_vs_qjson": dzp}
 
 
 def config(world, extra=None):
@@ -443,6 +472,9 @@ def main():
         print(json.dumps({"profile_forwards": args.profile_forwards, "launches_per_forward":
                           len(net.steps)}))
         return
+    calibration = None
+    if dist is not None and "calib" in W:
+        calibration = calibrate_over_nccl(world)
     net.capture()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -479,14 +511,27 @@ def main():
 
     # ---- e2e: pinned host images in, probabilities out, every step, through
     # the public pipelined call (each step's host->device copy overlaps the
-    # previous step's forward; every copy is inside the timed region)
+    # previous step's forward; every copy is inside the timed region).  With
+    # several ranks every step also all-gathers the ranks' output shards on
+    # the device (NCCL) and copies the whole batch's probabilities out.
     e2e_steps = max(min(args.steps, 50), 1)
-    net.run_pipelined([x_pinned] * 3, [out_pinned] * 3)
+    collect = None
+    if dist is not None:
+        from quantanything_b200 import distributed
+
+        gathered = torch.empty((world * PER_GPU_BATCH, W["classes"]), dtype=torch.float32,
+                               device=dev)
+        out_pinned = torch.empty(tuple(gathered.shape), dtype=torch.float32).pin_memory()
+
+        def collect(y):
+            return distributed.gather_outputs_device(y, gathered)
+
+    net.run_pipelined([x_pinned] * 3, [out_pinned] * 3, collect)
     es = torch.cuda.Event(enable_timing=True)
     ee = torch.cuda.Event(enable_timing=True)
     barrier()
     es.record(stream)
-    net.run_pipelined([x_pinned] * e2e_steps, [out_pinned] * e2e_steps)
+    net.run_pipelined([x_pinned] * e2e_steps, [out_pinned] * e2e_steps, collect)
     ee.record(stream)
     barrier()
     e2e_ms = max_over_ranks(es.elapsed_time(ee))
@@ -571,6 +616,12 @@ def main():
                 "fused_gemm": fused_gemm, "elementwise": elementwise, "kernels": kernels}
         if dropin:
             line["e2e_dropin"] = dropin
+        if dist is not None:
+            line["collectives"] = {
+                "backend": dist.get_backend(), "nccl_ranks": world,
+                "e2e_gather": f"all_gather_into_tensor of float32 [{PER_GPU_BATCH}, "
+                              f"{W['classes']}] per rank per step, inside the e2e region",
+                "calibration_allreduce": calibration}
         print(json.dumps(line), flush=True)
     del net._graph
     if dist is not None:

@@ -276,6 +276,14 @@ int qa_i32_to_bytes_dev(const int32_t* x, void* y, int64_t y_stride, int64_t N, 
  * recorded by any kernel on this device. */
 int qa_device_status_dev(void* stream);
 
+/* Self-test of the bounded-wait error channel (no counterpart in the
+ * reference, which has no device code): one thread waits, for at most
+ * `budget_cycles` SM cycles (<= 2^32), on an mbarrier that it releases
+ * itself only when `arrive` is nonzero.  A wait that runs out records a
+ * timeout that the next qa_device_status_dev reports as kDeviceTimeout;
+ * the context stays usable. */
+int qa_wait_probe_dev(int64_t budget_cycles, int arrive, void* stream);
+
 /* Fused network-input layer: float32 NCHW images with c_in <= 4 channels
  * are quantized with (scale, desc->x_zp, qmin, qmax) exactly like
  * qa_quantize_f32, convolved with the packed int8 weights of `desc`
@@ -412,10 +420,10 @@ int qa_maxpool16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, 
 
 /* Allocation-free narrow GEMM.  No counterpart in the reference: it exists
  * for callers that may not allocate GPU memory while they run (a service
- * that reserves all device memory up front, work recorded into a CUDA graph,
- * a host runtime that passes only input and output buffers), which the
- * regular entry points cannot serve because they grow device buffers with
- * cudaMalloc on first use.
+ * that reserves all device memory up front and forbids allocation later, a
+ * host runtime that passes only the input and output buffers it owns),
+ * which the regular entry points cannot serve because they grow device
+ * buffers with cudaMalloc on first use.
  *
  * C[M,N] = A[M,K]·B[K,N] (int16 operands, int32 results, bit-identical to
  * qa_gemm_i16_i32) on DEVICE pointers, enqueued on `stream`.  The operands
@@ -424,10 +432,17 @@ int qa_maxpool16_dev(const void* x, int64_t x_plane, int64_t x_stride, void* y, 
  * requests needing more (about 2*M*K + 2*N*K bytes) are rejected with an
  * error.  The first call on each device looks up the array's address, so
  * make it before any stream capture.  Calls share the array: calls that
- * overlap on the GPU (different streams, or another thread) race. */
+ * overlap on the GPU (different streams, or another thread) race.
+ *
+ * qa_noalloc_status_dev(stream): after the calls' stream work, reads and
+ * clears this entry point's own bounded-wait status word (one device-to-host
+ * word copy and a synchronize of `stream`; call it outside any stream
+ * capture).  Returns 0, or kDeviceTimeout (3) when a kernel of an earlier
+ * call gave up a wait and left that call's C incomplete. */
 int64_t qa_noalloc_scratch_bytes(void);
 int qa_gemm_i16_i32_noalloc_dev(const int16_t* A, const int16_t* B, int32_t* C, int64_t M,
                                 int64_t N, int64_t K, void* stream);
+int qa_noalloc_status_dev(void* stream);
 
 #ifdef __cplusplus
 }

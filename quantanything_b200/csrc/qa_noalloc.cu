@@ -3,10 +3,10 @@
 //
 // Who needs it: callers that must not allocate GPU memory while they run --
 // a service that reserves all of its device memory up front and forbids
-// allocation afterwards, code that records work into a CUDA graph, or a
-// host runtime that hands this library only the input and output buffers.
-// The regular entry points grow a per-thread device arena and a packing
-// buffer with cudaMalloc on first use, which such callers cannot allow.
+// allocation afterwards, or a host runtime that hands this library only the
+// input and output buffers it manages itself.  The regular entry points grow
+// a per-thread device arena and a packing buffer with cudaMalloc on first
+// use, which such callers cannot allow.
 //
 // This entry point packs its operands into a fixed, library-owned scratch
 // array instead: a file-scope __device__ array of kNoAllocScratchBytes (16 MiB)
@@ -76,6 +76,31 @@ bool device_symbols(DeviceSymbols* out) {
 using namespace qa;
 
 QA_API int64_t qa_noalloc_scratch_bytes(void) { return (int64_t)kNoAllocScratchBytes; }
+
+// Reads and clears this entry point's bounded-wait status word on `stream`
+// (a device-to-host copy of one word, then a synchronize of `stream`):
+// returns kDeviceTimeout, with the error recorded, when a kernel of an
+// earlier call gave up a wait, which leaves that call's C incomplete.
+QA_API int qa_noalloc_status_dev(void* stream) {
+  clear_error();
+  DeviceSymbols sym;
+  if (!device_symbols(&sym)) return last_status();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t h = 0;
+  if (cuda_failed(cudaMemcpyAsync(&h, sym.status, sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+                  "cudaMemcpyAsync(no-alloc status)") ||
+      cuda_failed(cudaStreamSynchronize(st), "cudaStreamSynchronize"))
+    return last_status();
+  if (h != 0) {
+    if (cuda_failed(cudaMemsetAsync(sym.status, 0, sizeof(int32_t), st),
+                    "cudaMemsetAsync(no-alloc status)") ||
+        cuda_failed(cudaStreamSynchronize(st), "cudaStreamSynchronize"))
+      return last_status();
+    set_error(kDeviceTimeout, "qa_gemm_i16_i32_noalloc_dev: a kernel gave up a bounded wait "
+                              "(device status " + std::to_string(h) + "); its output is incomplete");
+  }
+  return last_status();
+}
 
 QA_API int qa_gemm_i16_i32_noalloc_dev(const int16_t* A, const int16_t* B, int32_t* C,
                                        int64_t M, int64_t N, int64_t K, void* stream) {

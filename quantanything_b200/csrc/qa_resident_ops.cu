@@ -1073,6 +1073,39 @@ QA_API int qa_device_status_dev(void* stream) {
   return check_device_status((cudaStream_t)stream) ? 0 : last_status();
 }
 
+// Self-test of the bounded-wait error channel every tensor-core kernel uses:
+// one thread initialises an mbarrier expecting one arrival, arrives on it
+// only when `arrive` is set, and waits with the same bounded wait as the
+// kernels.  A wait that runs out records its code in the device status word
+// (read by qa_device_status_dev) and the thread returns; no copy is in
+// flight, so the context stays usable.
+namespace qa {
+namespace {
+constexpr int kWaitProbeTimeoutCode = 0x7100;
+
+__global__ void wait_probe_kernel(int* status, unsigned long long budget_cycles, int arrive) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = ptx::smem_addr(&bar);
+  ptx::mbar_init(b, 1);
+  ptx::fence_mbar_init();
+  if (arrive) ptx::mbar_arrive(b);
+  if (!ptx::mbar_wait(b, 0, budget_cycles)) atomicExch(status, kWaitProbeTimeoutCode);
+}
+}  // namespace
+}  // namespace qa
+
+QA_API int qa_wait_probe_dev(int64_t budget_cycles, int arrive, void* stream) {
+  clear_error();
+  QA_REQUIRE(budget_cycles >= 0 && budget_cycles <= (int64_t(1) << 32),
+             "qa_wait_probe_dev: budget must lie in [0, 2^32] SM cycles", last_status());
+  int* status = device_status_word();
+  if (!status) return last_status();
+  return launch_ex(wait_probe_kernel, dim3(1), dim3(1), 0, (cudaStream_t)stream, false, status,
+                   (unsigned long long)budget_cycles, arrive)
+             ? 0
+             : last_status();
+}
+
 // ================================================ fused input convolution ==
 // Graph input (float32 NCHW, at most 4 channels) -> quantize -> conv ->
 // layer epilogue, in one CUDA-core kernel.  A block owns an 8 x 32 tile of

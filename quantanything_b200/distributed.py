@@ -79,10 +79,15 @@ def allreduce_ranges(ranges, group=None):
 
 def gather_outputs(y, total, group=None):
     """All-gathers per-rank output shards (float32 [n_r, C], contiguous
-    shards in rank order) into the full [total, C] array on every rank."""
+    shards in rank order) into the full [total, C] array on every rank.
+    ``y`` may be a host array or a tensor; a tensor already on the group's
+    device is gathered there and the result stays a device tensor (only
+    host inputs come back as a NumPy array)."""
     world = dist.get_world_size(group)
     dev = _device_for(group)
-    t = torch.as_tensor(np.ascontiguousarray(y)).to(dev)
+    on_device = isinstance(y, torch.Tensor) and y.device == dev and dev.type == "cuda"
+    t = y if on_device else torch.as_tensor(np.ascontiguousarray(
+        y.cpu().numpy() if isinstance(y, torch.Tensor) else y)).to(dev)
     spans = [shard_bounds(total, r, world) for r in range(world)]
     rows = max(hi - lo for lo, hi in spans)
     # collectives move equal-sized buffers: pad every shard to the largest
@@ -90,7 +95,21 @@ def gather_outputs(y, total, group=None):
     padded[: t.shape[0]] = t
     buf = [torch.empty_like(padded) for _ in range(world)]
     dist.all_gather(buf, padded, group=group)
-    return torch.cat([b[: hi - lo] for b, (lo, hi) in zip(buf, spans)]).cpu().numpy()
+    full = torch.cat([b[: hi - lo] for b, (lo, hi) in zip(buf, spans)])
+    return full if on_device else full.cpu().numpy()
+
+
+def gather_outputs_device(y, out, group=None):
+    """All-gathers equal-sized per-rank output shards that are already on the
+    group's device: ``y`` [n, C] on every rank -> ``out`` [world * n, C]
+    (rank order), one ``all_gather_into_tensor`` enqueued on the current
+    stream -- no host round trip.  Returns ``out``."""
+    world = dist.get_world_size(group)
+    if out.shape[0] != world * y.shape[0] or out.shape[1:] != y.shape[1:]:
+        raise ValueError(f"gather buffer {tuple(out.shape)} does not hold {world} shards of "
+                         f"{tuple(y.shape)}")
+    dist.all_gather_into_tensor(out, y.contiguous(), group=group)
+    return out
 
 
 def calibrate_sharded(container, batches, group=None):

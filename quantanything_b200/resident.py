@@ -91,6 +91,7 @@ _DEV_SIGNATURES = {
     "qa_maxpool_bytes_dev": (ctypes.c_int, [_P, _I64, _I64, _P] + [_I64] * 16 + [_P]),
     "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
     "qa_device_status_dev": (ctypes.c_int, [_P]),
+    "qa_wait_probe_dev": (ctypes.c_int, [_I64, ctypes.c_int, _P]),
     "qa_requantize_i32_dev": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64,
                                              _I64, _I64, _P]),
     "qa_conv_input_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P, _I64,
@@ -962,7 +963,7 @@ class ResidentNet:
         out_pinned.copy_(y, non_blocking=True)
         return out_pinned
 
-    def run_pipelined(self, xs_pinned, outs_pinned):
+    def run_pipelined(self, xs_pinned, outs_pinned, collect=None):
         """Host-to-host forwards of a sequence of pinned float32 batches, each
         batch's host->device copy overlapped with the previous batch's
         forward: the copies run on a side stream into two alternating staging
@@ -970,7 +971,12 @@ class ResidentNet:
         input buffer (device to device), replays the captured forward and
         copies the float32 result into ``outs_pinned[i]``.  Everything is
         enqueued; the outputs are valid after the current stream
-        synchronizes."""
+        synchronizes.
+
+        ``collect``: optional callable applied to each batch's float32 device
+        output before the copy to the host (for example the multi-GPU
+        all-gather of every rank's shard, ``distributed.gather_outputs_device``);
+        ``outs_pinned[i]`` then receives what it returns."""
         if len(xs_pinned) != len(outs_pinned):
             raise ValueError("one output buffer per input batch")
         comp = torch.cuda.current_stream(self.device)
@@ -993,7 +999,10 @@ class ResidentNet:
             comp.wait_event(self._copied[b])
             self.x_dev.copy_(self._staging[b], non_blocking=True)
             self._consumed[b].record(comp)
-            out.copy_(self.replay(), non_blocking=True)
+            y = self.replay()
+            if collect is not None:
+                y = collect(y)
+            out.copy_(y, non_blocking=True)
         return outs_pinned
 
     def run(self, x_host, out=None):

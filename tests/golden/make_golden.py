@@ -2,7 +2,10 @@
 
 Run in the development container, where the reference project is importable:
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--graphs]
+    python tests/golden/make_golden.py [--ref <reference checkout>] [--graphs]
+
+(--ref defaults to $QA_REFERENCE_ROOT, else a directory named `reference`
+beside this repository.)
 
 Every expected value below is produced by the REFERENCE itself: its Python
 package (quantization/*) imported read-only with an import stub for the
@@ -285,7 +288,8 @@ def config_digests(native):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("QA_REFERENCE_ROOT",
+                                                  str(REPO.parent / "reference")))
     ap.add_argument("--graphs", action="store_true")
     ap.add_argument("--only", nargs="*", help="graph fixtures to (re)write; nothing else")
     args = ap.parse_args()

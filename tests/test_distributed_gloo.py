@@ -42,6 +42,13 @@ def _worker(rank, world, port, outdir):
     y = qc.run_graph(distributed.shard(x, rank, world), "integer")
     full = distributed.gather_outputs(y, len(x))
     np.save(os.path.join(outdir, f"y{rank}.npy"), full)
+    # equal shards already in tensors: one all_gather_into_tensor, rank order
+    import torch
+
+    shard_t = torch.as_tensor(np.asarray(y, np.float32))[:2]
+    gathered = torch.empty((world * 2, shard_t.shape[1]), dtype=torch.float32)
+    distributed.gather_outputs_device(shard_t, gathered)
+    np.save(os.path.join(outdir, f"g{rank}.npy"), gathered.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -65,6 +72,9 @@ def test_sharded_calibration_and_gather(tmp_path):
     expect = single.run_graph(networks.images(5, 32, seed=9), "integer")
     for r in range(world):
         np.testing.assert_array_equal(np.load(tmp_path / f"y{r}.npy"), expect)
+    # ranks hold images [0, 3) and [3, 5): their first two rows, in rank order
+    for r in range(world):
+        np.testing.assert_array_equal(np.load(tmp_path / f"g{r}.npy"), expect[[0, 1, 3, 4]])
 
 
 def test_shard_bounds_cover_batch():
