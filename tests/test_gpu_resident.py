@@ -105,6 +105,37 @@ def test_fused_input_layer_matches_separate_path(gpu_lib, name, batch):
     np.testing.assert_array_equal(_run(fused, x), _run(plain, x))
 
 
+def test_fused_input_layer_special_values(gpu_lib):
+    """The fused input layer on images full of hard cases for its float
+    quantizer -- products near rounding ties (a few ulps either side of
+    (k + 1/2) * scale), NaN, +-inf, values far beyond the clamp range --
+    gives every integer tensor of the separate quantize kernel + conv path
+    (itself pinned to the oracle's qa_quantize_f32 / conv)."""
+    fused, qc, meta = _net("yolov8n_cls_int8", gpu_lib, 2, fuse_input=True)
+    plain, _, _ = _net("yolov8n_cls_int8", gpu_lib, 2, fuse_input=False)
+    qp = qc.qparams[qc.graph.inputs[0].name]
+    rng = np.random.default_rng(77)
+    x = networks.images(2, 224, seed=5)
+    flat = x.reshape(-1)
+    k = rng.integers(qp.qmin - qp.zp - 2, qp.qmax - qp.zp + 2, flat.size)
+    ties = ((k + 0.5) * qp.scale).astype(np.float32)
+    ulps = rng.integers(-3, 4, flat.size).astype(np.int32)
+    near = (ties.view(np.int32) + ulps).view(np.float32)
+    pick = rng.random(flat.size)
+    flat[pick < 0.3] = near[pick < 0.3]
+    flat[(pick >= 0.3) & (pick < 0.301)] = np.nan
+    flat[(pick >= 0.301) & (pick < 0.302)] = np.inf
+    flat[(pick >= 0.302) & (pick < 0.303)] = -np.inf
+    flat[(pick >= 0.303) & (pick < 0.31)] *= 1e6
+    _run(fused, x)
+    _run(plain, x)
+    names = [n for n in fused._views if n in plain._views and n != qc.graph.inputs[0].name]
+    assert names
+    for n in names:
+        np.testing.assert_array_equal(fused.tensor(n).cpu().numpy(), plain.tensor(n).cpu().numpy(),
+                                      err_msg=n)
+
+
 def test_sppf_mini_int8_maxpool(gpu_lib):
     """Resident MaxPool (padded with qmin) chained three times into a Concat."""
     net, qc, meta = _net("sppf_mini_int8", gpu_lib, 2)

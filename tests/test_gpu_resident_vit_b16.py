@@ -40,9 +40,9 @@ NAME = "vit_b16_int8"
 INTEGER_KINDS = ("conv", "vit_embed", "gather")
 FALLBACK_KINDS = ("layernorm", "attention")
 FALLBACK_LSB = 1
-FALLBACK_FLIP_FRACTION = 1e-3
+FALLBACK_FLIP_FRACTION = 1e-4
 E2E_MAX_LSB = 8
-E2E_MIN_IDENTICAL = 0.10
+E2E_MIN_IDENTICAL = 0.15
 
 
 def _mirror_lib():
