@@ -537,8 +537,10 @@ def main():
     e2e_ms = max_over_ranks(es.elapsed_time(ee))
     e2e = world * PER_GPU_BATCH * e2e_steps / (e2e_ms / 1e3)
 
-    # ---- roofline of the dominant kernel (per-step CUDA events)
-    step_ms = net.time_steps(reps=20)
+    # ---- roofline of the dominant kernel: every step captured alone in a
+    # CUDA graph and replayed with CUDA events around each replay (L2 flushed
+    # before each, outside the events), so host launch work is not timed
+    step_ms = net.time_steps_graphed(reps=20, flush=flush)
     costs = net.step_costs()
     dom = int(np.argmax(step_ms))
     label, dom_bytes, dom_ops = costs[dom]

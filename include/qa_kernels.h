@@ -266,6 +266,17 @@ int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signed, void
                          int64_t DH, int64_t DW, int64_t OH, int64_t OW, int64_t pad_value,
                          void* stream);
 
+/* Pad / Slice / Transpose of an NHWC byte tensor (quant_layers.py:593-650:
+ * scale-preserving, Pad fills with the input zero point): output element
+ * (n, c, y, x) of the [ON, OC, OH, OW] result (NHWC bytes, y_pix_stride per
+ * pixel) reads x + sum_a (start[a] + i[a] * step[a]) * stride[a] (host
+ * arrays of four, NCHW axis order; stride[a] in bytes of the source axis
+ * output axis a reads), or `fill` where a coordinate leaves [0, dim[a]). */
+int qa_window_copy_bytes_dev(const void* x, void* y, int64_t y_pix_stride, int64_t ON,
+                             int64_t OC, int64_t OH, int64_t OW, const int64_t* start,
+                             const int64_t* step, const int64_t* dim, const int64_t* stride,
+                             int64_t fill, void* stream);
+
 /* Layout conversion between NHWC byte views and NCHW int32 tensors. */
 int qa_bytes_to_i32_dev(const void* x, int64_t x_stride, int64_t x_signed, int32_t* y,
                         int64_t N, int64_t HW, int64_t C, void* stream);

@@ -1073,6 +1073,86 @@ QA_API int qa_device_status_dev(void* stream) {
   return check_device_status((cudaStream_t)stream) ? 0 : last_status();
 }
 
+// ======================================================== window copy ==
+// The resident form of the scale-preserving layout operators Pad, Slice and
+// Transpose (quant_layers.py:593-650; float_ops.py Pad / Slice / Transpose):
+// an NHWC byte tensor is copied into a new one, output element (n, c, y, x)
+// (NCHW order) reading source element
+//     base + sum_a (start[a] + i[a] * step[a]) * stride[a]
+// (i = (n, c, y, x); stride[a] in bytes of the source axis that output axis
+// a reads, so a Transpose permutes the strides), or `fill` -- the Pad's zero
+// point -- when a source coordinate lies outside [0, dim[a]).  A thread
+// writes one 16-channel chunk of one output pixel.
+namespace qa {
+namespace {
+struct WindowGeom {
+  int64_t start[4], step[4], dim[4], stride[4];
+};
+
+__global__ void window_copy_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                                   int64_t y_stride, int64_t ON, int64_t OC, int64_t OH,
+                                   int64_t OW, WindowGeom g, uint32_t fill, int vec) {
+  ptx::pdl_wait();
+  const int64_t chunks = (OC + 15) / 16;
+  const int64_t total = ON * OH * OW * chunks;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t cg = t % chunks;
+    const int64_t pix = t / chunks;
+    const int64_t ox = pix % OW, oy = (pix / OW) % OH, n = pix / (OW * OH);
+    const int64_t sn = g.start[0] + n * g.step[0], sy = g.start[2] + oy * g.step[2],
+                  sx = g.start[3] + ox * g.step[3];
+    const bool pix_in = (uint64_t)sn < (uint64_t)g.dim[0] && (uint64_t)sy < (uint64_t)g.dim[2] &&
+                        (uint64_t)sx < (uint64_t)g.dim[3];
+    const int64_t base = sn * g.stride[0] + sy * g.stride[2] + sx * g.stride[3];
+    uint32_t w[4] = {0, 0, 0, 0};
+    const int64_t c0 = cg * 16;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t sc = g.start[1] + (c0 + j) * g.step[1];
+      const bool in = pix_in && (uint64_t)sc < (uint64_t)g.dim[1];
+      const uint32_t b = in ? (uint32_t)x[base + sc * g.stride[1]] : fill;
+      w[j >> 2] |= (b & 0xFFu) << (8 * (j & 3));
+    }
+    uint8_t* dst = y + pix * y_stride + c0;
+    if (vec && c0 + 16 <= OC) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int j = 0; j < 16 && c0 + j < OC; ++j) dst[j] = (uint8_t)(w[j >> 2] >> (8 * (j & 3)));
+    }
+  }
+}
+}  // namespace
+}  // namespace qa
+
+QA_API int qa_window_copy_bytes_dev(const void* x, void* y, int64_t y_pix_stride, int64_t ON,
+                                    int64_t OC, int64_t OH, int64_t OW, const int64_t* start,
+                                    const int64_t* step, const int64_t* dim,
+                                    const int64_t* stride, int64_t fill, void* stream) {
+  clear_error();
+  QA_REQUIRE(x && y && start && step && dim && stride && ON >= 0 && OC >= 0 && OH >= 0 &&
+                 OW >= 0 && y_pix_stride >= OC,
+             "qa_window_copy_bytes_dev: bad arguments", last_status());
+  QA_REQUIRE(fill >= -128 && fill <= 255, "qa_window_copy_bytes_dev: fill must be a byte value",
+             last_status());
+  const int64_t total = ON * OH * OW * ((OC + 15) / 16);
+  if (total == 0) return 0;
+  WindowGeom g;
+  for (int a = 0; a < 4; ++a) {
+    g.start[a] = start[a];
+    g.step[a] = step[a];
+    g.dim[a] = dim[a];
+    g.stride[a] = stride[a];
+  }
+  const int vec = (reinterpret_cast<uintptr_t>(y) % 16 == 0) && (y_pix_stride % 16 == 0);
+  return launch_ex(window_copy_kernel, dim3(grid_for(total, 256)), dim3(256), 0,
+                   (cudaStream_t)stream, true, static_cast<const uint8_t*>(x),
+                   static_cast<uint8_t*>(y), y_pix_stride, ON, OC, OH, OW, g,
+                   (uint32_t)(fill & 0xFF), vec)
+             ? 0
+             : last_status();
+}
+
 // Self-test of the bounded-wait error channel every tensor-core kernel uses:
 // one thread initialises an mbarrier expecting one arrival, arrives on it
 // only when `arrive` is set, and waits with the same bounded wait as the
@@ -1138,6 +1218,7 @@ struct InputConvParams {
   int32_t tiles_x, tiles_y, tiles;
   int32_t tmem_cols;
   uint32_t pw_magic;         // ceil(2^32 / patch_w): i / patch_w == umulhi(i, pw_magic)
+  int32_t patch_words;       // quantized patch words in shared memory (stem form: patch_h x box_w)
   QuantK qk;
   const int8_t* w;  // [Cout][KH*KW*4] rows of w_kp bytes
   int64_t w_kp;
@@ -1434,6 +1515,386 @@ __global__ void __launch_bounds__(kInThreads, 2)
 
 }  // namespace qa
 
+// ============================================ warp-specialized stem layer ==
+// The 3 x 3, stride-2, undilated input layer over three float channels (the
+// YOLO stem), same arithmetic as input_conv_kernel, with the four steps of a
+// tile run by separate warps that hand work to each other through mbarriers
+// (one CTA per SM, 20 warps), so the quantization of one tile, the MMAs of
+// the previous one and the epilogue of the one before overlap:
+//   warp 0     lane 0 keeps kStemStages float patches in flight by TMA;
+//   warp 1     allocates TMEM; lane 0 issues the tile's MMAs (four 128-row
+//              blocks, two K-steps) into one of two accumulator sets;
+//   warps 2-11 quantize the patch four box columns at a time (16-byte reads
+//              of each channel row) into 4-channel words, then write the
+//              tile's 448 implicit-GEMM rows (nine words at fixed offsets)
+//              into one of two A buffers;
+//   warps 12-19 drain the finished accumulator set through the epilogue.
+namespace qa {
+namespace {
+constexpr int kStemC = 3;           // float channels of the stem form
+constexpr int kStemStages = 3;      // float patches in flight
+constexpr int kStemBuildWarp0 = 2, kStemBuildThreads = 320;
+constexpr int kStemEpiWarp0 = 12, kStemEpiWarps = 8;  // two per TMEM lane quarter
+constexpr int kStemThreads = (kStemEpiWarp0 + kStemEpiWarps) * 32;
+constexpr int kStemBarBuild = 1;    // named barrier of the builder warps
+constexpr int kStemTimeout = 0x7004;
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier whose result (OR of every participant's `pred`) is the same
+// for all participants.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kStemThreads, 1)
+    stem_conv_kernel(const __grid_constant__ InputConvParams p,
+                     const __grid_constant__ CUtensorMap xmap) {
+  extern __shared__ uint8_t in_smem_raw[];
+  const uint32_t raw = ptx::smem_addr(in_smem_raw);
+  uint8_t* sm = in_smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const int CoutP = p.CoutP, taps = p.KH * p.KW;
+  const float* s_x = reinterpret_cast<const float*>(sm);
+  uint8_t* s_a = sm + kStemStages * p.stage_bytes;      // 2 x 4 A blocks
+  uint8_t* s_b = s_a + 8 * kInABlock;                   // CoutP rows x 64 B
+  int4* s_ch = reinterpret_cast<int4*>(s_b + CoutP * 64);
+  int64_t* s_bias = reinterpret_cast<int64_t*>(s_ch + CoutP);
+  int64_t* s_mult = s_bias + CoutP;
+  int64_t* s_shift = s_mult + CoutP;
+  int32_t* s_tab = reinterpret_cast<int32_t*>(s_shift + CoutP);
+  uint32_t* s_patch = reinterpret_cast<uint32_t*>(s_tab + kInTab);  // patch_h x box_w words
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(s_patch + p.patch_words) + 7) & ~uintptr_t(7));
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * kStemStages + 8);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+  const uint32_t bar0 = ptx::smem_addr(bars);
+  auto patch_full = [&](int s) { return bar0 + 8u * s; };
+  auto patch_empty = [&](int s) { return bar0 + 8u * (kStemStages + s); };
+  auto a_full = [&](int b) { return bar0 + 8u * (2 * kStemStages + b); };
+  auto a_empty = [&](int b) { return bar0 + 8u * (2 * kStemStages + 2 + b); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (2 * kStemStages + 4 + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * kStemStages + 6 + b); };
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const FusedEpilogue& e = p.epi;
+  const uint32_t b_lbo = (uint32_t)(CoutP / 8) * 128u;
+  const bool has_zp_fold = e.zp > -(1 << 20) && e.zp < (1 << 20);
+
+  // ---- prologue (static operands; overlaps the previous kernel)
+  int hi_ok = 1, fold_ok = 1;
+  for (int i = tid; i < CoutP * 4; i += kStemThreads) {
+    const int co = i / 4, j = i % 4;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (co < p.Cout) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int tap = 4 * j + q;
+        wv[q] = tap < taps ? *reinterpret_cast<const uint32_t*>(p.w + co * p.w_kp + tap * 4) : 0u;
+      }
+      v = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    *reinterpret_cast<uint4*>(s_b + j * b_lbo + (co / 8) * 128 + (co % 8) * 16) = v;
+  }
+  for (int c = tid; c < CoutP; c += kStemThreads) {
+    const bool v = c < p.Cout;
+    s_bias[c] = (v && e.bias) ? e.bias[c] : 0;
+    s_mult[c] = v ? e.mult[c] : 0;
+    s_shift[c] = v ? e.shift[c] : 0;
+    const int ts = (int)(31 + s_shift[c]);
+    const bool hi = ts >= 33 && ts <= 62;
+    if (v && !hi) hi_ok = 0;
+    const int sh = hi ? ts - 32 : 1;
+    // the zero point joins the rounding term while the sum stays in int32
+    // (|hi32((acc + b) * M0)| < 2^30)
+    const int64_t z = (int64_t)1 << (sh - 1);
+    const int64_t zz = has_zp_fold ? e.zp * ((int64_t)1 << sh) : 0;
+    if (zz + z >= ((int64_t)1 << 30) || zz + z < -((int64_t)1 << 30)) fold_ok = 0;
+    s_ch[c] = make_int4((int32_t)s_bias[c], (int32_t)s_mult[c], (int32_t)(uint32_t)(z + zz), sh);
+  }
+  if (e.lut)
+    for (int i = tid; i < kInTab; i += kStemThreads) {
+      const int64_t idx = min(max((int64_t)(i - 128) - e.lut_offset, (int64_t)0), e.lut_len - 1);
+      s_tab[i] = (int32_t)min(max((int64_t)e.lut[idx], (int64_t)-128), (int64_t)255);
+    }
+  // K bytes 36 .. 63 of every A row stay zero: written once
+  for (int P = tid; P < 2 * 512; P += kStemThreads) {
+    uint8_t* row = s_a + (P / 128) * kInABlock + ((P % 128) / 8) * 128 + (P % 8) * 16;
+    *reinterpret_cast<uint4*>(row + 2 * 2048) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(row + 3 * 2048) = make_uint4(0, 0, 0, 0);
+  }
+  ptx::fence_proxy_async_smem();  // B and the zero K bytes are read by the tensor cores
+  if (tid == 0) {
+    for (int s = 0; s < kStemStages; ++s) {
+      ptx::mbar_init(patch_full(s), 1);
+      ptx::mbar_init(patch_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(a_full(b), 1);
+      ptx::mbar_init(a_empty(b), 1);
+      ptx::mbar_init(acc_full(b), 1);
+      ptx::mbar_init(acc_empty(b), kStemEpiWarps);  // one arrival per epilogue warp
+    }
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&xmap);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_addr(s_tmem), (uint32_t)p.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  const int hi_all = __syncthreads_and(hi_ok);
+  const int fold_all = __syncthreads_and(fold_ok);
+  ptx::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+
+  const int my_tiles = p.tiles > (int)blockIdx.x
+                           ? (p.tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                           : 0;
+  const uint32_t set_cols = (uint32_t)(4 * CoutP);
+  // bounded wait; false (and the abort flag set) on expiry or after an abort
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (ptx::mbar_wait(bar, parity, kInBudget)) return true;
+    *s_abort = 1;
+    if (p.status) atomicExch(p.status, kStemTimeout);
+    return false;
+  };
+  auto tile_origin = [&](int k, int& img, int& oy0, int& ox0) {
+    const int t = blockIdx.x + k * gridDim.x;
+    img = t / (p.tiles_x * p.tiles_y);
+    const int r = t - img * p.tiles_x * p.tiles_y;
+    oy0 = (r / p.tiles_x) * kInTileH;
+    ox0 = (r % p.tiles_x) * kInTileW;
+  };
+
+  int issued = 0;     // producer: tiles whose patch load was issued
+  int committed = 0;  // MMA issuer: tiles whose MMAs were committed
+  if (warp == 0) {
+    // ---------------------------------------------------- patch producer --
+    if (lane == 0) {
+      for (int k = 0; k < my_tiles; ++k) {
+        const int s = k % kStemStages;
+        if (k >= kStemStages && !wait(patch_empty(s), ((k / kStemStages) - 1) & 1)) break;
+        int img, oy0, ox0;
+        tile_origin(k, img, oy0, ox0);
+        ptx::mbar_arrive_expect_tx(patch_full(s), (uint32_t)(kStemC * p.patch_h * p.box_w * 4));
+        ptx::tma_load_4d(ptx::smem_addr(sm) + s * p.stage_bytes, &xmap, patch_full(s),
+                         ox0 * p.SW - p.PW - p.shift, oy0 * p.SH - p.PH, 0, img);
+        issued = k + 1;
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      const uint32_t idesc = ptx::idesc_i8(128, CoutP, 1, 1);
+      const uint32_t b_base = ptx::smem_addr(s_b);
+      for (int k = 0; k < my_tiles; ++k) {
+        const int set = k & 1;
+        if (!wait(a_full(set), (k >> 1) & 1)) break;
+        if (k >= 2 && !wait(acc_empty(set), ((k >> 1) - 1) & 1)) break;
+        ptx::tc_fence_after();
+        const uint32_t a_base = ptx::smem_addr(s_a) + set * 4 * kInABlock;
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+            ptx::mma_i8(tmem + set * set_cols + (uint32_t)(b * CoutP),
+                        ptx::smem_desc_kmajor_plain(a_base + b * kInABlock + kk * 4096, 2048, 128),
+                        ptx::smem_desc_kmajor_plain(b_base + kk * 2 * b_lbo, b_lbo, 128), idesc,
+                        kk > 0 ? 1u : 0u);
+        ptx::mma_commit(a_empty(set));
+        ptx::mma_commit(acc_full(set));
+        committed = k + 1;
+      }
+    }
+  } else if (warp < kStemEpiWarp0) {
+    // ------------------------------------------ quantizer / row builders --
+    const int bt = tid - kStemBuildWarp0 * 32;
+    const uint32_t in_zp = (uint32_t)p.qk.zp_i & 0xFFu;
+    const int plane = p.patch_h * p.box_w;
+    const int groups = p.patch_h * (p.box_w / 4);
+    const int bw = p.box_w;
+    for (int k = 0; k < my_tiles; ++k) {
+      const int s = k % kStemStages, set = k & 1;
+      const bool got = wait(patch_full(s), (k / kStemStages) & 1);
+      if (named_bar_or(kStemBarBuild, kStemBuildThreads, !got)) break;
+      // (1) quantize the box: four columns of the three channel rows per step
+      const float* xs = s_x + s * (p.stage_bytes / 4);
+      for (int g = bt; g < groups; g += kStemBuildThreads) {
+        const int off = 4 * g;  // box rows hold box_w floats: groups never straddle them
+        float4 f[kStemC];
+#pragma unroll
+        for (int c = 0; c < kStemC; ++c)
+          f[c] = *reinterpret_cast<const float4*>(xs + c * plane + off);
+        // per-element exactness flags: an element within 2^-20 of a
+        // rounding tie (a few in a million) is decided on its own
+        // (quantize_byte_near_tie)
+        bool ok[kStemC][4];
+        uint32_t t[kStemC][4];
+#pragma unroll
+        for (int c = 0; c < kStemC; ++c) {
+          const float fv[4] = {f[c].x, f[c].y, f[c].z, f[c].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            ok[c][u] = true;
+            t[c][u] = quantize_bits_split(fv[u], p.qk, ok[c][u]);
+          }
+        }
+        bool all_ok = true;
+#pragma unroll
+        for (int c = 0; c < kStemC; ++c)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) all_ok = all_ok & ok[c][u];
+        if (!all_ok) {
+#pragma unroll
+          for (int c = 0; c < kStemC; ++c) {
+            const float fv[4] = {f[c].x, f[c].y, f[c].z, f[c].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (!ok[c][u]) t[c][u] = quantize_byte_near_tie(fv[u], p.qk);
+          }
+        }
+        uint4 w;
+        w.x = pack_bytes(t[0][0], t[1][0], t[2][0], in_zp);
+        w.y = pack_bytes(t[0][1], t[1][1], t[2][1], in_zp);
+        w.z = pack_bytes(t[0][2], t[1][2], t[2][2], in_zp);
+        w.w = pack_bytes(t[0][3], t[1][3], t[2][3], in_zp);
+        *reinterpret_cast<uint4*>(s_patch + off) = w;
+      }
+      named_bar_sync(kStemBarBuild, kStemBuildThreads);
+      if (bt == 0) ptx::mbar_arrive(patch_empty(s));  // the stage may be refilled
+      const bool freed = k < 2 || wait(a_empty(set), ((k >> 1) - 1) & 1);
+      if (named_bar_or(kStemBarBuild, kStemBuildThreads, !freed)) break;
+      // (2) the implicit-GEMM rows of the tile: pixel P is row P % 128 of
+      // block P / 128; K chunk j holds taps 4j .. 4j + 3
+      uint8_t* a_set = s_a + set * 4 * kInABlock;
+      for (int P = bt; P < kInPix; P += kStemBuildThreads) {
+        const int py = P / kInTileW, px = P - (P / kInTileW) * kInTileW;
+        uint8_t* row = a_set + (P / 128) * kInABlock + ((P % 128) / 8) * 128 + (P % 8) * 16;
+        // box word of tap (ky, kx): (2 py + ky) * box_w + 2 px + kx + shift
+        const uint32_t* pw = s_patch + 2 * py * bw + 2 * px + p.shift;
+        uint32_t tw[9];
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+          for (int kx = 0; kx < 3; ++kx) tw[3 * ky + kx] = pw[ky * bw + kx];
+        *reinterpret_cast<uint4*>(row) = make_uint4(tw[0], tw[1], tw[2], tw[3]);
+        *reinterpret_cast<uint4*>(row + 2048) = make_uint4(tw[4], tw[5], tw[6], tw[7]);
+        *reinterpret_cast<uint32_t*>(row + 2 * 2048) = tw[8];
+      }
+      ptx::fence_proxy_async_smem();
+      named_bar_sync(kStemBarBuild, kStemBuildThreads);
+      if (bt == 0) ptx::mbar_arrive(a_full(set));
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue --
+    const int ew = warp - kStemEpiWarp0;
+    const int quarter = warp & 3;  // TMEM lane quarter of this warp
+    const bool hi_rq = p.fast && hi_all && has_zp_fold;
+    const bool zfold = hi_rq && fold_all;
+    const int32_t zp32 = (int32_t)e.zp, qmin32 = (int32_t)e.qmin, qmax32 = (int32_t)e.qmax;
+    const int32_t* t_lut = s_tab + 128;
+    const bool has_lut = e.lut != nullptr;
+    uint8_t* const out_p = e.out;
+    const int64_t out_stride = e.out_pix_stride;
+    for (int k = 0; k < my_tiles; ++k) {
+      const int set = k & 1;
+      const bool got = wait(acc_full(set), (k >> 1) & 1);
+      if (!__all_sync(0xffffffffu, got)) break;
+      ptx::tc_fence_after();
+      int img, oy0, ox0;
+      tile_origin(k, img, oy0, ox0);
+      // 128-row blocks ew / 4, ew / 4 + kStemEpiWarps / 4, ...
+#pragma unroll 1
+      for (int b = ew >> 2; b < 4; b += kStemEpiWarps / 4) {
+        const int P = b * 128 + quarter * 32 + lane;
+        const int oy = oy0 + P / kInTileW, ox = ox0 + P % kInTileW;
+        const bool valid = P < kInPix && oy < p.OH && ox < p.OW;
+        const int64_t m = ((int64_t)img * p.OH + oy) * p.OW + ox;
+        // (warp-uniform: a quarter of block 3 past the 448 rows has no live row)
+        const bool live = __any_sync(0xffffffffu, valid);
+#pragma unroll 1
+        for (int c0 = 0; live && c0 < CoutP; c0 += 16) {
+          uint32_t v[16];
+          ptx::tmem_ld16(tmem + (((uint32_t)quarter * 32u) << 16) + set * set_cols +
+                             (uint32_t)(b * CoutP + c0),
+                         v);
+          ptx::tmem_ld_wait(v);
+          const int nval = min(16, p.Cout - c0);
+          if (!valid || nval <= 0) continue;
+          int32_t q[16];
+          if (zfold) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int4 ch = s_ch[c0 + j];
+              const int32_t rq = (__mulhi((int32_t)v[j] + ch.x, ch.y) + ch.z) >> ch.w;
+              q[j] = min(max(rq, qmin32), qmax32);
+            }
+          } else if (hi_rq) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int4 ch = s_ch[c0 + j];
+              // the plain rounding term (modulo 2^32: it fits int32)
+              const int32_t z = (int32_t)((uint32_t)ch.z - (uint32_t)zp32 * (1u << ch.w));
+              const int32_t rq = (__mulhi((int32_t)v[j] + ch.x, ch.y) + z) >> ch.w;
+              q[j] = min(max(rq + zp32, qmin32), qmax32);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int c = c0 + j;
+              const int64_t xv = (int64_t)(int32_t)v[j] + s_bias[c];
+              q[j] = p.fast ? (int32_t)requant_fast(xv, s_mult[c], (int)(31 + s_shift[c]), e.zp,
+                                                    e.qmin, e.qmax)
+                            : (int32_t)requant_exact(xv, s_mult[c], s_shift[c], e.zp, e.qmin,
+                                                     e.qmax);
+            }
+          }
+          if (has_lut) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) q[j] = t_lut[q[j]];
+          }
+          store_pixel16(q, out_p + m * out_stride + c0, p.vec_out && nval == 16, nval);
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(acc_empty(set));
+    }
+  }
+  // every role has left its loop; after an abort, the last patch load of
+  // every stage and the last committed MMAs complete before the CTA releases
+  // its shared memory and TMEM
+  __syncthreads();
+  if (tid == 0 && *s_abort)
+    for (int k = max(0, issued - kStemStages); k < issued; ++k)
+      ptx::mbar_wait(patch_full(k % kStemStages), (k / kStemStages) & 1, kInBudget);
+  if (tid == 32 && *s_abort && committed > 0)
+    ptx::mbar_wait(acc_full((committed - 1) & 1), ((committed - 1) >> 1) & 1, kInBudget);
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  }
+}
+
+}  // namespace qa
+
 QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, int64_t c_in,
                                    double scale, int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
@@ -1510,11 +1971,46 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
   const uint64_t strides[3] = {(uint64_t)d->W * 4, (uint64_t)(d->W * d->H) * 4,
                                (uint64_t)(d->W * d->H * c_in) * 4};
   const uint32_t box[4] = {(uint32_t)p.box_w, (uint32_t)p.patch_h, (uint32_t)c_in, 1u};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  // the stem form (3 x 3, stride 2, undilated, three float channels) runs
+  // on the warp-specialized kernel: one CTA per SM, three patch stages, two
+  // A buffers and two accumulator sets
+  const bool stem = p.KH == 3 && p.KW == 3 && p.SH == 2 && p.SW == 2 && p.DH == 1 &&
+                    p.DW == 1 && c_in == kStemC;
+  if (stem) {
+    p.patch_words = p.patch_h * p.box_w;
+    int cols = 32;
+    while (cols < 8 * p.CoutP) cols *= 2;
+    p.tmem_cols = cols;
+    const size_t ssmem = 1024 + (size_t)kStemStages * p.stage_bytes + 8 * kInABlock +
+                         (size_t)p.CoutP * (64 + 16 + 3 * 8) + kInTab * 4 +
+                         (size_t)p.patch_words * 4 + 8 + (2 * kStemStages + 8) * 8 + 16;
+    if (ssmem > 220 * 1024 || p.tmem_cols > 512) {
+      set_error(kUnsupported, "qa_conv_input_fused_dev: stem layer outside the kernel's limits");
+      return last_status();
+    }
+    if (!encode_tiled_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, box))
+      return last_status();
+    static size_t stem_attr[64] = {};
+    if (dev < 0 || dev >= 64 || stem_attr[dev] < ssmem) {
+      if (cuda_failed(cudaFuncSetAttribute(stem_conv_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)ssmem),
+                      "cudaFuncSetAttribute(stem_conv)"))
+        return last_status();
+      if (dev >= 0 && dev < 64) stem_attr[dev] = ssmem;
+    }
+    const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count());
+    return launch_ex(stem_conv_kernel, dim3((unsigned)grid), dim3(kStemThreads), ssmem,
+                     (cudaStream_t)stream, true, p, xmap)
+               ? 0
+               : last_status();
+  }
+  p.patch_words = p.patch_h * p.patch_w;
   if (!encode_tiled_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, box))
     return last_status();
   static size_t attr_bytes[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || attr_bytes[dev] < smem) {
     if (cuda_failed(cudaFuncSetAttribute(input_conv_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),

@@ -203,6 +203,39 @@ def bn_mini(seed=0, size=32, classes=10, width=16):
     return b.build(x, ["N", 3, size, size], y)
 
 
+def shaping_mini(seed=0, size=32, classes=10, width=16):
+    """Small graph with the reference's scale-preserving layout operators on
+    activations (quant_layers.py:593-650): an asymmetric zero-point Pad in
+    front of an unpadded conv, spatial Transposes, a channel Slice on a
+    16-channel boundary, a strided spatial Slice, an unaligned channel Slice
+    and a channel Pad."""
+    b = GraphBuilder(seed)
+    i64 = np.int64
+    x = "images"
+    y = b.conv_silu(x, 3, width, 3, 2)                                   # [N, w, s/2, s/2]
+    y = b.op("Pad", [y, b.const(np.array([0, 0, 1, 2, 0, 0, 2, 1], i64), "pads")],
+             mode="constant")                                             # H, W + 3
+    y = b.silu(b.conv(y, width, 2 * width, 3, 1, pad=0))                  # H, W + 1
+    y = b.op("Transpose", [y], perm=[0, 1, 3, 2])
+    y = b.op("Slice", [y, b.const(np.array([width], i64), "starts"),
+                       b.const(np.array([2 * width], i64), "ends"),
+                       b.const(np.array([1], i64), "axes")])              # channels w .. 2w
+    y = b.conv_silu(y, width, width, 3)
+    y = b.op("Slice", [y, b.const(np.array([1, 0], i64), "starts"),
+                       b.const(np.array([2**63 - 1, size // 2], i64), "ends"),
+                       b.const(np.array([2, 3], i64), "axes"),
+                       b.const(np.array([2, 1], i64), "steps")])          # rows 1::2, cols :s/2
+    y = b.op("Transpose", [y], perm=[0, 1, 3, 2])
+    y = b.op("Slice", [y, b.const(np.array([4], i64), "starts"),
+                       b.const(np.array([4 + width // 2], i64), "ends"),
+                       b.const(np.array([1], i64), "axes")])              # w/2 channels from 4
+    y = b.op("Pad", [y, b.const(np.array([0, 2, 0, 0, 0, width // 2 - 2, 0, 0], i64), "pads")],
+             mode="constant")                                             # back to w channels
+    y = b.conv_silu(y, width, 2 * width, 3, 2)
+    y = b.head(y, 2 * width, classes)
+    return b.build(x, ["N", 3, size, size], y)
+
+
 def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, mlp=4,
         std=None):
     """A Vision Transformer in the reference's post-pass form (the structure

@@ -92,6 +92,7 @@ _DEV_SIGNATURES = {
     "qa_bytes_to_i32_dev": (ctypes.c_int, [_P, _I64, _I64, _P, _I64, _I64, _I64, _P]),
     "qa_device_status_dev": (ctypes.c_int, [_P]),
     "qa_wait_probe_dev": (ctypes.c_int, [_I64, ctypes.c_int, _P]),
+    "qa_window_copy_bytes_dev": (ctypes.c_int, [_P, _P] + [_I64] * 5 + [_P] * 4 + [_I64, _P]),
     "qa_requantize_i32_dev": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64,
                                              _I64, _I64, _P]),
     "qa_conv_input_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P, _I64,
@@ -109,6 +110,9 @@ _DEV_SIGNATURES = {
     "qa_dequantize_rows_dev": (ctypes.c_int, [_P, _I64, ctypes.c_int32, _I64, ctypes.c_double,
                                               _P, _P, _I64, _I64, _P]),
 }
+
+
+WINDOW_OPS = ("Pad", "Slice", "Transpose")
 
 
 def device_api(lib):
@@ -180,6 +184,53 @@ def pad_corrections(wt, x_zp, H, W, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, max_
     row_class = np.array([rpat.index(t) for t in rows], np.int32)
     col_class = np.array([cpat.index(t) for t in cols], np.int32)
     return corr.astype(np.int32), row_class, col_class, len(cpat)
+
+
+def window_geometry(node, graph, in_shape):
+    """Pad / Slice / Transpose of a 4-D NCHW tensor as a window copy:
+    (output shape, source axis, start, step) per output axis, following the
+    reference's float ops (float_ops.py Pad: pads [begin..., end...] filled
+    with the zero point; Slice: NumPy slicing of starts / ends / axes /
+    steps, values beyond 2^62 meaning open ends; Transpose: perm, default
+    reversed).  The batch axis must stay whole and in place."""
+    from quantanything_b200.float_ops import _attr_or_input
+
+    s = tuple(int(v) for v in in_shape)
+    consts = [np.asarray(graph.initializers[i]) if i and graph.is_constant(i) else None
+              for i in node.inputs]
+    src, start, step, out = [0, 1, 2, 3], [0, 0, 0, 0], [1, 1, 1, 1], list(s)
+    op = node.op_type
+    if op == "Pad":
+        pads = [int(v) for v in np.asarray(_attr_or_input(node, consts, 1, "pads")).reshape(-1)]
+        if len(pads) != 8:
+            raise UnsupportedGraph(f"{node.name}: Pad of a 4-D tensor expected")
+        for a in range(4):
+            start[a] = -pads[a]
+            out[a] = s[a] + pads[a] + pads[a + 4]
+    elif op == "Slice":
+        starts = [int(v) for v in np.asarray(_attr_or_input(node, consts, 1, "starts")).reshape(-1)]
+        ends = [int(v) for v in np.asarray(_attr_or_input(node, consts, 2, "ends")).reshape(-1)]
+        axes = [int(v) for v in np.asarray(_attr_or_input(node, consts, 3, "axes",
+                                                          list(range(len(starts))))).reshape(-1)]
+        steps = [int(v) for v in np.asarray(_attr_or_input(node, consts, 4, "steps",
+                                                           [1] * len(starts))).reshape(-1)]
+        for st_, en, ax, sp in zip(starts, ends, axes, steps):
+            a = ax % 4
+            r = range(*slice(None if st_ >= 2**62 else st_, None if abs(en) >= 2**62 else en,
+                             sp).indices(s[a]))
+            start[a], step[a], out[a] = r.start, r.step, len(r)
+    elif op == "Transpose":
+        perm = [int(v) for v in (node.attr("perm") or [3, 2, 1, 0])]
+        if sorted(perm) != [0, 1, 2, 3]:
+            raise UnsupportedGraph(f"{node.name}: Transpose of a 4-D tensor expected")
+        src = perm
+        out = [s[a] for a in perm]
+    else:
+        raise AssertionError(op)
+    if src[0] != 0 or start[0] != 0 or step[0] != 1 or out[0] != s[0] or min(out) <= 0:
+        raise UnsupportedGraph(f"{node.name}: {op} must keep the batch axis and a non-empty "
+                               "result")
+    return tuple(out), src, start, step
 
 
 def _round_up(v, m):
@@ -332,6 +383,8 @@ class ResidentNet:
                 self._plan_gap(layer)
             elif isinstance(layer, ShapingQuantize) and node.op_type == "MaxPool":
                 self._plan_maxpool(layer)
+            elif isinstance(layer, ShapingQuantize) and node.op_type in WINDOW_OPS:
+                self._plan_window(layer)
             elif isinstance(layer, ActivationQuantize):
                 self._plan_lut(layer)
             elif isinstance(layer, AddQuantize):
@@ -404,6 +457,8 @@ class ResidentNet:
                 shapes[node.outputs[0]] = (s[0], s[1], 1, 1)
             elif node.op_type in ("Flatten", "Reshape", "Squeeze"):
                 shapes[node.outputs[0]] = (s[0], s[1] * s[2] * s[3], 1, 1)
+            elif node.op_type in WINDOW_OPS:
+                shapes[node.outputs[0]] = window_geometry(node, g, s)[0]
             elif node.op_type == "MaxPool":
                 from quantanything_b200.float_ops import pool_geometry
 
@@ -690,6 +745,33 @@ class ResidentNet:
         if copy is not None:
             self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
 
+    def _plan_window(self, layer):
+        """Pad / Slice / Transpose (quant_layers.py:593-650, scale preserving;
+        Pad fills with the input zero point): a channel Slice of step 1 on
+        16-byte boundaries is a view of its input, any other form one window
+        copy (qa_window_copy_bytes_dev) into a new tensor."""
+        node = layer.node
+        x = self._views[node.inputs[0]]
+        s = self._shapes[node.inputs[0]]
+        out_shape, src, start, step = window_geometry(node, self.graph, s)
+        N, C, H, W = out_shape
+        channel_view = (node.op_type == "Slice" and src == [0, 1, 2, 3] and step[1] == 1
+                        and (out_shape[2], out_shape[3]) == (s[2], s[3])
+                        and start[1] % 16 == 0 and C % 16 == 0
+                        and node.outputs[0] not in self._concat_slot)
+        if channel_view:
+            self._views[node.outputs[0]] = x.channel_slice(start[1], C)
+            return
+        view, copy = self._destination(node.outputs[0], layer.out_qp[0], N, H, W, C)
+        self._views[node.outputs[0]] = view
+        ps = x.pix_stride
+        src_stride = [s[2] * s[3] * ps, 1, s[3] * ps, ps]  # NCHW axes of the NHWC source
+        geom = np.array([start, step, [s[a] for a in src], [src_stride[a] for a in src]],
+                        np.int64)
+        self.steps.append(("window", (layer, x, view, geom, int(layer.in_zp))))
+        if copy is not None:
+            self.steps.append(("rescale", (copy[0], copy[1], view, copy[2])))
+
     def _plan_lut(self, layer):
         node = layer.node
         x = self._views[node.inputs[0]]
@@ -777,6 +859,10 @@ class ResidentNet:
             elif kind == "softmax":
                 layer, x = payload
                 costs.append((f"softmax {x.N}x{x.C}", x.N * x.C * 9, 0))
+            elif kind == "window":
+                layer, x, y = payload[:3]
+                costs.append((f"{layer.node.op_type.lower()} {y.C}@{y.H}x{y.W}",
+                              2 * y.N * y.H * y.W * y.C, 0))
             else:
                 src = payload[1] if kind != "rescale" else payload[2]
                 rows = src.N * src.H * src.W
@@ -799,6 +885,44 @@ class ResidentNet:
             self._launch_all(stream.cuda_stream, on_step=mark)
             stream.synchronize()
             totals += [events[i].elapsed_time(events[i + 1]) for i in range(len(self.steps))]
+        return totals / reps
+
+    def time_steps_graphed(self, reps=20, flush=None):
+        """Device time (ms) of every step, each captured alone in a CUDA graph
+        (so host-side launch work is not timed) and replayed ``reps`` times,
+        with CUDA events around each replay on the replaying stream;
+        ``flush`` (a device tensor, zeroed before every replay outside the
+        events) takes the step's inputs out of L2.  Returns the mean per
+        step."""
+        torch.cuda.synchronize(self.device)
+        self.forward_device()  # eager warm-up: one-time host preparation
+        torch.cuda.synchronize(self.device)
+        saved = self.steps
+        totals = np.zeros(len(saved))
+        s = torch.cuda.Stream(self.device)
+        try:
+            for i, step in enumerate(saved):
+                self.steps = [step]
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(s):
+                    with torch.cuda.graph(g, stream=s):
+                        self._launch_all(s.cuda_stream)
+                torch.cuda.synchronize(self.device)
+                for _ in range(reps):
+                    with torch.cuda.stream(s):
+                        if flush is not None:
+                            flush.zero_()
+                        e0 = torch.cuda.Event(enable_timing=True)
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        e0.record(s)
+                        g.replay()
+                        e1.record(s)
+                    e1.synchronize()
+                    totals[i] += e0.elapsed_time(e1)
+                del g
+        finally:
+            self.steps = saved
+            self.launch_count = len(saved)
         return totals / reps
 
     # ------------------------------------------------------------- launch --
@@ -879,6 +1003,12 @@ class ResidentNet:
                                               y.pix_stride, x.N, x.H, x.W, x.C, k[0], k[1],
                                               s_[0], s_[1], pd[0], pd[1], dl[0], dl[1], y.H,
                                               y.W, layer.in_qmin, st)
+            elif kind == "window":
+                layer, x, y, geom, fill = payload
+                rc = raw.qa_window_copy_bytes_dev(x.ptr, y.ptr, y.pix_stride, y.N, y.C, y.H, y.W,
+                                                  geom[0].ctypes.data, geom[1].ctypes.data,
+                                                  geom[2].ctypes.data, geom[3].ctypes.data,
+                                                  fill, st)
             elif kind == "softmax":
                 layer, x = payload
                 qi, o = layer.in_qp[0], layer.out_qp[0]

@@ -236,6 +236,17 @@ class ResidentNet16(ResidentNet):
                                           y.pix_stride, x.N, x.H, x.W, x.C, k[0], k[1], s_[0],
                                           s_[1], pd[0], pd[1], dl[0], dl[1], y.H, y.W,
                                           layer.in_qmin, st)
+            elif kind == "window":
+                # pure data movement: the byte copy on each plane (fill = the
+                # zero point's low byte, then its high byte)
+                layer, x, y, geom, fill = payload
+                rc = 0
+                for plane, f in ((0, fill & 0xFF), (1, (fill >> 8) & 0xFF)):
+                    if rc == 0:
+                        rc = raw.qa_window_copy_bytes_dev(
+                            x.ptr + plane * x.plane, y.ptr + plane * y.plane, y.pix_stride, y.N,
+                            y.C, y.H, y.W, geom[0].ctypes.data, geom[1].ctypes.data,
+                            geom[2].ctypes.data, geom[3].ctypes.data, f, st)
             elif kind == "softmax":
                 layer, x = payload
                 qi, o = layer.in_qp[0], layer.out_qp[0]

@@ -23,6 +23,8 @@ NETWORKS = {
     "yolov8n_cls_int16": ("yolov8n_cls", {}, "int16", 4, 8, 2),
     "sppf_mini_int8": ("sppf_mini", {"width": 16}, "int8", 2, 4, 2),
     "sppf_mini_uint8": ("sppf_mini", {"width": 16}, "uint8", 2, 4, 2),
+    "shaping_mini_int8": ("shaping_mini", {"width": 16}, "int8", 2, 4, 2),
+    "shaping_mini_int16": ("shaping_mini", {"width": 16}, "int16", 2, 4, 2),
     # the batch is static in a ViT graph: calibration and evaluation use it
     "vit_mini_int8": ("vit", {"batch": 4}, "int8", 2, 4, 4),
     "vit_mini_int16": ("vit", {"batch": 4}, "int16", 2, 4, 4),
