@@ -346,6 +346,22 @@ int qa_gather_table_dev(const void* x, int64_t x_stride, int32_t x_signed, int64
                         int64_t first, const int32_t* table, void* out, int64_t out_stride,
                         int64_t rows, int64_t D, void* stream);
 
+/* MatMul of two activations (the reference's float fallback,
+ * quant_layers.py:195-205 with the float MatMul of float_ops.py):
+ * Y[b, m, n] = clamp(rint(sa * sb * sum_k (A[b,m,k] - za)(B[b,k,n] - zb) / so)
+ * + zo, qmin, qmax), the integer sum exact (K * max|a - za| * max|b - zb| <
+ * 2^31, else kUnsupported).  A element (b, m, k) is the byte at
+ * a + b * a_sb + m * a_sm + k * a_sk, B element (b, k, n) at
+ * b + b * b_sb + k * b_sk + n * b_sn (a transposed operand swaps strides);
+ * Y element (b, m, n) at y + (b * M + m) * y_stride + n.  Agrees with the
+ * reference within one output step (its float32 sum rounds differently). */
+int qa_matmul_act_bytes_dev(const void* a, int32_t a_signed, int64_t a_sb, int64_t a_sm,
+                            int64_t a_sk, int64_t za, double sa, const void* b, int32_t b_signed,
+                            int64_t b_sb, int64_t b_sk, int64_t b_sn, int64_t zb, double sb,
+                            void* y, int64_t y_stride, int64_t batch, int64_t M, int64_t N,
+                            int64_t K, double so, int64_t zo, int64_t qmin, int64_t qmax,
+                            void* stream);
+
 /* Byte rows to int32 and/or float32 (qa_dequantize_f32 semantics). */
 int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_signed, int64_t zp,
                            double scale, int32_t* q_out, float* f_out, int64_t rows, int64_t C,

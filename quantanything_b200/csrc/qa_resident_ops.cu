@@ -1366,7 +1366,8 @@ __global__ void __launch_bounds__(kInThreads, 2)
   const bool has_lut = e.lut != nullptr;
   uint8_t* const out_p = e.out;
   const int64_t out_stride = e.out_pix_stride;
-  const uint32_t in_zp = (uint32_t)p.qk.zp_i & 0xFFu;
+  const QuantK qk = p.qk;  // in registers: no generic parameter loads in the loops
+  const uint32_t in_zp = (uint32_t)qk.zp_i & 0xFFu;
   const int plane = p.patch_h * p.box_w;  // floats per channel in a staged patch
   const int npatch = p.patch_h * p.patch_w;
   const uint32_t idesc = ptx::idesc_i8(128, CoutP, 1, 1);
@@ -1396,7 +1397,7 @@ __global__ void __launch_bounds__(kInThreads, 2)
       bool ok = true;
       uint32_t b[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) b[c] = c < p.C ? quantize_bits_try(f[c], p.qk, ok) : in_zp;
+      for (int c = 0; c < 4; ++c) b[c] = c < p.C ? quantize_bits_try(f[c], qk, ok) : in_zp;
       uint32_t word = pack_bytes(b[0], b[1], b[2], b[3]);
       if (!ok) word = quantize_word_exact(src, plane, p.C, in_zp, p.qk);
       s_patch[i] = word;
@@ -1724,7 +1725,10 @@ __global__ void __launch_bounds__(kStemThreads, 1)
   } else if (warp < kStemEpiWarp0) {
     // ------------------------------------------ quantizer / row builders --
     const int bt = tid - kStemBuildWarp0 * 32;
-    const uint32_t in_zp = (uint32_t)p.qk.zp_i & 0xFFu;
+    // the quantizer constants in registers (through a reference to the
+    // parameter block every read would be a long-latency generic load)
+    const QuantK qk = p.qk;
+    const uint32_t in_zp = (uint32_t)qk.zp_i & 0xFFu;
     const int plane = p.patch_h * p.box_w;
     const int groups = p.patch_h * (p.box_w / 4);
     const int bw = p.box_w;
@@ -1751,7 +1755,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             ok[c][u] = true;
-            t[c][u] = quantize_bits_split(fv[u], p.qk, ok[c][u]);
+            t[c][u] = quantize_bits_split(fv[u], qk, ok[c][u]);
           }
         }
         bool all_ok = true;

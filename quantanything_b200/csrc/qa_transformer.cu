@@ -1101,3 +1101,142 @@ QA_API int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_sig
              ? 0
              : last_status();
 }
+
+// ===================================== activation x activation MatMul ==
+// The reference's float fallback for a MatMul of two activations
+// (quant_layers.py:195-205: dequantize both, float_ops.py MatMul in float32,
+// quantize):  Y[b, m, n] = clamp(rint(sa * sb * S / so) + zo, qmin, qmax)
+// with S = sum_k (A[b, m, k] - za) * (B[b, k, n] - zb) exact in int32 (the
+// host bounds K * max|a - za| * max|b - zb| < 2^31).  Only the reference's
+// float32 summation rounds differently, so the outputs agree within one
+// output step.  Operands are byte tensors addressed by strides (a transposed
+// operand is the same bytes with its strides swapped); a CTA of 256 threads
+// computes a 64 x 64 output tile, each thread 4 x 4 outputs, from 32-wide K
+// slices staged as int32 in shared memory.
+namespace qa {
+namespace {
+constexpr int kMmTile = 64, kMmK = 32;
+
+struct MatMulActParams {
+  const uint8_t* a;
+  int64_t a_sb, a_sm, a_sk;
+  const uint8_t* b;
+  int64_t b_sb, b_sk, b_sn;
+  int32_t a_signed, b_signed, za, zb;
+  uint8_t* y;
+  int64_t y_stride;
+  int32_t M, N, K;
+  double ratio;  // sa * sb, and the output grid
+  double so;
+  int32_t zo, qmin, qmax;
+};
+
+__device__ __forceinline__ int32_t byte_value(const uint8_t* p, int is_signed) {
+  return is_signed ? (int32_t)(int8_t)*p : (int32_t)*p;
+}
+
+__global__ void __launch_bounds__(256) matmul_act_kernel(const MatMulActParams p) {
+  __shared__ int32_t sa[kMmK][kMmTile + 1];
+  __shared__ int32_t sb[kMmK][kMmTile + 1];
+  ptx::pdl_wait();
+  const int bz = blockIdx.z;
+  const int m0 = blockIdx.y * kMmTile, n0 = blockIdx.x * kMmTile;
+  const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;
+  const uint8_t* A = p.a + (int64_t)bz * p.a_sb;
+  const uint8_t* B = p.b + (int64_t)bz * p.b_sb;
+  int32_t acc[4][4] = {};
+  for (int k0 = 0; k0 < p.K; k0 += kMmK) {
+    for (int i = tid; i < kMmK * kMmTile; i += 256) {
+      const int kk = i / kMmTile, r = i % kMmTile;
+      const int k = k0 + kk;
+      const int m = m0 + r, n = n0 + r;
+      sa[kk][r] = (k < p.K && m < p.M)
+                      ? byte_value(A + (int64_t)m * p.a_sm + (int64_t)k * p.a_sk, p.a_signed) - p.za
+                      : 0;
+      sb[kk][r] = (k < p.K && n < p.N)
+                      ? byte_value(B + (int64_t)k * p.b_sk + (int64_t)n * p.b_sn, p.b_signed) - p.zb
+                      : 0;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < kMmK; ++kk) {
+      int32_t av[4], bv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        av[u] = sa[kk][tm + 16 * u];
+        bv[u] = sb[kk][tn + 16 * u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int w = 0; w < 4; ++w) acc[u][w] += av[u] * bv[w];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int m = m0 + tm + 16 * u;
+    if (m >= p.M) continue;
+    uint8_t* row = p.y + ((int64_t)bz * p.M + m) * p.y_stride;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int n = n0 + tn + 16 * w;
+      if (n >= p.N) continue;
+      double v = rint((double)acc[u][w] * p.ratio / p.so) + (double)p.zo;
+      v = fmin(fmax(v, (double)p.qmin), (double)p.qmax);
+      row[n] = (uint8_t)((int32_t)v & 0xFF);
+    }
+  }
+}
+}  // namespace
+}  // namespace qa
+
+QA_API int qa_matmul_act_bytes_dev(const void* a, int32_t a_signed, int64_t a_sb, int64_t a_sm,
+                                   int64_t a_sk, int64_t za, double sa, const void* b,
+                                   int32_t b_signed, int64_t b_sb, int64_t b_sk, int64_t b_sn,
+                                   int64_t zb, double sb, void* y, int64_t y_stride,
+                                   int64_t batch, int64_t M, int64_t N, int64_t K, double so,
+                                   int64_t zo, int64_t qmin, int64_t qmax, void* stream) {
+  clear_error();
+  if (!a || !b || !y || batch < 0 || M < 0 || N < 0 || K < 0 || y_stride < N ||
+      !(so > 0.0) || qmin > qmax || qmin < -128 || qmax > 255) {
+    set_error(kBadArgument, "qa_matmul_act_bytes_dev: bad arguments");
+    return last_status();
+  }
+  // exact int32 sums: K * max|a - za| * max|b - zb| < 2^31
+  const double ma = 255.0 + (double)std::llabs(za), mb = 255.0 + (double)std::llabs(zb);
+  if ((double)K * ma * mb >= 2147483648.0 || M > 0x7FFFFFFF || N > 0x7FFFFFFF ||
+      batch > 65535 || (M + kMmTile - 1) / kMmTile > 65535) {
+    set_error(kUnsupported, "qa_matmul_act_bytes_dev: sizes beyond the kernel's exact range");
+    return last_status();
+  }
+  if (batch == 0 || M == 0 || N == 0) return 0;
+  MatMulActParams p;
+  p.a = static_cast<const uint8_t*>(a);
+  p.a_sb = a_sb;
+  p.a_sm = a_sm;
+  p.a_sk = a_sk;
+  p.b = static_cast<const uint8_t*>(b);
+  p.b_sb = b_sb;
+  p.b_sk = b_sk;
+  p.b_sn = b_sn;
+  p.a_signed = a_signed ? 1 : 0;
+  p.b_signed = b_signed ? 1 : 0;
+  p.za = (int32_t)za;
+  p.zb = (int32_t)zb;
+  p.y = static_cast<uint8_t*>(y);
+  p.y_stride = y_stride;
+  p.M = (int32_t)M;
+  p.N = (int32_t)N;
+  p.K = (int32_t)K;
+  p.ratio = sa * sb;
+  p.so = so;
+  p.zo = (int32_t)zo;
+  p.qmin = (int32_t)qmin;
+  p.qmax = (int32_t)qmax;
+  const dim3 grid((unsigned)((N + kMmTile - 1) / kMmTile), (unsigned)((M + kMmTile - 1) / kMmTile),
+                  (unsigned)batch);
+  return launch_ex(matmul_act_kernel, grid, dim3(256), 0, (cudaStream_t)stream, true, p)
+             ? 0
+             : last_status();
+}

@@ -237,7 +237,7 @@ def shaping_mini(seed=0, size=32, classes=10, width=16):
 
 
 def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, mlp=4,
-        std=None):
+        std=None, attention="heads"):
     """A Vision Transformer in the reference's post-pass form (the structure
     of its ``build_vit`` test model after graph_passes.py): patch-embedding
     Conv -> Reshape -> Transpose, a constant cls token concatenated in front
@@ -251,7 +251,13 @@ def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, 
     1/sqrt(fan_in); ViT-B/16 uses 0.02).
 
     ``vit(img=224, patch=16, dim=768, heads=12, depth=12, classes=1000,
-    batch=B, std=0.02)`` is ViT-B/16."""
+    batch=B, std=0.02)`` is ViT-B/16.
+
+    ``attention="gram"`` replaces each block's multi-head attention by plain
+    activation x activation MatMuls on the token rows (no head split, no
+    Softmax): S = MatMul(q, Transpose(k, [0, 2, 1])), O = MatMul(S, v), then
+    the projection and residual Add -- a graph whose act x act MatMuls are
+    the reference's stand-alone float fallbacks (quant_layers.py:195-205)."""
     b = GraphBuilder(seed)
     rng = b.rng
     hd = dim // heads
@@ -300,6 +306,14 @@ def vit(seed=0, img=32, patch=8, dim=32, heads=4, depth=2, classes=10, batch=4, 
     x = b.op("Add", [x, b.const(rng.normal(0.0, 0.1, (1, tokens, dim)).astype(f32), "pos")])
     for _ in range(depth):
         h = layer_norm(x)
+        if attention == "gram":
+            q, k, v = linear(h, dim, dim), linear(h, dim, dim), linear(h, dim, dim)
+            s_ = b.op("MatMul", [q, b.op("Transpose", [k], perm=[0, 2, 1])])
+            o = b.op("MatMul", [s_, v])
+            x = b.op("Add", [x, linear(o, dim, dim)])
+            h = gelu(linear(layer_norm(x), dim, mlp * dim))
+            x = b.op("Add", [x, linear(h, mlp * dim, dim)])
+            continue
         qkv = linear(h, dim, 3 * dim)
         qkv = b.op("Reshape", [qkv, b.const(np.array([batch, tokens, 3, heads, hd], np.int64),
                                              "shape")])

@@ -93,6 +93,11 @@ _DEV_SIGNATURES = {
     "qa_device_status_dev": (ctypes.c_int, [_P]),
     "qa_wait_probe_dev": (ctypes.c_int, [_I64, ctypes.c_int, _P]),
     "qa_window_copy_bytes_dev": (ctypes.c_int, [_P, _P] + [_I64] * 5 + [_P] * 4 + [_I64, _P]),
+    "qa_matmul_act_bytes_dev": (ctypes.c_int, [_P, ctypes.c_int32, _I64, _I64, _I64, _I64,
+                                               ctypes.c_double, _P, ctypes.c_int32, _I64, _I64,
+                                               _I64, _I64, ctypes.c_double, _P, _I64, _I64,
+                                               _I64, _I64, _I64, ctypes.c_double, _I64, _I64,
+                                               _I64, _P]),
     "qa_requantize_i32_dev": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64,
                                              _I64, _I64, _P]),
     "qa_conv_input_fused_dev": (ctypes.c_int, [ctypes.POINTER(FusedConvDesc), _P, _I64,

@@ -58,6 +58,7 @@ class ResidentViT(ResidentNet):
                     consumers.setdefault(i, []).append(node)
         self._consumers = consumers
         self._concat_slot, self._concat_done, self._producer_step = {}, {}, {}
+        self._transposed = {}  # transposed token rows read in place by MatMuls
         in_name = g.inputs[0].name
         shp = g.inputs[0].shape
         if int(shp[0]) != self.batch:
@@ -94,8 +95,14 @@ class ResidentViT(ResidentNet):
                     self._views[in_name] = self._in_view = pv
                     self._in_patch = P
                 self._plan_contraction(layer, layers, fused_away, patch=P)
+            elif (op == "Transpose" and node.outputs[0] not in attention["all"]
+                  and node.inputs[0] != getattr(self, "_token_pending", None)):
+                self._plan_transposed_tokens(node)
             elif op in ("Reshape", "Transpose") and node.outputs[0] not in attention["all"]:
                 self._plan_token_alias(node)
+            elif (op == "MatMul" and type(layer) is BaseQuantLayer
+                  and node.outputs[0] not in attention["all"]):
+                self._plan_matmul_act(layer)
             elif isinstance(layer, ConcatQuantize):
                 self._plan_embed(layer, layers, fused_away)
             elif op == "LayerNormalization":
@@ -159,6 +166,46 @@ class ResidentViT(ResidentNet):
             self._views[node.outputs[0]] = View(x.buf, x.offset, x.pix_stride, rows, 1, 1, x.C,
                                                 x.signed, x.qp)
             self._tokens_per_image = x.H * x.W
+
+    def _plan_transposed_tokens(self, node):
+        """Transpose(perm [0, 2, 1]) of token rows [B, T, D] read only by
+        activation x activation MatMuls: no kernel, the MatMul reads the
+        rows with its strides swapped."""
+        x = self._views[node.inputs[0]]
+        readers = self._consumers.get(node.outputs[0], [])
+        if (node.attr("perm") != [0, 2, 1] or not readers
+                or any(r.op_type != "MatMul" or r.inputs[1] != node.outputs[0]
+                       for r in readers)):
+            raise UnsupportedGraph(f"{node.name}: only a [0, 2, 1] Transpose read as the "
+                                   "second operand of MatMuls is resident")
+        self._transposed[node.outputs[0]] = x
+
+    def _plan_matmul_act(self, layer):
+        """MatMul of two activations [B, M, K] x [B, K, N] (the reference's
+        float fallback, quant_layers.py:195-205): one qa_matmul_act_bytes_dev
+        launch over the token rows; a [0, 2, 1]-transposed second operand is
+        read in place."""
+        node = layer.node
+        a = self._views[node.inputs[0]]
+        Bn = self.batch
+        if len(node.inputs) > 2 and node.inputs[2] or a.N % Bn:
+            raise UnsupportedGraph(f"{node.name}: MatMul of [B, M, K] token rows expected")
+        M, K = a.N // Bn, a.C
+        if node.inputs[1] in self._transposed:
+            bt = self._transposed[node.inputs[1]]
+            if bt.C != K or bt.N % Bn:
+                raise UnsupportedGraph(f"{node.name}: operand shapes do not match")
+            N = bt.N // Bn
+            bview, strides = bt, (N * bt.pix_stride, 1, bt.pix_stride)   # b_sb, b_sk, b_sn
+        else:
+            bv = self._views[node.inputs[1]]
+            if bv.N != Bn * K:
+                raise UnsupportedGraph(f"{node.name}: operand shapes do not match")
+            N = bv.C
+            bview, strides = bv, (K * bv.pix_stride, bv.pix_stride, 1)
+        y = self._row_view(Bn * M, N, layer.out_qp[0])
+        self._views[node.outputs[0]] = y
+        self.steps.append(("matmul_act", (layer, a, bview, y, M, N, K, strides)))
 
     def _plan_embed(self, concat, layers, fused_away):
         """Concat(class token, patch tokens) -> Add(positions) as one table
@@ -338,6 +385,15 @@ class ResidentViT(ResidentNet):
                                               s_par.ctypes.data, z_par.ctypes.data,
                                               mul_table.data_ptr(), p_signed, y.ptr,
                                               y.pix_stride, st)
+        if kind == "matmul_act":
+            layer, a, b, y, M, N, K, (b_sb, b_sk, b_sn) = payload
+            qa, qb = layer.in_qp[0], layer.in_qp[1]
+            o = layer.out_qp[0]
+            return raw.qa_matmul_act_bytes_dev(a.ptr, int(a.signed), M * a.pix_stride,
+                                               a.pix_stride, 1, qa.zp, float(qa.scale), b.ptr,
+                                               int(b.signed), b_sb, b_sk, b_sn, qb.zp,
+                                               float(qb.scale), y.ptr, y.pix_stride, self.batch,
+                                               M, N, K, float(o.scale), o.zp, o.qmin, o.qmax, st)
         if kind == "gather":
             x, y, T, first, table = payload
             return raw.qa_gather_table_dev(x.ptr, x.pix_stride, int(x.signed), T, first,
@@ -361,6 +417,11 @@ class ResidentViT(ResidentNet):
             elif kind == "dequant":
                 y = payload[0]
                 costs.append((kind, y.N * y.C * 9, 0))
+            elif kind == "matmul_act":
+                layer, a, b, y, M, N, K = payload[:7]
+                costs.append((f"matmul act x act {self.batch}x{M}x{K}x{N}",
+                              self.batch * (M * K + K * N + M * N),
+                              2 * self.batch * M * N * K))
             else:
                 x, y = (payload[1], payload[2]) if kind == "layernorm" else payload[:2]
                 costs.append((kind, x.N * x.C + y.N * y.C, 0))

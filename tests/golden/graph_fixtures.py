@@ -28,6 +28,8 @@ NETWORKS = {
     # the batch is static in a ViT graph: calibration and evaluation use it
     "vit_mini_int8": ("vit", {"batch": 4}, "int8", 2, 4, 4),
     "vit_mini_int16": ("vit", {"batch": 4}, "int16", 2, 4, 4),
+    # stand-alone activation x activation MatMuls (no head split, no Softmax)
+    "vit_gram_mini_int8": ("vit", {"batch": 4, "attention": "gram"}, "int8", 2, 4, 4),
     # ViT-B/16 (cfg3's model) at batch 2: the full-size parity case
     "vit_b16_int8": ("vit", {"img": 224, "patch": 16, "dim": 768, "heads": 12, "depth": 12,
                              "classes": 1000, "batch": 2, "std": 0.02}, "int8", 2, 2, 2),

@@ -103,3 +103,35 @@ def test_vit_int16_is_rejected(gpu_lib):
     qc, meta = _load("vit_mini_int16", gpu_lib)
     with pytest.raises(UnsupportedGraph):
         ResidentViT(qc, meta["eval_batch"])
+
+
+def test_vit_gram_act_x_act_matmuls_against_the_reference(gpu_lib, oracle):
+    """Stand-alone activation x activation MatMuls (the reference's float
+    fallback, float_ops.py MatMul, quant_layers.py:195-205) on the resident
+    route: qa_matmul_act_bytes_dev reads a [0, 2, 1]-transposed operand in
+    place.  Each step fed the mirror's inputs: integer steps bit-exact, the
+    MatMuls and LayerNorms within one output step; the logits then keep the
+    reference's class."""
+    from quantanything_b200.resident_vit import ResidentViT
+    from tests.resident_steps import mirror_env, teacher_forced
+
+    name = "vit_gram_mini_int8"
+    meta = json.loads((GRAPHS / f"{name}.meta.json").read_text())
+    g = networks.vit(**meta["kwargs"])
+    qc = QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=gpu_lib)
+    net = ResidentViT(qc, meta["eval_batch"])
+    kinds = [k for k, _ in net.steps]
+    assert kinds.count("matmul_act") == 2 * meta["kwargs"].get("depth", 2)
+    x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
+    env = mirror_env(QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=oracle), x)
+    seen = set()
+    for i, kind, tname, diff in teacher_forced(net, env, x, g.inputs[0].name):
+        seen.add(kind)
+        tol = FALLBACK_LSB if kind in ("matmul_act", "layernorm") else 0
+        assert diff.max() <= tol, (i, kind, tname, int(diff.max()))
+    assert "matmul_act" in seen
+    net.forward_device(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    net.check_status()
+    ref = np.load(GRAPHS / f"{name}.npz")["q"]
+    np.testing.assert_array_equal(net.output_int().cpu().numpy().argmax(1), ref.argmax(1))

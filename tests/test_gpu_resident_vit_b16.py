@@ -33,6 +33,7 @@ import torch
 from quantanything_b200 import networks
 from quantanything_b200.container import QuantContainer
 from tests.conftest import GOLDEN, REF_LIB, _ensure_oracle
+from tests.resident_steps import mirror_env, teacher_forced
 
 pytestmark = pytest.mark.gpu
 GRAPHS = GOLDEN / "graphs"
@@ -51,60 +52,13 @@ def _mirror_lib():
     return KernelLibrary(REF_LIB if REF_LIB.exists() else _ensure_oracle())
 
 
-def _mirror_env(qc, x):
-    from quantanything_b200 import float_ops
-
-    env = qc.quantize_inputs(float_ops.normalize_feeds(qc.graph, x))
-    for n in qc._const_names:
-        env[n] = qc._const_q[n]
-    for node in qc.graph.nodes:
-        layer = qc.quant_layers[node.name]
-        env.update(zip(node.outputs,
-                       layer.quantized_infer_integer([env[n] for n in layer.data_inputs])))
-    return env
-
-
-def _step_io(kind, payload):
-    """(input pointers, output pointers) of one resident step."""
-    if kind == "conv":
-        d = payload.desc
-        return [p for p in (d.x, d.res) if p], [p for p in (d.out, d.out2) if p]
-    if kind in ("vit_embed", "gather", "attention"):
-        return [payload[0].ptr], [payload[1].ptr]
-    if kind == "layernorm":
-        return [payload[1].ptr], [payload[2].ptr]
-    return [], []
-
-
-def _write(net, name, value):
-    """Stores an int32 tensor (the mirror's layout of ``name``) into the
-    executor's byte view of ``name``."""
-    v = net._views[name]
-    rows = v.N * v.H * v.W
-    src = np.asarray(value).reshape(v.N, v.C, v.H, v.W).transpose(0, 2, 3, 1).reshape(rows, v.C)
-    dst = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset)
-    t = torch.from_numpy(np.ascontiguousarray(src.astype(np.int64) & 0xFF).astype(np.uint8))
-    dst.copy_(t.to(v.buf.device))
-
-
-def _run_step(net, step):
-    saved = net.steps
-    net.steps = [step]
-    try:
-        net.forward_device()
-    finally:
-        net.steps = saved
-    torch.cuda.synchronize()
-    net.check_status()
-
-
 @pytest.fixture(scope="module")
 def vit_b16(gpu_lib):
     meta = json.loads((GRAPHS / f"{NAME}.meta.json").read_text())
     g = networks.vit(**meta["kwargs"])
     x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
     mirror = QuantContainer.load(g, GRAPHS / f"{NAME}.qjson", lib=_mirror_lib())
-    env = _mirror_env(mirror, x)
+    env = mirror_env(mirror, x)
     qc = QuantContainer.load(g, GRAPHS / f"{NAME}.qjson", lib=gpu_lib)
     return qc, x, env, meta
 
@@ -116,31 +70,15 @@ def test_vit_b16_every_step_against_the_reference(vit_b16):
     net = ResidentViT(qc, meta["eval_batch"])
     kinds = [k for k, _ in net.steps]
     assert kinds.count("attention") == 12 and kinds.count("layernorm") == 25
-    in_name = qc.graph.inputs[0].name
-    by_ptr = {}
-    for name, v in net._views.items():
-        if name != in_name and name in env:
-            by_ptr.setdefault(v.ptr, []).append(name)
-    net.x_dev.copy_(torch.from_numpy(x))
     report = {}
-    for i, (kind, payload) in enumerate(net.steps):
-        ins, outs = _step_io(kind, payload)
-        for p in ins:
-            if p in by_ptr:
-                _write(net, by_ptr[p][0], env[by_ptr[p][0]])
-        _run_step(net, (kind, payload))
-        for p in outs:
-            for name in by_ptr.get(p, []):
-                got = net.tensor(name).cpu().numpy().reshape(-1).astype(np.int64)
-                want = np.asarray(env[name]).reshape(-1).astype(np.int64)
-                diff = np.abs(got - want)
-                report[f"{i}:{kind}:{name}"] = (int(diff.max()), int((diff != 0).sum()), diff.size)
-                if kind in INTEGER_KINDS:
-                    assert diff.max() == 0, (i, kind, name, int((diff != 0).sum()))
-                elif kind in FALLBACK_KINDS:
-                    assert diff.max() <= FALLBACK_LSB, (i, kind, name, int(diff.max()))
-                    assert (diff != 0).sum() <= FALLBACK_FLIP_FRACTION * diff.size, (
-                        i, kind, name, int((diff != 0).sum()))
+    for i, kind, name, diff in teacher_forced(net, env, x, qc.graph.inputs[0].name):
+        report[f"{i}:{kind}:{name}"] = (int(diff.max()), int((diff != 0).sum()), diff.size)
+        if kind in INTEGER_KINDS:
+            assert diff.max() == 0, (i, kind, name, int((diff != 0).sum()))
+        elif kind in FALLBACK_KINDS:
+            assert diff.max() <= FALLBACK_LSB, (i, kind, name, int(diff.max()))
+            assert (diff != 0).sum() <= FALLBACK_FLIP_FRACTION * diff.size, (
+                i, kind, name, int((diff != 0).sum()))
     checked = {k.split(":")[1] for k in report}
     assert set(INTEGER_KINDS + FALLBACK_KINDS) <= checked
     path = os.environ.get("QA_PARITY_REPORT")
