@@ -196,6 +196,7 @@ __global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* _
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const uint32_t pad = (uint32_t)(int32_t)k.zpd & 0xFFu;
+  const QuantK kk = k;  // the fast path's constants in registers
   // each warp takes 32 * kQ consecutive quads; lane l the quads l, l + 32,
   // ..., all of their 16-byte loads in flight before any is used
   constexpr int kQ = 2;
@@ -220,30 +221,35 @@ __global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* _
     for (int u = 0; u < kQ; ++u) {
       if (qi[u] >= quads) break;
       uint32_t bits[4][4];  // [channel][pixel]
-      bool ok = true;
+      bool ok[4][4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        if (c < C) {
-          bits[c][0] = quantize_bits_try(v[u][c].x, k, ok);
-          bits[c][1] = quantize_bits_try(v[u][c].y, k, ok);
-          bits[c][2] = quantize_bits_try(v[u][c].z, k, ok);
-          bits[c][3] = quantize_bits_try(v[u][c].w, k, ok);
-        } else {
-          bits[c][0] = bits[c][1] = bits[c][2] = bits[c][3] = pad;
+        const float fv[4] = {v[u][c].x, v[u][c].y, v[u][c].z, v[u][c].w};
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          ok[c][b] = true;
+          bits[c][b] = c < C ? quantize_bits_split(fv[b], kk, ok[c][b]) : pad;
+        }
+      }
+      bool all_ok = true;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) all_ok = all_ok & (ok[c][b] || c >= C);
+      if (!all_ok) {
+        // rare (an element within 2^-20 of a rounding tie, NaN, or no float
+        // scale): each such element is decided on its own
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float fv[4] = {v[u][c].x, v[u][c].y, v[u][c].z, v[u][c].w};
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            if (c < C && !ok[c][b]) bits[c][b] = quantize_byte_near_tie(fv[b], k);
         }
       }
       uint32_t px[4];
 #pragma unroll
       for (int b = 0; b < 4; ++b) px[b] = pack_bytes(bits[0][b], bits[1][b], bits[2][b], bits[3][b]);
-      if (!ok) {
-        // rare: an element near a rounding boundary, NaN, or no float scale;
-        // the four pixels are re-read and quantized exactly
-        const int n = qi[u] / quads_per_image, q = qi[u] - n * quads_per_image;
-        const float* src = x + (int64_t)n * C * quads_per_image * 4 + (int64_t)q * 4;
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-          px[b] = quantize_word_exact(src + b, (int64_t)quads_per_image * 4, C, pad, k);
-      }
       int64_t off = (int64_t)qi[u] * 16;
       if (P > 0) {
         const int n = qi[u] / quads_per_image, p0 = (qi[u] - n * quads_per_image) * 4;
@@ -319,6 +325,63 @@ __global__ void gap16ch_kernel(const uint8_t* __restrict__ x, int64_t x_pix_stri
     if (lane < 16) {
       const int64_t sum = (int64_t)mine - HW * zp_in;
       y[n * y_pix_stride + g * 16 + lane] = (uint8_t)requant_exact(sum, m, s, zp_out, qmin, qmax);
+    }
+  }
+}
+
+// Thread per (image, 16-channel group) for images of at most 256 pixels:
+// every pixel's 16-byte load is independent (all in flight), the bytes are
+// summed in 16-bit lanes (even and odd bytes of each word separately; a
+// signed byte is biased by 128 first, so each lane sums at most 256 * 255),
+// and the 64-bit rescale replaces the 128-bit one whenever the host proved
+// it exact (`fast`).
+__global__ void gap16_thread_kernel(const uint8_t* __restrict__ x, int64_t x_pix_stride,
+                                    int x_signed, int64_t N, int HW, int64_t groups,
+                                    int64_t zp_in, int64_t m, int64_t s, int64_t zp_out,
+                                    int64_t qmin, int64_t qmax, int fast, uint8_t* __restrict__ y,
+                                    int64_t y_pix_stride) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t total = N * groups;
+  const uint32_t flip = x_signed ? 0x80808080u : 0u;
+  const int ts = (int)(31 + s);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / groups, g = i - n * groups;
+    const uint8_t* base = x + n * HW * x_pix_stride + g * 16;
+    uint32_t even[4] = {0, 0, 0, 0}, odd[4] = {0, 0, 0, 0};
+#pragma unroll 8
+    for (int p = 0; p < HW; ++p) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)p * x_pix_stride));
+      const uint32_t w[4] = {v.x ^ flip, v.y ^ flip, v.z ^ flip, v.w ^ flip};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        even[k] += w[k] & 0x00FF00FFu;
+        odd[k] += (w[k] >> 8) & 0x00FF00FFu;
+      }
+    }
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t word = (j & 1) ? odd[j >> 2] : even[j >> 2];
+      int64_t sum = (int64_t)((word >> (16 * ((j >> 1) & 1))) & 0xFFFFu);
+      if (x_signed) sum -= 128 * (int64_t)HW;
+      sum -= (int64_t)HW * zp_in;
+      int64_t q;
+      if (fast) {
+        q = ((sum * m + ((int64_t)1 << (ts - 1))) >> ts) + zp_out;
+        q = q < qmin ? qmin : (q > qmax ? qmax : q);
+      } else {
+        q = requant_exact(sum, m, s, zp_out, qmin, qmax);
+      }
+      o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+    }
+    uint8_t* dst = y + n * y_pix_stride + g * 16;
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) dst[j] = (uint8_t)(o[j >> 2] >> (8 * (j & 3)));
     }
   }
 }
@@ -545,6 +608,55 @@ __device__ __forceinline__ void two_in_flight(const ByteView& a, const ByteView&
   }
 }
 
+// Add with conflict-free table reads: the two rescaled terms (sign applied
+// to the second) as int32 tables with one copy per lane (entry e of lane l
+// at word e * 32 + l: a warp's 32 lookups always hit 32 different banks,
+// where one shared copy serializes on the random banks of random bytes).
+// Used when the host proves every term within 2^29 and the zero point
+// within 2^30 (their sum is then exact in int32); 64 KB of shared memory
+// per block, persistent grid.
+constexpr int kAddRepThreads = 256;
+
+__global__ void __launch_bounds__(kAddRepThreads) add_bytes16_rep_kernel(
+    ByteView a, ByteView b, uint8_t* __restrict__ y, int64_t y_stride, int64_t rows,
+    int64_t groups, int64_t za, int64_t ma, int64_t sa, int64_t zb, int64_t mb, int64_t sb,
+    int64_t sign, int64_t zo, int64_t qmin, int64_t qmax) {
+  extern __shared__ int32_t add_rep[];  // [2][256][32]
+  ptx::pdl_launch_dependents();
+  for (int e = threadIdx.x; e < 256; e += blockDim.x) {
+    const int64_t va = a.is_signed ? (int64_t)(int8_t)e : (int64_t)e;
+    const int64_t vb = b.is_signed ? (int64_t)(int8_t)e : (int64_t)e;
+    const I128 x1 = mbqm(va - za, ma, sa);
+    I128 x2 = mbqm(vb - zb, mb, sb);
+    if (sign < 0) x2 = neg_i128(x2);
+    const int32_t t1 = (int32_t)(int64_t)x1.lo, t2 = (int32_t)(int64_t)x2.lo;
+#pragma unroll 8
+    for (int l = 0; l < 32; ++l) {
+      add_rep[e * 32 + l] = t1;
+      add_rep[(256 + e) * 32 + l] = t2;
+    }
+  }
+  __syncthreads();
+  ptx::pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int32_t* ta = add_rep + lane;
+  const int32_t* tb = add_rep + 256 * 32 + lane;
+  const int32_t zo32 = (int32_t)zo, lo32 = (int32_t)qmin, hi32 = (int32_t)qmax;
+  auto one = [&](const uint4 va4, const uint4 vb4) {
+    const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t ea = (wa[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+      const uint32_t eb = (wb[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+      const int32_t q = min(max(ta[ea * 32] + tb[eb * 32] + zo32, lo32), hi32);
+      o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  two_in_flight(a, b, y, y_stride, rows * groups, groups, one);
+}
+
 // Add: the two rescaled terms (sign applied to the second) as int64 tables;
 // exact when every entry's 128-bit value lies within +-2^61 (checked while
 // building: the sum of two terms and the zero point then cannot overflow),
@@ -568,13 +680,14 @@ __global__ void __launch_bounds__(256, 3) add_bytes16_kernel(ByteView a, ByteVie
     ok &= x2.hi == ((int64_t)x2.lo >> 63) && (int64_t)x2.lo > -lim && (int64_t)x2.lo < lim;
     ta[e] = (int64_t)x1.lo;
     tb[e] = (int64_t)x2.lo;
-    const int64_t l30 = (int64_t)1 << 30;
-    ok32 &= ta[e] > -l30 && ta[e] < l30 && tb[e] > -l30 && tb[e] < l30;
+    const int64_t l29 = (int64_t)1 << 29;
+    ok32 &= ta[e] > -l29 && ta[e] < l29 && tb[e] > -l29 && tb[e] < l29;
     ta32[e] = (int32_t)ta[e];
     tb32[e] = (int32_t)tb[e];
   }
   const bool tables = __syncthreads_and(ok);
-  // both terms and the zero point within 2^30 each: the sum is exact in int32
+  // both terms within 2^29 and the zero point within 2^30: the sum is
+  // exact in int32
   const bool tables32 = __syncthreads_and(ok32) && zo > -(1 << 30) && zo < (1 << 30) &&
                         qmin > -(1ll << 31) && qmax < (1ll << 31);
   ptx::pdl_wait();
@@ -612,11 +725,39 @@ __global__ void mul_bytes16_kernel(ByteView a, ByteView b, uint8_t* __restrict__
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const bool small = small_applies(m, s);
-  // the centred operands lie within +-2^9, so |p| < 2^18 always fits int32
-  const bool small32 = small && za > -(1 << 20) && za < (1 << 20) && zb > -(1 << 20) &&
-                       zb < (1 << 20);
+  // with |za|, |zb| < 2^12 the centred operands lie within +-(2^12 + 255),
+  // so |p| < 2^26 fits int32
+  const bool small32 = small && za > -(1 << 12) && za < (1 << 12) && zb > -(1 << 12) &&
+                       zb < (1 << 12);
   const int ts = (int)(31 + s);
   const int64_t rnd = small ? ((int64_t)1 << (ts - 1)) : 0;
+  // 32-bit form: (hi32(p * m) + 2^(ts - 33)) >> (ts - 32) equals the
+  // rounded shift for ts in [33, 62] (the low word cannot carry into the
+  // rounding bit), with 0 <= m < 2^31 and |p| < 2^31
+  const bool hi32 = small32 && ts >= 33 && ts <= 62 && m >= 0 && m < (int64_t(1) << 31) &&
+                    zo > -(1 << 20) && zo < (1 << 20);
+  if (hi32) {
+    const int32_t za32 = (int32_t)za, zb32 = (int32_t)zb, m32 = (int32_t)m;
+    const int32_t r32 = 1 << (ts - 33), sh = ts - 32;
+    const int32_t zo32 = (int32_t)zo, lo32 = (int32_t)qmin, hi32v = (int32_t)qmax;
+    const uint32_t fa = a.is_signed ? 0x80u : 0u, fb = b.is_signed ? 0x80u : 0u;
+    auto one32 = [&](const uint4 va4, const uint4 vb4) {
+      const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
+      uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        // a signed byte: (b ^ 0x80) - 0x80
+        const int32_t ea = (int32_t)(((wa[j >> 2] >> (8 * (j & 3))) & 0xFFu) ^ fa) - (int32_t)fa;
+        const int32_t eb = (int32_t)(((wb[j >> 2] >> (8 * (j & 3))) & 0xFFu) ^ fb) - (int32_t)fb;
+        const int32_t p = (ea - za32) * (eb - zb32);
+        const int32_t q = min(max(((__mulhi(p, m32) + r32) >> sh) + zo32, lo32), hi32v);
+        o[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+      }
+      return make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    two_in_flight(a, b, y, y_stride, rows * groups, groups, one32);
+    return;
+  }
   auto one = [&](const uint4 va4, const uint4 vb4) {
     const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
     uint32_t o[4] = {0, 0, 0, 0};
@@ -684,22 +825,28 @@ __global__ void maxpool_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int6
 
 // Stride-1 MaxPool (SPPF's k5 s1 p2) tiled and separable: a block stages
 // the input rows and columns of an 8 x 32 output tile (plus the window's
-// halo, out-of-image taps = the pad value) for one 16-channel group in
-// shared memory, takes the maxima along each row, then along each column.
-constexpr int kMpTH = 8, kMpTW = 32, kMpMaxK = 7;
+// halo, out-of-image taps = the pad value) for up to kMpG 16-channel groups
+// in shared memory (all of their loads in flight together), takes the
+// maxima along each row, then along each column.
+constexpr int kMpTH = 8, kMpTW = 32, kMpMaxK = 7, kMpG = 1;
+constexpr int kMpInR = kMpTH + kMpMaxK - 1, kMpInC = kMpTW + kMpMaxK - 1;
+constexpr size_t kMpSmem = (size_t)kMpG * (kMpInR * kMpInC + kMpInR * kMpTW) * sizeof(uint4);
 
 __global__ void __launch_bounds__(256)
     maxpool_bytes16_s1_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride, int64_t H,
                               int64_t W, int64_t groups, int KH, int KW, int64_t PH, int64_t PW,
                               int64_t OH, int64_t OW, int64_t tiles_x, int64_t tiles_y,
                               uint32_t pad_word) {
-  __shared__ uint4 s_in[kMpTH + kMpMaxK - 1][kMpTW + kMpMaxK - 1];
-  __shared__ uint4 s_row[kMpTH + kMpMaxK - 1][kMpTW];
+  extern __shared__ uint4 mp_smem[];
+  uint4* s_in = mp_smem;                               // [kMpG][kMpInR][kMpInC]
+  uint4* s_row = mp_smem + kMpG * kMpInR * kMpInC;     // [kMpG][kMpInR][kMpTW]
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
+  const int64_t chunks = (groups + kMpG - 1) / kMpG;
   const int64_t t = blockIdx.x;
-  const int64_t tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, ng = t / (tiles_x * tiles_y);
-  const int64_t n = ng / groups, g = ng - n * groups;
+  const int64_t tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, nc = t / (tiles_x * tiles_y);
+  const int64_t n = nc / chunks, g0 = (nc - n * chunks) * kMpG;
+  const int ng = (int)(groups - g0 < kMpG ? groups - g0 : kMpG);
   const int64_t oy0 = ty * kMpTH, ox0 = tx * kMpTW;
   const int rows = kMpTH + KH - 1, cols = kMpTW + KW - 1;
   auto vmax = [&](uint4 a, uint4 b) {
@@ -708,30 +855,36 @@ __global__ void __launch_bounds__(256)
                        : make_uint4(__vmaxu4(a.x, b.x), __vmaxu4(a.y, b.y), __vmaxu4(a.z, b.z),
                                     __vmaxu4(a.w, b.w));
   };
-  for (int i = threadIdx.x; i < rows * cols; i += blockDim.x) {
-    const int r = i / cols, c = i - r * cols;
+  const int per_g = rows * cols;
+  for (int i = threadIdx.x; i < ng * per_g; i += blockDim.x) {
+    const int g = i / per_g, rc = i - g * per_g;
+    const int r = rc / cols, c = rc - r * cols;
     const int64_t iy = oy0 - PH + r, ix = ox0 - PW + c;
     uint4 v = make_uint4(pad_word, pad_word, pad_word, pad_word);
     if (iy >= 0 && iy < H && ix >= 0 && ix < W)
       v = __ldg(reinterpret_cast<const uint4*>(x.p + ((n * H + iy) * W + ix) * x.stride +
-                                               g * 16));
-    s_in[r][c] = v;
+                                               (g0 + g) * 16));
+    s_in[(g * kMpInR + r) * kMpInC + c] = v;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < rows * kMpTW; i += blockDim.x) {
-    const int r = i / kMpTW, c = i - r * kMpTW;
-    uint4 m = s_in[r][c];
-    for (int k = 1; k < KW; ++k) m = vmax(m, s_in[r][c + k]);
-    s_row[r][c] = m;
+  for (int i = threadIdx.x; i < ng * rows * kMpTW; i += blockDim.x) {
+    const int g = i / (rows * kMpTW), rc = i - g * rows * kMpTW;
+    const int r = rc / kMpTW, c = rc - r * kMpTW;
+    const uint4* src = s_in + (g * kMpInR + r) * kMpInC + c;
+    uint4 m = src[0];
+    for (int k = 1; k < KW; ++k) m = vmax(m, src[k]);
+    s_row[(g * kMpInR + r) * kMpTW + c] = m;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < kMpTH * kMpTW; i += blockDim.x) {
-    const int r = i / kMpTW, c = i - r * kMpTW;
+  for (int i = threadIdx.x; i < ng * kMpTH * kMpTW; i += blockDim.x) {
+    const int g = i / (kMpTH * kMpTW), rc = i - g * kMpTH * kMpTW;
+    const int r = rc / kMpTW, c = rc - r * kMpTW;
     const int64_t oy = oy0 + r, ox = ox0 + c;
     if (oy >= OH || ox >= OW) continue;
-    uint4 m = s_row[r][c];
-    for (int k = 1; k < KH; ++k) m = vmax(m, s_row[r + k][c]);
-    *reinterpret_cast<uint4*>(y + ((n * OH + oy) * OW + ox) * y_stride + g * 16) = m;
+    const uint4* src = s_row + (g * kMpInR + r) * kMpTW + c;
+    uint4 m = src[0];
+    for (int k = 1; k < KH; ++k) m = vmax(m, src[k * kMpTW]);
+    *reinterpret_cast<uint4*>(y + ((n * OH + oy) * OW + ox) * y_stride + (g0 + g) * 16) = m;
   }
 }
 
@@ -892,6 +1045,22 @@ QA_API int qa_gap_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int
   clear_error();
   if (N * C == 0) return 0;
   if (C % 16 == 0 && x_pix_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      HW >= 1 && HW <= 256 && N * HW * x_pix_stride < (int64_t(1) << 62)) {
+    // 64-bit rescale exact: |sum| <= HW * 383 + HW * |zp_in|, the rounded
+    // product below 2^62
+    const int64_t ts = 31 + shift;
+    const double bound = (double)HW * (383.0 + std::fabs((double)zp_in)) *
+                             std::fabs((double)mult) + std::ldexp(1.0, (int)std::min<int64_t>(ts, 62));
+    const int fast = ts >= 1 && ts <= 62 && bound < std::ldexp(1.0, 62) ? 1 : 0;
+    const int64_t total = N * (C / 16);
+    return launch_ex(gap16_thread_kernel, dim3(grid_for(total, 128)), dim3(128), 0,
+                     (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_pix_stride,
+                     (int)x_signed, N, (int)HW, C / 16, zp_in, mult, shift, zp_out, qmin, qmax,
+                     fast, static_cast<uint8_t*>(y), y_pix_stride)
+               ? 0
+               : last_status();
+  }
+  if (C % 16 == 0 && x_pix_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       HW < (int64_t(1) << 23)) {
     const int64_t warps = N * (C / 16);
     return launch_ex(gap16ch_kernel, dim3(grid_for(warps * 32, 256)), dim3(256), 0,
@@ -959,7 +1128,43 @@ QA_API int qa_add_bytes_dev(const void* a, int64_t a_stride, int64_t a_signed, c
                             int64_t qmin, int64_t qmax, void* stream) {
   clear_error();
   if (rows * C == 0) return 0;
-  if (C % 16 == 0 && vec16_ok(a, a_stride) && vec16_ok(b, b_stride) && vec16_ok(y, y_stride))
+  // |mbqm(v - z, m, s)| <= (384 + |z|) * |m| * 2^-(31 + s) + 1 for every byte v
+  auto term_small = [](int64_t z, int64_t m, int64_t s) {
+    if (s < -64 || s > 64) return false;
+    const double t = (384.0 + std::fabs((double)z)) * std::fabs((double)m) *
+                         std::ldexp(1.0, -(int)(31 + s)) + 2.0;
+    return t < std::ldexp(1.0, 29) * 0.999;
+  };
+  const bool vec = C % 16 == 0 && vec16_ok(a, a_stride) && vec16_ok(b, b_stride) &&
+                   vec16_ok(y, y_stride);
+  if (vec && term_small(za, ma, sa) && term_small(zb, mb, sb) && (sign == 1 || sign == -1) &&
+      zo > -(1 << 30) && zo < (1 << 30) && qmin >= -128 && qmax <= 255) {
+    const size_t smem = 2 * 256 * 32 * sizeof(int32_t);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      if (cuda_failed(cudaFuncSetAttribute(add_bytes16_rep_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem),
+                      "cudaFuncSetAttribute(add_rep)"))
+        return last_status();
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int64_t vectors = rows * C / 16;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((vectors + kAddRepThreads - 1) /
+                                                                     kAddRepThreads,
+                                                                 (int64_t)sm_count() * 3));
+    return launch_ex(add_bytes16_rep_kernel, dim3((unsigned)grid), dim3(kAddRepThreads), smem,
+                     (cudaStream_t)stream, true,
+                     ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
+                     ByteView{static_cast<const uint8_t*>(b), b_stride, (int)b_signed},
+                     static_cast<uint8_t*>(y), y_stride, rows, C / 16, za, ma, sa, zb, mb, sb,
+                     sign, zo, qmin, qmax)
+               ? 0
+               : last_status();
+  }
+  if (vec)
     return launch_ex(add_bytes16_kernel, dim3(grid_for(rows * C / 16, 256)), dim3(256), 0,
                      (cudaStream_t)stream, true,
                      ByteView{static_cast<const uint8_t*>(a), a_stride, (int)a_signed},
@@ -1020,9 +1225,20 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
       DH == 1 && DW == 1 && KH <= kMpMaxK && KW <= kMpMaxK && KH >= 1 && KW >= 1) {
     const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
     const int64_t tiles_x = (OW + kMpTW - 1) / kMpTW, tiles_y = (OH + kMpTH - 1) / kMpTH;
-    const int64_t blocks = tiles_x * tiles_y * N * (C / 16);
+    const int64_t blocks = tiles_x * tiles_y * N * ((C / 16 + kMpG - 1) / kMpG);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      if (cuda_failed(cudaFuncSetAttribute(maxpool_bytes16_s1_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kMpSmem),
+                      "cudaFuncSetAttribute(maxpool_s1)"))
+        return last_status();
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
     if (blocks < 0x7FFFFFFF)
-      return launch_ex(maxpool_bytes16_s1_kernel, dim3((unsigned)blocks), dim3(256), 0,
+      return launch_ex(maxpool_bytes16_s1_kernel, dim3((unsigned)blocks), dim3(256), kMpSmem,
                        (cudaStream_t)stream, true,
                        ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
                        static_cast<uint8_t*>(y), y_stride, H, W, C / 16, (int)KH, (int)KW, PH,
