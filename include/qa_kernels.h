@@ -367,6 +367,36 @@ int qa_dequantize_rows_dev(const void* x, int64_t x_stride, int32_t x_signed, in
                            double scale, int32_t* q_out, float* f_out, int64_t rows, int64_t C,
                            void* stream);
 
+/* 16-bit transformer layers (int16 ViT graphs), on two-plane int16 tensors
+ * (see the 16-bit block below for the plane layout): the token embedding
+ * (ta: 65536-entry table indexed by value + 32768, cls_row int32 values),
+ * LayerNorm, the attention core (s_params: scales of scores, Mul output,
+ * softmax output, attention output; z_params: {zp, qmin, qmax} of each;
+ * mul_params: {constant, its zp, scores zp, mult, shift} of the integer
+ * scale Mul), the class-token Gather (65536-entry table) and the output
+ * dequantize -- the 8-bit route's float-fallback arithmetic
+ * (quant_layers.py:195-205), integer products exact. */
+int qa_vit_embed16_dev(const void* x, int64_t x_plane, int64_t x_stride, const int32_t* ta,
+                       const int32_t* pos, const int32_t* cls_row, int64_t qmin, int64_t qmax,
+                       void* out, int64_t out_plane, int64_t out_stride, int64_t B, int64_t T,
+                       int64_t D, void* stream);
+int qa_layernorm16_dev(const void* x, int64_t x_plane, int64_t x_stride, int64_t zp_in,
+                       double s_in, const float* gamma, const float* beta, double eps,
+                       double s_out, int64_t zp_out, int64_t qmin, int64_t qmax, void* out,
+                       int64_t out_plane, int64_t out_stride, int64_t rows, int64_t D,
+                       void* stream);
+int qa_attention16_dev(const void* qkv, int64_t qkv_plane, int64_t qkv_stride, int64_t z_qkv,
+                       double s_qkv, int64_t B, int64_t T, int64_t H, int64_t hd,
+                       const double* s_params, const int64_t* z_params,
+                       const int64_t* mul_params, void* out, int64_t out_plane,
+                       int64_t out_stride, void* stream);
+int qa_gather16_dev(const void* x, int64_t x_plane, int64_t x_stride, int64_t every,
+                    int64_t first, const int32_t* table, void* out, int64_t out_plane,
+                    int64_t out_stride, int64_t rows, int64_t D, void* stream);
+int qa_dequantize_rows16_dev(const void* x, int64_t x_plane, int64_t x_stride, int64_t zp,
+                             double scale, int32_t* q_out, float* f_out, int64_t rows, int64_t C,
+                             void* stream);
+
 /* 16-bit device-resident layers (int16 graphs: quant_type "int16").
  *
  * An int16 activation tensor is two NHWC byte planes of the same geometry:

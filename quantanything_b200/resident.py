@@ -1169,15 +1169,20 @@ class ResidentNet:
 
 def make_resident(container, batch, device=None):
     """The device-resident executor that runs ``container``'s graph: a
-    transformer graph (LayerNormalization present) on ResidentViT, int16 and
+    transformer graph (LayerNormalization present) on ResidentViT (int16:
+    ResidentViT16), int16 and
     uint8 graphs on ResidentNet16 (byte-split contractions; uint8 weights
     are asymmetric and exceed int8), other 8-bit graphs on ResidentNet.
     Raises UnsupportedGraph when none of them covers the graph."""
     from quantanything_b200.resident16 import ResidentNet16
     from quantanything_b200.resident_vit import ResidentViT
 
+    from quantanything_b200.resident_vit import ResidentViT16
+
     layer0 = container.layers[0]
     if any(n.op_type == "LayerNormalization" for n in container.graph.nodes):
+        if layer0.num_bits == 16:
+            return ResidentViT16(container, batch, device)
         return ResidentViT(container, batch, device)
     if layer0.num_bits == 16 or (layer0.num_bits == 8 and not layer0.signed):
         return ResidentNet16(container, batch, device)

@@ -255,7 +255,7 @@ class ResidentNet16(ResidentNet):
                                           o.qmax, self.out_q.data_ptr(), self.out_f32.data_ptr(),
                                           float(o.scale), o.zp, st)
             else:
-                raise UnsupportedGraph(f"{kind} has no 16-bit resident kernel")
+                rc = self._launch_step(kind, payload, raw, st)
             _check(self.lib, rc, f"{kind} step (16-bit)")
             if on_step is not None:
                 on_step(n)

@@ -31,6 +31,7 @@ from quantanything_b200.layers import (ActivationQuantize, AddQuantize, BaseQuan
                                        ConcatQuantize, ConvQuantize, GemmQuantize, MulQuantize,
                                        ShapingQuantize)
 from quantanything_b200.resident import ResidentNet, UnsupportedGraph, View, _round_up
+from quantanything_b200.resident16 import ResidentNet16, device_api16
 
 _I32_MIN, _I32_MAX = -(1 << 31), (1 << 31) - 1
 _TAB = np.arange(-128, 256, dtype=np.int64)  # byte-domain table index v + 128
@@ -39,6 +40,8 @@ _TAB = np.arange(-128, 256, dtype=np.int64)  # byte-domain table index v + 128
 class ResidentViT(ResidentNet):
     """Fused device-resident integer inference of a ViT graph (8-bit)."""
 
+    _domain = _TAB  # every activation value, in table-index order
+
     def __init__(self, container, batch, device=None):
         super().__init__(container, batch, device, fuse_input=False)
 
@@ -46,6 +49,12 @@ class ResidentViT(ResidentNet):
     def _row_view(self, rows, C, qp, pix_stride=None):
         stride = pix_stride or _round_up(C, 16)
         return View(self._alloc(rows * stride), 0, stride, rows, 1, 1, C, self.signed, qp)
+
+    def _input_view(self, N, H, W, C, stride, qp):
+        return View(self._alloc(N * H * W * stride), 0, stride, N, H, W, C, self.signed, qp)
+
+    def _cls_row_dev(self, cls_row):
+        return self._dev(cls_row.astype(np.int64) & 0xFF, np.uint8)
 
     def _plan(self):
         g, c = self.graph, self.c
@@ -67,9 +76,8 @@ class ResidentViT(ResidentNet):
         Cin = self.in_shape[1]
         qp_in = c.qparams[in_name]
         stride_in = _round_up(Cin, 4)
-        self._views = {in_name: View(self._alloc(self.batch * self.in_shape[2] * self.in_shape[3]
-                                                 * stride_in), 0, stride_in, self.batch,
-                                     self.in_shape[2], self.in_shape[3], Cin, self.signed, qp_in)}
+        self._views = {in_name: self._input_view(self.batch, self.in_shape[2], self.in_shape[3],
+                                                 Cin, stride_in, qp_in)}
         self._in_view = self._views[in_name]
         self.x_dev = torch.empty(self.in_shape, dtype=torch.float32, device=self.device)
         self.steps.append(("quantize", in_name))
@@ -164,7 +172,7 @@ class ResidentViT(ResidentNet):
                 raise UnsupportedGraph(f"{node.name}: unexpected transpose")
             rows = x.N * x.H * x.W
             self._views[node.outputs[0]] = View(x.buf, x.offset, x.pix_stride, rows, 1, 1, x.C,
-                                                x.signed, x.qp)
+                                                x.signed, x.qp, x.plane)
             self._tokens_per_image = x.H * x.W
 
     def _plan_transposed_tokens(self, node):
@@ -243,7 +251,7 @@ class ResidentViT(ResidentNet):
             return lib.rescale(np.asarray(v, np.int32), z, m, s, 0, _I32_MIN,
                                _I32_MAX).astype(np.int64)
 
-        ta = term(concat_rescale(_TAB, 1), qa.zp, ma, sa)
+        ta = term(concat_rescale(self._domain, 1), qa.zp, ma, sa)
         pos_q = np.asarray(c._const_q[add.inputs[1]], np.int64).reshape(T, D)
         pos = al._sign * term(pos_q, qb.zp, mb, sb) + ao.zp
         cls_q = np.asarray(c._const_q[cls_name], np.int64).reshape(-1, D)[0]
@@ -254,7 +262,7 @@ class ResidentViT(ResidentNet):
         fused_away.add(add.name)
         self.steps.append(("vit_embed", (x, y, T, D, ao,
                                          self._dev(ta, np.int32), self._dev(pos, np.int32),
-                                         self._dev(cls_row.astype(np.int64) & 0xFF, np.uint8))))
+                                         self._cls_row_dev(cls_row))))
 
     def _plan_layernorm(self, layer):
         node = layer.node
@@ -285,7 +293,8 @@ class ResidentViT(ResidentNet):
         T = x.N // self.batch
         first = int(idx[0]) % T
         # the Gather's requantization (dequantize -> take -> quantize) per byte
-        table = layer.quantized_infer_integer([_TAB.reshape(1, 1, -1).astype(np.int32)])[0]
+        table = layer.quantized_infer_integer(
+            [self._domain.reshape(1, 1, -1).astype(np.int32)])[0]
         table = np.asarray(table, np.int64).reshape(-1)
         y = self._row_view(self.batch, x.C, layer.out_qp[0])
         self._views[node.outputs[0]] = y
@@ -436,3 +445,122 @@ class _Only:
         self.in_shape = net.in_shape
         self._in_view = net._in_view
         self._in_patch = net._in_patch
+
+
+class ResidentViT16(ResidentViT, ResidentNet16):
+    """Device-resident integer inference of an int16 ViT graph (the
+    reference's accurate ViT route, README.md:130-135).
+
+    Activations are int16 tensors in two byte planes (the 16-bit executor's
+    layout): the patch embedding, QKV / projection / MLP MatMuls (GELU table
+    and residual Add fused) and the head run on the byte-split tensor-core
+    kernel with its exact int64 combine; the token embedding, the
+    class-token Gather, LayerNorm, the attention core and the output
+    dequantize run on the 16-bit plane kernels (qa_*16_dev), with the same
+    float-fallback arithmetic as the 8-bit route."""
+
+    _domain = np.arange(-32768, 32768, dtype=np.int64)
+
+    def __init__(self, container, batch, device=None):
+        self._planes = []
+        self._lut16 = {}
+        ResidentNet.__init__(self, container, batch, device, fuse_input=False)
+        device_api16(self.lib)
+        vit16_api(self.lib)
+        self._descs = {}
+
+    def _row_view(self, rows, C, qp, pix_stride=None):
+        return self._new_view(rows, 1, 1, C, qp, pix_stride)
+
+    def _input_view(self, N, H, W, C, stride, qp):
+        return self._new_view(N, H, W, C, qp, pix_stride=stride)
+
+    def _cls_row_dev(self, cls_row):
+        return self._dev(cls_row, np.int32)
+
+    def _patch_rows(self, layer):
+        return 0  # the patch embedding gathers 4-byte taps from the int16 planes
+
+    def _plan_matmul_act(self, layer):
+        raise UnsupportedGraph(f"{layer.name}: activation x activation MatMul of 16-bit "
+                               "tensors has no resident kernel")
+
+    def _plan_attention(self, info, layers):
+        c = self.c
+        qkv = self._views[info["qkv"]]
+        B, T, three, H, hd = info["shape"]
+        if three != 3 or B != self.batch or B * T != qkv.N or qkv.C != 3 * H * hd:
+            raise UnsupportedGraph("attention: QKV shape mismatch")
+        S, mul, sm, O = (layers[info[k].name] for k in ("mm1", "mul", "sm", "mm2"))
+        if not isinstance(mul, MulQuantize) or not all(
+                type(l) is BaseQuantLayer for l in (S, sm, O)):
+            raise UnsupportedGraph("attention: unexpected layer types")
+        qs, qm, qp_, qo = S.out_qp[0], mul.out_qp[0], sm.out_qp[0], O.out_qp[0]
+        data_idx = [i for i, n in enumerate(mul.node.inputs) if n != info["scale"]][0]
+        qd, qc = mul.in_qp[data_idx], mul.in_qp[1 - data_idx]
+        cq = int(np.asarray(c._const_q[info["scale"]], np.int64).reshape(-1)[0])
+        y = self._row_view(qkv.N, H * hd, qo)
+        self._views[info["out"]] = y
+        s_par = np.array([qs.scale, qm.scale, qp_.scale, qo.scale], np.float64)
+        z_par = np.array([qs.zp, qs.qmin, qs.qmax, qm.zp, qm.qmin, qm.qmax, qp_.zp, qp_.qmin,
+                          qp_.qmax, qo.zp, qo.qmin, qo.qmax], np.int64)
+        mul_par = np.array([cq, qc.zp, qd.zp, int(mul._mult), int(mul._shift)], np.int64)
+        self.steps.append(("attention", (qkv, y, T, H, hd, s_par, z_par, mul_par)))
+
+    def _launch_step(self, kind, payload, raw, st):
+        if kind == "vit_embed":
+            x, y, T, D, ao, ta, pos, cls_row = payload
+            return raw.qa_vit_embed16_dev(x.ptr, x.plane, x.pix_stride, ta.data_ptr(),
+                                          pos.data_ptr(), cls_row.data_ptr(), ao.qmin, ao.qmax,
+                                          y.ptr, y.plane, y.pix_stride, self.batch, T, D, st)
+        if kind == "layernorm":
+            layer, x, y, gamma, beta, eps = payload
+            qi, o = layer.in_qp[0], layer.out_qp[0]
+            return raw.qa_layernorm16_dev(x.ptr, x.plane, x.pix_stride, qi.zp, float(qi.scale),
+                                          gamma.data_ptr(),
+                                          None if beta is None else beta.data_ptr(), eps,
+                                          float(o.scale), o.zp, o.qmin, o.qmax, y.ptr, y.plane,
+                                          y.pix_stride, x.N, x.C, st)
+        if kind == "attention":
+            qkv, y, T, H, hd, s_par, z_par, mul_par = payload
+            qp = qkv.qp
+            return raw.qa_attention16_dev(qkv.ptr, qkv.plane, qkv.pix_stride, qp.zp,
+                                          float(qp.scale), self.batch, T, H, hd,
+                                          s_par.ctypes.data, z_par.ctypes.data,
+                                          mul_par.ctypes.data, y.ptr, y.plane, y.pix_stride, st)
+        if kind == "gather":
+            x, y, T, first, table = payload
+            return raw.qa_gather16_dev(x.ptr, x.plane, x.pix_stride, T, first, table.data_ptr(),
+                                       y.ptr, y.plane, y.pix_stride, y.N, y.C, st)
+        if kind == "dequant":
+            y, qp = payload
+            return raw.qa_dequantize_rows16_dev(y.ptr, y.plane, y.pix_stride, qp.zp,
+                                                float(qp.scale), self.out_q.data_ptr(),
+                                                self.out_f32.data_ptr(), y.N, y.C, st)
+        raise AssertionError(kind)
+
+
+_VIT16_SIGNATURES = {
+    "qa_vit_embed16_dev": [ctypes.c_void_p] + [ctypes.c_int64] * 2 + [ctypes.c_void_p] * 3
+    + [ctypes.c_int64] * 2 + [ctypes.c_void_p] + [ctypes.c_int64] * 5 + [ctypes.c_void_p],
+    "qa_layernorm16_dev": [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_double]
+    + [ctypes.c_void_p] * 2 + [ctypes.c_double] * 2 + [ctypes.c_int64] * 3 + [ctypes.c_void_p]
+    + [ctypes.c_int64] * 4 + [ctypes.c_void_p],
+    "qa_attention16_dev": [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_double]
+    + [ctypes.c_int64] * 4 + [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 2 + [ctypes.c_void_p],
+    "qa_gather16_dev": [ctypes.c_void_p] + [ctypes.c_int64] * 4 + [ctypes.c_void_p] * 2
+    + [ctypes.c_int64] * 4 + [ctypes.c_void_p],
+    "qa_dequantize_rows16_dev": [ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_double]
+    + [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 2 + [ctypes.c_void_p],
+}
+
+
+def vit16_api(lib):
+    """Declares the 16-bit transformer entry points on a loaded library."""
+    raw = lib.raw
+    if not getattr(raw, "_qa_vit16_declared", False):
+        for name, args in _VIT16_SIGNATURES.items():
+            fn = getattr(raw, name)
+            fn.restype, fn.argtypes = ctypes.c_int, args
+        raw._qa_vit16_declared = True
+    return raw

@@ -36,13 +36,17 @@ def step_io(kind, payload):
 
 def write_tensor(net, name, value):
     """Stores an int32 tensor (the mirror's layout of ``name``) into the
-    executor's byte view of ``name``."""
+    executor's view of ``name`` (bytes, or the two byte planes of an int16
+    tensor)."""
     v = net._views[name]
     rows = v.N * v.H * v.W
     src = np.asarray(value).reshape(v.N, v.C, v.H, v.W).transpose(0, 2, 3, 1).reshape(rows, v.C)
-    dst = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset)
-    t = torch.from_numpy(np.ascontiguousarray(src.astype(np.int64) & 0xFF).astype(np.uint8))
-    dst.copy_(t.to(v.buf.device))
+    planes = [(0, 0)] if not v.plane else [(0, 0), (v.plane, 8)]  # (offset, bit shift)
+    for off, shift in planes:
+        dst = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset + off)
+        t = torch.from_numpy(
+            np.ascontiguousarray((src.astype(np.int64) >> shift) & 0xFF).astype(np.uint8))
+        dst.copy_(t.to(v.buf.device))
 
 
 def run_step(net, step):

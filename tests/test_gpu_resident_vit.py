@@ -20,6 +20,7 @@ from tests.conftest import GOLDEN
 pytestmark = pytest.mark.gpu
 GRAPHS = GOLDEN / "graphs"
 FALLBACK_LSB = 1
+INT16_E2E_LSB = 64  # one-step flips of the float fallbacks, grown through two blocks
 
 
 def _load(name, lib):
@@ -96,13 +97,38 @@ def test_vit_batch_must_match_the_graph(gpu_lib):
         ResidentViT(qc, meta["eval_batch"] + 1)
 
 
-def test_vit_int16_is_rejected(gpu_lib):
-    from quantanything_b200.resident import UnsupportedGraph
-    from quantanything_b200.resident_vit import ResidentViT
+def test_vit_mini_int16_resident_against_the_reference(gpu_lib, oracle):
+    """int16 ViT on the resident route (ResidentViT16: byte-split tensor-core
+    contractions, 16-bit plane kernels for the embedding, LayerNorm, the
+    attention core and the Gather).  Each step fed the mirror's inputs:
+    integer steps bit-exact, the float fallbacks within one int16 output
+    step; end to end the logits stay within INT16_E2E_LSB of the reference's
+    and keep its class on every image."""
+    from quantanything_b200.resident import make_resident
+    from quantanything_b200.resident_vit import ResidentViT16
+    from tests.resident_steps import mirror_env, teacher_forced
 
     qc, meta = _load("vit_mini_int16", gpu_lib)
-    with pytest.raises(UnsupportedGraph):
-        ResidentViT(qc, meta["eval_batch"])
+    net = make_resident(qc, meta["eval_batch"])
+    assert isinstance(net, ResidentViT16)
+    kinds = [k for k, _ in net.steps]
+    assert kinds.count("attention") == 2 and kinds.count("layernorm") == 5
+    x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
+    g = qc.graph
+    env = mirror_env(QuantContainer.load(g, GRAPHS / "vit_mini_int16.qjson", lib=oracle), x)
+    seen = set()
+    for i, kind, tname, diff in teacher_forced(net, env, x, g.inputs[0].name):
+        seen.add(kind)
+        tol = FALLBACK_LSB if kind in ("attention", "layernorm") else 0
+        assert diff.max() <= tol, (i, kind, tname, int(diff.max()))
+    assert {"conv", "vit_embed", "layernorm", "attention", "gather"} <= seen
+    net.forward_device(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    net.check_status()
+    ref = np.load(GRAPHS / "vit_mini_int16.npz")["q"].astype(np.int64)
+    q = net.output_int().cpu().numpy().astype(np.int64)
+    np.testing.assert_array_equal(q.argmax(1), ref.argmax(1))
+    assert np.abs(q - ref).max() <= INT16_E2E_LSB
 
 
 def test_vit_gram_act_x_act_matmuls_against_the_reference(gpu_lib, oracle):
