@@ -825,28 +825,22 @@ __global__ void maxpool_bytes16_kernel(ByteView x, uint8_t* __restrict__ y, int6
 
 // Stride-1 MaxPool (SPPF's k5 s1 p2) tiled and separable: a block stages
 // the input rows and columns of an 8 x 32 output tile (plus the window's
-// halo, out-of-image taps = the pad value) for up to kMpG 16-channel groups
-// in shared memory (all of their loads in flight together), takes the
-// maxima along each row, then along each column.
-constexpr int kMpTH = 8, kMpTW = 32, kMpMaxK = 7, kMpG = 1;
-constexpr int kMpInR = kMpTH + kMpMaxK - 1, kMpInC = kMpTW + kMpMaxK - 1;
-constexpr size_t kMpSmem = (size_t)kMpG * (kMpInR * kMpInC + kMpInR * kMpTW) * sizeof(uint4);
+// halo, out-of-image taps = the pad value) for one 16-channel group in
+// shared memory, takes the maxima along each row, then along each column.
+constexpr int kMpTH = 8, kMpTW = 32, kMpMaxK = 7;
 
 __global__ void __launch_bounds__(256)
     maxpool_bytes16_s1_kernel(ByteView x, uint8_t* __restrict__ y, int64_t y_stride, int64_t H,
                               int64_t W, int64_t groups, int KH, int KW, int64_t PH, int64_t PW,
                               int64_t OH, int64_t OW, int64_t tiles_x, int64_t tiles_y,
                               uint32_t pad_word) {
-  extern __shared__ uint4 mp_smem[];
-  uint4* s_in = mp_smem;                               // [kMpG][kMpInR][kMpInC]
-  uint4* s_row = mp_smem + kMpG * kMpInR * kMpInC;     // [kMpG][kMpInR][kMpTW]
+  __shared__ uint4 s_in[kMpTH + kMpMaxK - 1][kMpTW + kMpMaxK - 1];
+  __shared__ uint4 s_row[kMpTH + kMpMaxK - 1][kMpTW];
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const int64_t chunks = (groups + kMpG - 1) / kMpG;
   const int64_t t = blockIdx.x;
-  const int64_t tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, nc = t / (tiles_x * tiles_y);
-  const int64_t n = nc / chunks, g0 = (nc - n * chunks) * kMpG;
-  const int ng = (int)(groups - g0 < kMpG ? groups - g0 : kMpG);
+  const int64_t tx = t % tiles_x, ty = (t / tiles_x) % tiles_y, ng = t / (tiles_x * tiles_y);
+  const int64_t n = ng / groups, g = ng - n * groups;
   const int64_t oy0 = ty * kMpTH, ox0 = tx * kMpTW;
   const int rows = kMpTH + KH - 1, cols = kMpTW + KW - 1;
   auto vmax = [&](uint4 a, uint4 b) {
@@ -855,36 +849,30 @@ __global__ void __launch_bounds__(256)
                        : make_uint4(__vmaxu4(a.x, b.x), __vmaxu4(a.y, b.y), __vmaxu4(a.z, b.z),
                                     __vmaxu4(a.w, b.w));
   };
-  const int per_g = rows * cols;
-  for (int i = threadIdx.x; i < ng * per_g; i += blockDim.x) {
-    const int g = i / per_g, rc = i - g * per_g;
-    const int r = rc / cols, c = rc - r * cols;
+  for (int i = threadIdx.x; i < rows * cols; i += blockDim.x) {
+    const int r = i / cols, c = i - r * cols;
     const int64_t iy = oy0 - PH + r, ix = ox0 - PW + c;
     uint4 v = make_uint4(pad_word, pad_word, pad_word, pad_word);
     if (iy >= 0 && iy < H && ix >= 0 && ix < W)
       v = __ldg(reinterpret_cast<const uint4*>(x.p + ((n * H + iy) * W + ix) * x.stride +
-                                               (g0 + g) * 16));
-    s_in[(g * kMpInR + r) * kMpInC + c] = v;
+                                               g * 16));
+    s_in[r][c] = v;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < ng * rows * kMpTW; i += blockDim.x) {
-    const int g = i / (rows * kMpTW), rc = i - g * rows * kMpTW;
-    const int r = rc / kMpTW, c = rc - r * kMpTW;
-    const uint4* src = s_in + (g * kMpInR + r) * kMpInC + c;
-    uint4 m = src[0];
-    for (int k = 1; k < KW; ++k) m = vmax(m, src[k]);
-    s_row[(g * kMpInR + r) * kMpTW + c] = m;
+  for (int i = threadIdx.x; i < rows * kMpTW; i += blockDim.x) {
+    const int r = i / kMpTW, c = i - r * kMpTW;
+    uint4 m = s_in[r][c];
+    for (int k = 1; k < KW; ++k) m = vmax(m, s_in[r][c + k]);
+    s_row[r][c] = m;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < ng * kMpTH * kMpTW; i += blockDim.x) {
-    const int g = i / (kMpTH * kMpTW), rc = i - g * kMpTH * kMpTW;
-    const int r = rc / kMpTW, c = rc - r * kMpTW;
+  for (int i = threadIdx.x; i < kMpTH * kMpTW; i += blockDim.x) {
+    const int r = i / kMpTW, c = i - r * kMpTW;
     const int64_t oy = oy0 + r, ox = ox0 + c;
     if (oy >= OH || ox >= OW) continue;
-    const uint4* src = s_row + (g * kMpInR + r) * kMpTW + c;
-    uint4 m = src[0];
-    for (int k = 1; k < KH; ++k) m = vmax(m, src[k * kMpTW]);
-    *reinterpret_cast<uint4*>(y + ((n * OH + oy) * OW + ox) * y_stride + (g0 + g) * 16) = m;
+    uint4 m = s_row[r][c];
+    for (int k = 1; k < KH; ++k) m = vmax(m, s_row[r + k][c]);
+    *reinterpret_cast<uint4*>(y + ((n * OH + oy) * OW + ox) * y_stride + g * 16) = m;
   }
 }
 
@@ -1225,20 +1213,9 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
       DH == 1 && DW == 1 && KH <= kMpMaxK && KW <= kMpMaxK && KH >= 1 && KW >= 1) {
     const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
     const int64_t tiles_x = (OW + kMpTW - 1) / kMpTW, tiles_y = (OH + kMpTH - 1) / kMpTH;
-    const int64_t blocks = tiles_x * tiles_y * N * ((C / 16 + kMpG - 1) / kMpG);
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      if (cuda_failed(cudaFuncSetAttribute(maxpool_bytes16_s1_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)kMpSmem),
-                      "cudaFuncSetAttribute(maxpool_s1)"))
-        return last_status();
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
+    const int64_t blocks = tiles_x * tiles_y * N * (C / 16);
     if (blocks < 0x7FFFFFFF)
-      return launch_ex(maxpool_bytes16_s1_kernel, dim3((unsigned)blocks), dim3(256), kMpSmem,
+      return launch_ex(maxpool_bytes16_s1_kernel, dim3((unsigned)blocks), dim3(256), 0,
                        (cudaStream_t)stream, true,
                        ByteView{static_cast<const uint8_t*>(x), x_stride, (int)x_signed},
                        static_cast<uint8_t*>(y), y_stride, H, W, C / 16, (int)KH, (int)KW, PH,
