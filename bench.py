@@ -38,6 +38,7 @@ run by the 16-bit resident executor (byte-split tensor-core contractions).
 """
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -515,19 +516,23 @@ def main():
     # ---- e2e: pinned host images in, probabilities out, every step, through
     # the public pipelined call (each step's host->device copy overlaps the
     # previous step's forward; every copy is inside the timed region).  With
-    # several ranks every step also all-gathers the ranks' output shards on
-    # the device (NCCL) and copies the whole batch's probabilities out.
+    # several ranks every step also gathers the whole batch's probabilities
+    # on every rank -- the output dequantize fused with the gather, one
+    # kernel per rank storing its rows into every rank's buffer over NVLink
+    # peer memory -- and copies the whole batch out.
     e2e_steps = max(min(args.steps, 50), 1)
     collect = None
+    gather = None
     if dist is not None:
         from quantanything_b200 import distributed
 
-        gathered = torch.empty((world * PER_GPU_BATCH, W["classes"]), dtype=torch.float32,
-                               device=dev)
-        out_pinned = torch.empty(tuple(gathered.shape), dtype=torch.float32).pin_memory()
+        gather = distributed.PeerGather(PER_GPU_BATCH, W["classes"])
+        out_qp = net.output_qparams()
+        out_pinned = torch.empty((world * PER_GPU_BATCH, W["classes"]),
+                                 dtype=torch.float32).pin_memory()
 
         def collect(y):
-            return distributed.gather_outputs_device(y, gathered)
+            return gather(net.output_int(), out_qp.scale, out_qp.zp)
 
     net.run_pipelined([x_pinned] * 3, [out_pinned] * 3, collect)
     es = torch.cuda.Event(enable_timing=True)
@@ -539,6 +544,17 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(es.elapsed_time(ee))
     e2e = world * PER_GPU_BATCH * e2e_steps / (e2e_ms / 1e3)
+    gather_ok = None
+    if gather is not None:
+        net.check_status()  # a gather wait that ran out is reported here
+        # the last step's gathered batch: this rank's rows equal its own
+        # dequantized output, and every rank holds the same bytes
+        own = torch.equal(out_pinned[rank * PER_GPU_BATCH:(rank + 1) * PER_GPU_BATCH],
+                          net.out_f32.cpu())
+        digest = float(int.from_bytes(
+            hashlib.sha1(out_pinned.numpy().tobytes()).digest()[:6], "little"))
+        same = max_over_ranks(digest) == -max_over_ranks(-digest)
+        gather_ok = max_over_ranks(0.0 if own else 1.0) == 0.0 and same
 
     # ---- roofline of the dominant kernel: every step captured alone in a
     # CUDA graph and replayed with CUDA events around each replay (L2 flushed
@@ -624,11 +640,17 @@ def main():
         if dist is not None:
             line["collectives"] = {
                 "backend": dist.get_backend(), "nccl_ranks": world,
-                "e2e_gather": f"all_gather_into_tensor of float32 [{PER_GPU_BATCH}, "
-                              f"{W['classes']}] per rank per step, inside the e2e region",
-                "calibration_allreduce": calibration}
+                "e2e_gather": f"qa_dequantize_gather_peers_dev: each rank's int32 [{PER_GPU_BATCH}, "
+                              f"{W['classes']}] output dequantized and stored into every rank's "
+                              "buffer over NVLink peer memory, one kernel per rank per step, "
+                              "inside the e2e region",
+                "calibration_allreduce": calibration,
+                "gather_matches_local_dequantize": gather_ok}
         print(json.dumps(line), flush=True)
     del net._graph
+    if gather is not None:
+        net.check_status()
+        gather.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

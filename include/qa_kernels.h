@@ -501,6 +501,48 @@ int qa_gemm_i16_i32_noalloc_dev(const int16_t* A, const int16_t* B, int32_t* C, 
                                 int64_t N, int64_t K, void* stream);
 int qa_noalloc_status_dev(void* stream);
 
+/* Output dequantize fused with the multi-GPU output gather.  No reference
+ * counterpart: the reference dequantizes each graph output on the host
+ * (quant_container.py:186-193, x = (q - zp) * scale in float64, stored as
+ * float32) and runs in one process.  Sharded by batch over one process per
+ * GPU, each rank calls qa_dequantize_gather_peers_dev once per step: it
+ * stores its float32 rows into EVERY rank's gather buffer over NVLink peer
+ * memory (plain stores) and waits for the other ranks' rows to land in its
+ * own, so no separate collective follows.
+ *
+ * qa_peer_buffer_create(bytes, &ptr, handle): cudaMalloc's `bytes` (at least
+ * qa_peer_buffer_header_bytes()) on the calling thread's device, zeroes the
+ * header and writes the buffer's 64-byte CUDA IPC handle to `handle`.
+ * qa_peer_buffer_open(handle, &ptr) maps another process's buffer;
+ * qa_peer_buffer_close unmaps it; qa_peer_buffer_destroy frees this
+ * process's own (after every peer has closed it).
+ *
+ * Buffer layout: a header of qa_peer_buffer_header_bytes() (4096) bytes --
+ * int64 consumed[8] at 0 and ready[8] at 128, written by the ranks, and a
+ * CTA counter at 256 -- then two slots of world * rows * cols float32.
+ * Epoch e (1, 2, ... per call, the same on every rank) fills slot e & 1 of
+ * every rank at rows [rank * rows, (rank + 1) * rows).
+ *
+ * qa_dequantize_gather_peers_dev(q, q_stride, zp, scale, rows, cols, bases,
+ * world, rank, epoch, budget_ns, stream): q is this rank's int32 output
+ * [rows, cols] (row stride q_stride elements); bases[r] is rank r's buffer
+ * as mapped in this process (bases[rank] = its own), world <= 8.  The launch
+ * first tells every rank that this one has consumed epoch - 1 (everything
+ * earlier on `stream` has finished), waits until every rank has consumed
+ * epoch - 2 before overwriting that slot, stores its rows and then waits
+ * until every rank's rows of this epoch have arrived.  Waits give up after
+ * budget_ns nanoseconds and set the device status word to kDeviceTimeout
+ * (3; read it with qa_device_status_dev). */
+int64_t qa_peer_buffer_header_bytes(void);
+int qa_peer_buffer_create(int64_t bytes, void** ptr, void* handle);
+int qa_peer_buffer_open(const void* handle, void** ptr);
+int qa_peer_buffer_close(void* ptr);
+int qa_peer_buffer_destroy(void* ptr);
+int qa_dequantize_gather_peers_dev(const void* q, int64_t q_stride, int64_t zp, double scale,
+                                   int64_t rows, int64_t cols, const void* const* bases,
+                                   int32_t world, int32_t rank, int64_t epoch, int64_t budget_ns,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

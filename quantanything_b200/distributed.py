@@ -10,13 +10,18 @@ collective on the data path.  Two collectives exist, both small:
   (MIN of the lows, MAX of the highs) before ``finalize``, so all ranks
   derive identical qparams -- exactly the ranges a single process would see
   (min / max are order independent);
-* output gather: the per-rank float32 outputs are gathered into the full
-  batch.
+* output gather: the per-rank outputs are gathered into the full batch --
+  on GPUs by ``PeerGather``, one kernel per rank that dequantizes the
+  rank's int32 output rows and stores them into every rank's buffer over
+  NVLink peer memory (no NCCL on that path); ``gather_outputs_device``
+  (NCCL ``all_gather_into_tensor``) and ``gather_outputs`` (any backend,
+  host or device tensors) remain for float32 shards.
 
 Backend: ``torch.distributed`` -- NCCL over NVLink on GPUs, gloo on CPU
 (tests).  One process per GPU.
 """
 
+import ctypes
 import os
 from datetime import timedelta
 
@@ -110,6 +115,137 @@ def gather_outputs_device(y, out, group=None):
                          f"{tuple(y.shape)}")
     dist.all_gather_into_tensor(out, y.contiguous(), group=group)
     return out
+
+
+class _DeviceView:
+    """A device pointer presented through ``__cuda_array_interface__`` so
+    that torch can wrap it without a copy."""
+
+    def __init__(self, ptr, shape, typestr="<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "strides": None,
+                                         "version": 3}
+
+
+_PEER_SIGNATURES = {
+    "qa_peer_buffer_header_bytes": (ctypes.c_int64, []),
+    "qa_peer_buffer_create": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p),
+                                             ctypes.c_void_p]),
+    "qa_peer_buffer_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "qa_peer_buffer_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_peer_buffer_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_dequantize_gather_peers_dev": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_double, ctypes.c_int64,
+        ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]),
+}
+IPC_HANDLE_BYTES = 64  # sizeof(cudaIpcMemHandle_t)
+
+
+def peer_api(lib):
+    """Declares the peer-buffer entry points on a loaded KernelLibrary."""
+    raw = lib.raw
+    if not getattr(raw, "_qa_peer_declared", False):
+        for name, (res, args) in _PEER_SIGNATURES.items():
+            fn = getattr(raw, name)
+            fn.restype, fn.argtypes = res, args
+        raw._qa_peer_declared = True
+    return raw
+
+
+class PeerGather:
+    """The graph output's dequantize fused with the all-gather of the
+    per-rank shards (quant_container.py:186-193 dequantizes each output;
+    the batch shards are then collected in rank order).
+
+    Each rank owns one device buffer, mapped into every other rank's
+    process through CUDA IPC.  ``__call__(q, scale, zp)`` launches ONE
+    kernel on the current stream (qa_dequantize_gather_peers_dev): it reads
+    this rank's int32 output rows, dequantizes them and stores the float32
+    rows into every rank's buffer over NVLink peer memory, then raises the
+    rank's flag in each buffer and waits (bounded) for the other ranks'
+    flags.  No NCCL call is made on this path.  The returned [world * rows,
+    cols] float32 tensor (rank order) is valid once the stream reaches the
+    end of the kernel and until the next call's kernel starts on this
+    stream: that launch tells the other ranks that this rank is done with
+    the slot, which they reuse one call later (two alternating slots).  A
+    rank that stops calling makes the others' waits
+    run out after ``budget_s`` with the device status set to a timeout.
+
+    Every rank must construct it (collective) and call it the same number
+    of times, with equal ``rows`` per rank.  ``close()`` is collective too.
+    """
+
+    def __init__(self, rows, cols, group=None, lib=None, budget_s=5.0):
+        from quantanything_b200 import native
+
+        self.lib = lib or native.get_library()
+        self.raw = peer_api(self.lib)
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the peer gather spans at most 8 GPUs")
+        self.rows, self.cols = int(rows), int(cols)
+        self.budget_ns = int(budget_s * 1e9)
+        self.header = int(self.raw.qa_peer_buffer_header_bytes())
+        self.slot_elems = self.world * self.rows * self.cols
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
+        self._call(self.raw.qa_peer_buffer_create(self.header + 2 * 4 * self.slot_elems,
+                                                  ctypes.byref(ptr), handle), "create")
+        self.own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        bases = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bases.append(self.own)
+                continue
+            buf = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(h)
+            p = ctypes.c_void_p()
+            self._call(self.raw.qa_peer_buffer_open(buf, ctypes.byref(p)), f"open rank {r}")
+            self._opened.append(p.value)
+            bases.append(p.value)
+        self._bases = (ctypes.c_void_p * self.world)(*bases)
+        self._views = [torch.as_tensor(
+            _DeviceView(self.own + self.header + 4 * s * self.slot_elems,
+                        (self.world * self.rows, self.cols)), device="cuda") for s in range(2)]
+        self.epoch = 0
+        dist.barrier(group=group)  # every rank has mapped every buffer
+
+    def _call(self, rc, what):
+        if rc != 0:
+            msg = self.lib.raw.qa_last_error().decode(errors="replace")
+            self.lib.raw.qa_clear_error()
+            raise RuntimeError(f"peer gather {what}: {msg}")
+
+    def __call__(self, q, scale, zp, stream=None):
+        if q.dtype != torch.int32 or q.dim() != 2 or tuple(q.shape) != (self.rows, self.cols):
+            raise ValueError(f"expected int32 [{self.rows}, {self.cols}], got "
+                             f"{q.dtype} {tuple(q.shape)}")
+        if q.stride(1) != 1:
+            raise ValueError("output rows must be contiguous")
+        st = stream or torch.cuda.current_stream()
+        self.epoch += 1
+        self._call(self.raw.qa_dequantize_gather_peers_dev(
+            q.data_ptr(), q.stride(0), int(zp), float(scale), self.rows, self.cols, self._bases,
+            self.world, self.rank, self.epoch, self.budget_ns, st.cuda_stream), "launch")
+        return self._views[self.epoch & 1]
+
+    def close(self):
+        """Collective: unmaps the peers' buffers and frees this rank's."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still stores into a buffer
+        for p in self._opened:
+            self._call(self.raw.qa_peer_buffer_close(p), "close")
+        self._opened = []
+        self._views = []
+        dist.barrier(group=self.group)  # every mapping of this rank's buffer is gone
+        self._call(self.raw.qa_peer_buffer_destroy(self.own), "destroy")
+        self.own = None
 
 
 def calibrate_sharded(container, batches, group=None):

@@ -1166,6 +1166,10 @@ class ResidentNet:
         """int32 graph output (before the final dequantize) of the last run."""
         return self.out_q
 
+    def output_qparams(self):
+        """QParams of the graph output (the grid ``output_int`` is on)."""
+        return self.c.qparams[self.graph.outputs[0]]
+
 
 def make_resident(container, batch, device=None):
     """The device-resident executor that runs ``container``'s graph: a
