@@ -543,6 +543,72 @@ int qa_dequantize_gather_peers_dev(const void* q, int64_t q_stride, int64_t zp, 
                                    int32_t world, int32_t rank, int64_t epoch, int64_t budget_ns,
                                    void* stream);
 
+/* Device float pass of calibration (QuantContainer.calibrate(...,
+ * device=True)).  The reference runs the float graph on host arrays
+ * (float_ops.py, with qa_conv_f32 / qa_gemm_f32) and reduces min / max of
+ * every layer output (quant_layers.py:130-137) and graph input
+ * (quant_container.py:141-149) with NumPy; these entry points keep the
+ * float tensors in device memory and fold the values each kernel writes
+ * into that tensor's range slot.  No reference counterpart for the
+ * individual symbols.
+ *
+ * A range slot is two uint32 words {min key, max key}, initialized to
+ * {0xFFFFFFFF, 0}, where key(f) = bits(f) ^ (sign ? 0xFFFFFFFF : 0x80000000)
+ * orders floats like their values (NaN above +inf).  `range` may be NULL (no
+ * reduction).  Float tensors are float32; strides and shapes are in
+ * elements, at most 6 dimensions (pass host arrays of `rank` int64).  Every
+ * call enqueues on `stream` and returns 0 or an error status.
+ *
+ * qa_f32_map_dev: y[i] = f(x[i]) for op 0 copy, 1 Sigmoid, 2 Relu,
+ *   3 LeakyRelu(p0), 4 Tanh, 5 HardSigmoid(p0, p1), 6 HardSwish, 7 Elu(p0),
+ *   8 Softplus, 9 Abs, 10 Neg, 11 Sqrt, 12 Exp, 13 Erf, 14 Gelu (erf),
+ *   15 Gelu (tanh), 16 Clip(p0, p1); float64 where float_ops widens.
+ * qa_f32_binary_dev: dense y over `shape` = a op b, a and b read through
+ *   broadcast strides; op 0 Add, 1 Sub, 2 Mul, 3 Div, 4 Max, 5 Min, 6 Pow.
+ * qa_f32_copy_dev: y[sum c * y_strides] = x[sum c * x_strides] over `shape`
+ *   (Transpose, Slice, Split, Concat, Pad interior, Expand, Gather).
+ * qa_f32_fill_dev: y[0, n) = value (Pad borders).
+ * qa_f32_range_dev: folds x[0, n) into the slot (graph inputs, views).
+ * qa_f32_range_decode_dev: `count` slots -> float32 pairs (lo, -hi); a
+ *   slot never folded gives (+inf, +inf).  One MIN all-reduce of the pairs
+ *   combines the tables of several ranks.
+ * qa_f32_gemm_dev: C[z] (dense [M, N]) = alpha * A[z] . B[z] for z < batch,
+ *   A[z][m][k] at A + z*a_batch + m*a_m + k*a_k, B alike; float32 sums.
+ * qa_f32_conv_dev: the qa_conv_f32 convolution on device pointers (same
+ *   kernel, same sums); no range (the bias Add that follows folds it).
+ * qa_f32_softmax_dev: last-axis softmax of [rows, cols], float64.
+ * qa_f32_layernorm_dev: [rows, D] normalized in float64, * gamma (+ beta).
+ * qa_f32_maxpool_dev: NCHW max pool, padding reads -inf.
+ * qa_f32_plane_mean_dev: y[p] = mean of x[p * HW, (p + 1) * HW). */
+int qa_f32_map_dev(const float* x, float* y, int64_t n, int32_t op, float p0, float p1,
+                   uint32_t* range, void* stream);
+int qa_f32_binary_dev(const float* a, const float* b, float* y, int32_t rank,
+                      const int64_t* shape, const int64_t* a_strides, const int64_t* b_strides,
+                      int32_t op, uint32_t* range, void* stream);
+int qa_f32_copy_dev(const float* x, float* y, int32_t rank, const int64_t* shape,
+                    const int64_t* x_strides, const int64_t* y_strides, uint32_t* range,
+                    void* stream);
+int qa_f32_fill_dev(float* y, int64_t n, float value, uint32_t* range, void* stream);
+int qa_f32_range_dev(const float* x, int64_t n, uint32_t* range, void* stream);
+int qa_f32_range_decode_dev(const uint32_t* range, float* out, int64_t count, void* stream);
+int qa_f32_gemm_dev(const float* A, const float* B, float* C, int64_t batch, int64_t M,
+                    int64_t N, int64_t K, int64_t a_batch, int64_t a_m, int64_t a_k,
+                    int64_t b_batch, int64_t b_k, int64_t b_n, float alpha, uint32_t* range,
+                    void* stream);
+int qa_f32_conv_dev(const float* x, const float* w, float* y, int64_t N, int64_t C, int64_t H,
+                    int64_t W, int64_t Cout, int64_t KH, int64_t KW, int64_t SH, int64_t SW,
+                    int64_t PH, int64_t PW, int64_t DH, int64_t DW, int64_t G, int64_t OH,
+                    int64_t OW, void* stream);
+int qa_f32_softmax_dev(const float* x, float* y, int64_t rows, int64_t cols, uint32_t* range,
+                       void* stream);
+int qa_f32_layernorm_dev(const float* x, const float* gamma, const float* beta, float* y,
+                         int64_t rows, int64_t D, double eps, uint32_t* range, void* stream);
+int qa_f32_maxpool_dev(const float* x, float* y, int64_t NC, int64_t H, int64_t W, int64_t kh,
+                       int64_t kw, int64_t sh, int64_t sw, int64_t pt, int64_t pl, int64_t dh,
+                       int64_t dw, int64_t OH, int64_t OW, uint32_t* range, void* stream);
+int qa_f32_plane_mean_dev(const float* x, float* y, int64_t NC, int64_t HW, uint32_t* range,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

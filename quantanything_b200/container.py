@@ -65,12 +65,24 @@ class QuantContainer:
         return list(self.quant_layers.values())
 
     # ---------------------------------------------------------- calibration --
-    def calibrate(self, x_calib, reduce_ranges=None):
+    def calibrate(self, x_calib, reduce_ranges=None, device=False):
         """Runs the calibration batches, combines ranges across ranks with
-        ``reduce_ranges`` when given, then finalizes (quant_container.py:75-91)."""
+        ``reduce_ranges`` when given, then finalizes (quant_container.py:75-91).
+
+        ``device=True`` runs the float pass and the range reductions on the
+        GPU (``calibrate_device.calibrate_on_device``): the batches' tensors
+        stay in device memory and only the range table comes back."""
         batches = [x_calib] if isinstance(x_calib, (np.ndarray, dict)) else list(x_calib)
         if not batches:
             raise ValueError("no calibration data provided")
+        if device:
+            from quantanything_b200.calibrate_device import calibrate_on_device
+
+            if reduce_ranges is not None:
+                raise ValueError("device calibration combines ranks with calibrate_on_device("
+                                 "..., reduce_group=...)")
+            calibrate_on_device(self, batches)
+            return
         for batch in batches:
             self.run_graph(batch, mode="calibrate")
         if reduce_ranges is not None:

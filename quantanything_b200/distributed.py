@@ -248,12 +248,24 @@ class PeerGather:
         self.own = None
 
 
-def calibrate_sharded(container, batches, group=None):
+def calibrate_sharded(container, batches, group=None, device=False, lib=None):
     """Each rank calibrates on its shard of ``batches`` (a list of arrays,
-    split by index), ranges are all-reduced, then every rank finalizes."""
+    split by index), ranges are all-reduced, then every rank finalizes.
+
+    ``device=True``: each rank's float pass and range reductions run on its
+    GPU and the range tables are combined in device memory with one
+    all-reduce (``calibrate_device``); ``device`` may also name the torch
+    device to use, and ``lib`` the kernel library (tests)."""
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     mine = [b for i, b in enumerate(batches) if i % world == rank]
     if not mine:
         raise ValueError("fewer calibration batches than ranks")
+    if device:
+        from quantanything_b200.calibrate_device import calibrate_on_device
+
+        calibrate_on_device(container, mine, reduce_group=group if group is not None else
+                            dist.group.WORLD, device=None if device is True else device,
+                            lib=lib)
+        return container
     container.calibrate(mine, reduce_ranges=lambda r: allreduce_ranges(r, group))
     return container

@@ -37,6 +37,14 @@ def _worker(rank, world, port, outdir):
     batches = [networks.images(3, 32, seed=50 + i) for i in range(4)]
     distributed.calibrate_sharded(qc, batches)
     qc.save(os.path.join(outdir, f"q{rank}.json"))
+    # the device calibration's path: per-rank range tables reduced with one
+    # all-reduce of the packed (lo, -hi) table (CPU tensors and NumPy
+    # stand-ins of the kernels here)
+    from tests.fake_float_kernels import FakeLibrary
+
+    qd = QuantContainer(networks.yolo_mini(width=16), "int8", lib=lib)
+    distributed.calibrate_sharded(qd, batches, device="cpu", lib=FakeLibrary(lib))
+    qd.save(os.path.join(outdir, f"d{rank}.json"))
     # each rank runs its shard of a 5-image batch; gather reassembles it
     x = networks.images(5, 32, seed=9)
     y = qc.run_graph(distributed.shard(x, rank, world), "integer")
@@ -69,6 +77,15 @@ def test_sharded_calibration_and_gather(tmp_path):
     ref = json.loads((tmp_path / "single.json").read_text())
     for r in range(world):
         assert json.loads((tmp_path / f"q{r}.json").read_text()) == ref
+    # device-path tables: identical on both ranks, and the single process's
+    # qparams up to the stand-in GEMM's float32 summation order
+    d0 = json.loads((tmp_path / "d0.json").read_text())
+    assert json.loads((tmp_path / "d1.json").read_text()) == d0
+    for name, want in ref["qparams"].items():
+        got = d0["qparams"][name]
+        assert (got["qmin"], got["qmax"]) == (want["qmin"], want["qmax"]), name
+        assert abs(got["zp"] - want["zp"]) <= 1, name
+        assert abs(got["scale"] - want["scale"]) <= 1e-5 * abs(want["scale"]), name
     expect = single.run_graph(networks.images(5, 32, seed=9), "integer")
     for r in range(world):
         np.testing.assert_array_equal(np.load(tmp_path / f"y{r}.npy"), expect)
