@@ -158,7 +158,7 @@ class DeviceCalibrator:
     def _const(self, name, value):
         t = self._consts.get(name)
         if t is None:
-            t = torch.from_numpy(np.ascontiguousarray(value, dtype=np.float32)).to(self.device)
+            t = torch.from_numpy(np.array(value, dtype=np.float32, order="C")).to(self.device)
             self._consts[name] = t
         return t
 
@@ -167,7 +167,7 @@ class DeviceCalibrator:
         if isinstance(v, torch.Tensor):
             return v
         if name is None:
-            return torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(self.device)
+            return torch.from_numpy(np.array(v, dtype=np.float32, order="C")).to(self.device)
         return self._const(name, v)
 
     def _range_of(self, t, key):
