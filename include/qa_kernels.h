@@ -427,6 +427,10 @@ typedef struct qa_fused_conv16_desc {
    * base.lut_len <= 65536); dense layers then keep the table in shared
    * memory */
   const int16_t* lut16;
+  /* weight byte planes at base.w, each base.w_rows x base.w_kp: 2 (or 0)
+   * for int16 weights (v & 0xFF, v >> 8); 3 for the 17-bit centred weights
+   * of uint16 graphs (v & 0xFF, (v >> 8) & 0xFF, v >> 16 as a signed byte) */
+  int64_t w_planes;
 } qa_fused_conv16_desc;
 
 int qa_conv16_fused_dev(const qa_fused_conv16_desc* desc, void* stream);

@@ -43,8 +43,9 @@ struct GroupedConv16Params {
   Planes16 x;
   int64_t x_zp;
   int64_t H, W, Cg, KH, KW, SH, SW, PH, PW, DH, DW, OH, OW, Cout, Cog;
-  const uint8_t* w;  // planes [2][w_rows][w_kp]
+  const uint8_t* w;  // planes [w_planes][w_rows][w_kp]
   int64_t w_plane, w_kp;
+  int32_t w_planes;  // 2: int16 weights; 3: 17-bit (bytes 0, 1 and a sign byte)
   int64_t M;
   FusedEpilogue epi;
 };
@@ -74,7 +75,11 @@ __global__ void grouped_conv16_kernel(const __grid_constant__ GroupedConv16Param
         const bool inside = iy >= 0 && iy < p.H && ix >= 0 && ix < p.W;
         const int64_t pix = img_pix + iy * p.W + ix;
         for (int64_t c = 0; c < p.Cg; ++c) {
-          const int64_t wv = plane16_value(wt + c, p.w_plane);
+          const int64_t wv =
+              p.w_planes == 3
+                  ? (int64_t)wt[c] + 256 * (int64_t)wt[c + p.w_plane] +
+                        65536 * (int64_t)(int8_t)wt[c + 2 * p.w_plane]
+                  : plane16_value(wt + c, p.w_plane);
           acc += wv * (inside ? at(p.x, pix, g * p.Cg + c) : p.x_zp);
         }
       }
@@ -111,6 +116,7 @@ bool grouped_conv16(const qa_fused_conv16_desc& d16, cudaStream_t st) {
   p.w = static_cast<const uint8_t*>(d.w);
   p.w_plane = d.w_rows * d.w_kp;
   p.w_kp = d.w_kp;
+  p.w_planes = d16.w_planes == 3 ? 3 : 2;
   p.M = d.N * d.OH * d.OW;
   fill_fused_epilogue(p.epi, d);
   p.epi.res_plane = d16.res_plane;

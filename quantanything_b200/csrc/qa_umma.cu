@@ -714,34 +714,42 @@ namespace qa {
 constexpr int kP16Threads = 448;
 constexpr int kP16LutEntries = 65536;
 
-// BN <= 64: two accumulator sets (double buffering, one epilogue warpgroup
-// per set); BN = 128: one set (3 x 128 of the 512 TMEM columns), both
-// epilogue warpgroups drain half of each tile's columns.
-template <int BN, bool kSmemLut>
+// kWP: weight byte planes.  2 for int16 weights (lo u8, hi s8): four MMAs
+// per K-step into three accumulators (shifts 0, 8, 16).  3 for the 17-bit
+// centred weights of uint16 graphs, w = b0 + 256 b1 + 65536 b2 (b0, b1 u8,
+// b2 s8 in {-1, 0}): six MMAs into four accumulators (shifts 0, 8, 16, 24).
+// Two accumulator sets (double buffering, one epilogue warpgroup per set)
+// when they fit the 512 TMEM columns, else one set that both epilogue
+// warpgroups drain half of each tile's columns.
+template <int BN, bool kSmemLut, int kWP>
 struct P16Layout {
-  static constexpr int kSets = 6 * BN <= 512 ? 2 : 1;
-  static constexpr int kStages = kSmemLut ? 2 : (BN >= 128 ? 3 : 4);
+  static constexpr int kAccs = kWP == 3 ? 4 : 3;  // accumulators per set
+  static constexpr int kSetCols = kAccs * BN;      // one accumulator set
+  static constexpr int kSets = 2 * kSetCols <= 512 ? 2 : 1;
   static constexpr int kAPlane = kBM * kBKBytes;  // 16 KB
   static constexpr int kBPlane = BN * kBKBytes;
-  static constexpr int kStage = 2 * kAPlane + 2 * kBPlane;
-  static constexpr int kSetCols = 3 * BN;  // one accumulator set
+  static constexpr int kStage = 2 * kAPlane + kWP * kBPlane;
+  static constexpr int kLutBytes = kSmemLut ? kP16LutEntries * 2 : 0;
+  static constexpr int kFit = (232448 - 1024 - 256 - kLutBytes) / kStage;
+  static constexpr int kStages =
+      kWP == 2 ? (kSmemLut ? 2 : (BN >= 128 ? 3 : 4)) : (kFit < 4 ? kFit : 4);
   static constexpr int kCols = kSets * kSetCols;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                    : kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "accumulator sets must fit TMEM");
+  static_assert(kStages >= 2, "at least two stages must fit shared memory");
   static_assert(!(kSmemLut && BN >= 128), "the shared-memory table leaves one stage at BN 128");
-  static constexpr int kLutBytes = kSmemLut ? kP16LutEntries * 2 : 0;
   static constexpr size_t kBarOff = (size_t)kStages * kStage + kLutBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + (2 * kStages + 4) * 8 + 16;
   static_assert(kSmem <= 232448, "shared memory per CTA");
 };
 
-template <int BN, int kChunk, bool kSmemLut>
+template <int BN, int kChunk, bool kSmemLut, int kWP>
 __global__ void __launch_bounds__(kP16Threads, 1)
     umma16_persistent_kernel(const __grid_constant__ ConvTileParams p,
                              const __grid_constant__ CUtensorMap tmap_b, int64_t n_tiles,
                              int64_t total_tiles) {
-  using L = P16Layout<BN, kSmemLut>;
+  using L = P16Layout<BN, kSmemLut, kWP>;
   constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_addr(smem_raw);
@@ -890,10 +898,11 @@ __global__ void __launch_bounds__(kP16Threads, 1)
         for (int kb = 0; kb < p.num_kb; ++kb, ++g) {
           const int s = (int)(g % S);
           if (g >= S && !wait(empty_bar(s), (uint32_t)(((g / S) - 1) & 1))) break;
-          ptx::mbar_arrive_expect_tx(full_bar(s), 2 * L::kBPlane);
-          ptx::tma_load_2d(b_tile(s, 0), &tmap_b, full_bar(s), kb * kBKBytes, n0);
-          ptx::tma_load_2d(b_tile(s, 1), &tmap_b, full_bar(s), kb * kBKBytes,
-                           p.b_plane_rows + n0);
+          ptx::mbar_arrive_expect_tx(full_bar(s), kWP * L::kBPlane);
+#pragma unroll
+          for (int pl = 0; pl < kWP; ++pl)
+            ptx::tma_load_2d(b_tile(s, pl), &tmap_b, full_bar(s), kb * kBKBytes,
+                             pl * p.b_plane_rows + n0);
         }
       }
     }
@@ -929,10 +938,21 @@ __global__ void __launch_bounds__(kP16Threads, 1)
           for (int kk = 0; kk < ksteps; ++kk) {
             const uint64_t a0 = al + (uint64_t)(kk * 2), b0 = bl + (uint64_t)(kk * 2);
             const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-            ptx::mma_i8(d0, a0, b0, id_ll, acc);
-            ptx::mma_i8(d0 + BN, a0, b0 + kBPl, id_lh, acc);
-            ptx::mma_i8(d0 + BN, a0 + kAPl, b0, id_hl, 1u);
-            ptx::mma_i8(d0 + 2 * BN, a0 + kAPl, b0 + kBPl, id_hh, acc);
+            if constexpr (kWP == 2) {
+              ptx::mma_i8(d0, a0, b0, id_ll, acc);
+              ptx::mma_i8(d0 + BN, a0, b0 + kBPl, id_lh, acc);
+              ptx::mma_i8(d0 + BN, a0 + kAPl, b0, id_hl, 1u);
+              ptx::mma_i8(d0 + 2 * BN, a0 + kAPl, b0 + kBPl, id_hh, acc);
+            } else {
+              // weights b0 (u8), b1 (u8), b2 (s8): shift 0: lo*b0; 8: lo*b1 +
+              // hi*b0; 16: lo*b2 + hi*b1; 24: hi*b2
+              ptx::mma_i8(d0, a0, b0, id_ll, acc);
+              ptx::mma_i8(d0 + BN, a0, b0 + kBPl, id_ll, acc);
+              ptx::mma_i8(d0 + BN, a0 + kAPl, b0, id_hl, 1u);
+              ptx::mma_i8(d0 + 2 * BN, a0, b0 + 2 * kBPl, id_lh, acc);
+              ptx::mma_i8(d0 + 2 * BN, a0 + kAPl, b0 + kBPl, id_hl, 1u);
+              ptx::mma_i8(d0 + 3 * BN, a0 + kAPl, b0 + 2 * kBPl, id_hh, acc);
+            }
           }
           ptx::mma_commit(empty_bar(s));
         }
@@ -963,9 +983,9 @@ __global__ void __launch_bounds__(kP16Threads, 1)
           tmem + (((uint32_t)quarter * 32u) << 16) + (uint32_t)(b * L::kSetCols);
 #pragma unroll 1
       for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-        uint32_t v[3][16];
+        uint32_t v[L::kAccs][16];
 #pragma unroll
-        for (int a = 0; a < 3; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
+        for (int a = 0; a < L::kAccs; ++a) ptx::tmem_ld16(lane_base + a * BN + c0, v[a]);
         ptx::tmem_ld_wait();
         const int nb = n_base + c0;
         const int cnt = p.n_valid - nb < 16 ? p.n_valid - nb : 16;
@@ -974,9 +994,11 @@ __global__ void __launch_bounds__(kP16Threads, 1)
         // checked); the int64 combination is the reference's accumulator
         int64_t acc[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < 16; ++j) {
           acc[j] = (int64_t)(int32_t)v[0][j] + (int64_t)(int32_t)v[1][j] * 256 +
                    (int64_t)(int32_t)v[2][j] * 65536;
+          if constexpr (kWP == 3) acc[j] += (int64_t)(int32_t)v[3][j] * 16777216;
+        }
         fused_epilogue_store16_run(p.epi, acc, m, nb, cnt, kSmemLut ? s_lut : nullptr);
       }
       ptx::tc_fence_before();
@@ -992,11 +1014,11 @@ __global__ void __launch_bounds__(kP16Threads, 1)
   }
 }
 
-template <int BN, int kChunk, bool kSmemLut>
+template <int BN, int kChunk, bool kSmemLut, int kWP>
 bool launch_umma16_persistent(const ConvTileParams& prm, const CUtensorMap& tmap,
                               int64_t n_tiles, cudaStream_t st) {
-  auto kern = umma16_persistent_kernel<BN, kChunk, kSmemLut>;
-  const size_t smem = P16Layout<BN, kSmemLut>::kSmem;
+  auto kern = umma16_persistent_kernel<BN, kChunk, kSmemLut, kWP>;
+  const size_t smem = P16Layout<BN, kSmemLut, kWP>::kSmem;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1019,27 +1041,37 @@ bool fill_fused_epilogue(FusedEpilogue& e, const qa_fused_conv_desc& d);  // qa_
 
 namespace {
 
-template <int kChunk, bool kSmemLut>
+template <int kChunk, bool kSmemLut, int kWP>
 bool launch_conv16_lut(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
                        int64_t n_tiles, cudaStream_t st) {
   switch (bn) {
-    case 16: return launch_umma16_persistent<16, kChunk, kSmemLut>(prm, tmap, n_tiles, st);
-    case 32: return launch_umma16_persistent<32, kChunk, kSmemLut>(prm, tmap, n_tiles, st);
-    default: return launch_umma16_persistent<64, kChunk, kSmemLut>(prm, tmap, n_tiles, st);
+    case 16: return launch_umma16_persistent<16, kChunk, kSmemLut, kWP>(prm, tmap, n_tiles, st);
+    case 32: return launch_umma16_persistent<32, kChunk, kSmemLut, kWP>(prm, tmap, n_tiles, st);
+    default:
+      if constexpr (kWP == 3 && kSmemLut) {
+        // three weight planes at BN 64 leave no room for the table
+        set_error(kBadArgument, "qa_conv16_fused_dev: no shared-memory table at BN 64");
+        return false;
+      } else {
+        return launch_umma16_persistent<64, kChunk, kSmemLut, kWP>(prm, tmap, n_tiles, st);
+      }
   }
 }
 
-template <int kChunk>
+template <int kChunk, int kWP>
 bool launch_conv16_bn(int bn, const ConvTileParams& prm, const CUtensorMap& tmap,
                       int64_t n_tiles, cudaStream_t st) {
   // BN = 128 keeps the table in global memory (see P16Layout)
-  if (bn == 128) return launch_umma16_persistent<128, kChunk, false>(prm, tmap, n_tiles, st);
-  // the kernel copies the table in 16-byte pieces
+  if (bn == 128)
+    return launch_umma16_persistent<128, kChunk, false, kWP>(prm, tmap, n_tiles, st);
+  // the kernel copies the table in 16-byte pieces; with three weight planes
+  // only the narrow tiles leave room for it
   const bool smem_lut = prm.epi.lut && prm.epi.lut16 && prm.epi.lut_len <= kP16LutEntries &&
                         prm.epi.lut_len % 8 == 0 &&
-                        (reinterpret_cast<uintptr_t>(prm.epi.lut16) & 15) == 0;
-  return smem_lut ? launch_conv16_lut<kChunk, true>(bn, prm, tmap, n_tiles, st)
-                  : launch_conv16_lut<kChunk, false>(bn, prm, tmap, n_tiles, st);
+                        (reinterpret_cast<uintptr_t>(prm.epi.lut16) & 15) == 0 &&
+                        (kWP == 2 || bn <= 32);
+  return smem_lut ? launch_conv16_lut<kChunk, true, kWP>(bn, prm, tmap, n_tiles, st)
+                  : launch_conv16_lut<kChunk, false, kWP>(bn, prm, tmap, n_tiles, st);
 }
 
 }  // namespace
@@ -1103,13 +1135,21 @@ bool umma_conv16_fused(const qa_fused_conv16_desc& d16, cudaStream_t st) {
   prm.epi.out_plane = d16.out_plane;
   prm.epi.out2_plane = d16.out2_plane;
   prm.epi.lut16 = d16.lut16;
+  const int wp = d16.w_planes == 3 ? 3 : 2;
+  if (d16.w_planes != 0 && d16.w_planes != 2 && d16.w_planes != 3) {
+    set_error(kBadArgument, "qa_conv16_fused_dev: w_planes must be 2 or 3");
+    return false;
+  }
   CUtensorMap tmap;
-  if (!make_weight_tmap(&tmap, d.w, 2 * d.w_rows, d.w_kp, (int)bn)) return false;
+  if (!make_weight_tmap(&tmap, d.w, wp * d.w_rows, d.w_kp, (int)bn)) return false;
   const bool wide = d.C % 16 == 0 && d.x_pix_stride % 16 == 0 && (xa & 15) == 0 &&
                     (d16.x_plane & 15) == 0;
   const int64_t n_tiles = d.w_rows / bn;
-  return wide ? launch_conv16_bn<16>((int)bn, prm, tmap, n_tiles, st)
-              : launch_conv16_bn<4>((int)bn, prm, tmap, n_tiles, st);
+  if (wp == 3)
+    return wide ? launch_conv16_bn<16, 3>((int)bn, prm, tmap, n_tiles, st)
+                : launch_conv16_bn<4, 3>((int)bn, prm, tmap, n_tiles, st);
+  return wide ? launch_conv16_bn<16, 2>((int)bn, prm, tmap, n_tiles, st)
+              : launch_conv16_bn<4, 2>((int)bn, prm, tmap, n_tiles, st);
 }
 
 }  // namespace qa

@@ -314,6 +314,10 @@ class ResidentNet:
         """Width of the contraction operands (packed weights, activations)."""
         return self.bits
 
+
+    def _weight_bits(self):
+        """Signed width the packed centred weights must fit."""
+        return self._operand_bits()
     def _alloc(self, nbytes):
         t = torch.empty(int(nbytes) + 64, dtype=torch.uint8, device=self.device)
         self._keep.append(t)
@@ -511,7 +515,7 @@ class ResidentNet:
             w4 = layer.w_centered.astype(np.int64)
             cout, cg, kh, kw = w4.shape
             groups = layer.node.attr("group", 1)
-        bits = self._operand_bits()
+        bits = self._weight_bits()
         lim = 1 << (bits - 1)
         if w4.min() < -lim or w4.max() >= lim:
             raise UnsupportedGraph(f"{layer.name}: centred weights exceed int{bits}")
@@ -521,7 +525,8 @@ class ResidentNet:
         rows = _round_up(cout, bn)
         k = kh * kw * ct
         kp = _round_up(k, 16)
-        packed = np.zeros((rows, kp), np.int8 if bits == 8 else np.int16)
+        packed = np.zeros((rows, kp), np.int8 if bits == 8 else np.int16 if bits == 16
+                          else np.int32)
         wt = np.zeros((cout, kh, kw, ct), np.int64)
         wt[:, :, :, :cg] = np.transpose(w4, (0, 2, 3, 1))
         packed[:cout, :k] = wt.reshape(cout, k)

@@ -48,7 +48,8 @@ class FusedConv16Desc(ctypes.Structure):
     """ctypes mirror of ``qa_fused_conv16_desc`` (include/qa_kernels.h)."""
 
     _fields_ = [("base", FusedConvDesc), ("x_plane", _I64), ("res_plane", _I64),
-                ("out_plane", _I64), ("out2_plane", _I64), ("lut16", _P)]
+                ("out_plane", _I64), ("out2_plane", _I64), ("lut16", _P),
+                ("w_planes", _I64)]
 
 
 _DEV16_SIGNATURES = {
@@ -82,8 +83,45 @@ def device_api16(lib):
     return raw
 
 
+UINT16_SHIFT = 32768
+
+
+def shifted_container(container, shift=UINT16_SHIFT):
+    """A view of ``container`` whose activations live ``shift`` lower: every
+    activation QParams (zp, qmin, qmax), activation table (values and index
+    offset) and quantized constant moves by ``-shift``; weights, scales,
+    multipliers and biases are untouched.  The reference's integer steps
+    read activations only through ``v - zp`` (contractions, Add, Mul,
+    Concat rescale, GAP, the float fallbacks), ``v - qmin`` (tables), order
+    (MaxPool) or write ``clamp(. + zp, qmin, qmax)`` (requantize), so every
+    value of the shifted graph is the original minus ``shift``: a uint16
+    graph ([0, 65535]) runs on signed int16 planes."""
+    import copy
+
+    from quantanything_b200.utils import QParams
+
+    def sq(qp):
+        return QParams(qp.scale, int(qp.zp) - shift, int(qp.qmin) - shift, int(qp.qmax) - shift)
+
+    c = copy.copy(container)
+    c.qparams = {k: sq(v) for k, v in container.qparams.items()}
+    c._const_q = {k: np.asarray(v, np.int64) - shift for k, v in container._const_q.items()}
+    layers = {}
+    for name, layer in container.quant_layers.items():
+        sl = copy.copy(layer)
+        sl.in_qp = [sq(q) for q in layer.in_qp]
+        sl.out_qp = [sq(q) for q in layer.out_qp]
+        if getattr(layer, "lut", None) is not None:
+            sl.lut = (np.asarray(layer.lut, np.int64) - shift).astype(np.int32)
+            sl.lut_offset = int(layer.lut_offset) - shift
+        layers[name] = sl
+    c.quant_layers = layers
+    return c
+
+
 class ResidentNet16(ResidentNet):
-    """Fused device-resident integer inference of a prepared int16 container."""
+    """Fused device-resident integer inference of a prepared int16 container
+    (also uint8, and uint16 through ``shifted_container``)."""
 
     # the persistent kernel runs column tiles up to 128 (two TMEM accumulator
     # sets of 3 x BN columns up to 64, one set at 128); measured on B200 the
@@ -94,6 +132,14 @@ class ResidentNet16(ResidentNet):
     def __init__(self, container, batch, device=None):
         self._planes = []  # (low plane start, plane bytes) of every allocation
         self._lut16 = {}   # int32 table address -> int16 device copy
+        layer0 = container.layers[0]
+        # uint16: activations stored 32768 lower (signed int16 planes); the
+        # centred weights span 17 bits and take three byte planes
+        self._act_shift = UINT16_SHIFT if (layer0.num_bits == 16 and not layer0.signed) else 0
+        self._w_planes = 3 if self._act_shift else 2
+        self._orig = container
+        if self._act_shift:
+            container = shifted_container(container, self._act_shift)
         super().__init__(container, batch, device, fuse_input=False)
         device_api16(self.lib)
         self._descs = {}
@@ -103,11 +149,22 @@ class ResidentNet16(ResidentNet):
         # uint8 graphs (asymmetric activations and weights) take this route
         # too: their centred weights span [-255, 255], past int8 but within
         # int16, and a uint8 value is an int16 with a zero high byte
-        if not ((self.bits == 16 and self.signed) or (self.bits == 8 and not self.signed)):
-            raise UnsupportedGraph("ResidentNet16 runs int16 and uint8 graphs")
+        if not (self.bits == 16 or (self.bits == 8 and not self.signed)):
+            raise UnsupportedGraph("ResidentNet16 runs int16, uint16 and uint8 graphs")
 
     def _operand_bits(self):
         return 16
+
+    def _weight_bits(self):
+        return 17 if self._w_planes == 3 else 16
+
+    def output_int(self):
+        """int32 graph output of the last run on the reference's grid (a
+        uint16 graph's shifted activations moved back: a new tensor)."""
+        return self.out_q + self._act_shift if self._act_shift else self.out_q
+
+    def output_qparams(self):
+        return self._orig.qparams[self.graph.outputs[0]]
 
     def _new_view(self, N, H, W, C, qp, pix_stride=None):
         stride = pix_stride or (C if C % 16 == 0 else _round_up(C, 16))
@@ -135,11 +192,11 @@ class ResidentNet16(ResidentNet):
                                          & (ts <= 94))))
 
     def _upload_weights(self, packed):
-        # [rows, kp] int16 -> [2][rows][kp] bytes: low plane, then high plane
+        # [rows, kp] -> [2][rows][kp] bytes (low plane, high plane) for int16
+        # weights, [3][rows][kp] (bytes 0, 1, sign byte) for 17-bit ones
         v = packed.astype(np.int64)
-        planes = np.concatenate([(v & 0xFF).astype(np.uint8),
-                                 ((v >> 8) & 0xFF).astype(np.uint8)])
-        return self._dev(planes, np.uint8)
+        planes = [(v >> (8 * i)) & 0xFF for i in range(self._w_planes)]
+        return self._dev(np.concatenate([p.astype(np.uint8) for p in planes]), np.uint8)
 
     def _desc16(self, step):
         d16 = self._descs.get(id(step))
@@ -153,6 +210,7 @@ class ResidentNet16(ResidentNet):
             d16.out2_plane = self._plane_of(d.out2) if d.out2 else 0
             lut = self._lut_as_int16(d.lut, d.lut_len) if d.lut else None
             d16.lut16 = lut.data_ptr() if lut is not None else None
+            d16.w_planes = self._w_planes
             self._descs[id(step)] = d16
         return d16
 
@@ -284,5 +342,5 @@ class ResidentNet16(ResidentNet):
         rows = v.N * v.H * v.W
         lo = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset).to(torch.int32)
         hi = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset + v.plane)
-        t = lo + hi.view(torch.int8).to(torch.int32) * 256
+        t = lo + hi.view(torch.int8).to(torch.int32) * 256 + self._act_shift
         return t.reshape(v.N, v.H, v.W, v.C).permute(0, 3, 1, 2).contiguous()

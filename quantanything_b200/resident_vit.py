@@ -464,6 +464,10 @@ class ResidentViT16(ResidentViT, ResidentNet16):
     def __init__(self, container, batch, device=None):
         self._planes = []
         self._lut16 = {}
+        self._act_shift, self._w_planes, self._orig = 0, 2, container
+        layer0 = container.layers[0]
+        if layer0.num_bits == 16 and not layer0.signed:
+            raise UnsupportedGraph("uint16 transformer graphs run on the per-layer ABI route")
         ResidentNet.__init__(self, container, batch, device, fuse_input=False)
         device_api16(self.lib)
         vit16_api(self.lib)

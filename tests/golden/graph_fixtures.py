@@ -25,6 +25,11 @@ NETWORKS = {
     "sppf_mini_uint8": ("sppf_mini", {"width": 16}, "uint8", 2, 4, 2),
     "shaping_mini_int8": ("shaping_mini", {"width": 16}, "int8", 2, 4, 2),
     "shaping_mini_int16": ("shaping_mini", {"width": 16}, "int16", 2, 4, 2),
+    # uint16: asymmetric 16-bit activations and weights (17-bit centred weights)
+    "yolo_mini_uint16": ("yolo_mini", {"width": 16}, "uint16", 2, 4, 2),
+    "sppf_mini_uint16": ("sppf_mini", {"width": 16}, "uint16", 2, 4, 2),
+    "shaping_mini_uint16": ("shaping_mini", {"width": 16}, "uint16", 2, 4, 2),
+    "yolov8n_cls_uint16": ("yolov8n_cls", {}, "uint16", 4, 8, 2),
     # the batch is static in a ViT graph: calibration and evaluation use it
     "vit_mini_int8": ("vit", {"batch": 4}, "int8", 2, 4, 4),
     "vit_mini_int16": ("vit", {"batch": 4}, "int16", 2, 4, 4),

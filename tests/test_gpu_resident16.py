@@ -144,3 +144,42 @@ def test_uint8_graphs_on_the_16bit_route(gpu_lib, name):
     env, logits = _integer_pass(qc, x)
     got = net.tensor(logits).cpu().numpy().reshape(env[logits].shape)
     np.testing.assert_array_equal(got, env[logits])
+
+
+@pytest.mark.parametrize("name", ["yolo_mini_uint16", "sppf_mini_uint16", "shaping_mini_uint16",
+                                  "yolov8n_cls_uint16"])
+def test_uint16_graphs_match_reference(gpu_lib, name):
+    """uint16 graphs on the resident 16-bit route: activations stored 32768
+    lower in the signed planes, 17-bit centred weights in three byte planes
+    (six 8-bit tensor-core products per K-step).  Every planned tensor must
+    equal the drop-in pass's (itself pinned to the reference) and the
+    output the reference's within the Softmax fallback's LSB."""
+    from quantanything_b200.resident import make_resident
+    from quantanything_b200.resident16 import ResidentNet16
+
+    meta = json.loads((GRAPHS / f"{name}.meta.json").read_text())
+    g = getattr(networks, meta["builder"])(**meta["kwargs"])
+    qc = QuantContainer.load(g, GRAPHS / f"{name}.qjson", lib=gpu_lib)
+    net = make_resident(qc, meta["eval_batch"])
+    assert isinstance(net, ResidentNet16) and net._w_planes == 3
+    x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
+    net.forward_device(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    net.check_status()
+    ref = np.load(GRAPHS / f"{name}.npz")
+    q = net.output_int().cpu().numpy().astype(np.int64)
+    assert q.min() >= 0 and np.abs(q - ref["q"]).max() <= SOFTMAX_LSB
+    env, _ = _integer_pass(qc, x)
+    # a tensor whose consumers are all Concats lands in the Concat's buffer
+    # (rescaled in the producer's epilogue); its own view is never written
+    concat_only = {t for t in net._views
+                   if all(n.op_type == "Concat" for n in g.nodes if t in n.inputs)
+                   and any(t in n.inputs for n in g.nodes)}
+    checked = 0
+    for tname in net._views:
+        if tname not in env or tname == qc.graph.inputs[0].name or tname in concat_only:
+            continue
+        got = net.tensor(tname).cpu().numpy().reshape(env[tname].shape)
+        np.testing.assert_array_equal(got, env[tname], err_msg=tname)
+        checked += 1
+    assert checked >= 5

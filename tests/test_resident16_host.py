@@ -7,6 +7,7 @@ pointers are placeholders.
 """
 import ctypes
 
+import numpy as np
 import pytest
 
 from quantanything_b200 import native
@@ -89,3 +90,32 @@ def test_quantize_to_planes16_rejects_out_of_range_bounds(lib):
     msg = lib.raw.qa_last_error().decode()
     lib.raw.qa_clear_error()
     assert rc != 0 and "qa_quantize_to_planes16_dev" in msg
+
+
+@pytest.mark.parametrize("name", ["yolo_mini_uint16", "sppf_mini_uint16", "shaping_mini_uint16"])
+def test_uint16_shift_is_exact_through_the_integer_pass(oracle, name):
+    """The uint16 resident route stores activations 32768 lower.  The
+    shifted container (every activation zp / qmin / qmax / table moved by
+    -32768) run through the drop-in integer pass gives the reference's
+    outputs minus 32768, bit for bit, and the same dequantized floats."""
+    import json
+
+    from quantanything_b200 import networks
+    from quantanything_b200.container import QuantContainer
+    from quantanything_b200.resident16 import UINT16_SHIFT, shifted_container
+    from tests.conftest import GOLDEN
+
+    graphs = GOLDEN / "graphs"
+    meta = json.loads((graphs / f"{name}.meta.json").read_text())
+    g = getattr(networks, meta["builder"])(**meta["kwargs"])
+    qc = QuantContainer.load(g, graphs / f"{name}.qjson", lib=oracle)
+    x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
+    ref = np.load(graphs / f"{name}.npz")
+    sc = shifted_container(qc)
+    q = np.asarray(sc.run_integer_raw(x), np.int64)
+    assert q.min() >= -UINT16_SHIFT and q.max() < UINT16_SHIFT
+    np.testing.assert_array_equal(q + UINT16_SHIFT, ref["q"])
+    y = sc.run_graph(x, "integer")
+    np.testing.assert_array_equal(np.asarray(y).view(np.uint32), ref["y"].view(np.uint32))
+    # the original container is untouched
+    np.testing.assert_array_equal(np.asarray(qc.run_integer_raw(x)), ref["q"])
