@@ -201,6 +201,19 @@ typedef struct qa_fused_conv_desc {
   const int32_t* pad_row_class;  /* [OH] */
   const int32_t* pad_col_class;  /* [OW] */
   int64_t pad_col_classes, pad_classes;
+  /* Optional GlobalAveragePool of this layer's (final 8-bit) output fused
+   * into the epilogue (gap_sum NULL: none; the reference's
+   * GlobalAveragePoolQuantize, quant_layers.py:563-590):
+   * gap_out[n * gap_out_stride + c] = clamp(mbqm(sum over the image's OH*OW
+   * pixels of (v - gap_zp_in), gap_mult, gap_shift) + gap_zp_out).
+   * gap_sum (int32 [N][Cout]) and gap_cnt (int32 [N][ceil(Cout / block_n)])
+   * must hold zeros on entry and hold zeros again on exit.  Pointwise layers
+   * (1x1, stride 1, no padding, C % 16 == 0) with block_n 128 or 256 and
+   * OH * OW >= 32 only; `out` may be NULL to skip the full-size store. */
+  int32_t* gap_sum;
+  int32_t* gap_cnt;
+  void* gap_out;
+  int64_t gap_out_stride, gap_zp_in, gap_mult, gap_shift, gap_zp_out, gap_qmin, gap_qmax;
 } qa_fused_conv_desc;
 
 int qa_conv_fused_dev(const qa_fused_conv_desc* desc, void* stream);

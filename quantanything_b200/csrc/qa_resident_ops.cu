@@ -2097,7 +2097,7 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
   clear_error();
   if (!d || !x || d->C != 4 || c_in < 1 || c_in > 4 || d->groups != 1 || !d->x_signed ||
       d->Cout > kInMaxCout || d->KH * d->KW > kInMaxTaps || d->w_kp < d->KH * d->KW * 4 ||
-      !d->out || d->res || d->out2 ||
+      !d->out || d->res || d->out2 || d->gap_sum ||
       !d->mult || !d->shift || scale == 0.0) {
     set_error(kBadArgument, "qa_conv_input_fused_dev: unsupported layer");
     return last_status();

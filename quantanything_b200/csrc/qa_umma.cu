@@ -1082,6 +1082,10 @@ bool umma_conv16_fused(const qa_fused_conv16_desc& d16, cudaStream_t st) {
   const int64_t bn = d.block_n;
   const int64_t K = d.KH * d.KW * d.C;
   const uintptr_t xa = reinterpret_cast<uintptr_t>(d.x);
+  if (d.gap_sum) {
+    set_error(kUnsupported, "qa_conv16_fused_dev: no fused GlobalAveragePool on 16-bit layers");
+    return false;
+  }
   if (bn != 16 && bn != 32 && bn != 64 && bn != 128) {
     set_error(kBadArgument, "qa_conv16_fused_dev: block_n must be 16, 32, 64 or 128");
     return false;

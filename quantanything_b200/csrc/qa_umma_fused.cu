@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -95,6 +96,18 @@ struct FusedParams {
   int32_t* status;
   FastFlags fast;
   FusedEpilogue epi;
+  // GlobalAveragePool of this layer's output fused into the epilogue
+  // (kGap): per (image, channel) sums of (v - gap_zp_in), per (image,
+  // column tile) counts of the (row, column) contributions; the warp whose
+  // contribution completes an (image, column tile) requantizes its pooled
+  // values and zeroes the sums and the count again
+  int32_t* gap_sum;  // [N][n_valid]
+  int32_t* gap_cnt;  // [N][n_tiles]
+  uint8_t* gap_out;
+  int64_t gap_out_stride;
+  int32_t gap_hw, gap_zp_in;
+  int64_t gap_mult, gap_shift, gap_zp_out, gap_qmin, gap_qmax;
+  int32_t gap_fast;  // (sum * M0 + 2^(ts-1)) >> ts is exact in 64 bits (host-proven)
 };
 
 __device__ __forceinline__ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) {
@@ -170,7 +183,7 @@ __device__ __noinline__ int64_t add_exact_ool(int64_t a, int64_t q, const FusedE
 // for a pointwise layer read as a row matrix by 2-D tiled TMA (one load per
 // K-block, 128-byte swizzle), or 0
 // for the TMA im2col gather (16-byte channel slices, no swizzle).
-template <int BN, int kChunk, bool kResidentB, int kStages>
+template <int BN, int kChunk, bool kResidentB, int kStages, bool kGap = false>
 __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThreads), 1)
     fused_conv_persistent(const __grid_constant__ FusedParams p,
                           const __grid_constant__ CUtensorMap tmap_b,
@@ -571,7 +584,7 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     // plain requantize to the full 8-bit range: clamp and pack in one step
     // (streamed-weight variants only: the resident ones are at their
     // register limit)
-    const bool pack_sat = !kResidentB && hi_rq && !e.lut && !e.res && !e.out2 &&
+    const bool pack_sat = !kGap && !kResidentB && hi_rq && !e.lut && !e.res && !e.out2 &&
                           ((e.qmin == 0 && e.qmax == 255) || (e.qmin == -128 && e.qmax == 127));
     const bool pack_signed = e.qmin < 0;
     const bool has_lut = e.lut != nullptr, add_tab = p.fast.add_tab;
@@ -595,6 +608,8 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
     const bool vec_ok = p.vec_ok != 0;
     const bool pad_corr = p.pad_corr != nullptr;
     const int64_t M = p.M;
+    int32_t* const gap_sum = p.gap_sum;
+    const int gap_hw = p.gap_hw, gap_zp = p.gap_zp_in;
     int j = 0;
     for (int mt = m_first; mt < p.m_tiles; mt += m_step, ++j) {
       if (!L::kSplit && j % L::kGroups != grp) continue;
@@ -606,6 +621,15 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       ptx::tc_fence_after();
       const int64_t m = (int64_t)mt * kBM + r;
       const bool row_ok = ok && m < M;
+      // fused GlobalAveragePool: this row's image (rows fit 32 bits) and the
+      // warp's first image; the warp's rows span at most two images
+      int gimg = -1, gimg0 = -1;
+      bool gtwo = false;
+      if constexpr (kGap) {
+        gimg = row_ok ? (int)((uint32_t)m / (uint32_t)gap_hw) : -1;
+        gimg0 = __shfl_sync(0xffffffffu, gimg, 0);
+        gtwo = __any_sync(0xffffffffu, gimg >= 0 && gimg != gimg0);
+      }
       // border class of this output pixel (nonzero input zero point with
       // out-of-image taps read as 0 by the TMA gather)
       const int32_t* corr = nullptr;
@@ -627,6 +651,11 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
         const int cc = cbase + c0;  // tile column of this chunk
         const bool more = c0 + 16 < gcols;
         if (more) ptx::tmem_ld16(lane_base + c0 + 16, vn);
+        int32_t gq[16];  // pooled contributions v - gap_zp of this chunk (kGap)
+        if constexpr (kGap) {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) gq[jj] = 0;
+        }
         if (row_ok && n0 + cc < n_valid) {
           const int nval = min(16, n_valid - (n0 + cc));
           if (corr) {
@@ -715,6 +744,10 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
                 q[jj] = (int32_t)add_exact_ool(sbyte(w[jj >> 2], jj, res_signed), q[jj], e);
             }
           }
+          if constexpr (kGap) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) gq[jj] = jj < nval ? q[jj] - gap_zp : 0;
+          }
           // primary store
           if (out_p) {
             uint32_t o[4];
@@ -748,6 +781,32 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
           }
           }  // requantize with table steps
         }
+        if constexpr (kGap) {
+          // the warp's 32 rows span at most two images (gap_hw >= 32, host-
+          // checked): one sum per image and column, added by lane jj
+          if (n0 + cc < n_valid && gimg0 >= 0) {
+            const bool first = gimg == gimg0;
+            int32_t mine0 = 0, mine1 = 0;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int32_t s0 = __reduce_add_sync(0xffffffffu, first ? gq[jj] : 0);
+              if (lane == jj) mine0 = s0;
+            }
+            if (gtwo) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const int32_t s1 = __reduce_add_sync(0xffffffffu, first ? 0 : gq[jj]);
+                if (lane == jj) mine1 = s1;
+              }
+            }
+            const int nv = min(16, n_valid - (n0 + cc));
+            if (lane < nv) {
+              int32_t* sp = gap_sum + (int64_t)gimg0 * n_valid + n0 + cc + lane;
+              if (mine0) atomicAdd(sp, mine0);
+              if (gtwo && mine1) atomicAdd(sp + n_valid, mine1);
+            }
+          }
+        }
         if (more) {
           ptx::tmem_ld_wait(vn);
 #pragma unroll
@@ -756,6 +815,58 @@ __global__ void __launch_bounds__((Layout<BN, kChunk, kResidentB, kStages>::kThr
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(acc_empty0 + 8u * ab);
+      if constexpr (kGap) {
+        // count this warp's (row, column) contributions per image; the warp
+        // that completes an (image, column tile) pools it
+        const int img0 = gimg0;
+        const int rows0 = __popc(__ballot_sync(0xffffffffu, gimg >= 0 && gimg == img0));
+        const int rows1 = __popc(__ballot_sync(0xffffffffu, gimg >= 0 && gimg != img0));
+        const int tile_cols = min(BN, n_valid - n0);
+        const int my_cols = max(0, min(gcols, n_valid - (n0 + cbase)));
+        const int target = gap_hw * tile_cols;
+        int fin = 0;
+        __threadfence();
+        if (lane == 0 && img0 >= 0 && my_cols > 0) {
+          int32_t* cp = p.gap_cnt + (int64_t)img0 * p.n_tiles + n_tile;
+          if (rows0 && atomicAdd(cp, rows0 * my_cols) + rows0 * my_cols == target) fin |= 1;
+          if (rows1 && atomicAdd(cp + p.n_tiles, rows1 * my_cols) + rows1 * my_cols == target)
+            fin |= 2;
+        }
+        fin = __shfl_sync(0xffffffffu, fin, 0);
+        for (int k = 0; k < 2; ++k) {
+          if (!((fin >> k) & 1)) continue;
+          const int im = img0 + k;
+          __threadfence();
+          // every sum of this (image, column tile) is complete in L2: read
+          // them all at once (L2-coherent loads), pool, zero them again
+          int32_t* const srow = gap_sum + (int64_t)im * n_valid + n0;
+          int32_t sv[BN / 32];
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i) {
+            const int c = lane + 32 * i;
+            sv[i] = c < tile_cols ? __ldcg(srow + c) : 0;
+          }
+          uint8_t* const orow = p.gap_out + (int64_t)im * p.gap_out_stride + n0;
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i) {
+            const int c = lane + 32 * i;
+            if (c >= tile_cols) continue;
+            int64_t q;
+            if (p.gap_fast) {
+              const int ts = 31 + (int)p.gap_shift;
+              q = clamp64((((int64_t)sv[i] * p.gap_mult + (int64_t(1) << (ts - 1))) >> ts) +
+                              p.gap_zp_out,
+                          p.gap_qmin, p.gap_qmax);
+            } else {
+              q = requant_exact_ool(sv[i], p.gap_mult, p.gap_shift, p.gap_zp_out, p.gap_qmin,
+                                    p.gap_qmax);
+            }
+            orow[c] = (uint8_t)q;
+            __stcg(srow + c, 0);
+          }
+          if (lane == 0) __stcg(p.gap_cnt + (int64_t)im * p.n_tiles + n_tile, 0);
+        }
+      }
     }
   }
 
@@ -780,10 +891,10 @@ size_t smem_bytes(int num_kb, int pad_classes) {
 constexpr int kStagesFused = 4;
 constexpr size_t kSmemCap = 227 * 1024;
 
-template <int BN, int kChunk, bool kResidentB, int kStages>
+template <int BN, int kChunk, bool kResidentB, int kStages, bool kGap = false>
 bool launch_persistent(const FusedParams& prm_in, const CUtensorMap& tmap,
                        const CUtensorMap& tmap_a, cudaStream_t st) {
-  auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStages>;
+  auto kern = fused_conv_persistent<BN, kChunk, kResidentB, kStages, kGap>;
   const size_t smem = smem_bytes<BN, kChunk, kResidentB, kStages>(prm_in.num_kb,
                                                                    prm_in.pad_classes);
   FusedParams prm = prm_in;
@@ -811,24 +922,24 @@ bool launch_persistent(const FusedParams& prm_in, const CUtensorMap& tmap,
 // TMA-fed layers keep up to eight activation stages in flight when shared
 // memory allows: a stage's load latency is then covered by the MMAs of the
 // stages ahead of it.
-template <int BN, int kChunk, bool kResidentB>
+template <int BN, int kChunk, bool kResidentB, bool kGap = false>
 bool launch_staged(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
                    cudaStream_t st) {
   if constexpr (kChunk <= 1) {
     if (smem_bytes<BN, kChunk, kResidentB, 8>(prm.num_kb, prm.pad_classes) <= kSmemCap)
-      return launch_persistent<BN, kChunk, kResidentB, 8>(prm, tmap, tmap_a, st);
+      return launch_persistent<BN, kChunk, kResidentB, 8, kGap>(prm, tmap, tmap_a, st);
     if (smem_bytes<BN, kChunk, kResidentB, 6>(prm.num_kb, prm.pad_classes) <= kSmemCap)
-      return launch_persistent<BN, kChunk, kResidentB, 6>(prm, tmap, tmap_a, st);
+      return launch_persistent<BN, kChunk, kResidentB, 6, kGap>(prm, tmap, tmap_a, st);
   }
-  return launch_persistent<BN, kChunk, kResidentB, kStagesFused>(prm, tmap, tmap_a, st);
+  return launch_persistent<BN, kChunk, kResidentB, kStagesFused, kGap>(prm, tmap, tmap_a, st);
 }
 
-template <int BN, int kChunk>
+template <int BN, int kChunk, bool kGap = false>
 bool launch_bn(const FusedParams& prm, const CUtensorMap& tmap, const CUtensorMap& tmap_a,
                cudaStream_t st) {
   if (smem_bytes<BN, kChunk, true, kStagesFused>(prm.num_kb, prm.pad_classes) <= kSmemCap)
-    return launch_staged<BN, kChunk, true>(prm, tmap, tmap_a, st);
-  return launch_staged<BN, kChunk, false>(prm, tmap, tmap_a, st);
+    return launch_staged<BN, kChunk, true, kGap>(prm, tmap, tmap_a, st);
+  return launch_staged<BN, kChunk, false, kGap>(prm, tmap, tmap_a, st);
 }
 
 using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -943,7 +1054,13 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
     set_error(kUnsupported, "qa_conv_fused_dev: output ranges must be 8-bit");
     return false;
   }
-  if (d.groups > 1) return fused_conv_grouped(d, st);
+  if (d.groups > 1) {
+    if (d.gap_sum) {
+      set_error(kUnsupported, "qa_conv_fused_dev: no fused GlobalAveragePool on grouped layers");
+      return false;
+    }
+    return fused_conv_grouped(d, st);
+  }
   const int chunk = (d.C % 16 == 0 && d.x_pix_stride % 16 == 0) ? 16
                     : (d.C % 4 == 0 && d.x_pix_stride % 4 == 0) ? 4 : 0;
   if (!chunk || (reinterpret_cast<uintptr_t>(d.x) & (chunk - 1)) || !d.w || !d.mult ||
@@ -1043,6 +1160,39 @@ bool fused_conv_v2(const qa_fused_conv_desc& d, cudaStream_t st) {
                            : 0;
   prm.fast.r64 = d.out2 ? small_rescale_fast(d.r_zp_in, d.r_m, d.r_s) : 0;
   fill_fused_epilogue(prm.epi, d);
+  if (d.gap_sum) {
+    // GlobalAveragePool fused into a pointwise layer's epilogue: the rows of
+    // one warp span at most two images, every pooled sum fits int32
+    const int64_t hw = d.OH * d.OW;
+    if (!tile_a || (bn != 128 && bn != 256) || !d.gap_cnt || !d.gap_out || hw < 32 ||
+        hw * 255 >= (int64_t(1) << 31) || d.gap_zp_in < -128 || d.gap_zp_in > 255 ||
+        d.gap_qmin < -128 || d.gap_qmax > 255) {
+      set_error(kUnsupported, "qa_conv_fused_dev: fused GlobalAveragePool needs a pointwise "
+                              "layer, a 128 or 256 column tile and at least 32 pixels per "
+                              "image");
+      return false;
+    }
+    prm.gap_sum = d.gap_sum;
+    prm.gap_cnt = d.gap_cnt;
+    prm.gap_out = static_cast<uint8_t*>(d.gap_out);
+    prm.gap_out_stride = d.gap_out_stride;
+    prm.gap_hw = (int32_t)hw;
+    prm.gap_zp_in = (int32_t)d.gap_zp_in;
+    prm.gap_mult = d.gap_mult;
+    prm.gap_shift = d.gap_shift;
+    prm.gap_zp_out = d.gap_zp_out;
+    prm.gap_qmin = d.gap_qmin;
+    prm.gap_qmax = d.gap_qmax;
+    {
+      // |sum| <= hw * 255 (int8 / uint8 input against its zero point)
+      const int64_t ts = 31 + d.gap_shift;
+      const double bound = (double)hw * 255.0 * std::fabs((double)d.gap_mult) +
+                           std::ldexp(1.0, (int)std::min<int64_t>(std::max<int64_t>(ts, 1), 62));
+      prm.gap_fast = ts >= 1 && ts <= 62 && bound < std::ldexp(1.0, 62) ? 1 : 0;
+    }
+    return bn == 128 ? launch_bn<128, 1, true>(prm, tmap, tmap_a, st)
+                     : launch_bn<256, 1, true>(prm, tmap, tmap_a, st);
+  }
   if (tile_a) {
     switch (bn) {
       case 16: return launch_bn<16, 1>(prm, tmap, tmap_a, st);

@@ -66,6 +66,9 @@ class FusedConvDesc(ctypes.Structure):
         ("block_n", _I64),
         ("pad_corr", _P), ("pad_row_class", _P), ("pad_col_class", _P),
         ("pad_col_classes", _I64), ("pad_classes", _I64),
+        ("gap_sum", _P), ("gap_cnt", _P), ("gap_out", _P), ("gap_out_stride", _I64),
+        ("gap_zp_in", _I64), ("gap_mult", _I64), ("gap_shift", _I64), ("gap_zp_out", _I64),
+        ("gap_qmin", _I64), ("gap_qmax", _I64),
     ]
 
 
@@ -271,6 +274,7 @@ class _ConvStep:
     layer: object
     desc: FusedConvDesc
     keep: list = field(default_factory=list)
+    gap: tuple = None  # (layer, x, y, area) of a GlobalAveragePool fused into the epilogue
 
 
 class UnsupportedGraph(NotImplementedError):
@@ -282,7 +286,7 @@ class ResidentNet:
 
     _max_block_n = 256  # widest column tile of the contraction kernel
 
-    def __init__(self, container, batch, device=None, fuse_input=True):
+    def __init__(self, container, batch, device=None, fuse_input=True, fuse_gap=True):
         if not container.calibrated:
             raise ValueError("container is not calibrated")
         self.c = container
@@ -298,6 +302,7 @@ class ResidentNet:
         self.bits, self.signed = container.layers[0].num_bits, container.layers[0].signed
         self._check_bits()
         self.fuse_input = fuse_input
+        self.fuse_gap = fuse_gap
         self._in_patch = 0  # > 0: the input quantizer writes patch rows (patch embedding)
         self._keep = []
         self.steps = []
@@ -743,7 +748,43 @@ class ResidentNet:
         if copy is not None:
             raise UnsupportedGraph("GlobalAveragePool feeding a Concat")
         self._views[node.outputs[0]] = view
-        self.steps.append(("gap", (layer, x, view, H * W)))
+        if not self._fuse_gap(layer, x, view, H * W):
+            self.steps.append(("gap", (layer, x, view, H * W)))
+
+    def _fuse_gap(self, layer, x, view, hw):
+        """GlobalAveragePool (quant_layers.py:563-590) folded into the epilogue
+        of the pointwise contraction that produces its input (the head conv
+        of YOLOv8n-cls): the epilogue sums each image's (v - zp_in) per
+        channel and the warp that completes an (image, column tile)
+        requantizes it, so the pooled tensor needs no separate launch and
+        the layer output is not read again.  8-bit graphs only; the
+        producer must be a pointwise conv with a 128 or 256 column tile
+        whose only reader is this pool, and an image must cover at least 32
+        pixels (a warp's rows then span at most two images)."""
+        if not self.fuse_gap or self._operand_bits() != 8:
+            return False
+        src = layer.node.inputs[0]
+        step = self._producer_step.get(src)
+        if step is None or src in self.graph.outputs or len(self._consumers.get(src, [])) != 1:
+            return False
+        d = step.desc
+        if (d.groups != 1 or d.KH != 1 or d.KW != 1 or d.SH != 1 or d.SW != 1 or d.PH or d.PW
+                or d.C % 16 or d.x_pix_stride % 16 or d.out2 or d.gap_sum
+                or d.block_n not in (128, 256) or hw < 32 or hw * 255 >= 2**31
+                or not d.out or d.out != x.ptr or not (-128 <= layer.in_zp <= 255)):
+            return False
+        m, s = layer.multiplier(hw)
+        n_tiles = -(-int(d.Cout) // int(d.block_n))
+        sums = torch.zeros((x.N, int(d.Cout)), dtype=torch.int32, device=self.device)
+        counts = torch.zeros((x.N, n_tiles), dtype=torch.int32, device=self.device)
+        self._keep += [sums, counts]
+        self._gap_scratch = getattr(self, "_gap_scratch", []) + [sums, counts]
+        d.gap_sum, d.gap_cnt = sums.data_ptr(), counts.data_ptr()
+        d.gap_out, d.gap_out_stride = view.ptr, view.pix_stride
+        d.gap_zp_in, d.gap_mult, d.gap_shift = int(layer.in_zp), int(m), int(s)
+        d.gap_zp_out, d.gap_qmin, d.gap_qmax = layer.out_zp, layer.out_qmin, layer.out_qmax
+        step.gap = (layer, x, view, hw)
+        return True
 
     def _plan_maxpool(self, layer):
         node = layer.node
@@ -862,6 +903,9 @@ class ResidentNet:
                          f"{cg * d.groups}->{d.Cout} @{d.OH}x{d.OW}")
                 if kind == "conv_input":
                     label = "quantize+" + label
+                if getattr(payload, "gap", None) is not None:
+                    label += "+gap"
+                    nbytes += d.N * d.Cout  # the pooled bytes
                 costs.append((label, nbytes, ops))
             elif kind == "gap":
                 layer, x, y, area = payload
@@ -1090,9 +1134,14 @@ class ResidentNet:
         return self.out_f32
 
     def check_status(self):
-        """Raises if any kernel reported a bounded-wait timeout."""
+        """Raises if any kernel reported a bounded-wait timeout.  A forward
+        that stopped early may leave the fused pooling's running sums
+        partly filled: they are zeroed again before the error is raised."""
         rc = self.lib.raw.qa_device_status_dev(
             ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream))
+        if rc != 0:
+            for t in getattr(self, "_gap_scratch", []):
+                t.zero_()
         _check(self.lib, rc, "device status")
 
     def run_async(self, x_pinned, out_pinned):

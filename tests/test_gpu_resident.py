@@ -203,3 +203,33 @@ def test_make_resident_picks_the_executor(gpu_lib, name, cls):
     q = _run(net, x)
     ref = np.load(GRAPHS / f"{name}.npz")["q"]
     assert np.abs(q.astype(np.int64) - ref).max() <= SOFTMAX_LSB
+
+
+@pytest.mark.parametrize("name,batch", [("yolov8n_cls_int8", 64), ("yolov8n_cls_int8", 33)])
+def test_gap_fused_into_head_conv_matches_separate_pool(gpu_lib, name, batch):
+    """GlobalAveragePool folded into the head conv's epilogue (per-image
+    channel sums, the completing warp requantizes) equals the separate
+    pooling kernel bit for bit, with one launch less, on every tensor;
+    repeated forwards (CUDA-graph replays) leave the sums clean."""
+    fused, qc, meta = _net(name, gpu_lib, batch)
+    plain, _, _ = _net(name, gpu_lib, batch, fuse_gap=False)
+    kinds_f = [k for k, _ in fused.steps]
+    kinds_p = [k for k, _ in plain.steps]
+    assert "gap" not in kinds_f and "gap" in kinds_p and len(kinds_f) == len(kinds_p) - 1
+    assert any(getattr(p, "gap", None) is not None for k, p in fused.steps if k == "conv")
+    for seed in (3, 4):
+        x = networks.images(batch, meta["image"], seed=seed)
+        qf = _run(fused, x)
+        qp = _run(plain, x)
+        np.testing.assert_array_equal(qf, qp)
+        for n in fused._views:
+            if n == qc.graph.inputs[0].name:
+                continue
+            np.testing.assert_array_equal(fused.tensor(n).cpu().numpy(),
+                                          plain.tensor(n).cpu().numpy(), err_msg=n)
+    fused.capture()
+    for _ in range(3):
+        fused.replay()
+    torch.cuda.synchronize()
+    fused.check_status()
+    np.testing.assert_array_equal(fused.out_q.cpu().numpy(), qp)
