@@ -386,6 +386,7 @@ __global__ void gap16_thread_kernel(const uint8_t* __restrict__ x, int64_t x_pix
   }
 }
 
+
 // -------------------------------------------------------------- Softmax --
 // The reference's float fallback (quant_layers.py:195-205, float_ops.py
 // :380-385): dequantize to float32, softmax in float64 with the row max
@@ -615,7 +616,23 @@ __device__ __forceinline__ void two_in_flight(const ByteView& a, const ByteView&
 // Used when the host proves every term within 2^29 and the zero point
 // within 2^30 (their sum is then exact in int32); 64 KB of shared memory
 // per block, persistent grid.
-constexpr int kAddRepThreads = 256;
+constexpr int kAddRepThreads = 512;
+
+// Four int32 values saturated to 8 bits (int8 or uint8) and packed
+// little-endian (cvt.pack.sat: sat(b) | sat(a) << 8 | c << 16).
+__device__ __forceinline__ uint32_t pack_sat4_bytes(int32_t a, int32_t b, int32_t c, int32_t d,
+                                                    bool is_signed) {
+  uint32_t hi, r;
+  const uint32_t zero = 0;
+  if (is_signed) {
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(d), "r"(c), "r"(zero));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  } else {
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(d), "r"(c), "r"(zero));
+    asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  }
+  return r;
+}
 
 __global__ void __launch_bounds__(kAddRepThreads) add_bytes16_rep_kernel(
     ByteView a, ByteView b, uint8_t* __restrict__ y, int64_t y_stride, int64_t rows,
@@ -642,6 +659,27 @@ __global__ void __launch_bounds__(kAddRepThreads) add_bytes16_rep_kernel(
   const int32_t* ta = add_rep + lane;
   const int32_t* tb = add_rep + 256 * 32 + lane;
   const int32_t zo32 = (int32_t)zo, lo32 = (int32_t)qmin, hi32 = (int32_t)qmax;
+  // a full 8-bit output range lets the saturating pack do the clamp
+  const bool sat_s8 = qmin == -128 && qmax == 127, sat_u8 = qmin == 0 && qmax == 255;
+  if (sat_s8 || sat_u8) {
+    auto one = [&](const uint4 va4, const uint4 vb4) {
+      const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        int32_t q[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t ea = (wa[k4] >> (8 * b)) & 0xFFu, eb = (wb[k4] >> (8 * b)) & 0xFFu;
+          q[b] = ta[ea * 32] + tb[eb * 32] + zo32;
+        }
+        o[k4] = pack_sat4_bytes(q[0], q[1], q[2], q[3], sat_s8);
+      }
+      return make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    two_in_flight(a, b, y, y_stride, rows * groups, groups, one);
+    return;
+  }
   auto one = [&](const uint4 va4, const uint4 vb4) {
     const uint32_t wa[4] = {va4.x, va4.y, va4.z, va4.w}, wb[4] = {vb4.x, vb4.y, vb4.z, vb4.w};
     uint32_t o[4] = {0, 0, 0, 0};
@@ -876,6 +914,88 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Column walker for stride-1 max pools with a KH x KW window known at compile
+// time: a thread owns one output column of one image and one 16-channel
+// group (lanes walk the groups of consecutive pixels, so a warp reads and
+// writes contiguous bytes), walks down a chunk of output rows, takes each
+// input row's maximum over the KW horizontal taps (neighbouring lanes' loads
+// hit L1) and keeps the last KH row maxima in registers: every input byte
+// comes from DRAM once, every output byte is written once.
+template <bool kSigned>
+__device__ __forceinline__ uint4 vmax16(uint4 a, uint4 b) {
+  if constexpr (kSigned)
+    return make_uint4(__vmaxs4(a.x, b.x), __vmaxs4(a.y, b.y), __vmaxs4(a.z, b.z),
+                      __vmaxs4(a.w, b.w));
+  else
+    return make_uint4(__vmaxu4(a.x, b.x), __vmaxu4(a.y, b.y), __vmaxu4(a.z, b.z),
+                      __vmaxu4(a.w, b.w));
+}
+
+template <int K, bool kSigned>
+__global__ void __launch_bounds__(256)
+    maxpool_s1_columns_kernel(const uint8_t* __restrict__ x, int64_t x_stride,
+                              uint8_t* __restrict__ y, int64_t y_stride, int H, int W, int groups,
+                              int PH, int PW, int OH, int OW, int rows_per, int chunks,
+                              int64_t total, uint32_t pad_word) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= total) return;
+  const int g = (int)(t % groups);
+  int64_t rest = t / groups;
+  const int ox = (int)(rest % OW);
+  rest /= OW;
+  const int chunk = (int)(rest % chunks);
+  const int64_t n = rest / chunks;
+  const int oy0 = chunk * rows_per;
+  const int oy1 = min(OH, oy0 + rows_per);
+  const uint4 pad = make_uint4(pad_word, pad_word, pad_word, pad_word);
+  // the K horizontal taps of this column: which lie inside the image (fixed
+  // for the thread) and the first one's address within a row
+  uint32_t inside = 0;
+#pragma unroll
+  for (int kx = 0; kx < K; ++kx) {
+    const int ix = ox - PW + kx;
+    inside |= (ix >= 0 && ix < W ? 1u : 0u) << kx;
+  }
+  const int64_t row_bytes = (int64_t)W * x_stride;
+  const uint8_t* const col = x + n * H * row_bytes + (int64_t)(ox - PW) * x_stride + g * 16;
+  const bool full = inside == (1u << K) - 1;
+  auto hmax = [&](int iy) {
+    if (iy < 0 || iy >= H) return pad;  // a padded row holds the pad value
+    const uint8_t* p = col + (int64_t)iy * row_bytes;
+    if (full) {
+      uint4 m = __ldg(reinterpret_cast<const uint4*>(p));
+#pragma unroll
+      for (int kx = 1; kx < K; ++kx)
+        m = vmax16<kSigned>(m, __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride)));
+      return m;
+    }
+    uint4 m = pad;  // some taps fall in the padding
+#pragma unroll
+    for (int kx = 0; kx < K; ++kx)
+      if (inside & (1u << kx))
+        m = vmax16<kSigned>(m, __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride)));
+    return m;
+  };
+  // win[k] = row maximum of input row (oy - PH + k) for the next output row
+  uint4 win[K];
+#pragma unroll
+  for (int k = 0; k < K - 1; ++k) win[k + 1] = hmax(oy0 - PH + k);
+  uint8_t* out = y + ((n * OH + oy0) * OW + ox) * y_stride + g * 16;
+  const int64_t out_row = (int64_t)OW * y_stride;
+  for (int oy = oy0; oy < oy1; ++oy) {
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+    win[K - 1] = hmax(oy - PH + K - 1);
+    uint4 m = win[0];
+#pragma unroll
+    for (int k = 1; k < K; ++k) m = vmax16<kSigned>(m, win[k]);
+    *reinterpret_cast<uint4*>(out) = m;
+    out += out_row;
+  }
+}
+
 __host__ __device__ inline bool vec16_ok(const void* p, int64_t stride) {
   return ((reinterpret_cast<uintptr_t>(p) | (uint64_t)stride) & 15) == 0;
 }
@@ -1041,7 +1161,11 @@ QA_API int qa_gap_dev(const void* x, int64_t x_pix_stride, int64_t x_signed, int
                              std::fabs((double)mult) + std::ldexp(1.0, (int)std::min<int64_t>(ts, 62));
     const int fast = ts >= 1 && ts <= 62 && bound < std::ldexp(1.0, 62) ? 1 : 0;
     const int64_t total = N * (C / 16);
-    return launch_ex(gap16_thread_kernel, dim3(grid_for(total, 128)), dim3(128), 0,
+    // one (image, group) per thread in a single pass: a capped grid would
+    // leave a partly filled second round
+    const int64_t gblocks = std::max<int64_t>(1, (total + 127) / 128);
+    return launch_ex(gap16_thread_kernel,
+                     dim3((unsigned)std::min<int64_t>(gblocks, 0x7FFFFFFF)), dim3(128), 0,
                      (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_pix_stride,
                      (int)x_signed, N, (int)HW, C / 16, zp_in, mult, shift, zp_out, qmin, qmax,
                      fast, static_cast<uint8_t*>(y), y_pix_stride)
@@ -1209,8 +1333,29 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
   clear_error();
   const int64_t total = N * OH * OW * C;
   if (total == 0) return 0;
-  if (C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride) && SH == 1 && SW == 1 &&
-      DH == 1 && DW == 1 && KH <= kMpMaxK && KW <= kMpMaxK && KH >= 1 && KW >= 1) {
+  const bool s1_vec = C % 16 == 0 && vec16_ok(x, x_stride) && vec16_ok(y, y_stride) &&
+                      SH == 1 && SW == 1 && DH == 1 && DW == 1;
+  if (s1_vec && KH == KW && (KH == 3 || KH == 5) && OH == H + 2 * PH - KH + 1 &&
+      OW == W + 2 * PW - KW + 1 && H * W * x_stride < (int64_t(1) << 31) && OW < (1 << 20)) {
+    // column walker: output rows in chunks of at most 16, enough threads to
+    // fill the GPU
+    const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
+    const int rows_per = (int)std::min<int64_t>(OH, 16);
+    const int chunks = (int)((OH + rows_per - 1) / rows_per);
+    const int64_t threads = N * chunks * OW * (C / 16);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    auto kern = KH == 3 ? (x_signed ? maxpool_s1_columns_kernel<3, true>
+                                    : maxpool_s1_columns_kernel<3, false>)
+                        : (x_signed ? maxpool_s1_columns_kernel<5, true>
+                                    : maxpool_s1_columns_kernel<5, false>);
+    return launch_ex(kern, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, true,
+                     static_cast<const uint8_t*>(x), x_stride, static_cast<uint8_t*>(y), y_stride,
+                     (int)H, (int)W, (int)(C / 16), (int)PH, (int)PW, (int)OH, (int)OW, rows_per,
+                     chunks, threads, pw)
+               ? 0
+               : last_status();
+  }
+  if (s1_vec && KH <= kMpMaxK && KW <= kMpMaxK && KH >= 1 && KW >= 1) {
     const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
     const int64_t tiles_x = (OW + kMpTW - 1) / kMpTW, tiles_y = (OH + kMpTH - 1) / kMpTH;
     const int64_t blocks = tiles_x * tiles_y * N * (C / 16);

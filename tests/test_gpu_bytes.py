@@ -88,23 +88,33 @@ def test_byte_layers(gpu_lib, oracle, raw, C, stride, signed):
         np.testing.assert_array_equal(got(), oracle.mul(a32, b32, 3, -1, mm, ss, 2, qmin, qmax))
 
 
+# (H, W, k, pad): the SPPF window, a 3x3 window, output columns taller than
+# one row chunk, a 1x1 image, no padding, and a pad the column walker does
+# not take (k5 p1)
+POOL_GEOMETRIES = [(9, 11, 5, 2), (9, 11, 3, 1), (40, 3, 5, 2), (1, 1, 3, 1), (7, 8, 5, 0),
+                   (9, 11, 5, 1)]
+
+
 @pytest.mark.parametrize("C,stride,signed", CASES)
-def test_maxpool_bytes(gpu_lib, raw, C, stride, signed):
-    rng = np.random.default_rng(C + stride)
-    N, H, W, k, st, pad = 2, 9, 11, 5, 1, 2
+@pytest.mark.parametrize("H,W,k,pad", POOL_GEOMETRIES)
+def test_maxpool_bytes(gpu_lib, raw, C, stride, signed, H, W, k, pad):
+    rng = np.random.default_rng(C + stride + 7 * H + W + k)
+    N, st = 2, 1
     qmin = -128 if signed else 0
     x = _vals(rng, (N * H * W, C), signed)
     dx = _dev(x, stride, signed)
-    OH, OW = H, W
+    OH, OW = H + 2 * pad - k + 1, W + 2 * pad - k + 1
     dy = torch.zeros(N * OH * OW * stride, dtype=torch.uint8, device="cuda")
-    _ok(gpu_lib, raw.qa_maxpool_bytes_dev(dx.data_ptr(), stride, signed, dy.data_ptr(), stride,
-                                          N, H, W, C, k, k, st, st, pad, pad, 1, 1, OH, OW, qmin,
-                                          None))
-    xp = np.full((N, H + 2 * pad, W + 2 * pad, C), qmin, np.int64)
-    xp[:, pad:pad + H, pad:pad + W] = x.reshape(N, H, W, C)
-    want = np.full((N, OH, OW, C), np.iinfo(np.int64).min)
-    for ky in range(k):
-        for kx in range(k):
-            want = np.maximum(want, xp[:, ky:ky + OH, kx:kx + OW])
-    np.testing.assert_array_equal(_host(dy, N * OH * OW, C, stride, signed),
-                                  want.reshape(-1, C))
+    # qmin (the reference's MaxPool padding) and a pad value above some inputs
+    for pad_value in (qmin, qmin + 100):
+        _ok(gpu_lib, raw.qa_maxpool_bytes_dev(dx.data_ptr(), stride, signed, dy.data_ptr(),
+                                              stride, N, H, W, C, k, k, st, st, pad, pad, 1, 1,
+                                              OH, OW, pad_value, None))
+        xp = np.full((N, H + 2 * pad, W + 2 * pad, C), pad_value, np.int64)
+        xp[:, pad:pad + H, pad:pad + W] = x.reshape(N, H, W, C)
+        want = np.full((N, OH, OW, C), np.iinfo(np.int64).min)
+        for ky in range(k):
+            for kx in range(k):
+                want = np.maximum(want, xp[:, ky:ky + OH, kx:kx + OW])
+        np.testing.assert_array_equal(_host(dy, N * OH * OW, C, stride, signed),
+                                      want.reshape(-1, C))
