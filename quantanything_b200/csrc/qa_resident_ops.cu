@@ -190,16 +190,17 @@ __global__ void quantize_to_nhwc_kernel(const float* __restrict__ x, uint8_t* __
 // (P > 0): the P x P pixels of patch (py, px) of image n form row
 // (n * H / P + py) * W / P + px of P * P * 4 bytes, pixel (ky, kx) at
 // (ky * P + kx) * 4 -- the im2col rows of a P x P, stride-P convolution.
-__global__ void quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
-                                         int C, int quads_per_image, int quads, int W, int P,
-                                         const QuantK k) {
+__global__ void __launch_bounds__(256, 4)
+    quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y, int C,
+                             int quads_per_image, int quads, int W, int P, const QuantK k) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const uint32_t pad = (uint32_t)(int32_t)k.zpd & 0xFFu;
   const QuantK kk = k;  // the fast path's constants in registers
   // each warp takes 32 * kQ consecutive quads; lane l the quads l, l + 32,
-  // ..., all of their 16-byte loads in flight before any is used
-  constexpr int kQ = 2;
+  // ..., all of their 16-byte loads in flight before any is used (one quad
+  // per lane keeps the registers low enough for four blocks per SM)
+  constexpr int kQ = 1;
   const int lane = threadIdx.x & 31;
   const int warp0 = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -334,8 +335,10 @@ __global__ void gap16ch_kernel(const uint8_t* __restrict__ x, int64_t x_pix_stri
 // summed in 16-bit lanes (even and odd bytes of each word separately; a
 // signed byte is biased by 128 first, so each lane sums at most 256 * 255),
 // and the 64-bit rescale replaces the 128-bit one whenever the host proved
-// it exact (`fast`).
-__global__ void gap16_thread_kernel(const uint8_t* __restrict__ x, int64_t x_pix_stride,
+// it exact (`fast`).  Four loads in flight per thread and at most 40
+// registers let twelve 128-thread blocks share an SM: DRAM latency is
+// covered by resident warps rather than by a long unroll.
+__global__ void __launch_bounds__(128, 12) gap16_thread_kernel(const uint8_t* __restrict__ x, int64_t x_pix_stride,
                                     int x_signed, int64_t N, int HW, int64_t groups,
                                     int64_t zp_in, int64_t m, int64_t s, int64_t zp_out,
                                     int64_t qmin, int64_t qmax, int fast, uint8_t* __restrict__ y,
@@ -350,7 +353,7 @@ __global__ void gap16_thread_kernel(const uint8_t* __restrict__ x, int64_t x_pix
     const int64_t n = i / groups, g = i - n * groups;
     const uint8_t* base = x + n * HW * x_pix_stride + g * 16;
     uint32_t even[4] = {0, 0, 0, 0}, odd[4] = {0, 0, 0, 0};
-#pragma unroll 8
+#pragma unroll 4
     for (int p = 0; p < HW; ++p) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)p * x_pix_stride));
       const uint32_t w[4] = {v.x ^ flip, v.y ^ flip, v.z ^ flip, v.w ^ flip};
@@ -1113,7 +1116,7 @@ QA_API int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C
   if (pix_stride == 4 && C <= 4 && HW % 4 == 0 && HW * N / 4 < 0x7FFFFFFF &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const int64_t quads = N * HW / 4;
-    return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256, 2)), dim3(256), 0,
+    return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
                      (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
                      (int)(HW / 4), (int)quads, (int)W, 0, make_quant_k(scale, zp, qmin, qmax))
                ? 0
@@ -1138,7 +1141,7 @@ QA_API int qa_quantize_to_patch_rows_dev(const float* x, void* y, int64_t N, int
   }
   const int64_t quads = N * H * W / 4;
   if (quads == 0) return 0;
-  return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256, 2)), dim3(256), 0,
+  return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
                    (int)(H * W / 4), (int)quads, (int)W, (int)P,
                    make_quant_k(scale, zp, qmin, qmax))
