@@ -14,7 +14,7 @@ the device with one NCCL all-reduce first.
 The float arithmetic follows ``float_ops`` (float32 tensors; float64 where
 the reference widens: Sigmoid, Exp, Softplus, Erf / Gelu, Pow, Softmax,
 LayerNormalization).  Sums run in another order than NumPy's, so ranges can
-differ at the last float32 bit -- the resulting qparams are judged against
+differ at the last float32 bit -- the resulting qparams are compared with
 the reference's q.json with the same tolerance as the host calibration.
 
 Operators: Conv, Gemm, MatMul, BatchNormalization, the element-wise unary
