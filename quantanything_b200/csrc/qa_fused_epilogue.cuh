@@ -115,10 +115,21 @@ __device__ __forceinline__ bool aligned16(const uint8_t* p, int64_t plane) {
 
 // s_lut: the activation table in shared memory (int16 entries), or null to
 // read e.lut from global memory.
+// One output channel's requantize parameters staged in shared memory by a
+// kernel whose CTA keeps one column tile: bias, multiplier, total shift
+// (31 + shift) and whether the high-word form applies.
+struct ChanParams16 {
+  int64_t bias;
+  int64_t mult;
+  int32_t ts;
+  int32_t hi;
+};
+
 __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& e,
                                                            const int64_t (&acc)[16], int64_t m,
                                                            int n0, int cnt,
-                                                           const int16_t* s_lut = nullptr) {
+                                                           const int16_t* s_lut = nullptr,
+                                                           const ChanParams16* s_par = nullptr) {
   // Phased so that the independent loads of the sixteen channels are in
   // flight together: channel parameters, then requantize, then the sixteen
   // table lookups, then the residual terms and the stores.  Columns past
@@ -128,17 +139,28 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
   uint8_t* op2 = e.out2 ? e.out2 + m * e.out2_pix_stride + n0 : nullptr;
   const bool full = cnt == 16;
   int64_t q[16];
+  if (s_par) {
+    // s_par[j]: channel n0 + j (columns past cnt hold channel n0's values)
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int n = n0 + (j < cnt ? j : 0);
-    const int64_t b = e.bias ? __ldg(e.bias + n) : 0;
-    const int64_t mv = __ldg(e.mult + n), sv = __ldg(e.shift + n);
-    // int16 accumulators pass 2^40: the high-word form when it applies (the
-    // usual positive M0 in [2^30, 2^31); e.fast: the host proved it for every
-    // channel of the layer), else the 128-bit mbqm
-    q[j] = (e.fast || hi32_applies(mv, 31 + sv))
-               ? requant_hi32(acc[j] + b, mv, (int)(31 + sv), e.zp, e.qmin, e.qmax)
-               : requant_exact_cold(acc[j] + b, mv, sv, e.zp, e.qmin, e.qmax);
+    for (int j = 0; j < 16; ++j) {
+      const ChanParams16 c = s_par[j < cnt ? j : 0];
+      q[j] = c.hi ? requant_hi32(acc[j] + c.bias, c.mult, c.ts, e.zp, e.qmin, e.qmax)
+                  : requant_exact_cold(acc[j] + c.bias, c.mult, (int64_t)c.ts - 31, e.zp,
+                                       e.qmin, e.qmax);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = n0 + (j < cnt ? j : 0);
+      const int64_t b = e.bias ? __ldg(e.bias + n) : 0;
+      const int64_t mv = __ldg(e.mult + n), sv = __ldg(e.shift + n);
+      // int16 accumulators pass 2^40: the high-word form when it applies (the
+      // usual positive M0 in [2^30, 2^31); e.fast: the host proved it for
+      // every channel of the layer), else the 128-bit mbqm
+      q[j] = (e.fast || hi32_applies(mv, 31 + sv))
+                 ? requant_hi32(acc[j] + b, mv, (int)(31 + sv), e.zp, e.qmin, e.qmax)
+                 : requant_exact_cold(acc[j] + b, mv, sv, e.zp, e.qmin, e.qmax);
+    }
   }
   if (e.lut) {
     int32_t t[16];

@@ -54,6 +54,9 @@ struct ConvTileParams {
   int64_t y_ctot;           // NCHW: channels of y; row mode: leading dimension
   int64_t ohw;
   int32_t* status;          // device error word
+  int32_t stage_params;     // persistent 16-bit kernel: every CTA keeps one column
+                            // tile (grid a multiple of the column tiles), so its
+                            // channel parameters are staged in shared memory once
   FusedEpilogue epi;
 };
 
@@ -730,7 +733,8 @@ struct P16Layout {
   static constexpr int kBPlane = BN * kBKBytes;
   static constexpr int kStage = 2 * kAPlane + kWP * kBPlane;
   static constexpr int kLutBytes = kSmemLut ? kP16LutEntries * 2 : 0;
-  static constexpr int kFit = (232448 - 1024 - 256 - kLutBytes) / kStage;
+  static constexpr int kParamBytes = BN * (int)sizeof(ChanParams16);  // one column tile
+  static constexpr int kFit = (232448 - 1024 - 256 - kLutBytes - kParamBytes) / kStage;
   static constexpr int kStages =
       kWP == 2 ? (kSmemLut ? 2 : (BN >= 128 ? 3 : 4)) : (kFit < 4 ? kFit : 4);
   static constexpr int kCols = kSets * kSetCols;
@@ -739,7 +743,7 @@ struct P16Layout {
   static_assert(kCols <= 512, "accumulator sets must fit TMEM");
   static_assert(kStages >= 2, "at least two stages must fit shared memory");
   static_assert(!(kSmemLut && BN >= 128), "the shared-memory table leaves one stage at BN 128");
-  static constexpr size_t kBarOff = (size_t)kStages * kStage + kLutBytes;
+  static constexpr size_t kBarOff = (size_t)kStages * kStage + kLutBytes + kParamBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + (2 * kStages + 4) * 8 + 16;
   static_assert(kSmem <= 232448, "shared memory per CTA");
 };
@@ -762,6 +766,8 @@ __global__ void __launch_bounds__(kP16Threads, 1)
   auto acce_bar = [&](int b) { return bar_base + 8u * (2 * S + 2 + b); };
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::kBarOff + (2 * S + 4) * 8);
   int16_t* s_lut = reinterpret_cast<int16_t*>(smem + (size_t)S * L::kStage);
+  ChanParams16* s_par =
+      reinterpret_cast<ChanParams16*>(smem + (size_t)S * L::kStage + L::kLutBytes);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   auto a_tile = [&](int s, int pl) { return base + s * L::kStage + pl * L::kAPlane; };
   auto b_tile = [&](int s, int pl) {
@@ -793,6 +799,20 @@ __global__ void __launch_bounds__(kP16Threads, 1)
     const uint4* src = reinterpret_cast<const uint4*>(p.epi.lut16);
     uint4* dst = reinterpret_cast<uint4*>(s_lut);
     for (int64_t i = tid; i < n16; i += kP16Threads) dst[i] = __ldg(src + i);
+  }
+  if (p.stage_params) {
+    // this CTA's column tile (the host made the grid a multiple of n_tiles)
+    const int nb0 = (int)(blockIdx.x % n_tiles) * BN;
+    for (int c = tid; c < BN; c += kP16Threads) {
+      const int n = nb0 + c < p.n_valid ? nb0 + c : nb0;
+      const int64_t mv = p.epi.mult[n], sv = p.epi.shift[n];
+      ChanParams16 cp;
+      cp.bias = p.epi.bias ? p.epi.bias[n] : 0;
+      cp.mult = mv;
+      cp.ts = (int32_t)(31 + sv);
+      cp.hi = (p.epi.fast || hi32_applies(mv, 31 + sv)) ? 1 : 0;
+      s_par[c] = cp;
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -999,7 +1019,8 @@ __global__ void __launch_bounds__(kP16Threads, 1)
                    (int64_t)(int32_t)v[2][j] * 65536;
           if constexpr (kWP == 3) acc[j] += (int64_t)(int32_t)v[3][j] * 16777216;
         }
-        fused_epilogue_store16_run(p.epi, acc, m, nb, cnt, kSmemLut ? s_lut : nullptr);
+        fused_epilogue_store16_run(p.epi, acc, m, nb, cnt, kSmemLut ? s_lut : nullptr,
+                                   p.stage_params ? s_par + c0 : nullptr);
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(acce_bar(b));
@@ -1031,8 +1052,16 @@ bool launch_umma16_persistent(const ConvTileParams& prm, const CUtensorMap& tmap
   }
   const int64_t m_tiles = (prm.M + kBM - 1) / kBM;
   const int64_t total = m_tiles * n_tiles;
-  const int64_t grid = total < sm_count() ? total : sm_count();
-  kern<<<(unsigned)grid, kP16Threads, smem, st>>>(prm, tmap, n_tiles, total);
+  int64_t grid = total < sm_count() ? total : sm_count();
+  // a grid that is a multiple of the column tiles keeps every CTA on one
+  // column tile: its channel parameters are then staged once
+  ConvTileParams prm2 = prm;
+  const int64_t even = grid / n_tiles * n_tiles;
+  if (even >= 1) {
+    grid = even;
+    prm2.stage_params = 1;
+  }
+  kern<<<(unsigned)grid, kP16Threads, smem, st>>>(prm2, tmap, n_tiles, total);
   return !cuda_failed(cudaGetLastError(), "umma16_persistent_kernel launch");
 }
 
