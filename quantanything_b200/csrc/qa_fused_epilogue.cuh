@@ -129,7 +129,8 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
                                                            const int64_t (&acc)[16], int64_t m,
                                                            int n0, int cnt,
                                                            const int16_t* s_lut = nullptr,
-                                                           const ChanParams16* s_par = nullptr) {
+                                                           const ChanParams16* s_par = nullptr,
+                                                           bool par_all_hi = false) {
   // Phased so that the independent loads of the sixteen channels are in
   // flight together: channel parameters, then requantize, then the sixteen
   // table lookups, then the residual terms and the stores.  Columns past
@@ -139,7 +140,14 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
   uint8_t* op2 = e.out2 ? e.out2 + m * e.out2_pix_stride + n0 : nullptr;
   const bool full = cnt == 16;
   int64_t q[16];
-  if (s_par) {
+  if (s_par && par_all_hi) {
+    // every staged channel takes the high-word form
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const ChanParams16 c = s_par[j < cnt ? j : 0];
+      q[j] = requant_hi32(acc[j] + c.bias, c.mult, c.ts, e.zp, e.qmin, e.qmax);
+    }
+  } else if (s_par) {
     // s_par[j]: channel n0 + j (columns past cnt hold channel n0's values)
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -164,10 +172,11 @@ __device__ __forceinline__ void fused_epilogue_store16_run(const FusedEpilogue& 
   }
   if (e.lut) {
     int32_t t[16];
+    // q lies in [qmin, qmax] (16-bit): the table index fits 32 bits
+    const int32_t off = (int32_t)e.lut_offset, last = (int32_t)e.lut_len - 1;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      int64_t idx = q[j] - e.lut_offset;
-      idx = idx < 0 ? 0 : (idx >= e.lut_len ? e.lut_len - 1 : idx);
+      const int32_t idx = min(max((int32_t)q[j] - off, 0), last);
       t[j] = s_lut ? (int32_t)s_lut[idx] : __ldg(e.lut + idx);
     }
 #pragma unroll

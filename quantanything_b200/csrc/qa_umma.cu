@@ -800,6 +800,7 @@ __global__ void __launch_bounds__(kP16Threads, 1)
     uint4* dst = reinterpret_cast<uint4*>(s_lut);
     for (int64_t i = tid; i < n16; i += kP16Threads) dst[i] = __ldg(src + i);
   }
+  int par_hi = 1;
   if (p.stage_params) {
     // this CTA's column tile (the host made the grid a multiple of n_tiles)
     const int nb0 = (int)(blockIdx.x % n_tiles) * BN;
@@ -811,11 +812,12 @@ __global__ void __launch_bounds__(kP16Threads, 1)
       cp.mult = mv;
       cp.ts = (int32_t)(31 + sv);
       cp.hi = (p.epi.fast || hi32_applies(mv, 31 + sv)) ? 1 : 0;
+      par_hi &= cp.hi;
       s_par[c] = cp;
     }
   }
   ptx::tc_fence_before();
-  __syncthreads();
+  const bool par_all_hi = __syncthreads_and(par_hi) != 0;
   ptx::tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
@@ -1020,7 +1022,7 @@ __global__ void __launch_bounds__(kP16Threads, 1)
           if constexpr (kWP == 3) acc[j] += (int64_t)(int32_t)v[3][j] * 16777216;
         }
         fused_epilogue_store16_run(p.epi, acc, m, nb, cnt, kSmemLut ? s_lut : nullptr,
-                                   p.stage_params ? s_par + c0 : nullptr);
+                                   p.stage_params ? s_par + c0 : nullptr, par_all_hi);
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(acce_bar(b));
