@@ -31,7 +31,8 @@ from quantanything_b200.layers import (ActivationQuantize, AddQuantize, BaseQuan
                                        ConcatQuantize, ConvQuantize, GemmQuantize, MulQuantize,
                                        ShapingQuantize)
 from quantanything_b200.resident import ResidentNet, UnsupportedGraph, View, _round_up
-from quantanything_b200.resident16 import ResidentNet16, device_api16
+from quantanything_b200.resident16 import (UINT16_SHIFT, ResidentNet16, device_api16,
+                                          shifted_container)
 
 _I32_MIN, _I32_MAX = -(1 << 31), (1 << 31) - 1
 _TAB = np.arange(-128, 256, dtype=np.int64)  # byte-domain table index v + 128
@@ -457,17 +458,25 @@ class ResidentViT16(ResidentViT, ResidentNet16):
     kernel with its exact int64 combine; the token embedding, the
     class-token Gather, LayerNorm, the attention core and the output
     dequantize run on the 16-bit plane kernels (qa_*16_dev), with the same
-    float-fallback arithmetic as the 8-bit route."""
+    float-fallback arithmetic as the 8-bit route.  uint16 graphs run here too,
+    their activations held 32768 lower (``resident16.shifted_container``)
+    and their 17-bit centred weights in three byte planes."""
 
     _domain = np.arange(-32768, 32768, dtype=np.int64)
 
     def __init__(self, container, batch, device=None):
         self._planes = []
         self._lut16 = {}
-        self._act_shift, self._w_planes, self._orig = 0, 2, container
+        # uint16: activations held 32768 lower in the signed planes (every
+        # activation zero point, range, table and quantized constant moved
+        # with them) and the 17-bit centred weights in three byte planes, as
+        # in ResidentNet16
         layer0 = container.layers[0]
-        if layer0.num_bits == 16 and not layer0.signed:
-            raise UnsupportedGraph("uint16 transformer graphs run on the per-layer ABI route")
+        self._orig = container
+        self._act_shift = UINT16_SHIFT if (layer0.num_bits == 16 and not layer0.signed) else 0
+        self._w_planes = 3 if self._act_shift else 2
+        if self._act_shift:
+            container = shifted_container(container, self._act_shift)
         ResidentNet.__init__(self, container, batch, device, fuse_input=False)
         device_api16(self.lib)
         vit16_api(self.lib)

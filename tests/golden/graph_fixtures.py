@@ -33,6 +33,7 @@ NETWORKS = {
     # the batch is static in a ViT graph: calibration and evaluation use it
     "vit_mini_int8": ("vit", {"batch": 4}, "int8", 2, 4, 4),
     "vit_mini_int16": ("vit", {"batch": 4}, "int16", 2, 4, 4),
+    "vit_mini_uint16": ("vit", {"batch": 4}, "uint16", 2, 4, 4),
     # stand-alone activation x activation MatMuls (no head split, no Softmax)
     "vit_gram_mini_int8": ("vit", {"batch": 4, "attention": "gram"}, "int8", 2, 4, 4),
     # ViT-B/16 (cfg3's model) at batch 2: the full-size parity case

@@ -41,6 +41,8 @@ def write_tensor(net, name, value):
     v = net._views[name]
     rows = v.N * v.H * v.W
     src = np.asarray(value).reshape(v.N, v.C, v.H, v.W).transpose(0, 2, 3, 1).reshape(rows, v.C)
+    # uint16 executors hold activations 32768 lower (net.tensor adds it back)
+    src = src.astype(np.int64) - getattr(net, "_act_shift", 0)
     planes = [(0, 0)] if not v.plane else [(0, 0), (v.plane, 8)]  # (offset, bit shift)
     for off, shift in planes:
         dst = torch.as_strided(v.buf, (rows, v.C), (v.pix_stride, 1), v.offset + off)

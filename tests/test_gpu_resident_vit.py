@@ -131,6 +131,39 @@ def test_vit_mini_int16_resident_against_the_reference(gpu_lib, oracle):
     assert np.abs(q - ref).max() <= INT16_E2E_LSB
 
 
+def test_vit_mini_uint16_resident_against_the_reference(gpu_lib, oracle):
+    """uint16 ViT on ResidentViT16: activations held 32768 lower in the
+    signed planes (every activation zero point, range and table shifted with
+    them), 17-bit centred weights in three byte planes.  Teacher-forced
+    steps as for int16: integer steps bit-exact, the float fallbacks within
+    one output step; end to end the logits stay within INT16_E2E_LSB of the
+    reference's and keep its class on every image."""
+    from quantanything_b200.resident import make_resident
+    from quantanything_b200.resident_vit import ResidentViT16
+    from tests.resident_steps import mirror_env, teacher_forced
+
+    qc, meta = _load("vit_mini_uint16", gpu_lib)
+    net = make_resident(qc, meta["eval_batch"])
+    assert isinstance(net, ResidentViT16) and net._w_planes == 3 and net._act_shift == 32768
+    x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
+    g = qc.graph
+    env = mirror_env(QuantContainer.load(g, GRAPHS / "vit_mini_uint16.qjson", lib=oracle), x)
+    seen = set()
+    for i, kind, tname, diff in teacher_forced(net, env, x, g.inputs[0].name):
+        seen.add(kind)
+        tol = FALLBACK_LSB if kind in ("attention", "layernorm") else 0
+        assert diff.max() <= tol, (i, kind, tname, int(diff.max()))
+    assert {"conv", "vit_embed", "layernorm", "attention", "gather"} <= seen
+    net.forward_device(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    net.check_status()
+    ref = np.load(GRAPHS / "vit_mini_uint16.npz")["q"].astype(np.int64)
+    q = net.output_int().cpu().numpy().astype(np.int64)
+    assert q.min() >= 0
+    np.testing.assert_array_equal(q.argmax(1), ref.argmax(1))
+    assert np.abs(q - ref).max() <= INT16_E2E_LSB
+
+
 def test_vit_gram_act_x_act_matmuls_against_the_reference(gpu_lib, oracle):
     """Stand-alone activation x activation MatMuls (the reference's float
     fallback, float_ops.py MatMul, quant_layers.py:195-205) on the resident

@@ -38,7 +38,7 @@ def test_prepared_parameters_match_reference(oracle, name):
 @pytest.mark.parametrize("name", ["yolo_mini_int8", "yolo_mini_uint8", "yolo_mini_int16",
                                   "yolov8n_cls_int8", "sppf_mini_int8", "sppf_mini_uint8",
                                   "vit_mini_int8", "vit_mini_int16", "yolo_mini_uint16",
-                                  "sppf_mini_uint16", "shaping_mini_uint16"])
+                                  "sppf_mini_uint16", "shaping_mini_uint16", "vit_mini_uint16"])
 def test_integer_outputs_match_reference(oracle, name):
     qc, meta = load(name, oracle)
     x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])

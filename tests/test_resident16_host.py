@@ -92,7 +92,8 @@ def test_quantize_to_planes16_rejects_out_of_range_bounds(lib):
     assert rc != 0 and "qa_quantize_to_planes16_dev" in msg
 
 
-@pytest.mark.parametrize("name", ["yolo_mini_uint16", "sppf_mini_uint16", "shaping_mini_uint16"])
+@pytest.mark.parametrize("name", ["yolo_mini_uint16", "sppf_mini_uint16", "shaping_mini_uint16",
+                                  "vit_mini_uint16"])
 def test_uint16_shift_is_exact_through_the_integer_pass(oracle, name):
     """The uint16 resident route stores activations 32768 lower.  The
     shifted container (every activation zp / qmin / qmax / table moved by
@@ -111,7 +112,7 @@ def test_uint16_shift_is_exact_through_the_integer_pass(oracle, name):
     qc = QuantContainer.load(g, graphs / f"{name}.qjson", lib=oracle)
     x = networks.images(meta["eval_batch"], meta["image"], seed=meta["eval_seed"])
     ref = np.load(graphs / f"{name}.npz")
-    sc = shifted_container(qc)
+    sc = shifted_container(qc)  # the ViT's float fallbacks see (q - zp) only, too
     q = np.asarray(sc.run_integer_raw(x), np.int64)
     assert q.min() >= -UINT16_SHIFT and q.max() < UINT16_SHIFT
     np.testing.assert_array_equal(q + UINT16_SHIFT, ref["q"])
