@@ -23,10 +23,11 @@ __device__ __forceinline__ uint32_t quantize_byte(float xv, double scale, double
 }
 
 struct QuantK {
-  float inv, inv_lo;  // fl32(1 / scale) and fl32(1 / scale - inv)
+  float inv;  // fl32(1 / scale)
   float zp, qmin, qmax;
   float lo, hi;      // qmin - zp, qmax - zp
   float magic_zp;    // 1.5 * 2^23 + zp
+  float t_lo, t_hi;  // 1.5 * 2^23 + qmin, 1.5 * 2^23 + qmax
   int32_t zp_i, qmin_i, qmax_i;
   double scale, zpd, qmind, qmaxd;
 };
@@ -50,55 +51,45 @@ __device__ __forceinline__ uint32_t quantize_bits_try(float xv, const QuantK& k,
   return __float_as_uint(t);
 }
 
-// NaN-propagating float min / max (a NaN operand yields NaN).
-__device__ __forceinline__ float fmax_nan(float a, float b) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ float fmin_nan(float a, float b) {
-  float r;
-  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
-// quantize_bits_try with the quotient carried to about 46 bits: the product
-// with the two-float reciprocal, x * inv + x * inv_lo, is formed as p + pl
-// (pl collects x * inv_lo and the exact rounding error of p = fl32(x * inv),
-// one FMA each), within 2^-34 of the exact quotient q = x / scale for |q| <
-// 2^11.  p is clamped to [lo - 2, hi + 2] (NaN-propagating), rounded in the
-// float adder to r, and d = (p - r) + pl estimates q - r (p - r alone when
-// p was clamped, which keeps infinities and far values off the slow path); unless d lies
-// within 2^-20 of +-1/2, r is the nearest integer to q and to the double
-// quotient fl64(q) alike (their distance is below 2^-34 + 2^-42), so
-// clamp(r, lo, hi) + zp is the reference's value; for an unclamped p the
-// difference p - r is exact.  `ok` is cleared in that band (about 2^-19 of
-// uniform fractions, against 2^-10 for the one-float product), for NaN and
-// when the host could not invert the scale; the caller then uses
-// quantize_byte.  The byte is the low byte of the returned word.
-__device__ __forceinline__ uint32_t quantize_bits_split(float xv, const QuantK& k, bool& ok) {
-  const float p = __fmul_rn(xv, k.inv);
-  const float e = __fmaf_rn(xv, k.inv, -p);       // exact: p + e == x * inv
-  const float pl = __fmaf_rn(xv, k.inv_lo, e);
-  const float pc = fmin_nan(fmax_nan(p, k.lo - 2.0f), k.hi + 2.0f);
-  const float r = __fsub_rn(__fadd_rn(pc, 12582912.0f), 12582912.0f);  // rint(pc)
-  // (a clamped product lands on an integer: its low part plays no role)
-  const float d = __fadd_rn(__fsub_rn(pc, r), pc == p ? pl : 0.0f);
-  ok = ok & (fabsf(d) < 0.49999904632568359375f);  // 1/2 - 2^-20; false for NaN
-  const float rc = fminf(fmaxf(r, k.lo), k.hi);
-  return __float_as_uint(__fadd_rn(rc, k.magic_zp));
+// The quantized byte in six instructions: the product x * inv is rounded to
+// an integer inside one FMA, t = fl(x * inv + (1.5 * 2^23 + zp)) =
+// 1.5 * 2^23 + zp + rint(x * inv) while |x * inv + zp| < 2^22, and clamped
+// as a float to [1.5 * 2^23 + qmin, 1.5 * 2^23 + qmax]; the low byte of the
+// clamped word is the byte.  The tie test takes the rounding's residual from
+// a second FMA: r = t - (1.5 * 2^23 + zp) is exact, d = fl(x * inv - r) is
+// the exact residual rounded once (|d| <= 1/2).
+// Error bound: inv = fl32(1 / scale) carries a relative error below
+// 2^-24 + 2^-53, so for |q| <= 1025.5 (q = x / scale, the range where the
+// clamp can leave the rounding visible: make_quant_k bounds |qmin - zp| and
+// |qmax - zp| by 1024) |x * inv - q| < 2^-13.99, and
+// |q - r| <= |d| (1 + 2^-23) + 2^-13.99 < 1/2 - 2^-14 whenever
+// |d| < 1/2 - 2^-13; the double quotient fl64(q) is within 2^-42 of q, so
+// rint(fl64(q)) = r as well and the clamped value is the reference's.  A
+// product beyond the clamp is decided by the clamp alone (rounding is
+// monotonic and |x * inv - q| < 1/2 there), whatever d says; beyond 2^22,
+// where d is no residual, `ok` may go either way.  `ok` is cleared in the
+// band (2^-12 of uniform fractions), for NaN and infinite inputs and when
+// the host could not invert the scale (inv = NaN); the caller then uses
+// quantize_byte_near_tie, which holds for every input.
+__device__ __forceinline__ uint32_t quantize_bits_fma(float xv, const QuantK& k, bool& ok) {
+  const float t = __fmaf_rn(xv, k.inv, k.magic_zp);
+  const float r = __fsub_rn(t, k.magic_zp);
+  const float d = __fmaf_rn(xv, k.inv, -r);
+  ok = ok & (fabsf(d) < 0.4998779296875f);  // 1/2 - 2^-13; false for NaN
+  return __float_as_uint(fminf(fmaxf(t, k.t_lo), k.t_hi));
 }
 
-// The byte of an element quantize_bits_try could not decide, without a
-// division in the common case.  For a finite x whose clamped float product
-// mc lies within 2^-11 of k + 1/2 (k = floor(mc), lo <= k < hi), the exact
-// quotient q = x / scale is within 2^-12 of the product, so the reference's
-// rint(fl64(q)) is k or k + 1: with scale > 0 the sign of
-// t = fma(k + 1/2, scale, -x) (one rounding of the exact (k + 1/2 - q) *
-// scale) says which, unless |t| <= 2^-42 * scale, where fl64(q) may round
-// onto the tie itself (|q| < 2^11, so its half ulp is below 2^-42).  NaN,
-// a scale the host could not invert, a negative scale and those last cases
-// take the double division (quantize_byte).
+// The byte of an element the float paths could not decide, without a
+// division in the common case.  For a finite x with unclamped float product
+// m = fl32(x * inv), the exact quotient q = x / scale is within 2^-12 of m,
+// so with k = floor(m) the reference's rint(fl64(q)) is k or k + 1 (an
+// element that reaches this is near k + 1/2); a product clamped to lo or hi
+// leaves k = lo or hi, and the clamp of k or k + 1 is right there as well.
+// With scale > 0 the sign of t = fma(k + 1/2, scale, -x) (one rounding of
+// the exact (k + 1/2 - q) * scale) says which, unless |t| <= 2^-42 * scale,
+// where fl64(q) may round onto the tie itself (|q| < 2^11, so its half ulp
+// is below 2^-42).  NaN, a scale the host could not invert, a negative
+// scale and those last cases take the double division (quantize_byte).
 static __device__ __noinline__ uint32_t quantize_byte_call(float xv, double scale, double zp,
                                                    double qmin, double qmax) {
   return quantize_byte(xv, scale, zp, qmin, qmax);
@@ -161,11 +152,12 @@ inline QuantK make_quant_k(double scale, int64_t zp, int64_t qmin, int64_t qmax)
   k.lo = (float)(qmin - zp);
   k.hi = (float)(qmax - zp);
   k.magic_zp = 12582912.0f + (float)zp;
+  k.t_lo = 12582912.0f + (float)qmin;
+  k.t_hi = 12582912.0f + (float)qmax;
   const bool ok = std::fabs(scale) > 1e-30 && std::fabs(scale) < 1e30 &&
                   std::llabs(zp) <= 1024 && std::llabs(qmin - zp) <= 1024 &&
                   std::llabs(qmax - zp) <= 1024 && qmin <= qmax;
   k.inv = ok ? (float)(1.0 / scale) : std::nanf("");
-  k.inv_lo = ok ? (float)(1.0 / scale - (double)k.inv) : std::nanf("");
   return k;
 }
 

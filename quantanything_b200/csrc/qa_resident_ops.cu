@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(256, 4)
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
           ok[c][b] = true;
-          bits[c][b] = c < C ? quantize_bits_split(fv[b], kk, ok[c][b]) : pad;
+          bits[c][b] = c < C ? quantize_bits_fma(fv[b], kk, ok[c][b]) : pad;
         }
       }
       bool all_ok = true;
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(256, 4)
 #pragma unroll
         for (int b = 0; b < 4; ++b) all_ok = all_ok & (ok[c][b] || c >= C);
       if (!all_ok) {
-        // rare (an element within 2^-20 of a rounding tie, NaN, or no float
+        // rare (an element within 2^-13 of a rounding tie, NaN, or no float
         // scale): each such element is decided on its own
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -2085,8 +2085,8 @@ __global__ void __launch_bounds__(kStemThreads, 1)
 #pragma unroll
         for (int c = 0; c < kStemC; ++c)
           f[c] = *reinterpret_cast<const float4*>(xs + c * plane + off);
-        // per-element exactness flags: an element within 2^-20 of a
-        // rounding tie (a few in a million) is decided on its own
+        // per-element exactness flags: an element within 2^-13 of a
+        // rounding tie (about one in 4096) is decided on its own
         // (quantize_byte_near_tie)
         bool ok[kStemC][4];
         uint32_t t[kStemC][4];
@@ -2096,7 +2096,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             ok[c][u] = true;
-            t[c][u] = quantize_bits_split(fv[u], qk, ok[c][u]);
+            t[c][u] = quantize_bits_fma(fv[u], qk, ok[c][u]);
           }
         }
         bool all_ok = true;
