@@ -924,14 +924,56 @@ __global__ void __launch_bounds__(256)
 // input row's maximum over the KW horizontal taps (neighbouring lanes' loads
 // hit L1) and keeps the last KH row maxima in registers: every input byte
 // comes from DRAM once, every output byte is written once.
+// The maxima run on 16-bit lanes with one native `max.{s,u}16x2` per two
+// bytes.  A 16-bit lane compares its high byte first (signed for signed
+// bytes, as `max.s16x2` reads it), so the high byte of a lane maximum is the
+// maximum of the high bytes whatever the low bytes hold: a 16-byte vector
+// is kept as eight words, each input word w as is (its odd bytes 1 and 3
+// are lane high bytes) and w << 8 (its even bytes 0 and 2 become lane high
+// bytes); the result's high bytes are gathered back with one `prmt` a word.
+struct Wide16 {
+  uint32_t e[4], o[4];  // word i << 8 (even bytes high) / word i (odd bytes high)
+};
+
 template <bool kSigned>
-__device__ __forceinline__ uint4 vmax16(uint4 a, uint4 b) {
+__device__ __forceinline__ Wide16 widen16(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  Wide16 r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    r.e[i] = w[i] << 8;
+    r.o[i] = w[i];
+  }
+  return r;
+}
+
+template <bool kSigned>
+__device__ __forceinline__ uint32_t max16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
   if constexpr (kSigned)
-    return make_uint4(__vmaxs4(a.x, b.x), __vmaxs4(a.y, b.y), __vmaxs4(a.z, b.z),
-                      __vmaxs4(a.w, b.w));
+    asm("max.s16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   else
-    return make_uint4(__vmaxu4(a.x, b.x), __vmaxu4(a.y, b.y), __vmaxu4(a.z, b.z),
-                      __vmaxu4(a.w, b.w));
+    asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <bool kSigned>
+__device__ __forceinline__ Wide16 wmax16(const Wide16& a, const Wide16& b) {
+  Wide16 r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    r.e[i] = max16x2<kSigned>(a.e[i], b.e[i]);
+    r.o[i] = max16x2<kSigned>(a.o[i], b.o[i]);
+  }
+  return r;
+}
+
+__device__ __forceinline__ uint4 narrow16(const Wide16& a) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)  // high bytes: even lane 0, odd lane 0, even lane 1, odd lane 1
+    asm("prmt.b32 %0, %1, %2, 0x7351;" : "=r"(w[i]) : "r"(a.e[i]), "r"(a.o[i]));
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int K, bool kSigned>
@@ -952,7 +994,7 @@ __global__ void __launch_bounds__(256)
   const int64_t n = rest / chunks;
   const int oy0 = chunk * rows_per;
   const int oy1 = min(OH, oy0 + rows_per);
-  const uint4 pad = make_uint4(pad_word, pad_word, pad_word, pad_word);
+  const Wide16 pad = widen16<kSigned>(make_uint4(pad_word, pad_word, pad_word, pad_word));
   // the K horizontal taps of this column: which lie inside the image (fixed
   // for the thread) and the first one's address within a row
   uint32_t inside = 0;
@@ -967,35 +1009,42 @@ __global__ void __launch_bounds__(256)
   auto hmax = [&](int iy) {
     if (iy < 0 || iy >= H) return pad;  // a padded row holds the pad value
     const uint8_t* p = col + (int64_t)iy * row_bytes;
+    uint4 v[K];
     if (full) {
-      uint4 m = __ldg(reinterpret_cast<const uint4*>(p));
 #pragma unroll
-      for (int kx = 1; kx < K; ++kx)
-        m = vmax16<kSigned>(m, __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride)));
-      return m;
+      for (int kx = 0; kx < K; ++kx) v[kx] = __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride));
+    } else {  // some taps fall in the padding
+      const uint4 pv = make_uint4(pad_word, pad_word, pad_word, pad_word);
+#pragma unroll
+      for (int kx = 0; kx < K; ++kx)
+        v[kx] = (inside & (1u << kx)) ? __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride))
+                                      : pv;
     }
-    uint4 m = pad;  // some taps fall in the padding
+    Wide16 m = widen16<kSigned>(v[0]);
 #pragma unroll
-    for (int kx = 0; kx < K; ++kx)
-      if (inside & (1u << kx))
-        m = vmax16<kSigned>(m, __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride)));
+    for (int kx = 1; kx < K; ++kx) m = wmax16<kSigned>(m, widen16<kSigned>(v[kx]));
     return m;
   };
-  // win[k] = row maximum of input row (oy - PH + k) for the next output row
-  uint4 win[K];
+  // the row maxima of the K input rows under output row oy live in a ring:
+  // input row oy - PH + k sits in win[(oy - oy0 + k) % K]; the row loop is
+  // unrolled K times so that every ring index is a constant
+  Wide16 win[K];
 #pragma unroll
-  for (int k = 0; k < K - 1; ++k) win[k + 1] = hmax(oy0 - PH + k);
+  for (int k = 0; k < K - 1; ++k) win[k] = hmax(oy0 - PH + k);
   uint8_t* out = y + ((n * OH + oy0) * OW + ox) * y_stride + g * 16;
   const int64_t out_row = (int64_t)OW * y_stride;
-  for (int oy = oy0; oy < oy1; ++oy) {
+  for (int oy = oy0; oy < oy1; oy += K) {
 #pragma unroll
-    for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
-    win[K - 1] = hmax(oy - PH + K - 1);
-    uint4 m = win[0];
+    for (int j = 0; j < K; ++j) {
+      if (oy + j < oy1) {
+        win[(j + K - 1) % K] = hmax(oy + j - PH + K - 1);
+        Wide16 m = win[0];
 #pragma unroll
-    for (int k = 1; k < K; ++k) m = vmax16<kSigned>(m, win[k]);
-    *reinterpret_cast<uint4*>(out) = m;
-    out += out_row;
+        for (int k = 1; k < K; ++k) m = wmax16<kSigned>(m, win[k]);
+        *reinterpret_cast<uint4*>(out) = narrow16(m);
+        out += out_row;
+      }
+    }
   }
 }
 
