@@ -190,11 +190,14 @@ __global__ void quantize_to_nhwc_kernel(const float* __restrict__ x, uint8_t* __
 // (P > 0): the P x P pixels of patch (py, px) of image n form row
 // (n * H / P + py) * W / P + px of P * P * 4 bytes, pixel (ky, kx) at
 // (ky * P + kx) * 4 -- the im2col rows of a P x P, stride-P convolution.
+// kC3: the tensor has three channels (an RGB image), known at compile time.
+template <bool kC3>
 __global__ void __launch_bounds__(256, 4)
-    quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y, int C,
+    quantize_to_nhwc4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y, int C_,
                              int quads_per_image, int quads, int W, int P, const QuantK k) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
+  const int C = kC3 ? 3 : C_;
   const uint32_t pad = (uint32_t)(int32_t)k.zpd & 0xFFu;
   const QuantK kk = k;  // the fast path's constants in registers
   // each warp takes 32 * kQ consecutive quads; lane l the quads l, l + 32,
@@ -1165,7 +1168,8 @@ QA_API int qa_quantize_to_nhwc_dev(const float* x, void* y, int64_t N, int64_t C
   if (pix_stride == 4 && C <= 4 && HW % 4 == 0 && HW * N / 4 < 0x7FFFFFFF &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const int64_t quads = N * HW / 4;
-    return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
+    return launch_ex(C == 3 ? quantize_to_nhwc4_kernel<true> : quantize_to_nhwc4_kernel<false>,
+                     dim3(grid_for(quads, 256)), dim3(256), 0,
                      (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
                      (int)(HW / 4), (int)quads, (int)W, 0, make_quant_k(scale, zp, qmin, qmax))
                ? 0
@@ -1190,7 +1194,8 @@ QA_API int qa_quantize_to_patch_rows_dev(const float* x, void* y, int64_t N, int
   }
   const int64_t quads = N * H * W / 4;
   if (quads == 0) return 0;
-  return launch_ex(quantize_to_nhwc4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
+  return launch_ex(C == 3 ? quantize_to_nhwc4_kernel<true> : quantize_to_nhwc4_kernel<false>,
+                   dim3(grid_for(quads, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), (int)C,
                    (int)(H * W / 4), (int)quads, (int)W, (int)P,
                    make_quant_k(scale, zp, qmin, qmax))
