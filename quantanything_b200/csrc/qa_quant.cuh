@@ -116,6 +116,50 @@ __device__ __forceinline__ int32_t quantize_value(float xv, const QuantK& k) {
   return k.qmin_i < 0 ? (int32_t)(int8_t)b : (int32_t)b;
 }
 
+// ---- 16-bit outputs (qmin >= -32768, qmax <= 32767): the same FMA
+// rounding with the error bound of the wider range.  With |qmin - zp|,
+// |qmax - zp| and |zp| at most 2^16 (make_quant_k16), |q| <= 2^16 + 1 where
+// the clamp can leave the rounding visible, so |x * inv - q| < 2^-7.99 and
+// |d| < 1/2 - 2^-7 proves |q - r| < 1/2 - 2^-9, beyond the 2^-36 half ulp
+// of the double quotient there; t keeps its integer form while
+// |x * inv + zp| < 2^22.  The value is the low 16 bits of the returned
+// word (its mantissa holds 2^22 + value).
+__device__ __forceinline__ uint32_t quantize_bits16_fma(float xv, const QuantK& k, bool& ok) {
+  const float t = __fmaf_rn(xv, k.inv, k.magic_zp);
+  const float r = __fsub_rn(t, k.magic_zp);
+  const float d = __fmaf_rn(xv, k.inv, -r);
+  ok = ok & (fabsf(d) < 0.4921875f);  // 1/2 - 2^-7; false for NaN
+  return __float_as_uint(fminf(fmaxf(t, k.t_lo), k.t_hi));
+}
+
+// The reference's value in double precision (NaN converts to 0, whose low
+// 16 bits equal those of x86's 0x80000000).
+static __device__ __noinline__ int32_t quantize_value_double(float xv, double scale, double zp,
+                                                             double qmin, double qmax) {
+  double v = rint((double)xv / scale) + zp;
+  if (v < qmin) v = qmin;
+  if (qmax < v) v = qmax;
+  return (int32_t)v;
+}
+
+// The value of an element quantize_bits16_fma could not decide: as
+// quantize_byte_near_tie, with m = fl32(x * inv) within 2^-7 of q on the
+// 16-bit range (so rint(fl64(q)) is floor(m) or floor(m) + 1 for an
+// unclamped m) and the double division taken when |k + 1/2 - q| may be
+// within the 2^-36 half ulp of fl64(q) (|q| < 2^17).
+__device__ __forceinline__ int32_t quantize_value16_near_tie(float xv, const QuantK& k) {
+  const float m = __fmul_rn(xv, k.inv);
+  if (!(m == m) || !(k.scale > 0.0))
+    return quantize_value_double(xv, k.scale, k.zpd, k.qmind, k.qmaxd);
+  const float mc = fminf(fmaxf(m, k.lo), k.hi);
+  const float kf = floorf(mc);
+  const double t = fma((double)kf + 0.5, k.scale, -(double)xv);
+  if (fabs(t) <= k.scale * 0x1p-35)
+    return quantize_value_double(xv, k.scale, k.zpd, k.qmind, k.qmaxd);
+  const int v = (int)kf + (t < 0.0 ? 1 : 0) + k.zp_i;
+  return min(max(v, k.qmin_i), k.qmax_i);
+}
+
 // Word of four channel bytes from quantize_bits_try results (byte 0 of each).
 __device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_t b2,
                                                uint32_t b3) {
@@ -157,6 +201,17 @@ inline QuantK make_quant_k(double scale, int64_t zp, int64_t qmin, int64_t qmax)
   const bool ok = std::fabs(scale) > 1e-30 && std::fabs(scale) < 1e30 &&
                   std::llabs(zp) <= 1024 && std::llabs(qmin - zp) <= 1024 &&
                   std::llabs(qmax - zp) <= 1024 && qmin <= qmax;
+  k.inv = ok ? (float)(1.0 / scale) : std::nanf("");
+  return k;
+}
+
+// make_quant_k for 16-bit outputs: the float path covers |qmin - zp|,
+// |qmax - zp| and |zp| up to 2^16 (quantize_bits16_fma's error bound).
+inline QuantK make_quant_k16(double scale, int64_t zp, int64_t qmin, int64_t qmax) {
+  QuantK k = make_quant_k(scale, zp, qmin, qmax);
+  const bool ok = std::fabs(scale) > 1e-30 && std::fabs(scale) < 1e30 &&
+                  std::llabs(zp) <= 65536 && std::llabs(qmin - zp) <= 65536 &&
+                  std::llabs(qmax - zp) <= 65536 && qmin <= qmax;
   k.inv = ok ? (float)(1.0 / scale) : std::nanf("");
   return k;
 }

@@ -19,6 +19,7 @@
 #include "qa_fixedpoint.cuh"
 #include "qa_fused_epilogue.cuh"
 #include "qa_ptx.cuh"
+#include "qa_quant.cuh"
 #include "qa_umma.cuh"
 
 namespace qa {
@@ -154,34 +155,58 @@ __global__ void quantize_to_planes16_kernel(const float* __restrict__ x, uint8_t
 
 // Four consecutive pixels per thread (pix_stride 4, C <= 4, H*W % 4 == 0):
 // 16-byte reads of each channel plane, 16-byte stores of both output planes.
-__global__ void quantize_to_planes16_x4_kernel(const float* __restrict__ x,
-                                               uint8_t* __restrict__ y, int64_t plane, int C,
-                                               int64_t HW, int64_t quads, double scale,
-                                               double zp, double qmin, double qmax) {
+// Each value is rounded inside one FMA (quantize_bits16_fma); an element in
+// the tie band, NaN or +-inf is decided on its own (quantize_value16_near_tie).
+// kC3: three channels (an RGB image), known at compile time.
+template <bool kC3>
+__global__ void __launch_bounds__(256, 4)
+    quantize_to_planes16_x4_kernel(const float* __restrict__ x, uint8_t* __restrict__ y,
+                                   int64_t plane, int C_, int64_t HW, int64_t quads,
+                                   const QuantK k) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
+  const int C = kC3 ? 3 : C_;
+  const QuantK kk = k;  // the fast path's constants in registers
+  const uint32_t pad = (uint32_t)kk.zp_i;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < quads; q += stride) {
     const int64_t p0 = q * 4;
     const int64_t n = p0 / HW, pix = p0 - n * HW;
-    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+    float4 v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      v[c] = c < C ? __ldg(reinterpret_cast<const float4*>(x + (n * C + c) * HW + pix))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t bits[4][4];  // [channel][pixel]: the value in the low 16 bits
+    bool ok[4][4];
+    bool all_ok = true;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c < C) v = __ldg(reinterpret_cast<const float4*>(x + (n * C + c) * HW + pix));
-      const float e[4] = {v.x, v.y, v.z, v.w};
+      const float e[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        double d = zp;
-        if (c < C) {
-          d = rint((double)e[j] / scale) + zp;
-          if (d < qmin) d = qmin;
-          if (qmax < d) d = qmax;
-        }
-        const uint32_t b = (uint32_t)(int32_t)d;
-        lo[j] |= (b & 0xFFu) << (8 * c);
-        hi[j] |= ((b >> 8) & 0xFFu) << (8 * c);
+        ok[c][j] = true;
+        bits[c][j] = c < C ? quantize_bits16_fma(e[j], kk, ok[c][j]) : pad;
+        all_ok = all_ok & (ok[c][j] || c >= C);
       }
+    }
+    if (!all_ok) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float e[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (c < C && !ok[c][j]) bits[c][j] = (uint32_t)quantize_value16_near_tie(e[j], k);
+      }
+    }
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // byte 0 (low plane) and byte 1 (high plane) of each channel's value
+      lo[j] = __byte_perm(__byte_perm(bits[0][j], bits[1][j], 0x0040),
+                          __byte_perm(bits[2][j], bits[3][j], 0x0040), 0x5410);
+      hi[j] = __byte_perm(__byte_perm(bits[0][j], bits[1][j], 0x0051),
+                          __byte_perm(bits[2][j], bits[3][j], 0x0051), 0x5410);
     }
     *reinterpret_cast<uint4*>(y + p0 * 4) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     *reinterpret_cast<uint4*>(y + plane + p0 * 4) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
@@ -462,9 +487,11 @@ QA_API int qa_quantize_to_planes16_dev(const float* x, void* y, int64_t y_plane,
   if (pix_stride == 4 && C <= 4 && HW % 4 == 0 && (y_plane & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const int64_t quads = N * HW / 4;
-    return launch_ex(quantize_to_planes16_x4_kernel, dim3(grid_for(quads, 256)), dim3(256), 0,
+    return launch_ex(C == 3 ? quantize_to_planes16_x4_kernel<true>
+                            : quantize_to_planes16_x4_kernel<false>,
+                     dim3(grid_for(quads, 256)), dim3(256), 0,
                      (cudaStream_t)stream, true, x, static_cast<uint8_t*>(y), y_plane, (int)C,
-                     HW, quads, scale, (double)zp, (double)qmin, (double)qmax)
+                     HW, quads, make_quant_k16(scale, zp, qmin, qmax))
                ? 0
                : last_status();
   }

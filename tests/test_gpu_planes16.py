@@ -126,6 +126,44 @@ def test_quantize_to_planes(gpu_lib, oracle, raw, C, H, W, stride):
     assert (got[:, C:] == zp).all()  # padding channels hold the zero point
 
 
+@pytest.mark.parametrize("scale,zp", [(9.155e-05, 3), (1.0 / 32767, 0), (2.5e-05, 32767),
+                                      (0.001, -32768), (3e35, 0), (1e-35, 5)])
+def test_quantize_to_planes_near_ties(gpu_lib, oracle, raw, scale, zp):
+    """The four-pixel kernel rounds inside one FMA and decides the elements
+    within 2^-7 of a rounding tie on their own: inputs on and a few ulps
+    around every half-integer (k + 1/2) * scale across the int16 range,
+    saturating and special values, against the reference's double division.
+    The last two scales are outside the float path's range (every element
+    takes the division)."""
+    rng = np.random.default_rng(abs(zp) + 3)
+    with np.errstate(over="ignore"):  # the largest scale overflows float32: +-inf inputs
+        k = rng.integers(-70000, 70000, 60000).astype(np.float64)
+        ties = ((k + 0.5) * scale).astype(np.float32)
+        ulps = rng.integers(-4, 5, ties.size).astype(np.int32)
+        near = (ties.view(np.int32) + ulps).view(np.float32)
+        ints = (rng.integers(-40000, 40000, 4000) * scale).astype(np.float32)
+        rand = (rng.standard_normal(4096) * 20000 * scale).astype(np.float32)
+    special = np.array([np.nan, np.inf, -np.inf, 1e30, -1e30, 3.4e38, -3.4e38, 1e-40, -1e-40,
+                        0.0, -0.0, 1e-30], np.float32)
+    vals = np.concatenate([near, ints, special, rand])
+    C, H = 3, 4
+    W = -(-vals.size // (C * H))
+    W += (-W) % 4
+    x = np.zeros(C * H * W, np.float32)
+    x[:vals.size] = vals
+    x = x.reshape(1, C, H, W)
+    xd = torch.from_numpy(x).cuda()
+    rows = H * W
+    dy, py = _planes(np.zeros((rows, 4), np.int64), 4)
+    _ok(gpu_lib, raw.qa_quantize_to_planes16_dev(xd.data_ptr(), dy.data_ptr(), py, 1, C, H, W,
+                                                 4, scale, zp, QMIN, QMAX, None))
+    want = oracle.quantize_f32(x, scale, zp, QMIN, QMAX)  # NCHW int32 (NaN as x86 leaves it)
+    got = _values(dy, py, rows, 4, 4)
+    want16 = ((want.reshape(C, rows).T.astype(np.int64) + 32768) & 0xFFFF) - 32768
+    np.testing.assert_array_equal(got[:, :C], want16)
+    assert (got[:, C] == zp).all()
+
+
 def test_softmax_planes(gpu_lib, oracle, raw):
     rng = np.random.default_rng(9)
     N, C, stride = 5, 1000, 1008
