@@ -140,7 +140,14 @@ def measure_elementwise(dev, stream, flush, hbm_peak, reps=5):
     """The standalone memory-bound resident kernels on tensors larger than
     L2 (2^21 pixels x 64 channels: 128 MiB per 8-bit operand): median
     CUDA-event time of single launches, L2 flushed before each; algorithmic
-    bytes = every operand read once plus the output written once."""
+    bytes = every operand read once plus the output written once.
+
+    Two timings per kernel: after the flush alone (a zero fill of a buffer
+    larger than L2, whose dirty lines the kernel's own misses then write
+    back to DRAM during the timed launch), and with L2 clean (the same fill
+    followed, outside the events, by a read of another buffer larger than
+    L2, which writes those lines back first): the second is the kernel's
+    own DRAM traffic, as an ncu capture with its cache control sees it."""
     import ctypes
 
     import torch
@@ -162,6 +169,7 @@ def measure_elementwise(dev, stream, flush, hbm_peak, reps=5):
     mult = torch.full((C,), 1 << 30, dtype=torch.int64, device=dev)
     shift = torch.full((C,), 4, dtype=torch.int64, device=dev)
     img = torch.randn(2048, 3, 64, 64, device=dev)  # 2^23 pixels: 100 MB, past L2
+    clean = torch.ones(flush.numel(), dtype=torch.uint8, device=dev)  # read-only after this
     m30 = 1 << 30
     cases = {
         "lut (table)": (2 * n, lambda: raw.qa_lut_bytes_dev(a.data_ptr(), C, 1, y.data_ptr(), C,
@@ -196,23 +204,32 @@ def measure_elementwise(dev, stream, flush, hbm_peak, reps=5):
         for _ in range(2):
             if fn() != 0:
                 raise RuntimeError(f"{name}: {lib.raw.qa_last_error().decode()}")
-        times = []
+        times, times_clean = [], []
         for _ in range(reps):
-            flush.zero_()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            fn()
-            e1.record(stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
+            for clean_l2 in (False, True):
+                flush.zero_()
+                if clean_l2:
+                    torch.amax(clean)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                e1.synchronize()
+                (times_clean if clean_l2 else times).append(e0.elapsed_time(e1))
         t = float(np.median(times)) / 1e3
-        gbs = nbytes / t / 1e9
+        tc = float(np.median(times_clean)) / 1e3
+        gbs, gbs_c = nbytes / t / 1e9, nbytes / tc / 1e9
         res[name] = {"us": round(t * 1e6, 1), "GB/s": round(gbs, 1),
-                     "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes)}
+                     "frac": round(gbs / hbm_peak, 4), "bytes": int(nbytes),
+                     "us_clean_l2": round(tc * 1e6, 1),
+                     "frac_clean_l2": round(gbs_c / hbm_peak, 4)}
     res["timing"] = (f"median of {reps} single launches on 2^21 pixels x 64 channels (the "
-                     "float quantizer: 2^23 pixels x 3 channels), L2 flushed before each; bytes "
-                     "= operands read once + output written once")
+                     "float quantizer: 2^23 pixels x 3 channels), L2 flushed before each (a zero "
+                     "fill larger than L2; its dirty lines are written back during the launch); "
+                     "*_clean_l2: the fill then a read of another buffer larger than L2, outside "
+                     "the events, so only the kernel's own traffic is timed; bytes = operands "
+                     "read once + output written once")
     return res
 
 
