@@ -980,7 +980,7 @@ __device__ __forceinline__ uint4 narrow16(const Wide16& a) {
 }
 
 template <int K, bool kSigned>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
     maxpool_s1_columns_kernel(const uint8_t* __restrict__ x, int64_t x_stride,
                               uint8_t* __restrict__ y, int64_t y_stride, int H, int W, int groups,
                               int PH, int PW, int OH, int OW, int rows_per, int chunks,
@@ -997,7 +997,7 @@ __global__ void __launch_bounds__(256)
   const int64_t n = rest / chunks;
   const int oy0 = chunk * rows_per;
   const int oy1 = min(OH, oy0 + rows_per);
-  const Wide16 pad = widen16<kSigned>(make_uint4(pad_word, pad_word, pad_word, pad_word));
+  const uint4 padv = make_uint4(pad_word, pad_word, pad_word, pad_word);
   // the K horizontal taps of this column: which lie inside the image (fixed
   // for the thread) and the first one's address within a row
   uint32_t inside = 0;
@@ -1010,7 +1010,7 @@ __global__ void __launch_bounds__(256)
   const uint8_t* const col = x + n * H * row_bytes + (int64_t)(ox - PW) * x_stride + g * 16;
   const bool full = inside == (1u << K) - 1;
   auto hmax = [&](int iy) {
-    if (iy < 0 || iy >= H) return pad;  // a padded row holds the pad value
+    if (iy < 0 || iy >= H) return padv;  // a padded row holds the pad value
     const uint8_t* p = col + (int64_t)iy * row_bytes;
     uint4 v[K];
     if (full) {
@@ -1026,12 +1026,13 @@ __global__ void __launch_bounds__(256)
     Wide16 m = widen16<kSigned>(v[0]);
 #pragma unroll
     for (int kx = 1; kx < K; ++kx) m = wmax16<kSigned>(m, widen16<kSigned>(v[kx]));
-    return m;
+    return narrow16(m);
   };
-  // the row maxima of the K input rows under output row oy live in a ring:
+  // the row maxima of the K input rows under output row oy live in a ring,
+  // packed (16 bytes each, so that four 256-thread blocks fit an SM):
   // input row oy - PH + k sits in win[(oy - oy0 + k) % K]; the row loop is
   // unrolled K times so that every ring index is a constant
-  Wide16 win[K];
+  uint4 win[K];
 #pragma unroll
   for (int k = 0; k < K - 1; ++k) win[k] = hmax(oy0 - PH + k);
   uint8_t* out = y + ((n * OH + oy0) * OW + ox) * y_stride + g * 16;
@@ -1041,9 +1042,9 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < K; ++j) {
       if (oy + j < oy1) {
         win[(j + K - 1) % K] = hmax(oy + j - PH + K - 1);
-        Wide16 m = win[0];
+        Wide16 m = widen16<kSigned>(win[0]);
 #pragma unroll
-        for (int k = 1; k < K; ++k) m = wmax16<kSigned>(m, win[k]);
+        for (int k = 1; k < K; ++k) m = wmax16<kSigned>(m, widen16<kSigned>(win[k]));
         *reinterpret_cast<uint4*>(out) = narrow16(m);
         out += out_row;
       }
