@@ -576,10 +576,13 @@ def main():
         same = max_over_ranks(digest) == -max_over_ranks(-digest)
         gather_ok = max_over_ranks(0.0 if own else 1.0) == 0.0 and same
 
-    # ---- roofline of the dominant kernel: every step captured alone in a
-    # CUDA graph and replayed with CUDA events around each replay (L2 flushed
-    # before each, outside the events), so host launch work is not timed
-    step_ms = net.time_steps_graphed(reps=20, flush=flush)
+    # ---- roofline of the dominant kernel: every step timed inside a CUDA
+    # graph of ten (L2 flush, step) rounds against a graph of the ten flushes
+    # alone (no host launch work; the event granularity and the graph launch
+    # spread over ten launches); the single-replay figure of the dominant
+    # step (one graph launch per event pair) is reported beside it
+    step_ms = net.time_steps_in_graph(flush)
+    single_ms = net.time_steps_graphed(reps=20, flush=flush)
     costs = net.step_costs()
     dom = int(np.argmax(step_ms))
     label, dom_bytes, dom_ops = costs[dom]
@@ -606,6 +609,11 @@ def main():
                     "unit": "TOPS", "frac": round(achieved / tensor_peak, 4),
                     "traffic": traffic, "algorithmic_ops": int(dom_ops)}
     roofline.update({"kernel": label, "us_per_launch": round(step_ms[dom] * 1e3, 2),
+                     "us_per_launch_single_replay": round(single_ms[dom] * 1e3, 2),
+                     "timing": "in-graph: (10 x (L2 flush + launch) - 10 x flush) / 10, median "
+                               "of 5; single replay: one graph launch of the step per CUDA-event "
+                               "pair, L2 flushed before each (its figures fall on a 2.048 us "
+                               "grid and carry the graph launch)",
                      "share_of_step": round(float(step_ms[dom] / step_ms.sum()), 4),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json; int8 tensor = 2 x "
                                     f"measured bf16 cuBLAS{tensor_note})"})

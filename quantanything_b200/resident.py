@@ -979,6 +979,60 @@ class ResidentNet:
             self.launch_count = len(saved)
         return totals / reps
 
+    def time_steps_in_graph(self, flush, repeat=10, reps=5):
+        """Device time (ms) of every step, from one CUDA graph holding
+        ``repeat`` rounds of (zero ``flush``, launch the step) against one
+        holding the ``repeat`` flushes alone: the difference of their replay
+        times (median of ``reps``) over ``repeat``.  Each launch starts with
+        its inputs out of L2, as in :meth:`time_steps_graphed`, but the graph
+        launch and the granularity of the event timestamps (single-replay
+        figures fell on a 2.048 µs grid on B200) are spread over ``repeat``
+        launches; what remains is the launch's own time after the flush
+        kernel it depends on."""
+        torch.cuda.synchronize(self.device)
+        self.forward_device()  # eager warm-up: one-time host preparation
+        torch.cuda.synchronize(self.device)
+        saved = self.steps
+        out = np.zeros(len(saved))
+        s = torch.cuda.Stream(self.device)
+
+        def replay_ms(g):
+            with torch.cuda.stream(s):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                g.replay()
+                e1.record(s)
+            e1.synchronize()
+            return e0.elapsed_time(e1)
+
+        try:
+            g0 = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g0, stream=s):
+                    for _ in range(repeat):
+                        flush.zero_()
+            for i, step in enumerate(saved):
+                self.steps = [step]
+                g1 = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(s):
+                    with torch.cuda.graph(g1, stream=s):
+                        for _ in range(repeat):
+                            flush.zero_()
+                            self._launch_all(s.cuda_stream)
+                torch.cuda.synchronize(self.device)
+                t1, t0 = [], []
+                for _ in range(reps):
+                    t1.append(replay_ms(g1))
+                    t0.append(replay_ms(g0))
+                out[i] = max(float(np.median(t1) - np.median(t0)), 0.0) / repeat
+                del g1
+            del g0
+        finally:
+            self.steps = saved
+            self.launch_count = len(saved)
+        return out
+
     # ------------------------------------------------------------- launch --
     def _launch_all(self, stream, on_step=None):
         raw = self.lib.raw
