@@ -102,10 +102,50 @@ def select_workload(name):
     METRIC, PER_GPU_BATCH = W["metric"], W["batch"]
 
 
+def in_graph_ms(launch, flush, stream, repeat=10, reps=5):
+    """Device time (ms) of one launch of ``launch(stream_handle)``: a CUDA
+    graph of ``repeat`` rounds of (zero ``flush``, launch) against one of the
+    ``repeat`` flushes alone, the difference of the medians of ``reps``
+    replays over ``repeat`` (single launches between CUDA events carry the
+    launch and the events' 2.048 us timestamp grid on B200)."""
+    import torch
+
+    s = torch.cuda.Stream(flush.device)
+    g0, g1 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g0, stream=s):
+            for _ in range(repeat):
+                flush.zero_()
+        with torch.cuda.graph(g1, stream=s):
+            for _ in range(repeat):
+                flush.zero_()
+                launch(s.cuda_stream)
+    torch.cuda.synchronize(flush.device)
+
+    def replay_ms(g):
+        with torch.cuda.stream(s):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            g.replay()
+            e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    t1, t0 = [], []
+    for _ in range(reps):
+        t1.append(replay_ms(g1))
+        t0.append(replay_ms(g0))
+    del g0, g1
+    return max(float(np.median(t1) - np.median(t0)), 0.0) / repeat
+
+
 def measure_fused_configs(dev, stream, flush, peak_tops, reps=10):
     """cfg0 (Linear 256x768x3072) and cfg1 (conv 3x3 [32,64,56,56] -> 128 with
     the SiLU table) on the fused int8 tensor-core kernel, device-resident:
-    median CUDA-event time of single launches, L2 flushed before each one."""
+    the in-graph launch time (``in_graph_ms``, L2 flushed before each
+    launch) and, beside it, the median CUDA-event time of single launches,
+    L2 flushed before each one."""
     import torch
 
     from quantanything_b200 import native
@@ -127,12 +167,17 @@ def measure_fused_configs(dev, stream, flush, peak_tops, reps=10):
             e1.record(stream)
             e1.synchronize()
             times.append(e0.elapsed_time(e1))
-        t = float(np.median(times)) / 1e3
+        t1 = float(np.median(times)) / 1e3
+        t = in_graph_ms(case.launch, flush, stream) / 1e3
         tops = case.ops / t / 1e12
         res[name] = {"shape": shape, "us": round(t * 1e6, 2), "TOPS": round(tops, 1),
-                     "frac": round(tops / peak_tops, 4), "block_n": int(case.desc.block_n)}
+                     "frac": round(tops / peak_tops, 4), "block_n": int(case.desc.block_n),
+                     "us_single_launch": round(t1 * 1e6, 2),
+                     "frac_single_launch": round(case.ops / t1 / 1e12 / peak_tops, 4)}
     res["peak_TOPS"] = peak_tops
-    res["timing"] = f"median of {reps} single launches, L2 flushed before each"
+    res["timing"] = ("in-graph: (10 x (L2 flush + launch) - 10 x flush) / 10, median of 5; "
+                     f"*_single_launch: median of {reps} single launches between CUDA events, "
+                     "L2 flushed before each")
     return res
 
 
