@@ -921,12 +921,12 @@ __global__ void __launch_bounds__(256)
 }
 
 // Column walker for stride-1 max pools with a KH x KW window known at compile
-// time: a thread owns one output column of one image and one 16-channel
-// group (lanes walk the groups of consecutive pixels, so a warp reads and
-// writes contiguous bytes), walks down a chunk of output rows, takes each
-// input row's maximum over the KW horizontal taps (neighbouring lanes' loads
-// hit L1) and keeps the last KH row maxima in registers: every input byte
-// comes from DRAM once, every output byte is written once.
+// time: a thread owns two neighbouring output columns of one image and one
+// 16-channel group (lanes walk the groups of consecutive pixel pairs, so a
+// warp reads and writes contiguous bytes), walks down a chunk of output
+// rows, takes each input row's maxima over the horizontal taps (neighbouring
+// lanes' loads hit L1) and keeps the last KH row maxima in registers: every
+// input byte comes from DRAM once, every output byte is written once.
 // The maxima run on 16-bit lanes with one native `max.{s,u}16x2` per two
 // bytes.  A 16-bit lane compares its high byte first (signed for signed
 // bytes, as `max.s16x2` reads it), so the high byte of a lane maximum is the
@@ -979,73 +979,86 @@ __device__ __forceinline__ uint4 narrow16(const Wide16& a) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Two output columns per thread: the windows of columns ox and ox + 1 share
+// K - 1 of their K + 1 taps, so a row costs K + 1 loads and one maximum of
+// the middle K - 1 taps for both columns, and a thread keeps two fresh
+// 16-byte DRAM loads in flight.  The row maxima of the K input rows under
+// output row oy live in one ring per column, packed (16 bytes each):
+// input row oy - PH + k sits in slot (oy - oy0 + k) % K; the row loop is
+// unrolled K times so that every ring index is a constant.
 template <int K, bool kSigned>
-__global__ void __launch_bounds__(256, 4)
-    maxpool_s1_columns_kernel(const uint8_t* __restrict__ x, int64_t x_stride,
-                              uint8_t* __restrict__ y, int64_t y_stride, int H, int W, int groups,
-                              int PH, int PW, int OH, int OW, int rows_per, int chunks,
-                              int64_t total, uint32_t pad_word) {
+__global__ void __launch_bounds__(256)
+    maxpool_s1_pairs_kernel(const uint8_t* __restrict__ x, int64_t x_stride,
+                            uint8_t* __restrict__ y, int64_t y_stride, int H, int W, int groups,
+                            int PH, int PW, int OH, int OW, int rows_per, int chunks,
+                            int64_t total, uint32_t pad_word) {
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= total) return;
+  const int pairs = (OW + 1) / 2;
   const int g = (int)(t % groups);
   int64_t rest = t / groups;
-  const int ox = (int)(rest % OW);
-  rest /= OW;
+  const int ox = 2 * (int)(rest % pairs);
+  rest /= pairs;
   const int chunk = (int)(rest % chunks);
   const int64_t n = rest / chunks;
   const int oy0 = chunk * rows_per;
   const int oy1 = min(OH, oy0 + rows_per);
+  const bool two = ox + 1 < OW;
   const uint4 padv = make_uint4(pad_word, pad_word, pad_word, pad_word);
-  // the K horizontal taps of this column: which lie inside the image (fixed
-  // for the thread) and the first one's address within a row
+  // taps j = 0 .. K: input column ox - PW + j (column ox reads 0 .. K - 1,
+  // column ox + 1 reads 1 .. K)
   uint32_t inside = 0;
 #pragma unroll
-  for (int kx = 0; kx < K; ++kx) {
-    const int ix = ox - PW + kx;
-    inside |= (ix >= 0 && ix < W ? 1u : 0u) << kx;
+  for (int j = 0; j <= K; ++j) {
+    const int ix = ox - PW + j;
+    inside |= (ix >= 0 && ix < W ? 1u : 0u) << j;
   }
   const int64_t row_bytes = (int64_t)W * x_stride;
   const uint8_t* const col = x + n * H * row_bytes + (int64_t)(ox - PW) * x_stride + g * 16;
-  const bool full = inside == (1u << K) - 1;
-  auto hmax = [&](int iy) {
-    if (iy < 0 || iy >= H) return padv;  // a padded row holds the pad value
+  const bool full = inside == (1u << (K + 1)) - 1;
+  auto hmax = [&](int iy, uint4& m0, uint4& m1) {
+    if (iy < 0 || iy >= H) {  // a padded row holds the pad value
+      m0 = padv;
+      m1 = padv;
+      return;
+    }
     const uint8_t* p = col + (int64_t)iy * row_bytes;
-    uint4 v[K];
+    uint4 v[K + 1];
     if (full) {
 #pragma unroll
-      for (int kx = 0; kx < K; ++kx) v[kx] = __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride));
-    } else {  // some taps fall in the padding
-      const uint4 pv = make_uint4(pad_word, pad_word, pad_word, pad_word);
+      for (int j = 0; j <= K; ++j) v[j] = __ldg(reinterpret_cast<const uint4*>(p + j * x_stride));
+    } else {
 #pragma unroll
-      for (int kx = 0; kx < K; ++kx)
-        v[kx] = (inside & (1u << kx)) ? __ldg(reinterpret_cast<const uint4*>(p + kx * x_stride))
-                                      : pv;
+      for (int j = 0; j <= K; ++j)
+        v[j] = (inside & (1u << j)) ? __ldg(reinterpret_cast<const uint4*>(p + j * x_stride))
+                                    : padv;
     }
-    Wide16 m = widen16<kSigned>(v[0]);
+    Wide16 mid = widen16<kSigned>(v[1]);
 #pragma unroll
-    for (int kx = 1; kx < K; ++kx) m = wmax16<kSigned>(m, widen16<kSigned>(v[kx]));
-    return narrow16(m);
+    for (int j = 2; j < K; ++j) mid = wmax16<kSigned>(mid, widen16<kSigned>(v[j]));
+    m0 = narrow16(wmax16<kSigned>(mid, widen16<kSigned>(v[0])));
+    m1 = narrow16(wmax16<kSigned>(mid, widen16<kSigned>(v[K])));
   };
-  // the row maxima of the K input rows under output row oy live in a ring,
-  // packed (16 bytes each, so that four 256-thread blocks fit an SM):
-  // input row oy - PH + k sits in win[(oy - oy0 + k) % K]; the row loop is
-  // unrolled K times so that every ring index is a constant
-  uint4 win[K];
+  uint4 w0[K], w1[K];
 #pragma unroll
-  for (int k = 0; k < K - 1; ++k) win[k] = hmax(oy0 - PH + k);
+  for (int k = 0; k < K - 1; ++k) hmax(oy0 - PH + k, w0[k], w1[k]);
   uint8_t* out = y + ((n * OH + oy0) * OW + ox) * y_stride + g * 16;
   const int64_t out_row = (int64_t)OW * y_stride;
   for (int oy = oy0; oy < oy1; oy += K) {
 #pragma unroll
     for (int j = 0; j < K; ++j) {
       if (oy + j < oy1) {
-        win[(j + K - 1) % K] = hmax(oy + j - PH + K - 1);
-        Wide16 m = widen16<kSigned>(win[0]);
+        hmax(oy + j - PH + K - 1, w0[(j + K - 1) % K], w1[(j + K - 1) % K]);
+        Wide16 a = widen16<kSigned>(w0[0]), b = widen16<kSigned>(w1[0]);
 #pragma unroll
-        for (int k = 1; k < K; ++k) m = wmax16<kSigned>(m, widen16<kSigned>(win[k]));
-        *reinterpret_cast<uint4*>(out) = narrow16(m);
+        for (int k = 1; k < K; ++k) {
+          a = wmax16<kSigned>(a, widen16<kSigned>(w0[k]));
+          b = wmax16<kSigned>(b, widen16<kSigned>(w1[k]));
+        }
+        *reinterpret_cast<uint4*>(out) = narrow16(a);
+        if (two) *reinterpret_cast<uint4*>(out + y_stride) = narrow16(b);
         out += out_row;
       }
     }
@@ -1400,12 +1413,12 @@ QA_API int qa_maxpool_bytes_dev(const void* x, int64_t x_stride, int64_t x_signe
     const uint32_t pw = ((uint32_t)pad_value & 0xFFu) * 0x01010101u;
     const int rows_per = (int)std::min<int64_t>(OH, 16);
     const int chunks = (int)((OH + rows_per - 1) / rows_per);
-    const int64_t threads = N * chunks * OW * (C / 16);
+    const int64_t threads = N * chunks * ((OW + 1) / 2) * (C / 16);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
-    auto kern = KH == 3 ? (x_signed ? maxpool_s1_columns_kernel<3, true>
-                                    : maxpool_s1_columns_kernel<3, false>)
-                        : (x_signed ? maxpool_s1_columns_kernel<5, true>
-                                    : maxpool_s1_columns_kernel<5, false>);
+    auto kern = KH == 3 ? (x_signed ? maxpool_s1_pairs_kernel<3, true>
+                                    : maxpool_s1_pairs_kernel<3, false>)
+                        : (x_signed ? maxpool_s1_pairs_kernel<5, true>
+                                    : maxpool_s1_pairs_kernel<5, false>);
     return launch_ex(kern, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, true,
                      static_cast<const uint8_t*>(x), x_stride, static_cast<uint8_t*>(y), y_stride,
                      (int)H, (int)W, (int)(C / 16), (int)PH, (int)PW, (int)OH, (int)OW, rows_per,
