@@ -102,7 +102,7 @@ def select_workload(name):
     METRIC, PER_GPU_BATCH = W["metric"], W["batch"]
 
 
-def in_graph_ms(launch, flush, stream, repeat=10, reps=5):
+def in_graph_ms(launch, flush, repeat=10, reps=5):
     """Device time (ms) of one launch of ``launch(stream_handle)``: a CUDA
     graph of ``repeat`` rounds of (zero ``flush``, launch) against one of the
     ``repeat`` flushes alone, the difference of the medians of ``reps``
@@ -168,7 +168,7 @@ def measure_fused_configs(dev, stream, flush, peak_tops, reps=10):
             e1.synchronize()
             times.append(e0.elapsed_time(e1))
         t1 = float(np.median(times)) / 1e3
-        t = in_graph_ms(case.launch, flush, stream) / 1e3
+        t = in_graph_ms(case.launch, flush) / 1e3
         tops = case.ops / t / 1e12
         res[name] = {"shape": shape, "us": round(t * 1e6, 2), "TOPS": round(tops, 1),
                      "frac": round(tops / peak_tops, 4), "block_n": int(case.desc.block_n),
