@@ -22,7 +22,9 @@ the Softmax float fallback, captured in a CUDA graph.
   e2e_dropin -- images/s of the drop-in route: the reference's layer-by-layer
             execution driving the CUDA library's host-pointer ABI
             (one H2D/D2H per layer), wall clock.
-  roofline -- dominant kernel of the step, measured live with CUDA events.
+  roofline -- dominant kernel of the step, measured live with CUDA events:
+            a CUDA graph of ten (L2 flush, step) rounds against one of the
+            ten flushes alone (the single-replay figure beside it).
   cpu_baseline -- the reference's own C++ kernels (oracle/_ref, OpenMP, all
             host threads) driven layer by layer, on a bounded sample.
 
