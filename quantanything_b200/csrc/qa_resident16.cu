@@ -279,6 +279,66 @@ __global__ void gap16_planes_kernel(Planes16 x, int64_t N, int64_t HW, int64_t C
   }
 }
 
+// Thread per (image, 16-channel group) for images of at most 256 pixels:
+// every pixel's two 16-byte plane loads are independent (several pixels in
+// flight per thread), the two bytes of each value become one sign-extended
+// int32 in one `prmt` (selector nibbles with bit 3 set replicate the sign of
+// the high byte), and the int32 sums (at most 256 * 2^15 in magnitude) are
+// requantized once per channel.
+__device__ __forceinline__ int32_t plane_value(uint32_t lo, uint32_t hi, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "r"(sel));
+  return (int32_t)r;
+}
+
+__global__ void __launch_bounds__(256)
+    gap16_thread_planes_kernel(Planes16 x, int64_t N, int HW, int64_t groups, int64_t zp_in,
+                               int64_t m, int64_t s, int64_t zp_out, int64_t qmin, int64_t qmax,
+                               uint8_t* __restrict__ y, int64_t y_plane, int64_t y_pix_stride,
+                               int vec_out) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  // value k of a word pair: bytes (lo.k, hi.k, sign(hi.k), sign(hi.k))
+  constexpr uint32_t kSel[4] = {0xCC40u, 0xDD51u, 0xEE62u, 0xFF73u};
+  const int64_t total = N * groups;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / groups, g = i - n * groups;
+    const uint8_t* base = x.p + n * HW * x.stride + g * 16;
+    int32_t acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0;
+#pragma unroll 4
+    for (int p = 0; p < HW; ++p) {
+      const uint4 l = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)p * x.stride));
+      const uint4 h =
+          __ldg(reinterpret_cast<const uint4*>(base + x.plane + (int64_t)p * x.stride));
+      const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] += plane_value(lw[j >> 2], hw[j >> 2], kSel[j & 3]);
+    }
+    uint8_t* dst = y + n * y_pix_stride + g * 16;
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int64_t q =
+          requant_exact((int64_t)acc[j] - (int64_t)HW * zp_in, m, s, zp_out, qmin, qmax);
+      lo[j >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (j & 3));
+      hi[j >> 2] |= (((uint32_t)q >> 8) & 0xFFu) << (8 * (j & 3));
+    }
+    if (vec_out) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      *reinterpret_cast<uint4*>(dst + y_plane) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        dst[j] = (uint8_t)(lo[j >> 2] >> (8 * (j & 3)));
+        dst[y_plane + j] = (uint8_t)(hi[j >> 2] >> (8 * (j & 3)));
+      }
+    }
+  }
+}
+
 // Integer Mul of two activations (qa_kernels.cpp:334-345): the product of
 // two centred int16 values fits int64; the 128-bit mbqm requantizes it.
 __global__ void mul16_kernel(Planes16 a, Planes16 b, uint8_t* __restrict__ y, int64_t y_plane,
@@ -508,6 +568,21 @@ QA_API int qa_gap16_dev(const void* x, int64_t x_plane, int64_t x_pix_stride, in
                         int64_t y_pix_stride, void* stream) {
   clear_error();
   if (N * C == 0) return 0;
+  if (C % 16 == 0 && x_pix_stride % 16 == 0 && (x_plane & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && HW >= 1 && HW <= 256) {
+    // one thread per (image, 16-channel group), every group in one pass
+    const int64_t total = N * (C / 16);
+    const int vec_out = ((reinterpret_cast<uintptr_t>(y) | (uint64_t)y_plane |
+                          (uint64_t)y_pix_stride) & 15) == 0;
+    return launch_ex(gap16_thread_planes_kernel,
+                     dim3((unsigned)std::min<int64_t>((total + 255) / 256, 0x7FFFFFFF)),
+                     dim3(256), 0, (cudaStream_t)stream, true,
+                     Planes16{static_cast<const uint8_t*>(x), x_plane, x_pix_stride}, N,
+                     (int)HW, C / 16, zp_in, mult, shift, zp_out, qmin, qmax,
+                     static_cast<uint8_t*>(y), y_plane, y_pix_stride, vec_out)
+               ? 0
+               : last_status();
+  }
   if (C % 16 == 0 && x_pix_stride % 16 == 0 && (x_plane & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     const int64_t warps = N * (C / 16);
