@@ -81,6 +81,59 @@ __global__ void vit_embed_kernel(const uint8_t* __restrict__ x, int64_t x_stride
   }
 }
 
+// The same with sixteen features per thread (D % 16 == 0, 16-byte aligned
+// rows): one 16-byte load of x and of the output, the 384-entry term table
+// in shared memory, the position terms as four 16-byte loads.
+template <bool kSigned>
+__global__ void __launch_bounds__(256)
+    vit_embed16_kernel(const uint8_t* __restrict__ x, int64_t x_stride,
+                       const int32_t* __restrict__ ta, const int32_t* __restrict__ pos,
+                       const uint8_t* __restrict__ cls_row, int32_t qmin, int32_t qmax,
+                       uint8_t* __restrict__ out, int64_t out_stride, int64_t B, int T, int D) {
+  __shared__ int32_t s_ta[384];
+  for (int i = threadIdx.x; i < 384; i += blockDim.x) s_ta[i] = ta[i];
+  __syncthreads();
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  const int dq = D / 16;
+  const int64_t total = B * T * dq;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / dq;
+    const int j = (int)(i - row * dq);
+    const int64_t n = row / T;
+    const int t = (int)(row - n * T);
+    uint4 v;
+    if (t == 0) {
+      v = *reinterpret_cast<const uint4*>(cls_row + 16 * j);
+    } else {
+      const uint4 xv = *reinterpret_cast<const uint4*>(
+          x + (n * (T - 1) + t - 1) * x_stride + 16 * j);
+      const int4* pp = reinterpret_cast<const int4*>(pos + (int64_t)t * D + 16 * j);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int4 p4 = __ldg(pp + k4);
+        const int32_t pv[4] = {p4.x, p4.y, p4.z, p4.w};
+        uint32_t w = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t b = (xw[k4] >> (8 * e)) & 0xFFu;
+          const int32_t a = kSigned ? (int32_t)(int8_t)b : (int32_t)b;
+          // int64: the two int32 terms may sum past int32
+          const int64_t sum = (int64_t)s_ta[a + 128] + pv[e];
+          const int32_t sv = (int32_t)(sum < qmin ? qmin : (sum > qmax ? qmax : sum));
+          w |= ((uint32_t)sv & 0xFFu) << (8 * e);
+        }
+        ow[k4] = w;
+      }
+      v = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    *reinterpret_cast<uint4*>(out + row * out_stride + 16 * j) = v;
+  }
+}
+
 // ------------------------------------------------------------ LayerNorm --
 // One warp per row: float64 mean and variance of the dequantized row,
 // (x - mean) / sqrt(var + eps) * gamma + beta in float64, rounded to float32,
@@ -916,6 +969,20 @@ QA_API int qa_vit_embed_dev(const void* x, int64_t x_stride, int32_t x_signed,
     return last_status();
   }
   if (B == 0) return 0;
+  const bool vec = D % 16 == 0 && x_stride % 16 == 0 && out_stride % 16 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                     reinterpret_cast<uintptr_t>(pos) | reinterpret_cast<uintptr_t>(cls_row)) &
+                    15) == 0 &&
+                   qmin >= -128 && qmax <= 255 && T < (1 << 30) && D < (1 << 30);
+  if (vec) {
+    auto kern = x_signed ? vit_embed16_kernel<true> : vit_embed16_kernel<false>;
+    return launch_ex(kern, dim3(grid_for(B * T * (D / 16), 256)), dim3(256), 0,
+                     (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_stride, ta,
+                     pos, static_cast<const uint8_t*>(cls_row), (int32_t)qmin, (int32_t)qmax,
+                     static_cast<uint8_t*>(out), out_stride, B, (int)T, (int)D)
+               ? 0
+               : last_status();
+  }
   return launch_ex(vit_embed_kernel, dim3(grid_for(B * T * D, 256)), dim3(256), 0,
                    (cudaStream_t)stream, true, static_cast<const uint8_t*>(x), x_stride,
                    (int)x_signed, ta, pos, static_cast<const uint8_t*>(cls_row), qmin, qmax,
