@@ -1928,23 +1928,29 @@ __global__ void __launch_bounds__(kInThreads, 2)
 // ============================================ warp-specialized stem layer ==
 // The 3 x 3, stride-2, undilated input layer over three float channels (the
 // YOLO stem), same arithmetic as input_conv_kernel, with the four steps of a
-// tile run by separate warps that hand work to each other through mbarriers
-// (one CTA per SM, 20 warps), so the quantization of one tile, the MMAs of
-// the previous one and the epilogue of the one before overlap:
+// tile run by separate warps that hand work to each other through mbarriers,
+// so the quantization of one tile, the MMAs of the previous one and the
+// epilogue of the one before overlap.  Two CTAs of 10 warps share an SM
+// (two float patch stages and one A buffer each): the roles are latency-
+// bound, and two independent pipelines per SM cover each other's waits
+// (one CTA of 20 warps, three stages and two A buffers ran 12% slower):
 //   warp 0     lane 0 keeps kStemStages float patches in flight by TMA;
 //   warp 1     allocates TMEM; lane 0 issues the tile's MMAs (four 128-row
 //              blocks, two K-steps) into one of two accumulator sets;
-//   warps 2-11 quantize the patch four box columns at a time (16-byte reads
+//   warps 2-5  quantize the patch four box columns at a time (16-byte reads
 //              of each channel row) into 4-channel words, then write the
 //              tile's 448 implicit-GEMM rows (nine words at fixed offsets)
-//              into one of two A buffers;
-//   warps 12-19 drain the finished accumulator set through the epilogue.
+//              into the A buffer;
+//   warps 6-9  drain the finished accumulator set through the epilogue, one
+//              per TMEM lane quarter.
 namespace qa {
 namespace {
 constexpr int kStemC = 3;           // float channels of the stem form
-constexpr int kStemStages = 3;      // float patches in flight
-constexpr int kStemBuildWarp0 = 2, kStemBuildThreads = 320;
-constexpr int kStemEpiWarp0 = 12, kStemEpiWarps = 8;  // two per TMEM lane quarter
+constexpr int kStemStages = 2;      // float patches in flight
+constexpr int kStemASets = 1;       // A buffers
+constexpr int kStemCtas = 2;        // CTAs per SM
+constexpr int kStemBuildWarp0 = 2, kStemBuildThreads = 128;
+constexpr int kStemEpiWarp0 = 6, kStemEpiWarps = 4;  // one per TMEM lane quarter
 constexpr int kStemThreads = (kStemEpiWarp0 + kStemEpiWarps) * 32;
 constexpr int kStemBarBuild = 1;    // named barrier of the builder warps
 constexpr int kStemTimeout = 0x7004;
@@ -1968,7 +1974,7 @@ __device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
 }
 }  // namespace
 
-__global__ void __launch_bounds__(kStemThreads, 1)
+__global__ void __launch_bounds__(kStemThreads, kStemCtas)
     stem_conv_kernel(const __grid_constant__ InputConvParams p,
                      const __grid_constant__ CUtensorMap xmap) {
   extern __shared__ uint8_t in_smem_raw[];
@@ -1977,7 +1983,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
   const int CoutP = p.CoutP, taps = p.KH * p.KW;
   const float* s_x = reinterpret_cast<const float*>(sm);
   uint8_t* s_a = sm + kStemStages * p.stage_bytes;      // 2 x 4 A blocks
-  uint8_t* s_b = s_a + 8 * kInABlock;                   // CoutP rows x 64 B
+  uint8_t* s_b = s_a + kStemASets * 4 * kInABlock;      // CoutP rows x 64 B
   int4* s_ch = reinterpret_cast<int4*>(s_b + CoutP * 64);
   int64_t* s_bias = reinterpret_cast<int64_t*>(s_ch + CoutP);
   int64_t* s_mult = s_bias + CoutP;
@@ -2038,7 +2044,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
       s_tab[i] = (int32_t)min(max((int64_t)e.lut[idx], (int64_t)-128), (int64_t)255);
     }
   // K bytes 36 .. 63 of every A row stay zero: written once
-  for (int P = tid; P < 2 * 512; P += kStemThreads) {
+  for (int P = tid; P < kStemASets * 512; P += kStemThreads) {
     uint8_t* row = s_a + (P / 128) * kInABlock + ((P % 128) / 8) * 128 + (P % 8) * 16;
     *reinterpret_cast<uint4*>(row + 2 * 2048) = make_uint4(0, 0, 0, 0);
     *reinterpret_cast<uint4*>(row + 3 * 2048) = make_uint4(0, 0, 0, 0);
@@ -2113,11 +2119,11 @@ __global__ void __launch_bounds__(kStemThreads, 1)
       const uint32_t idesc = ptx::idesc_i8(128, CoutP, 1, 1);
       const uint32_t b_base = ptx::smem_addr(s_b);
       for (int k = 0; k < my_tiles; ++k) {
-        const int set = k & 1;
-        if (!wait(a_full(set), (k >> 1) & 1)) break;
+        const int set = k & 1, aset = k % kStemASets;
+        if (!wait(a_full(aset), (k / kStemASets) & 1)) break;
         if (k >= 2 && !wait(acc_empty(set), ((k >> 1) - 1) & 1)) break;
         ptx::tc_fence_after();
-        const uint32_t a_base = ptx::smem_addr(s_a) + set * 4 * kInABlock;
+        const uint32_t a_base = ptx::smem_addr(s_a) + aset * 4 * kInABlock;
 #pragma unroll
         for (int b = 0; b < 4; ++b)
 #pragma unroll
@@ -2126,7 +2132,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
                         ptx::smem_desc_kmajor_plain(a_base + b * kInABlock + kk * 4096, 2048, 128),
                         ptx::smem_desc_kmajor_plain(b_base + kk * 2 * b_lbo, b_lbo, 128), idesc,
                         kk > 0 ? 1u : 0u);
-        ptx::mma_commit(a_empty(set));
+        ptx::mma_commit(a_empty(aset));
         ptx::mma_commit(acc_full(set));
         committed = k + 1;
       }
@@ -2142,7 +2148,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
     const int groups = p.patch_h * (p.box_w / 4);
     const int bw = p.box_w;
     for (int k = 0; k < my_tiles; ++k) {
-      const int s = k % kStemStages, set = k & 1;
+      const int s = k % kStemStages, set = k % kStemASets;
       const bool got = wait(patch_full(s), (k / kStemStages) & 1);
       if (named_bar_or(kStemBarBuild, kStemBuildThreads, !got)) break;
       // (1) quantize the box: four columns of the three channel rows per step
@@ -2190,7 +2196,7 @@ __global__ void __launch_bounds__(kStemThreads, 1)
       }
       named_bar_sync(kStemBarBuild, kStemBuildThreads);
       if (bt == 0) ptx::mbar_arrive(patch_empty(s));  // the stage may be refilled
-      const bool freed = k < 2 || wait(a_empty(set), ((k >> 1) - 1) & 1);
+      const bool freed = k < kStemASets || wait(a_empty(set), ((k / kStemASets) - 1) & 1);
       if (named_bar_or(kStemBarBuild, kStemBuildThreads, !freed)) break;
       // (2) the implicit-GEMM rows of the tile: pixel P is row P % 128 of
       // block P / 128; K chunk j holds taps 4j .. 4j + 3
@@ -2387,8 +2393,8 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
   int dev = 0;
   cudaGetDevice(&dev);
   // the stem form (3 x 3, stride 2, undilated, three float channels) runs
-  // on the warp-specialized kernel: one CTA per SM, three patch stages, two
-  // A buffers and two accumulator sets
+  // on the warp-specialized kernel: two CTAs per SM, each with two patch
+  // stages, one A buffer and two accumulator sets
   const bool stem = p.KH == 3 && p.KW == 3 && p.SH == 2 && p.SW == 2 && p.DH == 1 &&
                     p.DW == 1 && c_in == kStemC;
   if (stem) {
@@ -2396,10 +2402,10 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
     int cols = 32;
     while (cols < 8 * p.CoutP) cols *= 2;
     p.tmem_cols = cols;
-    const size_t ssmem = 1024 + (size_t)kStemStages * p.stage_bytes + 8 * kInABlock +
+    const size_t ssmem = 1024 + (size_t)kStemStages * p.stage_bytes + kStemASets * 4 * kInABlock +
                          (size_t)p.CoutP * (64 + 16 + 3 * 8) + kInTab * 4 +
                          (size_t)p.patch_words * 4 + 8 + (2 * kStemStages + 8) * 8 + 16;
-    if (ssmem > 220 * 1024 || p.tmem_cols > 512) {
+    if (ssmem > 220 * 1024 / kStemCtas || p.tmem_cols * kStemCtas > 512) {
       set_error(kUnsupported, "qa_conv_input_fused_dev: stem layer outside the kernel's limits");
       return last_status();
     }
@@ -2414,7 +2420,7 @@ QA_API int qa_conv_input_fused_dev(const qa_fused_conv_desc* d, const float* x, 
         return last_status();
       if (dev >= 0 && dev < 64) stem_attr[dev] = ssmem;
     }
-    const int64_t grid = std::min<int64_t>(tiles, (int64_t)sm_count());
+    const int64_t grid = std::min<int64_t>(tiles, (int64_t)kStemCtas * sm_count());
     return launch_ex(stem_conv_kernel, dim3((unsigned)grid), dim3(kStemThreads), ssmem,
                      (cudaStream_t)stream, true, p, xmap)
                ? 0
