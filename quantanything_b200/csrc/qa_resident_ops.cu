@@ -1982,7 +1982,7 @@ __global__ void __launch_bounds__(kStemThreads, kStemCtas)
   uint8_t* sm = in_smem_raw + (((raw + 1023u) & ~1023u) - raw);
   const int CoutP = p.CoutP, taps = p.KH * p.KW;
   const float* s_x = reinterpret_cast<const float*>(sm);
-  uint8_t* s_a = sm + kStemStages * p.stage_bytes;      // 2 x 4 A blocks
+  uint8_t* s_a = sm + kStemStages * p.stage_bytes;      // kStemASets x 4 A blocks
   uint8_t* s_b = s_a + kStemASets * 4 * kInABlock;      // CoutP rows x 64 B
   int4* s_ch = reinterpret_cast<int4*>(s_b + CoutP * 64);
   int64_t* s_bias = reinterpret_cast<int64_t*>(s_ch + CoutP);
